@@ -1,0 +1,320 @@
+#!/usr/bin/env python
+"""Benchmark: Q8_0 LFM2-8B-A1B-shaped greedy decode on B200.
+
+One "step" = one greedy decode token (batch 1) through all 24 layers: 18 short-conv +
+6 GQA attention layers, 2 dense FFNs, 22 MoE FFNs (32 experts, top-4), lm_head + argmax.
+Weights are seeded random-init Q8_0 (no checkpoints exist here); the prompt is 512 seeded
+uniform token ids, prefilled untimed; then W warm-up and K timed decode steps.
+
+  value  -- tok/s of the device-resident decode loop (token fed back on the device, all
+            inputs in HBM; each step streams 1.66 GB of weights, far above the 126 MB L2)
+  e2e    -- tok/s through the public engine API (Lfm2CudaEngine.forward_argmax): each step
+            copies its token/position host->device and reads the argmax back
+  N > 1  -- independent replicas, one per GPU (one process per GPU; the batch-1 decode has
+            no exchange step), value = total tokens / max-over-ranks time
+
+`--impl reference` times the reference algorithm's CPU implementation (the C restatement
+of the JS CPU path in oracle/, all host threads) on a bounded slice of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+from __graft_entry__ import load_package  # noqa: E402
+
+METRIC = "decode tok/s and MoE-layer HBM GB/s (Q8_0 LFM2-MoE) at 1/2/4/8 B200"
+SEED = 1234
+PROMPT = 512
+THINK_ID = 124901  # LFM2 <think> (lfm2-engine.js:539); >= vocab 65536 here, so nothing to suppress
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic():
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return {}
+    return {}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _lfm2_model_bytes(spec) -> dict:
+    """Algorithmic bytes per decode token (Q8_0 = 34 B / 32 weights)."""
+    E, F, Fe, V, NE, k = spec.n_embd, spec.n_ff, spec.n_ff_exp, spec.n_vocab, spec.n_expert, spec.n_expert_used
+    q8 = 34 / 32
+    nq = spec.n_head * spec.head_dim
+    nkv = spec.n_head_kv * spec.head_dim
+    conv = (E * 3 * E + E * E) * q8
+    attn = (E * (nq + 2 * nkv) + nq * E) * q8
+    dense = 3 * E * F * q8
+    router = E * NE * q8
+    expert = 3 * E * Fe * q8
+    gateup = k * 2 * E * Fe * q8 + 4 * E + 4 * k * Fe
+    down = k * Fe * E * q8 + 4 * k * Fe + 8 * E
+    moe_layer = router + k * expert + 3 * 4 * E
+    n_attn = sum(1 for i in range(spec.n_layers) if spec.is_attn(i))
+    n_moe = sum(1 for i in range(spec.n_layers) if spec.is_moe(i))
+    weights = ((spec.n_layers - n_attn) * conv + n_attn * attn + (spec.n_layers - n_moe) * dense
+               + n_moe * (router + k * expert) + E * V * q8)
+    return dict(gateup=gateup, down=down, moe_layer=moe_layer, weights_per_token=weights)
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
+    qq3 = load_package()
+    qq3.build.build_all()
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
+    t0 = time.time()
+    tensors = qq3.synth.build_tensors(spec)
+    gen_s = time.time() - t0
+    g = qq3.synth.MemoryGGUF(spec, tensors)
+    max_ctx = PROMPT + args.warmup + 2 * args.steps + 16
+    eng = qq3.Lfm2CudaEngine(g, device=local, max_ctx=max_ctx)
+    stream = torch.cuda.Stream(device=local)
+    eng.ctx.set_stream(stream.cuda_stream)
+    prompt = qq3.synth.uniform_tokens(PROMPT, SEED + rank, spec.n_vocab)
+    suppress = THINK_ID if THINK_ID < spec.n_vocab else -1
+
+    eng.prefill(prompt[:-1].tolist())
+    pos = PROMPT - 1
+    toks = eng.model.decode_loop(int(prompt[-1]), pos, args.warmup, suppress_id=suppress)
+    pos += args.warmup
+    cur = int(toks[-1]) if len(toks) else int(prompt[-1])
+
+    # ---- value: device-resident greedy decode loop
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        out = eng.model.decode_loop(cur, pos, args.steps, suppress_id=suppress)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    pos += args.steps
+    cur = int(out[-1])
+
+    # ---- e2e: public engine API, host token in / argmax out per step
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e2.record(stream)
+    for _ in range(args.steps):
+        cur = eng.forward_argmax(cur, pos, suppress)
+        pos += 1
+    e3.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+
+    # ---- dominant kernel (expert gate/up GEMV) and whole MoE layer, timed alone over all layers
+    nbytes = _lfm2_model_bytes(spec)
+    ms_gateup = eng.model.bench_kernel(qq3.runtime.QQ_KERN_MOE_GATEUP, 3)
+    ms_layer = eng.model.bench_kernel(qq3.runtime.QQ_KERN_MOE_LAYER, 3)
+    step_kernels = eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS)
+
+    if dist:
+        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = float(t[0]), float(t[1])
+    peak, peak_kind = _peaks()
+    achieved = nbytes["gateup"] / (ms_gateup * 1e-3) / 1e9
+    traffic = _traffic().get("moe_gateup_bytes_per_launch")
+    tok_s = ws * args.steps / (ms * 1e-3)
+    e2e_tok_s = ws * args.steps / (ms_e2e * 1e-3)
+    res = {
+        "metric": METRIC, "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32 (Q8_0 weights, f32 activations)",
+        "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)",
+        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (BASELINE config 4)",
+                   "layers": "24 (18 short-conv, 6 GQA attention; 2 dense FFN 7168, 22 MoE 32x top-4 x 1792)",
+                   "hidden": 2048, "vocab": 65536, "prompt": PROMPT, "global_batch": ws,
+                   "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                   "l2": "inputs larger than L2: each step streams 1.66 GB of weights"},
+        "moe_layer_hbm_gbs": round(nbytes["moe_layer"] / (ms_layer * 1e-3) / 1e9, 1),
+        "step_weight_gbs_per_gpu": round(nbytes["weights_per_token"] * args.steps / (ms * 1e-3) / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": "moe expert gate/up SwiGLU GEMV (4 experts x 2 x 2048x1792 Q8_0)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes": int(nbytes["gateup"]), "avg_launch_ms": round(ms_gateup, 5)},
+        "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                "api": "Lfm2CudaEngine.forward_argmax -> qq_forward"},
+        "gpu_launches": int(step_kernels * args.steps),
+        "clocks": clk.summary(),
+        "setup_s": {"weight_generation": round(gen_s, 1)},
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(g, spec, budget_s=args.cpu_seconds)
+    if dist:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    eng.close()
+
+
+def _oracle():
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as orc  # noqa: WPS433
+
+    return orc
+
+
+def cpu_baseline(g, spec, budget_s: float = 12.0, prompt_len: int = 8, steps=None, warmup: int = 0):
+    """The oracle (C restatement of the JS CPU path) on the host cores: prompt_len-token
+    prompt, then greedy decode steps (time-bounded unless steps is given)."""
+    orc = _oracle()
+    cores = os.cpu_count() or 1
+    m = orc.OracleModel(g, max_ctx=prompt_len + (steps or 256) + warmup + 8, threads=cores)
+    prompt = load_package().synth.uniform_tokens(prompt_len, SEED, spec.n_vocab)
+    for p, t in enumerate(prompt[:-1]):
+        m.forward(int(t), p, True)
+    cur, pos = int(prompt[-1]), prompt_len - 1
+    for _ in range(warmup):
+        cur = int(np.argmax(m.forward(cur, pos, False)))
+        pos += 1
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cur = int(np.argmax(m.forward(cur, pos, False)))
+        pos += 1
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and (el >= budget_s and n >= 2)):
+            break
+    return {"value": round(n / el, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"LFM2-8B-A1B-shaped decode: {prompt_len}-token prompt then {n} greedy steps "
+                      f"(all 24 layers, f64-accumulating C restatement of the JS CPU path, {cores} threads)"}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    qq3 = load_package()
+    spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
+    g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
+    cb = cpu_baseline(g, spec, prompt_len=16, steps=args.steps, warmup=args.warmup)
+    res = {
+        "metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1000.0 / cb["value"], 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64 accumulate (JS numbers), f32 stores",
+        "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)", "impl": "reference",
+        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (BASELINE config 4)",
+                   "prompt": 16, "note": "bounded slice: 16-token prompt instead of 512 (CPU time)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+    else:
+        run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

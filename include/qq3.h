@@ -1,0 +1,219 @@
+/*
+ * qq3.h -- C ABI of libqq3cuda.so, the sm_100a (B200) backend for the QwenQwen3.js
+ * quantised inference path.
+ *
+ * The reference engines (src/qwen3-engine.js, src/lfm2-engine.js, and their WebGPU
+ * twins in src/webgpu.js) call an ops layer with GGUF tensor-meta objects and host
+ * Float32Arrays.  This header is what a binding (N-API addon, ctypes, cgo, ...) calls
+ * instead: plain pointers and sizes, no framework types.
+ *
+ * Conventions
+ *   - Every function returns QQ_OK (0) or a negative QQ_ERR_* code; qq_last_error()
+ *     returns a thread-local description of the last failure on the calling thread
+ *     (the JS engines throw; webgpu.js:443).
+ *   - Pointers named *_dev are device pointers on the context's device; every other
+ *     buffer is host memory, copied by the call (the caller keeps ownership, as with
+ *     GPUDevice.uploadBuffer, webgpu.js:370-383).
+ *   - Calls that take or return host buffers are synchronous.  Calls on *_dev buffers
+ *     are enqueued on the context stream (qq_set_stream) and complete in stream order;
+ *     qq_synchronize() waits for them.
+ *   - There is no CPU fallback: without a usable sm_100 device qq_init fails.
+ */
+#ifndef QQ3_H
+#define QQ3_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QQ_OK 0
+#define QQ_ERR_INVALID -1     /* bad argument, shape or state */
+#define QQ_ERR_CUDA -2        /* CUDA runtime error */
+#define QQ_ERR_OOM -3         /* device allocation failed */
+#define QQ_ERR_UNSUPPORTED -4 /* valid request this build does not implement */
+
+/* ggml tensor types accepted by qq_upload_tensor (gguf.js:25-34) */
+#define QQ_TYPE_F32 0
+#define QQ_TYPE_Q8_0 8
+
+typedef struct qq_ctx qq_ctx;
+typedef struct qq_tensor qq_tensor;
+typedef struct qq_model qq_model;
+
+/* ---------------------------------------------------------------- context */
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+const char* qq_last_error(void);
+
+/* Open a context on devices[0..n_devices).  Replaces GPUDevice.create (webgpu.js:355-367).
+ * This build drives one device per context (n_devices == 1); multi-GPU runs use one
+ * process and one context per GPU. */
+int qq_init(const int* devices, int n_devices, qq_ctx** out);
+int qq_destroy(qq_ctx* ctx);
+/* Make subsequent work of this context run on a caller-owned cudaStream_t (NULL = the
+ * context's own stream). */
+int qq_set_stream(qq_ctx* ctx, void* cuda_stream);
+int qq_synchronize(qq_ctx* ctx);
+
+/* ---------------------------------------------------------------- tensors */
+
+/* Upload one GGUF tensor from its raw file bytes.  Replaces GPUDevice.uploadBuffer of
+ * new Uint8Array(meta.buffer, meta.offset, meta.nbytes) (webgpu.js:370-383, 569-624,
+ * 1538-1629).  Q8_0 data is the 34-byte block stream (fp16 d + 32 int8, tensor.js:1-2);
+ * ne[0] must be a multiple of 32.  nbytes may exceed the exact size (gguf.js pads each
+ * tensor slice to 256 bytes, gguf.js:78-79).  n_dims in 1..3. */
+int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type, const int64_t* ne, int n_dims,
+                     qq_tensor** out);
+int qq_free_tensor(qq_tensor* t);
+/* Shape/type of an uploaded tensor (the meta.shape / meta.type fields, gguf.js:235-254). */
+int qq_tensor_info(const qq_tensor* t, int* ggml_type, int64_t* ne4, int* n_dims);
+/* out_dev[i] = element i in storage order, dequantised as q*d (bit-exact; the column
+ * readers of tensor.js:56-77 and _readWeightF32, tensor.js:80-100). */
+int qq_dequant(const qq_tensor* t, float* out_dev);
+
+/* ---------------------------------------------------------------- ops */
+
+/* y_dev[m][c] = sum_k x_dev[m][k] * W[k, c] for m < M: M independent calls of
+ * matmulQ80xF32 / matmulGeneric (tensor.js:26-53, 485-496); W is [K, N] Q8_0 and a 3-D
+ * tensor is taken as its first [K, N] matrix, as the JS does. */
+int qq_q8_matmul(qq_ctx* ctx, const qq_tensor* W, const float* x_dev, int M, float* y_dev);
+/* Row-wise RMSNorm, y = w * x / sqrt(mean(x^2) + eps) (rmsnorm, tensor.js:103-114; per
+ * head, perHeadRMSNorm, tensor.js:117-129).  w is an F32 tensor of length n. y may equal x. */
+int qq_rmsnorm(qq_ctx* ctx, const float* x_dev, int64_t n_rows, int n, const qq_tensor* w, float eps,
+               float* y_dev);
+
+/* ---------------------------------------------------------------- model */
+
+/* Per-layer tensor slots; names as the engines look them up (qwen3-engine.js:46-75,
+ * lfm2-engine.js:88-140). */
+enum {
+    QQ_ATTN_NORM = 0, /* blk.N.attn_norm.weight */
+    QQ_FFN_NORM,      /* blk.N.ffn_norm.weight */
+    QQ_WQ,            /* blk.N.attn_q.weight */
+    QQ_WK,            /* blk.N.attn_k.weight */
+    QQ_WV,            /* blk.N.attn_v.weight */
+    QQ_WO,            /* blk.N.attn_output.weight */
+    QQ_Q_NORM,        /* blk.N.attn_q_norm.weight */
+    QQ_K_NORM,        /* blk.N.attn_k_norm.weight */
+    QQ_CONV,          /* blk.N.shortconv.conv.weight (F32 [3, E]) */
+    QQ_IN_PROJ,       /* blk.N.shortconv.in_proj.weight */
+    QQ_OUT_PROJ,      /* blk.N.shortconv.out_proj.weight */
+    QQ_FFN_GATE,      /* blk.N.ffn_gate.weight */
+    QQ_FFN_UP,        /* blk.N.ffn_up.weight */
+    QQ_FFN_DOWN,      /* blk.N.ffn_down.weight */
+    QQ_ROUTER,        /* blk.N.ffn_gate_inp.weight */
+    QQ_GATE_EXPS,     /* blk.N.ffn_gate_exps.weight [E_in, F, n_expert] */
+    QQ_UP_EXPS,       /* blk.N.ffn_up_exps.weight */
+    QQ_DOWN_EXPS,     /* blk.N.ffn_down_exps.weight [F, E_in, n_expert] */
+    QQ_EXP_BIAS,      /* blk.N.exp_probs_b.bias (F32 [n_expert]) */
+    QQ_SLOT_COUNT
+};
+
+typedef struct qq_layer_desc {
+    int32_t is_attn; /* 1 = GQA attention; 0 = LFM2 short-conv (shortconv.conv.weight present, lfm2-engine.js:90-91) */
+    int32_t is_moe;  /* 1 = MoE FFN (Lfm2Engine._moEFFN); 0 = dense SwiGLU */
+    qq_tensor* t[QQ_SLOT_COUNT]; /* NULL where a slot does not apply */
+} qq_layer_desc;
+
+#define QQ_ARCH_QWEN3 0
+#define QQ_ARCH_LFM2 1
+
+/* The hyper-parameters the engine constructors read (gguf.js getArch :264-291,
+ * qwen3-engine.js:2-29, lfm2-engine.js:15-74) plus the tensors they bind. */
+typedef struct qq_model_desc {
+    int32_t arch;
+    int32_t n_layers;
+    int32_t n_embd;
+    int32_t n_head;
+    int32_t n_head_kv;
+    int32_t head_dim;
+    int32_t n_vocab;
+    int32_t n_expert;      /* 0 for dense models */
+    int32_t n_expert_used;
+    int32_t max_ctx;       /* KV capacity in positions (the JS default is min(ctx, 4096)) */
+    int32_t n_seq;         /* independent sequences (KV caches / conv states) */
+    float rms_eps;
+    double rope_base;
+    qq_tensor* tok_embd;    /* token_embd.weight */
+    qq_tensor* output_norm; /* output_norm.weight (Qwen3) / token_embd_norm.weight (LFM2) */
+    qq_tensor* output;      /* output.weight, or NULL for tied embeddings */
+    const qq_layer_desc* layers;
+} qq_model_desc;
+
+/* Bind uploaded tensors into an engine.  Replaces Qwen3GPUEngine.create /
+ * Lfm2GPUEngine.create (webgpu.js:498-567, 1470-1536).  Tensors stay owned by the caller
+ * and must outlive the model. */
+int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out);
+int qq_model_destroy(qq_model* m);
+
+/* forward(tokenId, position, skipLogits) for n_tokens consecutive tokens of sequence
+ * seq_id starting at position pos0 (qwen3-engine.js:115-245, lfm2-engine.js:228-269,
+ * webgpu.js:806-875, 1954-2034); n_tokens > 1 is exactly n sequential forward() calls.
+ * Only the last token produces logits, and only when want_logits != 0:
+ *   logits_out (nullable) receives n_vocab floats,
+ *   argmax_out (nullable) receives the greedy id (sampleGreedy, tensor.js:231-237) with
+ *   suppress_id (>= 0) excluded first (thinking suppression, tensor.js:247-248). */
+int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, int pos0, int want_logits,
+               float* logits_out, int32_t* argmax_out, int suppress_id);
+/* Greedy generate(): reset, prefill, then up to max_steps decode steps, stopping at
+ * eos_id (qwen3-engine.js:397-457, lfm2-engine.js:523-583, webgpu.js:1032-1098,
+ * 2047-2117 with temperature 0 and thinkingMode 'suppress').  out_tokens gets the
+ * generated ids; *n_out their count. */
+int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps, int think_id,
+                int eos_id, int32_t* out_tokens, int* n_out);
+/* resetState()/resetKVCache() (lfm2-engine.js:216-224, kv-cache.js:50-52): zero the
+ * conv states of seq_id; the KV cache is overwritten before it is read. */
+int qq_reset(qq_model* m, int seq_id);
+/* Routing record of the most recent token for MoE layer moe_layer (0-based among MoE
+ * layers): [top_k ids | top_k normalised weights | n_expert sigmoid probs] as floats, the
+ * buffer read by _readbackRoutingData (webgpu.js:1617-1618, 1922-1945). */
+int qq_read_routing(qq_model* m, int moe_layer, float* out);
+/* expertMask (lfm2-engine.js:464, router-viz.html:274): masked experts are skipped in
+ * the combine without renormalising.  n == 0 clears the mask. */
+int qq_set_expert_mask(qq_model* m, const int32_t* ids, int n);
+/* Hidden state after every layer for the last token of a qq_forward call, [n_layers][n_embd]
+ * (the parity probe used by the tests; the JS logs per-layer maxima, qwen3-engine.js:189-215). */
+int qq_forward_dump(qq_model* m, int32_t token_id, int seq_id, int pos, float* hidden_out);
+/* Device-resident greedy decode: starting from token first_token at position pos0, run
+ * n_steps forward+argmax steps with the next token fed back on the device (no host round
+ * trip).  tokens_out (nullable, host) receives the n_steps generated ids. */
+int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_steps, int suppress_id,
+                   int32_t* tokens_out);
+
+/* ---------------------------------------------------------------- diagnostics */
+
+/* Statistics of a model (no reference counterpart; used by the benchmark):
+ *   QQ_STAT_STEP_KERNELS  kernels launched by one decode step with logits
+ *   QQ_STAT_N_MOE         number of MoE layers */
+#define QQ_STAT_STEP_KERNELS 0
+#define QQ_STAT_N_MOE 1
+int qq_model_stat(qq_model* m, int what, int64_t* value);
+/* Time one kernel class over every MoE layer in turn (so no layer's weights are still in
+ * L2 when it is read again), iters rounds, using the routing of the latest token; returns
+ * the mean duration of one launch in *ms (CUDA events on the context stream).  Clobbers the
+ * hidden state of the current step.  No reference counterpart.
+ *   QQ_KERN_MOE_LAYER   router + expert gate/up + expert down-combine of one layer
+ *   QQ_KERN_MOE_GATEUP  the expert gate/up SwiGLU GEMV
+ *   QQ_KERN_MOE_DOWN    the expert down GEMV + weighted combine */
+#define QQ_KERN_MOE_LAYER 0
+#define QQ_KERN_MOE_GATEUP 1
+#define QQ_KERN_MOE_DOWN 2
+int qq_bench_kernel(qq_model* m, int what, int iters, float* ms);
+
+/* ---------------------------------------------------------------- MoE block */
+
+/* The LFM2-MoE FFN (Lfm2Engine._moEFFN, lfm2-engine.js:413-487; WGSL_MOE_SIGMOID_TOPK +
+ * WGSL_MATMUL_EXPERT_Q80 + WGSL_AXPY_EXPERT, webgpu.js:1243-1283, 1290-1324, 1441-1454) on
+ * T token rows: x_dev [T][E_in] is the ffn-normalised input, out_dev [T][E_in] receives
+ * sum_k w_k * expert_k(x); routing_dev (nullable) [T][2*top_k + n_expert] the records.
+ * layer->t[QQ_ROUTER], [QQ_GATE_EXPS], [QQ_UP_EXPS], [QQ_DOWN_EXPS], [QQ_EXP_BIAS] are used. */
+int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
+                 float* out_dev, float* routing_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QQ3_H */

@@ -1,0 +1,893 @@
+// api.cu -- the extern "C" boundary of libqq3cuda.so and the decode runtime behind it.
+//
+// Runtime design (one B200, one sequence per decode step):
+//   * weights are uploaded raw (GGUF Q8_0 blocks) and split on the device into qs/d planes;
+//   * a decode step is a fixed sequence of ~5 launches per layer (see enqueue_step), every
+//     kernel reading the token id and position from device memory, so the whole step is
+//     captured once per (sequence, with/without logits) as a CUDA graph and replayed;
+//   * greedy decode can run entirely on the device: the step's last kernel writes the
+//     argmax back as the next step's token (qq_decode_loop).
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/qq3.h"
+#include "kernels.h"
+
+namespace qq3 {
+static thread_local std::string g_err;
+void set_error(const std::string& msg) { g_err = msg; }
+}  // namespace qq3
+
+using qq3::DTensor;
+using qq3::Error;
+
+struct qq_ctx {
+    int device = 0;
+    cudaStream_t own = nullptr;
+    cudaStream_t stream = nullptr;
+    // scratch arena for op-level calls (grow-only)
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+struct qq_tensor {
+    qq_ctx* ctx = nullptr;
+    DTensor t;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) QQ_CUDA_TRY(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+template <class F>
+int guard(F&& f) {
+    try {
+        f();
+        return QQ_OK;
+    } catch (const Error& e) {
+        qq3::set_error(e.msg);
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        qq3::set_error("host allocation failed");
+        return QQ_ERR_OOM;
+    } catch (const std::exception& e) {
+        qq3::set_error(e.what());
+        return QQ_ERR_INVALID;
+    }
+}
+
+void* dmalloc(size_t bytes) {
+    void* p = nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        throw Error{QQ_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + " bytes) failed: " + cudaGetErrorString(e)};
+    }
+    return p;
+}
+
+template <class T>
+T* dalloc(size_t n) {
+    return static_cast<T*>(dmalloc(n * sizeof(T)));
+}
+
+void* ctx_scratch(qq_ctx* c, size_t bytes) {
+    if (bytes > c->scratch_bytes) {
+        if (c->scratch) {
+            QQ_CUDA_TRY(cudaStreamSynchronize(c->stream));
+            cudaFree(c->scratch);
+            c->scratch = nullptr;
+            c->scratch_bytes = 0;
+        }
+        c->scratch = dmalloc(bytes);
+        c->scratch_bytes = bytes;
+    }
+    return c->scratch;
+}
+
+const DTensor* dt(qq_tensor* t) { return t ? &t->t : nullptr; }
+
+void need(bool cond, const std::string& msg) { QQ_CHECK(cond, QQ_ERR_INVALID, msg); }
+
+void check_shape(const DTensor* t, int type, int64_t ne0, int64_t ne1, int64_t ne2, const char* what) {
+    need(t != nullptr, std::string("missing tensor: ") + what);
+    need(t->type == type, std::string("wrong ggml type for ") + what);
+    need(t->ne[0] == ne0 && t->ne[1] == ne1 && t->ne[2] == ne2,
+         std::string("wrong shape for ") + what + ": got [" + std::to_string(t->ne[0]) + ", " +
+             std::to_string(t->ne[1]) + ", " + std::to_string(t->ne[2]) + "]");
+}
+
+}  // namespace
+
+// =====================================================================================
+// Model
+
+struct Layer {
+    bool attn = false, moe = false;
+    const DTensor* t[QQ_SLOT_COUNT] = {nullptr};
+    int attn_slot = -1, moe_slot = -1;
+};
+
+struct qq_model {
+    qq_ctx* ctx = nullptr;
+    qq_model_desc d{};
+    std::vector<Layer> layers;
+    const DTensor* tok_embd = nullptr;
+    const DTensor* out_norm = nullptr;
+    const DTensor* output = nullptr;
+    int n_attn = 0, n_moe = 0, n_ff_max = 0, n_split = 1, rec_len = 0;
+    // activations
+    float *hidden = nullptr, *qkv = nullptr, *attn_out = nullptr, *y = nullptr, *h = nullptr, *logits = nullptr;
+    // per-sequence state
+    float *k_cache = nullptr, *v_cache = nullptr, *conv_state = nullptr;
+    int* trace = nullptr;  // [n_seq][max_ctx + 1] greedy ids produced by device-driven steps
+    // tables / scratch
+    float* rope_cs = nullptr;
+    float* attn_part = nullptr;
+    unsigned int* attn_counter = nullptr;
+    float* rec = nullptr;
+    int* ridx = nullptr;
+    float* rw = nullptr;
+    uint32_t* mask = nullptr;
+    int* ctl = nullptr;       // [token, pos]
+    int* suppress = nullptr;  // [1]
+    unsigned long long* best = nullptr;
+    float* dump = nullptr;    // [n_layers][n_embd] for qq_forward_dump
+    int* h_ctl = nullptr;     // pinned staging [2 * h_ctl_cap]
+    size_t h_ctl_cap = 0;
+    int* h_small = nullptr;   // pinned [4]
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+    cudaStream_t cap = nullptr;
+    int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
+
+    size_t kv_stride_seq() const { return (size_t)n_attn * d.n_head_kv * d.max_ctx * d.head_dim; }
+    size_t kv_stride_layer() const { return (size_t)d.n_head_kv * d.max_ctx * d.head_dim; }
+    float* conv(int seq, int l) const { return conv_state + ((size_t)seq * d.n_layers + l) * 2 * d.n_embd; }
+};
+
+namespace {
+
+void free_model(qq_model* m) {
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    m->graphs.clear();
+    void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
+                    m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->ridx, m->rw, m->mask, m->ctl,
+                    m->suppress, m->best, m->dump};
+    for (void* p : bufs)
+        if (p) cudaFree(p);
+    if (m->h_ctl) cudaFreeHost(m->h_ctl);
+    if (m->h_small) cudaFreeHost(m->h_small);
+    if (m->cap) cudaStreamDestroy(m->cap);
+}
+
+// One decode step for sequence `seq` (token/position in m->ctl), as the fixed kernel
+// sequence of Qwen3Engine.forward / Lfm2Engine.forward.
+void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool dump) {
+    const qq_model_desc& d = m->d;
+    const int E = d.n_embd, hd = d.head_dim;
+    const int nq = d.n_head * hd;
+    qq3::launch_embed(*m->tok_embd, m->ctl, m->hidden, want_logits ? m->best : nullptr, s);
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        qq3::XStage st;
+        st.x[0] = m->hidden;
+        st.K = E;
+        st.norm_w = L.t[QQ_ATTN_NORM]->f32;
+        st.eps = d.rms_eps;
+        if (L.attn) {
+            qq3::launch_gemv_qkv(*L.t[QQ_WQ], *L.t[QQ_WK], *L.t[QQ_WV], st, m->qkv, s);
+            qq3::AttnArgs a;
+            a.qkv = m->qkv;
+            a.q_norm = L.t[QQ_Q_NORM]->f32;
+            a.k_norm = L.t[QQ_K_NORM]->f32;
+            a.rope_cs = m->rope_cs;
+            a.k_cache = m->k_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+            a.v_cache = m->v_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+            a.out = m->attn_out;
+            a.part = m->attn_part;
+            a.counter = m->attn_counter;
+            a.pos = m->ctl + 1;
+            a.n_head = d.n_head;
+            a.n_kv = d.n_head_kv;
+            a.hd = hd;
+            a.max_ctx = d.max_ctx;
+            a.n_split = m->n_split;
+            a.eps = d.rms_eps;
+            qq3::launch_attention_decode(a, s);
+            qq3::XStage so;
+            so.x[0] = m->attn_out;
+            so.K = nq;
+            qq3::launch_gemv_rows(*L.t[QQ_WO], 0, E, so, m->hidden, true, s);
+        } else {
+            qq3::launch_gemv_conv(*L.t[QQ_IN_PROJ], L.t[QQ_CONV]->f32, m->conv(seq, l), st, m->y, s);
+            qq3::XStage so;
+            so.x[0] = m->y;
+            so.K = E;
+            qq3::launch_gemv_rows(*L.t[QQ_OUT_PROJ], 0, E, so, m->hidden, true, s);
+        }
+        qq3::XStage sf;
+        sf.x[0] = m->hidden;
+        sf.K = E;
+        sf.norm_w = L.t[QQ_FFN_NORM]->f32;
+        sf.eps = d.rms_eps;
+        if (L.moe) {
+            const int k = d.n_expert_used;
+            float* rec = m->rec + (size_t)L.moe_slot * m->rec_len;
+            int* idx = m->ridx + (size_t)L.moe_slot * k;
+            float* w = m->rw + (size_t)L.moe_slot * k;
+            const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+            qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, m->hidden, 1, sf.norm_w, sf.eps, d.n_expert, k, rec, idx,
+                                    w, s);
+            qq3::launch_moe_gateup(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], idx, m->mask, k, sf, m->h, s);
+            qq3::launch_moe_down_combine(*L.t[QQ_DOWN_EXPS], idx, w, m->mask, k, m->h, m->hidden, s);
+        } else {
+            qq3::launch_gemv_swiglu(*L.t[QQ_FFN_GATE], *L.t[QQ_FFN_UP], sf, m->h, s);
+            qq3::XStage sd;
+            sd.x[0] = m->h;
+            sd.K = (int)L.t[QQ_FFN_GATE]->ne[1];
+            qq3::launch_gemv_rows(*L.t[QQ_FFN_DOWN], 0, E, sd, m->hidden, true, s);
+        }
+        if (dump)
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->dump + (size_t)l * E, m->hidden, sizeof(float) * E,
+                                        cudaMemcpyDeviceToDevice, s));
+    }
+    if (want_logits) {
+        qq3::XStage so;
+        so.x[0] = m->hidden;
+        so.K = E;
+        so.norm_w = m->out_norm->f32;
+        so.eps = d.rms_eps;
+        const DTensor* out = m->output ? m->output : m->tok_embd;
+        qq3::launch_gemv_logits_argmax(*out, so, m->logits, m->best, m->suppress, s);
+        qq3::launch_argmax_finish(m->best, m->ctl, m->trace + (size_t)seq * (d.max_ctx + 1), s);
+    }
+}
+
+cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
+    auto key = std::make_pair(seq, want_logits ? 1 : 0);
+    auto it = m->graphs.find(key);
+    if (it != m->graphs.end()) return it->second;
+    cudaGraph_t g = nullptr;
+    QQ_CUDA_TRY(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeRelaxed));
+    try {
+        enqueue_step(m, seq, want_logits, m->cap, false);
+    } catch (...) {
+        cudaStreamEndCapture(m->cap, &g);
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        throw;
+    }
+    QQ_CUDA_TRY(cudaStreamEndCapture(m->cap, &g));
+    if (want_logits) {
+        size_t n = 0;
+        cudaGraphGetNodes(g, nullptr, &n);
+        std::vector<cudaGraphNode_t> nodes(n);
+        cudaGraphGetNodes(g, nodes.data(), &n);
+        int64_t k = 0;
+        for (auto nd : nodes) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+        }
+        m->step_kernels = k;
+    }
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    QQ_CUDA_TRY(e);
+    m->graphs[key] = ge;
+    return ge;
+}
+
+void ensure_h_ctl(qq_model* m, size_t n) {
+    if (n <= m->h_ctl_cap) return;
+    if (m->h_ctl) {
+        QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+        cudaFreeHost(m->h_ctl);
+        m->h_ctl = nullptr;
+    }
+    size_t cap = 64;
+    while (cap < n) cap *= 2;
+    QQ_CUDA_TRY(cudaMallocHost(&m->h_ctl, cap * 2 * sizeof(int)));
+    m->h_ctl_cap = cap;
+}
+
+void check_seq_pos(qq_model* m, int seq, int pos0, int n) {
+    need(seq >= 0 && seq < m->d.n_seq, "seq_id out of range");
+    need(pos0 >= 0 && n >= 0 && (int64_t)pos0 + n <= m->d.max_ctx,
+         "positions [" + std::to_string(pos0) + ", " + std::to_string(pos0 + n) + ") exceed the KV capacity " +
+             std::to_string(m->d.max_ctx));
+}
+
+void set_suppress(qq_model* m, int id) {
+    m->h_small[0] = id;
+    QQ_CUDA_TRY(cudaMemcpyAsync(m->suppress, m->h_small, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+}
+
+// host-driven steps: token_ids[i] at pos0 + i; logits graph for the last one if requested
+void run_tokens(qq_model* m, const int32_t* token_ids, int n, int seq, int pos0, bool want_logits) {
+    cudaStream_t s = m->ctx->stream;
+    ensure_h_ctl(m, (size_t)n);
+    for (int i = 0; i < n; i++) {
+        need(token_ids[i] >= 0 && token_ids[i] < m->d.n_vocab, "token id out of range");
+        m->h_ctl[2 * i] = token_ids[i];
+        m->h_ctl[2 * i + 1] = pos0 + i;
+    }
+    for (int i = 0; i < n; i++) {
+        const bool logits = want_logits && i == n - 1;
+        cudaGraphExec_t g = get_graph(m, seq, logits);
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->ctl, m->h_ctl + 2 * i, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+        QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+    }
+}
+
+}  // namespace
+
+// =====================================================================================
+// C ABI
+
+extern "C" {
+
+const char* qq_last_error(void) { return qq3::g_err.c_str(); }
+
+int qq_init(const int* devices, int n_devices, qq_ctx** out) {
+    return guard([&] {
+        need(out != nullptr, "qq_init: out is NULL");
+        need(n_devices == 1 && devices != nullptr,
+             "qq_init: this build drives one device per context (run one process per GPU)");
+        int count = 0;
+        QQ_CUDA_TRY(cudaGetDeviceCount(&count));
+        need(devices[0] >= 0 && devices[0] < count, "qq_init: device index out of range");
+        cudaDeviceProp p;
+        QQ_CUDA_TRY(cudaGetDeviceProperties(&p, devices[0]));
+        QQ_CHECK(p.major == 10 && p.minor == 0, QQ_ERR_UNSUPPORTED,
+                 std::string("qq_init: libqq3cuda.so is built for sm_100a (B200); device is ") + p.name);
+        DeviceGuard dg(devices[0]);
+        qq_ctx* c = new qq_ctx;
+        c->device = devices[0];
+        cudaError_t e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            delete c;
+            QQ_CUDA_TRY(e);
+        }
+        c->stream = c->own;
+        *out = c;
+    });
+}
+
+int qq_destroy(qq_ctx* ctx) {
+    return guard([&] {
+        if (!ctx) return;
+        DeviceGuard dg(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        if (ctx->scratch) cudaFree(ctx->scratch);
+        if (ctx->own) cudaStreamDestroy(ctx->own);
+        delete ctx;
+    });
+}
+
+int qq_set_stream(qq_ctx* ctx, void* cuda_stream) {
+    return guard([&] {
+        need(ctx != nullptr, "qq_set_stream: ctx is NULL");
+        ctx->stream = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : ctx->own;
+    });
+}
+
+int qq_synchronize(qq_ctx* ctx) {
+    return guard([&] {
+        need(ctx != nullptr, "qq_synchronize: ctx is NULL");
+        DeviceGuard dg(ctx->device);
+        QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    });
+}
+
+int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type, const int64_t* ne, int n_dims,
+                     qq_tensor** out) {
+    return guard([&] {
+        need(ctx && host && ne && out, "qq_upload_tensor: NULL argument");
+        need(n_dims >= 1 && n_dims <= 4, "qq_upload_tensor: n_dims must be 1..4");
+        QQ_CHECK(ggml_type == QQ_TYPE_F32 || ggml_type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED,
+                 "qq_upload_tensor: only F32 (0) and Q8_0 (8) tensors are supported");
+        DTensor t;
+        t.type = ggml_type;
+        t.n_dims = n_dims;
+        int64_t n = 1;
+        for (int i = 0; i < n_dims; i++) {
+            need(ne[i] >= 1, "qq_upload_tensor: every ne[i] must be >= 1");
+            t.ne[i] = ne[i];
+            n *= ne[i];
+        }
+        t.K = t.ne[0];
+        t.rows = n / t.ne[0];
+        t.device = ctx->device;
+        DeviceGuard dg(ctx->device);
+        if (ggml_type == QQ_TYPE_F32) {
+            need(nbytes >= (size_t)n * 4, "qq_upload_tensor: buffer shorter than ne0*ne1*... floats");
+            t.f32 = dalloc<float>((size_t)n);
+            QQ_CUDA_TRY(cudaMemcpy(t.f32, host, (size_t)n * 4, cudaMemcpyHostToDevice));
+        } else {
+            need(t.ne[0] % 32 == 0, "qq_upload_tensor: Q8_0 needs ne[0] % 32 == 0");
+            const int64_t nb = n / 32;
+            need(nbytes >= (size_t)nb * 34, "qq_upload_tensor: buffer shorter than the Q8_0 block stream");
+            uint8_t* raw = dalloc<uint8_t>((size_t)nb * 34);
+            try {
+                t.qs = dalloc<int8_t>((size_t)n);
+                t.d = dalloc<__half>((size_t)nb);
+                QQ_CUDA_TRY(cudaMemcpy(raw, host, (size_t)nb * 34, cudaMemcpyHostToDevice));
+                qq3::launch_repack_q8(raw, nb, t.qs, t.d, ctx->stream);
+                QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+            } catch (...) {
+                cudaFree(raw);
+                if (t.qs) cudaFree(t.qs);
+                if (t.d) cudaFree(t.d);
+                throw;
+            }
+            cudaFree(raw);
+        }
+        qq_tensor* r = new qq_tensor;
+        r->ctx = ctx;
+        r->t = t;
+        *out = r;
+    });
+}
+
+int qq_free_tensor(qq_tensor* t) {
+    return guard([&] {
+        if (!t) return;
+        DeviceGuard dg(t->t.device);
+        if (t->t.qs) cudaFree(t->t.qs);
+        if (t->t.d) cudaFree(t->t.d);
+        if (t->t.f32) cudaFree(t->t.f32);
+        delete t;
+    });
+}
+
+int qq_tensor_info(const qq_tensor* t, int* ggml_type, int64_t* ne4, int* n_dims) {
+    return guard([&] {
+        need(t != nullptr, "qq_tensor_info: NULL tensor");
+        if (ggml_type) *ggml_type = t->t.type;
+        if (n_dims) *n_dims = t->t.n_dims;
+        if (ne4)
+            for (int i = 0; i < 4; i++) ne4[i] = t->t.ne[i];
+    });
+}
+
+int qq_dequant(const qq_tensor* t, float* out_dev) {
+    return guard([&] {
+        need(t && out_dev, "qq_dequant: NULL argument");
+        DeviceGuard dg(t->t.device);
+        cudaStream_t s = t->ctx->stream;
+        if (t->t.type == QQ_TYPE_F32)
+            QQ_CUDA_TRY(cudaMemcpyAsync(out_dev, t->t.f32, sizeof(float) * t->t.K * t->t.rows,
+                                        cudaMemcpyDeviceToDevice, s));
+        else
+            qq3::launch_dequant_q8(t->t, out_dev, s);
+    });
+}
+
+int qq_q8_matmul(qq_ctx* ctx, const qq_tensor* W, const float* x_dev, int M, float* y_dev) {
+    return guard([&] {
+        need(ctx && W && x_dev && y_dev, "qq_q8_matmul: NULL argument");
+        need(M >= 0, "qq_q8_matmul: M < 0");
+        QQ_CHECK(W->t.type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED, "qq_q8_matmul: W must be Q8_0");
+        DeviceGuard dg(ctx->device);
+        const int64_t K = W->t.ne[0], N = W->t.ne[1];
+        for (int r = 0; r < M; r++) {
+            qq3::XStage st;
+            st.x[0] = x_dev + (size_t)r * K;
+            st.K = (int)K;
+            qq3::launch_gemv_rows(W->t, 0, N, st, y_dev + (size_t)r * N, false, ctx->stream);
+        }
+    });
+}
+
+int qq_rmsnorm(qq_ctx* ctx, const float* x_dev, int64_t n_rows, int n, const qq_tensor* w, float eps, float* y_dev) {
+    return guard([&] {
+        need(ctx && x_dev && w && y_dev, "qq_rmsnorm: NULL argument");
+        need(w->t.type == QQ_TYPE_F32 && w->t.K * w->t.rows == n, "qq_rmsnorm: w must be F32 of length n");
+        DeviceGuard dg(ctx->device);
+        qq3::launch_rmsnorm(const_cast<float*>(x_dev), n_rows, n, w->t.f32, eps, y_dev, ctx->stream);
+    });
+}
+
+int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
+    return guard([&] {
+        need(ctx && desc && out && desc->layers, "qq_model_create: NULL argument");
+        const qq_model_desc& d = *desc;
+        need(d.arch == QQ_ARCH_QWEN3 || d.arch == QQ_ARCH_LFM2, "qq_model_create: unknown arch");
+        need(d.n_layers >= 1 && d.n_embd >= 32 && d.n_embd % 32 == 0, "qq_model_create: bad n_layers/n_embd");
+        need(d.n_head >= 1 && d.n_head_kv >= 1 && d.n_head % d.n_head_kv == 0, "qq_model_create: bad head counts");
+        QQ_CHECK(d.head_dim == 64 || d.head_dim == 128, QQ_ERR_UNSUPPORTED, "qq_model_create: head_dim must be 64/128");
+        QQ_CHECK(d.n_head / d.n_head_kv <= 8, QQ_ERR_UNSUPPORTED, "qq_model_create: GQA group larger than 8");
+        need(d.max_ctx >= 1 && d.n_seq >= 1 && d.n_vocab >= 1, "qq_model_create: bad max_ctx/n_seq/n_vocab");
+        const int E = d.n_embd, hd = d.head_dim;
+        const int nq = d.n_head * hd, nkv = d.n_head_kv * hd;
+        DeviceGuard dg(ctx->device);
+        qq_model* m = new qq_model;
+        m->ctx = ctx;
+        m->d = d;
+        m->d.layers = nullptr;
+        try {
+            m->tok_embd = dt(d.tok_embd);
+            check_shape(m->tok_embd, QQ_TYPE_Q8_0, E, d.n_vocab, 1, "token_embd.weight");
+            m->out_norm = dt(d.output_norm);
+            check_shape(m->out_norm, QQ_TYPE_F32, E, 1, 1, "output norm");
+            m->output = dt(d.output);
+            if (m->output) check_shape(m->output, QQ_TYPE_Q8_0, E, d.n_vocab, 1, "output.weight");
+            m->layers.resize(d.n_layers);
+            for (int l = 0; l < d.n_layers; l++) {
+                const qq_layer_desc& ld = d.layers[l];
+                Layer& L = m->layers[l];
+                L.attn = ld.is_attn != 0;
+                L.moe = ld.is_moe != 0;
+                for (int s = 0; s < QQ_SLOT_COUNT; s++) {
+                    L.t[s] = dt(ld.t[s]);
+                    if (ld.t[s]) need(ld.t[s]->ctx == ctx, "qq_model_create: tensor from another context");
+                }
+                const std::string b = "blk." + std::to_string(l) + ".";
+                check_shape(L.t[QQ_ATTN_NORM], QQ_TYPE_F32, E, 1, 1, (b + "attn_norm.weight").c_str());
+                check_shape(L.t[QQ_FFN_NORM], QQ_TYPE_F32, E, 1, 1, (b + "ffn_norm.weight").c_str());
+                if (L.attn) {
+                    L.attn_slot = m->n_attn++;
+                    check_shape(L.t[QQ_WQ], QQ_TYPE_Q8_0, E, nq, 1, (b + "attn_q.weight").c_str());
+                    check_shape(L.t[QQ_WK], QQ_TYPE_Q8_0, E, nkv, 1, (b + "attn_k.weight").c_str());
+                    check_shape(L.t[QQ_WV], QQ_TYPE_Q8_0, E, nkv, 1, (b + "attn_v.weight").c_str());
+                    check_shape(L.t[QQ_WO], QQ_TYPE_Q8_0, nq, E, 1, (b + "attn_output.weight").c_str());
+                    check_shape(L.t[QQ_Q_NORM], QQ_TYPE_F32, hd, 1, 1, (b + "attn_q_norm.weight").c_str());
+                    check_shape(L.t[QQ_K_NORM], QQ_TYPE_F32, hd, 1, 1, (b + "attn_k_norm.weight").c_str());
+                } else {
+                    need(d.arch == QQ_ARCH_LFM2, "qq_model_create: short-conv layers exist only in LFM2");
+                    check_shape(L.t[QQ_CONV], QQ_TYPE_F32, 3, E, 1, (b + "shortconv.conv.weight").c_str());
+                    check_shape(L.t[QQ_IN_PROJ], QQ_TYPE_Q8_0, E, 3 * E, 1, (b + "shortconv.in_proj.weight").c_str());
+                    check_shape(L.t[QQ_OUT_PROJ], QQ_TYPE_Q8_0, E, E, 1, (b + "shortconv.out_proj.weight").c_str());
+                }
+                if (L.moe) {
+                    QQ_CHECK(d.arch == QQ_ARCH_LFM2, QQ_ERR_UNSUPPORTED,
+                             "qq_model_create: Qwen3-MoE softmax routing is not in this build");
+                    QQ_CHECK(d.n_expert_used == 4 && d.n_expert <= 32, QQ_ERR_UNSUPPORTED,
+                             "qq_model_create: MoE layers need top-4 of <= 32 experts in this build");
+                    L.moe_slot = m->n_moe++;
+                    const int64_t F = L.t[QQ_GATE_EXPS] ? L.t[QQ_GATE_EXPS]->ne[1] : 0;
+                    check_shape(L.t[QQ_ROUTER], QQ_TYPE_Q8_0, E, d.n_expert, 1, (b + "ffn_gate_inp.weight").c_str());
+                    check_shape(L.t[QQ_GATE_EXPS], QQ_TYPE_Q8_0, E, F, d.n_expert, (b + "ffn_gate_exps.weight").c_str());
+                    check_shape(L.t[QQ_UP_EXPS], QQ_TYPE_Q8_0, E, F, d.n_expert, (b + "ffn_up_exps.weight").c_str());
+                    check_shape(L.t[QQ_DOWN_EXPS], QQ_TYPE_Q8_0, F, E, d.n_expert, (b + "ffn_down_exps.weight").c_str());
+                    if (L.t[QQ_EXP_BIAS])
+                        check_shape(L.t[QQ_EXP_BIAS], QQ_TYPE_F32, d.n_expert, 1, 1, (b + "exp_probs_b.bias").c_str());
+                    need(F % 32 == 0, "expert FFN width must be a multiple of 32");
+                    if (d.n_expert_used * F > m->n_ff_max) m->n_ff_max = (int)(d.n_expert_used * F);
+                } else {
+                    const int64_t F = L.t[QQ_FFN_GATE] ? L.t[QQ_FFN_GATE]->ne[1] : 0;
+                    check_shape(L.t[QQ_FFN_GATE], QQ_TYPE_Q8_0, E, F, 1, (b + "ffn_gate.weight").c_str());
+                    check_shape(L.t[QQ_FFN_UP], QQ_TYPE_Q8_0, E, F, 1, (b + "ffn_up.weight").c_str());
+                    check_shape(L.t[QQ_FFN_DOWN], QQ_TYPE_Q8_0, F, E, 1, (b + "ffn_down.weight").c_str());
+                    need(F % 32 == 0, "FFN width must be a multiple of 32");
+                    if (F > m->n_ff_max) m->n_ff_max = (int)F;
+                }
+            }
+            m->n_split = qq3::attention_splits(d.max_ctx);
+            m->rec_len = 2 * d.n_expert_used + d.n_expert;
+            m->hidden = dalloc<float>(E);
+            m->qkv = dalloc<float>((size_t)nq + 2 * nkv);
+            m->attn_out = dalloc<float>(nq);
+            m->y = dalloc<float>(E);
+            m->h = dalloc<float>((size_t)std::max(m->n_ff_max, 32));
+            m->logits = dalloc<float>(d.n_vocab);
+            const size_t kv = (size_t)d.n_seq * std::max(m->n_attn, 1) * nkv * d.max_ctx;
+            m->k_cache = dalloc<float>(kv);
+            m->v_cache = dalloc<float>(kv);
+            QQ_CUDA_TRY(cudaMemset(m->k_cache, 0, kv * 4));
+            QQ_CUDA_TRY(cudaMemset(m->v_cache, 0, kv * 4));
+            const size_t cs = (size_t)d.n_seq * d.n_layers * 2 * E;
+            m->conv_state = dalloc<float>(cs);
+            QQ_CUDA_TRY(cudaMemset(m->conv_state, 0, cs * 4));
+            m->trace = dalloc<int>((size_t)d.n_seq * (d.max_ctx + 1));
+            // RoPE table: cos/sin of position * base^(-i/half) in double (tensor.js:137-140)
+            {
+                const int half = hd / 2;
+                std::vector<float> tab((size_t)d.max_ctx * hd);
+                for (int p = 0; p < d.max_ctx; p++)
+                    for (int i = 0; i < half; i++) {
+                        const double freq = 1.0 / std::pow(d.rope_base, (double)i / (double)half);
+                        const double th = (double)p * freq;
+                        tab[(size_t)p * hd + 2 * i] = (float)std::cos(th);
+                        tab[(size_t)p * hd + 2 * i + 1] = (float)std::sin(th);
+                    }
+                m->rope_cs = dalloc<float>(tab.size());
+                QQ_CUDA_TRY(cudaMemcpy(m->rope_cs, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+            }
+            m->attn_part = dalloc<float>((size_t)d.n_head * m->n_split * (hd + 2));
+            m->attn_counter = dalloc<unsigned int>(d.n_head_kv);
+            QQ_CUDA_TRY(cudaMemset(m->attn_counter, 0, sizeof(unsigned int) * d.n_head_kv));
+            const int nm = std::max(m->n_moe, 1);
+            m->rec = dalloc<float>((size_t)nm * std::max(m->rec_len, 1));
+            m->ridx = dalloc<int>((size_t)nm * std::max(d.n_expert_used, 1));
+            m->rw = dalloc<float>((size_t)nm * std::max(d.n_expert_used, 1));
+            QQ_CUDA_TRY(cudaMemset(m->rec, 0, sizeof(float) * nm * std::max(m->rec_len, 1)));
+            QQ_CUDA_TRY(cudaMemset(m->ridx, 0, sizeof(int) * nm * std::max(d.n_expert_used, 1)));
+            m->mask = dalloc<uint32_t>(8);
+            QQ_CUDA_TRY(cudaMemset(m->mask, 0, 32));
+            m->ctl = dalloc<int>(2);
+            QQ_CUDA_TRY(cudaMemset(m->ctl, 0, 8));
+            m->suppress = dalloc<int>(1);
+            QQ_CUDA_TRY(cudaMemset(m->suppress, 0xff, 4));
+            m->best = dalloc<unsigned long long>(1);
+            m->dump = dalloc<float>((size_t)d.n_layers * E);
+            QQ_CUDA_TRY(cudaMallocHost(&m->h_small, 4 * sizeof(int)));
+            QQ_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking));
+        } catch (...) {
+            free_model(m);
+            delete m;
+            throw;
+        }
+        *out = m;
+    });
+}
+
+int qq_model_destroy(qq_model* m) {
+    return guard([&] {
+        if (!m) return;
+        DeviceGuard dg(m->ctx->device);
+        cudaStreamSynchronize(m->ctx->stream);
+        free_model(m);
+        delete m;
+    });
+}
+
+int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, int pos0, int want_logits,
+               float* logits_out, int32_t* argmax_out, int suppress_id) {
+    return guard([&] {
+        need(m && token_ids && n_tokens >= 1, "qq_forward: NULL argument or n_tokens < 1");
+        check_seq_pos(m, seq_id, pos0, n_tokens);
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        const bool logits = want_logits != 0;
+        if (logits) set_suppress(m, suppress_id);
+        run_tokens(m, token_ids, n_tokens, seq_id, pos0, logits);
+        if (logits && logits_out)
+            QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, sizeof(float) * m->d.n_vocab, cudaMemcpyDeviceToHost, s));
+        if (logits && argmax_out)
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->ctl, sizeof(int), cudaMemcpyDeviceToHost, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        if (logits && argmax_out) *argmax_out = m->h_small[1];
+    });
+}
+
+int qq_forward_dump(qq_model* m, int32_t token_id, int seq_id, int pos, float* hidden_out) {
+    return guard([&] {
+        need(m && hidden_out, "qq_forward_dump: NULL argument");
+        check_seq_pos(m, seq_id, pos, 1);
+        need(token_id >= 0 && token_id < m->d.n_vocab, "token id out of range");
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        m->h_small[2] = token_id;
+        m->h_small[3] = pos;
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->ctl, m->h_small + 2, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+        enqueue_step(m, seq_id, false, s, true);
+        QQ_CUDA_TRY(cudaMemcpyAsync(hidden_out, m->dump, sizeof(float) * m->d.n_layers * m->d.n_embd,
+                                    cudaMemcpyDeviceToHost, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+    });
+}
+
+int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_steps, int suppress_id,
+                   int32_t* tokens_out) {
+    return guard([&] {
+        need(m != nullptr && n_steps >= 0, "qq_decode_loop: bad argument");
+        check_seq_pos(m, seq_id, pos0, n_steps);
+        need(first_token >= 0 && first_token < m->d.n_vocab, "token id out of range");
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        set_suppress(m, suppress_id);
+        cudaGraphExec_t g = get_graph(m, seq_id, true);
+        m->h_small[2] = first_token;
+        m->h_small[3] = pos0;
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->ctl, m->h_small + 2, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
+        for (int i = 0; i < n_steps; i++) QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+        if (tokens_out && n_steps > 0)
+            QQ_CUDA_TRY(cudaMemcpyAsync(tokens_out, m->trace + (size_t)seq_id * (m->d.max_ctx + 1) + pos0 + 1,
+                                        sizeof(int) * n_steps, cudaMemcpyDeviceToHost, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+    });
+}
+
+int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps, int think_id,
+                int eos_id, int32_t* out_tokens, int* n_out) {
+    return guard([&] {
+        need(m && prompt && n_prompt >= 1 && max_steps >= 0 && n_out, "qq_generate: bad argument");
+        check_seq_pos(m, seq_id, 0, n_prompt + max_steps);
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        // resetState(): conv states to zero; KV positions are rewritten before use
+        QQ_CUDA_TRY(cudaMemsetAsync(m->conv(seq_id, 0), 0, sizeof(float) * m->d.n_layers * 2 * m->d.n_embd, s));
+        set_suppress(m, think_id);
+        run_tokens(m, prompt, n_prompt, seq_id, 0, true);
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->ctl, sizeof(int), cudaMemcpyDeviceToHost, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        int cur = m->h_small[1];
+        int n = 0;
+        if (eos_id < 0) {
+            // no stop token: the whole continuation runs on the device
+            if (max_steps > 0) {
+                std::vector<int32_t> tail(max_steps);
+                cudaGraphExec_t g = get_graph(m, seq_id, true);
+                for (int i = 0; i < max_steps; i++) QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+                QQ_CUDA_TRY(cudaMemcpyAsync(tail.data(), m->trace + (size_t)seq_id * (m->d.max_ctx + 1) + n_prompt + 1,
+                                            sizeof(int) * max_steps, cudaMemcpyDeviceToHost, s));
+                QQ_CUDA_TRY(cudaStreamSynchronize(s));
+                // generated = [cur, tail[0], ..., tail[max_steps-2]] (the last id is sampled, not fed)
+                for (int i = 0; i < max_steps; i++) out_tokens[n++] = i == 0 ? cur : tail[i - 1];
+            }
+        } else {
+            for (int step = 0; step < max_steps; step++) {
+                if (cur == eos_id) break;
+                int32_t t = cur;
+                run_tokens(m, &t, 1, seq_id, n_prompt + step, true);
+                QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->ctl, sizeof(int), cudaMemcpyDeviceToHost, s));
+                QQ_CUDA_TRY(cudaStreamSynchronize(s));
+                out_tokens[n++] = cur;
+                cur = m->h_small[1];
+            }
+        }
+        *n_out = n;
+    });
+}
+
+int qq_reset(qq_model* m, int seq_id) {
+    return guard([&] {
+        need(m != nullptr, "qq_reset: NULL model");
+        need(seq_id >= 0 && seq_id < m->d.n_seq, "seq_id out of range");
+        DeviceGuard dg(m->ctx->device);
+        QQ_CUDA_TRY(cudaMemsetAsync(m->conv(seq_id, 0), 0, sizeof(float) * m->d.n_layers * 2 * m->d.n_embd,
+                                    m->ctx->stream));
+        QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int qq_read_routing(qq_model* m, int moe_layer, float* out) {
+    return guard([&] {
+        need(m && out, "qq_read_routing: NULL argument");
+        need(moe_layer >= 0 && moe_layer < m->n_moe, "qq_read_routing: moe_layer out of range");
+        DeviceGuard dg(m->ctx->device);
+        QQ_CUDA_TRY(cudaMemcpyAsync(out, m->rec + (size_t)moe_layer * m->rec_len, sizeof(float) * m->rec_len,
+                                    cudaMemcpyDeviceToHost, m->ctx->stream));
+        QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int qq_set_expert_mask(qq_model* m, const int32_t* ids, int n) {
+    return guard([&] {
+        need(m != nullptr && n >= 0 && (n == 0 || ids), "qq_set_expert_mask: bad argument");
+        uint32_t bits[8] = {0};
+        for (int i = 0; i < n; i++) {
+            need(ids[i] >= 0 && ids[i] < m->d.n_expert, "qq_set_expert_mask: expert id out of range");
+            bits[ids[i] >> 5] |= 1u << (ids[i] & 31);
+        }
+        DeviceGuard dg(m->ctx->device);
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->mask, bits, sizeof(bits), cudaMemcpyHostToDevice, m->ctx->stream));
+        QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int qq_model_stat(qq_model* m, int what, int64_t* value) {
+    return guard([&] {
+        need(m && value, "qq_model_stat: NULL argument");
+        if (what == QQ_STAT_STEP_KERNELS) {
+            get_graph(m, 0, true);
+            *value = m->step_kernels;
+        } else if (what == QQ_STAT_N_MOE) {
+            *value = m->n_moe;
+        } else {
+            need(false, "qq_model_stat: unknown statistic");
+        }
+    });
+}
+
+int qq_bench_kernel(qq_model* m, int what, int iters, float* ms) {
+    return guard([&] {
+        need(m && ms && iters >= 1, "qq_bench_kernel: bad argument");
+        need(m->n_moe > 0, "qq_bench_kernel: the model has no MoE layer");
+        need(what >= QQ_KERN_MOE_LAYER && what <= QQ_KERN_MOE_DOWN, "qq_bench_kernel: unknown kernel class");
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        const qq_model_desc& d = m->d;
+        const int k = d.n_expert_used;
+        cudaEvent_t e0, e1;
+        QQ_CUDA_TRY(cudaEventCreate(&e0));
+        QQ_CUDA_TRY(cudaEventCreate(&e1));
+        int64_t launches = 0;
+        auto run = [&](bool timed) {
+            for (int it = 0; it < (timed ? iters : 1); it++)
+                for (const Layer& L : m->layers) {
+                    if (!L.moe) continue;
+                    qq3::XStage sf;
+                    sf.x[0] = m->hidden;
+                    sf.K = d.n_embd;
+                    sf.norm_w = L.t[QQ_FFN_NORM]->f32;
+                    sf.eps = d.rms_eps;
+                    float* rec = m->rec + (size_t)L.moe_slot * m->rec_len;
+                    int* idx = m->ridx + (size_t)L.moe_slot * k;
+                    float* w = m->rw + (size_t)L.moe_slot * k;
+                    const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+                    if (what == QQ_KERN_MOE_LAYER)
+                        qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, m->hidden, 1, sf.norm_w, sf.eps, d.n_expert, k,
+                                                rec, idx, w, s);
+                    if (what != QQ_KERN_MOE_DOWN)
+                        qq3::launch_moe_gateup(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], idx, m->mask, k, sf, m->h, s);
+                    if (what != QQ_KERN_MOE_GATEUP)
+                        qq3::launch_moe_down_combine(*L.t[QQ_DOWN_EXPS], idx, w, m->mask, k, m->h, m->hidden, s);
+                    if (timed) launches++;
+                }
+        };
+        run(false);  // warm-up round
+        QQ_CUDA_TRY(cudaEventRecord(e0, s));
+        run(true);
+        QQ_CUDA_TRY(cudaEventRecord(e1, s));
+        QQ_CUDA_TRY(cudaEventSynchronize(e1));
+        float t = 0.f;
+        QQ_CUDA_TRY(cudaEventElapsedTime(&t, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        *ms = t / (float)launches;
+    });
+}
+
+int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
+                 float* out_dev, float* routing_dev) {
+    return guard([&] {
+        need(ctx && layer && x_dev && out_dev && T >= 0, "qq_moe_block: bad argument");
+        const DTensor* router = dt(layer->t[QQ_ROUTER]);
+        const DTensor* gate = dt(layer->t[QQ_GATE_EXPS]);
+        const DTensor* up = dt(layer->t[QQ_UP_EXPS]);
+        const DTensor* down = dt(layer->t[QQ_DOWN_EXPS]);
+        const DTensor* bias = dt(layer->t[QQ_EXP_BIAS]);
+        need(router && gate && up && down, "qq_moe_block: router and expert tensors are required");
+        QQ_CHECK(top_k == 4 && n_expert >= 4 && n_expert <= 32, QQ_ERR_UNSUPPORTED,
+                 "qq_moe_block: this build routes top-4 of <= 32 experts");
+        const int64_t K = router->ne[0], F = gate->ne[1];
+        check_shape(router, QQ_TYPE_Q8_0, K, n_expert, 1, "ffn_gate_inp.weight");
+        check_shape(gate, QQ_TYPE_Q8_0, K, F, n_expert, "ffn_gate_exps.weight");
+        check_shape(up, QQ_TYPE_Q8_0, K, F, n_expert, "ffn_up_exps.weight");
+        check_shape(down, QQ_TYPE_Q8_0, F, K, n_expert, "ffn_down_exps.weight");
+        if (bias) check_shape(bias, QQ_TYPE_F32, n_expert, 1, 1, "exp_probs_b.bias");
+        if (T == 0) return;
+        DeviceGuard dg(ctx->device);
+        cudaStream_t s = ctx->stream;
+        const int rec_len = 2 * top_k + n_expert;
+        // scratch: idx [T][k] | w [T][k] | record [T][rec_len] (unless the caller wants it) | h [k][F]
+        const size_t b_idx = (size_t)T * top_k * 4, b_w = b_idx, b_rec = routing_dev ? 0 : (size_t)T * rec_len * 4;
+        const size_t b_h = (size_t)top_k * F * 4;
+        auto align = [](size_t v) { return (v + 255) & ~(size_t)255; };
+        char* base = static_cast<char*>(ctx_scratch(ctx, align(b_idx) + align(b_w) + align(b_rec) + align(b_h)));
+        int* idx = reinterpret_cast<int*>(base);
+        float* w = reinterpret_cast<float*>(base + align(b_idx));
+        float* rec = routing_dev ? routing_dev : reinterpret_cast<float*>(base + align(b_idx) + align(b_w));
+        float* h = reinterpret_cast<float*>(base + align(b_idx) + align(b_w) + align(b_rec));
+        qq3::launch_lfm2_router(*router, bias ? bias->f32 : nullptr, x_dev, T, nullptr, 0.f, n_expert, top_k, rec, idx,
+                                w, s);
+        QQ_CUDA_TRY(cudaMemsetAsync(out_dev, 0, sizeof(float) * (size_t)T * K, s));
+        for (int t = 0; t < T; t++) {
+            qq3::XStage st;
+            st.x[0] = x_dev + (size_t)t * K;
+            st.K = (int)K;
+            qq3::launch_moe_gateup(*gate, *up, idx + (size_t)t * top_k, nullptr, top_k, st, h, s);
+            qq3::launch_moe_down_combine(*down, idx + (size_t)t * top_k, w + (size_t)t * top_k, nullptr, top_k, h,
+                                         out_dev + (size_t)t * K, s);
+        }
+    });
+}
+
+}  // extern "C"

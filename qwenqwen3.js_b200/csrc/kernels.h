@@ -1,0 +1,79 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (internal to libqq3cuda.so).
+#pragma once
+#include "common.cuh"
+
+namespace qq3 {
+
+// Input staging of a GEMV launch: nvec input vectors of length K (K % 32 == 0) are copied
+// into shared memory once per CTA.  With norm_w set (nvec == 1) the copy is the
+// RMSNorm of x (tensor.js:103-114) so the norm is fused into the consumer.
+struct XStage {
+    const float* x[8] = {nullptr};
+    int nvec = 1;
+    int K = 0;
+    const float* norm_w = nullptr;
+    float eps = 0.f;
+};
+
+// y[i] (+)= W[row0 + i] . x for i < n
+void launch_gemv_rows(const DTensor& W, int64_t row0, int64_t n, const XStage& st, float* y, bool residual,
+                      cudaStream_t s);
+// Q|K|V projections into one buffer qkv = [wq rows | wk rows | wv rows]
+void launch_gemv_qkv(const DTensor& wq, const DTensor& wk, const DTensor& wv, const XStage& st, float* qkv,
+                     cudaStream_t s);
+// h[j] = silu(gate[j] . x) * (up[j] . x)
+void launch_gemv_swiglu(const DTensor& gate, const DTensor& up, const XStage& st, float* h, cudaStream_t s);
+// LFM2 short-conv: in_proj rows (j, E+j, 2E+j) -> B, C, x; depthwise causal conv with the
+// rolling state (updated in place); y[j] = C * conv_out (lfm2-engine.js:282-321)
+void launch_gemv_conv(const DTensor& in_proj, const float* conv_w, float* state, const XStage& st, float* y,
+                      cudaStream_t s);
+// logits = W . x and a fused first-max argmax into *best (packed key, see argmax_key).
+// *suppress_dev >= 0 is excluded from the argmax (thinking suppression, tensor.js:247-248).
+void launch_gemv_logits_argmax(const DTensor& W, const XStage& st, float* logits, unsigned long long* best,
+                               const int* suppress_dev, cudaStream_t s);
+// MoE expert gate/up for one token: h[k][j] = silu(gate_e . x) * (up_e . x), e = idx[k]
+void launch_moe_gateup(const DTensor& gate_exps, const DTensor& up_exps, const int* idx, const uint32_t* mask,
+                       int top_k, const XStage& st, float* h, cudaStream_t s);
+// MoE down + weighted combine + residual: hidden[j] += sum_k w[k] * (down_e[k] . h[k])
+void launch_moe_down_combine(const DTensor& down_exps, const int* idx, const float* w, const uint32_t* mask,
+                             int top_k, const float* h, float* hidden, cudaStream_t s);
+
+// ---- misc kernels (kernels_misc.cu) ----
+void launch_repack_q8(const uint8_t* raw, int64_t n_blocks, int8_t* qs, __half* d, cudaStream_t s);
+void launch_dequant_q8(const DTensor& W, float* out, cudaStream_t s);
+// hidden = dequantised row `token` of the embedding (tensor.js:56-77); token read from device
+void launch_embed(const DTensor& E, const int* token, float* hidden, unsigned long long* argmax_reset,
+                  cudaStream_t s);
+// in place RMSNorm over n_rows rows of length n (tensor.js:103-114 / 117-129)
+void launch_rmsnorm(float* x, int64_t n_rows, int n, const float* w, float eps, float* y, cudaStream_t s);
+// ctl = [token, pos]: token <- argmax, pos <- pos + 1, trace[pos] <- token (device-driven decode)
+void launch_argmax_finish(const unsigned long long* best, int* ctl, int* trace, cudaStream_t s);
+
+// ---- attention (kernels_attn.cu) ----
+struct AttnArgs {
+    const float* qkv;      // [n_head*hd | n_kv*hd | n_kv*hd] raw projections (pre norm/rope)
+    const float* q_norm;   // [hd]
+    const float* k_norm;   // [hd]
+    const float* rope_cs;  // [max_ctx][hd/2][2] cos, sin
+    float* k_cache;        // [n_kv][max_ctx][hd] for this layer (and sequence)
+    float* v_cache;
+    float* out;            // [n_head*hd]
+    float* part;           // scratch: [n_head][n_split][hd + 2]
+    unsigned int* counter; // scratch: [n_kv] arrival counters (self-resetting)
+    const int* pos;        // device position
+    int n_head, n_kv, hd, max_ctx, n_split;
+    float eps;
+};
+void launch_attention_decode(const AttnArgs& a, cudaStream_t s);
+int attention_splits(int max_ctx);
+
+// ---- MoE routing (kernels_moe.cu) ----
+// LFM2 sigmoid router for T tokens (lfm2-engine.js:417-447).  x: [T][K] hidden rows,
+// RMS-normalised in the prologue when norm_w is set.  Outputs per token t:
+// record[t] = [ids | normalised weights | sigmoid probs] (2k+E floats), idx[t][k], w[t][k].
+void launch_lfm2_router(const DTensor& router, const float* bias, const float* x, int T, const float* norm_w,
+                        float eps, int n_expert, int top_k, float* record, int* idx, float* w, cudaStream_t s);
+
+int num_sms();
+
+}  // namespace qq3

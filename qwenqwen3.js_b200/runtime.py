@@ -1,0 +1,315 @@
+"""ctypes binding of libqq3cuda.so (declared in include/qq3.h).
+
+This is the Python twin of the N-API addon a Node host would load: it calls the C ABI
+with plain pointers and sizes.  There is no CPU fallback -- if the library or a B200 is
+missing, opening a context raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+from . import build as _build
+
+QQ_OK = 0
+QQ_ERR_INVALID = -1
+QQ_ERR_CUDA = -2
+QQ_ERR_OOM = -3
+QQ_ERR_UNSUPPORTED = -4
+
+QQ_TYPE_F32 = 0
+QQ_TYPE_Q8_0 = 8
+
+QQ_ARCH_QWEN3 = 0
+QQ_ARCH_LFM2 = 1
+
+# per-layer tensor slots (include/qq3.h)
+SLOTS = [
+    "attn_norm", "ffn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn_q_norm", "attn_k_norm",
+    "shortconv.conv", "shortconv.in_proj", "shortconv.out_proj", "ffn_gate", "ffn_up", "ffn_down",
+    "ffn_gate_inp", "ffn_gate_exps", "ffn_up_exps", "ffn_down_exps", "exp_probs_b",
+]
+SLOT_COUNT = len(SLOTS)
+SLOT = {name: i for i, name in enumerate(SLOTS)}
+
+# GGUF tensor name of each slot for layer N (qwen3-engine.js:46-75, lfm2-engine.js:88-140)
+SLOT_TENSOR_NAMES = {
+    "attn_norm": "attn_norm.weight", "ffn_norm": "ffn_norm.weight", "attn_q": "attn_q.weight",
+    "attn_k": "attn_k.weight", "attn_v": "attn_v.weight", "attn_output": "attn_output.weight",
+    "attn_q_norm": "attn_q_norm.weight", "attn_k_norm": "attn_k_norm.weight",
+    "shortconv.conv": "shortconv.conv.weight", "shortconv.in_proj": "shortconv.in_proj.weight",
+    "shortconv.out_proj": "shortconv.out_proj.weight", "ffn_gate": "ffn_gate.weight", "ffn_up": "ffn_up.weight",
+    "ffn_down": "ffn_down.weight", "ffn_gate_inp": "ffn_gate_inp.weight", "ffn_gate_exps": "ffn_gate_exps.weight",
+    "ffn_up_exps": "ffn_up_exps.weight", "ffn_down_exps": "ffn_down_exps.weight", "exp_probs_b": "exp_probs_b.bias",
+}
+
+
+class QQError(RuntimeError):
+    """A failed qq_* call: .code is the QQ_ERR_* status, the message is qq_last_error()."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class LayerDesc(C.Structure):
+    _fields_ = [("is_attn", C.c_int32), ("is_moe", C.c_int32), ("t", C.c_void_p * SLOT_COUNT)]
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [
+        ("arch", C.c_int32), ("n_layers", C.c_int32), ("n_embd", C.c_int32), ("n_head", C.c_int32),
+        ("n_head_kv", C.c_int32), ("head_dim", C.c_int32), ("n_vocab", C.c_int32), ("n_expert", C.c_int32),
+        ("n_expert_used", C.c_int32), ("max_ctx", C.c_int32), ("n_seq", C.c_int32), ("rms_eps", C.c_float),
+        ("rope_base", C.c_double), ("tok_embd", C.c_void_p), ("output_norm", C.c_void_p), ("output", C.c_void_p),
+        ("layers", C.POINTER(LayerDesc)),
+    ]
+
+
+_P = C.c_void_p
+_I = C.c_int
+_I64 = C.c_int64
+_SIGS = {
+    "qq_last_error": (C.c_char_p, []),
+    "qq_init": (_I, [C.POINTER(_I), _I, C.POINTER(_P)]),
+    "qq_destroy": (_I, [_P]),
+    "qq_set_stream": (_I, [_P, _P]),
+    "qq_synchronize": (_I, [_P]),
+    "qq_upload_tensor": (_I, [_P, _P, C.c_size_t, _I, C.POINTER(_I64), _I, C.POINTER(_P)]),
+    "qq_free_tensor": (_I, [_P]),
+    "qq_tensor_info": (_I, [_P, C.POINTER(_I), C.POINTER(_I64), C.POINTER(_I)]),
+    "qq_dequant": (_I, [_P, _P]),
+    "qq_q8_matmul": (_I, [_P, _P, _P, _I, _P]),
+    "qq_rmsnorm": (_I, [_P, _P, _I64, _I, _P, C.c_float, _P]),
+    "qq_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
+    "qq_model_destroy": (_I, [_P]),
+    "qq_forward": (_I, [_P, C.POINTER(C.c_int32), _I, _I, _I, _I, _P, C.POINTER(C.c_int32), _I]),
+    "qq_generate": (_I, [_P, _I, C.POINTER(C.c_int32), _I, _I, _I, _I, C.POINTER(C.c_int32), C.POINTER(_I)]),
+    "qq_reset": (_I, [_P, _I]),
+    "qq_read_routing": (_I, [_P, _I, _P]),
+    "qq_set_expert_mask": (_I, [_P, C.POINTER(C.c_int32), _I]),
+    "qq_forward_dump": (_I, [_P, C.c_int32, _I, _I, _P]),
+    "qq_decode_loop": (_I, [_P, _I, _I, _I, _I, _I, C.POINTER(C.c_int32)]),
+    "qq_moe_block": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
+    "qq_model_stat": (_I, [_P, _I, C.POINTER(_I64)]),
+    "qq_bench_kernel": (_I, [_P, _I, _I, C.POINTER(C.c_float)]),
+}
+
+QQ_STAT_STEP_KERNELS = 0
+QQ_STAT_N_MOE = 1
+QQ_KERN_MOE_LAYER = 0
+QQ_KERN_MOE_GATEUP = 1
+QQ_KERN_MOE_DOWN = 2
+
+_lib = None
+
+
+def library_path() -> Path:
+    return _build.CUDA_LIB
+
+
+def load(build_if_missing: bool = False) -> C.CDLL:
+    """Load libqq3cuda.so (raises if it is absent: there is no fallback path)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not path.exists():
+        if not build_if_missing:
+            raise RuntimeError(f"{path} is missing; run qwenqwen3.js_b200/build.py (no CPU fallback exists)")
+        _build.build_cuda()
+    lib = C.CDLL(str(path))
+    for name, (res, args) in _SIGS.items():
+        f = getattr(lib, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def check(rc: int) -> None:
+    if rc != QQ_OK:
+        msg = load().qq_last_error().decode("utf-8", "replace")
+        raise QQError(rc, msg)
+
+
+def _ptr(a) -> int | None:
+    """Device pointer of a torch tensor / int, or host pointer of a numpy array."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    raise TypeError(f"cannot take a pointer of {type(a)}")
+
+
+class Context:
+    """qq_ctx on one device."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        dev = (C.c_int * 1)(device)
+        h = C.c_void_p()
+        check(self.lib.qq_init(dev, 1, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.h:
+            check(self.lib.qq_destroy(self.h))
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, cuda_stream: int | None) -> None:
+        check(self.lib.qq_set_stream(self.h, cuda_stream))
+
+    def synchronize(self) -> None:
+        check(self.lib.qq_synchronize(self.h))
+
+    def upload(self, raw: np.ndarray, ggml_type: int, ne) -> "Tensor":
+        raw = np.ascontiguousarray(raw)
+        ne = list(int(v) for v in ne)
+        arr = (C.c_int64 * len(ne))(*ne)
+        h = C.c_void_p()
+        check(self.lib.qq_upload_tensor(self.h, raw.ctypes.data, raw.nbytes, ggml_type, arr, len(ne), C.byref(h)))
+        return Tensor(self, h, ggml_type, ne)
+
+    def q8_matmul(self, W: "Tensor", x_dev, M: int, y_dev) -> None:
+        check(self.lib.qq_q8_matmul(self.h, W.h, _ptr(x_dev), M, _ptr(y_dev)))
+
+    def rmsnorm(self, x_dev, n_rows: int, n: int, w: "Tensor", eps: float, y_dev) -> None:
+        check(self.lib.qq_rmsnorm(self.h, _ptr(x_dev), n_rows, n, w.h, eps, _ptr(y_dev)))
+
+    def moe_block(self, layer: LayerDesc, n_expert: int, top_k: int, x_dev, T: int, out_dev, routing_dev=None) -> None:
+        check(self.lib.qq_moe_block(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(out_dev),
+                                    _ptr(routing_dev)))
+
+
+class Tensor:
+    """An uploaded tensor (qq_tensor)."""
+
+    def __init__(self, ctx: Context, h, ggml_type: int, ne):
+        self.ctx = ctx
+        self.h = h
+        self.type = ggml_type
+        self.ne = list(ne)
+
+    @property
+    def numel(self) -> int:
+        return int(np.prod(self.ne))
+
+    def info(self):
+        t = C.c_int()
+        ne = (C.c_int64 * 4)()
+        nd = C.c_int()
+        check(self.ctx.lib.qq_tensor_info(self.h, C.byref(t), ne, C.byref(nd)))
+        return t.value, list(ne)[: nd.value]
+
+    def dequant(self, out_dev) -> None:
+        check(self.ctx.lib.qq_dequant(self.h, _ptr(out_dev)))
+
+    def free(self) -> None:
+        if self.h:
+            check(self.ctx.lib.qq_free_tensor(self.h))
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            if self.h and self.ctx.h:
+                self.free()
+        except Exception:
+            pass
+
+
+class Model:
+    """qq_model: an engine over uploaded tensors."""
+
+    def __init__(self, ctx: Context, desc: ModelDesc, layers_arr, keepalive):
+        self.ctx = ctx
+        self.desc = desc
+        self._layers = layers_arr
+        self._keep = keepalive
+        h = C.c_void_p()
+        check(ctx.lib.qq_model_create(ctx.h, C.byref(desc), C.byref(h)))
+        self.h = h
+        self.n_vocab = desc.n_vocab
+        self.n_layers = desc.n_layers
+        self.n_embd = desc.n_embd
+
+    def close(self) -> None:
+        if self.h:
+            check(self.ctx.lib.qq_model_destroy(self.h))
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            if self.h and self.ctx.h:
+                self.close()
+        except Exception:
+            pass
+
+    def forward(self, tokens, seq: int = 0, pos0: int = 0, want_logits: bool = True, logits: bool = True,
+                suppress_id: int = -1):
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        out = np.empty(self.n_vocab, dtype=np.float32) if (want_logits and logits) else None
+        am = C.c_int32(-1)
+        check(self.ctx.lib.qq_forward(self.h, toks.ctypes.data_as(C.POINTER(C.c_int32)), len(toks), seq, pos0,
+                                      1 if want_logits else 0, _ptr(out), C.byref(am) if want_logits else None,
+                                      suppress_id))
+        return out, am.value
+
+    def forward_dump(self, token: int, seq: int, pos: int) -> np.ndarray:
+        out = np.empty((self.n_layers, self.n_embd), dtype=np.float32)
+        check(self.ctx.lib.qq_forward_dump(self.h, token, seq, pos, out.ctypes.data))
+        return out
+
+    def decode_loop(self, first_token: int, pos0: int, n_steps: int, seq: int = 0, suppress_id: int = -1,
+                    want_tokens: bool = True):
+        out = np.empty(max(n_steps, 1), dtype=np.int32) if want_tokens else None
+        check(self.ctx.lib.qq_decode_loop(self.h, seq, first_token, pos0, n_steps, suppress_id,
+                                          out.ctypes.data_as(C.POINTER(C.c_int32)) if want_tokens else None))
+        return out[:n_steps] if want_tokens else None
+
+    def generate(self, prompt, max_steps: int, think_id: int = -1, eos_id: int = -1, seq: int = 0) -> np.ndarray:
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))
+        out = np.empty(max(max_steps, 1), dtype=np.int32)
+        n = C.c_int(0)
+        check(self.ctx.lib.qq_generate(self.h, seq, p.ctypes.data_as(C.POINTER(C.c_int32)), len(p), max_steps,
+                                       think_id, eos_id, out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(n)))
+        return out[: n.value]
+
+    def reset(self, seq: int = 0) -> None:
+        check(self.ctx.lib.qq_reset(self.h, seq))
+
+    def read_routing(self, moe_layer: int, rec_len: int) -> np.ndarray:
+        out = np.empty(rec_len, dtype=np.float32)
+        check(self.ctx.lib.qq_read_routing(self.h, moe_layer, out.ctypes.data))
+        return out
+
+    def stat(self, what: int) -> int:
+        v = C.c_int64(0)
+        check(self.ctx.lib.qq_model_stat(self.h, what, C.byref(v)))
+        return v.value
+
+    def bench_kernel(self, what: int, iters: int) -> float:
+        ms = C.c_float(0)
+        check(self.ctx.lib.qq_bench_kernel(self.h, what, iters, C.byref(ms)))
+        return ms.value
+
+    def set_expert_mask(self, ids) -> None:
+        ids = np.ascontiguousarray(np.asarray(sorted(ids), dtype=np.int32))
+        check(self.ctx.lib.qq_set_expert_mask(self.h, ids.ctypes.data_as(C.POINTER(C.c_int32)), len(ids)))

@@ -1,0 +1,143 @@
+"""Op-level parity of the CUDA path (through the C ABI) against the CPU oracle.
+
+Tolerances: dequantised weights are bit-exact; floating-point outputs must be within the
+north-star bar of 1e-2 max relative error (max|got-want| / max|want|), and the f32-vs-f64
+accumulation gap is additionally held to TIGHT so that a dropped block or row shows up.
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2      # north-star bar for activations / logits
+TIGHT = 2e-5    # f32 accumulation vs the oracle's f64 on a single matmul
+
+SWEEP = [(1024, 1024), (3072, 1024), (1024, 3072), (151936, 1024), (7168, 2048)]
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+
+    assert t.cuda.is_available()
+    return t
+
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("N,K", SWEEP + [(1792, 2048 * 32), (96, 32)])
+def test_dequant_bit_exact(qq3, orc, gpu_ctx, torch, N, K):
+    raw = qq3.synth.q8_0_blocks(N * K, seed=100 + N + K, mode=1)
+    W = gpu_ctx.upload(raw, 8, [K, N])
+    out = torch.empty(N * K, dtype=torch.float32, device="cuda")
+    W.dequant(out)
+    gpu_ctx.synchronize()
+    want = orc.dequant(raw, 8, [K, N])
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    W.free()
+
+
+@pytest.mark.parametrize("N,K", SWEEP)
+@pytest.mark.parametrize("M", [1, 16])
+def test_q8_matmul_vs_oracle(qq3, orc, gpu_ctx, torch, N, K, M):
+    orc.set_threads(8)
+    raw = qq3.synth.q8_0_blocks(N * K, seed=7 + N * 3 + K, mode=1)
+    x = qq3.synth.normal_f32(M * K, seed=M + N).reshape(M, K)
+    W = gpu_ctx.upload(raw, 8, [K, N])
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    xd = _dev(torch, x)
+    torch.cuda.synchronize()
+    gpu_ctx.q8_matmul(W, xd, M, y)
+    gpu_ctx.synchronize()
+    got = y.cpu().numpy()
+    want = orc.matmul(raw, 8, [K, N], x)
+    for r in range(M):
+        e = rel_err(got[r], want[r])
+        assert e < TIGHT, f"row {r}: rel err {e:.3e}"
+    W.free()
+
+
+@pytest.mark.parametrize("M", [512, 4096])
+def test_q8_matmul_large_m_sampled_rows(qq3, orc, gpu_ctx, torch, M):
+    """Large-M sweep points: every row on the GPU, a seeded sample of rows on the oracle."""
+    orc.set_threads(8)
+    N, K = 7168, 2048
+    raw = qq3.synth.q8_0_blocks(N * K, seed=900 + M, mode=1)
+    x = qq3.synth.normal_f32(M * K, seed=M).reshape(M, K)
+    W = gpu_ctx.upload(raw, 8, [K, N])
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    gpu_ctx.q8_matmul(W, _dev(torch, x), M, y)
+    gpu_ctx.synchronize()
+    got = y.cpu().numpy()
+    rows = np.unique(np.concatenate([[0, M - 1], qq3.synth.uniform_tokens(6, M, M)]))
+    want = orc.matmul(raw, 8, [K, N], x[rows])
+    for i, r in enumerate(rows):
+        assert rel_err(got[r], want[i]) < TIGHT
+    assert np.isfinite(got).all()
+    W.free()
+
+
+def test_rmsnorm_vs_oracle(qq3, orc, gpu_ctx, torch):
+    n, rows = 2048, 5
+    x = qq3.synth.normal_f32(n * rows, seed=3).reshape(rows, n) * 3
+    w = qq3.synth.normal_f32(n, seed=4)
+    wt = gpu_ctx.upload(w.view(np.uint8), 0, [n])
+    xd = _dev(torch, x)
+    yd = torch.empty_like(xd)
+    gpu_ctx.rmsnorm(xd, rows, n, wt, 1e-5, yd)
+    gpu_ctx.synchronize()
+    want = orc.rmsnorm(x, w, float(np.float32(1e-5)))
+    assert rel_err(yd.cpu().numpy(), want) < 1e-6
+
+
+def _moe_layer(qq3, E=2048, F=1792, NE=32, seed=5):
+    spec = qq3.synth.lfm2_8b_a1b(seed=seed)
+    names = [f"blk.2.{n}" for n in ("ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                    "ffn_down_exps.weight", "exp_probs_b.bias")]
+    t = qq3.synth.build_tensors(spec, only=set(names))
+    return {k.split(".", 2)[2]: v for k, v in t.items()}
+
+
+def _upload_layer(qq3, gpu_ctx, tensors):
+    rt = qq3.runtime
+    L = rt.LayerDesc()
+    keep = []
+    for name, (t, ne, raw) in tensors.items():
+        slot = rt.SLOT[[s for s, n in rt.SLOT_TENSOR_NAMES.items() if n == name][0]]
+        h = gpu_ctx.upload(raw, t, ne)
+        keep.append(h)
+        L.t[slot] = h.h.value
+    L.is_moe = 1
+    return L, keep
+
+
+@pytest.mark.parametrize("T", [1, 64])
+def test_moe_block_vs_oracle(qq3, orc, gpu_ctx, torch, T):
+    orc.set_threads(8)
+    tensors = _moe_layer(qq3)
+    L, keep = _upload_layer(qq3, gpu_ctx, tensors)
+    x = qq3.synth.normal_f32(T * 2048, seed=T).reshape(T, 2048)
+    out = torch.empty((T, 2048), dtype=torch.float32, device="cuda")
+    rec = torch.empty((T, 2 * 4 + 32), dtype=torch.float32, device="cuda")
+    gpu_ctx.moe_block(L, 32, 4, _dev(torch, x), T, out, rec)
+    gpu_ctx.synchronize()
+    want, want_rec = orc.lfm2_moe(tensors, 2048, 32, 4, x)
+    got_rec = rec.cpu().numpy()
+    # router: identical top-k ids except near-ties (selection-score gap < 1e-5)
+    sel_ids_ok = np.array_equal(got_rec[:, :4], want_rec[:, :4])
+    if not sel_ids_ok:
+        bias = tensors["exp_probs_b.bias"][2].view(np.float32)
+        for t in range(T):
+            if not np.array_equal(got_rec[t, :4], want_rec[t, :4]):
+                s = np.sort(want_rec[t, 8:] + bias)[::-1]
+                assert abs(s[3] - s[4]) < 1e-5, f"token {t}: top-k differs without a near-tie"
+    assert rel_err(got_rec[:, 8:], want_rec[:, 8:]) < 1e-6  # sigmoid probs
+    assert rel_err(got_rec[:, 4:8], want_rec[:, 4:8]) < 1e-5  # normalised weights
+    for t in range(T):
+        assert rel_err(out.cpu().numpy()[t], want[t]) < TOL
+    for k in keep:
+        k.free()

@@ -1,0 +1,114 @@
+"""Host-side logic and the C ABI boundary, without a GPU."""
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_library_exports_every_declared_symbol(qq3):
+    qq3.build.build_cuda()
+    header = (ROOT / "include" / "qq3.h").read_text()
+    declared = sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(qq_\w+)\s*\(", header, re.M)))
+    assert len(declared) >= 20
+    lib = qq3.runtime.load()
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert sorted(qq3.runtime.exported_symbols()) == declared
+
+
+def test_init_without_gpu_fails_loudly(qq3):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(qq3.runtime.QQError) as e:
+        qq3.runtime.Context(0)
+    assert e.value.code in (qq3.runtime.QQ_ERR_CUDA, qq3.runtime.QQ_ERR_INVALID)
+    assert str(e.value)
+
+
+def test_gguf_round_trip(qq3, tmp_path):
+    spec = qq3.synth.tiny_lfm2(seed=2)
+    path = tmp_path / "m.gguf"
+    qq3.synth.write_gguf(spec, path)
+    r = qq3.gguf.GGUFReader.fromFile(path)
+    arch = r.getArch()
+    assert arch["architecture"] == "lfm2moe" and arch["blockCount"] == spec.n_layers
+    assert arch["headCountKV"] == spec.n_head_kv  # per-layer array, max of the non-zero entries
+    assert r.getKeyValue("general.alignment") == 32
+    mem = qq3.synth.build_tensors(spec)
+    for name, (t, ne, raw) in mem.items():
+        m = r.getTensorMetaByName(name)
+        assert m.type == t and m.shape == ne
+        assert m.offset % 32 == 0 and m.nbytes % 256 == 0
+        assert np.array_equal(m.raw(), raw)
+    assert len(r.getKeyValue("tokenizer.ggml.tokens")) == spec.n_vocab
+    assert r.getKeyValue("tokenizer.ggml.merges") == []
+
+
+def test_synth_is_deterministic_and_sliceable(qq3):
+    a = qq3.synth.q8_0_blocks(32 * 100, seed=9)
+    b = qq3.synth.q8_0_blocks(32 * 100, seed=9)
+    assert np.array_equal(a, b)
+    c = qq3.synth.q8_0_blocks(32 * 40, seed=9, block0=60)
+    assert np.array_equal(a[60 * 34:], c)
+    q = a.reshape(-1, 34)[:, 2:].view(np.int8)
+    assert q.min() >= -127 and q.max() <= 127
+    d = a.reshape(-1, 34)[:, :2].copy().view(np.float16).astype(np.float64)
+    assert np.all(d > 0) and abs(d.mean() - 0.02 / 127) < 0.1 * 0.02 / 127
+
+
+def test_f16_conversion_matches_numpy(qq3):
+    vals = np.concatenate([qq3.synth.normal_f32(5000, seed=1) * 1e-3, qq3.synth.normal_f32(5000, seed=2) * 1e-6,
+                           np.array([65504, 65519, 65520, 1e-8, 3e-8, 6e-8, 5.96e-8, 2.98e-8, 0.0, -0.0], np.float32),
+                           qq3.synth.normal_f32(5000, seed=3) * 3e4])
+    ours = np.array([qq3.synth.f32_to_f16_bits(float(v)) for v in vals], dtype=np.uint16)
+    with np.errstate(over="ignore"):
+        want = vals.astype(np.float16).view(np.uint16)
+    assert np.array_equal(ours, want)
+
+
+def test_zipf_bias_calibration(qq3):
+    spec = qq3.synth.lfm2_8b_a1b(seed=5)
+    t = qq3.synth.build_tensors(spec, only={"blk.2.ffn_gate_inp.weight", "blk.2.exp_probs_b.bias"})
+    alpha = spec.extra["zipf_alpha"]["blk.2.exp_probs_b.bias"]
+    assert 0.0 < alpha < 0.5
+    bias = t["blk.2.exp_probs_b.bias"][2].view(np.float32)
+    assert bias.shape == (32,) and np.all(bias <= 0)
+
+
+def test_engine_hparams_mirror_js(qq3):
+    """Lfm2Engine / Qwen3Engine constructor derivations, without binding a device."""
+    spec = qq3.synth.lfm2_8b_a1b()
+    g = qq3.synth.MemoryGGUF(spec, {n: (t, ne, np.zeros(1, np.uint8)) for n, t, ne in qq3.synth.tensor_specs(spec)})
+    e = object.__new__(qq3.Lfm2CudaEngine)
+    e.gguf = g
+    e._read_hparams(g)
+    assert (e.nLayers, e.nEmb, e.nHeads, e.nHeadKV, e.headDim) == (24, 2048, 32, 8, 64)
+    assert (e.nExperts, e.nExpertsUsed, e.nVocab, e.maxCtx) == (32, 4, 65536, 4096)
+    assert [i for i in range(24) if e._is_attn(i)] == list(qq3.synth.LFM2_8B_ATTN_LAYERS)
+    assert [i for i in range(24) if e._is_moe(i)] == list(range(2, 24))
+    assert abs(e.eps - 1e-5) < 1e-12 and e.ropeFreqBase == 1e6
+    spec = qq3.synth.qwen3_0p6b()
+    g = qq3.synth.MemoryGGUF(spec, {n: (t, ne, np.zeros(1, np.uint8)) for n, t, ne in qq3.synth.tensor_specs(spec)})
+    q = object.__new__(qq3.Qwen3CudaEngine)
+    q._read_hparams(g)
+    assert (q.nLayers, q.nEmb, q.nHeads, q.nHeadKV, q.headDim, q.nVocab, q.maxCtx) == (28, 1024, 16, 8, 128, 151936, 4096)
+
+
+def test_host_sampling_mirrors_tensor_js(qq3):
+    from qq3.engine import sample_top_p_top_k, sample_with_think_control
+
+    logits = np.array([0.1, 2.0, 2.0, -1.0, 0.5], np.float32)
+    assert sample_with_think_control(logits.copy(), 0.0, 0.9, 40, dict(mode="full", thinkId=1, endThinkId=4)) == 1
+    assert sample_with_think_control(logits.copy(), 0.0, 0.9, 40, dict(mode="suppress", thinkId=1, endThinkId=4)) == 2
+    # 'shorten': </think> forced when fewer than topK logits beat it
+    assert sample_with_think_control(logits.copy(), 0.0, 0.9, 3, dict(mode="shorten", thinkId=1, endThinkId=4,
+                                                                       thinkingDone=False)) == 4
+    # top-k = 1: a draw inside the kept mass returns the most probable id; the JS does not
+    # renormalise after the cut, so a draw above it falls through to the last sorted id
+    assert sample_top_p_top_k(logits, 0.7, 0.9, 1, rng=lambda: 0.1) == 1
+    assert sample_top_p_top_k(logits, 0.7, 0.9, 1, rng=lambda: 0.999) == 3
