@@ -246,9 +246,12 @@ class OracleModel:
         self.n_moe = lib().orc_n_moe_layers(h)
 
     def __del__(self):
-        if getattr(self, "h", None):
-            lib().orc_model_destroy(self.h)
-            self.h = None
+        try:
+            if getattr(self, "h", None) and _lib is not None:
+                _lib.orc_model_destroy(self.h)
+        except Exception:
+            pass
+        self.h = None
 
     def reset(self):
         lib().orc_reset(self.h)

@@ -417,7 +417,10 @@ int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type
         if (ggml_type == QQ_TYPE_F32) {
             need(nbytes >= (size_t)n * 4, "qq_upload_tensor: buffer shorter than ne0*ne1*... floats");
             t.f32 = dalloc<float>((size_t)n);
-            QQ_CUDA_TRY(cudaMemcpy(t.f32, host, (size_t)n * 4, cudaMemcpyHostToDevice));
+            // ordered on the context stream: a pageable cudaMemcpy may return before its DMA
+            // lands and only orders against the legacy stream, not this non-blocking one
+            QQ_CUDA_TRY(cudaMemcpyAsync(t.f32, host, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+            QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
         } else {
             need(t.ne[0] % 32 == 0, "qq_upload_tensor: Q8_0 needs ne[0] % 32 == 0");
             const int64_t nb = n / 32;
@@ -426,7 +429,7 @@ int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type
             try {
                 t.qs = dalloc<int8_t>((size_t)n);
                 t.d = dalloc<__half>((size_t)nb);
-                QQ_CUDA_TRY(cudaMemcpy(raw, host, (size_t)nb * 34, cudaMemcpyHostToDevice));
+                QQ_CUDA_TRY(cudaMemcpyAsync(raw, host, (size_t)nb * 34, cudaMemcpyHostToDevice, ctx->stream));
                 qq3::launch_repack_q8(raw, nb, t.qs, t.d, ctx->stream);
                 QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
             } catch (...) {
@@ -589,11 +592,11 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
             const size_t kv = (size_t)d.n_seq * std::max(m->n_attn, 1) * nkv * d.max_ctx;
             m->k_cache = dalloc<float>(kv);
             m->v_cache = dalloc<float>(kv);
-            QQ_CUDA_TRY(cudaMemset(m->k_cache, 0, kv * 4));
-            QQ_CUDA_TRY(cudaMemset(m->v_cache, 0, kv * 4));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->k_cache, 0, kv * 4, ctx->stream));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->v_cache, 0, kv * 4, ctx->stream));
             const size_t cs = (size_t)d.n_seq * d.n_layers * 2 * E;
             m->conv_state = dalloc<float>(cs);
-            QQ_CUDA_TRY(cudaMemset(m->conv_state, 0, cs * 4));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->conv_state, 0, cs * 4, ctx->stream));
             m->trace = dalloc<int>((size_t)d.n_seq * (d.max_ctx + 1));
             // RoPE table: cos/sin of position * base^(-i/half) in double (tensor.js:137-140)
             {
@@ -607,27 +610,29 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                         tab[(size_t)p * hd + 2 * i + 1] = (float)std::sin(th);
                     }
                 m->rope_cs = dalloc<float>(tab.size());
-                QQ_CUDA_TRY(cudaMemcpy(m->rope_cs, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+                QQ_CUDA_TRY(cudaMemcpyAsync(m->rope_cs, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+                QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));  // tab is a local buffer
             }
             m->attn_part = dalloc<float>((size_t)d.n_head * m->n_split * (hd + 2));
             m->attn_counter = dalloc<unsigned int>(d.n_head_kv);
-            QQ_CUDA_TRY(cudaMemset(m->attn_counter, 0, sizeof(unsigned int) * d.n_head_kv));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->attn_counter, 0, sizeof(unsigned int) * d.n_head_kv, ctx->stream));
             const int nm = std::max(m->n_moe, 1);
             m->rec = dalloc<float>((size_t)nm * std::max(m->rec_len, 1));
             m->ridx = dalloc<int>((size_t)nm * std::max(d.n_expert_used, 1));
             m->rw = dalloc<float>((size_t)nm * std::max(d.n_expert_used, 1));
-            QQ_CUDA_TRY(cudaMemset(m->rec, 0, sizeof(float) * nm * std::max(m->rec_len, 1)));
-            QQ_CUDA_TRY(cudaMemset(m->ridx, 0, sizeof(int) * nm * std::max(d.n_expert_used, 1)));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->rec, 0, sizeof(float) * nm * std::max(m->rec_len, 1), ctx->stream));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->ridx, 0, sizeof(int) * nm * std::max(d.n_expert_used, 1), ctx->stream));
             m->mask = dalloc<uint32_t>(8);
-            QQ_CUDA_TRY(cudaMemset(m->mask, 0, 32));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->mask, 0, 32, ctx->stream));
             m->ctl = dalloc<int>(2);
-            QQ_CUDA_TRY(cudaMemset(m->ctl, 0, 8));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->ctl, 0, 8, ctx->stream));
             m->suppress = dalloc<int>(1);
-            QQ_CUDA_TRY(cudaMemset(m->suppress, 0xff, 4));
+            QQ_CUDA_TRY(cudaMemsetAsync(m->suppress, 0xff, 4, ctx->stream));
             m->best = dalloc<unsigned long long>(1);
             m->dump = dalloc<float>((size_t)d.n_layers * E);
             QQ_CUDA_TRY(cudaMallocHost(&m->h_small, 4 * sizeof(int)));
             QQ_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking));
+            QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
         } catch (...) {
             free_model(m);
             delete m;

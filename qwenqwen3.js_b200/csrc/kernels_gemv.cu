@@ -257,6 +257,9 @@ static void launch(const XStage& st, const Map& map, const Epi& epi, int n_items
     QQ_CHECK(st.K % 32 == 0 && st.K > 0, -1, "GEMV inner dimension must be a positive multiple of 32");
     const size_t smem = (size_t)st.nvec * st.K * sizeof(float);
     QQ_CHECK(smem <= kMaxStageBytes, -4, "GEMV input vectors exceed the shared-memory staging limit");
+    for (int v = 0; v < st.nvec; v++)
+        QQ_CHECK(st.x[v] && ((uintptr_t)st.x[v] & 15u) == 0, -1, "GEMV input must be a 16-byte aligned device pointer");
+    QQ_CHECK(((uintptr_t)st.norm_w & 15u) == 0, -1, "norm weight must be 16-byte aligned");
     static int per_sm = 0;
     auto kern = k_gemv<S, Map, Epi>;
     if (!per_sm) {

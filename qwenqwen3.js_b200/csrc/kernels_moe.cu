@@ -63,6 +63,9 @@ __global__ void __launch_bounds__(kGemvThreads)
                 bi = oi;
             }
         }
+        // all lanes agree unless the scores are NaN; keep lane 0's choice and an in-range id
+        bi = __shfl_sync(0xffffffffu, bi, 0);
+        if (bi < 0 || bi >= n_expert) bi = 0;
         if (lane == bi) taken = true;
         top_i[k] = bi;
         top_p[k] = __shfl_sync(0xffffffffu, prob, bi & 31);
@@ -92,6 +95,8 @@ void launch_lfm2_router(const DTensor& router, const float* bias, const float* x
     QQ_CHECK(router.rows >= n_expert, -1, "router: fewer rows than experts");
     if (T <= 0) return;
     const int K = (int)router.K;
+    QQ_CHECK(((uintptr_t)x & 15u) == 0 && ((uintptr_t)norm_w & 15u) == 0 && K % 32 == 0, -1,
+             "router input must be 16-byte aligned with K % 32 == 0");
     const size_t smem = (size_t)K * sizeof(float);
     static bool init = false;
     if (!init) {
