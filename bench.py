@@ -159,15 +159,16 @@ def run_ours(args, ws, rank, local):
     tensors = qq3.synth.build_tensors(spec)
     gen_s = time.time() - t0
     g = qq3.synth.MemoryGGUF(spec, tensors)
-    max_ctx = PROMPT + args.warmup + 2 * args.steps + 16
-    eng = qq3.Lfm2CudaEngine(g, device=local, max_ctx=max_ctx)
+    max_ctx = args.prompt + args.warmup + 2 * args.steps + 16
+    # sequence 1 only serves the clock-sampling soak, so sequence 0's state stays the true continuation
+    eng = qq3.Lfm2CudaEngine(g, device=local, max_ctx=max_ctx, n_seq=2)
     stream = torch.cuda.Stream(device=local)
     eng.ctx.set_stream(stream.cuda_stream)
-    prompt = qq3.synth.uniform_tokens(PROMPT, SEED + rank, spec.n_vocab)
+    prompt = qq3.synth.uniform_tokens(args.prompt, SEED + rank, spec.n_vocab)
     suppress = THINK_ID if THINK_ID < spec.n_vocab else -1
 
     eng.prefill(prompt[:-1].tolist())
-    pos = PROMPT - 1
+    pos = args.prompt - 1
     toks = eng.model.decode_loop(int(prompt[-1]), pos, args.warmup, suppress_id=suppress)
     pos += args.warmup
     cur = int(toks[-1]) if len(toks) else int(prompt[-1])
@@ -178,6 +179,11 @@ def run_ours(args, ws, rank, local):
         dist.barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
+        # un-timed soak of the same loop on sequence 1 so that nvidia-smi sees the clocks under
+        # this load (the 200 ms sampler needs ~1 s); sequence 0 is untouched
+        t_soak = time.time()
+        while time.time() - t_soak < 1.0:
+            eng.model.decode_loop(cur, pos, args.steps, seq=1, suppress_id=suppress, want_tokens=False)
         e0.record(stream)
         out = eng.model.decode_loop(cur, pos, args.steps, suppress_id=suppress)
         e1.record(stream)
@@ -221,7 +227,7 @@ def run_ours(args, ws, rank, local):
         "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)",
         "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (BASELINE config 4)",
                    "layers": "24 (18 short-conv, 6 GQA attention; 2 dense FFN 7168, 22 MoE 32x top-4 x 1792)",
-                   "hidden": 2048, "vocab": 65536, "prompt": PROMPT, "global_batch": ws,
+                   "hidden": 2048, "vocab": 65536, "prompt": args.prompt, "global_batch": ws,
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
                    "l2": "inputs larger than L2: each step streams 1.66 GB of weights"},
         "moe_layer_hbm_gbs": round(nbytes["moe_layer"] / (ms_layer * 1e-3) / 1e9, 1),
@@ -298,8 +304,65 @@ def run_reference(args, ws, rank):
     print(json.dumps(res), flush=True)
 
 
+def run_moe_block(args, ws, rank, local):
+    """the isolated LFM2-MoE block on T tokens (also the small case the
+    ncu captures use).  One step = one qq_moe_block call over T token rows."""
+    import torch
+
+    qq3 = load_package()
+    qq3.build.build_all()
+    torch.cuda.set_device(local)
+    spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
+    names = {f"blk.2.{n}" for n in ("ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                    "ffn_down_exps.weight", "exp_probs_b.bias")}
+    tensors = qq3.synth.build_tensors(spec, only=names)
+    ctx = qq3.runtime.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    L = qq3.runtime.LayerDesc()
+    keep = []
+    for name, (t, ne, raw) in tensors.items():
+        suffix = name.split(".", 2)[2]
+        slot = [k for k, v in qq3.runtime.SLOT_TENSOR_NAMES.items() if v == suffix][0]
+        h = ctx.upload(raw, t, ne)
+        keep.append(h)
+        L.t[qq3.runtime.SLOT[slot]] = h.h.value
+    L.is_moe = 1
+    T = args.tokens
+    x = torch.from_numpy(qq3.synth.normal_f32(T * 2048, seed=T).reshape(T, 2048)).cuda()
+    out = torch.empty_like(x)
+    rec = torch.empty((T, 40), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        ctx.moe_block(L, 32, 4, x, T, out, rec)
+    ctx.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ctx.moe_block(L, 32, 4, x, T, out, rec)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ids = rec[:, :4].cpu().numpy().astype(np.int64)
+    distinct = len(np.unique(ids))
+    q8 = 34 / 32
+    nbytes = 2048 * 32 * q8 + distinct * 3 * 2048 * 1792 * q8 + T * 2048 * 8
+    res = {"metric": "MoE-layer HBM GB/s (isolated LFM2-MoE block)", "value": round(nbytes / (ms * 1e-3) / 1e9, 1),
+           "unit": "GB/s", "tokens": T, "distinct_experts": distinct, "ms_per_step": round(ms, 4),
+           "steps": args.steps, "warmup": args.warmup,
+           "note": "weights only re-read from HBM when the 375 MB of experts exceed L2 between steps"}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    for k in keep:
+        k.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--case", choices=["decode", "moe-block"], default="decode")
+    ap.add_argument("--tokens", type=int, default=1, help="token rows for --case moe-block")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (decode)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
@@ -312,6 +375,8 @@ def main():
     ws, rank, local = _dist()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+    elif args.case == "moe-block":
+        run_moe_block(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
 

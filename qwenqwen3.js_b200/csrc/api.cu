@@ -8,13 +8,14 @@
 //   * greedy decode can run entirely on the device: the step's last kernel writes the
 //     argmax back as the next step's token (qq_decode_loop).
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <new>
 #include <string>
 #include <vector>
 
-#include "../../include/qq3.h"
+#include "qq3.h"
 #include "kernels.h"
 
 namespace qq3 {
@@ -140,6 +141,8 @@ struct qq_model {
     float* attn_part = nullptr;
     unsigned int* attn_counter = nullptr;
     float* rec = nullptr;
+    float* rlogits = nullptr;          // router logits scratch [n_expert]
+    unsigned int* rcounter = nullptr;  // router last-CTA ticket (self-resetting)
     int* ridx = nullptr;
     float* rw = nullptr;
     uint32_t* mask = nullptr;
@@ -165,7 +168,8 @@ void free_model(qq_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     m->graphs.clear();
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
-                    m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->ridx, m->rw, m->mask, m->ctl,
+                    m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
+                    m->mask, m->ctl,
                     m->suppress, m->best, m->dump};
     for (void* p : bufs)
         if (p) cudaFree(p);
@@ -230,8 +234,10 @@ void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool d
             int* idx = m->ridx + (size_t)L.moe_slot * k;
             float* w = m->rw + (size_t)L.moe_slot * k;
             const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
-            qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, m->hidden, 1, sf.norm_w, sf.eps, d.n_expert, k, rec, idx,
-                                    w, s);
+            if (!(qq3::stream_path() && qq3::launch2_router(*L.t[QQ_ROUTER], bias, sf, d.n_expert, k, m->rlogits,
+                                                            m->rcounter, rec, idx, w, s)))
+                qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, m->hidden, 1, sf.norm_w, sf.eps, d.n_expert, k, rec,
+                                        idx, w, s);
             qq3::launch_moe_gateup(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], idx, m->mask, k, sf, m->h, s);
             qq3::launch_moe_down_combine(*L.t[QQ_DOWN_EXPS], idx, w, m->mask, k, m->h, m->hidden, s);
         } else {
@@ -312,6 +318,11 @@ void check_seq_pos(qq_model* m, int seq, int pos0, int n) {
              std::to_string(m->d.max_ctx));
 }
 
+void check_kernel_error(cudaStream_t s) {
+    const int e = qq3::take_kernel_error(s);
+    QQ_CHECK(e == 0, QQ_ERR_CUDA, "a kernel pipeline wait timed out (code " + std::to_string(e) + ")");
+}
+
 void set_suppress(qq_model* m, int id) {
     m->h_small[0] = id;
     QQ_CUDA_TRY(cudaMemcpyAsync(m->suppress, m->h_small, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
@@ -364,6 +375,8 @@ int qq_init(const int* devices, int n_devices, qq_ctx** out) {
             QQ_CUDA_TRY(e);
         }
         c->stream = c->own;
+        if (const char* v = getenv("QQ3_STREAM_GEMV")) qq3::set_stream_path(atoi(v));
+        if (const char* v = getenv("QQ3_PDL")) qq3::set_pdl(atoi(v));
         *out = c;
     });
 }
@@ -391,6 +404,7 @@ int qq_synchronize(qq_ctx* ctx) {
         need(ctx != nullptr, "qq_synchronize: ctx is NULL");
         DeviceGuard dg(ctx->device);
         QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        check_kernel_error(ctx->stream);
     });
 }
 
@@ -427,8 +441,9 @@ int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type
             need(nbytes >= (size_t)nb * 34, "qq_upload_tensor: buffer shorter than the Q8_0 block stream");
             uint8_t* raw = dalloc<uint8_t>((size_t)nb * 34);
             try {
-                t.qs = dalloc<int8_t>((size_t)n);
-                t.d = dalloc<__half>((size_t)nb);
+                // +256 bytes: the streamed GEMV rounds the last group's scale copy up to 16 bytes
+                t.qs = dalloc<int8_t>((size_t)n + 256);
+                t.d = dalloc<__half>((size_t)nb + 128);
                 QQ_CUDA_TRY(cudaMemcpyAsync(raw, host, (size_t)nb * 34, cudaMemcpyHostToDevice, ctx->stream));
                 qq3::launch_repack_q8(raw, nb, t.qs, t.d, ctx->stream);
                 QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
@@ -618,6 +633,9 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
             QQ_CUDA_TRY(cudaMemsetAsync(m->attn_counter, 0, sizeof(unsigned int) * d.n_head_kv, ctx->stream));
             const int nm = std::max(m->n_moe, 1);
             m->rec = dalloc<float>((size_t)nm * std::max(m->rec_len, 1));
+            m->rlogits = dalloc<float>(std::max(d.n_expert, 1));
+            m->rcounter = dalloc<unsigned int>(1);
+            QQ_CUDA_TRY(cudaMemsetAsync(m->rcounter, 0, sizeof(unsigned int), ctx->stream));
             m->ridx = dalloc<int>((size_t)nm * std::max(d.n_expert_used, 1));
             m->rw = dalloc<float>((size_t)nm * std::max(d.n_expert_used, 1));
             QQ_CUDA_TRY(cudaMemsetAsync(m->rec, 0, sizeof(float) * nm * std::max(m->rec_len, 1), ctx->stream));
@@ -667,6 +685,7 @@ int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, 
         if (logits && argmax_out)
             QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->ctl, sizeof(int), cudaMemcpyDeviceToHost, s));
         QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        check_kernel_error(s);
         if (logits && argmax_out) *argmax_out = m->h_small[1];
     });
 }
@@ -685,6 +704,7 @@ int qq_forward_dump(qq_model* m, int32_t token_id, int seq_id, int pos, float* h
         QQ_CUDA_TRY(cudaMemcpyAsync(hidden_out, m->dump, sizeof(float) * m->d.n_layers * m->d.n_embd,
                                     cudaMemcpyDeviceToHost, s));
         QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        check_kernel_error(s);
     });
 }
 
@@ -706,6 +726,7 @@ int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_ste
             QQ_CUDA_TRY(cudaMemcpyAsync(tokens_out, m->trace + (size_t)seq_id * (m->d.max_ctx + 1) + pos0 + 1,
                                         sizeof(int) * n_steps, cudaMemcpyDeviceToHost, s));
         QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        check_kernel_error(s);
     });
 }
 

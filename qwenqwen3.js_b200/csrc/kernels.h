@@ -76,4 +76,31 @@ void launch_lfm2_router(const DTensor& router, const float* bias, const float* x
 
 int num_sms();
 
+// ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
+// Each returns false when the shape is outside the streamed path (the caller then uses the
+// kernels above).  Launched with programmatic dependent launch unless set_pdl(0).
+bool launch2_rows(const DTensor& W, int64_t row0, int64_t n, const XStage& st, float* y, bool residual,
+                  cudaStream_t s);
+bool launch2_qkv(const DTensor& wq, const DTensor& wk, const DTensor& wv, const XStage& st, float* qkv,
+                 cudaStream_t s);
+bool launch2_swiglu(const DTensor& gate, const DTensor& up, const XStage& st, float* h, cudaStream_t s);
+bool launch2_conv(const DTensor& in_proj, const float* conv_w, float* state, const XStage& st, float* y,
+                  cudaStream_t s);
+bool launch2_logits_argmax(const DTensor& W, const XStage& st, float* logits, unsigned long long* best,
+                           const int* suppress_dev, cudaStream_t s);
+bool launch2_moe_gateup(const DTensor& gate_exps, const DTensor& up_exps, const int* idx, const uint32_t* mask,
+                        int top_k, const XStage& st, float* h, cudaStream_t s);
+bool launch2_moe_down_combine(const DTensor& down_exps, const int* idx, const float* w, const uint32_t* mask,
+                              int top_k, const float* h, float* hidden, cudaStream_t s);
+// router for ONE token: logits_tmp [n_expert] and counter (zero, self-resetting) are scratch
+bool launch2_router(const DTensor& router, const float* bias, const XStage& st, int n_expert, int top_k,
+                    float* logits_tmp, unsigned int* counter, float* record, int* idx, float* w, cudaStream_t s);
+void set_pdl(int on);
+// 0 forces the register-streamed kernels of kernels_gemv.cu everywhere (A/B measurements)
+void set_stream_path(int on);
+int stream_path();
+// error word written by bounded waits that gave up (0 = none); read-and-clear
+int* kernel_err_ptr();
+int take_kernel_error(cudaStream_t s);
+
 }  // namespace qq3

@@ -279,9 +279,14 @@ static void check_q8(const DTensor& W) {
     QQ_CHECK(W.type == 8 && W.qs && W.d, -1, "weight must be a Q8_0 tensor");
 }
 
+static int g_stream_path = 1;
+void set_stream_path(int on) { g_stream_path = on; }
+int stream_path() { return g_stream_path; }
+
 void launch_gemv_rows(const DTensor& W, int64_t row0, int64_t n, const XStage& st, float* y, bool residual,
                       cudaStream_t s) {
     check_q8(W);
+    if (g_stream_path && launch2_rows(W, row0, n, st, y, residual, s)) return;
     QQ_CHECK(st.K == W.K, -1, "GEMV: input length does not match the weight's ne[0]");
     QQ_CHECK(row0 >= 0 && row0 + n <= W.rows, -1, "GEMV: row range outside the tensor");
     MapRows m{W.qs, W.d, W.K, row0};
@@ -292,6 +297,7 @@ void launch_gemv_qkv(const DTensor& wq, const DTensor& wk, const DTensor& wv, co
                      cudaStream_t s) {
     check_q8(wq); check_q8(wk); check_q8(wv);
     QQ_CHECK(wq.K == st.K && wk.K == st.K && wv.K == st.K, -1, "QKV: inner dimensions differ");
+    if (g_stream_path && launch2_qkv(wq, wk, wv, st, qkv, s)) return;
     MapConcat3 m;
     m.qs[0] = wq.qs; m.qs[1] = wk.qs; m.qs[2] = wv.qs;
     m.d[0] = wq.d; m.d[1] = wk.d; m.d[2] = wv.d;
@@ -302,6 +308,7 @@ void launch_gemv_qkv(const DTensor& wq, const DTensor& wk, const DTensor& wv, co
 void launch_gemv_swiglu(const DTensor& gate, const DTensor& up, const XStage& st, float* h, cudaStream_t s) {
     check_q8(gate); check_q8(up);
     QQ_CHECK(gate.K == st.K && up.K == st.K && gate.rows == up.rows, -1, "SwiGLU: gate/up shapes differ");
+    if (g_stream_path && launch2_swiglu(gate, up, st, h, s)) return;
     MapPair m{gate.qs, gate.d, up.qs, up.d, st.K};
     launch<2>(st, m, EpiSwiGLU{h}, (int)gate.rows, s);
 }
@@ -311,6 +318,7 @@ void launch_gemv_conv(const DTensor& in_proj, const float* conv_w, float* state,
     check_q8(in_proj);
     QQ_CHECK(in_proj.rows % 3 == 0 && in_proj.K == st.K, -1, "short-conv in_proj must be [E, 3E]");
     const int E = (int)(in_proj.rows / 3);
+    if (g_stream_path && launch2_conv(in_proj, conv_w, state, st, y, s)) return;
     MapStride3 m{in_proj.qs, in_proj.d, st.K, E};
     launch<3>(st, m, EpiConv{conv_w, state, y, E}, E, s);
 }
@@ -319,6 +327,7 @@ void launch_gemv_logits_argmax(const DTensor& W, const XStage& st, float* logits
                                const int* suppress_dev, cudaStream_t s) {
     check_q8(W);
     QQ_CHECK(W.K == st.K, -1, "lm_head: inner dimension mismatch");
+    if (g_stream_path && launch2_logits_argmax(W, st, logits, best, suppress_dev, s)) return;
     const int64_t n = W.ne[1];
     MapRows m{W.qs, W.d, W.K, 0};
     launch<1>(st, m, EpiArgmax{logits, best, suppress_dev}, (int)n, s);
@@ -328,6 +337,7 @@ void launch_moe_gateup(const DTensor& gate_exps, const DTensor& up_exps, const i
                        int top_k, const XStage& st, float* h, cudaStream_t s) {
     check_q8(gate_exps); check_q8(up_exps);
     const int N = (int)gate_exps.ne[1];
+    if (g_stream_path && launch2_moe_gateup(gate_exps, up_exps, idx, mask, top_k, st, h, s)) return;
     MapExpertPair m{gate_exps.qs, gate_exps.d, up_exps.qs, up_exps.d, idx, mask, st.K, N};
     launch<2>(st, m, EpiSwiGLU{h}, top_k * N, s);
 }
@@ -336,6 +346,7 @@ void launch_moe_down_combine(const DTensor& down_exps, const int* idx, const flo
                              int top_k, const float* h, float* hidden, cudaStream_t s) {
     check_q8(down_exps);
     QQ_CHECK(top_k == 4, -4, "MoE down-combine is built for top_k = 4");
+    if (g_stream_path && launch2_moe_down_combine(down_exps, idx, w, mask, top_k, h, hidden, s)) return;
     const int K = (int)down_exps.K, N = (int)down_exps.ne[1];
     XStage st;
     st.nvec = top_k;

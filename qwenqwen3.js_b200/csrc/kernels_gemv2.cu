@@ -1,0 +1,759 @@
+// kernels_gemv2.cu -- bulk-copy-streamed Q8_0 GEMV for single-token decode (sm_100a).
+//
+// Same contract as the kernels of kernels_gemv.cu (matmulQ80xF32, tensor.js:26-53, with the
+// engines' surrounding elementwise ops fused), organised for the B200 memory system:
+//
+//  * one producer warp streams the weight rows of each group of kG output items into a ring
+//    of shared-memory stages with 1-D bulk copies (cp.async.bulk, completion on an mbarrier),
+//    so bytes in flight do not depend on registers and the stream starts before the input
+//    prologue (weights never depend on earlier kernels; the producer only waits on the
+//    previous grid when the rows it needs are chosen by it, i.e. MoE experts);
+//  * eight consumer warps, each owning one item of a stage, read the rows from shared memory;
+//  * the input vector is RMS-normalised (when fused) and each block of 32 inputs is written
+//    as three int8 "digits" in registers: x ~= s * (d1 + d2/254 + d3/254^2), s = max|x|/127,
+//    residual <= 0.5/254^2 * s (6e-8 of the block maximum, the size of an f32 rounding), so a
+//    16-weight chunk is 12 dp4a + one fp32 combine instead of 16 conversions and 16 FMAs.
+//
+// Consumer mode A: the S rows of an item share one input (plain / QKV / gate+up / conv B,C,x).
+// Consumer mode B: source s has its own input h[s] (MoE down over the top-k experts); each
+//   warp computes one source for all kG items of a stage, partials meet in shared memory and
+//   are combined in slot order with the routing weights.
+#include "gemv_core.cuh"
+#include "pipe.cuh"
+
+namespace qq3 {
+
+constexpr int kCW = 8;                 // consumer warps
+constexpr int kG = 4;                  // items per stage
+constexpr int kSets = kCW / kG;        // consumer sets taking alternate stages (mode A)
+constexpr int kThreads2 = (kCW + 1) * 32;
+constexpr int kConsumerThreads = kCW * 32;
+constexpr size_t kSmemBudget = 110 * 1024;  // leaves room for a second (PDL-overlapped) CTA per SM
+
+__device__ __forceinline__ uint32_t round16(uint32_t v) { return (v + 15u) & ~15u; }
+
+// --- activation digits -------------------------------------------------------------------
+// Shared layout of one input vector of length K (nch = K/16 chunks, K/32 blocks):
+//   dig [3][nch] uint4 : digit plane d of chunk c = 16 int8 digits (element 16c + 4w + b in
+//                        byte b of word w), so lanes reading consecutive chunks never conflict
+//   xsc [K/32] float   : block scale s
+// The x-digit form: x ~= s * (d1 + d2/254 + d3/254^2) with s = max|x_block| / 127.
+
+__host__ __device__ inline size_t digit_bytes(int K) { return (size_t)3 * (K >> 4) * 16 + (size_t)(K >> 5) * 4; }
+
+// exact int -> float for |v| < 2^22 on the FMA/ALU pipes (1.5 * 2^23 has unit ulp)
+__device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
+// round-to-nearest-even to an integer, |r| < 2^22, returning the integer and its float value
+__device__ __forceinline__ int round_small(float r, float& rf) {
+    const float t = r + 12582912.0f;
+    rf = t - 12582912.0f;
+    return __float_as_int(t) - 0x4B400000;
+}
+
+// Thread t of the nthreads consumer threads digitises elements [8t, 8t+8) of x (already
+// normalised values in xv[8]).  Quads of threads share a 32-block.
+__device__ __forceinline__ void digitise8(const float (&xv)[8], int e0, int K, uint4* dig, float* xsc) {
+    const int nch = K >> 4;
+    float m = 0.f;
+    if (e0 < K) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) m = fmaxf(m, fabsf(xv[e]));
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    if (e0 >= K) return;
+    const float inv = m > 0.f ? 127.0f / m : 0.f;
+    if ((e0 & 31) == 0) xsc[e0 >> 5] = m > 0.f ? m / 127.0f : 0.f;
+    uint32_t wd[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float f1, f2, f3;
+        const float r0 = xv[e] * inv;
+        const int d1 = round_small(r0, f1);
+        const float r1 = (r0 - f1) * 254.0f;
+        const int d2 = round_small(r1, f2);
+        const int d3 = round_small((r1 - f2) * 254.0f, f3);
+        const int sh = 8 * (e & 3);
+        wd[0][e >> 2] |= ((uint32_t)d1 & 0xffu) << sh;
+        wd[1][e >> 2] |= ((uint32_t)d2 & 0xffu) << sh;
+        wd[2][e >> 2] |= ((uint32_t)d3 & 0xffu) << sh;
+    }
+    const int c = e0 >> 4, half = (e0 >> 3) & 1;  // 8 elements = words {2*half, 2*half+1} of chunk c
+#pragma unroll
+    for (int d = 0; d < 3; d++)
+        reinterpret_cast<uint2*>(dig + (size_t)d * nch + c)[half] = make_uint2(wd[d][0], wd[d][1]);
+}
+
+// 12 dp4a of a 16-weight chunk against the three digit planes, combined in fp32
+__device__ __forceinline__ float chunk_dot(const uint4 w, const uint4 g0, const uint4 g1, const uint4 g2) {
+    int a1 = __dp4a((int)w.x, (int)g0.x, 0);
+    int a2 = __dp4a((int)w.x, (int)g1.x, 0);
+    int a3 = __dp4a((int)w.x, (int)g2.x, 0);
+    a1 = __dp4a((int)w.y, (int)g0.y, a1);
+    a2 = __dp4a((int)w.y, (int)g1.y, a2);
+    a3 = __dp4a((int)w.y, (int)g2.y, a3);
+    a1 = __dp4a((int)w.z, (int)g0.z, a1);
+    a2 = __dp4a((int)w.z, (int)g1.z, a2);
+    a3 = __dp4a((int)w.z, (int)g2.z, a3);
+    a1 = __dp4a((int)w.w, (int)g0.w, a1);
+    a2 = __dp4a((int)w.w, (int)g1.w, a2);
+    a3 = __dp4a((int)w.w, (int)g2.w, a3);
+    return fmaf(i2f_small(a3), 1.0f / 64516.0f, fmaf(i2f_small(a2), 1.0f / 254.0f, i2f_small(a1)));
+}
+
+// lane partials of S rows (shared memory) against one digitised input
+template <int S, int CPL>
+__device__ __forceinline__ void rows_dot(const int8_t* const (&q)[S], const __half* const (&d)[S],
+                                         const bool (&on)[S], const uint4* dig, const float* xsc, int nch,
+                                         float (&acc)[S]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < CPL; i++) {
+        const int c = lane + 32 * i;
+        if (c < nch) {
+            const uint4 g0 = dig[c], g1 = dig[nch + c], g2 = dig[2 * nch + c];
+            const float sx = xsc[c >> 1];
+#pragma unroll
+            for (int s = 0; s < S; s++) {
+                if (!on[s]) continue;
+                const uint4 w = *reinterpret_cast<const uint4*>(q[s] + 16 * c);
+                const float dw = __half2float(d[s][c >> 1]);
+                acc[s] = fmaf(chunk_dot(w, g0, g1, g2), dw * sx, acc[s]);
+            }
+        }
+    }
+}
+
+// --- input staging (consumer threads only) ----------------------------------------------
+// Loads x (K <= 2048, 8 elements per consumer thread), optionally applies RMSNorm
+// (tensor.js:103-114; the sum of squares in double as the JS does), digitises into smem.
+__device__ __forceinline__ void stage_digits(const float* __restrict__ x, const float* __restrict__ norm_w, float eps,
+                                             int K, uint4* dig, float* xsc, double* red) {
+    const int t = threadIdx.x;
+    const int e0 = 8 * t;
+    float xv[8];
+    if (e0 < K) {
+        const float4 a = reinterpret_cast<const float4*>(x + e0)[0];
+        const float4 b = reinterpret_cast<const float4*>(x + e0)[1];
+        xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) xv[e] = 0.f;
+    }
+    if (norm_w) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss += (double)xv[e] * xv[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((t & 31) == 0) red[t >> 5] = ss;
+        named_bar(1, kConsumerThreads);
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < kCW; w++) tot += red[w];
+        const float inv = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
+        if (e0 < K) {
+            const float4 a = reinterpret_cast<const float4*>(norm_w + e0)[0];
+            const float4 b = reinterpret_cast<const float4*>(norm_w + e0)[1];
+            const float wv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) xv[e] = (wv[e] * xv[e]) * inv;
+        }
+    }
+    digitise8(xv, e0, K, dig, xsc);
+}
+
+// --- the producer --------------------------------------------------------------------------
+
+struct Ring {
+    uint8_t* base;
+    uint64_t* full;
+    uint64_t* empty;
+    int stages;
+    uint32_t qs_bytes;  // per source per stage: kG * K
+    uint32_t d_bytes;   // per source per stage: round16(kG * K / 16)
+    uint32_t stage_bytes;
+};
+
+template <int S, class Map>
+__device__ __forceinline__ void produce(const Map& map, const Ring& r, int K, int n_items, int* err,
+                                        volatile int* abort_flag) {
+    const int n_groups = (n_items + kG - 1) / kG;
+    if (Map::kDependentRows) pdl_wait();
+    int i = 0;
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
+        const int slot = i % r.stages;
+        const uint32_t use = (uint32_t)(i / r.stages);
+        if (use > 0 && !mbar_wait(&r.empty[slot], (use - 1) & 1u)) {
+            set_err(err, kErrEmptyWait);
+            *abort_flag = 1;
+            return;
+        }
+        if (*abort_flag) return;
+        const int item0 = g * kG;
+        const int rows = min(kG, n_items - item0);
+        const int8_t* q[S];
+        const __half* d[S];
+        bool on[S];
+        map.group(item0, q, d, on);
+        uint32_t tx = 0;
+#pragma unroll
+        for (int s = 0; s < S; s++)
+            if (on[s]) tx += (uint32_t)rows * K + round16((uint32_t)rows * (K >> 4));
+        uint8_t* sb = r.base + (size_t)slot * r.stage_bytes;
+        mbar_arrive_expect_tx(&r.full[slot], tx);
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            if (!on[s]) continue;
+            bulk_g2s(sb + s * r.qs_bytes, q[s], (uint32_t)rows * K, &r.full[slot]);
+            bulk_g2s(sb + S * r.qs_bytes + s * r.d_bytes, d[s], round16((uint32_t)rows * (K >> 4)), &r.full[slot]);
+        }
+    }
+}
+
+// Shared-memory carve-up: [stages][S][kG][K] qs | [S][d_bytes] | x staging | barriers
+template <int S>
+__device__ __forceinline__ Ring make_ring(uint8_t* smem, int K, int stages) {
+    Ring r;
+    r.stages = stages;
+    r.qs_bytes = (uint32_t)kG * K;
+    r.d_bytes = round16((uint32_t)kG * (K >> 4));
+    r.stage_bytes = S * (r.qs_bytes + r.d_bytes);
+    r.base = smem;
+    return r;
+}
+
+__host__ __device__ inline size_t ring_bytes(int S, int K, int stages) {
+    const size_t per = (size_t)S * ((size_t)kG * K + (((size_t)kG * (K >> 4) + 15) & ~(size_t)15));
+    return per * stages;
+}
+
+// --- mode A kernel -------------------------------------------------------------------------
+
+template <int S, int CPL, class Map, class Epi>
+__global__ void __launch_bounds__(kThreads2, 2)
+    k_gemv2(XStage st, Map map, Epi epi, int n_items, int stages, int* err) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ double red[kCW];
+    __shared__ int abort_flag;
+    const int K = st.K, nch = K >> 4;
+    Ring r = make_ring<S>(smem, K, stages);
+    uint4* dig = reinterpret_cast<uint4*>(smem + ring_bytes(S, K, stages));
+    float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
+    r.full = reinterpret_cast<uint64_t*>(smem + ring_bytes(S, K, stages) + ((digit_bytes(K) + 15) & ~(size_t)15));
+    r.empty = r.full + stages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; s++) {
+            mbar_init(&r.full[s], 1);
+            mbar_init(&r.empty[s], kG);
+        }
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (warp == kCW) {
+        if (lane == 0) produce<S>(map, r, K, n_items, err, &abort_flag);
+        return;
+    }
+    // consumers: inputs come from the previous kernel
+    pdl_wait();
+    stage_digits(st.x[0], st.norm_w, st.eps, K, dig, xsc, red);
+    named_bar(1, kConsumerThreads);
+    typename Epi::WarpState ws;
+    epi.init(ws);
+    const int set = warp / kG, w = warp % kG;
+    const int n_groups = (n_items + kG - 1) / kG;
+    int i = 0;
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
+        if (i % kSets != set) continue;
+        const int slot = i % stages;
+        if (!mbar_wait(&r.full[slot], (uint32_t)(i / stages) & 1u)) {
+            set_err(err, kErrFullWait);
+            abort_flag = 1;
+            break;
+        }
+        const int item = g * kG + w;
+        const uint8_t* sb = r.base + (size_t)slot * r.stage_bytes;
+        if (item < n_items) {
+            bool on[S];
+            map.active(item, on);
+            const int8_t* q[S];
+            const __half* d[S];
+            float acc[S];
+#pragma unroll
+            for (int s = 0; s < S; s++) {
+                q[s] = reinterpret_cast<const int8_t*>(sb + s * r.qs_bytes) + (size_t)w * K;
+                d[s] = reinterpret_cast<const __half*>(sb + S * r.qs_bytes + s * r.d_bytes) + w * (K >> 5);
+                acc[s] = 0.f;
+            }
+            rows_dot<S, CPL>(q, d, on, dig, xsc, nch, acc);
+#pragma unroll
+            for (int s = 0; s < S; s++) acc[s] = warp_sum(acc[s]);
+            epi.apply(ws, item, acc, on);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+    }
+    epi.finish2(ws);
+}
+
+// rows j0.. of each selected expert's down matrix (ids chosen by the router, previous kernel)
+template <int S>
+struct M2Down {
+    static constexpr bool kDependentRows = true;
+    const int8_t* qs; const __half* d; const int* idx; const uint32_t* mask; int K, N;
+    __device__ void group(int item0, const int8_t* (&q)[S], const __half* (&dd)[S], bool (&on)[S]) const {
+#pragma unroll
+        for (int s = 0; s < S; s++) {
+            const int e = idx[s];
+            const int64_t row = (int64_t)e * N + item0;
+            q[s] = qs + row * K;
+            dd[s] = d + row * (K >> 5);
+            on[s] = !(mask && ((mask[e >> 5] >> (e & 31)) & 1u));
+        }
+    }
+};
+
+// --- mode B kernel (MoE down + combine) -----------------------------------------------------
+// Stage = kG output rows j of each of the S = top_k selected experts.  Warp w serves source
+// s = w % S for the stages of set w / S (alternate stages), computing all kG rows of s.
+
+template <int S, int CPL>
+__global__ void __launch_bounds__(kThreads2, 2)
+    k_moe_down2(const int8_t* __restrict__ qs, const __half* __restrict__ dsc, const int* __restrict__ idx,
+                const float* __restrict__ wts, const uint32_t* __restrict__ mask, const float* __restrict__ h,
+                float* __restrict__ hidden, int K, int N, int stages, int* err) {
+    static_assert(kCW % S == 0, "warps must split evenly across sources");
+    constexpr int kSetsB = kCW / S;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int abort_flag;
+    __shared__ float part[kSetsB][kG][S];
+    __shared__ double red[kCW];
+    const int nch = K >> 4;
+    const size_t dbytes = (digit_bytes(K) + 15) & ~(size_t)15;
+    Ring r = make_ring<S>(smem, K, stages);
+    uint8_t* dbase = smem + ring_bytes(S, K, stages);
+    r.full = reinterpret_cast<uint64_t*>(dbase + S * dbytes);
+    r.empty = r.full + stages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; s++) {
+            mbar_init(&r.full[s], 1);
+            mbar_init(&r.empty[s], S);
+        }
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (warp == kCW) {
+        if (lane == 0) produce<S>(M2Down<S>{qs, dsc, idx, mask, K, N}, r, K, N, err, &abort_flag);
+        return;
+    }
+    pdl_wait();
+    // digitise the S expert inputs h[s]
+    for (int s = 0; s < S; s++) {
+        uint4* dig = reinterpret_cast<uint4*>(dbase + s * dbytes);
+        stage_digits(h + (size_t)s * K, nullptr, 0.f, K, dig, reinterpret_cast<float*>(dig + 3 * nch), red);
+    }
+    named_bar(1, kConsumerThreads);
+    const int src_s = warp % S, set = warp / S;
+    const uint4* dig = reinterpret_cast<const uint4*>(dbase + src_s * dbytes);
+    const float* xsc = reinterpret_cast<const float*>(dig + 3 * nch);
+    float wk[S];
+    bool ons[S];
+#pragma unroll
+    for (int s = 0; s < S; s++) {
+        wk[s] = wts[s];
+        const int es = idx[s];
+        ons[s] = !(mask && ((mask[es >> 5] >> (es & 31)) & 1u));
+    }
+    const int n_groups = (N + kG - 1) / kG;
+    int i = 0;
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
+        if (i % kSetsB != set) continue;
+        const int slot = i % stages;
+        if (!mbar_wait(&r.full[slot], (uint32_t)(i / stages) & 1u)) {
+            set_err(err, kErrFullWait);
+            abort_flag = 1;
+            break;
+        }
+        const uint8_t* sb = r.base + (size_t)slot * r.stage_bytes;
+        const int rows = min(kG, N - g * kG);
+        float acc[kG];
+#pragma unroll
+        for (int j = 0; j < kG; j++) {
+            acc[j] = 0.f;
+            if (j < rows && ons[src_s]) {
+                const int8_t* q[1] = {reinterpret_cast<const int8_t*>(sb + src_s * r.qs_bytes) + (size_t)j * K};
+                const __half* d[1] = {reinterpret_cast<const __half*>(sb + S * r.qs_bytes + src_s * r.d_bytes) +
+                                      j * (K >> 5)};
+                const bool on1[1] = {true};
+                float a1[1] = {0.f};
+                rows_dot<1, CPL>(q, d, on1, dig, xsc, nch, a1);
+                acc[j] = a1[0];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kG; j++) {
+            const float v = warp_sum(acc[j]);
+            if (lane == 0) part[set][j][src_s] = v;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+        named_bar(2 + set, S * 32);  // the S warps of this set
+        // combine in slot order (lfm2-engine.js:459-486): moe = sum_k w_k * down_k; hidden += moe
+        if (warp % S == 0 && lane < rows) {
+            float moe = 0.f;
+#pragma unroll
+            for (int s = 0; s < S; s++)
+                if (ons[s]) moe += wk[s] * part[set][lane][s];
+            hidden[g * kG + lane] += moe;
+        }
+        named_bar(2 + set, S * 32);
+    }
+}
+
+// --- row maps: item -> the S weight rows of the group starting at item0 -------------------
+// Rows of consecutive items are consecutive in every source, so a group is one bulk copy of
+// kG rows per source.  Host checks keep groups from straddling a tensor / expert boundary.
+
+__device__ __forceinline__ bool is_masked(const uint32_t* mask, int e) {
+    return mask && ((mask[e >> 5] >> (e & 31)) & 1u);
+}
+
+struct M2Rows {
+    static constexpr bool kDependentRows = false;
+    const int8_t* qs; const __half* d; int64_t K, row0;
+    __device__ void group(int item0, const int8_t* (&q)[1], const __half* (&dd)[1], bool (&on)[1]) const {
+        const int64_t row = row0 + item0;
+        q[0] = qs + row * K; dd[0] = d + row * (K >> 5); on[0] = true;
+    }
+    __device__ void active(int, bool (&on)[1]) const { on[0] = true; }
+};
+
+struct M2Concat3 {
+    static constexpr bool kDependentRows = false;
+    const int8_t* qs[3]; const __half* d[3]; int n0, n1; int64_t K;
+    __device__ void group(int item0, const int8_t* (&q)[1], const __half* (&dd)[1], bool (&on)[1]) const {
+        int t = 0, row = item0;
+        if (item0 >= n0 + n1) { t = 2; row = item0 - n0 - n1; }
+        else if (item0 >= n0) { t = 1; row = item0 - n0; }
+        q[0] = qs[t] + (int64_t)row * K; dd[0] = d[t] + (int64_t)row * (K >> 5); on[0] = true;
+    }
+    __device__ void active(int, bool (&on)[1]) const { on[0] = true; }
+};
+
+struct M2Pair {
+    static constexpr bool kDependentRows = false;
+    const int8_t* qa; const __half* da; const int8_t* qb; const __half* db; int64_t K;
+    __device__ void group(int item0, const int8_t* (&q)[2], const __half* (&dd)[2], bool (&on)[2]) const {
+        q[0] = qa + (int64_t)item0 * K; dd[0] = da + (int64_t)item0 * (K >> 5);
+        q[1] = qb + (int64_t)item0 * K; dd[1] = db + (int64_t)item0 * (K >> 5);
+        on[0] = on[1] = true;
+    }
+    __device__ void active(int, bool (&on)[2]) const { on[0] = on[1] = true; }
+};
+
+struct M2Stride3 {
+    static constexpr bool kDependentRows = false;
+    const int8_t* qs; const __half* d; int64_t K, stride;
+    __device__ void group(int item0, const int8_t* (&q)[3], const __half* (&dd)[3], bool (&on)[3]) const {
+#pragma unroll
+        for (int s = 0; s < 3; s++) {
+            const int64_t row = item0 + s * stride;
+            q[s] = qs + row * K; dd[s] = d + row * (K >> 5); on[s] = true;
+        }
+    }
+    __device__ void active(int, bool (&on)[3]) const { on[0] = on[1] = on[2] = true; }
+};
+
+struct M2ExpertPair {  // item = k*N + j; the expert ids come from the router (previous kernel)
+    static constexpr bool kDependentRows = true;
+    const int8_t* qa; const __half* da; const int8_t* qb; const __half* db;
+    const int* idx; const uint32_t* mask; int64_t K; int N;
+    __device__ void group(int item0, const int8_t* (&q)[2], const __half* (&dd)[2], bool (&on)[2]) const {
+        const int k = item0 / N, j0 = item0 - k * N;
+        const int e = idx[k];
+        const int64_t row = (int64_t)e * N + j0;
+        q[0] = qa + row * K; dd[0] = da + row * (K >> 5);
+        q[1] = qb + row * K; dd[1] = db + row * (K >> 5);
+        on[0] = on[1] = !is_masked(mask, e);
+    }
+    __device__ void active(int item, bool (&on)[2]) const { on[0] = on[1] = !is_masked(mask, idx[item / N]); }
+};
+
+// --- epilogues (lane 0 writes; finish2 synchronises consumer threads only) ------------------
+
+struct NoState2 {};
+
+struct E2Store {
+    float* y; bool residual;
+    using WarpState = NoState2;
+    __device__ void init(WarpState&) const {}
+    __device__ void apply(WarpState&, int item, const float (&acc)[1], const bool (&)[1]) const {
+        if ((threadIdx.x & 31) == 0) y[item] = residual ? y[item] + acc[0] : acc[0];
+    }
+    __device__ void finish2(WarpState&) const {}
+};
+
+struct E2SwiGLU {  // siluInPlace(gate); mulInPlace(gate, up)  (tensor.js:167-178)
+    float* h;
+    using WarpState = NoState2;
+    __device__ void init(WarpState&) const {}
+    __device__ void apply(WarpState&, int item, const float (&acc)[2], const bool (&on)[2]) const {
+        if ((threadIdx.x & 31) == 0 && on[0]) h[item] = acc[0] * (1.0f / (1.0f + expf(-acc[0]))) * acc[1];
+    }
+    __device__ void finish2(WarpState&) const {}
+};
+
+struct E2Conv {  // lfm2-engine.js:294-321 for element j
+    const float* kw; float* state; float* y; int E;
+    using WarpState = NoState2;
+    __device__ void init(WarpState&) const {}
+    __device__ void apply(WarpState&, int j, const float (&acc)[3], const bool (&)[3]) const {
+        if ((threadIdx.x & 31) != 0) return;
+        const float bx = acc[0] * acc[2];
+        const float s0 = state[j], s1 = state[E + j];
+        const float co = kw[j * 3 + 0] * s0 + kw[j * 3 + 1] * s1 + kw[j * 3 + 2] * bx;
+        state[j] = s1;
+        state[E + j] = bx;
+        y[j] = acc[1] * co;
+    }
+    __device__ void finish2(WarpState&) const {}
+};
+
+struct E2Argmax {  // logits + first-max argmax (sampleGreedy, tensor.js:231-237)
+    float* logits; unsigned long long* best; const int* suppress;
+    struct WarpState { unsigned long long k; int skip; };
+    __device__ void init(WarpState& s) const { s.k = 0ull; s.skip = suppress ? *suppress : -1; }
+    __device__ void apply(WarpState& s, int item, const float (&acc)[1], const bool (&)[1]) const {
+        if ((threadIdx.x & 31) == 0) {
+            logits[item] = acc[0];
+            if (item != s.skip) {
+                const unsigned long long k = argmax_key(acc[0], item);
+                if (k > s.k) s.k = k;
+            }
+        }
+    }
+    __device__ void finish2(WarpState& s) const {
+        __shared__ unsigned long long keys[kCW];
+        if ((threadIdx.x & 31) == 0) keys[threadIdx.x >> 5] = s.k;
+        named_bar(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            unsigned long long m = 0ull;
+            for (int w = 0; w < kCW; w++) m = keys[w] > m ? keys[w] : m;
+            if (m) atomicMax(best, m);
+        }
+    }
+};
+
+// LFM2 router (lfm2-engine.js:417-447, WGSL_MOE_SIGMOID_TOPK webgpu.js:1243-1283): logits by
+// the streamed GEMV over a few CTAs; the last CTA to finish does sigmoid, +bias selection,
+// top-k (ties to the lower id) and the (1e-6 + sum) normalisation.
+struct E2Router {
+    float* logits; unsigned int* counter; const float* bias;
+    float* record; int* idx; float* w; int n_expert, top_k;
+    using WarpState = NoState2;
+    __device__ void init(WarpState&) const {}
+    __device__ void apply(WarpState&, int item, const float (&acc)[1], const bool (&)[1]) const {
+        if ((threadIdx.x & 31) == 0) logits[item] = acc[0];
+    }
+    __device__ void finish2(WarpState&) const {
+        __shared__ int last;
+        named_bar(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            __threadfence();
+            last = atomicAdd(counter, 1u) == gridDim.x - 1;
+        }
+        named_bar(1, kConsumerThreads);
+        if (!last || threadIdx.x >= 32) return;
+        __threadfence();
+        const int lane = threadIdx.x;
+        const bool live = lane < n_expert;
+        const float prob = live ? 1.0f / (1.0f + expf(-__ldcg(logits + lane))) : 0.f;
+        const float sel = live ? prob + (bias ? bias[lane] : 0.f) : -INFINITY;
+        bool taken = !live;
+        double sum_w = 1e-6;
+        int top_i[8];
+        float top_p[8];
+        for (int k = 0; k < top_k; k++) {
+            float bv = taken ? -INFINITY : sel;
+            int bi = taken ? 0x7fffffff : lane;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            bi = __shfl_sync(0xffffffffu, bi, 0);
+            if (bi < 0 || bi >= n_expert) bi = 0;  // only reachable with NaN scores
+            if (lane == bi) taken = true;
+            top_i[k] = bi;
+            top_p[k] = __shfl_sync(0xffffffffu, prob, bi & 31);
+            sum_w += (double)top_p[k];
+        }
+        const double inv = 1.0 / sum_w;
+        if (lane == 0) {
+            for (int k = 0; k < top_k; k++) {
+                const float wk = (float)((double)top_p[k] * inv);
+                idx[k] = top_i[k];
+                w[k] = wk;
+                if (record) { record[k] = (float)top_i[k]; record[top_k + k] = wk; }
+            }
+            *counter = 0u;
+        }
+        if (record && live) record[2 * top_k + lane] = prob;
+    }
+};
+
+// --- launch plumbing --------------------------------------------------------------------------
+
+static int g_pdl = 0;  // programmatic dependent launch; off by default (measured slower end to end), QQ3_PDL=1 enables
+void set_pdl(int on) { g_pdl = on; }
+
+__device__ int g_kernel_err;
+
+int* kernel_err_ptr() {
+    static int* p = nullptr;
+    if (!p) QQ_CUDA_TRY(cudaGetSymbolAddress((void**)&p, g_kernel_err));
+    return p;
+}
+
+int take_kernel_error(cudaStream_t s) {
+    int v = 0;
+    QQ_CUDA_TRY(cudaMemcpyAsync(&v, kernel_err_ptr(), sizeof(int), cudaMemcpyDeviceToHost, s));
+    QQ_CUDA_TRY(cudaStreamSynchronize(s));
+    if (v) QQ_CUDA_TRY(cudaMemsetAsync(kernel_err_ptr(), 0, sizeof(int), s));
+    return v;
+}
+
+template <class Kern, class... Args>
+static void launch_ex(Kern kern, int grid, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads2);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
+}
+
+static int pick_stages(size_t per_stage, size_t fixed) {
+    const size_t avail = kSmemBudget > fixed ? kSmemBudget - fixed : 0;
+    int st = (int)(avail / per_stage);
+    if (st > 8) st = 8;
+    if (st < 2) st = 2;
+    return st;
+}
+
+// the streamed path needs K % 64 == 0 (16-byte aligned scale rows per 4-row group), K <= 2048
+static bool k_ok(int64_t K) { return K >= 64 && K <= 2048 && K % 64 == 0; }
+
+template <int S, int CPL, class Map, class Epi>
+static void launch_a(const XStage& st, const Map& map, const Epi& epi, int n_items, cudaStream_t s) {
+    const int K = st.K;
+    const size_t per = ring_bytes(S, K, 1);
+    const size_t fixed = (digit_bytes(K) + 15) & ~(size_t)15;
+    const int stages = pick_stages(per, fixed);
+    const size_t smem = ring_bytes(S, K, stages) + fixed + 2 * (size_t)stages * sizeof(uint64_t);
+    auto kern = k_gemv2<S, CPL, Map, Epi>;
+    static bool init = false;
+    if (!init) {
+        QQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        init = true;
+    }
+    const int groups = (n_items + kG - 1) / kG;
+    const int grid = groups < num_sms() ? groups : num_sms();
+    launch_ex(kern, grid, smem, s, st, map, epi, n_items, stages, kernel_err_ptr());
+}
+
+template <int S, class Map, class Epi>
+static bool dispatch_a(const XStage& st, const Map& map, const Epi& epi, int n_items, cudaStream_t s) {
+    if (!k_ok(st.K) || st.nvec != 1 || ((uintptr_t)st.x[0] & 15u) || ((uintptr_t)st.norm_w & 15u)) return false;
+    if (st.K <= 512) launch_a<S, 1>(st, map, epi, n_items, s);
+    else if (st.K <= 1024) launch_a<S, 2>(st, map, epi, n_items, s);
+    else launch_a<S, 4>(st, map, epi, n_items, s);
+    return true;
+}
+
+bool launch2_rows(const DTensor& W, int64_t row0, int64_t n, const XStage& st, float* y, bool residual,
+                  cudaStream_t s) {
+    if (W.type != 8 || row0 % kG) return false;
+    return dispatch_a<1>(st, M2Rows{W.qs, W.d, W.K, row0}, E2Store{y, residual}, (int)n, s);
+}
+
+bool launch2_qkv(const DTensor& wq, const DTensor& wk, const DTensor& wv, const XStage& st, float* qkv,
+                 cudaStream_t s) {
+    if (wq.rows % kG || wk.rows % kG) return false;
+    M2Concat3 m;
+    m.qs[0] = wq.qs; m.qs[1] = wk.qs; m.qs[2] = wv.qs;
+    m.d[0] = wq.d; m.d[1] = wk.d; m.d[2] = wv.d;
+    m.n0 = (int)wq.rows; m.n1 = (int)wk.rows; m.K = st.K;
+    return dispatch_a<1>(st, m, E2Store{qkv, false}, (int)(wq.rows + wk.rows + wv.rows), s);
+}
+
+bool launch2_swiglu(const DTensor& gate, const DTensor& up, const XStage& st, float* h, cudaStream_t s) {
+    return dispatch_a<2>(st, M2Pair{gate.qs, gate.d, up.qs, up.d, st.K}, E2SwiGLU{h}, (int)gate.rows, s);
+}
+
+bool launch2_conv(const DTensor& in_proj, const float* conv_w, float* state, const XStage& st, float* y,
+                  cudaStream_t s) {
+    const int E = (int)(in_proj.rows / 3);
+    if (E % kG) return false;
+    return dispatch_a<3>(st, M2Stride3{in_proj.qs, in_proj.d, st.K, E}, E2Conv{conv_w, state, y, E}, E, s);
+}
+
+bool launch2_logits_argmax(const DTensor& W, const XStage& st, float* logits, unsigned long long* best,
+                           const int* suppress_dev, cudaStream_t s) {
+    return dispatch_a<1>(st, M2Rows{W.qs, W.d, W.K, 0}, E2Argmax{logits, best, suppress_dev}, (int)W.ne[1], s);
+}
+
+bool launch2_moe_gateup(const DTensor& gate_exps, const DTensor& up_exps, const int* idx, const uint32_t* mask,
+                        int top_k, const XStage& st, float* h, cudaStream_t s) {
+    const int N = (int)gate_exps.ne[1];
+    if (N % kG) return false;
+    M2ExpertPair m{gate_exps.qs, gate_exps.d, up_exps.qs, up_exps.d, idx, mask, st.K, N};
+    return dispatch_a<2>(st, m, E2SwiGLU{h}, top_k * N, s);
+}
+
+bool launch2_router(const DTensor& router, const float* bias, const XStage& st, int n_expert, int top_k,
+                    float* logits_tmp, unsigned int* counter, float* record, int* idx, float* w, cudaStream_t s) {
+    if (n_expert > 32 || top_k > 8 || n_expert % kG) return false;
+    E2Router e{logits_tmp, counter, bias, record, idx, w, n_expert, top_k};
+    return dispatch_a<1>(st, M2Rows{router.qs, router.d, router.K, 0}, e, n_expert, s);
+}
+
+bool launch2_moe_down_combine(const DTensor& down_exps, const int* idx, const float* w, const uint32_t* mask,
+                              int top_k, const float* h, float* hidden, cudaStream_t s) {
+    const int K = (int)down_exps.K, N = (int)down_exps.ne[1];
+    if (top_k != 4 || !k_ok(K) || N % kG || ((uintptr_t)h & 15u)) return false;
+    const size_t per = ring_bytes(4, K, 1);
+    const size_t fixed = 4 * ((digit_bytes(K) + 15) & ~(size_t)15);
+    const int stages = pick_stages(per, fixed);
+    const size_t smem = ring_bytes(4, K, stages) + fixed + 2 * (size_t)stages * sizeof(uint64_t);
+    const int groups = (N + kG - 1) / kG;
+    const int grid = groups < num_sms() ? groups : num_sms();
+    if (K <= 512) {
+        static bool init = false;
+        if (!init) { QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); init = true; }
+        launch_ex(k_moe_down2<4, 1>, grid, smem, s, down_exps.qs, down_exps.d, idx, w, mask, h, hidden, K, N, stages, kernel_err_ptr());
+    } else if (K <= 1024) {
+        static bool init = false;
+        if (!init) { QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); init = true; }
+        launch_ex(k_moe_down2<4, 2>, grid, smem, s, down_exps.qs, down_exps.d, idx, w, mask, h, hidden, K, N, stages, kernel_err_ptr());
+    } else {
+        static bool init = false;
+        if (!init) { QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); init = true; }
+        launch_ex(k_moe_down2<4, 4>, grid, smem, s, down_exps.qs, down_exps.d, idx, w, mask, h, hidden, K, N, stages, kernel_err_ptr());
+    }
+    return true;
+}
+
+}  // namespace qq3

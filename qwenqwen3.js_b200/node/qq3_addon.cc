@@ -24,7 +24,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/qq3.h"
+#include "qq3.h"  // include/ (built with -I include)
 
 #define NAPI_CALL(env, call)                                        \
     do {                                                            \
