@@ -213,6 +213,25 @@ int qq_bench_kernel(qq_model* m, int what, int iters, float* ms);
 int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
                  float* out_dev, float* routing_dev);
 
+/* ---------------------------------------------------------------- allocation-free MoE block */
+
+/* No counterpart in the reference.  qq_moe_block without any device allocation, for callers
+ * that cannot let the library call cudaMalloc while a layer runs: a host that owns all device
+ * memory through its own pool or budget (an embedding runtime such as a JS engine's addon, or a
+ * serving process that pre-plans its memory), or code that issues the block while recording
+ * its own stream work.  Inputs and outputs are the caller's, exactly as for qq_moe_block; the
+ * scratch is one fixed device array of the library module (256 KiB, held by every GPU that
+ * loads the library until the process exits).
+ * Limits: T <= QQ_NOALLOC_MAX_TOKENS, expert FFN width <= QQ_NOALLOC_MAX_FF, top_k == 4,
+ * n_expert <= 32; beyond them the call fails with QQ_ERR_INVALID and does no GPU work.
+ * The first call on a device resolves the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture.  All calls on a device share the array and it
+ * keeps the last call's contents: calls whose GPU work overlaps race. */
+#define QQ_NOALLOC_MAX_TOKENS 1024
+#define QQ_NOALLOC_MAX_FF 4096
+int qq_moe_block_noalloc(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev,
+                         int T, float* out_dev, float* routing_dev);
+
 #ifdef __cplusplus
 }
 #endif

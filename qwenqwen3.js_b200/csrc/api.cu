@@ -15,60 +15,17 @@
 #include <string>
 #include <vector>
 
-#include "qq3.h"
-#include "kernels.h"
+#include "api_internal.h"
 
 namespace qq3 {
 static thread_local std::string g_err;
 void set_error(const std::string& msg) { g_err = msg; }
+const char* last_error_cstr() { return g_err.c_str(); }
 }  // namespace qq3
 
-using qq3::DTensor;
-using qq3::Error;
-
-struct qq_ctx {
-    int device = 0;
-    cudaStream_t own = nullptr;
-    cudaStream_t stream = nullptr;
-    // scratch arena for op-level calls (grow-only)
-    void* scratch = nullptr;
-    size_t scratch_bytes = 0;
-};
-
-struct qq_tensor {
-    qq_ctx* ctx = nullptr;
-    DTensor t;
-};
+using namespace qq3api;
 
 namespace {
-
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev) {
-        cudaGetDevice(&prev);
-        if (prev != dev) QQ_CUDA_TRY(cudaSetDevice(dev));
-    }
-    ~DeviceGuard() {
-        if (prev >= 0) cudaSetDevice(prev);
-    }
-};
-
-template <class F>
-int guard(F&& f) {
-    try {
-        f();
-        return QQ_OK;
-    } catch (const Error& e) {
-        qq3::set_error(e.msg);
-        return e.code;
-    } catch (const std::bad_alloc&) {
-        qq3::set_error("host allocation failed");
-        return QQ_ERR_OOM;
-    } catch (const std::exception& e) {
-        qq3::set_error(e.what());
-        return QQ_ERR_INVALID;
-    }
-}
 
 void* dmalloc(size_t bytes) {
     void* p = nullptr;
@@ -98,18 +55,6 @@ void* ctx_scratch(qq_ctx* c, size_t bytes) {
         c->scratch_bytes = bytes;
     }
     return c->scratch;
-}
-
-const DTensor* dt(qq_tensor* t) { return t ? &t->t : nullptr; }
-
-void need(bool cond, const std::string& msg) { QQ_CHECK(cond, QQ_ERR_INVALID, msg); }
-
-void check_shape(const DTensor* t, int type, int64_t ne0, int64_t ne1, int64_t ne2, const char* what) {
-    need(t != nullptr, std::string("missing tensor: ") + what);
-    need(t->type == type, std::string("wrong ggml type for ") + what);
-    need(t->ne[0] == ne0 && t->ne[1] == ne1 && t->ne[2] == ne2,
-         std::string("wrong shape for ") + what + ": got [" + std::to_string(t->ne[0]) + ", " +
-             std::to_string(t->ne[1]) + ", " + std::to_string(t->ne[2]) + "]");
 }
 
 }  // namespace
@@ -352,7 +297,7 @@ void run_tokens(qq_model* m, const int32_t* token_ids, int n, int seq, int pos0,
 
 extern "C" {
 
-const char* qq_last_error(void) { return qq3::g_err.c_str(); }
+const char* qq_last_error(void) { return qq3::last_error_cstr(); }
 
 int qq_init(const int* devices, int n_devices, qq_ctx** out) {
     return guard([&] {

@@ -95,7 +95,11 @@ _SIGS = {
     "qq_moe_block": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
     "qq_model_stat": (_I, [_P, _I, C.POINTER(_I64)]),
     "qq_bench_kernel": (_I, [_P, _I, _I, C.POINTER(C.c_float)]),
+    "qq_moe_block_noalloc": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
 }
+
+QQ_NOALLOC_MAX_TOKENS = 1024
+QQ_NOALLOC_MAX_FF = 4096
 
 QQ_STAT_STEP_KERNELS = 0
 QQ_STAT_N_MOE = 1
@@ -197,6 +201,13 @@ class Context:
     def moe_block(self, layer: LayerDesc, n_expert: int, top_k: int, x_dev, T: int, out_dev, routing_dev=None) -> None:
         check(self.lib.qq_moe_block(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(out_dev),
                                     _ptr(routing_dev)))
+
+
+    def moe_block_noalloc(self, layer: LayerDesc, n_expert: int, top_k: int, x_dev, T: int, out_dev,
+                          routing_dev=None) -> None:
+        """qq_moe_block without device allocation (scratch in the library's fixed device array)."""
+        check(self.lib.qq_moe_block_noalloc(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(out_dev),
+                                            _ptr(routing_dev)))
 
 
 class Tensor:
