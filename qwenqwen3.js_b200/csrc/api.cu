@@ -15,7 +15,10 @@
 #include <string>
 #include <vector>
 
+#include <numeric>
+
 #include "api_internal.h"
+#include "decode_prog.h"
 
 namespace qq3 {
 static thread_local std::string g_err;
@@ -100,6 +103,15 @@ struct qq_model {
     int* h_small = nullptr;   // pinned [4]
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
     cudaStream_t cap = nullptr;
+    // persistent decode kernel programs, per (sequence, with logits)
+    struct Prog {
+        qq3::PhaseDesc* d_prog = nullptr;
+        int n = 0;
+        qq3::DecodeCtl* ctl = nullptr;
+        unsigned int* done = nullptr;
+    };
+    std::map<std::pair<int, int>, Prog> progs;
+    int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
     size_t kv_stride_seq() const { return (size_t)n_attn * d.n_head_kv * d.max_ctx * d.head_dim; }
@@ -112,6 +124,12 @@ namespace {
 void free_model(qq_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     m->graphs.clear();
+    for (auto& kv : m->progs) {
+        if (kv.second.d_prog) cudaFree(kv.second.d_prog);
+        if (kv.second.ctl) cudaFree(kv.second.ctl);
+        if (kv.second.done) cudaFree(kv.second.done);
+    }
+    m->progs.clear();
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
                     m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
                     m->mask, m->ctl,
@@ -208,14 +226,208 @@ void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool d
     }
 }
 
+// The decode step as a phase program for the persistent kernel (kernels_decode.cu); the same
+// sequence of operations as enqueue_step.
+std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits) {
+    using namespace qq3;
+    const qq_model_desc& d = m->d;
+    const int E = d.n_embd, hd = d.head_dim, nq = d.n_head * hd, nkv = d.n_head_kv * hd;
+    std::vector<PhaseDesc> prog;
+    auto blank = [] {
+        PhaseDesc p;
+        std::memset(&p, 0, sizeof(p));
+        p.S = 1;
+        return p;
+    };
+    {
+        PhaseDesc p = blank();
+        p.type = PH_EMBED;
+        p.emb_qs = m->tok_embd->qs;
+        p.emb_d = m->tok_embd->d;
+        p.emb_K = (int)m->tok_embd->K;
+        p.n_vocab = d.n_vocab;
+        p.ctl = m->ctl;
+        p.y = m->hidden;
+        p.best = want_logits ? m->best : nullptr;
+        prog.push_back(p);
+    }
+    auto gemv = [&](int map, int epi, int S, int K, int n_items, const float* x, const float* norm_w) {
+        PhaseDesc p = blank();
+        p.type = PH_GEMV;
+        p.map = map;
+        p.epi = epi;
+        p.S = S;
+        p.K = K;
+        p.n_items = n_items;
+        p.x = x;
+        p.norm_w = norm_w;
+        p.eps = d.rms_eps;
+        p.G = qq3::decode_stage_items(S, K, n_items);
+        return p;
+    };
+    auto set_src = [](PhaseDesc& p, int i, const DTensor* t) {
+        p.qs[i] = t->qs;
+        p.d[i] = t->d;
+    };
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        const float* an = L.t[QQ_ATTN_NORM]->f32;
+        const float* fn = L.t[QQ_FFN_NORM]->f32;
+        if (L.attn) {
+            PhaseDesc q = gemv(MK_CONCAT3, EK_STORE, 1, E, nq + 2 * nkv, m->hidden, an);
+            set_src(q, 0, L.t[QQ_WQ]);
+            set_src(q, 1, L.t[QQ_WK]);
+            set_src(q, 2, L.t[QQ_WV]);
+            q.n0 = nq;
+            q.n1 = nkv;
+            q.G = qq3::decode_stage_items(1, E, std::gcd(nq, nkv));  // groups must not straddle q|k|v
+            q.y = m->qkv;
+            prog.push_back(q);
+            PhaseDesc a = blank();
+            a.type = PH_ATTN;
+            a.attn.qkv = m->qkv;
+            a.attn.q_norm = L.t[QQ_Q_NORM]->f32;
+            a.attn.k_norm = L.t[QQ_K_NORM]->f32;
+            a.attn.rope_cs = m->rope_cs;
+            a.attn.k_cache = m->k_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+            a.attn.v_cache = m->v_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+            a.attn.out = m->attn_out;
+            a.attn.part = m->attn_part;
+            a.attn.counter = m->attn_counter;
+            a.attn.pos = m->ctl + 1;
+            a.attn.n_head = d.n_head;
+            a.attn.n_kv = d.n_head_kv;
+            a.attn.hd = hd;
+            a.attn.max_ctx = d.max_ctx;
+            a.attn.n_split = m->n_split;
+            a.attn.eps = d.rms_eps;
+            prog.push_back(a);
+            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, nq, E, m->attn_out, nullptr);
+            set_src(o, 0, L.t[QQ_WO]);
+            o.y = m->hidden;
+            prog.push_back(o);
+        } else {
+            PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, m->hidden, an);
+            set_src(c, 0, L.t[QQ_IN_PROJ]);
+            c.stride = E;
+            c.conv_w = L.t[QQ_CONV]->f32;
+            c.state = m->conv(seq, l);
+            c.E = E;
+            c.y = m->y;
+            prog.push_back(c);
+            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, E, E, m->y, nullptr);
+            set_src(o, 0, L.t[QQ_OUT_PROJ]);
+            o.y = m->hidden;
+            prog.push_back(o);
+        }
+        if (L.moe) {
+            const int k = d.n_expert_used;
+            const int F = (int)L.t[QQ_GATE_EXPS]->ne[1];
+            PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_SWIGLU, 2, E, k * F, m->hidden, fn);
+            g.G = qq3::decode_stage_items(2, E, F);  // groups must not straddle experts
+            set_src(g, 0, L.t[QQ_GATE_EXPS]);
+            set_src(g, 1, L.t[QQ_UP_EXPS]);
+            g.r_qs = L.t[QQ_ROUTER]->qs;  // the router runs inside this phase, in every CTA
+            g.r_d = L.t[QQ_ROUTER]->d;
+            g.bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+            g.rec = m->rec + (size_t)L.moe_slot * m->rec_len;
+            g.ridx = m->ridx + (size_t)L.moe_slot * k;
+            g.rw = m->rw + (size_t)L.moe_slot * k;
+            g.n_expert = d.n_expert;
+            g.top_k = k;
+            g.mask = m->mask;
+            g.N = F;
+            g.y = m->h;
+            prog.push_back(g);
+            PhaseDesc dn = blank();
+            dn.type = PH_DOWN4;
+            dn.map = MK_DOWN4;
+            dn.G = 4;
+            dn.S = 4;
+            dn.K = F;
+            dn.n_items = E;
+            dn.x = m->h;
+            set_src(dn, 0, L.t[QQ_DOWN_EXPS]);
+            dn.top_k = k;
+            dn.mask = m->mask;
+            dn.N = E;
+            dn.y = m->hidden;
+            prog.push_back(dn);
+        } else {
+            const int F = (int)L.t[QQ_FFN_GATE]->ne[1];
+            PhaseDesc g = gemv(MK_PAIR, EK_SWIGLU, 2, E, F, m->hidden, fn);
+            set_src(g, 0, L.t[QQ_FFN_GATE]);
+            set_src(g, 1, L.t[QQ_FFN_UP]);
+            g.y = m->h;
+            prog.push_back(g);
+            PhaseDesc dn = gemv(MK_ROWS, EK_RESID, 1, F, E, m->h, nullptr);
+            set_src(dn, 0, L.t[QQ_FFN_DOWN]);
+            dn.y = m->hidden;
+            prog.push_back(dn);
+        }
+    }
+    if (want_logits) {
+        const DTensor* out = m->output ? m->output : m->tok_embd;
+        PhaseDesc h = gemv(MK_ROWS, EK_ARGMAX, 1, E, d.n_vocab, m->hidden, m->out_norm->f32);
+        h.G = qq3::decode_stage_items(1, E, d.n_vocab);
+        set_src(h, 0, out);
+        h.logits = m->logits;
+        h.best = m->best;
+        h.suppress = m->suppress;
+        prog.push_back(h);
+        PhaseDesc f = blank();
+        f.type = PH_FINISH;
+        f.best = m->best;
+        f.ctl = m->ctl;
+        f.trace = m->trace + (size_t)seq * (d.max_ctx + 1);
+        prog.push_back(f);
+    }
+    return prog;
+}
+
+bool mega_enabled(qq_model* m) {
+    if (m->mega < 0) {
+        // opt-in until the persistent step is faster than the per-phase kernels on every shape
+        const char* env = getenv("QQ3_PERSISTENT");
+        bool ok = env && atoi(env) != 0 && qq3::stream_path();
+        if (ok) {
+            for (const auto& p : build_program(m, 0, true))
+                if (!qq3::decode_phase_fits(p)) { ok = false; break; }
+        }
+        m->mega = ok ? 1 : 0;
+    }
+    return m->mega == 1;
+}
+
+qq_model::Prog& get_prog(qq_model* m, int seq, bool want_logits) {
+    auto key = std::make_pair(seq, want_logits ? 1 : 0);
+    auto it = m->progs.find(key);
+    if (it != m->progs.end()) return it->second;
+    std::vector<qq3::PhaseDesc> host = build_program(m, seq, want_logits);
+    qq_model::Prog pr;
+    pr.n = (int)host.size();
+    pr.d_prog = dalloc<qq3::PhaseDesc>(host.size());
+    pr.ctl = dalloc<qq3::DecodeCtl>(1);
+    pr.done = dalloc<unsigned int>(host.size());
+    cudaStream_t s = m->ctx->stream;
+    QQ_CUDA_TRY(cudaMemcpyAsync(pr.d_prog, host.data(), sizeof(qq3::PhaseDesc) * host.size(), cudaMemcpyHostToDevice, s));
+    QQ_CUDA_TRY(cudaMemsetAsync(pr.ctl, 0, sizeof(qq3::DecodeCtl), s));
+    QQ_CUDA_TRY(cudaMemsetAsync(pr.done, 0, sizeof(unsigned int) * host.size(), s));
+    QQ_CUDA_TRY(cudaStreamSynchronize(s));  // host vector goes out of scope
+    return m->progs[key] = pr;
+}
+
 cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
     auto key = std::make_pair(seq, want_logits ? 1 : 0);
     auto it = m->graphs.find(key);
     if (it != m->graphs.end()) return it->second;
     cudaGraph_t g = nullptr;
+    const bool mega = mega_enabled(m);
+    qq_model::Prog* pr = mega ? &get_prog(m, seq, want_logits) : nullptr;
     QQ_CUDA_TRY(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeRelaxed));
     try {
-        enqueue_step(m, seq, want_logits, m->cap, false);
+        if (mega) qq3::launch_decode_step(pr->d_prog, pr->n, pr->ctl, pr->done, qq3::kernel_err_ptr(), m->cap);
+        else enqueue_step(m, seq, want_logits, m->cap, false);
     } catch (...) {
         cudaStreamEndCapture(m->cap, &g);
         if (g) cudaGraphDestroy(g);
@@ -223,7 +435,7 @@ cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
         throw;
     }
     QQ_CUDA_TRY(cudaStreamEndCapture(m->cap, &g));
-    if (want_logits) {
+    if (want_logits && !mega) {
         size_t n = 0;
         cudaGraphGetNodes(g, nullptr, &n);
         std::vector<cudaGraphNode_t> nodes(n);
@@ -239,6 +451,7 @@ cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
     cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
     QQ_CUDA_TRY(e);
+    if (mega) m->step_kernels = 1;
     m->graphs[key] = ge;
     return ge;
 }

@@ -1,0 +1,84 @@
+// decode_prog.h -- the decode step as a device-side program of phases, run by one persistent
+// kernel (kernels_decode.cu).  Built once per (model, sequence) by the runtime (api.cu).
+#pragma once
+#include "kernels.h"
+
+namespace qq3 {
+
+enum PhaseType : int {
+    PH_EMBED = 0,   // hidden = dequantised embedding row of the token; argmax key reset
+    PH_GEMV = 1,    // streamed Q8_0 GEMV, one shared input (consumer mode A)
+    PH_DOWN4 = 2,   // MoE down + combine + residual over the 4 routed experts (consumer mode B)
+    PH_ATTN = 3,    // GQA decode attention with QK-norm, RoPE and KV append
+    PH_FINISH = 4,  // token = argmax, pos += 1, trace
+};
+
+enum MapKind : int { MK_ROWS = 0, MK_CONCAT3 = 1, MK_PAIR = 2, MK_STRIDE3 = 3, MK_EXPERT_PAIR = 4, MK_DOWN4 = 5 };
+
+enum EpiKind : int { EK_STORE = 0, EK_RESID = 1, EK_SWIGLU = 2, EK_CONV = 3, EK_ARGMAX = 4 };
+
+struct PhaseDesc {
+    int type, map, epi, S;
+    int K;        // inner dimension (input length)
+    int n_items;  // outputs of the phase
+    int pad0;
+    int G;        // items per stage (multiple of 4; stages are sized to ~16 KB for the bulk-copy stream)
+    // input
+    const float* x;       // mode A input, or the 4 expert inputs h[0..3] (stride K) for PH_DOWN4
+    const float* norm_w;  // fused RMSNorm weight (nullable)
+    float eps;
+    int n0, n1;           // MK_CONCAT3 boundaries
+    int N;                // rows per expert (expert maps)
+    int64_t stride;       // MK_STRIDE3
+    const int8_t* qs[3];
+    const __half* d[3];
+    int* ridx;            // routed expert ids / weights / record, written by CTA 0 for the host
+    float* rw;
+    float* rec;
+    const uint32_t* mask;
+    // epilogue
+    float* y;
+    const float* conv_w;
+    float* state;
+    int E;
+    int n_expert, top_k;
+    int pad1;
+    float* logits;
+    unsigned long long* best;
+    const int* suppress;
+    const int8_t* r_qs;     // router rows fused into the expert gate/up phase (nullable)
+    const __half* r_d;
+    const float* bias;
+    // attention / embed / finish
+    AttnArgs attn;
+    const int8_t* emb_qs;
+    const __half* emb_d;
+    int emb_K, n_vocab;
+    int* ctl;    // [token, pos]
+    int* trace;  // per-sequence greedy ids by position
+};
+
+// Per-launch control block of the persistent kernel.
+struct DecodeCtl {
+    unsigned int epoch;      // completed steps; counters below are cumulative (epoch * grid per phase)
+    unsigned int pad[31];
+};
+
+// Shared-memory plan of the persistent kernel: a byte ring of kDecRingBytes holding up to
+// kDecSlots in-flight stages of any size (so bytes in flight fill the ring whatever the phase),
+// the input digits of the current phase, and attention scratch.
+constexpr int kDecSlots = 16;
+constexpr int kDecRingBytes = 176 * 1024;
+constexpr int kDecMaxStageBytes = 40 * 1024;
+constexpr int kDecDigitBytes = 24 * 1024;
+constexpr int kDecAttnBytes = 16 * 1024;
+
+// Launch one decode step (grid = one CTA per SM).  done: [n_phases] cumulative counters.
+void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, unsigned int* done, int* err,
+                        cudaStream_t s);
+// Items per stage for a streamed phase (multiple of 4, dividing n_items when possible).
+int decode_stage_items(int S, int K, int n_items);
+// Whether a phase fits the persistent kernel's shared-memory plan.
+bool decode_phase_fits(const PhaseDesc& p);
+
+}  // namespace qq3

@@ -1,0 +1,1102 @@
+// kernels_decode.cu -- one persistent kernel per decode step (sm_100a).
+//
+// The decode step of Qwen3Engine.forward / Lfm2Engine.forward (qwen3-engine.js:115-245,
+// lfm2-engine.js:228-269) is a chain of ~100 dependent phases: embedding, per layer the
+// operator (short-conv or attention) and the FFN (dense, or router -> experts -> down), then
+// lm_head + argmax.  Launched as separate kernels, every phase pays a launch, a DRAM ramp and
+// a tail (about 3.5 us each on this part, measured), which is more than the data time of the
+// whole step.  Here one grid (one CTA per SM) runs all phases:
+//
+//  * the producer warp of each CTA walks the whole phase list and streams the weight rows of
+//    the groups this CTA owns into a ring of shared-memory slots with 1-D bulk copies.  Weights
+//    never depend on activations, so it runs ahead across phase boundaries; it only stops on
+//    a full ring, or before an expert gate/up phase until its own CTA has routed the token;
+//  * the consumer warps run the phases in order; between phases they wait on a grid-wide
+//    completion counter (cumulative across steps, so nothing is ever reset);
+//  * the MoE router is not a phase of its own: every CTA computes the 32 router logits and
+//    the top-k itself at the start of the expert gate/up phase (identical arithmetic in every
+//    CTA, so every CTA routes identically), which saves a grid-wide barrier per MoE layer;
+//  * a warp dots up to four rows at once, reading the activation digits of a chunk once for
+//    all of them;
+//  * every wait is bounded: on timeout the kernel records an error, raises an abort flag that
+//    all waits poll, drains its in-flight copies (bounded) and returns.
+#include "decode_prog.h"
+#include "gemv2_core.cuh"
+
+namespace qq3 {
+
+constexpr int kDecThreads = kThreads2;  // 8 consumer warps + 1 producer warp
+constexpr int kMaxRoutes = 32;          // experts the fused router handles
+constexpr int kMaxStageK = 8192;        // largest K of a streamed phase (4 staging passes)
+constexpr uint32_t kDecPrefetchBytes = 160 * 1024;  // L2 prefetch per CTA while a token is routed
+
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// wait until *c >= target (bounded; false on timeout or abort)
+__device__ __forceinline__ bool wait_count(const unsigned int* c, unsigned int target, int* err) {
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {  // each poll is an L2 round trip: ~2 s in all
+        if ((int)(ld_acquire(c) - target) >= 0) return true;
+        if ((it & 255u) == 255u && ld_volatile(err)) return false;
+    }
+    set_err(err, 3);
+    return false;
+}
+
+__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* err) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((it & 63u) == 63u && ld_volatile(err)) return false;
+    }
+    set_err(err, kErrFullWait);
+    return false;
+}
+
+__device__ __forceinline__ bool streamed(int type) { return type == PH_GEMV || type == PH_DOWN4; }
+
+__device__ __forceinline__ bool dec_masked(const uint32_t* mask, int e) {
+    return mask && ((mask[e >> 5] >> (e & 31)) & 1u);
+}
+
+struct DecRing {
+    uint8_t* base;       // kDecRingBytes
+    uint64_t* full;      // [kDecSlots]
+    uint64_t* empty;     // [kDecSlots]
+    uint32_t* off;       // [kDecSlots] ring offset of the stage in each descriptor
+    uint32_t* charge;    // [kDecSlots] ring bytes the stage holds (its size + any skipped ring end)
+};
+
+// Routing of the current MoE layer, computed by the CTA itself (shared memory).
+struct DecRoute {
+    int id[4];
+    float w[4];
+    float logit[kMaxRoutes];
+    uint64_t bar;  // completes once per MoE layer: the producer may read id[]
+};
+
+// Per-phase values the hot loops need, loaded once into registers (the descriptor lives in
+// global memory and every asm memory clobber would otherwise force it to be re-read).
+struct PhaseRegs {
+    int K, S, map, n_items, N, n0, n1, G;
+    int64_t stride;
+    const int8_t* q[3];
+    const __half* d[3];
+    int e[4];     // routed expert ids (expert maps)
+    bool on[4];   // source active (expert not masked)
+};
+
+__device__ __forceinline__ void load_phase(const PhaseDesc* pp, PhaseRegs& R, const DecRoute* route) {
+    R.K = pp->K; R.S = pp->S; R.map = pp->map; R.n_items = pp->n_items; R.N = pp->N;
+    R.n0 = pp->n0; R.n1 = pp->n1; R.stride = pp->stride; R.G = pp->G;
+    for (int s = 0; s < 3; s++) { R.q[s] = pp->qs[s]; R.d[s] = pp->d[s]; }
+    for (int s = 0; s < 4; s++) { R.e[s] = 0; R.on[s] = s < R.S; }
+    if (route) {
+        const uint32_t* mask = pp->mask;
+        for (int s = 0; s < 4; s++) {
+            R.e[s] = route->id[s];
+            R.on[s] = !dec_masked(mask, R.e[s]);
+        }
+    }
+}
+
+__device__ __forceinline__ bool expert_map(int map) { return map == MK_EXPERT_PAIR || map == MK_DOWN4; }
+
+// Row pointers of the group starting at item0 (registers only).
+__device__ __forceinline__ void group_ptrs(const PhaseRegs& R, int item0, const int8_t* (&q)[4],
+                                           const __half* (&d)[4], bool (&on)[4]) {
+    const int64_t K = R.K, KS = R.K >> 5;
+    switch (R.map) {
+        case MK_ROWS:
+            q[0] = R.q[0] + item0 * K; d[0] = R.d[0] + item0 * KS; on[0] = true;
+            break;
+        case MK_CONCAT3: {
+            const int t = item0 >= R.n0 + R.n1 ? 2 : (item0 >= R.n0 ? 1 : 0);
+            const int row = item0 - (t == 2 ? R.n0 + R.n1 : (t == 1 ? R.n0 : 0));
+            q[0] = R.q[t] + row * K; d[0] = R.d[t] + row * KS; on[0] = true;
+            break;
+        }
+        case MK_PAIR:
+            q[0] = R.q[0] + item0 * K; d[0] = R.d[0] + item0 * KS;
+            q[1] = R.q[1] + item0 * K; d[1] = R.d[1] + item0 * KS;
+            on[0] = on[1] = true;
+            break;
+        case MK_STRIDE3:
+            for (int s = 0; s < 3; s++) {
+                const int64_t row = item0 + s * R.stride;
+                q[s] = R.q[0] + row * K; d[s] = R.d[0] + row * KS; on[s] = true;
+            }
+            break;
+        case MK_EXPERT_PAIR: {
+            const int k = item0 / R.N, j0 = item0 - k * R.N;
+            const int64_t row = (int64_t)R.e[k] * R.N + j0;
+            q[0] = R.q[0] + row * K; d[0] = R.d[0] + row * KS;
+            q[1] = R.q[1] + row * K; d[1] = R.d[1] + row * KS;
+            on[0] = on[1] = R.on[k];
+            break;
+        }
+        case MK_DOWN4:
+            for (int s = 0; s < 4; s++) {
+                const int64_t row = (int64_t)R.e[s] * R.N + item0;
+                q[s] = R.q[0] + row * K; d[s] = R.d[0] + row * KS; on[s] = R.on[s];
+            }
+            break;
+    }
+}
+
+__device__ __forceinline__ uint32_t qs_stride(int G, int K) { return (uint32_t)G * K; }
+__device__ __forceinline__ uint32_t d_stride(int G, int K) { return round16((uint32_t)G * (K >> 4)); }
+__device__ __forceinline__ uint32_t stage_bytes(int S, int G, int K) {
+    return (S * (qs_stride(G, K) + d_stride(G, K)) + 127u) & ~127u;
+}
+
+// ---- producer ------------------------------------------------------------------------------
+
+// L2 prefetch of the rows this CTA will stream for phase pp; returns the bytes requested.
+__device__ uint32_t prefetch_phase(const PhaseDesc* pp, const DecRoute* route) {
+    PhaseRegs R;
+    load_phase(pp, R, route);
+    const int K = R.K, G = R.G;
+    const int n_groups = (R.n_items + G - 1) / G;
+    uint32_t bytes = 0;
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
+        const int rows = min(G, R.n_items - g * G);
+        const int8_t* q[4];
+        const __half* d[4];
+        bool on[4] = {false, false, false, false};
+        group_ptrs(R, g * G, q, d, on);
+        const uint32_t qb = (uint32_t)rows * K, db = round16((uint32_t)rows * (K >> 4));
+        for (int s = 0; s < R.S; s++) {
+            if (!on[s]) continue;
+            bulk_prefetch_l2(q[s], qb);
+            bulk_prefetch_l2(d[s], db);
+            bytes += qb + db;
+        }
+    }
+    return bytes;
+}
+
+// Splits of the context used this step: at most one (kv head, split) item per CTA.
+__device__ __forceinline__ int dec_attn_splits(const AttnArgs& a) {
+    int n = (int)gridDim.x / a.n_kv;
+    if (n > a.n_split) n = a.n_split;
+    return n < 1 ? 1 : n;
+}
+
+// Positions [p0, p1) of the context that split `split` of n_split covers at length len.
+__device__ __forceinline__ void dec_attn_range(int len, int n_split, int split, int& p0, int& p1) {
+    int chunk = (len + n_split - 1) / n_split;
+    if (chunk < 32) chunk = 32;
+    p0 = split * chunk;
+    p1 = min(len, p0 + chunk);
+}
+
+// L2 prefetch of what this CTA's attention item reads: the cached K/V rows before `pos`, the
+// head norms and the RoPE row.
+__device__ void prefetch_attention(const AttnArgs& a) {
+    const int pos = *a.pos;
+    const int n_split = dec_attn_splits(a);
+    const int item = blockIdx.x;
+    if (item >= a.n_kv * n_split || pos < 0 || pos >= a.max_ctx) return;
+    const int kvh = item / n_split, split = item - kvh * n_split;
+    int p0, p1;
+    dec_attn_range(pos + 1, n_split, split, p0, p1);
+    p1 = min(p1, pos);  // the row at pos is written this step
+    if (p0 < p1) {
+        const uint32_t bytes = (uint32_t)(p1 - p0) * a.hd * 4u;
+        bulk_prefetch_l2(a.k_cache + ((size_t)kvh * a.max_ctx + p0) * a.hd, bytes);
+        bulk_prefetch_l2(a.v_cache + ((size_t)kvh * a.max_ctx + p0) * a.hd, bytes);
+    }
+    bulk_prefetch_l2(a.rope_cs + (size_t)pos * a.hd, 4u * a.hd);
+    bulk_prefetch_l2(a.q_norm, 4u * a.hd);
+    bulk_prefetch_l2(a.k_norm, 4u * a.hd);
+}
+
+// Ring bookkeeping of the producer thread: stages are issued in consumption order into a byte
+// ring; a stage that does not fit before the ring end starts at offset 0 and is charged the
+// skipped bytes too.
+struct ProdRing {
+    uint32_t i = 0;         // stages issued
+    uint32_t tail = 0;      // oldest stage not yet known to be released
+    uint32_t head = 0;      // next free ring offset
+    uint32_t inflight = 0;  // ring bytes held by stages tail..i-1
+
+    // Reserve `need` bytes for stage i; false on a timeout or abort.
+    __device__ __forceinline__ bool alloc(const DecRing& r, uint32_t need, int* err, int& slot, uint8_t*& sb) {
+        const bool wrap = head + need > (uint32_t)kDecRingBytes;
+        const uint32_t charge = need + (wrap ? kDecRingBytes - head : 0u);
+        while (tail < i && (i - tail >= (uint32_t)kDecSlots || inflight + charge > (uint32_t)kDecRingBytes)) {
+            if (!slot_wait(&r.empty[tail % kDecSlots], (tail / kDecSlots) & 1u, err)) return false;
+            inflight -= r.charge[tail % kDecSlots];
+            ++tail;
+        }
+        slot = i % kDecSlots;
+        const uint32_t off = wrap ? 0u : head;
+        head = off + need;
+        inflight += charge;
+        r.charge[slot] = charge;
+        r.off[slot] = off;
+        sb = r.base + off;
+        return true;
+    }
+};
+
+__device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, DecRoute* route, int* err) {
+    ProdRing pr;
+    uint32_t routed = 0;  // MoE layers whose routing this CTA has seen
+    for (int ph = 0; ph < n_phases; ph++) {
+        const PhaseDesc* pp = prog + ph;
+        if (pp->type == PH_ATTN) prefetch_attention(pp->attn);
+        if (!streamed(pp->type)) continue;
+        const bool ex = expert_map(pp->map);
+        if (pp->map == MK_EXPERT_PAIR) {
+            // The router rows go first, as two stages of up to 16 rows (one per consumer set).
+            const int K = pp->K, ne = pp->n_expert;
+            for (int h = 0; h < 2; ++h, ++pr.i) {
+                int slot;
+                uint8_t* sb;
+                if (!pr.alloc(r, stage_bytes(1, 16, K), err, slot, sb)) goto drain;
+                const int rows = max(0, min(16, ne - 16 * h));
+                const uint32_t qb = (uint32_t)rows * K, db = round16((uint32_t)rows * (K >> 4));
+                mbar_arrive_expect_tx(&r.full[slot], rows ? qb + db : 0u);
+                if (rows) {
+                    bulk_g2s(sb, pp->r_qs + (int64_t)16 * h * K, qb, &r.full[slot]);
+                    bulk_g2s(sb + qs_stride(16, K), pp->r_d + (int64_t)16 * h * (K >> 5), db, &r.full[slot]);
+                }
+            }
+            // While the consumers route the token, pull the next layer's operator rows into L2
+            // (they depend on nothing); then wait for this CTA's routing.
+            uint32_t budget = kDecPrefetchBytes;
+            for (int ph2 = ph + 1; ph2 < n_phases && budget > 0; ph2++) {
+                const PhaseDesc* p2 = prog + ph2;
+                if (p2->map == MK_EXPERT_PAIR) break;
+                if (!streamed(p2->type) || expert_map(p2->map)) continue;
+                const uint32_t b = prefetch_phase(p2, nullptr);
+                budget = b >= budget ? 0u : budget - b;
+            }
+            if (!slot_wait(&route->bar, routed & 1u, err)) goto drain;
+            ++routed;
+        }
+        {
+            PhaseRegs R;
+            load_phase(pp, R, ex ? route : nullptr);
+            const int K = R.K, S = R.S, G = R.G;
+            const uint32_t need = stage_bytes(S, G, K), qsz = qs_stride(G, K), dsz = d_stride(G, K);
+            const int n_groups = (R.n_items + G - 1) / G;
+            for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++pr.i) {
+                int slot;
+                uint8_t* sb;
+                if (!pr.alloc(r, need, err, slot, sb)) goto drain;
+                const int item0 = g * G;
+                const int rows = min(G, R.n_items - item0);
+                const int8_t* q[4];
+                const __half* d[4];
+                bool on[4] = {false, false, false, false};
+                group_ptrs(R, item0, q, d, on);
+                const uint32_t qb = (uint32_t)rows * K, db = round16((uint32_t)rows * (K >> 4));
+                uint32_t tx = 0;
+                for (int s = 0; s < S; s++)
+                    if (on[s]) tx += qb + db;
+                mbar_arrive_expect_tx(&r.full[slot], tx);  // release: publishes r.off[slot] too
+                for (int s = 0; s < S; s++) {
+                    if (!on[s]) continue;
+                    bulk_g2s(sb + s * qsz, q[s], qb, &r.full[slot]);
+                    bulk_g2s(sb + S * qsz + s * dsz, d[s], db, &r.full[slot]);
+                }
+                if (pp->epi == EK_CONV) {  // the epilogue's conv state and taps of these items
+                    bulk_prefetch_l2(pp->state + item0, 4u * rows);
+                    bulk_prefetch_l2(pp->state + pp->E + item0, 4u * rows);
+                    bulk_prefetch_l2(pp->conv_w + 3 * item0, 12u * rows);
+                }
+            }
+        }
+    }
+    return;
+drain:
+    // abort: let every copy already issued land before the CTA exits (bounded)
+    for (uint32_t j = pr.tail; j < pr.i; ++j) slot_wait(&r.full[j % kDecSlots], (j / kDecSlots) & 1u, err);
+}
+
+// ---- consumer helpers --------------------------------------------------------------------
+
+// Digitise an input of runtime length K <= kMaxStageK (8 elements per consumer thread per
+// pass, at most 4 passes held in registers), with an optional RMSNorm (tensor.js:103-114;
+// sum of squares in double as the JS does).
+__device__ void dec_stage_digits(const float* __restrict__ x, const float* __restrict__ norm_w, float eps, int K,
+                                 uint4* dig, float* xsc, double* red) {
+    const int t = threadIdx.x;
+    float xv[4][8];
+    double ss = 0.0;
+#pragma unroll
+    for (int ps = 0; ps < 4; ps++) {
+        const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+        if (e0 < K) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(x + e0));
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(x + e0) + 1);
+            xv[ps][0] = a.x; xv[ps][1] = a.y; xv[ps][2] = a.z; xv[ps][3] = a.w;
+            xv[ps][4] = b.x; xv[ps][5] = b.y; xv[ps][6] = b.z; xv[ps][7] = b.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) xv[ps][e] = 0.f;
+        }
+    }
+    if (norm_w) {
+#pragma unroll
+        for (int ps = 0; ps < 4; ps++)
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss += (double)xv[ps][e] * xv[ps][e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((t & 31) == 0) red[t >> 5] = ss;
+        named_bar(1, kConsumerThreads);
+        double tot = 0.0;
+#pragma unroll
+        for (int w = 0; w < kCW; w++) tot += red[w];
+        const float inv = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
+#pragma unroll
+        for (int ps = 0; ps < 4; ps++) {
+            const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+            if (e0 < K) {
+                const float4 wa = reinterpret_cast<const float4*>(norm_w + e0)[0];
+                const float4 wb = reinterpret_cast<const float4*>(norm_w + e0)[1];
+                const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                for (int e = 0; e < 8; e++) xv[ps][e] = (wv[e] * xv[ps][e]) * inv;
+            }
+        }
+    }
+#pragma unroll
+    for (int ps = 0; ps < 4; ps++) {
+        const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+        if (ps * 8 * kConsumerThreads < K) digitise8(xv[ps], e0, K, dig, xsc);
+    }
+}
+
+// 24 dp4a of one 32-weight Q8_0 block (w0 | w1) against its three digit planes, combined in
+// fp32: (i1 + i2/254 + i3/254^2).  |i| <= 32*127*127 < 2^22, so the conversions are exact.
+__device__ __forceinline__ float block_dot(const uint4 w0, const uint4 w1, const uint4 (&g)[3][2]) {
+    int a1 = __dp4a((int)w0.x, (int)g[0][0].x, 0);
+    int a2 = __dp4a((int)w0.x, (int)g[1][0].x, 0);
+    int a3 = __dp4a((int)w0.x, (int)g[2][0].x, 0);
+    a1 = __dp4a((int)w0.y, (int)g[0][0].y, a1);
+    a2 = __dp4a((int)w0.y, (int)g[1][0].y, a2);
+    a3 = __dp4a((int)w0.y, (int)g[2][0].y, a3);
+    a1 = __dp4a((int)w0.z, (int)g[0][0].z, a1);
+    a2 = __dp4a((int)w0.z, (int)g[1][0].z, a2);
+    a3 = __dp4a((int)w0.z, (int)g[2][0].z, a3);
+    a1 = __dp4a((int)w0.w, (int)g[0][0].w, a1);
+    a2 = __dp4a((int)w0.w, (int)g[1][0].w, a2);
+    a3 = __dp4a((int)w0.w, (int)g[2][0].w, a3);
+    a1 = __dp4a((int)w1.x, (int)g[0][1].x, a1);
+    a2 = __dp4a((int)w1.x, (int)g[1][1].x, a2);
+    a3 = __dp4a((int)w1.x, (int)g[2][1].x, a3);
+    a1 = __dp4a((int)w1.y, (int)g[0][1].y, a1);
+    a2 = __dp4a((int)w1.y, (int)g[1][1].y, a2);
+    a3 = __dp4a((int)w1.y, (int)g[2][1].y, a3);
+    a1 = __dp4a((int)w1.z, (int)g[0][1].z, a1);
+    a2 = __dp4a((int)w1.z, (int)g[1][1].z, a2);
+    a3 = __dp4a((int)w1.z, (int)g[2][1].z, a3);
+    a1 = __dp4a((int)w1.w, (int)g[0][1].w, a1);
+    a2 = __dp4a((int)w1.w, (int)g[1][1].w, a2);
+    a3 = __dp4a((int)w1.w, (int)g[2][1].w, a3);
+    return fmaf(i2f_small(a3), 1.0f / 64516.0f, fmaf(i2f_small(a2), 1.0f / 254.0f, i2f_small(a1)));
+}
+
+// Lane partials of up to NR rows against the staged input.  Lane l takes the 32-weight blocks
+// l, l+32, ... of every row (one float combination per block); the digits of a block are read
+// once for all rows of the batch.  Each row adds its blocks in that order wherever it lives
+// (ring slot in shared memory, or global memory for the router rows).
+template <int NR, bool GLOBAL>
+__device__ __forceinline__ void rows_dot(const int8_t* const (&q)[NR], const __half* const (&d)[NR], int n_rows,
+                                         const uint4* dig, const float* xsc, int nch, int pstride, float (&acc)[NR]) {
+    const int lane = threadIdx.x & 31;
+    const int nb = nch >> 1;
+#pragma unroll
+    for (int r = 0; r < NR; r++) acc[r] = 0.f;
+#pragma unroll 2
+    for (int b = lane; b < nb; b += 32) {
+        uint4 g[3][2];
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            g[pl][0] = dig[pl * pstride + 2 * b];
+            g[pl][1] = dig[pl * pstride + 2 * b + 1];
+        }
+        const float sx = xsc[b];
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+            if (r < n_rows) {
+                const uint4* wp = reinterpret_cast<const uint4*>(q[r] + 32 * b);
+                const uint4 w0 = GLOBAL ? __ldg(wp) : wp[0];
+                const uint4 w1 = GLOBAL ? __ldg(wp + 1) : wp[1];
+                const float dw = __half2float(GLOBAL ? __ldg(d[r] + b) : d[r][b]);
+                acc[r] = fmaf(block_dot(w0, w1, g), dw * sx, acc[r]);
+            }
+        }
+    }
+}
+
+// Warp sums of NR (1, 2 or 4) lane values by halving: a level exchanges half of the values a
+// lane still holds.  Returns the sum of row (lane >> 3) for NR = 4, (lane >> 4) for NR = 2,
+// row 0 for NR = 1, in every lane of that row's group.
+template <int NR>
+__device__ __forceinline__ float warp_reduce_rows(const float (&v)[NR]) {
+    const int lane = threadIdx.x & 31;
+    float k;
+    if (NR == 4) {
+        const bool hi = lane & 16;
+        float k0 = hi ? v[2 % NR] : v[0];
+        float k1 = hi ? v[3 % NR] : v[1 % NR];
+        const float s0 = hi ? v[0] : v[2 % NR];
+        const float s1 = hi ? v[1 % NR] : v[3 % NR];
+        k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+        k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+        const bool b3 = lane & 8;
+        k = b3 ? k1 : k0;
+        k += __shfl_xor_sync(0xffffffffu, b3 ? k0 : k1, 8);
+    } else if (NR == 2) {
+        const bool hi = lane & 16;
+        k = hi ? v[1 % NR] : v[0];
+        k += __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[1 % NR], 16);
+        k += __shfl_xor_sync(0xffffffffu, k, 8);
+    } else {
+        k = v[0];
+        k += __shfl_xor_sync(0xffffffffu, k, 16);
+        k += __shfl_xor_sync(0xffffffffu, k, 8);
+    }
+    k += __shfl_xor_sync(0xffffffffu, k, 4);
+    k += __shfl_xor_sync(0xffffffffu, k, 2);
+    k += __shfl_xor_sync(0xffffffffu, k, 1);
+    return k;
+}
+
+// butterfly sums of the first n (warp-uniform) of N lane values, interleaved
+template <int N>
+__device__ __forceinline__ void warp_sum_n(float (&v)[N], int n) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < N; j++)
+            if (j < n) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g * (1.0f / (1.0f + expf(-g))) * u; }
+
+// ---- the fused router (every CTA, at the start of the expert gate/up phase) -----------------
+// lfm2-engine.js:417-447: logits = W_router . norm(h); p = sigmoid(logits); top-k on p + bias
+// (stable: the lower expert id wins a tie); weights = p / (sum + 1e-6).
+__device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
+                          int nch, DecRoute* route, int* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int K = p.K, ne = p.n_expert;
+    const int set = warp / 4, w = warp % 4;
+    // the router rows arrive as two ring stages of 16 rows; warp w of the set dots rows 4w..4w+3
+    for (int h = 0; h < 2; h++) {
+        const uint32_t ih = i + h;
+        if ((int)(ih % kSets) != set) continue;
+        const int slot = ih % kDecSlots;
+        const bool ok = slot_wait(&r.full[slot], (ih / kDecSlots) & 1u, err);
+        const uint8_t* sb = r.base + r.off[slot];
+        const int row0 = 16 * h + 4 * w;
+        const int n_rows = ok ? max(0, min(4, ne - row0)) : 0;
+        const int8_t* q[4];
+        const __half* d[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            q[j] = reinterpret_cast<const int8_t*>(sb) + (size_t)(4 * w + j) * K;
+            d[j] = reinterpret_cast<const __half*>(sb + qs_stride(16, K)) + (4 * w + j) * (K >> 5);
+        }
+        float acc[4];
+        rows_dot<4, false>(q, d, n_rows, dig, xsc, nch, nch, acc);
+        const float sum = warp_reduce_rows<4>(acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+        const int j = lane >> 3;
+        if ((lane & 7) == 0 && j < n_rows) route->logit[row0 + j] = sum;
+    }
+    i += 2;
+    named_bar(1, kConsumerThreads);
+    if (warp == 0) {
+        const bool live = lane < ne;
+        const float prob = live ? 1.0f / (1.0f + expf(-route->logit[lane])) : 0.f;
+        const float sel = live ? prob + (p.bias ? p.bias[lane] : 0.f) : -INFINITY;
+        bool taken = !live;
+        double sum_w = 1e-6;
+        int top_i[4];
+        float top_p[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            float bv = taken ? -INFINITY : sel;
+            int bi = taken ? 0x7fffffff : lane;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            bi = __shfl_sync(0xffffffffu, bi, 0);
+            if (bi < 0 || bi >= ne) bi = 0;
+            if (lane == bi) taken = true;
+            top_i[k] = bi;
+            top_p[k] = __shfl_sync(0xffffffffu, prob, bi & 31);
+            sum_w += (double)top_p[k];
+        }
+        const double inv = 1.0 / sum_w;
+        if (lane < 4) {
+            float wk = 0.f;
+            int ik = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (lane == k) { wk = (float)((double)top_p[k] * inv); ik = top_i[k]; }
+            route->id[lane] = ik;
+            route->w[lane] = wk;
+            if (blockIdx.x == 0) {
+                p.ridx[lane] = ik;
+                p.rw[lane] = wk;
+                p.rec[lane] = (float)ik;
+                p.rec[4 + lane] = wk;
+            }
+        }
+        if (blockIdx.x == 0 && live) p.rec[8 + lane] = prob;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&route->bar);  // release: the producer may read id[]
+    }
+    named_bar(1, kConsumerThreads);
+}
+
+// ---- mode A: one shared input, S sources per item, G = 4 IPW items per stage ------------------
+// The four warps of a set share each stage: warp w takes items w IPW .. w IPW + IPW - 1, i.e.
+// NR = S IPW <= 4 rows (item-major, source-minor), so its row dots and reductions overlap.
+template <int S, int IPW>
+__device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R, const DecRing& r, uint32_t& i,
+                                          const uint4* dig, const float* xsc, unsigned long long& best_k, int* err) {
+    constexpr int NR = S * IPW;
+    constexpr int NRP = NR == 3 ? 4 : NR;  // rows padded for the halving reduction
+    constexpr int SH = NRP == 4 ? 3 : (NRP == 2 ? 4 : 5);  // lane >> SH = row of the reduced sum
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int set = warp / 4, w = warp % 4;
+    const int K = R.K, nch = K >> 4;
+    constexpr int G = 4 * IPW;
+    const uint32_t qsz = qs_stride(G, K), dsz = d_stride(G, K);
+    const int n_groups = (R.n_items + G - 1) / G;
+    const int epi = p.epi;
+    const int skip = (epi == EK_ARGMAX && p.suppress) ? *p.suppress : -1;
+    float* const y = p.y;
+    // the lane that finishes item j of the warp (after the reduction it holds the item's first
+    // source; the other sources come from the lanes of the next row groups)
+    const int row = lane >> SH;
+    const bool lead = (lane & ((1 << SH) - 1)) == 0 && row < NR && row % S == 0;
+    const int my_j = row / S;
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
+        if ((int)(i % kSets) != set) continue;
+        const int slot = i % kDecSlots;
+        // on a timeout leave the loop but keep every later barrier of the CTA (the next
+        // phase wait sees the error word and all consumer warps return together)
+        if (!slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err)) break;
+        const uint8_t* sb = r.base + r.off[slot];
+        const bool gon = R.map != MK_EXPERT_PAIR || R.on[(g * G) / R.N];
+        const int li0 = w * IPW;
+        const int n_left = R.n_items - g * G - li0;  // items of this warp that exist
+        const int n_ok = !gon ? 0 : (n_left >= IPW ? IPW : (n_left > 0 ? n_left : 0));
+        const int item = g * G + li0 + my_j;
+        const bool mine = lead && my_j < n_ok;
+        float pre[5] = {0.f, 0.f, 0.f, 0.f, 0.f};  // epilogue operands, fetched before the dots
+        if (mine) {
+            if (epi == EK_RESID) {
+                pre[0] = __ldcg(y + item);
+            } else if (epi == EK_CONV) {
+                pre[0] = p.state[item];
+                pre[1] = p.state[p.E + item];
+                pre[2] = p.conv_w[item * 3];
+                pre[3] = p.conv_w[item * 3 + 1];
+                pre[4] = p.conv_w[item * 3 + 2];
+            }
+        }
+        const int8_t* q[NRP];
+        const __half* d[NRP];
+#pragma unroll
+        for (int j = 0; j < NRP; j++) {
+            const int jj = j < NR ? j : 0;
+            const int li = li0 + jj / S, s = jj % S;
+            q[j] = reinterpret_cast<const int8_t*>(sb + s * qsz) + (size_t)li * K;
+            d[j] = reinterpret_cast<const __half*>(sb + S * qsz + s * dsz) + li * (K >> 5);
+        }
+        float acc[NRP];
+        rows_dot<NRP, false>(q, d, n_ok * S, dig, xsc, nch, nch, acc);
+        const float a0 = warp_reduce_rows<NRP>(acc);
+        const float a1 = S > 1 ? __shfl_down_sync(0xffffffffu, a0, 1 << SH) : 0.f;
+        const float a2 = S > 2 ? __shfl_down_sync(0xffffffffu, a0, 2 << SH) : 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+        if (mine) {
+            switch (epi) {
+                case EK_STORE: y[item] = a0; break;
+                case EK_RESID: y[item] = pre[0] + a0; break;
+                case EK_SWIGLU: y[item] = silu_mul(a0, a1); break;
+                case EK_CONV: {  // lfm2-engine.js:294-321
+                    const float bx = a0 * a2;
+                    const float co = pre[2] * pre[0] + pre[3] * pre[1] + pre[4] * bx;
+                    p.state[item] = pre[1];
+                    p.state[p.E + item] = bx;
+                    y[item] = a1 * co;
+                    break;
+                }
+                case EK_ARGMAX: {
+                    p.logits[item] = a0;
+                    if (item != skip) {
+                        const unsigned long long k = argmax_key(a0, item);
+                        if (k > best_k) best_k = k;
+                    }
+                    break;
+                }
+            }
+        }
+    }
+}
+
+// ---- mode B: MoE down + combine + residual (4 sources with their own inputs) -----------------
+// Warp (set, src) holds the digits of expert input src; per stage it dots the kG rows of its
+// source, the set combines them in expert-slot order (lfm2-engine.js:459-486).
+__device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R, const DecRing& r, uint32_t& i,
+                                          const uint4* dg, const float* xsc, const DecRoute* route,
+                                          float (*part)[kG][4], int* set_ok, int* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int src = warp % 4, set = warp / 4;
+    const int K = R.K, nch = K >> 4;
+    float* const y = p.y;
+    float wk[4];
+#pragma unroll
+    for (int s = 0; s < 4; s++) wk[s] = route->w[s];
+    const uint32_t qsz = qs_stride(kG, K), dsz = d_stride(kG, K);
+    const int n_groups = (R.n_items + kG - 1) / kG;
+    for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
+        if ((int)(i % 2) != set) continue;
+        const int slot = i % kDecSlots;
+        const int rows = min(kG, R.n_items - g * kG);
+        const bool mine = src == 0 && lane < rows;
+        const float yold = mine ? __ldcg(y + g * kG + lane) : 0.f;
+        // one warp of the set waits; the set follows it through a named barrier, so a
+        // timeout makes the same decision in all four warps
+        if (src == 0 && lane == 0) set_ok[set] = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err) ? 1 : 0;
+        named_bar(2 + set, 128);
+        if (!set_ok[set]) break;
+        const uint8_t* sb = r.base + r.off[slot];
+        const int8_t* q[kG];
+        const __half* d[kG];
+#pragma unroll
+        for (int j = 0; j < kG; j++) {
+            q[j] = reinterpret_cast<const int8_t*>(sb + src * qsz) + (size_t)j * K;
+            d[j] = reinterpret_cast<const __half*>(sb + 4 * qsz + src * dsz) + j * (K >> 5);
+        }
+        float acc[kG];
+        rows_dot<kG, false>(q, d, R.on[src] ? rows : 0, dg, xsc, nch, 4 * nch, acc);
+        const float sum = warp_reduce_rows<kG>(acc);
+        if ((lane & 7) == 0) part[set][lane >> 3][src] = sum;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&r.empty[slot]);
+        named_bar(2 + set, 128);
+        if (mine) {
+            float moe = 0.f;
+#pragma unroll
+            for (int s = 0; s < 4; s++)
+                if (R.on[s]) moe += wk[s] * part[set][lane][s];
+            y[g * kG + lane] = yold + moe;
+        }
+        named_bar(2 + set, 128);
+    }
+}
+
+// ---- attention phase (8 consumer warps per (kv head, split) item) ------------------------
+
+template <int HD>
+__device__ void dec_norm_rope(float* v, const float* __restrict__ w, float eps, const float* __restrict__ cs) {
+    const int lane = threadIdx.x & 31;
+    double ss = 0.0;
+    for (int i = lane; i < HD; i += 32) ss += (double)v[i] * v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = (float)(1.0 / sqrt(ss / (double)HD + (double)eps));
+    __syncwarp();
+    for (int i = lane; i < HD; i += 32) v[i] = (w[i] * v[i]) * inv;
+    __syncwarp();
+    constexpr int half = HD / 2;
+    for (int i = lane; i < half; i += 32) {
+        const float c = cs[2 * i], s = cs[2 * i + 1];
+        const float x0 = v[i], x1 = v[i + half];
+        v[i] = x0 * c - x1 * s;
+        v[i + half] = x0 * s + x1 * c;
+    }
+    __syncwarp();
+}
+
+template <int HD>
+__device__ void dec_attention(const AttnArgs& a, float* scratch) {
+    constexpr int PL = HD / 32;
+    constexpr int W = kCW;
+    const int G = a.n_head / a.n_kv;
+    float* q_s = scratch;                      // [G][HD]
+    float* kv_s = q_s + 8 * HD;                // [2][HD]
+    float* m_s = kv_s + 2 * HD;                // [W][8]
+    float* l_s = m_s + W * 8;                  // [W][8]
+    float* acc_s = l_s + W * 8;                // [W][G][HD] (G <= 4 for HD=128, <= 8 for HD=64)
+    __shared__ int is_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = *a.pos;
+    const int len = pos + 1;
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    const float* cs = a.rope_cs + (size_t)pos * HD;
+    const int n_split = dec_attn_splits(a);
+    const int n_items = a.n_kv * n_split;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int kvh = item / n_split, split = item - kvh * n_split;
+        int p0, p1;
+        dec_attn_range(len, n_split, split, p0, p1);
+        float* kc = a.k_cache + (size_t)kvh * a.max_ctx * HD;
+        float* vc = a.v_cache + (size_t)kvh * a.max_ctx * HD;
+        float* part_base = a.part + (size_t)kvh * G * a.n_split * (HD + 2);
+        if (p0 < p1) {
+            for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads)
+                q_s[i] = __ldcg(a.qkv + (size_t)kvh * G * HD + i);
+            const bool owns = p0 <= pos && pos < p1;
+            if (owns)
+                for (int d = threadIdx.x; d < HD; d += kConsumerThreads) {
+                    kv_s[d] = __ldcg(a.qkv + (size_t)a.n_head * HD + (size_t)kvh * HD + d);
+                    kv_s[HD + d] = __ldcg(a.qkv + (size_t)(a.n_head + a.n_kv) * HD + (size_t)kvh * HD + d);
+                }
+            named_bar(1, kConsumerThreads);
+            for (int g = warp; g < G; g += W) dec_norm_rope<HD>(q_s + g * HD, a.q_norm, a.eps, cs);
+            if (owns && warp == W - 1) {
+                dec_norm_rope<HD>(kv_s, a.k_norm, a.eps, cs);
+                for (int d = lane; d < HD; d += 32) {
+                    kc[(size_t)pos * HD + d] = kv_s[d];
+                    vc[(size_t)pos * HD + d] = kv_s[HD + d];
+                }
+            }
+            named_bar(1, kConsumerThreads);
+            float m[8], l[8], acc[8][PL], qv[8][PL];
+#pragma unroll
+            for (int g = 0; g < 8; g++) {
+                m[g] = -INFINITY;
+                l[g] = 0.f;
+#pragma unroll
+                for (int j = 0; j < PL; j++) {
+                    acc[g][j] = 0.f;
+                    qv[g][j] = g < G ? q_s[g * HD + lane * PL + j] : 0.f;
+                }
+            }
+            constexpr int U = 4;  // positions per warp whose K/V loads are in flight together
+            for (int pb = p0 + warp; pb < p1; pb += U * W) {
+                float kr[U][PL], vr[U][PL];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int p = pb + u * W;
+                    // the row at `pos` was written above by this CTA: read it from shared memory
+                    const bool own_row = owns && p == pos;
+#pragma unroll
+                    for (int j = 0; j < PL; j++) {
+                        kr[u][j] = 0.f;
+                        vr[u][j] = 0.f;
+                        if (p < p1) {
+                            kr[u][j] = own_row ? kv_s[lane * PL + j] : __ldcg(kc + (size_t)p * HD + lane * PL + j);
+                            vr[u][j] = own_row ? kv_s[HD + lane * PL + j] : __ldcg(vc + (size_t)p * HD + lane * PL + j);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    if (pb + u * W >= p1) break;
+                    float dot[8];
+#pragma unroll
+                    for (int g = 0; g < 8; g++) {
+                        dot[g] = 0.f;
+#pragma unroll
+                        for (int j = 0; j < PL; j++) dot[g] = fmaf(qv[g][j], kr[u][j], dot[g]);
+                    }
+                    warp_sum_n(dot, G);
+#pragma unroll
+                    for (int g = 0; g < 8; g++) {
+                        if (g >= G) break;
+                        const float sc = dot[g] * scale;
+                        const float mn = fmaxf(m[g], sc);
+                        const float cf = expf(m[g] - mn), pe = expf(sc - mn);
+                        l[g] = l[g] * cf + pe;
+#pragma unroll
+                        for (int j = 0; j < PL; j++) acc[g][j] = fmaf(acc[g][j], cf, pe * vr[u][j]);
+                        m[g] = mn;
+                    }
+                }
+            }
+            for (int g = 0; g < G; g++) {
+                if (lane == 0) { m_s[warp * 8 + g] = m[g]; l_s[warp * 8 + g] = l[g]; }
+#pragma unroll
+                for (int j = 0; j < PL; j++) acc_s[((size_t)warp * G + g) * HD + lane * PL + j] = acc[g][j];
+            }
+            named_bar(1, kConsumerThreads);
+            for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads) {
+                const int g = i / HD, d = i - g * HD;
+                float M = -INFINITY;
+                for (int w = 0; w < W; w++) M = fmaxf(M, m_s[w * 8 + g]);
+                float L = 0.f, A = 0.f;
+                for (int w = 0; w < W; w++) {
+                    if (m_s[w * 8 + g] == -INFINITY) continue;
+                    const float f = expf(m_s[w * 8 + g] - M);
+                    L += l_s[w * 8 + g] * f;
+                    A += acc_s[((size_t)w * G + g) * HD + d] * f;
+                }
+                float* pp = part_base + ((size_t)g * a.n_split + split) * (HD + 2);
+                pp[d] = A;
+                if (d == 0) { pp[HD] = M; pp[HD + 1] = L; }
+            }
+        } else {
+            for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads) {
+                const int g = i / HD, d = i - g * HD;
+                float* pp = part_base + ((size_t)g * a.n_split + split) * (HD + 2);
+                pp[d] = 0.f;
+                if (d == 0) { pp[HD] = -INFINITY; pp[HD + 1] = 0.f; }
+            }
+        }
+        named_bar(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            __threadfence();
+            is_last = atomicAdd(a.counter + kvh, 1u) == (unsigned)n_split - 1;
+        }
+        named_bar(1, kConsumerThreads);
+        if (is_last) {
+            __threadfence();
+            // merge the splits; all loads of a thread are issued before the first use
+            for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads) {
+                const int g = i / HD, d = i - g * HD;
+                const float* base = part_base + (size_t)g * a.n_split * (HD + 2);
+                float ms[32];
+#pragma unroll
+                for (int s = 0; s < 32; s++) ms[s] = s < n_split ? __ldcg(base + s * (HD + 2) + HD) : -INFINITY;
+                float M = -INFINITY;
+#pragma unroll
+                for (int s = 0; s < 32; s++) M = fmaxf(M, ms[s]);
+                float L = 0.f, A = 0.f;
+#pragma unroll
+                for (int s0 = 0; s0 < 32; s0 += 8) {
+                    if (s0 >= n_split) break;
+                    float ls[8], as[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const bool live = s0 + j < n_split;
+                        ls[j] = live ? __ldcg(base + (s0 + j) * (HD + 2) + HD + 1) : 0.f;
+                        as[j] = live ? __ldcg(base + (s0 + j) * (HD + 2) + d) : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        if (ms[s0 + j] == -INFINITY) continue;
+                        const float f = expf(ms[s0 + j] - M);
+                        L += ls[j] * f;
+                        A += as[j] * f;
+                    }
+                }
+                a.out[(size_t)(kvh * G + g) * HD + d] = A / L;
+            }
+            if (threadIdx.x == 0) a.counter[kvh] = 0u;
+        }
+        named_bar(1, kConsumerThreads);
+    }
+}
+
+// ---- the kernel ----------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kDecThreads, 1)
+    k_decode(const PhaseDesc* __restrict__ prog, int n_phases, DecodeCtl* ctl, unsigned int* done, int* err) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ double red[kCW];
+    __shared__ unsigned long long keys[kCW];
+    __shared__ int flag_last;
+    __shared__ float part[2][kG][4];
+    __shared__ int set_ok[2];
+    __shared__ DecRoute route;
+    DecRing r;
+    r.base = smem;
+    uint8_t* dig_base = smem + kDecRingBytes;
+    float* attn_scratch = reinterpret_cast<float*>(dig_base + kDecDigitBytes);
+    r.full = reinterpret_cast<uint64_t*>(dig_base + kDecDigitBytes + kDecAttnBytes);
+    r.empty = r.full + kDecSlots;
+    r.off = reinterpret_cast<uint32_t*>(r.empty + kDecSlots);
+    r.charge = r.off + kDecSlots;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned int target = (ctl->epoch + 1u) * gridDim.x;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kDecSlots; s++) {
+            mbar_init(&r.full[s], 1);
+            mbar_init(&r.empty[s], kG);
+        }
+        mbar_init(&route.bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (warp == kCW) {
+        if (lane == 0) dec_producer(prog, n_phases, r, &route, err);
+        return;
+    }
+    uint32_t i = 0;  // ring position, advanced exactly as the producer advances it
+    for (int ph = 0; ph < n_phases; ph++) {
+        const PhaseDesc& p = prog[ph];
+        if (ph > 0) {
+            // grid barrier: the previous phase is complete in every CTA
+            if (threadIdx.x == 0) flag_last = wait_count(done + ph - 1, target, err) ? 0 : -1;
+            named_bar(1, kConsumerThreads);
+            if (flag_last < 0) return;
+        }
+        if (p.type == PH_EMBED) {
+            if (blockIdx.x == 0) {
+                int tok = p.ctl[0];
+                if (tok < 0 || tok >= p.n_vocab) tok = 0;
+                const int8_t* q = p.emb_qs + (int64_t)tok * p.emb_K;
+                const __half* d = p.emb_d + (int64_t)tok * (p.emb_K >> 5);
+                for (int e = threadIdx.x; e < p.emb_K; e += kConsumerThreads)
+                    p.y[e] = (float)q[e] * __half2float(d[e >> 5]);
+                if (p.best && threadIdx.x == 0) *p.best = 0ull;
+            }
+        } else if (p.type == PH_ATTN) {
+            if (p.attn.hd == 64) dec_attention<64>(p.attn, attn_scratch);
+            else dec_attention<128>(p.attn, attn_scratch);
+        } else if (p.type == PH_FINISH) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) {
+                const int t = argmax_key_index(__ldcg(p.best));
+                const int pos = p.ctl[1] + 1;
+                p.ctl[0] = t;
+                p.ctl[1] = pos;
+                p.trace[pos] = t;
+            }
+        } else if (p.type == PH_GEMV) {
+            const int K = p.K, nch = K >> 4;
+            uint4* dig = reinterpret_cast<uint4*>(dig_base);
+            float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
+            dec_stage_digits(p.x, p.norm_w, p.eps, K, dig, xsc, red);
+            named_bar(1, kConsumerThreads);
+            if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, &route, err);
+            PhaseRegs R;
+            load_phase(&p, R, expert_map(p.map) ? &route : nullptr);
+            unsigned long long best_k = 0ull;
+            const int ipw = R.G / 4;
+            if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, best_k, err);
+            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, best_k, err);
+            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, best_k, err);
+            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, best_k, err);
+            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, best_k, err);
+            else consume_a<3, 1>(p, R, r, i, dig, xsc, best_k, err);
+            if (p.epi == EK_ARGMAX) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long ok = __shfl_xor_sync(0xffffffffu, best_k, o);
+                    best_k = ok > best_k ? ok : best_k;
+                }
+                if (lane == 0) keys[warp] = best_k;
+                named_bar(1, kConsumerThreads);
+                if (threadIdx.x == 0) {
+                    unsigned long long m = 0ull;
+                    for (int ww = 0; ww < kCW; ww++) m = keys[ww] > m ? keys[ww] : m;
+                    if (m) atomicMax(p.best, m);
+                }
+            }
+        } else if (p.type == PH_DOWN4) {
+            PhaseRegs R;
+            load_phase(&p, R, &route);
+            const int K = R.K, nch = K >> 4;
+            // the four expert inputs are one vector of 4K (blocks never straddle two of them)
+            uint4* dig = reinterpret_cast<uint4*>(dig_base);
+            float* xsc_all = reinterpret_cast<float*>(dig + 3 * 4 * nch);
+            dec_stage_digits(p.x, nullptr, 0.f, 4 * K, dig, xsc_all, red);
+            named_bar(1, kConsumerThreads);
+            const int src = warp % 4;
+            const uint4* dg = dig + src * nch;
+            const float* xsc = xsc_all + src * (K >> 5);
+            consume_b(p, R, r, i, dg, xsc, &route, part, set_ok, err);
+        }
+        // phase complete for this CTA (release by one thread after the CTA barrier, as a
+        // cooperative-groups grid sync does)
+        named_bar(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(done + ph, 1u);
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        // every CTA has arrived at the last phase, so all of them have read the epoch
+        if (wait_count(done + n_phases - 1, target, err)) ctl->epoch += 1u;
+    }
+}
+
+int decode_stage_items(int S, int K, int n_items) {
+    // Stages of ~32 KB keep the bulk-copy stream at full rate with few handshakes; a consumer
+    // warp takes G/4 items of S rows each, at most 4 rows.
+    const int per_item = S * (K + K / 16);
+    int G = 4;
+    while (S * (2 * G) / 4 <= 4 && G * per_item < 32 * 1024 && (G * 2) * per_item <= kDecMaxStageBytes) G *= 2;
+    while (G > 4 && n_items % G) G /= 2;
+    return G;
+}
+
+bool decode_phase_fits(const PhaseDesc& p) {
+    if (p.type != PH_GEMV && p.type != PH_DOWN4) {
+        if (p.type == PH_ATTN) {
+            const int G = p.attn.n_head / p.attn.n_kv;
+            const size_t need = ((size_t)8 * p.attn.hd + 2 * p.attn.hd + 2 * kCW * 8 + (size_t)kCW * G * p.attn.hd) * 4;
+            return (p.attn.hd == 64 || p.attn.hd == 128) && G <= 8 && need <= (size_t)kDecAttnBytes &&
+                   p.attn.n_split <= 32;
+        }
+        return true;
+    }
+    const int K = p.K, G = p.G;
+    if (K < 64 || K % 64 != 0 || K > kMaxStageK || G < 4 || G % 4 != 0) return false;
+    if (p.type == PH_GEMV && (G > 16 || p.S * G / 4 > 4)) return false;
+    if (p.S < 1 || p.S > (p.type == PH_DOWN4 ? 4 : 3)) return false;
+    if (p.type == PH_DOWN4 && (G != kG || p.top_k != 4)) return false;
+    const size_t qs = (size_t)G * K, d = ((size_t)G * (K >> 4) + 15) & ~(size_t)15;
+    if ((size_t)p.S * (qs + d) > (size_t)kDecMaxStageBytes) return false;
+    const int KT = p.type == PH_DOWN4 ? 4 * K : K;  // staged input length
+    if (KT > kMaxStageK) return false;
+    if ((size_t)3 * (KT >> 4) * 16 + (size_t)(KT >> 5) * 4 > (size_t)kDecDigitBytes) return false;
+    if (p.map == MK_CONCAT3 && (p.n0 % G || p.n1 % G)) return false;
+    if ((p.map == MK_EXPERT_PAIR || p.map == MK_DOWN4) && p.N % G) return false;
+    if (p.map == MK_STRIDE3 && p.stride % G) return false;
+    if (p.map == MK_EXPERT_PAIR &&
+        (!p.r_qs || p.top_k != 4 || p.n_expert < 4 || p.n_expert > kMaxRoutes ||
+         (size_t)16 * K + K > (size_t)kDecMaxStageBytes))  // router stages: 16 rows each
+        return false;
+    return true;
+}
+
+void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, unsigned int* done, int* err,
+                        cudaStream_t s) {
+    const size_t smem = (size_t)kDecRingBytes + kDecDigitBytes + kDecAttnBytes + 2 * kDecSlots * 8 + 2 * kDecSlots * 4;
+    static bool init = false;
+    if (!init) {
+        QQ_CUDA_TRY(cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        init = true;
+    }
+    static int per_sm = -1;
+    if (per_sm < 0) QQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode, kDecThreads, smem));
+    QQ_CHECK(per_sm >= 1, -4, "persistent decode kernel does not fit on an SM");
+    // every CTA waits on the others, so all must be resident: a cooperative launch guarantees it
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms());
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_decode, prog, n_phases, ctl, done, err));
+}
+
+}  // namespace qq3
