@@ -7,6 +7,7 @@
 //     captured once per (sequence, with/without logits) as a CUDA graph and replayed;
 //   * greedy decode can run entirely on the device: the step's last kernel writes the
 //     argmax back as the next step's token (qq_decode_loop).
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -107,10 +108,11 @@ struct qq_model {
     struct Prog {
         qq3::PhaseDesc* d_prog = nullptr;
         int n = 0;
-        qq3::DecodeCtl* ctl = nullptr;
-        unsigned int* done = nullptr;
     };
     std::map<std::pair<int, int>, Prog> progs;
+    qq3::DecodeCtl* dctl = nullptr;  // model-wide control block of the persistent kernel
+    qq3::tword* tarena = nullptr;    // tagged activations: one buffer per phase output
+    size_t tarena_len = 0;
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
@@ -124,12 +126,11 @@ namespace {
 void free_model(qq_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     m->graphs.clear();
-    for (auto& kv : m->progs) {
+    for (auto& kv : m->progs)
         if (kv.second.d_prog) cudaFree(kv.second.d_prog);
-        if (kv.second.ctl) cudaFree(kv.second.ctl);
-        if (kv.second.done) cudaFree(kv.second.done);
-    }
     m->progs.clear();
+    if (m->dctl) cudaFree(m->dctl);
+    if (m->tarena) cudaFree(m->tarena);
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
                     m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
                     m->mask, m->ctl,
@@ -226,12 +227,45 @@ void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool d
     }
 }
 
+// Tagged-activation words the persistent program of this model needs: a bound on the sum of
+// all phase outputs (at most three vectors per layer, plus the embedding).
+size_t tarena_bound(const qq_model* m) {
+    const qq_model_desc& d = m->d;
+    size_t v = (size_t)d.n_embd;
+    v = std::max(v, (size_t)(d.n_head + 2 * d.n_head_kv) * d.head_dim);
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        if (L.moe) v = std::max(v, (size_t)d.n_expert_used * L.t[QQ_GATE_EXPS]->ne[1]);
+        else if (L.t[QQ_FFN_GATE]) v = std::max(v, (size_t)L.t[QQ_FFN_GATE]->ne[1]);
+    }
+    v = (v + 31) & ~(size_t)31;
+    return (size_t)(3 * d.n_layers + 2) * v;
+}
+
 // The decode step as a phase program for the persistent kernel (kernels_decode.cu); the same
-// sequence of operations as enqueue_step.
+// sequence of operations as enqueue_step.  Each phase writes its own tagged output buffer and
+// names the phase that wrote each vector it reads.
 std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits) {
     using namespace qq3;
     const qq_model_desc& d = m->d;
     const int E = d.n_embd, hd = d.head_dim, nq = d.n_head * hd, nkv = d.n_head_kv * hd;
+    if (!m->tarena) {
+        m->tarena_len = tarena_bound(m);
+        m->tarena = dalloc<tword>(m->tarena_len);
+        // tag 0 never matches a step's tags
+        QQ_CUDA_TRY(cudaMemsetAsync(m->tarena, 0, sizeof(tword) * m->tarena_len, m->ctx->stream));
+    }
+    if (!m->dctl) {
+        m->dctl = dalloc<DecodeCtl>(1);
+        QQ_CUDA_TRY(cudaMemsetAsync(m->dctl, 0, sizeof(DecodeCtl), m->ctx->stream));
+    }
+    size_t cursor = 0;
+    auto take = [&](size_t n) {
+        tword* t = m->tarena + cursor;
+        cursor += (n + 31) & ~(size_t)31;
+        QQ_CHECK(cursor <= m->tarena_len, QQ_ERR_INVALID, "persistent program: activation arena too small");
+        return t;
+    };
     std::vector<PhaseDesc> prog;
     auto blank = [] {
         PhaseDesc p;
@@ -239,6 +273,8 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         p.S = 1;
         return p;
     };
+    const tword* hid = nullptr;  // residual stream and the phase that wrote it
+    int hid_ph = -1;
     {
         PhaseDesc p = blank();
         p.type = PH_EMBED;
@@ -247,11 +283,12 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         p.emb_K = (int)m->tok_embd->K;
         p.n_vocab = d.n_vocab;
         p.ctl = m->ctl;
-        p.y = m->hidden;
-        p.best = want_logits ? m->best : nullptr;
+        p.y = take(E);
+        hid = p.y;
+        hid_ph = 0;
         prog.push_back(p);
     }
-    auto gemv = [&](int map, int epi, int S, int K, int n_items, const float* x, const float* norm_w) {
+    auto gemv = [&](int map, int epi, int S, int K, int n_items, const tword* x, int x_ph, const float* norm_w) {
         PhaseDesc p = blank();
         p.type = PH_GEMV;
         p.map = map;
@@ -260,10 +297,21 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         p.K = K;
         p.n_items = n_items;
         p.x = x;
+        p.x_ph = x_ph;
         p.norm_w = norm_w;
         p.eps = d.rms_eps;
-        p.G = qq3::decode_stage_items(S, K, n_items);
+        p.G = qq3::decode_stage_items(S, K, n_items, n_items);
         return p;
+    };
+    auto resid = [&](PhaseDesc& p) {  // y = hid + acc: a new version of the residual stream
+        p.res = hid;
+        p.res_ph = hid_ph;
+        p.y = take(E);
+    };
+    auto push_hid = [&](PhaseDesc& p) {
+        prog.push_back(p);
+        hid = p.y;
+        hid_ph = (int)prog.size() - 1;
     };
     auto set_src = [](PhaseDesc& p, int i, const DTensor* t) {
         p.qs[i] = t->qs;
@@ -274,24 +322,25 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         const float* an = L.t[QQ_ATTN_NORM]->f32;
         const float* fn = L.t[QQ_FFN_NORM]->f32;
         if (L.attn) {
-            PhaseDesc q = gemv(MK_CONCAT3, EK_STORE, 1, E, nq + 2 * nkv, m->hidden, an);
+            PhaseDesc q = gemv(MK_CONCAT3, EK_STORE, 1, E, nq + 2 * nkv, hid, hid_ph, an);
             set_src(q, 0, L.t[QQ_WQ]);
             set_src(q, 1, L.t[QQ_WK]);
             set_src(q, 2, L.t[QQ_WV]);
             q.n0 = nq;
             q.n1 = nkv;
-            q.G = qq3::decode_stage_items(1, E, std::gcd(nq, nkv));  // groups must not straddle q|k|v
-            q.y = m->qkv;
+            q.G = qq3::decode_stage_items(1, E, std::gcd(nq, nkv), nq + 2 * nkv);  // groups must not straddle q|k|v
+            q.y = take(nq + 2 * nkv);
             prog.push_back(q);
             PhaseDesc a = blank();
             a.type = PH_ATTN;
-            a.attn.qkv = m->qkv;
+            a.a_qkv = q.y;
+            a.a_qkv_ph = (int)prog.size() - 1;
+            a.a_out = take(nq);
             a.attn.q_norm = L.t[QQ_Q_NORM]->f32;
             a.attn.k_norm = L.t[QQ_K_NORM]->f32;
             a.attn.rope_cs = m->rope_cs;
             a.attn.k_cache = m->k_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
             a.attn.v_cache = m->v_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
-            a.attn.out = m->attn_out;
             a.attn.part = m->attn_part;
             a.attn.counter = m->attn_counter;
             a.attn.pos = m->ctl + 1;
@@ -302,29 +351,29 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             a.attn.n_split = m->n_split;
             a.attn.eps = d.rms_eps;
             prog.push_back(a);
-            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, nq, E, m->attn_out, nullptr);
+            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, nq, E, a.a_out, (int)prog.size() - 1, nullptr);
             set_src(o, 0, L.t[QQ_WO]);
-            o.y = m->hidden;
-            prog.push_back(o);
+            resid(o);
+            push_hid(o);
         } else {
-            PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, m->hidden, an);
+            PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, hid, hid_ph, an);
             set_src(c, 0, L.t[QQ_IN_PROJ]);
             c.stride = E;
             c.conv_w = L.t[QQ_CONV]->f32;
             c.state = m->conv(seq, l);
             c.E = E;
-            c.y = m->y;
+            c.y = take(E);
             prog.push_back(c);
-            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, E, E, m->y, nullptr);
+            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, E, E, c.y, (int)prog.size() - 1, nullptr);
             set_src(o, 0, L.t[QQ_OUT_PROJ]);
-            o.y = m->hidden;
-            prog.push_back(o);
+            resid(o);
+            push_hid(o);
         }
         if (L.moe) {
             const int k = d.n_expert_used;
             const int F = (int)L.t[QQ_GATE_EXPS]->ne[1];
-            PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_SWIGLU, 2, E, k * F, m->hidden, fn);
-            g.G = qq3::decode_stage_items(2, E, F);  // groups must not straddle experts
+            PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_SWIGLU, 2, E, k * F, hid, hid_ph, fn);
+            g.G = qq3::decode_stage_items(2, E, F, k * F);  // groups must not straddle experts
             set_src(g, 0, L.t[QQ_GATE_EXPS]);
             set_src(g, 1, L.t[QQ_UP_EXPS]);
             g.r_qs = L.t[QQ_ROUTER]->qs;  // the router runs inside this phase, in every CTA
@@ -337,7 +386,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             g.top_k = k;
             g.mask = m->mask;
             g.N = F;
-            g.y = m->h;
+            g.y = take((size_t)k * F);
             prog.push_back(g);
             PhaseDesc dn = blank();
             dn.type = PH_DOWN4;
@@ -346,52 +395,59 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             dn.S = 4;
             dn.K = F;
             dn.n_items = E;
-            dn.x = m->h;
+            dn.x = g.y;
+            dn.x_ph = (int)prog.size() - 1;
             set_src(dn, 0, L.t[QQ_DOWN_EXPS]);
             dn.top_k = k;
             dn.mask = m->mask;
             dn.N = E;
-            dn.y = m->hidden;
-            prog.push_back(dn);
+            resid(dn);
+            push_hid(dn);
         } else {
             const int F = (int)L.t[QQ_FFN_GATE]->ne[1];
-            PhaseDesc g = gemv(MK_PAIR, EK_SWIGLU, 2, E, F, m->hidden, fn);
+            PhaseDesc g = gemv(MK_PAIR, EK_SWIGLU, 2, E, F, hid, hid_ph, fn);
             set_src(g, 0, L.t[QQ_FFN_GATE]);
             set_src(g, 1, L.t[QQ_FFN_UP]);
-            g.y = m->h;
+            g.y = take(F);
             prog.push_back(g);
-            PhaseDesc dn = gemv(MK_ROWS, EK_RESID, 1, F, E, m->h, nullptr);
+            PhaseDesc dn = gemv(MK_ROWS, EK_RESID, 1, F, E, g.y, (int)prog.size() - 1, nullptr);
             set_src(dn, 0, L.t[QQ_FFN_DOWN]);
-            dn.y = m->hidden;
-            prog.push_back(dn);
+            resid(dn);
+            push_hid(dn);
         }
     }
     if (want_logits) {
         const DTensor* out = m->output ? m->output : m->tok_embd;
-        PhaseDesc h = gemv(MK_ROWS, EK_ARGMAX, 1, E, d.n_vocab, m->hidden, m->out_norm->f32);
-        h.G = qq3::decode_stage_items(1, E, d.n_vocab);
+        PhaseDesc h = gemv(MK_ROWS, EK_ARGMAX, 1, E, d.n_vocab, hid, hid_ph, m->out_norm->f32);
         set_src(h, 0, out);
         h.logits = m->logits;
-        h.best = m->best;
+        h.best = &m->dctl->best;
         h.suppress = m->suppress;
         prog.push_back(h);
         PhaseDesc f = blank();
         f.type = PH_FINISH;
-        f.best = m->best;
+        f.best = &m->dctl->best;
         f.ctl = m->ctl;
         f.trace = m->trace + (size_t)seq * (d.max_ctx + 1);
         prog.push_back(f);
     }
+    QQ_CHECK((int)prog.size() <= qq3::kMaxPhases, QQ_ERR_UNSUPPORTED, "persistent program: too many phases");
     return prog;
 }
 
 bool mega_enabled(qq_model* m) {
     if (m->mega < 0) {
-        // opt-in until the persistent step is faster than the per-phase kernels on every shape
+        // the persistent step is the default; QQ3_PERSISTENT=0 selects the per-phase kernels
         const char* env = getenv("QQ3_PERSISTENT");
-        bool ok = env && atoi(env) != 0 && qq3::stream_path();
+        bool ok = !(env && atoi(env) == 0) && qq3::stream_path();
         if (ok) {
-            for (const auto& p : build_program(m, 0, true))
+            std::vector<qq3::PhaseDesc> prog;
+            try {
+                prog = build_program(m, 0, true);
+            } catch (const qq3::Error&) {
+                ok = false;  // e.g. more phases than a tag can name: use the per-phase kernels
+            }
+            for (const auto& p : prog)
                 if (!qq3::decode_phase_fits(p)) { ok = false; break; }
         }
         m->mega = ok ? 1 : 0;
@@ -407,12 +463,8 @@ qq_model::Prog& get_prog(qq_model* m, int seq, bool want_logits) {
     qq_model::Prog pr;
     pr.n = (int)host.size();
     pr.d_prog = dalloc<qq3::PhaseDesc>(host.size());
-    pr.ctl = dalloc<qq3::DecodeCtl>(1);
-    pr.done = dalloc<unsigned int>(host.size());
     cudaStream_t s = m->ctx->stream;
     QQ_CUDA_TRY(cudaMemcpyAsync(pr.d_prog, host.data(), sizeof(qq3::PhaseDesc) * host.size(), cudaMemcpyHostToDevice, s));
-    QQ_CUDA_TRY(cudaMemsetAsync(pr.ctl, 0, sizeof(qq3::DecodeCtl), s));
-    QQ_CUDA_TRY(cudaMemsetAsync(pr.done, 0, sizeof(unsigned int) * host.size(), s));
     QQ_CUDA_TRY(cudaStreamSynchronize(s));  // host vector goes out of scope
     return m->progs[key] = pr;
 }
@@ -426,7 +478,7 @@ cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
     qq_model::Prog* pr = mega ? &get_prog(m, seq, want_logits) : nullptr;
     QQ_CUDA_TRY(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeRelaxed));
     try {
-        if (mega) qq3::launch_decode_step(pr->d_prog, pr->n, pr->ctl, pr->done, qq3::kernel_err_ptr(), m->cap);
+        if (mega) qq3::launch_decode_step(pr->d_prog, pr->n, m->dctl, qq3::kernel_err_ptr(), m->cap);
         else enqueue_step(m, seq, want_logits, m->cap, false);
     } catch (...) {
         cudaStreamEndCapture(m->cap, &g);

@@ -1,9 +1,19 @@
 // decode_prog.h -- the decode step as a device-side program of phases, run by one persistent
 // kernel (kernels_decode.cu).  Built once per (model, sequence) by the runtime (api.cu).
+//
+// Activations between phases are tagged words: (tag << 32 | float bits), written once per step
+// with one 64-bit store, tag = step epoch * 256 + writing phase + 1.  A reader spins until the
+// words it needs carry the tag of their producer phase, so data arrival is the only
+// synchronisation between CTAs; every phase writes its own output buffer, so no word is
+// written twice in one step.
 #pragma once
 #include "kernels.h"
 
 namespace qq3 {
+
+typedef unsigned long long tword;  // tagged activation word
+
+constexpr int kMaxPhases = 255;  // phase index fits the low byte of a tag
 
 enum PhaseType : int {
     PH_EMBED = 0,   // hidden = dequantised embedding row of the token; argmax key reset
@@ -24,7 +34,10 @@ struct PhaseDesc {
     int pad0;
     int G;        // items per stage (multiple of 4; stages are sized to ~16 KB for the bulk-copy stream)
     // input
-    const float* x;       // mode A input, or the 4 expert inputs h[0..3] (stride K) for PH_DOWN4
+    const tword* x;       // mode A input, or the 4 expert inputs h[0..3] (stride K) for PH_DOWN4
+    int x_ph;             // phase that writes x
+    int res_ph;           // phase that writes res
+    const tword* res;     // residual stream read by EK_RESID and PH_DOWN4 (own items)
     const float* norm_w;  // fused RMSNorm weight (nullable)
     float eps;
     int n0, n1;           // MK_CONCAT3 boundaries
@@ -37,7 +50,7 @@ struct PhaseDesc {
     float* rec;
     const uint32_t* mask;
     // epilogue
-    float* y;
+    tword* y;             // output (tagged with this phase)
     const float* conv_w;
     float* state;
     int E;
@@ -50,7 +63,11 @@ struct PhaseDesc {
     const __half* r_d;
     const float* bias;
     // attention / embed / finish
-    AttnArgs attn;
+    AttnArgs attn;        // qkv and out are unused: the tagged forms below replace them
+    const tword* a_qkv;
+    int a_qkv_ph;
+    int pad2;
+    tword* a_out;
     const int8_t* emb_qs;
     const __half* emb_d;
     int emb_K, n_vocab;
@@ -58,10 +75,12 @@ struct PhaseDesc {
     int* trace;  // per-sequence greedy ids by position
 };
 
-// Per-launch control block of the persistent kernel.
+// Control block of the persistent kernel, one per model (shared by all its programs).
 struct DecodeCtl {
-    unsigned int epoch;      // completed steps; counters below are cumulative (epoch * grid per phase)
-    unsigned int pad[31];
+    unsigned int epoch;       // steps run; tags of the current step derive from it
+    unsigned int end_ticket;  // CTAs done with the current step (the last one closes the step)
+    unsigned long long best;  // argmax key of the logits (reset by the CTA that closes the step)
+    unsigned int pad[28];
 };
 
 // Shared-memory plan of the persistent kernel: a byte ring of kDecRingBytes holding up to
@@ -69,15 +88,14 @@ struct DecodeCtl {
 // the input digits of the current phase, and attention scratch.
 constexpr int kDecSlots = 16;
 constexpr int kDecRingBytes = 176 * 1024;
-constexpr int kDecMaxStageBytes = 40 * 1024;
+constexpr int kDecMaxStageBytes = 72 * 1024;
 constexpr int kDecDigitBytes = 24 * 1024;
-constexpr int kDecAttnBytes = 16 * 1024;
+constexpr int kDecAttnBytes = 20 * 1024;
 
-// Launch one decode step (grid = one CTA per SM).  done: [n_phases] cumulative counters.
-void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, unsigned int* done, int* err,
-                        cudaStream_t s);
-// Items per stage for a streamed phase (multiple of 4, dividing n_items when possible).
-int decode_stage_items(int S, int K, int n_items);
+// Launch one decode step (grid = one CTA per SM).
+void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, int* err, cudaStream_t s);
+// Items per stage for a streamed phase (a power of two >= 4 dividing n_div when possible).
+int decode_stage_items(int S, int K, int n_div, int n_total);
 // Whether a phase fits the persistent kernel's shared-memory plan.
 bool decode_phase_fits(const PhaseDesc& p);
 

@@ -11,8 +11,9 @@
 //    the groups this CTA owns into a ring of shared-memory slots with 1-D bulk copies.  Weights
 //    never depend on activations, so it runs ahead across phase boundaries; it only stops on
 //    a full ring, or before an expert gate/up phase until its own CTA has routed the token;
-//  * the consumer warps run the phases in order; between phases they wait on a grid-wide
-//    completion counter (cumulative across steps, so nothing is ever reset);
+//  * the consumer warps run the phases in order.  There is no grid-wide barrier: activations
+//    are tagged words (decode_prog.h) and a CTA waits only for the words it reads to carry the
+//    tag of their producer phase; a CTA with no work in a phase skips it;
 //  * the MoE router is not a phase of its own: every CTA computes the 32 router logits and
 //    the top-k itself at the start of the expert gate/up phase (identical arithmetic in every
 //    CTA, so every CTA routes identically), which saves a grid-wide barrier per MoE layer;
@@ -28,24 +29,54 @@ namespace qq3 {
 constexpr int kDecThreads = kThreads2;  // 8 consumer warps + 1 producer warp
 constexpr int kMaxRoutes = 32;          // experts the fused router handles
 constexpr int kMaxStageK = 8192;        // largest K of a streamed phase (4 staging passes)
-constexpr uint32_t kDecPrefetchBytes = 160 * 1024;  // L2 prefetch per CTA while a token is routed
-
-__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
+constexpr int kMaxRowsPerWarp = 8;      // rows a consumer warp dots per stage
+constexpr int kStageTarget = 64 * 1024; // stage size the item count per stage aims for
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
-// wait until *c >= target (bounded; false on timeout or abort)
-__device__ __forceinline__ bool wait_count(const unsigned int* c, unsigned int target, int* err) {
-    for (uint32_t it = 0; it < kSpinLimit; ++it) {  // each poll is an L2 round trip: ~2 s in all
-        if ((int)(ld_acquire(c) - target) >= 0) return true;
-        if ((it & 255u) == 255u && ld_volatile(err)) return false;
+__device__ __forceinline__ uint32_t step_tag(uint32_t epoch, int ph) { return epoch * 256u + (uint32_t)ph + 1u; }
+
+__device__ __forceinline__ void st_tw(tword* p, float v, uint32_t tag) {
+    const tword w = ((tword)tag << 32) | (tword)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ tword ld_tw(const tword* p) {
+    tword w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+__device__ __forceinline__ bool tw_is(tword w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+__device__ __forceinline__ float tw_val(tword w) { return __uint_as_float((uint32_t)w); }
+
+// the value of *p once it carries `tag` (bounded; 0 on timeout or abort)
+__device__ __forceinline__ float wait_tw(const tword* p, uint32_t tag, int* err) {
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        const tword w = ld_tw(p);
+        if (tw_is(w, tag)) return tw_val(w);
+        if ((it & 255u) == 255u && ld_volatile(err)) return 0.f;
     }
-    set_err(err, 3);
-    return false;
+    set_err(err, 4);
+    return 0.f;
+}
+
+// eight consecutive words once all carry `tag` (bounded)
+__device__ __forceinline__ void wait_tw8(const tword* p, uint32_t tag, int* err, float (&v)[8]) {
+    tword w[8];
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            w[j] = ld_tw(p + j);
+            ok = ok && tw_is(w[j], tag);
+        }
+        if (ok) break;
+        if ((it & 255u) == 255u && ld_volatile(err)) break;
+        if (it + 1 == kSpinLimit) set_err(err, 4);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = tw_val(w[j]);
 }
 
 __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -164,30 +195,6 @@ __device__ __forceinline__ uint32_t stage_bytes(int S, int G, int K) {
 
 // ---- producer ------------------------------------------------------------------------------
 
-// L2 prefetch of the rows this CTA will stream for phase pp; returns the bytes requested.
-__device__ uint32_t prefetch_phase(const PhaseDesc* pp, const DecRoute* route) {
-    PhaseRegs R;
-    load_phase(pp, R, route);
-    const int K = R.K, G = R.G;
-    const int n_groups = (R.n_items + G - 1) / G;
-    uint32_t bytes = 0;
-    for (int g = blockIdx.x; g < n_groups; g += gridDim.x) {
-        const int rows = min(G, R.n_items - g * G);
-        const int8_t* q[4];
-        const __half* d[4];
-        bool on[4] = {false, false, false, false};
-        group_ptrs(R, g * G, q, d, on);
-        const uint32_t qb = (uint32_t)rows * K, db = round16((uint32_t)rows * (K >> 4));
-        for (int s = 0; s < R.S; s++) {
-            if (!on[s]) continue;
-            bulk_prefetch_l2(q[s], qb);
-            bulk_prefetch_l2(d[s], db);
-            bytes += qb + db;
-        }
-    }
-    return bytes;
-}
-
 // Splits of the context used this step: at most one (kv head, split) item per CTA.
 __device__ __forceinline__ int dec_attn_splits(const AttnArgs& a) {
     int n = (int)gridDim.x / a.n_kv;
@@ -201,27 +208,6 @@ __device__ __forceinline__ void dec_attn_range(int len, int n_split, int split, 
     if (chunk < 32) chunk = 32;
     p0 = split * chunk;
     p1 = min(len, p0 + chunk);
-}
-
-// L2 prefetch of what this CTA's attention item reads: the cached K/V rows before `pos`, the
-// head norms and the RoPE row.
-__device__ void prefetch_attention(const AttnArgs& a) {
-    const int pos = *a.pos;
-    const int n_split = dec_attn_splits(a);
-    const int item = blockIdx.x;
-    if (item >= a.n_kv * n_split || pos < 0 || pos >= a.max_ctx) return;
-    const int kvh = item / n_split, split = item - kvh * n_split;
-    int p0, p1;
-    dec_attn_range(pos + 1, n_split, split, p0, p1);
-    p1 = min(p1, pos);  // the row at pos is written this step
-    if (p0 < p1) {
-        const uint32_t bytes = (uint32_t)(p1 - p0) * a.hd * 4u;
-        bulk_prefetch_l2(a.k_cache + ((size_t)kvh * a.max_ctx + p0) * a.hd, bytes);
-        bulk_prefetch_l2(a.v_cache + ((size_t)kvh * a.max_ctx + p0) * a.hd, bytes);
-    }
-    bulk_prefetch_l2(a.rope_cs + (size_t)pos * a.hd, 4u * a.hd);
-    bulk_prefetch_l2(a.q_norm, 4u * a.hd);
-    bulk_prefetch_l2(a.k_norm, 4u * a.hd);
 }
 
 // Ring bookkeeping of the producer thread: stages are issued in consumption order into a byte
@@ -258,7 +244,6 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
     uint32_t routed = 0;  // MoE layers whose routing this CTA has seen
     for (int ph = 0; ph < n_phases; ph++) {
         const PhaseDesc* pp = prog + ph;
-        if (pp->type == PH_ATTN) prefetch_attention(pp->attn);
         if (!streamed(pp->type)) continue;
         const bool ex = expert_map(pp->map);
         if (pp->map == MK_EXPERT_PAIR) {
@@ -276,16 +261,8 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                     bulk_g2s(sb + qs_stride(16, K), pp->r_d + (int64_t)16 * h * (K >> 5), db, &r.full[slot]);
                 }
             }
-            // While the consumers route the token, pull the next layer's operator rows into L2
-            // (they depend on nothing); then wait for this CTA's routing.
-            uint32_t budget = kDecPrefetchBytes;
-            for (int ph2 = ph + 1; ph2 < n_phases && budget > 0; ph2++) {
-                const PhaseDesc* p2 = prog + ph2;
-                if (p2->map == MK_EXPERT_PAIR) break;
-                if (!streamed(p2->type) || expert_map(p2->map)) continue;
-                const uint32_t b = prefetch_phase(p2, nullptr);
-                budget = b >= budget ? 0u : budget - b;
-            }
+            // Wait for this CTA's routing.  (Pulling the next layer's rows into L2 meanwhile was
+            // measured slower: it competes with the expert rows for DRAM right after routing.)
             if (!slot_wait(&route->bar, routed & 1u, err)) goto drain;
             ++routed;
         }
@@ -315,11 +292,6 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                     bulk_g2s(sb + s * qsz, q[s], qb, &r.full[slot]);
                     bulk_g2s(sb + S * qsz + s * dsz, d[s], db, &r.full[slot]);
                 }
-                if (pp->epi == EK_CONV) {  // the epilogue's conv state and taps of these items
-                    bulk_prefetch_l2(pp->state + item0, 4u * rows);
-                    bulk_prefetch_l2(pp->state + pp->E + item0, 4u * rows);
-                    bulk_prefetch_l2(pp->conv_w + 3 * item0, 12u * rows);
-                }
             }
         }
     }
@@ -334,8 +306,8 @@ drain:
 // Digitise an input of runtime length K <= kMaxStageK (8 elements per consumer thread per
 // pass, at most 4 passes held in registers), with an optional RMSNorm (tensor.js:103-114;
 // sum of squares in double as the JS does).
-__device__ void dec_stage_digits(const float* __restrict__ x, const float* __restrict__ norm_w, float eps, int K,
-                                 uint4* dig, float* xsc, double* red) {
+__device__ void dec_stage_digits(const tword* __restrict__ x, uint32_t tag, const float* __restrict__ norm_w,
+                                 float eps, int K, uint4* dig, float* xsc, double* red, int* err) {
     const int t = threadIdx.x;
     float xv[4][8];
     double ss = 0.0;
@@ -343,10 +315,7 @@ __device__ void dec_stage_digits(const float* __restrict__ x, const float* __res
     for (int ps = 0; ps < 4; ps++) {
         const int e0 = 8 * t + ps * 8 * kConsumerThreads;
         if (e0 < K) {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(x + e0));
-            const float4 b = __ldcg(reinterpret_cast<const float4*>(x + e0) + 1);
-            xv[ps][0] = a.x; xv[ps][1] = a.y; xv[ps][2] = a.z; xv[ps][3] = a.w;
-            xv[ps][4] = b.x; xv[ps][5] = b.y; xv[ps][6] = b.z; xv[ps][7] = b.w;
+            wait_tw8(x + e0, tag, err, xv[ps]);
         } else {
 #pragma unroll
             for (int e = 0; e < 8; e++) xv[ps][e] = 0.f;
@@ -414,18 +383,19 @@ __device__ __forceinline__ float block_dot(const uint4 w0, const uint4 w1, const
     return fmaf(i2f_small(a3), 1.0f / 64516.0f, fmaf(i2f_small(a2), 1.0f / 254.0f, i2f_small(a1)));
 }
 
-// Lane partials of up to NR rows against the staged input.  Lane l takes the 32-weight blocks
-// l, l+32, ... of every row (one float combination per block); the digits of a block are read
-// once for all rows of the batch.  Each row adds its blocks in that order wherever it lives
-// (ring slot in shared memory, or global memory for the router rows).
-template <int NR, bool GLOBAL>
-__device__ __forceinline__ void rows_dot(const int8_t* const (&q)[NR], const __half* const (&d)[NR], int n_rows,
+// Lane partials of NR rows (in a ring slot) against the staged input.  Lane l takes the
+// 32-weight blocks l, l+32, ... of every row (one float combination per block); the digits of a
+// block are read once for all rows.  Every row is computed (rows past the valid ones point at
+// valid shared memory and their sums are discarded), so the compiler can interleave the NR x 3
+// dp4a chains.
+template <int NR>
+__device__ __forceinline__ void rows_dot(const int8_t* const (&q)[NR], const __half* const (&d)[NR],
                                          const uint4* dig, const float* xsc, int nch, int pstride, float (&acc)[NR]) {
     const int lane = threadIdx.x & 31;
     const int nb = nch >> 1;
 #pragma unroll
     for (int r = 0; r < NR; r++) acc[r] = 0.f;
-#pragma unroll 2
+#pragma unroll (NR > 4 ? 1 : 2)
     for (int b = lane; b < nb; b += 32) {
         uint4 g[3][2];
 #pragma unroll
@@ -436,24 +406,43 @@ __device__ __forceinline__ void rows_dot(const int8_t* const (&q)[NR], const __h
         const float sx = xsc[b];
 #pragma unroll
         for (int r = 0; r < NR; r++) {
-            if (r < n_rows) {
-                const uint4* wp = reinterpret_cast<const uint4*>(q[r] + 32 * b);
-                const uint4 w0 = GLOBAL ? __ldg(wp) : wp[0];
-                const uint4 w1 = GLOBAL ? __ldg(wp + 1) : wp[1];
-                const float dw = __half2float(GLOBAL ? __ldg(d[r] + b) : d[r][b]);
-                acc[r] = fmaf(block_dot(w0, w1, g), dw * sx, acc[r]);
-            }
+            const uint4* wp = reinterpret_cast<const uint4*>(q[r] + 32 * b);
+            const uint4 w0 = wp[0], w1 = wp[1];
+            const float dw = __half2float(d[r][b]);
+            acc[r] = fmaf(block_dot(w0, w1, g), dw * sx, acc[r]);
         }
     }
 }
 
-// Warp sums of NR (1, 2 or 4) lane values by halving: a level exchanges half of the values a
-// lane still holds.  Returns the sum of row (lane >> 3) for NR = 4, (lane >> 4) for NR = 2,
-// row 0 for NR = 1, in every lane of that row's group.
+// Warp sums of NR (1, 2, 4 or 8) lane values by halving: a level exchanges half of the values a
+// lane still holds.  Returns the sum of row (lane >> 2) for NR = 8, (lane >> 3) for NR = 4,
+// (lane >> 4) for NR = 2, row 0 for NR = 1, in every lane of that row's group.
 template <int NR>
 __device__ __forceinline__ float warp_reduce_rows(const float (&v)[NR]) {
     const int lane = threadIdx.x & 31;
     float k;
+    if (NR == 8) {
+        const bool h16 = lane & 16;
+        float k4[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            k4[j] = h16 ? v[(4 + j) % NR] : v[j];
+            k4[j] += __shfl_xor_sync(0xffffffffu, h16 ? v[j] : v[(4 + j) % NR], 16);
+        }
+        const bool h8 = lane & 8;
+        float k2[2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            k2[j] = h8 ? k4[2 + j] : k4[j];
+            k2[j] += __shfl_xor_sync(0xffffffffu, h8 ? k4[j] : k4[2 + j], 8);
+        }
+        const bool h4 = lane & 4;
+        k = h4 ? k2[1] : k2[0];
+        k += __shfl_xor_sync(0xffffffffu, h4 ? k2[0] : k2[1], 4);
+        k += __shfl_xor_sync(0xffffffffu, k, 2);
+        k += __shfl_xor_sync(0xffffffffu, k, 1);
+        return k;
+    }
     if (NR == 4) {
         const bool hi = lane & 16;
         float k0 = hi ? v[2 % NR] : v[0];
@@ -518,7 +507,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
             d[j] = reinterpret_cast<const __half*>(sb + qs_stride(16, K)) + (4 * w + j) * (K >> 5);
         }
         float acc[4];
-        rows_dot<4, false>(q, d, n_rows, dig, xsc, nch, nch, acc);
+        rows_dot<4>(q, d, dig, xsc, nch, nch, acc);
         const float sum = warp_reduce_rows<4>(acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(&r.empty[slot]);
@@ -580,10 +569,11 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
 // NR = S IPW <= 4 rows (item-major, source-minor), so its row dots and reductions overlap.
 template <int S, int IPW>
 __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R, const DecRing& r, uint32_t& i,
-                                          const uint4* dig, const float* xsc, unsigned long long& best_k, int* err) {
+                                          const uint4* dig, const float* xsc, uint32_t tag_out, uint32_t tag_res,
+                                          unsigned long long& best_k, int* err) {
     constexpr int NR = S * IPW;
-    constexpr int NRP = NR == 3 ? 4 : NR;  // rows padded for the halving reduction
-    constexpr int SH = NRP == 4 ? 3 : (NRP == 2 ? 4 : 5);  // lane >> SH = row of the reduced sum
+    constexpr int NRP = NR == 3 ? 4 : (NR > 4 ? 8 : NR);  // rows padded for the halving reduction
+    constexpr int SH = NRP == 8 ? 2 : (NRP == 4 ? 3 : (NRP == 2 ? 4 : 5));  // lane >> SH = row of the sum
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int set = warp / 4, w = warp % 4;
     const int K = R.K, nch = K >> 4;
@@ -592,7 +582,7 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
     const int n_groups = (R.n_items + G - 1) / G;
     const int epi = p.epi;
     const int skip = (epi == EK_ARGMAX && p.suppress) ? *p.suppress : -1;
-    float* const y = p.y;
+    tword* const y = p.y;
     // the lane that finishes item j of the warp (after the reduction it holds the item's first
     // source; the other sources come from the lanes of the next row groups)
     const int row = lane >> SH;
@@ -608,13 +598,13 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
         const bool gon = R.map != MK_EXPERT_PAIR || R.on[(g * G) / R.N];
         const int li0 = w * IPW;
         const int n_left = R.n_items - g * G - li0;  // items of this warp that exist
-        const int n_ok = !gon ? 0 : (n_left >= IPW ? IPW : (n_left > 0 ? n_left : 0));
+        const int n_have = n_left >= IPW ? IPW : (n_left > 0 ? n_left : 0);
         const int item = g * G + li0 + my_j;
-        const bool mine = lead && my_j < n_ok;
+        const bool mine = lead && my_j < n_have;
         float pre[5] = {0.f, 0.f, 0.f, 0.f, 0.f};  // epilogue operands, fetched before the dots
         if (mine) {
             if (epi == EK_RESID) {
-                pre[0] = __ldcg(y + item);
+                pre[0] = wait_tw(p.res + item, tag_res, err);
             } else if (epi == EK_CONV) {
                 pre[0] = p.state[item];
                 pre[1] = p.state[p.E + item];
@@ -633,7 +623,7 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
             d[j] = reinterpret_cast<const __half*>(sb + S * qsz + s * dsz) + li * (K >> 5);
         }
         float acc[NRP];
-        rows_dot<NRP, false>(q, d, n_ok * S, dig, xsc, nch, nch, acc);
+        rows_dot<NRP>(q, d, dig, xsc, nch, nch, acc);
         const float a0 = warp_reduce_rows<NRP>(acc);
         const float a1 = S > 1 ? __shfl_down_sync(0xffffffffu, a0, 1 << SH) : 0.f;
         const float a2 = S > 2 ? __shfl_down_sync(0xffffffffu, a0, 2 << SH) : 0.f;
@@ -641,15 +631,16 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
         if (lane == 0) mbar_arrive(&r.empty[slot]);
         if (mine) {
             switch (epi) {
-                case EK_STORE: y[item] = a0; break;
-                case EK_RESID: y[item] = pre[0] + a0; break;
-                case EK_SWIGLU: y[item] = silu_mul(a0, a1); break;
+                case EK_STORE: st_tw(y + item, a0, tag_out); break;
+                case EK_RESID: st_tw(y + item, pre[0] + a0, tag_out); break;
+                // a masked expert's outputs are written as zeros (its down rows are skipped)
+                case EK_SWIGLU: st_tw(y + item, gon ? silu_mul(a0, a1) : 0.f, tag_out); break;
                 case EK_CONV: {  // lfm2-engine.js:294-321
                     const float bx = a0 * a2;
                     const float co = pre[2] * pre[0] + pre[3] * pre[1] + pre[4] * bx;
                     p.state[item] = pre[1];
                     p.state[p.E + item] = bx;
-                    y[item] = a1 * co;
+                    st_tw(y + item, a1 * co, tag_out);
                     break;
                 }
                 case EK_ARGMAX: {
@@ -670,11 +661,12 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
 // source, the set combines them in expert-slot order (lfm2-engine.js:459-486).
 __device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R, const DecRing& r, uint32_t& i,
                                           const uint4* dg, const float* xsc, const DecRoute* route,
-                                          float (*part)[kG][4], int* set_ok, int* err) {
+                                          float (*part)[kG][4], int* set_ok, uint32_t tag_out, uint32_t tag_res,
+                                          int* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int src = warp % 4, set = warp / 4;
     const int K = R.K, nch = K >> 4;
-    float* const y = p.y;
+    tword* const y = p.y;
     float wk[4];
 #pragma unroll
     for (int s = 0; s < 4; s++) wk[s] = route->w[s];
@@ -685,7 +677,7 @@ __device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R
         const int slot = i % kDecSlots;
         const int rows = min(kG, R.n_items - g * kG);
         const bool mine = src == 0 && lane < rows;
-        const float yold = mine ? __ldcg(y + g * kG + lane) : 0.f;
+        const float yold = mine ? wait_tw(p.res + g * kG + lane, tag_res, err) : 0.f;
         // one warp of the set waits; the set follows it through a named barrier, so a
         // timeout makes the same decision in all four warps
         if (src == 0 && lane == 0) set_ok[set] = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err) ? 1 : 0;
@@ -700,7 +692,7 @@ __device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R
             d[j] = reinterpret_cast<const __half*>(sb + 4 * qsz + src * dsz) + j * (K >> 5);
         }
         float acc[kG];
-        rows_dot<kG, false>(q, d, R.on[src] ? rows : 0, dg, xsc, nch, 4 * nch, acc);
+        rows_dot<kG>(q, d, dg, xsc, nch, 4 * nch, acc);
         const float sum = warp_reduce_rows<kG>(acc);
         if ((lane & 7) == 0) part[set][lane >> 3][src] = sum;
         __syncwarp();
@@ -711,7 +703,7 @@ __device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R
 #pragma unroll
             for (int s = 0; s < 4; s++)
                 if (R.on[s]) moe += wk[s] * part[set][lane][s];
-            y[g * kG + lane] = yold + moe;
+            st_tw(y + g * kG + lane, yold + moe, tag_out);
         }
         named_bar(2 + set, 128);
     }
@@ -740,16 +732,22 @@ __device__ void dec_norm_rope(float* v, const float* __restrict__ w, float eps, 
     __syncwarp();
 }
 
+// One (kv head, split) item: the G query heads of kv head `kvh` over positions [p0, p1).
+// Tiles of 32 positions are staged in shared memory by all consumer threads (K rows padded so
+// that lane-per-position reads do not conflict); warp g < G then scores query head g with one
+// position per lane, updates its online softmax and accumulates V (lane owns HD/32 dims).
+// Shared layout (floats): q [8][HD] | kv [2][HD] | K tile [32][HD+4] | V tile [32][HD].
 template <int HD>
-__device__ void dec_attention(const AttnArgs& a, float* scratch) {
+__device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_in, tword* out, uint32_t tag_out,
+                              float* scratch, int* err) {
     constexpr int PL = HD / 32;
-    constexpr int W = kCW;
+    constexpr int T = 32;
+    constexpr int KS = HD + 4;  // padded K row stride
     const int G = a.n_head / a.n_kv;
-    float* q_s = scratch;                      // [G][HD]
-    float* kv_s = q_s + 8 * HD;                // [2][HD]
-    float* m_s = kv_s + 2 * HD;                // [W][8]
-    float* l_s = m_s + W * 8;                  // [W][8]
-    float* acc_s = l_s + W * 8;                // [W][G][HD] (G <= 4 for HD=128, <= 8 for HD=64)
+    float* q_s = scratch;          // [8][HD]
+    float* kv_s = q_s + 8 * HD;    // [2][HD]
+    float* k_t = kv_s + 2 * HD;    // [T][KS]
+    float* v_t = k_t + T * KS;     // [T][HD]
     __shared__ int is_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *a.pos;
@@ -767,16 +765,16 @@ __device__ void dec_attention(const AttnArgs& a, float* scratch) {
         float* part_base = a.part + (size_t)kvh * G * a.n_split * (HD + 2);
         if (p0 < p1) {
             for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads)
-                q_s[i] = __ldcg(a.qkv + (size_t)kvh * G * HD + i);
+                q_s[i] = wait_tw(qkv + (size_t)kvh * G * HD + i, tag_in, err);
             const bool owns = p0 <= pos && pos < p1;
             if (owns)
                 for (int d = threadIdx.x; d < HD; d += kConsumerThreads) {
-                    kv_s[d] = __ldcg(a.qkv + (size_t)a.n_head * HD + (size_t)kvh * HD + d);
-                    kv_s[HD + d] = __ldcg(a.qkv + (size_t)(a.n_head + a.n_kv) * HD + (size_t)kvh * HD + d);
+                    kv_s[d] = wait_tw(qkv + (size_t)a.n_head * HD + (size_t)kvh * HD + d, tag_in, err);
+                    kv_s[HD + d] = wait_tw(qkv + (size_t)(a.n_head + a.n_kv) * HD + (size_t)kvh * HD + d, tag_in, err);
                 }
             named_bar(1, kConsumerThreads);
-            for (int g = warp; g < G; g += W) dec_norm_rope<HD>(q_s + g * HD, a.q_norm, a.eps, cs);
-            if (owns && warp == W - 1) {
+            for (int g = warp; g < G; g += kCW) dec_norm_rope<HD>(q_s + g * HD, a.q_norm, a.eps, cs);
+            if (owns && warp == kCW - 1) {
                 dec_norm_rope<HD>(kv_s, a.k_norm, a.eps, cs);
                 for (int d = lane; d < HD; d += 32) {
                     kc[(size_t)pos * HD + d] = kv_s[d];
@@ -784,79 +782,64 @@ __device__ void dec_attention(const AttnArgs& a, float* scratch) {
                 }
             }
             named_bar(1, kConsumerThreads);
-            float m[8], l[8], acc[8][PL], qv[8][PL];
+            float m = -INFINITY, l = 0.f, acc[PL];
 #pragma unroll
-            for (int g = 0; g < 8; g++) {
-                m[g] = -INFINITY;
-                l[g] = 0.f;
-#pragma unroll
-                for (int j = 0; j < PL; j++) {
-                    acc[g][j] = 0.f;
-                    qv[g][j] = g < G ? q_s[g * HD + lane * PL + j] : 0.f;
+            for (int j = 0; j < PL; j++) acc[j] = 0.f;
+            for (int t0 = p0; t0 < p1; t0 += T) {
+                const int n = min(T, p1 - t0);
+                // rows before `pos` were written by earlier steps; the row at `pos` is in kv_s
+                for (int idx = threadIdx.x; idx < n * (HD / 4); idx += kConsumerThreads) {
+                    const int row = idx / (HD / 4), c = (idx % (HD / 4)) * 4;
+                    const int p = t0 + row;
+                    float4 k4, v4;
+                    if (owns && p == pos) {
+                        k4 = *reinterpret_cast<const float4*>(kv_s + c);
+                        v4 = *reinterpret_cast<const float4*>(kv_s + HD + c);
+                    } else {
+                        k4 = __ldg(reinterpret_cast<const float4*>(kc + (size_t)p * HD + c));
+                        v4 = __ldg(reinterpret_cast<const float4*>(vc + (size_t)p * HD + c));
+                    }
+                    *reinterpret_cast<float4*>(k_t + row * KS + c) = k4;
+                    *reinterpret_cast<float4*>(v_t + row * HD + c) = v4;
                 }
-            }
-            constexpr int U = 4;  // positions per warp whose K/V loads are in flight together
-            for (int pb = p0 + warp; pb < p1; pb += U * W) {
-                float kr[U][PL], vr[U][PL];
+                named_bar(1, kConsumerThreads);
+                if (warp < G) {
+                    const float* qg = q_s + warp * HD;
+                    float s = -INFINITY;
+                    if (lane < n) {
+                        const float* kr = k_t + lane * KS;
+                        float dot = 0.f;
 #pragma unroll
-                for (int u = 0; u < U; u++) {
-                    const int p = pb + u * W;
-                    // the row at `pos` was written above by this CTA: read it from shared memory
-                    const bool own_row = owns && p == pos;
-#pragma unroll
-                    for (int j = 0; j < PL; j++) {
-                        kr[u][j] = 0.f;
-                        vr[u][j] = 0.f;
-                        if (p < p1) {
-                            kr[u][j] = own_row ? kv_s[lane * PL + j] : __ldcg(kc + (size_t)p * HD + lane * PL + j);
-                            vr[u][j] = own_row ? kv_s[HD + lane * PL + j] : __ldcg(vc + (size_t)p * HD + lane * PL + j);
+                        for (int c = 0; c < HD; c += 4) {
+                            const float4 q4 = *reinterpret_cast<const float4*>(qg + c);
+                            const float4 k4 = *reinterpret_cast<const float4*>(kr + c);
+                            dot = fmaf(q4.x, k4.x, dot);
+                            dot = fmaf(q4.y, k4.y, dot);
+                            dot = fmaf(q4.z, k4.z, dot);
+                            dot = fmaf(q4.w, k4.w, dot);
                         }
+                        s = dot * scale;
                     }
+                    const float m_new = fmaxf(m, warp_max(s));
+                    const float pl = lane < n ? expf(s - m_new) : 0.f;
+                    const float cf = expf(m - m_new);
+                    l = l * cf + warp_sum(pl);
+#pragma unroll
+                    for (int j = 0; j < PL; j++) acc[j] *= cf;
+                    for (int jj = 0; jj < n; jj++) {
+                        const float pj = __shfl_sync(0xffffffffu, pl, jj);
+#pragma unroll
+                        for (int j = 0; j < PL; j++) acc[j] = fmaf(pj, v_t[jj * HD + lane * PL + j], acc[j]);
+                    }
+                    m = m_new;
                 }
-#pragma unroll
-                for (int u = 0; u < U; u++) {
-                    if (pb + u * W >= p1) break;
-                    float dot[8];
-#pragma unroll
-                    for (int g = 0; g < 8; g++) {
-                        dot[g] = 0.f;
-#pragma unroll
-                        for (int j = 0; j < PL; j++) dot[g] = fmaf(qv[g][j], kr[u][j], dot[g]);
-                    }
-                    warp_sum_n(dot, G);
-#pragma unroll
-                    for (int g = 0; g < 8; g++) {
-                        if (g >= G) break;
-                        const float sc = dot[g] * scale;
-                        const float mn = fmaxf(m[g], sc);
-                        const float cf = expf(m[g] - mn), pe = expf(sc - mn);
-                        l[g] = l[g] * cf + pe;
-#pragma unroll
-                        for (int j = 0; j < PL; j++) acc[g][j] = fmaf(acc[g][j], cf, pe * vr[u][j]);
-                        m[g] = mn;
-                    }
-                }
+                named_bar(1, kConsumerThreads);  // the next tile reuses the buffers
             }
-            for (int g = 0; g < G; g++) {
-                if (lane == 0) { m_s[warp * 8 + g] = m[g]; l_s[warp * 8 + g] = l[g]; }
+            if (warp < G) {
+                float* pp = part_base + ((size_t)warp * a.n_split + split) * (HD + 2);
 #pragma unroll
-                for (int j = 0; j < PL; j++) acc_s[((size_t)warp * G + g) * HD + lane * PL + j] = acc[g][j];
-            }
-            named_bar(1, kConsumerThreads);
-            for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads) {
-                const int g = i / HD, d = i - g * HD;
-                float M = -INFINITY;
-                for (int w = 0; w < W; w++) M = fmaxf(M, m_s[w * 8 + g]);
-                float L = 0.f, A = 0.f;
-                for (int w = 0; w < W; w++) {
-                    if (m_s[w * 8 + g] == -INFINITY) continue;
-                    const float f = expf(m_s[w * 8 + g] - M);
-                    L += l_s[w * 8 + g] * f;
-                    A += acc_s[((size_t)w * G + g) * HD + d] * f;
-                }
-                float* pp = part_base + ((size_t)g * a.n_split + split) * (HD + 2);
-                pp[d] = A;
-                if (d == 0) { pp[HD] = M; pp[HD + 1] = L; }
+                for (int j = 0; j < PL; j++) pp[lane * PL + j] = acc[j];
+                if (lane == 0) { pp[HD] = m; pp[HD + 1] = l; }
             }
         } else {
             for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads) {
@@ -903,7 +886,7 @@ __device__ void dec_attention(const AttnArgs& a, float* scratch) {
                         A += as[j] * f;
                     }
                 }
-                a.out[(size_t)(kvh * G + g) * HD + d] = A / L;
+                st_tw(out + (size_t)(kvh * G + g) * HD + d, A / L, tag_out);
             }
             if (threadIdx.x == 0) a.counter[kvh] = 0u;
         }
@@ -914,24 +897,24 @@ __device__ void dec_attention(const AttnArgs& a, float* scratch) {
 // ---- the kernel ----------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kDecThreads, 1)
-    k_decode(const PhaseDesc* __restrict__ prog, int n_phases, DecodeCtl* ctl, unsigned int* done, int* err) {
+    k_decode(const PhaseDesc* __restrict__ prog, int n_phases, DecodeCtl* ctl, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ double red[kCW];
     __shared__ unsigned long long keys[kCW];
-    __shared__ int flag_last;
     __shared__ float part[2][kG][4];
     __shared__ int set_ok[2];
     __shared__ DecRoute route;
     DecRing r;
     r.base = smem;
     uint8_t* dig_base = smem + kDecRingBytes;
-    float* attn_scratch = reinterpret_cast<float*>(dig_base + kDecDigitBytes);
     r.full = reinterpret_cast<uint64_t*>(dig_base + kDecDigitBytes + kDecAttnBytes);
     r.empty = r.full + kDecSlots;
     r.off = reinterpret_cast<uint32_t*>(r.empty + kDecSlots);
     r.charge = r.off + kDecSlots;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const unsigned int target = (ctl->epoch + 1u) * gridDim.x;
+    // every CTA reads the epoch before any CTA can close the step (the closing CTA is the last
+    // one to finish all phases)
+    const uint32_t epoch = *reinterpret_cast<const volatile unsigned int*>(&ctl->epoch);
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDecSlots; s++) {
             mbar_init(&r.full[s], 1);
@@ -948,50 +931,48 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     uint32_t i = 0;  // ring position, advanced exactly as the producer advances it
     for (int ph = 0; ph < n_phases; ph++) {
         const PhaseDesc& p = prog[ph];
-        if (ph > 0) {
-            // grid barrier: the previous phase is complete in every CTA
-            if (threadIdx.x == 0) flag_last = wait_count(done + ph - 1, target, err) ? 0 : -1;
-            named_bar(1, kConsumerThreads);
-            if (flag_last < 0) return;
-        }
+        const uint32_t tag = step_tag(epoch, ph);
         if (p.type == PH_EMBED) {
-            if (blockIdx.x == 0) {
-                int tok = p.ctl[0];
-                if (tok < 0 || tok >= p.n_vocab) tok = 0;
-                const int8_t* q = p.emb_qs + (int64_t)tok * p.emb_K;
-                const __half* d = p.emb_d + (int64_t)tok * (p.emb_K >> 5);
-                for (int e = threadIdx.x; e < p.emb_K; e += kConsumerThreads)
-                    p.y[e] = (float)q[e] * __half2float(d[e >> 5]);
-                if (p.best && threadIdx.x == 0) *p.best = 0ull;
-            }
+            if (blockIdx.x != 0) continue;
+            int tok = p.ctl[0];
+            if (tok < 0 || tok >= p.n_vocab) tok = 0;
+            const int8_t* q = p.emb_qs + (int64_t)tok * p.emb_K;
+            const __half* d = p.emb_d + (int64_t)tok * (p.emb_K >> 5);
+            for (int e = threadIdx.x; e < p.emb_K; e += kConsumerThreads)
+                st_tw(p.y + e, (float)q[e] * __half2float(d[e >> 5]), tag);
         } else if (p.type == PH_ATTN) {
-            if (p.attn.hd == 64) dec_attention<64>(p.attn, attn_scratch);
-            else dec_attention<128>(p.attn, attn_scratch);
+            if ((int)blockIdx.x >= p.attn.n_kv * dec_attn_splits(p.attn)) continue;
+            const uint32_t tin = step_tag(epoch, p.a_qkv_ph);
+            // the attention phase uses the digit buffer and the attention scratch as one region
+            float* scratch = reinterpret_cast<float*>(dig_base);
+            if (p.attn.hd == 64) dec_attention<64>(p.attn, p.a_qkv, tin, p.a_out, tag, scratch, err);
+            else dec_attention<128>(p.attn, p.a_qkv, tin, p.a_out, tag, scratch, err);
         } else if (p.type == PH_FINISH) {
-            if (blockIdx.x == 0 && threadIdx.x == 0) {
-                const int t = argmax_key_index(__ldcg(p.best));
-                const int pos = p.ctl[1] + 1;
-                p.ctl[0] = t;
-                p.ctl[1] = pos;
-                p.trace[pos] = t;
-            }
+            continue;  // done by the CTA that closes the step
         } else if (p.type == PH_GEMV) {
+            // a CTA without groups skips the phase; the router phase runs everywhere (every CTA
+            // needs the routing of its own down rows)
+            if (!p.r_qs && (int)blockIdx.x >= (p.n_items + p.G - 1) / p.G) continue;
             const int K = p.K, nch = K >> 4;
             uint4* dig = reinterpret_cast<uint4*>(dig_base);
             float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
-            dec_stage_digits(p.x, p.norm_w, p.eps, K, dig, xsc, red);
+            dec_stage_digits(p.x, step_tag(epoch, p.x_ph), p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
             if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, &route, err);
             PhaseRegs R;
             load_phase(&p, R, expert_map(p.map) ? &route : nullptr);
             unsigned long long best_k = 0ull;
             const int ipw = R.G / 4;
-            if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, best_k, err);
-            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, best_k, err);
-            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, best_k, err);
-            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, best_k, err);
-            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, best_k, err);
-            else consume_a<3, 1>(p, R, r, i, dig, xsc, best_k, err);
+            const uint32_t tres = step_tag(epoch, p.res_ph);
+            if (R.S == 1 && ipw == 8) consume_a<1, 8>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 2 && ipw == 4) consume_a<2, 4>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else if (R.S == 3 && ipw == 2) consume_a<3, 2>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            else consume_a<3, 1>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
             if (p.epi == EK_ARGMAX) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -1007,56 +988,72 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 }
             }
         } else if (p.type == PH_DOWN4) {
+            if ((int)blockIdx.x >= (p.n_items + kG - 1) / kG) continue;
             PhaseRegs R;
             load_phase(&p, R, &route);
             const int K = R.K, nch = K >> 4;
             // the four expert inputs are one vector of 4K (blocks never straddle two of them)
             uint4* dig = reinterpret_cast<uint4*>(dig_base);
             float* xsc_all = reinterpret_cast<float*>(dig + 3 * 4 * nch);
-            dec_stage_digits(p.x, nullptr, 0.f, 4 * K, dig, xsc_all, red);
+            dec_stage_digits(p.x, step_tag(epoch, p.x_ph), nullptr, 0.f, 4 * K, dig, xsc_all, red, err);
             named_bar(1, kConsumerThreads);
             const int src = warp % 4;
             const uint4* dg = dig + src * nch;
             const float* xsc = xsc_all + src * (K >> 5);
-            consume_b(p, R, r, i, dg, xsc, &route, part, set_ok, err);
+            consume_b(p, R, r, i, dg, xsc, &route, part, set_ok, tag, step_tag(epoch, p.res_ph), err);
         }
-        // phase complete for this CTA (release by one thread after the CTA barrier, as a
-        // cooperative-groups grid sync does)
+        // the CTA's warps leave the phase together (shared digits and scratch are reused)
         named_bar(1, kConsumerThreads);
-        if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(done + ph, 1u);
-        }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        // every CTA has arrived at the last phase, so all of them have read the epoch
-        if (wait_count(done + n_phases - 1, target, err)) ctl->epoch += 1u;
+    // close the step: the last CTA to get here finishes the token and advances the epoch
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int t = atomicAdd(&ctl->end_ticket, 1u);
+        if (t == gridDim.x - 1) {
+            __threadfence();
+            const PhaseDesc& f = prog[n_phases - 1];
+            if (f.type == PH_FINISH) {
+                const int tok = argmax_key_index(__ldcg(f.best));
+                const int pos = f.ctl[1] + 1;
+                f.ctl[0] = tok;
+                f.ctl[1] = pos;
+                f.trace[pos] = tok;
+            }
+            ctl->best = 0ull;
+            ctl->end_ticket = 0u;
+            __threadfence();
+            ctl->epoch = epoch + 1u;
+        }
     }
 }
 
-int decode_stage_items(int S, int K, int n_items) {
-    // Stages of ~32 KB keep the bulk-copy stream at full rate with few handshakes; a consumer
-    // warp takes G/4 items of S rows each, at most 4 rows.
+int decode_stage_items(int S, int K, int n_div, int n_total) {
+    // Large stages amortise the per-stage work of the producer and of the consumer warps (up to
+    // kMaxRowsPerWarp rows each).  Measured on the LFM2-8B-A1B step, this wins even where it
+    // leaves CTAs without a stage in a small phase (out_proj: 64 groups of 32 rows beat 256 of
+    // 8).  G divides n_div (groups must not straddle a tensor or an expert).
+    (void)n_total;
     const int per_item = S * (K + K / 16);
     int G = 4;
-    while (S * (2 * G) / 4 <= 4 && G * per_item < 32 * 1024 && (G * 2) * per_item <= kDecMaxStageBytes) G *= 2;
-    while (G > 4 && n_items % G) G /= 2;
+    while (S * (2 * G) / 4 <= kMaxRowsPerWarp && G * per_item < kStageTarget && (G * 2) * per_item <= kDecMaxStageBytes)
+        G *= 2;
+    while (G > 4 && n_div % G) G /= 2;
     return G;
 }
 
 bool decode_phase_fits(const PhaseDesc& p) {
     if (p.type != PH_GEMV && p.type != PH_DOWN4) {
         if (p.type == PH_ATTN) {
-            const int G = p.attn.n_head / p.attn.n_kv;
-            const size_t need = ((size_t)8 * p.attn.hd + 2 * p.attn.hd + 2 * kCW * 8 + (size_t)kCW * G * p.attn.hd) * 4;
-            return (p.attn.hd == 64 || p.attn.hd == 128) && G <= 8 && need <= (size_t)kDecAttnBytes &&
-                   p.attn.n_split <= 32;
+            const int G = p.attn.n_head / p.attn.n_kv, hd = p.attn.hd;
+            const size_t need = ((size_t)8 * hd + 2 * hd + (size_t)32 * (hd + 4) + (size_t)32 * hd) * 4;
+            return (hd == 64 || hd == 128) && G >= 1 && G <= kCW && p.attn.n_head % p.attn.n_kv == 0 &&
+                   need <= (size_t)(kDecDigitBytes + kDecAttnBytes) && p.attn.n_split <= 32;
         }
         return true;
     }
     const int K = p.K, G = p.G;
     if (K < 64 || K % 64 != 0 || K > kMaxStageK || G < 4 || G % 4 != 0) return false;
-    if (p.type == PH_GEMV && (G > 16 || p.S * G / 4 > 4)) return false;
+    if (p.type == PH_GEMV && (G > 32 || p.S * G / 4 > kMaxRowsPerWarp)) return false;
     if (p.S < 1 || p.S > (p.type == PH_DOWN4 ? 4 : 3)) return false;
     if (p.type == PH_DOWN4 && (G != kG || p.top_k != 4)) return false;
     const size_t qs = (size_t)G * K, d = ((size_t)G * (K >> 4) + 15) & ~(size_t)15;
@@ -1074,8 +1071,7 @@ bool decode_phase_fits(const PhaseDesc& p) {
     return true;
 }
 
-void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, unsigned int* done, int* err,
-                        cudaStream_t s) {
+void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, int* err, cudaStream_t s) {
     const size_t smem = (size_t)kDecRingBytes + kDecDigitBytes + kDecAttnBytes + 2 * kDecSlots * 8 + 2 * kDecSlots * 4;
     static bool init = false;
     if (!init) {
@@ -1096,7 +1092,7 @@ void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, uns
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    QQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_decode, prog, n_phases, ctl, done, err));
+    QQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_decode, prog, n_phases, ctl, err));
 }
 
 }  // namespace qq3

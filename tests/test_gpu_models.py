@@ -190,3 +190,12 @@ def test_lfm2_8b_a1b_config_greedy_slice(qq3, orc):
     got = eng.model.generate(prompt, 8, think_id=124901)
     assert got.tolist() == want.tolist()
     eng.close()
+
+
+def test_default_decode_step_is_one_kernel(qq3):
+    """The persistent decode step (one kernel per token) is the default path."""
+    spec = qq3.synth.tiny_lfm2(seed=5)
+    g = qq3.synth.memory_model(spec)
+    eng = qq3.engine_for(g, device=0, max_ctx=32)
+    assert eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS) == 1
+    eng.close()
