@@ -47,6 +47,11 @@ T* dalloc(size_t n) {
     return static_cast<T*>(dmalloc(n * sizeof(T)));
 }
 
+bool getenv_flag(const char* name) {
+    const char* v = getenv(name);
+    return v && atoi(v) != 0;
+}
+
 void* ctx_scratch(qq_ctx* c, size_t bytes) {
     if (bytes > c->scratch_bytes) {
         if (c->scratch) {
@@ -713,6 +718,12 @@ int qq_q8_matmul(qq_ctx* ctx, const qq_tensor* W, const float* x_dev, int M, flo
         QQ_CHECK(W->t.type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED, "qq_q8_matmul: W must be Q8_0");
         DeviceGuard dg(ctx->device);
         const int64_t K = W->t.ne[0], N = W->t.ne[1];
+        if (M >= 2 && qq3::gemm_q8_supported(W->t) && !getenv_flag("QQ3_NO_TCGEN05")) {
+            // tensor cores: fp16 operands, f32 accumulation in TMEM (kernels_gemm.cu)
+            __half* x16 = static_cast<__half*>(ctx_scratch(ctx, qq3::gemm_q8_scratch_bytes(M, K)));
+            qq3::launch_gemm_q8(W->t, x_dev, M, x16, y_dev, ctx->stream);
+            return;
+        }
         for (int r = 0; r < M; r++) {
             qq3::XStage st;
             st.x[0] = x_dev + (size_t)r * K;

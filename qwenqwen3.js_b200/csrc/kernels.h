@@ -76,6 +76,12 @@ void launch_lfm2_router(const DTensor& router, const float* bias, const float* x
 
 int num_sms();
 
+// ---- tensor-core Q8_0 matmul for M >= 2 rows (kernels_gemm.cu) ----
+// y[M][N] = x[M][K] . W^T with x f32 row-major; x16 = scratch of gemm_q8_scratch_bytes(M, K).
+bool gemm_q8_supported(const DTensor& W);
+size_t gemm_q8_scratch_bytes(int64_t M, int64_t K);
+void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s);
+
 // ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
 // Each returns false when the shape is outside the streamed path (the caller then uses the
 // kernels above).  Launched with programmatic dependent launch unless set_pdl(0).
