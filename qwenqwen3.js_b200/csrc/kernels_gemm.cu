@@ -15,6 +15,11 @@
 //  * epilogue: each warp reads its 32 accumulator lanes (rows) with tcgen05.ld and stores f32.
 //
 // All waits are bounded (error code in the kernel error word, no hang).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <string>
+
 #include "kernels.h"
 #include "pipe.cuh"
 #include "qq3.h"
@@ -25,11 +30,8 @@ namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kStages = 3;
-constexpr int kThreadsG = 128;
 constexpr int kATile = kBM * kBK * 2;  // 16 KB
 constexpr int kBTile = kBN * kBK * 2;  // 32 KB
-constexpr int kStageBytes = kATile + kBTile;
-constexpr int kGemmSmem = kStages * kStageBytes + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 256;
 
 // K-major, 128-byte swizzle: row r of a tile is 128 B (64 fp16 of K) at r*128; its 16-byte
@@ -71,124 +73,200 @@ __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int* err)
     return false;
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
+// TMA: 2-D tiled bulk copy global -> shared, completing on an mbarrier (no multicast).
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
-__global__ void __launch_bounds__(kThreadsG, 1)
-    k_gemm_q8(const __half* __restrict__ A, int M, int K, const int8_t* __restrict__ qs, const __half* __restrict__ d,
-              int N, float* __restrict__ C, int ldc, int* err) {
+// 4 signed int8 weights -> two fp16 pairs scaled by d (exact int -> fp16 via the 1024 + byte
+// bit pattern; RN(q * d) with one HMUL2, the same rounding as converting the exact product).
+__device__ __forceinline__ void dq4(uint32_t w, __half2 d2, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;  // b + 128 per byte
+    uint32_t a = __byte_perm(u, 0x64646464u, 0x5140), b = __byte_perm(u, 0x64646464u, 0x5342);
+    const __half2 bias = __float2half2_rn(1152.0f);
+    __half2 ha = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&a), bias), d2);
+    __half2 hb = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&b), bias), d2);
+    lo = *reinterpret_cast<uint32_t*>(&ha);
+    hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+// Warp roles: 0-7 dequantise B (row = thread) and run the epilogue; 8 issues the TMA loads;
+// 9 allocates tensor memory and issues the MMAs.
+constexpr int kConvWarps = 8;
+constexpr int kThreadsG2 = (kConvWarps + 2) * 32;
+constexpr int kRawTile = kBN * kBK;                          // int8 B tile, 16 KB
+constexpr int kStage2 = kATile + kBTile + kRawTile;          // 64 KB
+constexpr int kGemmSmem2 = kStages * kStage2 + 1024;
+
+__global__ void __launch_bounds__(kThreadsG2, 1)
+    k_gemm_q8_tma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
+                  const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, int* err) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t mma_bar[kStages];
+    __shared__ __align__(8) uint64_t full_a[kStages], full_raw[kStages], raw_free[kStages], conv_done[kStages],
+        mma_done[kStages], done_bar;
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
-    if (warp == 0) {
+    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;  // M-tiles adjacent: they share the B tile in L2
+    const int nk = (K + kBK - 1) / kBK;
+    const int KB = K >> 5;
+    if (warp == kConvWarps + 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (t == 0) {
-        for (int s = 0; s < kStages; s++) mbar_init(&mma_bar[s], 1);
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full_a[s], 1);
+            mbar_init(&full_raw[s], 1);
+            mbar_init(&raw_free[s], kConvWarps);
+            mbar_init(&conv_done[s], kConvWarps);
+            mbar_init(&mma_done[s], 1);
+        }
+        mbar_init(&done_bar, 1);
         mbar_fence_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    const int nk = (K + kBK - 1) / kBK;
-    const int KB = K >> 5;  // Q8_0 blocks per row
     bool ok = true;
-    for (int kt = 0; kt < nk; kt++) {
-        const int s = kt % kStages;
-        // every thread waits for the tensor core to release this stage; the outcome is made
-        // uniform by the barrier below, so all threads leave the loop together on a timeout
-        if (kt >= kStages) ok = bar_wait(&mma_bar[s], (uint32_t)((kt / kStages - 1) & 1), err) && ok;
-        uint8_t* sa = smem + s * kStageBytes;
-        uint8_t* sb = sa + kATile;
-        const int k0 = kt * kBK;
-        // A: thread t converts row t of the tile (64 fp16 = 8 chunks); zero past M or K
-        {
-            const int row = t, m = m0 + row;
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                const int k = k0 + 8 * c;
-                if (m < M && k < K) v = __ldg(reinterpret_cast<const uint4*>(A + (size_t)m * K + k));
-                *reinterpret_cast<uint4*>(sa + sw128(row, c)) = v;
+    if (warp == kConvWarps) {
+        if (lane == 0) {  // TMA producer
+            int issued = 0;
+            for (int kt = 0; kt < nk && ok; kt++, issued++) {
+                const int s = kt % kStages;
+                const uint32_t pu = (uint32_t)((kt / kStages - 1) & 1);
+                if (kt >= kStages) ok = bar_wait(&raw_free[s], pu, err) && bar_wait(&mma_done[s], pu, err);
+                if (!ok) break;
+                uint8_t* st = smem + s * kStage2;
+                mbar_arrive_expect_tx(&full_a[s], (uint32_t)kATile);
+                tma_2d(st, &tmA, kt * kBK, m0, &full_a[s]);
+                mbar_arrive_expect_tx(&full_raw[s], (uint32_t)kRawTile);
+                tma_2d(st + kATile + kBTile, &tmB, kt * kBK, n0, &full_raw[s]);
+            }
+            // every issued copy lands before the CTA can exit (already true unless a wait failed)
+            for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; kt++) {
+                const uint32_t pu = (uint32_t)((kt / kStages) & 1);
+                bar_wait(&full_a[kt % kStages], pu, err);
+                bar_wait(&full_raw[kt % kStages], pu, err);
             }
         }
-        // B: thread t dequantises rows t and t + 128 (64 weights = two Q8_0 blocks each)
+    } else if (warp == kConvWarps + 1) {
+        if (lane == 0) {  // MMA issuer
+            for (int kt = 0; kt < nk && ok; kt++) {
+                const int s = kt % kStages;
+                const uint32_t pu = (uint32_t)((kt / kStages) & 1);
+                ok = bar_wait(&full_a[s], pu, err) && bar_wait(&conv_done[s], pu, err);
+                if (!ok) break;
+                tc_fence_after();
+                uint8_t* st = smem + s * kStage2;
+                const uint32_t a0 = smem_u32(st), b0 = smem_u32(st + kATile);
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int row = t + h * kThreadsG, n = n0 + row;
-#pragma unroll
-            for (int b = 0; b < 2; b++) {
-                const int kb = (k0 >> 5) + b;
-                uint4 q0 = make_uint4(0u, 0u, 0u, 0u), q1 = q0;
-                float sc = 0.f;
-                if (n < N && kb < KB) {
-                    const uint4* qp = reinterpret_cast<const uint4*>(qs + (size_t)n * K + (size_t)kb * 32);
-                    q0 = __ldg(qp);
-                    q1 = __ldg(qp + 1);
-                    sc = __half2float(d[(size_t)n * KB + kb]);
-                }
-                const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                for (int c = 0; c < 4; c++) {  // 8 weights per 16-byte chunk
-                    const uint32_t lo = w[2 * c], hi = w[2 * c + 1];
-                    uint4 o;
-                    o.x = pack_h2((float)(int8_t)(lo & 0xff) * sc, (float)(int8_t)((lo >> 8) & 0xff) * sc);
-                    o.y = pack_h2((float)(int8_t)((lo >> 16) & 0xff) * sc, (float)(int8_t)(lo >> 24) * sc);
-                    o.z = pack_h2((float)(int8_t)(hi & 0xff) * sc, (float)(int8_t)((hi >> 8) & 0xff) * sc);
-                    o.w = pack_h2((float)(int8_t)((hi >> 16) & 0xff) * sc, (float)(int8_t)(hi >> 24) * sc);
-                    *reinterpret_cast<uint4*>(sb + sw128(row, 4 * b + c)) = o;
-                }
+                for (int ks = 0; ks < kBK / 16; ks++)
+                    umma_f16(tmem, umma_desc(a0 + 32u * ks), umma_desc(b0 + 32u * ks), (kt | ks) != 0 ? 1u : 0u);
+                umma_commit(&mma_done[s]);
             }
+            umma_commit(&done_bar);  // covers every MMA issued
         }
-        fence_async_smem();  // generic-proxy stores -> visible to the tensor core (async proxy)
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        if (t == 0) {
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb);
+    } else {
+        // converters: thread t dequantises B row t of each stage
+        const int n = n0 + t;
+        uint32_t dnext = 0u;  // the two block scales of the next k-step, as a half2
+        auto load_d = [&](int kt) -> uint32_t {
+            __half2 v = __float2half2_rn(0.f);
+            const int kb = 2 * kt;
+            if (n < N && kb < KB) {
+                const __half* dp = d + (size_t)n * KB + kb;
+                v = __halves2half2(dp[0], kb + 1 < KB ? dp[1] : __float2half(0.f));
+            }
+            return *reinterpret_cast<uint32_t*>(&v);
+        };
+        dnext = load_d(0);
+        for (int kt = 0; kt < nk && ok; kt++) {
+            const int s = kt % kStages;
+            const uint32_t pu = (uint32_t)((kt / kStages) & 1);
+            const uint32_t dcur = dnext;
+            if (kt + 1 < nk) dnext = load_d(kt + 1);
+            uint8_t* st = smem + s * kStage2;
+            ok = __all_sync(0xffffffffu, bar_wait(&full_raw[s], pu, err));  // warp-uniform outcome
+            uint4 raw[4];
+            if (ok) {
+                const uint4* rp = reinterpret_cast<const uint4*>(st + kATile + kBTile + t * kBK);
 #pragma unroll
-            for (int ks = 0; ks < kBK / 16; ks++)  // K = 16 fp16 = 32 bytes per instruction
-                umma_f16(tmem, umma_desc(a0 + 32u * ks), umma_desc(b0 + 32u * ks), (kt | ks) != 0 ? 1u : 0u);
-            umma_commit(&mma_bar[s]);
+                for (int j = 0; j < 4; j++) raw[j] = rp[j];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_free[s]);
+            if (ok && kt >= kStages)
+                ok = __all_sync(0xffffffffu, bar_wait(&mma_done[s], (uint32_t)((kt / kStages - 1) & 1), err));
+            if (!ok) break;
+            __half2 dd[2];
+            {
+                const __half2 dc = *reinterpret_cast<const __half2*>(&dcur);
+                dd[0] = __low2half2(dc);
+                dd[1] = __high2half2(dc);
+            }
+            uint8_t* sb = st + kATile;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {  // chunk c = weights 8c..8c+7 of the 64
+                const uint4 r4 = raw[c >> 1];
+                const uint32_t w0 = (c & 1) ? r4.z : r4.x, w1 = (c & 1) ? r4.w : r4.y;
+                const __half2 d2 = dd[c >> 2];
+                uint4 o;
+                dq4(w0, d2, o.x, o.y);
+                dq4(w1, d2, o.z, o.w);
+                *reinterpret_cast<uint4*>(sb + sw128(t, c)) = o;
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&conv_done[s]);
         }
-    }
-    // the last commit covers every MMA issued before it
-    if (ok && nk > 0) ok = bar_wait(&mma_bar[(nk - 1) % kStages], (uint32_t)(((nk - 1) / kStages) & 1), err);
-    ok = __syncthreads_and(ok);
-    tc_fence_after();
-    if (ok) {
-        const int row = warp * 32 + lane, m = m0 + row;
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. (rows), columns 128 (w / 4) ..
+        if (ok) ok = bar_wait(&done_bar, 0u, err);
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+        if (ok) {
+            const int q = warp & 3, half = warp >> 2;
+            const int row = q * 32 + lane, m = m0 + row;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 16) {
-            uint32_t v[16];
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-                "[%16];"
-                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (m < M) {
-                float* crow = C + (size_t)m * ldc + n0 + c0;
+            for (int c0 = half * (kBN / 2); c0 < (half + 1) * (kBN / 2); c0 += 16) {
+                uint32_t v[16];
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                      "=r"(v[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (m < M) {
+                    float* crow = C + (size_t)m * ldc + n0 + c0;
+                    if (n0 + c0 + 16 <= N && (ldc & 3) == 0) {
 #pragma unroll
-                for (int j = 0; j < 16; j++)
-                    if (n0 + c0 + j < N) crow[j] = __uint_as_float(v[j]);
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4*>(crow + j) =
+                                make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                            __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            if (n0 + c0 + j < N) crow[j] = __uint_as_float(v[j]);
+                    }
+                }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    if (warp == kConvWarps + 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
 __global__ void k_f32_to_f16(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
@@ -204,6 +282,36 @@ bool gemm_q8_supported(const DTensor& W) { return W.K % 32 == 0 && W.K >= 32 && 
 
 size_t gemm_q8_scratch_bytes(int64_t M, int64_t K) { return (size_t)M * K * sizeof(__half); }
 
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        QQ_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        QQ_CHECK(p != nullptr && q == cudaDriverEntryPointSuccess, QQ_ERR_CUDA, "cuTensorMapEncodeTiled not available");
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D tensor map over a row-major [rows][cols] matrix; box = box_cols x box_rows.
+CUtensorMap tensor_map(void* base, CUtensorMapDataType type, int elem_bytes, uint64_t cols, uint64_t rows,
+                       uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * (cuuint64_t)elem_bytes};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, type, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    QQ_CHECK(r == CUDA_SUCCESS, QQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return m;
+}
+
+}  // namespace
+
 void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s) {
     const int64_t K = W.K, N = W.rows;
     QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
@@ -212,13 +320,18 @@ void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float*
     const size_t n = (size_t)M * K;
     k_f32_to_f16<<<(unsigned)std::min<size_t>((n / 2 + 255) / 256, 148 * 16), 256, 0, s>>>(x, x16, n);
     QQ_CUDA_TRY(cudaGetLastError());
+    // TMA: the fp16 activations arrive already 128-byte swizzled; the int8 weights plain
+    const CUtensorMap ta = tensor_map(x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K, (uint64_t)M, kBK, kBM,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMap tb = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)N, kBK, kBN,
+                                      CU_TENSOR_MAP_SWIZZLE_NONE);
     static bool init = false;
     if (!init) {
-        QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+        QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem2));
         init = true;
     }
-    dim3 grid((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
-    k_gemm_q8<<<grid, kThreadsG, kGemmSmem, s>>>(x16, M, (int)K, W.qs, W.d, (int)N, y, (int)N, kernel_err_ptr());
+    dim3 grid((unsigned)((M + kBM - 1) / kBM), (unsigned)((N + kBN - 1) / kBN));
+    k_gemm_q8_tma<<<grid, kThreadsG2, kGemmSmem2, s>>>(ta, tb, M, (int)K, W.d, (int)N, y, (int)N, kernel_err_ptr());
     QQ_CUDA_TRY(cudaGetLastError());
 }
 
