@@ -368,8 +368,11 @@ def run_moe_block(args, ws, rank, local):
     distinct = len(np.unique(ids))
     q8 = 34 / 32
     nbytes = 2048 * 32 * q8 + distinct * 3 * 2048 * 1792 * q8 + T * 2048 * 8
+    flops = T * (2 * 2048 * 32 + 4 * 3 * 2 * 2048 * 1792)  # router + 4 experts x (gate, up, down) per token
     res = {"metric": "MoE-layer HBM GB/s (isolated LFM2-MoE block)", "value": round(nbytes / (ms * 1e-3) / 1e9, 1),
            "unit": "GB/s", "tokens": T, "distinct_experts": distinct, "ms_per_step": round(ms, 4),
+           "tflops": round(flops / (ms * 1e-3) / 1e12, 2),
+           "path": "per-token expert GEMVs" if T < 16 else "rows regrouped by expert, tcgen05 GEMMs",
            "steps": args.steps, "warmup": args.warmup,
            "note": "weights only re-read from HBM when the 375 MB of experts exceed L2 between steps"}
     if rank == 0:
@@ -379,9 +382,52 @@ def run_moe_block(args, ws, rank, local):
     ctx.close()
 
 
+def run_matmul(args, ws, rank, local):
+    """one Q8_0 matmul Y[M][N] = X[M][K] . W^T (qq_q8_matmul). M = 1 runs the
+    streamed GEMV, M >= 2 the tcgen05 tensor-core kernel."""
+    import torch
+
+    qq3 = load_package()
+    qq3.build.build_all()
+    torch.cuda.set_device(local)
+    M, N, K = args.M, args.N, args.K
+    ctx = qq3.runtime.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    W = ctx.upload(qq3.synth.q8_0_blocks(N * K, seed=N + K, mode=1), 8, [K, N])
+    x = torch.from_numpy(qq3.synth.normal_f32(M * K, seed=M).reshape(M, K)).cuda()
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        ctx.q8_matmul(W, x, M, y)
+    ctx.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ctx.q8_matmul(W, x, M, y)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nbytes = 34 / 32 * N * K + 4 * M * K + 4 * M * N
+    peak, kind = _peaks()
+    res = {"metric": "Q8_0 matmul throughput", "value": round(2 * M * N * K / (ms * 1e-3) / 1e12, 2),
+           "unit": "TFLOP/s", "M": M, "N": N, "K": K, "ms_per_step": round(ms, 5),
+           "hbm_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1), "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+           "peak_kind": kind, "path": "streamed GEMV" if M == 1 else "tcgen05 fp16 GEMM (TMEM accumulators)",
+           "steps": args.steps, "warmup": args.warmup,
+           "note": "weights are the same every step; M = 1 re-reads them from HBM only beyond the 126 MB L2"}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    W.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--case", choices=["decode", "moe-block"], default="decode")
+    ap.add_argument("--case", choices=["decode", "moe-block", "matmul"], default="decode")
+    ap.add_argument("--M", type=int, default=4096, help="rows for --case matmul")
+    ap.add_argument("--N", type=int, default=151936, help="output columns for --case matmul")
+    ap.add_argument("--K", type=int, default=1024, help="inner dimension for --case matmul")
     ap.add_argument("--tokens", type=int, default=1, help="token rows for --case moe-block")
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (decode)")
     ap.add_argument("--gpus", type=int, default=1)
@@ -400,6 +446,8 @@ def main():
         run_reference(args, ws, rank)
     elif args.case == "moe-block":
         run_moe_block(args, ws, rank, local)
+    elif args.case == "matmul":
+        run_matmul(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
 

@@ -1092,6 +1092,10 @@ int qq_bench_kernel(qq_model* m, int what, int iters, float* ms) {
     });
 }
 
+// T at and above which qq_moe_block regroups the rows by expert (tensor-core GEMMs) instead of
+// running the per-token expert GEMVs
+constexpr int kGroupedMoeRows = 16;
+
 int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
                  float* out_dev, float* routing_dev) {
     return guard([&] {
@@ -1116,7 +1120,9 @@ int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_
         const int rec_len = 2 * top_k + n_expert;
         // scratch: idx [T][k] | w [T][k] | record [T][rec_len] (unless the caller wants it) | h [k][F]
         const size_t b_idx = (size_t)T * top_k * 4, b_w = b_idx, b_rec = routing_dev ? 0 : (size_t)T * rec_len * 4;
-        const size_t b_h = (size_t)top_k * F * 4;
+        const bool grouped = T >= kGroupedMoeRows && qq3::gemm_q8_supported(*gate) && qq3::gemm_q8_supported(*down) &&
+                             !getenv_flag("QQ3_NO_TCGEN05");
+        const size_t b_h = grouped ? qq3::moe_grouped_scratch_bytes(T, top_k, n_expert, K, F) : (size_t)top_k * F * 4;
         auto align = [](size_t v) { return (v + 255) & ~(size_t)255; };
         char* base = static_cast<char*>(ctx_scratch(ctx, align(b_idx) + align(b_w) + align(b_rec) + align(b_h)));
         int* idx = reinterpret_cast<int*>(base);
@@ -1125,6 +1131,10 @@ int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_
         float* h = reinterpret_cast<float*>(base + align(b_idx) + align(b_w) + align(b_rec));
         qq3::launch_lfm2_router(*router, bias ? bias->f32 : nullptr, x_dev, T, nullptr, 0.f, n_expert, top_k, rec, idx,
                                 w, s);
+        if (grouped) {  // rows regrouped by expert: each expert's weights stream once (tensor cores)
+            qq3::launch_moe_grouped(*gate, *up, *down, idx, w, x_dev, T, top_k, n_expert, h, out_dev, s);
+            return;
+        }
         QQ_CUDA_TRY(cudaMemsetAsync(out_dev, 0, sizeof(float) * (size_t)T * K, s));
         for (int t = 0; t < T; t++) {
             qq3::XStage st;

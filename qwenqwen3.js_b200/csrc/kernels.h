@@ -81,6 +81,23 @@ int num_sms();
 bool gemm_q8_supported(const DTensor& W);
 size_t gemm_q8_scratch_bytes(int64_t M, int64_t K);
 void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s);
+// Grouped form: W holds groups of group_rows rows (e.g. the experts of a packed tensor); work
+// item i = tiles[i] = (group, first row of a16, rows <= 128), *n_tiles items, max_tiles >= it.
+struct GemmGroups {
+    const int4* tiles;
+    const int* n_tiles;
+    int max_tiles;
+};
+// y[r][c] (row stride ldc) = a16[r] . W[group * group_rows + c] for c < group_rows
+void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16, int M, float* y, int ldc,
+                        const GemmGroups* groups, cudaStream_t s);
+void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
+
+// ---- MoE block for T rows regrouped by expert on the tensor cores (kernels_moe_grouped.cu) ----
+size_t moe_grouped_scratch_bytes(int T, int top_k, int n_expert, int64_t K, int64_t F);
+// idx/w: routed ids and weights [T][top_k]; out[T][K] = sum_s w[t][s] * down_e(silu(gate_e x) * up_e x)
+void launch_moe_grouped(const DTensor& gate, const DTensor& up, const DTensor& down, const int* idx, const float* w,
+                        const float* x, int T, int top_k, int n_expert, void* scratch, float* out, cudaStream_t s);
 
 // ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
 // Each returns false when the shape is outside the streamed path (the caller then uses the

@@ -104,14 +104,28 @@ constexpr int kGemmSmem2 = kStages * kStage2 + 1024;
 
 __global__ void __launch_bounds__(kThreadsG2, 1)
     k_gemm_q8_tma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
-                  const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, int* err) {
+                  const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, const int4* __restrict__ tiles,
+                  const int* __restrict__ n_tiles, int* err) {
+    // Dense: CTA (x, y) computes rows [128x, 128x + 128) x columns [256y, 256y + 256).
+    // Grouped (tiles != null): CTA x takes work item tiles[x] = (group g, first row, rows); its B
+    // rows are those of group g (rows g*N .. g*N + N - 1 of W), e.g. one expert of a packed
+    // expert tensor.  Items past *n_tiles exit at once.
+    int grp = 0, m0 = blockIdx.x * kBM, m_rows = M - m0;
+    if (tiles) {
+        if ((int)blockIdx.x >= *n_tiles) return;
+        const int4 ti = tiles[blockIdx.x];
+        grp = ti.x;
+        m0 = ti.y;
+        m_rows = ti.z;
+    }
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t full_a[kStages], full_raw[kStages], raw_free[kStages], conv_done[kStages],
         mma_done[kStages], done_bar;
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;  // M-tiles adjacent: they share the B tile in L2
+    const int n0 = blockIdx.y * kBN;  // M-tiles adjacent: they share the B tile in L2
+    const int nb0 = grp * N + n0;     // first B row of the tile in W
     const int nk = (K + kBK - 1) / kBK;
     const int KB = K >> 5;
     if (warp == kConvWarps + 1) {
@@ -148,7 +162,7 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                 mbar_arrive_expect_tx(&full_a[s], (uint32_t)kATile);
                 tma_2d(st, &tmA, kt * kBK, m0, &full_a[s]);
                 mbar_arrive_expect_tx(&full_raw[s], (uint32_t)kRawTile);
-                tma_2d(st + kATile + kBTile, &tmB, kt * kBK, n0, &full_raw[s]);
+                tma_2d(st + kATile + kBTile, &tmB, kt * kBK, nb0, &full_raw[s]);
             }
             // every issued copy lands before the CTA can exit (already true unless a wait failed)
             for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; kt++) {
@@ -176,13 +190,14 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
         }
     } else {
         // converters: thread t dequantises B row t of each stage
-        const int n = n0 + t;
+        const int n = n0 + t;                 // column of the output
+        const size_t drow = (size_t)(nb0 + t);  // row of W
         uint32_t dnext = 0u;  // the two block scales of the next k-step, as a half2
         auto load_d = [&](int kt) -> uint32_t {
             __half2 v = __float2half2_rn(0.f);
             const int kb = 2 * kt;
             if (n < N && kb < KB) {
-                const __half* dp = d + (size_t)n * KB + kb;
+                const __half* dp = d + drow * KB + kb;
                 v = __halves2half2(dp[0], kb + 1 < KB ? dp[1] : __float2half(0.f));
             }
             return *reinterpret_cast<uint32_t*>(&v);
@@ -234,6 +249,7 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
         if (ok) {
             const int q = warp & 3, half = warp >> 2;
             const int row = q * 32 + lane, m = m0 + row;
+            const bool live = row < m_rows;
 #pragma unroll 1
             for (int c0 = half * (kBN / 2); c0 < (half + 1) * (kBN / 2); c0 += 16) {
                 uint32_t v[16];
@@ -246,7 +262,7 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                       "=r"(v[15])
                     : "r"(taddr));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (m < M) {
+                if (live) {
                     float* crow = C + (size_t)m * ldc + n0 + c0;
                     if (n0 + c0 + 16 <= N && (ldc & 3) == 0) {
 #pragma unroll
@@ -312,27 +328,41 @@ CUtensorMap tensor_map(void* base, CUtensorMapDataType type, int elem_bytes, uin
 
 }  // namespace
 
-void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s) {
-    const int64_t K = W.K, N = W.rows;
+void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16, int M, float* y, int ldc,
+                        const GemmGroups* groups, cudaStream_t s) {
+    const int64_t K = W.K, N = group_rows;
     QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
-    QQ_CHECK(N <= (int64_t)65535 * kBN && M <= 65535 * kBM, QQ_ERR_INVALID, "tensor-core Q8_0 matmul: too large");
-    if (M <= 0 || N <= 0) return;
-    const size_t n = (size_t)M * K;
-    k_f32_to_f16<<<(unsigned)std::min<size_t>((n / 2 + 255) / 256, 148 * 16), 256, 0, s>>>(x, x16, n);
-    QQ_CUDA_TRY(cudaGetLastError());
+    QQ_CHECK(N >= 1 && W.rows % N == 0 && N <= (int64_t)65535 * kBN && M <= 65535 * kBM, QQ_ERR_INVALID,
+             "tensor-core Q8_0 matmul: bad shape");
+    if (M <= 0) return;
     // TMA: the fp16 activations arrive already 128-byte swizzled; the int8 weights plain
-    const CUtensorMap ta = tensor_map(x16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K, (uint64_t)M, kBK, kBM,
-                                      CU_TENSOR_MAP_SWIZZLE_128B);
-    const CUtensorMap tb = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)N, kBK, kBN,
+    const CUtensorMap ta = tensor_map(const_cast<__half*>(a16), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
+                                      (uint64_t)M, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMap tb = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, kBK, kBN,
                                       CU_TENSOR_MAP_SWIZZLE_NONE);
     static bool init = false;
     if (!init) {
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem2));
         init = true;
     }
-    dim3 grid((unsigned)((M + kBM - 1) / kBM), (unsigned)((N + kBN - 1) / kBN));
-    k_gemm_q8_tma<<<grid, kThreadsG2, kGemmSmem2, s>>>(ta, tb, M, (int)K, W.d, (int)N, y, (int)N, kernel_err_ptr());
+    const unsigned gx = groups ? (unsigned)groups->max_tiles : (unsigned)((M + kBM - 1) / kBM);
+    dim3 grid(gx, (unsigned)((N + kBN - 1) / kBN));
+    k_gemm_q8_tma<<<grid, kThreadsG2, kGemmSmem2, s>>>(ta, tb, M, (int)K, W.d, (int)N, y, ldc,
+                                                       groups ? groups->tiles : nullptr,
+                                                       groups ? groups->n_tiles : nullptr, kernel_err_ptr());
     QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
+    if (n == 0) return;
+    k_f32_to_f16<<<(unsigned)std::min<size_t>((n / 2 + 255) / 256, 148 * 16), 256, 0, s>>>(x, y, n);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s) {
+    if (M <= 0 || W.rows <= 0) return;
+    launch_f32_to_f16(x, x16, (size_t)M * W.K, s);
+    launch_gemm_q8_f16(W, W.rows, x16, M, y, (int)W.rows, nullptr, s);
 }
 
 }  // namespace qq3

@@ -136,8 +136,9 @@ def _upload_layer(qq3, gpu_ctx, tensors):
     return L, keep
 
 
-@pytest.mark.parametrize("T", [1, 64])
+@pytest.mark.parametrize("T", [1, 15, 16, 64])
 def test_moe_block_vs_oracle(qq3, orc, gpu_ctx, torch, T):
+    """T < 16: per-token expert GEMVs; T >= 16: rows regrouped by expert on the tensor cores."""
     orc.set_threads(8)
     tensors = _moe_layer(qq3)
     L, keep = _upload_layer(qq3, gpu_ctx, tensors)
@@ -160,5 +161,29 @@ def test_moe_block_vs_oracle(qq3, orc, gpu_ctx, torch, T):
     assert rel_err(got_rec[:, 4:8], want_rec[:, 4:8]) < 1e-5  # normalised weights
     for t in range(T):
         assert rel_err(out.cpu().numpy()[t], want[t]) < TOL
+    for k in keep:
+        k.free()
+
+
+def test_moe_block_t2048_sampled_rows(qq3, orc, gpu_ctx, torch):
+    """BASELINE config 3 at T = 2048 (grouped tensor-core path): every row on the GPU, a seeded
+    sample of rows on the oracle (the block is row-independent)."""
+    orc.set_threads(8)
+    T = 2048
+    tensors = _moe_layer(qq3, seed=9)
+    L, keep = _upload_layer(qq3, gpu_ctx, tensors)
+    x = qq3.synth.normal_f32(T * 2048, seed=77).reshape(T, 2048)
+    out = torch.empty((T, 2048), dtype=torch.float32, device="cuda")
+    rec = torch.empty((T, 2 * 4 + 32), dtype=torch.float32, device="cuda")
+    gpu_ctx.moe_block(L, 32, 4, _dev(torch, x), T, out, rec)
+    gpu_ctx.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = np.unique(np.concatenate([[0, T - 1], qq3.synth.uniform_tokens(14, 5, T)]))
+    want, want_rec = orc.lfm2_moe(tensors, 2048, 32, 4, x[rows])
+    got_rec = rec.cpu().numpy()[rows]
+    for i, t in enumerate(rows):
+        if np.array_equal(got_rec[i, :4], want_rec[i, :4]):
+            assert rel_err(got[t], want[i]) < TOL, f"token {t}"
     for k in keep:
         k.free()
