@@ -171,7 +171,11 @@ def run_ours(args, ws, rank, local):
     prompt = qq3.synth.uniform_tokens(args.prompt, SEED + rank, spec.n_vocab)
     suppress = THINK_ID if THINK_ID < spec.n_vocab else -1
 
-    eng.prefill(prompt[:-1].tolist())
+    torch.cuda.synchronize()
+    t_pf = time.perf_counter()
+    eng.prefill(prompt[:-1].tolist())  # batched (tensor cores) from 64 tokens on
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t_pf
     pos = args.prompt - 1
     toks = eng.model.decode_loop(int(prompt[-1]), pos, args.warmup, suppress_id=suppress)
     pos += args.warmup
@@ -261,6 +265,8 @@ def run_ours(args, ws, rank, local):
                 "api": "Lfm2CudaEngine.forward_argmax -> qq_forward"},
         "gpu_launches": int(step_kernels * args.steps),
         "clocks": clk.summary(),
+        "prefill": {"tokens": args.prompt - 1, "ms": round(prefill_s * 1e3, 2),
+                    "tok_s": round((args.prompt - 1) / prefill_s, 1), "note": "untimed setup, host wall clock"},
         "setup_s": {"weight_generation": round(gen_s, 1)},
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:

@@ -116,6 +116,9 @@ struct qq_model {
     };
     std::map<std::pair<int, int>, Prog> progs;
     qq3::DecodeCtl* dctl = nullptr;  // model-wide control block of the persistent kernel
+    // batched prefill buffers for up to pf_cap tokens (grow-only)
+    int pf_cap = 0;
+    void* pf_arena = nullptr;
     qq3::tword* tarena = nullptr;    // tagged activations: one buffer per phase output
     size_t tarena_len = 0;
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
@@ -135,6 +138,7 @@ void free_model(qq_model* m) {
         if (kv.second.d_prog) cudaFree(kv.second.d_prog);
     m->progs.clear();
     if (m->dctl) cudaFree(m->dctl);
+    if (m->pf_arena) cudaFree(m->pf_arena);
     if (m->tarena) cudaFree(m->tarena);
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
                     m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
@@ -543,9 +547,170 @@ void set_suppress(qq_model* m, int id) {
     QQ_CUDA_TRY(cudaMemcpyAsync(m->suppress, m->h_small, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
 }
 
+// ---- batched prefill -------------------------------------------------------------------
+// T prompt tokens at positions pos0.. through the layers at once: projections as tensor-core
+// GEMMs, the MoE regrouped by expert, causal attention and the short-conv recurrence over the
+// T rows (kernels_prefill.cu).  Same semantics as T sequential forward(t, pos, true) calls
+// (qwen3-engine.js:397-457, lfm2-engine.js:523-583); the routing record of each MoE layer is
+// that of the last token, as after the sequential calls.
+
+constexpr int kPrefillChunk = 1024;  // tokens per pass (bounds the buffers)
+// Shorter prompts take the per-token decode step.  Both meet the parity bar, but the tensor-core
+// projections carry ~3e-6 relative error at K = 2048 (the tensor core's f32 accumulation) against
+// ~1e-7 for the GEMV, so a router near-tie (selection-score gap < 1e-5, which the bar exempts)
+// can resolve the other way in a batched prefill and change later tokens.
+constexpr int kBatchedPrefillMin = 64;
+
+struct PrefillBufs {
+    int* tok;
+    float *hidden, *xn, *y, *tmp, *bcx, *q, *k, *v, *attn, *g, *u, *h, *rec, *w;
+    int* idx;
+    __half* x16;
+    void* moe;
+};
+
+PrefillBufs prefill_bufs(qq_model* m, int T) {
+    const qq_model_desc& d = m->d;
+    const size_t E = d.n_embd, nq = (size_t)d.n_head * d.head_dim, nkv = (size_t)d.n_head_kv * d.head_dim;
+    size_t F = 0, Fe = 0;
+    for (const Layer& L : m->layers) {
+        if (L.moe) Fe = std::max<size_t>(Fe, L.t[QQ_GATE_EXPS]->ne[1]);
+        else if (L.t[QQ_FFN_GATE]) F = std::max<size_t>(F, L.t[QQ_FFN_GATE]->ne[1]);
+    }
+    const int k = std::max(d.n_expert_used, 1);
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t C = (size_t)T;
+    const size_t sizes[] = {al(C * 4),                                            // tok
+                            al(C * E * 4), al(C * E * 4), al(C * E * 4), al(C * E * 4),  // hidden xn y tmp
+                            al(C * 3 * E * 4), al(C * nq * 4), al(C * nkv * 4), al(C * nkv * 4),
+                            al(C * nq * 4),                                        // attn
+                            al(C * F * 4), al(C * F * 4), al(C * F * 4),           // g u h
+                            al(C * (2 * k + d.n_expert) * 4), al(C * k * 4), al(C * k * 4),  // rec w idx
+                            al(C * std::max({E, nq, F}) * 2 * (qq3::gemm_exact() ? 2 : 1)),  // x16 (hi, lo)
+                            Fe ? al(qq3::moe_grouped_scratch_bytes(T, k, d.n_expert, E, Fe)) : 0};
+    size_t total = 0;
+    for (size_t v : sizes) total += v;
+    if (T > m->pf_cap) {
+        if (m->pf_arena) {
+            QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+            cudaFree(m->pf_arena);
+            m->pf_arena = nullptr;
+            m->pf_cap = 0;
+        }
+        m->pf_arena = dmalloc(total);
+        m->pf_cap = T;
+    }
+    char* b = static_cast<char*>(m->pf_arena);
+    size_t i = 0;
+    auto take = [&]() {
+        char* r = b;
+        b += sizes[i++];
+        return r;
+    };
+    PrefillBufs p;
+    p.tok = reinterpret_cast<int*>(take());
+    p.hidden = reinterpret_cast<float*>(take());
+    p.xn = reinterpret_cast<float*>(take());
+    p.y = reinterpret_cast<float*>(take());
+    p.tmp = reinterpret_cast<float*>(take());
+    p.bcx = reinterpret_cast<float*>(take());
+    p.q = reinterpret_cast<float*>(take());
+    p.k = reinterpret_cast<float*>(take());
+    p.v = reinterpret_cast<float*>(take());
+    p.attn = reinterpret_cast<float*>(take());
+    p.g = reinterpret_cast<float*>(take());
+    p.u = reinterpret_cast<float*>(take());
+    p.h = reinterpret_cast<float*>(take());
+    p.rec = reinterpret_cast<float*>(take());
+    p.w = reinterpret_cast<float*>(take());
+    p.idx = reinterpret_cast<int*>(take());
+    p.x16 = reinterpret_cast<__half*>(take());
+    p.moe = take();
+    return p;
+}
+
+void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0) {
+    const qq_model_desc& d = m->d;
+    cudaStream_t s = m->ctx->stream;
+    const int E = d.n_embd, hd = d.head_dim;
+    PrefillBufs b = prefill_bufs(m, T);
+    QQ_CUDA_TRY(cudaMemcpyAsync(b.tok, tokens, sizeof(int) * T, cudaMemcpyHostToDevice, s));
+    qq3::launch_embed_rows(*m->tok_embd, b.tok, T, d.n_vocab, b.hidden, s);
+    const size_t TE = (size_t)T * E;
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
+        if (L.attn) {
+            qq3::launch_gemm_q8(*L.t[QQ_WQ], b.xn, T, b.x16, b.q, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WV], b.xn, T, b.x16, b.v, s);
+            qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
+            qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
+            qq3::launch_rope_rows(b.q, T, d.n_head, hd, m->rope_cs, pos0, s);
+            qq3::launch_rope_rows(b.k, T, d.n_head_kv, hd, m->rope_cs, pos0, s);
+            float* kc = m->k_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+            float* vc = m->v_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+            qq3::launch_kv_append(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, pos0, kc, vc, s);
+            qq3::launch_attn_prefill(b.q, kc, vc, T, pos0, d.n_head, d.n_head_kv, hd, d.max_ctx, b.attn, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WO], b.attn, T, b.x16, b.tmp, s);
+        } else {
+            qq3::launch_gemm_q8(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.bcx, s);
+            qq3::launch_conv_prefill(b.bcx, L.t[QQ_CONV]->f32, m->conv(seq, l), T, E, b.y, s);
+            qq3::launch_gemm_q8(*L.t[QQ_OUT_PROJ], b.y, T, b.x16, b.tmp, s);
+        }
+        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
+        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, s);
+        if (L.moe) {
+            const int k = d.n_expert_used;
+            const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+            qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, b.xn, T, nullptr, 0.f, d.n_expert, k, b.rec, b.idx, b.w, s);
+            // the layer's routing record / ids / weights: those of the last token
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->rec + (size_t)L.moe_slot * m->rec_len, b.rec + (size_t)(T - 1) * m->rec_len,
+                                        sizeof(float) * m->rec_len, cudaMemcpyDeviceToDevice, s));
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->ridx + (size_t)L.moe_slot * k, b.idx + (size_t)(T - 1) * k,
+                                        sizeof(int) * k, cudaMemcpyDeviceToDevice, s));
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->rw + (size_t)L.moe_slot * k, b.w + (size_t)(T - 1) * k, sizeof(float) * k,
+                                        cudaMemcpyDeviceToDevice, s));
+            qq3::launch_moe_grouped(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], *L.t[QQ_DOWN_EXPS], b.idx, b.w, m->mask,
+                                    b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
+        } else {
+            const size_t F = L.t[QQ_FFN_GATE]->ne[1];
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.g, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s);
+            qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s);
+        }
+        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
+    }
+}
+
+bool batched_prefill_ok(qq_model* m) {
+    if (getenv_flag("QQ3_NO_TCGEN05")) return false;
+    if (const char* v = getenv("QQ3_PREFILL_BATCH"))
+        if (atoi(v) == 0) return false;
+    const qq_model_desc& d = m->d;
+    if (d.head_dim != 64 && d.head_dim != 128) return false;
+    for (const Layer& L : m->layers)
+        for (int sl = 0; sl < QQ_SLOT_COUNT; sl++)
+            if (L.t[sl] && L.t[sl]->type == QQ_TYPE_Q8_0 && !qq3::gemm_q8_supported(*L.t[sl])) return false;
+    return true;
+}
+
 // host-driven steps: token_ids[i] at pos0 + i; logits graph for the last one if requested
 void run_tokens(qq_model* m, const int32_t* token_ids, int n, int seq, int pos0, bool want_logits) {
     cudaStream_t s = m->ctx->stream;
+    for (int i = 0; i < n; i++) need(token_ids[i] >= 0 && token_ids[i] < m->d.n_vocab, "token id out of range");
+    // a long prefix runs batched; the token that needs logits takes the decode step below
+    const int n_batch = want_logits ? n - 1 : n;
+    if (n_batch >= kBatchedPrefillMin && batched_prefill_ok(m)) {
+        for (int c = 0; c < n_batch; c += kPrefillChunk)
+            prefill_chunk(m, token_ids + c, std::min(kPrefillChunk, n_batch - c), seq, pos0 + c);
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // the host token array is read asynchronously above
+        token_ids += n_batch;
+        pos0 += n_batch;
+        n -= n_batch;
+        if (n == 0) return;
+    }
     ensure_h_ctl(m, (size_t)n);
     for (int i = 0; i < n; i++) {
         need(token_ids[i] >= 0 && token_ids[i] < m->d.n_vocab, "token id out of range");
@@ -1132,7 +1297,7 @@ int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_
         qq3::launch_lfm2_router(*router, bias ? bias->f32 : nullptr, x_dev, T, nullptr, 0.f, n_expert, top_k, rec, idx,
                                 w, s);
         if (grouped) {  // rows regrouped by expert: each expert's weights stream once (tensor cores)
-            qq3::launch_moe_grouped(*gate, *up, *down, idx, w, x_dev, T, top_k, n_expert, h, out_dev, s);
+            qq3::launch_moe_grouped(*gate, *up, *down, idx, w, nullptr, x_dev, T, top_k, n_expert, h, out_dev, s);
             return;
         }
         QQ_CUDA_TRY(cudaMemsetAsync(out_dev, 0, sizeof(float) * (size_t)T * K, s));

@@ -79,6 +79,9 @@ int num_sms();
 // ---- tensor-core Q8_0 matmul for M >= 2 rows (kernels_gemm.cu) ----
 // y[M][N] = x[M][K] . W^T with x f32 row-major; x16 = scratch of gemm_q8_scratch_bytes(M, K).
 bool gemm_q8_supported(const DTensor& W);
+// true (default): three-product fp16 split, ~2^-22 relative like the f32 GEMV; QQ3_GEMM_FAST=1:
+// one fp16 product (~1e-3).  Operand buffers then hold hi rows followed by lo rows.
+bool gemm_exact();
 size_t gemm_q8_scratch_bytes(int64_t M, int64_t K);
 void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s);
 // Grouped form: W holds groups of group_rows rows (e.g. the experts of a packed tensor); work
@@ -96,8 +99,21 @@ void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 // ---- MoE block for T rows regrouped by expert on the tensor cores (kernels_moe_grouped.cu) ----
 size_t moe_grouped_scratch_bytes(int T, int top_k, int n_expert, int64_t K, int64_t F);
 // idx/w: routed ids and weights [T][top_k]; out[T][K] = sum_s w[t][s] * down_e(silu(gate_e x) * up_e x)
+// over the slots whose expert is not set in mask (nullable bitset)
 void launch_moe_grouped(const DTensor& gate, const DTensor& up, const DTensor& down, const int* idx, const float* w,
-                        const float* x, int T, int top_k, int n_expert, void* scratch, float* out, cudaStream_t s);
+                        const uint32_t* mask, const float* x, int T, int top_k, int n_expert, void* scratch, float* out,
+                        cudaStream_t s);
+
+// ---- batched prefill pieces (kernels_prefill.cu) ----
+void launch_embed_rows(const DTensor& E, const int* tok, int T, int n_vocab, float* out, cudaStream_t s);
+void launch_rope_rows(float* x, int T, int n_heads, int hd, const float* cs, int pos0, cudaStream_t s);
+void launch_kv_append(const float* k, const float* v, int T, int n_kv, int hd, int max_ctx, int pos0, float* kc,
+                      float* vc, cudaStream_t s);
+void launch_conv_prefill(const float* bcx, const float* w, float* state, int T, int E, float* y, cudaStream_t s);
+void launch_add_rows(float* x, const float* d, size_t n, cudaStream_t s);
+void launch_swiglu_rows(const float* g, const float* u, size_t n, float* h, cudaStream_t s);
+void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T, int pos0, int n_head, int n_kv,
+                         int hd, int max_ctx, float* out, cudaStream_t s);
 
 // ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
 // Each returns false when the shape is outside the streamed path (the caller then uses the

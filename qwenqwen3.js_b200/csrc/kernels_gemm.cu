@@ -28,10 +28,8 @@ namespace qq3 {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kBM = 128, kBK = 64;
 constexpr int kStages = 3;
-constexpr int kATile = kBM * kBK * 2;  // 16 KB
-constexpr int kBTile = kBN * kBK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = 256;
 
 // K-major, 128-byte swizzle: row r of a tile is 128 B (64 fp16 of K) at r*128; its 16-byte
@@ -45,17 +43,6 @@ __device__ __forceinline__ uint32_t sw128(int row, int chunk) {
 // version 1, layout SWIZZLE_128B (2).
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// Instruction descriptor: D f32, A/B fp16, both K-major, N = kBN, M = kBM.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
-    const uint32_t mask[4] = {0u, 0u, 0u, 0u};
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate), "r"(mask[0]), "r"(mask[1]), "r"(mask[2]), "r"(mask[3]));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -94,22 +81,58 @@ __device__ __forceinline__ void dq4(uint32_t w, __half2 d2, uint32_t& lo, uint32
     hi = *reinterpret_cast<uint32_t*>(&hb);
 }
 
-// Warp roles: 0-7 dequantise B (row = thread) and run the epilogue; 8 issues the TMA loads;
-// 9 allocates tensor memory and issues the MMAs.
+// Warp roles: 0-7 dequantise B and run the epilogue; 8 issues the TMA loads; 9 allocates
+// tensor memory and issues the MMAs.
 constexpr int kConvWarps = 8;
 constexpr int kThreadsG2 = (kConvWarps + 2) * 32;
-constexpr int kRawTile = kBN * kBK;                          // int8 B tile, 16 KB
-constexpr int kStage2 = kATile + kBTile + kRawTile;          // 64 KB
-constexpr int kGemmSmem2 = kStages * kStage2 + 1024;
 
+// SPLIT = 1: one fp16 product (x and w = q*d rounded to 11-bit significands; ~1e-3 relative).
+// SPLIT = 3: x = xh + xl/2048 and w = wh + wl/2048 split into fp16 pairs (w exactly: q*d has at
+//   most 18 significant bits), three products xh.wh -> D1 and xh.wl + xl.wh -> D2 in two TMEM
+//   accumulators, y = D1 + D2/2048: ~2^-22 relative, the f32 GEMV's accuracy.
+template <int SPLIT>
+struct Cfg {
+    static constexpr int BN = SPLIT == 1 ? 256 : 128;
+    static constexpr int NT = SPLIT == 1 ? 1 : 2;     // operand tiles per side (hi, lo)
+    static constexpr int ATile = kBM * kBK * 2;       // 16 KB
+    static constexpr int BTile = BN * kBK * 2;        // 32 KB / 16 KB
+    static constexpr int RawTile = BN * kBK;          // int8
+    static constexpr int Stage = NT * ATile + NT * BTile + RawTile;
+    static constexpr int Smem = kStages * Stage + 1024;
+    static constexpr uint32_t Idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+    static constexpr int RowThreads = 256 / BN;       // converter threads per B row
+};
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    const uint32_t mask[4] = {0u, 0u, 0u, 0u};
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask[0]), "r"(mask[1]), "r"(mask[2]), "r"(mask[3]));
+}
+
+__device__ __forceinline__ uint32_t h2bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
+template <int SPLIT>
 __global__ void __launch_bounds__(kThreadsG2, 1)
     k_gemm_q8_tma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
                   const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, const int4* __restrict__ tiles,
                   const int* __restrict__ n_tiles, int* err) {
-    // Dense: CTA (x, y) computes rows [128x, 128x + 128) x columns [256y, 256y + 256).
+    using G = Cfg<SPLIT>;
+    constexpr int BN = G::BN;
+    // Dense: CTA (x, y) computes rows [128x, 128x + 128) x columns [BN y, BN y + BN).
     // Grouped (tiles != null): CTA x takes work item tiles[x] = (group g, first row, rows); its B
     // rows are those of group g (rows g*N .. g*N + N - 1 of W), e.g. one expert of a packed
-    // expert tensor.  Items past *n_tiles exit at once.
+    // expert tensor.  Items past *n_tiles exit at once.  With SPLIT = 3 the A map holds the hi
+    // rows at 0.. and the lo rows at M..
     int grp = 0, m0 = blockIdx.x * kBM, m_rows = M - m0;
     if (tiles) {
         if ((int)blockIdx.x >= *n_tiles) return;
@@ -124,10 +147,14 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int n0 = blockIdx.y * kBN;  // M-tiles adjacent: they share the B tile in L2
+    const int n0 = blockIdx.y * BN;   // M-tiles adjacent: they share the B tile in L2
     const int nb0 = grp * N + n0;     // first B row of the tile in W
     const int nk = (K + kBK - 1) / kBK;
     const int KB = K >> 5;
+    // stage layout: A tiles | B tiles | raw int8 B
+    auto a_tile = [&](uint8_t* st, int h) { return st + h * G::ATile; };
+    auto b_tile = [&](uint8_t* st, int h) { return st + G::NT * G::ATile + h * G::BTile; };
+    auto raw_tile = [&](uint8_t* st) { return st + G::NT * (G::ATile + G::BTile); };
     if (warp == kConvWarps + 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
                      "r"(kTmemCols)
@@ -158,11 +185,12 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                 const uint32_t pu = (uint32_t)((kt / kStages - 1) & 1);
                 if (kt >= kStages) ok = bar_wait(&raw_free[s], pu, err) && bar_wait(&mma_done[s], pu, err);
                 if (!ok) break;
-                uint8_t* st = smem + s * kStage2;
-                mbar_arrive_expect_tx(&full_a[s], (uint32_t)kATile);
-                tma_2d(st, &tmA, kt * kBK, m0, &full_a[s]);
-                mbar_arrive_expect_tx(&full_raw[s], (uint32_t)kRawTile);
-                tma_2d(st + kATile + kBTile, &tmB, kt * kBK, nb0, &full_raw[s]);
+                uint8_t* st = smem + s * G::Stage;
+                mbar_arrive_expect_tx(&full_a[s], (uint32_t)(G::NT * G::ATile));
+                tma_2d(a_tile(st, 0), &tmA, kt * kBK, m0, &full_a[s]);
+                if (SPLIT == 3) tma_2d(a_tile(st, 1), &tmA, kt * kBK, M + m0, &full_a[s]);
+                mbar_arrive_expect_tx(&full_raw[s], (uint32_t)G::RawTile);
+                tma_2d(raw_tile(st), &tmB, kt * kBK, nb0, &full_raw[s]);
             }
             // every issued copy lands before the CTA can exit (already true unless a wait failed)
             for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; kt++) {
@@ -179,70 +207,91 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                 ok = bar_wait(&full_a[s], pu, err) && bar_wait(&conv_done[s], pu, err);
                 if (!ok) break;
                 tc_fence_after();
-                uint8_t* st = smem + s * kStage2;
-                const uint32_t a0 = smem_u32(st), b0 = smem_u32(st + kATile);
+                uint8_t* st = smem + s * G::Stage;
+                const uint32_t ah = smem_u32(a_tile(st, 0)), bh = smem_u32(b_tile(st, 0));
 #pragma unroll
-                for (int ks = 0; ks < kBK / 16; ks++)
-                    umma_f16(tmem, umma_desc(a0 + 32u * ks), umma_desc(b0 + 32u * ks), (kt | ks) != 0 ? 1u : 0u);
+                for (int ks = 0; ks < kBK / 16; ks++) {
+                    const uint32_t acc = (kt | ks) != 0 ? 1u : 0u;
+                    umma_f16(tmem, umma_desc(ah + 32u * ks), umma_desc(bh + 32u * ks), G::Idesc, acc);
+                    if (SPLIT == 3) {
+                        const uint32_t al = smem_u32(a_tile(st, 1)), bl = smem_u32(b_tile(st, 1));
+                        umma_f16(tmem + BN, umma_desc(ah + 32u * ks), umma_desc(bl + 32u * ks), G::Idesc, acc);
+                        umma_f16(tmem + BN, umma_desc(al + 32u * ks), umma_desc(bh + 32u * ks), G::Idesc, 1u);
+                    }
+                }
                 umma_commit(&mma_done[s]);
             }
             umma_commit(&done_bar);  // covers every MMA issued
         }
     } else {
-        // converters: thread t dequantises B row t of each stage
-        const int n = n0 + t;                 // column of the output
-        const size_t drow = (size_t)(nb0 + t);  // row of W
-        uint32_t dnext = 0u;  // the two block scales of the next k-step, as a half2
-        auto load_d = [&](int kt) -> uint32_t {
+        // converters: RowThreads threads per B row, each 64 / RowThreads weights of it
+        constexpr int RT = G::RowThreads, WPT = kBK / RT;  // weights per thread: 64 or 32
+        const int brow = t / RT, part = t % RT;
+        const int n = n0 + brow;                 // column of the output
+        const size_t drow = (size_t)(nb0 + brow);  // row of W
+        auto load_d = [&](int kt) -> uint32_t {  // block scales of this thread's weights, as a half2
             __half2 v = __float2half2_rn(0.f);
-            const int kb = 2 * kt;
+            const int kb = 2 * kt + (RT == 2 ? part : 0);
             if (n < N && kb < KB) {
                 const __half* dp = d + drow * KB + kb;
-                v = __halves2half2(dp[0], kb + 1 < KB ? dp[1] : __float2half(0.f));
+                v = RT == 2 ? __halves2half2(dp[0], dp[0]) : __halves2half2(dp[0], kb + 1 < KB ? dp[1] : __float2half(0.f));
             }
-            return *reinterpret_cast<uint32_t*>(&v);
+            return h2bits(v);
         };
-        dnext = load_d(0);
+        uint32_t dnext = load_d(0);
         for (int kt = 0; kt < nk && ok; kt++) {
             const int s = kt % kStages;
             const uint32_t pu = (uint32_t)((kt / kStages) & 1);
             const uint32_t dcur = dnext;
             if (kt + 1 < nk) dnext = load_d(kt + 1);
-            uint8_t* st = smem + s * kStage2;
+            uint8_t* st = smem + s * G::Stage;
             ok = __all_sync(0xffffffffu, bar_wait(&full_raw[s], pu, err));  // warp-uniform outcome
-            uint4 raw[4];
+            uint4 raw[WPT / 16];
             if (ok) {
-                const uint4* rp = reinterpret_cast<const uint4*>(st + kATile + kBTile + t * kBK);
+                const uint4* rp = reinterpret_cast<const uint4*>(raw_tile(st) + brow * kBK + part * WPT);
 #pragma unroll
-                for (int j = 0; j < 4; j++) raw[j] = rp[j];
+                for (int j = 0; j < WPT / 16; j++) raw[j] = rp[j];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_free[s]);
             if (ok && kt >= kStages)
                 ok = __all_sync(0xffffffffu, bar_wait(&mma_done[s], (uint32_t)((kt / kStages - 1) & 1), err));
             if (!ok) break;
-            __half2 dd[2];
-            {
-                const __half2 dc = *reinterpret_cast<const __half2*>(&dcur);
-                dd[0] = __low2half2(dc);
-                dd[1] = __high2half2(dc);
-            }
-            uint8_t* sb = st + kATile;
+            const __half2 dc = *reinterpret_cast<const __half2*>(&dcur);
+            const int c0 = part * (WPT / 8);  // first 8-weight chunk of this thread in the row
 #pragma unroll
-            for (int c = 0; c < 8; c++) {  // chunk c = weights 8c..8c+7 of the 64
+            for (int c = 0; c < WPT / 8; c++) {
                 const uint4 r4 = raw[c >> 1];
                 const uint32_t w0 = (c & 1) ? r4.z : r4.x, w1 = (c & 1) ? r4.w : r4.y;
-                const __half2 d2 = dd[c >> 2];
-                uint4 o;
-                dq4(w0, d2, o.x, o.y);
-                dq4(w1, d2, o.z, o.w);
-                *reinterpret_cast<uint4*>(sb + sw128(t, c)) = o;
+                if (SPLIT == 1) {
+                    const __half2 d2 = (c >> 2) ? __high2half2(dc) : __low2half2(dc);
+                    uint4 o;
+                    dq4(w0, d2, o.x, o.y);
+                    dq4(w1, d2, o.z, o.w);
+                    *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = o;
+                } else {
+                    const float df = __low2float(dc);
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const uint32_t word = j < 2 ? w0 : w1;
+                        const int sh = 16 * (j & 1);
+                        const float wa = (float)(int8_t)((word >> sh) & 0xff) * df;        // exact
+                        const float wb = (float)(int8_t)((word >> (sh + 8)) & 0xff) * df;
+                        const __half2 h = __floats2half2_rn(wa, wb);
+                        const float2 hf = __half22float2(h);
+                        hw[j] = h2bits(h);
+                        lw[j] = h2bits(__floats2half2_rn((wa - hf.x) * 2048.f, (wb - hf.y) * 2048.f));  // exact
+                    }
+                    *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(b_tile(st, 1) + sw128(brow, c0 + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&conv_done[s]);
         }
-        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. (rows), columns 128 (w / 4) ..
+        // epilogue: warp w reads TMEM lanes 32 (w % 4) .. (rows), columns BN/2 (w / 4) ..
         if (ok) ok = bar_wait(&done_bar, 0u, err);
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
@@ -251,29 +300,27 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
             const int row = q * 32 + lane, m = m0 + row;
             const bool live = row < m_rows;
 #pragma unroll 1
-            for (int c0 = half * (kBN / 2); c0 < (half + 1) * (kBN / 2); c0 += 16) {
-                uint32_t v[16];
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-                    "[%16];"
-                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                      "=r"(v[15])
-                    : "r"(taddr));
+            for (int cc = half * (BN / 2); cc < (half + 1) * (BN / 2); cc += 16) {
+                uint32_t v[16], v2[16];
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc;
+                tmem_ld16(taddr, v);
+                if (SPLIT == 3) tmem_ld16(taddr + BN, v2);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float f[16];
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    f[j] = SPLIT == 3 ? fmaf(__uint_as_float(v2[j]), 1.0f / 2048.0f, __uint_as_float(v[j]))
+                                      : __uint_as_float(v[j]);
                 if (live) {
-                    float* crow = C + (size_t)m * ldc + n0 + c0;
-                    if (n0 + c0 + 16 <= N && (ldc & 3) == 0) {
+                    float* crow = C + (size_t)m * ldc + n0 + cc;
+                    if (n0 + cc + 16 <= N && (ldc & 3) == 0) {
 #pragma unroll
                         for (int j = 0; j < 16; j += 4)
-                            *reinterpret_cast<float4*>(crow + j) =
-                                make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                            __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                            *reinterpret_cast<float4*>(crow + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 16; j++)
-                            if (n0 + c0 + j < N) crow[j] = __uint_as_float(v[j]);
+                            if (n0 + cc + j < N) crow[j] = f[j];
                     }
                 }
             }
@@ -283,6 +330,17 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
     __syncthreads();
     if (warp == kConvWarps + 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// x -> (xh, xl) with xh = fp16(x), xl = fp16((x - xh) * 2048), rows of xl after those of xh
+__global__ void k_f32_to_f16_split(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 2; i += (size_t)gridDim.x * blockDim.x) {
+        const float2 v = reinterpret_cast<const float2*>(x)[i];
+        const __half2 h = __floats2half2_rn(v.x, v.y);
+        const float2 hf = __half22float2(h);
+        reinterpret_cast<__half2*>(y)[i] = h;
+        reinterpret_cast<__half2*>(y + n)[i] = __floats2half2_rn((v.x - hf.x) * 2048.f, (v.y - hf.y) * 2048.f);
+    }
 }
 
 __global__ void k_f32_to_f16(const float* __restrict__ x, __half* __restrict__ y, size_t n) {
@@ -296,7 +354,16 @@ __global__ void k_f32_to_f16(const float* __restrict__ x, __half* __restrict__ y
 
 bool gemm_q8_supported(const DTensor& W) { return W.K % 32 == 0 && W.K >= 32 && W.K % 8 == 0; }
 
-size_t gemm_q8_scratch_bytes(int64_t M, int64_t K) { return (size_t)M * K * sizeof(__half); }
+bool gemm_exact() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QQ3_GEMM_FAST");
+        v = (e && atoi(e) != 0) ? 0 : 1;
+    }
+    return v == 1;
+}
+
+size_t gemm_q8_scratch_bytes(int64_t M, int64_t K) { return (size_t)M * K * sizeof(__half) * (gemm_exact() ? 2 : 1); }
 
 namespace {
 
@@ -328,34 +395,46 @@ CUtensorMap tensor_map(void* base, CUtensorMapDataType type, int elem_bytes, uin
 
 }  // namespace
 
-void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16, int M, float* y, int ldc,
-                        const GemmGroups* groups, cudaStream_t s) {
-    const int64_t K = W.K, N = group_rows;
-    QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
-    QQ_CHECK(N >= 1 && W.rows % N == 0 && N <= (int64_t)65535 * kBN && M <= 65535 * kBM, QQ_ERR_INVALID,
-             "tensor-core Q8_0 matmul: bad shape");
-    if (M <= 0) return;
-    // TMA: the fp16 activations arrive already 128-byte swizzled; the int8 weights plain
+template <int SPLIT>
+void launch_split(const DTensor& W, int64_t N, const __half* a16, int M, float* y, int ldc, const GemmGroups* groups,
+                  cudaStream_t s) {
+    using G = Cfg<SPLIT>;
+    const int64_t K = W.K;
+    // TMA: the fp16 activations arrive already 128-byte swizzled (hi rows, then lo rows when
+    // split); the int8 weights plain
     const CUtensorMap ta = tensor_map(const_cast<__half*>(a16), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
-                                      (uint64_t)M, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
-    const CUtensorMap tb = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, kBK, kBN,
-                                      CU_TENSOR_MAP_SWIZZLE_NONE);
+                                      (uint64_t)M * (SPLIT == 3 ? 2 : 1), kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMap tb = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, kBK,
+                                      G::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
     static bool init = false;
     if (!init) {
-        QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem2));
+        QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_tma<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::Smem));
         init = true;
     }
+    QQ_CHECK(N <= (int64_t)65535 * G::BN, QQ_ERR_INVALID, "tensor-core Q8_0 matmul: too many columns");
     const unsigned gx = groups ? (unsigned)groups->max_tiles : (unsigned)((M + kBM - 1) / kBM);
-    dim3 grid(gx, (unsigned)((N + kBN - 1) / kBN));
-    k_gemm_q8_tma<<<grid, kThreadsG2, kGemmSmem2, s>>>(ta, tb, M, (int)K, W.d, (int)N, y, ldc,
-                                                       groups ? groups->tiles : nullptr,
-                                                       groups ? groups->n_tiles : nullptr, kernel_err_ptr());
+    dim3 grid(gx, (unsigned)((N + G::BN - 1) / G::BN));
+    k_gemm_q8_tma<SPLIT><<<grid, kThreadsG2, G::Smem, s>>>(ta, tb, M, (int)K, W.d, (int)N, y, ldc,
+                                                           groups ? groups->tiles : nullptr,
+                                                           groups ? groups->n_tiles : nullptr, kernel_err_ptr());
     QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16, int M, float* y, int ldc,
+                        const GemmGroups* groups, cudaStream_t s) {
+    const int64_t N = group_rows;
+    QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
+    QQ_CHECK(N >= 1 && W.rows % N == 0 && M <= 65535 * kBM, QQ_ERR_INVALID, "tensor-core Q8_0 matmul: bad shape");
+    if (M <= 0) return;
+    if (gemm_exact()) launch_split<3>(W, N, a16, M, y, ldc, groups, s);
+    else launch_split<1>(W, N, a16, M, y, ldc, groups, s);
 }
 
 void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
     if (n == 0) return;
-    k_f32_to_f16<<<(unsigned)std::min<size_t>((n / 2 + 255) / 256, 148 * 16), 256, 0, s>>>(x, y, n);
+    const unsigned g = (unsigned)std::min<size_t>((n / 2 + 255) / 256, 148 * 16);
+    if (gemm_exact()) k_f32_to_f16_split<<<g, 256, 0, s>>>(x, y, n);
+    else k_f32_to_f16<<<g, 256, 0, s>>>(x, y, n);
     QQ_CUDA_TRY(cudaGetLastError());
 }
 

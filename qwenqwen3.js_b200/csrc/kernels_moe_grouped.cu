@@ -50,33 +50,43 @@ __global__ void __launch_bounds__(kPlanThreads)
     }
 }
 
+// GEMM operand of value v at index i: fp16(v), and when split (the exact GEMM) the scaled
+// residual fp16((v - fp16(v)) * 2048) at index n + i
+__device__ __forceinline__ void put_operand(__half* out, size_t i, size_t n, float v, bool split) {
+    const __half h = __float2half_rn(v);
+    out[i] = h;
+    if (split) out[n + i] = __float2half_rn((v - __half2float(h)) * 2048.f);
+}
+
 __global__ void k_gather_rows_f16(const float* __restrict__ x, int K, const int* __restrict__ row_token, int P,
-                                  __half* __restrict__ out) {
-    const int k2 = K / 2;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)P * k2;
-         i += (size_t)gridDim.x * blockDim.x) {
-        const int p = (int)(i / k2), j = (int)(i % k2);
-        const float2 v = reinterpret_cast<const float2*>(x + (size_t)row_token[p] * K)[j];
-        reinterpret_cast<__half2*>(out + (size_t)p * K)[j] = __floats2half2_rn(v.x, v.y);
+                                  bool split, __half* __restrict__ out) {
+    const size_t n = (size_t)P * K;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i / K), j = (int)(i % K);
+        put_operand(out, i, n, x[(size_t)row_token[p] * K + j], split);
     }
 }
 
-__global__ void k_swiglu_f16(const float* __restrict__ g, const float* __restrict__ u, size_t n,
+__global__ void k_swiglu_f16(const float* __restrict__ g, const float* __restrict__ u, size_t n, bool split,
                              __half* __restrict__ h) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float a = g[i];
-        h[i] = __float2half_rn(a * (1.0f / (1.0f + expf(-a))) * u[i]);  // tensor.js:168-180
+        put_operand(h, i, n, a * (1.0f / (1.0f + expf(-a))) * u[i], split);  // tensor.js:168-180
     }
 }
 
 __global__ void k_moe_combine(const float* __restrict__ down, const int* __restrict__ pos, const float* __restrict__ w,
-                              int T, int top_k, int K, float* __restrict__ out) {
+                              const int* __restrict__ idx, const uint32_t* __restrict__ mask, int T, int top_k, int K,
+                              float* __restrict__ out) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * K;
          i += (size_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / K), c = (int)(i % K);
         float acc = 0.f;
-        for (int s = 0; s < top_k; s++)  // slot order (lfm2-engine.js:459-486)
+        for (int s = 0; s < top_k; s++) {  // slot order; a masked expert is skipped (lfm2-engine.js:459-486)
+            const int e = idx[t * top_k + s];
+            if (mask && ((mask[e >> 5] >> (e & 31)) & 1u)) continue;
             acc += w[t * top_k + s] * down[(size_t)pos[t * top_k + s] * K + c];
+        }
         out[i] = acc;
     }
 }
@@ -89,12 +99,14 @@ size_t moe_grouped_scratch_bytes(int T, int top_k, int n_expert, int64_t K, int6
     const size_t P = (size_t)T * top_k;
     const size_t tiles = (P + 127) / 128 + n_expert;
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-    return al(P * 4) * 2 + al(tiles * 16) + al(4) + al(P * K * 2) + al(P * F * 4) * 2 + al(P * F * 2) +
+    const size_t sp = gemm_exact() ? 2 : 1;  // hi (and lo) fp16 operands
+    return al(P * 4) * 2 + al(tiles * 16) + al(4) + al(P * K * 2 * sp) + al(P * F * 4) * 2 + al(P * F * 2 * sp) +
            al(P * K * 4);
 }
 
 void launch_moe_grouped(const DTensor& gate, const DTensor& up, const DTensor& down, const int* idx, const float* w,
-                        const float* x, int T, int top_k, int n_expert, void* scratch, float* out, cudaStream_t s) {
+                        const uint32_t* mask, const float* x, int T, int top_k, int n_expert, void* scratch, float* out,
+                        cudaStream_t s) {
     const int64_t K = gate.K, F = gate.rows / n_expert;
     QQ_CHECK(n_expert <= kMaxExperts && K % 32 == 0 && F % 32 == 0, -4, "grouped MoE: unsupported shape");
     const int P = T * top_k;
@@ -109,27 +121,29 @@ void launch_moe_grouped(const DTensor& gate, const DTensor& up, const DTensor& d
     b += al((size_t)max_tiles * 16);
     int* n_tiles = reinterpret_cast<int*>(b);
     b += al(4);
+    const bool split = gemm_exact();
+    const size_t sp = split ? 2 : 1;
     __half* xg = reinterpret_cast<__half*>(b);
-    b += al((size_t)P * K * 2);
+    b += al((size_t)P * K * 2 * sp);
     float* g = reinterpret_cast<float*>(b);
     b += al((size_t)P * F * 4);
     float* u = reinterpret_cast<float*>(b);
     b += al((size_t)P * F * 4);
     __half* h = reinterpret_cast<__half*>(b);
-    b += al((size_t)P * F * 2);
+    b += al((size_t)P * F * 2 * sp);
     float* dn = reinterpret_cast<float*>(b);
 
     k_moe_plan<<<1, kPlanThreads, 0, s>>>(idx, P, top_k, n_expert, pos, row_token, tiles, n_tiles);
     QQ_CUDA_TRY(cudaGetLastError());
-    k_gather_rows_f16<<<grid_for((size_t)P * K / 2), 256, 0, s>>>(x, (int)K, row_token, P, xg);
+    k_gather_rows_f16<<<grid_for((size_t)P * K), 256, 0, s>>>(x, (int)K, row_token, P, split, xg);
     QQ_CUDA_TRY(cudaGetLastError());
     const GemmGroups grp{tiles, n_tiles, max_tiles};
     launch_gemm_q8_f16(gate, F, xg, P, g, (int)F, &grp, s);
     launch_gemm_q8_f16(up, F, xg, P, u, (int)F, &grp, s);
-    k_swiglu_f16<<<grid_for((size_t)P * F), 256, 0, s>>>(g, u, (size_t)P * F, h);
+    k_swiglu_f16<<<grid_for((size_t)P * F), 256, 0, s>>>(g, u, (size_t)P * F, split, h);
     QQ_CUDA_TRY(cudaGetLastError());
     launch_gemm_q8_f16(down, K, h, P, dn, (int)K, &grp, s);
-    k_moe_combine<<<grid_for((size_t)T * K), 256, 0, s>>>(dn, pos, w, T, top_k, (int)K, out);
+    k_moe_combine<<<grid_for((size_t)T * K), 256, 0, s>>>(dn, pos, w, idx, mask, T, top_k, (int)K, out);
     QQ_CUDA_TRY(cudaGetLastError());
 }
 

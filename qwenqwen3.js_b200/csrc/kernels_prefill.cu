@@ -1,0 +1,202 @@
+// kernels_prefill.cu -- batched prefill: T prompt tokens through a layer at once (sm_100a).
+//
+// The reference prefills one token at a time (`forward(t_i, i, true)`, qwen3-engine.js:397-457,
+// lfm2-engine.js:523-583); a T-token call is semantically the same as T sequential calls.  Here
+// the projections of all T tokens run as tensor-core GEMMs (kernels_gemm.cu) and the few
+// sequential pieces are kernels over the T rows:
+//   k_embed_rows      embedding rows of T tokens (tensor.js:56-77)
+//   k_rope_rows       split-half RoPE of T x heads rows at positions pos0.. (tensor.js:132-147)
+//   k_kv_append       K/V of T tokens into the cache at pos0.. (kv-cache.js:16-32)
+//   k_conv_prefill    short-conv over the T tokens, carrying the 2-tap state (lfm2-engine.js:282-325)
+//   k_attn_prefill    causal GQA attention of each token over positions 0..pos0+t
+//                     (qwen3-engine.js:249-301, lfm2-engine.js:329-390)
+//   k_add_rows / k_swiglu_rows   residual add and SwiGLU (tensor.js:168-185)
+#include "kernels.h"
+
+namespace qq3 {
+
+namespace {
+
+unsigned grid_n(size_t n) { return (unsigned)std::min<size_t>((n + 255) / 256, (size_t)148 * 64); }
+
+__global__ void k_embed_rows(const int8_t* __restrict__ qs, const __half* __restrict__ d, int K, const int* tok,
+                             int T, int n_vocab, float* __restrict__ out) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * K; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / K), k = (int)(i % K);
+        int v = tok[t];
+        v = v < 0 || v >= n_vocab ? 0 : v;
+        out[i] = (float)qs[(size_t)v * K + k] * __half2float(d[(size_t)v * (K >> 5) + (k >> 5)]);
+    }
+}
+
+// x: [T][n_heads][hd], already RMS-normalised per head; rotate halves at position pos0 + t
+__global__ void k_rope_rows(float* __restrict__ x, int T, int n_heads, int hd, const float* __restrict__ cs, int pos0) {
+    const int half = hd / 2;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * n_heads * half;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i % half);
+        const size_t row = i / half;
+        const int t = (int)(row / n_heads);
+        float* v = x + row * hd;
+        const float c = cs[(size_t)(pos0 + t) * hd + 2 * j], s = cs[(size_t)(pos0 + t) * hd + 2 * j + 1];
+        const float x0 = v[j], x1 = v[j + half];
+        v[j] = x0 * c - x1 * s;
+        v[j + half] = x0 * s + x1 * c;
+    }
+}
+
+// cache layout [n_kv][max_ctx][hd]; k, v: [T][n_kv][hd]
+__global__ void k_kv_append(const float* __restrict__ k, const float* __restrict__ v, int T, int n_kv, int hd,
+                            int max_ctx, int pos0, float* __restrict__ kc, float* __restrict__ vc) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * n_kv * hd;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int dd = (int)(i % hd);
+        const int h = (int)((i / hd) % n_kv);
+        const int t = (int)(i / ((size_t)hd * n_kv));
+        const size_t dst = ((size_t)h * max_ctx + pos0 + t) * hd + dd;
+        kc[dst] = k[i];
+        vc[dst] = v[i];
+    }
+}
+
+// bcx: [T][3E] = (B | C | x) rows of in_proj; conv taps w[E][3]; state[2][E] = (s0, s1)
+__global__ void k_conv_prefill(const float* __restrict__ bcx, const float* __restrict__ w, float* __restrict__ state,
+                               int T, int E, float* __restrict__ y) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= E) return;
+    float s0 = state[c], s1 = state[E + c];
+    const float k0 = w[c * 3], k1 = w[c * 3 + 1], k2 = w[c * 3 + 2];
+    for (int t = 0; t < T; t++) {
+        const float* r = bcx + (size_t)t * 3 * E;
+        const float bx = r[c] * r[2 * E + c];
+        const float co = k0 * s0 + k1 * s1 + k2 * bx;
+        y[(size_t)t * E + c] = r[E + c] * co;
+        s0 = s1;
+        s1 = bx;
+    }
+    state[c] = s0;
+    state[E + c] = s1;
+}
+
+__global__ void k_add_rows(float* __restrict__ x, const float* __restrict__ d, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] += d[i];
+}
+
+__global__ void k_swiglu_rows(const float* __restrict__ g, const float* __restrict__ u, size_t n, float* __restrict__ h) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float a = g[i];
+        h[i] = a * (1.0f / (1.0f + expf(-a))) * u[i];
+    }
+}
+
+// One CTA per (token t, kv head): warp g scores query head kvh*G + g against positions
+// 0..pos0+t in tiles of 32 (one position per lane), online softmax, V accumulation (lane owns
+// HD/32 dims).  q: [T][n_head][HD] (normalised, rotated); out: [T][n_head][HD].
+template <int HD>
+__global__ void k_attn_prefill(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                               int pos0, int n_head, int n_kv, int max_ctx, float* __restrict__ out) {
+    constexpr int PL = HD / 32;
+    const int t = blockIdx.x, kvh = blockIdx.y;
+    const int G = n_head / n_kv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp >= G) return;
+    const int h = kvh * G + warp;
+    const int len = pos0 + t + 1;
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    const float* qh = q + ((size_t)t * n_head + h) * HD;
+    float qv[HD];
+#pragma unroll
+    for (int j = 0; j < HD; j += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(qh + j);
+        qv[j] = v4.x;
+        qv[j + 1] = v4.y;
+        qv[j + 2] = v4.z;
+        qv[j + 3] = v4.w;
+    }
+    const float* kb = kc + (size_t)kvh * max_ctx * HD;
+    const float* vb = vc + (size_t)kvh * max_ctx * HD;
+    float m = -INFINITY, l = 0.f, acc[PL];
+#pragma unroll
+    for (int j = 0; j < PL; j++) acc[j] = 0.f;
+    for (int p0 = 0; p0 < len; p0 += 32) {
+        const int p = p0 + lane;
+        float s = -INFINITY;
+        if (p < len) {
+            const float* kr = kb + (size_t)p * HD;
+            float dot = 0.f;
+#pragma unroll
+            for (int j = 0; j < HD; j += 4) {
+                const float4 k4 = __ldg(reinterpret_cast<const float4*>(kr + j));
+                dot = fmaf(qv[j], k4.x, dot);
+                dot = fmaf(qv[j + 1], k4.y, dot);
+                dot = fmaf(qv[j + 2], k4.z, dot);
+                dot = fmaf(qv[j + 3], k4.w, dot);
+            }
+            s = dot * scale;
+        }
+        const float m_new = fmaxf(m, warp_max(s));
+        const float pl = p < len ? expf(s - m_new) : 0.f;
+        const float cf = expf(m - m_new);
+        l = l * cf + warp_sum(pl);
+#pragma unroll
+        for (int j = 0; j < PL; j++) acc[j] *= cf;
+        const int n = min(32, len - p0);
+        for (int jj = 0; jj < n; jj++) {
+            const float pj = __shfl_sync(0xffffffffu, pl, jj);
+            const float* vr = vb + (size_t)(p0 + jj) * HD + lane * PL;
+#pragma unroll
+            for (int j = 0; j < PL; j++) acc[j] = fmaf(pj, __ldg(vr + j), acc[j]);
+        }
+        m = m_new;
+    }
+    float* o = out + ((size_t)t * n_head + h) * HD + lane * PL;
+#pragma unroll
+    for (int j = 0; j < PL; j++) o[j] = acc[j] / l;
+}
+
+}  // namespace
+
+void launch_embed_rows(const DTensor& E, const int* tok, int T, int n_vocab, float* out, cudaStream_t s) {
+    k_embed_rows<<<grid_n((size_t)T * E.K), 256, 0, s>>>(E.qs, E.d, (int)E.K, tok, T, n_vocab, out);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_rope_rows(float* x, int T, int n_heads, int hd, const float* cs, int pos0, cudaStream_t s) {
+    k_rope_rows<<<grid_n((size_t)T * n_heads * hd / 2), 256, 0, s>>>(x, T, n_heads, hd, cs, pos0);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_kv_append(const float* k, const float* v, int T, int n_kv, int hd, int max_ctx, int pos0, float* kc,
+                      float* vc, cudaStream_t s) {
+    k_kv_append<<<grid_n((size_t)T * n_kv * hd), 256, 0, s>>>(k, v, T, n_kv, hd, max_ctx, pos0, kc, vc);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_conv_prefill(const float* bcx, const float* w, float* state, int T, int E, float* y, cudaStream_t s) {
+    k_conv_prefill<<<(E + 127) / 128, 128, 0, s>>>(bcx, w, state, T, E, y);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_add_rows(float* x, const float* d, size_t n, cudaStream_t s) {
+    k_add_rows<<<grid_n(n), 256, 0, s>>>(x, d, n);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_swiglu_rows(const float* g, const float* u, size_t n, float* h, cudaStream_t s) {
+    k_swiglu_rows<<<grid_n(n), 256, 0, s>>>(g, u, n, h);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T, int pos0, int n_head, int n_kv,
+                         int hd, int max_ctx, float* out, cudaStream_t s) {
+    const int G = n_head / n_kv;
+    QQ_CHECK(G >= 1 && G <= 32 && n_head % n_kv == 0, -4, "prefill attention: unsupported head grouping");
+    dim3 grid((unsigned)T, (unsigned)n_kv);
+    if (hd == 64) k_attn_prefill<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, pos0, n_head, n_kv, max_ctx, out);
+    else if (hd == 128) k_attn_prefill<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, pos0, n_head, n_kv, max_ctx, out);
+    else QQ_CHECK(false, -4, "prefill attention: head_dim must be 64 or 128");
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+}  // namespace qq3

@@ -199,3 +199,42 @@ def test_default_decode_step_is_one_kernel(qq3):
     eng = qq3.engine_for(g, device=0, max_ctx=32)
     assert eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS) == 1
     eng.close()
+
+
+def _min_router_gap(g, spec, ref_recs):
+    """Smallest 4th-vs-5th selection-score gap over the oracle's routing records."""
+    gap = np.inf
+    for rec in ref_recs:
+        for m, layer in enumerate([i for i in range(spec.n_layers) if spec.is_moe(i)]):
+            bias = g.getTensorMetaByName(f"blk.{layer}.exp_probs_b.bias").raw().view(np.float32)
+            sel = np.sort((rec[m][8:] + bias).astype(np.float32))[::-1]
+            gap = min(gap, float(sel[3] - sel[4]))
+    return gap
+
+
+@pytest.mark.parametrize("arch", ["lfm2", "qwen3"])
+def test_batched_prefill_vs_oracle(qq3, orc, arch):
+    """A 72-token prompt takes the batched prefill (tensor-core projections, grouped MoE, causal
+    attention over the rows); the next token's logits match the oracle's sequential forward.
+    A router near-tie (gap < 1e-5) may resolve differently there, which the bar exempts."""
+    if arch == "lfm2":
+        spec = qq3.synth.lfm2_8b_a1b(seed=91)
+        spec.n_layers = 4
+        spec.attn_layers = (2,)
+    else:
+        spec = qq3.synth.qwen3_0p6b(seed=92)
+        spec.n_layers = 3
+    g, eng, ref = _pair(qq3, orc, spec, max_ctx=96)
+    toks = qq3.synth.uniform_tokens(73, 8, spec.n_vocab)
+    eng.prefill(toks[:-1].tolist())
+    got = eng.forward(int(toks[-1]), 72, False)
+    recs = []
+    for p, t in enumerate(toks[:-1]):
+        _, _, rec = ref.forward(int(t), p, True, dump=True, routing=True)
+        recs.append(rec)
+    want = ref.forward(int(toks[-1]), 72, False)
+    if arch == "lfm2" and _min_router_gap(g, spec, recs) < 1e-5:
+        pytest.skip("router near-tie in the prompt: the bar exempts it")
+    assert rel_err(got, want) < TOL
+    assert int(np.argmax(got)) == int(np.argmax(want))
+    eng.close()

@@ -13,8 +13,8 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-2      # north-star bar for activations / logits
 TIGHT = 2e-5    # f32 accumulation vs the oracle's f64 on a single matmul
-TC = 2e-3       # M >= 2 rows run on the tensor cores with fp16 operands (w = q*d and x rounded
-                # to 11-bit significands, f32 accumulation): ~2e-4 expected, well under TOL
+TC = 1e-4       # M >= 2 rows run on the tensor cores: x and w = q*d split into fp16 hi/lo pairs,
+                # three products accumulated in f32 (~2^-22 per product, like the f32 GEMV)
 
 SWEEP = [(1024, 1024), (3072, 1024), (1024, 3072), (151936, 1024), (7168, 2048)]
 
