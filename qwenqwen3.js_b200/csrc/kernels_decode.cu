@@ -34,6 +34,19 @@ constexpr int kStageTarget = 64 * 1024; // stage size the item count per stage a
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
+// Loads issued where they stand: a volatile asm keeps the compiler from sinking a prefetch of
+// data that does not depend on this step below a spin wait on data that does.
+__device__ __forceinline__ float4 ld_early_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ld_early_f32(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ uint32_t step_tag(uint32_t epoch, int ph) { return epoch * 256u + (uint32_t)ph + 1u; }
 
 __device__ __forceinline__ void st_tw(tword* p, float v, uint32_t tag) {
@@ -311,6 +324,18 @@ __device__ void dec_stage_digits(const tword* __restrict__ x, uint32_t tag, cons
     const int t = threadIdx.x;
     float xv[4][8];
     double ss = 0.0;
+    // the norm weights do not depend on the input: request them before waiting for it (they are
+    // read once per step, so they usually come from DRAM)
+    float4 nw[4][2];
+#pragma unroll
+    for (int ps = 0; ps < 4; ps++) {
+        const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+        nw[ps][0] = nw[ps][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (norm_w && e0 < K) {
+            nw[ps][0] = ld_early_f4(norm_w + e0);
+            nw[ps][1] = ld_early_f4(norm_w + e0 + 4);
+        }
+    }
 #pragma unroll
     for (int ps = 0; ps < 4; ps++) {
         const int e0 = 8 * t + ps * 8 * kConsumerThreads;
@@ -338,8 +363,7 @@ __device__ void dec_stage_digits(const tword* __restrict__ x, uint32_t tag, cons
         for (int ps = 0; ps < 4; ps++) {
             const int e0 = 8 * t + ps * 8 * kConsumerThreads;
             if (e0 < K) {
-                const float4 wa = reinterpret_cast<const float4*>(norm_w + e0)[0];
-                const float4 wb = reinterpret_cast<const float4*>(norm_w + e0)[1];
+                const float4 wa = nw[ps][0], wb = nw[ps][1];
                 const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
                 for (int e = 0; e < 8; e++) xv[ps][e] = (wv[e] * xv[ps][e]) * inv;
@@ -486,7 +510,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g * (1.0f /
 // lfm2-engine.js:417-447: logits = W_router . norm(h); p = sigmoid(logits); top-k on p + bias
 // (stable: the lower expert id wins a tie); weights = p / (sum + 1e-6).
 __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
-                          int nch, DecRoute* route, int* err) {
+                          int nch, float bias_v, DecRoute* route, int* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.K, ne = p.n_expert;
     const int set = warp / 4, w = warp % 4;
@@ -519,7 +543,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     if (warp == 0) {
         const bool live = lane < ne;
         const float prob = live ? 1.0f / (1.0f + expf(-route->logit[lane])) : 0.f;
-        const float sel = live ? prob + (p.bias ? p.bias[lane] : 0.f) : -INFINITY;
+        const float sel = live ? prob + bias_v : -INFINITY;
         bool taken = !live;
         double sum_w = 1e-6;
         int top_i[4];
@@ -736,7 +760,8 @@ __device__ void dec_norm_rope(float* v, const float* __restrict__ w, float eps, 
 // Tiles of 32 positions are staged in shared memory by all consumer threads (K rows padded so
 // that lane-per-position reads do not conflict); warp g < G then scores query head g with one
 // position per lane, updates its online softmax and accumulates V (lane owns HD/32 dims).
-// Shared layout (floats): q [8][HD] | kv [2][HD] | K tile [32][HD+4] | V tile [32][HD].
+// Shared layout (floats): q [8][HD] | kv [2][HD] | K tile [32][HD+4] | V tile [32][HD] |
+// q norm, k norm, RoPE row [3][HD].
 template <int HD>
 __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_in, tword* out, uint32_t tag_out,
                               float* scratch, int* err) {
@@ -748,6 +773,7 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
     float* kv_s = q_s + 8 * HD;    // [2][HD]
     float* k_t = kv_s + 2 * HD;    // [T][KS]
     float* v_t = k_t + T * KS;     // [T][HD]
+    float* nrm_s = v_t + T * HD;   // [3][HD]: q norm, k norm, RoPE row
     __shared__ int is_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *a.pos;
@@ -764,6 +790,14 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
         float* vc = a.v_cache + (size_t)kvh * a.max_ctx * HD;
         float* part_base = a.part + (size_t)kvh * G * a.n_split * (HD + 2);
         if (p0 < p1) {
+            // norm weights and the RoPE row do not depend on this step's data: request them
+            // before waiting for q/k/v, store them after (HD <= 128 < consumer threads)
+            float qn = 0.f, kn = 0.f, cr = 0.f;
+            if (threadIdx.x < HD) {
+                qn = ld_early_f32(a.q_norm + threadIdx.x);
+                kn = ld_early_f32(a.k_norm + threadIdx.x);
+                cr = ld_early_f32(cs + threadIdx.x);
+            }
             for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads)
                 q_s[i] = wait_tw(qkv + (size_t)kvh * G * HD + i, tag_in, err);
             const bool owns = p0 <= pos && pos < p1;
@@ -772,10 +806,15 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
                     kv_s[d] = wait_tw(qkv + (size_t)a.n_head * HD + (size_t)kvh * HD + d, tag_in, err);
                     kv_s[HD + d] = wait_tw(qkv + (size_t)(a.n_head + a.n_kv) * HD + (size_t)kvh * HD + d, tag_in, err);
                 }
+            if (threadIdx.x < HD) {
+                nrm_s[threadIdx.x] = qn;
+                nrm_s[HD + threadIdx.x] = kn;
+                nrm_s[2 * HD + threadIdx.x] = cr;
+            }
             named_bar(1, kConsumerThreads);
-            for (int g = warp; g < G; g += kCW) dec_norm_rope<HD>(q_s + g * HD, a.q_norm, a.eps, cs);
+            for (int g = warp; g < G; g += kCW) dec_norm_rope<HD>(q_s + g * HD, nrm_s, a.eps, nrm_s + 2 * HD);
             if (owns && warp == kCW - 1) {
-                dec_norm_rope<HD>(kv_s, a.k_norm, a.eps, cs);
+                dec_norm_rope<HD>(kv_s, nrm_s + HD, a.eps, nrm_s + 2 * HD);
                 for (int d = lane; d < HD; d += 32) {
                     kc[(size_t)pos * HD + d] = kv_s[d];
                     vc[(size_t)pos * HD + d] = kv_s[HD + d];
@@ -954,11 +993,28 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             // needs the routing of its own down rows)
             if (!p.r_qs && (int)blockIdx.x >= (p.n_items + p.G - 1) / p.G) continue;
             const int K = p.K, nch = K >> 4;
+            // the short-conv state and taps of this CTA's items are read once per step: pull them
+            // into L2 now, before the input wait (tiny; the epilogue then hits L2)
+            if (p.epi == EK_CONV) {
+                const int G = p.G, n_groups = (p.n_items + G - 1) / G;
+                const int mine = (n_groups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+                for (int j = threadIdx.x; j < mine * G; j += kConsumerThreads) {
+                    const int item = ((int)blockIdx.x + (j / G) * (int)gridDim.x) * G + (j % G);
+                    if (item < p.n_items) {
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.state + item));
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.state + p.E + item));
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_w + 3 * item));
+                    }
+                }
+            }
+            // the router's expert bias is read once per step: request it before the input wait
+            float bias_v = 0.f;
+            if (p.r_qs && warp == 0 && lane < p.n_expert && p.bias) bias_v = ld_early_f32(p.bias + lane);
             uint4* dig = reinterpret_cast<uint4*>(dig_base);
             float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
             dec_stage_digits(p.x, step_tag(epoch, p.x_ph), p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
-            if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, &route, err);
+            if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
             PhaseRegs R;
             load_phase(&p, R, expert_map(p.map) ? &route : nullptr);
             unsigned long long best_k = 0ull;
@@ -1045,7 +1101,7 @@ bool decode_phase_fits(const PhaseDesc& p) {
     if (p.type != PH_GEMV && p.type != PH_DOWN4) {
         if (p.type == PH_ATTN) {
             const int G = p.attn.n_head / p.attn.n_kv, hd = p.attn.hd;
-            const size_t need = ((size_t)8 * hd + 2 * hd + (size_t)32 * (hd + 4) + (size_t)32 * hd) * 4;
+            const size_t need = ((size_t)8 * hd + 2 * hd + (size_t)32 * (hd + 4) + (size_t)32 * hd + 3 * hd) * 4;
             return (hd == 64 || hd == 128) && G >= 1 && G <= kCW && p.attn.n_head % p.attn.n_kv == 0 &&
                    need <= (size_t)(kDecDigitBytes + kDecAttnBytes) && p.attn.n_split <= 32;
         }
