@@ -168,7 +168,7 @@ __device__ __forceinline__ void produce(const Map& map, const Ring& r, int K, in
     for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
         const int slot = i % r.stages;
         const uint32_t use = (uint32_t)(i / r.stages);
-        if (use > 0 && !mbar_wait(&r.empty[slot], (use - 1) & 1u)) {
+        if (use > 0 && !mbar_wait(&r.empty[slot], (use - 1) & 1u, 200)) {
             set_err(err, kErrEmptyWait);
             *abort_flag = 1;
             return;

@@ -30,6 +30,8 @@ constexpr int kDecThreads = kThreads2;  // 8 consumer warps + 1 producer warp
 constexpr int kMaxRoutes = 32;          // experts the fused router handles
 constexpr int kMaxStageK = 8192;        // largest K of a streamed phase (4 staging passes)
 constexpr int kMaxRowsPerWarp = 8;      // rows a consumer warp dots per stage
+constexpr uint32_t kProducerBackoffNs = 200;
+constexpr int kRouteWarp = 1;           // consumer warp that computes the top-k
 constexpr int kStageTarget = 64 * 1024; // stage size the item count per stage aims for
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
@@ -92,18 +94,15 @@ __device__ __forceinline__ void wait_tw8(const tword* p, uint32_t tag, int* err,
     for (int j = 0; j < 8; j++) v[j] = tw_val(w[j]);
 }
 
-__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Bounded wait on a ring / routing mbarrier.  The producer backs off with __nanosleep after a
+// few polls (it shares an SM sub-partition with consumer warps 0 and 4); consumers poll tightly
+// (measured: a consumer backoff cost ~1.3% of the step, the producer's none).
+__device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* err, uint32_t backoff_ns = 0) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t it = 0; it < kSpinLimit; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (ok) return true;
+    for (uint32_t it = 0; it < kWaitPolls; ++it) {
+        if (mbar_try_wait(a, parity)) return true;
         if ((it & 63u) == 63u && ld_volatile(err)) return false;
+        if (backoff_ns && it >= 4) __nanosleep(backoff_ns);
     }
     set_err(err, kErrFullWait);
     return false;
@@ -237,7 +236,7 @@ struct ProdRing {
         const bool wrap = head + need > (uint32_t)kDecRingBytes;
         const uint32_t charge = need + (wrap ? kDecRingBytes - head : 0u);
         while (tail < i && (i - tail >= (uint32_t)kDecSlots || inflight + charge > (uint32_t)kDecRingBytes)) {
-            if (!slot_wait(&r.empty[tail % kDecSlots], (tail / kDecSlots) & 1u, err)) return false;
+            if (!slot_wait(&r.empty[tail % kDecSlots], (tail / kDecSlots) & 1u, err, kProducerBackoffNs)) return false;
             inflight -= r.charge[tail % kDecSlots];
             ++tail;
         }
@@ -276,7 +275,7 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
             }
             // Wait for this CTA's routing.  (Pulling the next layer's rows into L2 meanwhile was
             // measured slower: it competes with the expert rows for DRAM right after routing.)
-            if (!slot_wait(&route->bar, routed & 1u, err)) goto drain;
+            if (!slot_wait(&route->bar, routed & 1u, err, kProducerBackoffNs)) goto drain;
             ++routed;
         }
         {
@@ -540,31 +539,32 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     }
     i += 2;
     named_bar(1, kConsumerThreads);
-    if (warp == 0) {
+    if (warp == kRouteWarp) {  // not warp 0: it shares a sub-partition with the producer warp
         const bool live = lane < ne;
         const float prob = live ? 1.0f / (1.0f + expf(-route->logit[lane])) : 0.f;
         const float sel = live ? prob + bias_v : -INFINITY;
-        bool taken = !live;
+        // rank of this expert in the stable descending order of the selection scores (a higher
+        // score first; the lower id first on a tie): 32 independent comparisons, no dependent
+        // reduction chain.  The top-k are the experts of rank 0..k-1 (lfm2-engine.js:434-442).
+        int rank = 0;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float o = __shfl_sync(0xffffffffu, sel, j);
+            rank += (o > sel || (o == sel && j < lane)) ? 1 : 0;
+        }
         double sum_w = 1e-6;
         int top_i[4];
         float top_p[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            float bv = taken ? -INFINITY : sel;
-            int bi = taken ? 0x7fffffff : lane;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            bi = __shfl_sync(0xffffffffu, bi, 0);
-            if (bi < 0 || bi >= ne) bi = 0;
-            if (lane == bi) taken = true;
+            const unsigned m = __ballot_sync(0xffffffffu, live && rank == k);
+            int bi = m ? __ffs(m) - 1 : 0;
+            if (bi >= ne) bi = 0;
             top_i[k] = bi;
             top_p[k] = __shfl_sync(0xffffffffu, prob, bi & 31);
-            sum_w += (double)top_p[k];
         }
+#pragma unroll
+        for (int k = 0; k < 4; k++) sum_w += (double)top_p[k];  // selection order, as the JS sums
         const double inv = 1.0 / sum_w;
         if (lane < 4) {
             float wk = 0.f;
@@ -1009,7 +1009,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
             // the router's expert bias is read once per step: request it before the input wait
             float bias_v = 0.f;
-            if (p.r_qs && warp == 0 && lane < p.n_expert && p.bias) bias_v = ld_early_f32(p.bias + lane);
+            if (p.r_qs && warp == kRouteWarp && lane < p.n_expert && p.bias) bias_v = ld_early_f32(p.bias + lane);
             uint4* dig = reinterpret_cast<uint4*>(dig_base);
             float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
             dec_stage_digits(p.x, step_tag(epoch, p.x_ph), p.norm_w, p.eps, K, dig, xsc, red, err);

@@ -30,19 +30,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
 }
 
-// Wait for completion of the phase with the given parity; false after kSpinLimit polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+// One poll of an mbarrier phase (returns at once or after a short hardware-chosen wait).
+constexpr uint32_t kWaitPolls = 1u << 22;  // a wait gives up after this many polls (~seconds)
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for completion of the phase with the given parity; false after kWaitPolls polls.  With
+// backoff_ns the waiter sleeps between polls after the first few, leaving issue slots to the
+// warps of its SM sub-partition (used by producer threads, whose waits are not latency-critical).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, uint32_t backoff_ns = 0) {
     const uint32_t a = smem_u32(b);
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (ok) return true;
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (backoff_ns && i >= 4) __nanosleep(backoff_ns);
     }
     return false;
 }
