@@ -187,9 +187,13 @@ int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_ste
 
 /* Statistics of a model (no reference counterpart; used by the benchmark):
  *   QQ_STAT_STEP_KERNELS  kernels launched by one decode step with logits
- *   QQ_STAT_N_MOE         number of MoE layers */
+ *   QQ_STAT_N_MOE         number of MoE layers
+ *   QQ_STAT_STEP_PHASES   phases of the persistent decode step with logits (0: per-phase kernels)
+ *   QQ_STAT_MOE_FUSED     MoE layers the persistent step runs as one fused phase */
 #define QQ_STAT_STEP_KERNELS 0
 #define QQ_STAT_N_MOE 1
+#define QQ_STAT_STEP_PHASES 2
+#define QQ_STAT_MOE_FUSED 3
 int qq_model_stat(qq_model* m, int what, int64_t* value);
 /* Time one kernel class over every MoE layer in turn (so no layer's weights are still in
  * L2 when it is read again), iters rounds, using the routing of the latest token; returns

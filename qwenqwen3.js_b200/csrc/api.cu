@@ -75,6 +75,9 @@ struct Layer {
     bool attn = false, moe = false;
     const DTensor* t[QQ_SLOT_COUNT] = {nullptr};
     int attn_slot = -1, moe_slot = -1;
+    // the expert down tensor transposed for the fused decode MoE (owned; built on first use)
+    int8_t* dt_qs = nullptr;
+    __half* dt_d = nullptr;
 };
 
 struct qq_model {
@@ -121,6 +124,8 @@ struct qq_model {
     void* pf_arena = nullptr;
     qq3::tword* tarena = nullptr;    // tagged activations: one buffer per phase output
     size_t tarena_len = 0;
+    float* aarena = nullptr;         // accumulated vectors + counters, two halves of aarena_half words
+    size_t aarena_half = 0;
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
@@ -140,6 +145,13 @@ void free_model(qq_model* m) {
     if (m->dctl) cudaFree(m->dctl);
     if (m->pf_arena) cudaFree(m->pf_arena);
     if (m->tarena) cudaFree(m->tarena);
+    if (m->aarena) cudaFree(m->aarena);
+    for (Layer& L : m->layers) {
+        if (L.dt_qs) cudaFree(L.dt_qs);
+        if (L.dt_d) cudaFree(L.dt_d);
+        L.dt_qs = nullptr;
+        L.dt_d = nullptr;
+    }
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
                     m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
                     m->mask, m->ctl,
@@ -251,6 +263,23 @@ size_t tarena_bound(const qq_model* m) {
     return (size_t)(3 * d.n_layers + 2) * v;
 }
 
+// Whether the MoE layers run as fused phases (router + experts + down in one phase, outputs
+// accumulated); QQ3_MOE_FUSED=0 selects the two-phase form (gate/up, then down + combine).
+bool moe_fused(const qq_model* m) {
+    const char* env = getenv("QQ3_MOE_FUSED");
+    if (env && atoi(env) == 0) return false;
+    const qq_model_desc& d = m->d;
+    bool any = false;
+    for (const Layer& L : m->layers) {
+        if (!L.moe) continue;
+        any = true;
+        if (!qq3::decode_moe_fits(d.n_embd, (int)L.t[QQ_GATE_EXPS]->ne[1], d.n_embd, d.n_expert, d.n_expert_used) ||
+            (int)L.t[QQ_DOWN_EXPS]->K != (int)L.t[QQ_GATE_EXPS]->ne[1])
+            return false;
+    }
+    return any;
+}
+
 // The decode step as a phase program for the persistent kernel (kernels_decode.cu); the same
 // sequence of operations as enqueue_step.  Each phase writes its own tagged output buffer and
 // names the phase that wrote each vector it reads.
@@ -258,6 +287,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     using namespace qq3;
     const qq_model_desc& d = m->d;
     const int E = d.n_embd, hd = d.head_dim, nq = d.n_head * hd, nkv = d.n_head_kv * hd;
+    const bool fuse = moe_fused(m);
     if (!m->tarena) {
         m->tarena_len = tarena_bound(m);
         m->tarena = dalloc<tword>(m->tarena_len);
@@ -267,6 +297,26 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     if (!m->dctl) {
         m->dctl = dalloc<DecodeCtl>(1);
         QQ_CUDA_TRY(cudaMemsetAsync(m->dctl, 0, sizeof(DecodeCtl), m->ctx->stream));
+    }
+    // fused MoE: one accumulated vector (E floats) + counter (padded to 32 words) per MoE layer
+    const size_t aslot = ((size_t)E + 32 + 31) & ~(size_t)31;
+    if (fuse && !m->aarena) {
+        m->aarena_half = aslot * (size_t)std::max(m->n_moe, 1);
+        m->aarena = dalloc<float>(2 * m->aarena_half);
+        cudaStream_t s = m->ctx->stream;
+        QQ_CUDA_TRY(cudaMemsetAsync(m->aarena, 0, sizeof(float) * 2 * m->aarena_half, s));
+        float* a = m->aarena;
+        long long h = (long long)m->aarena_half;
+        QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->arena, &a, sizeof(a), cudaMemcpyHostToDevice, s));
+        QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->arena_half, &h, sizeof(h), cudaMemcpyHostToDevice, s));
+        for (Layer& L : m->layers) {
+            if (!L.moe || L.dt_qs) continue;
+            const DTensor& W = *L.t[QQ_DOWN_EXPS];
+            L.dt_qs = dalloc<int8_t>((size_t)W.rows * W.K);
+            L.dt_d = dalloc<__half>((size_t)W.rows * (W.K / 32));
+            qq3::launch_transpose_experts(W, d.n_expert, L.dt_qs, L.dt_d, s);
+        }
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // the pointers above are host locals
     }
     size_t cursor = 0;
     auto take = [&](size_t n) {
@@ -282,8 +332,16 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         p.S = 1;
         return p;
     };
-    const tword* hid = nullptr;  // residual stream and the phase that wrote it
-    int hid_ph = -1;
+    // a vector between phases: tagged words and the phase that wrote them, or an accumulated
+    // vector with its counter and the count that completes it
+    struct Ref {
+        const tword* t = nullptr;
+        int ph = -1;
+        const float* a = nullptr;
+        const unsigned* c = nullptr;
+        int n = 0;
+    };
+    Ref hid;  // the residual stream
     {
         PhaseDesc p = blank();
         p.type = PH_EMBED;
@@ -293,11 +351,17 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         p.n_vocab = d.n_vocab;
         p.ctl = m->ctl;
         p.y = take(E);
-        hid = p.y;
-        hid_ph = 0;
+        hid.t = p.y;
+        hid.ph = 0;
         prog.push_back(p);
     }
-    auto gemv = [&](int map, int epi, int S, int K, int n_items, const tword* x, int x_ph, const float* norm_w) {
+    auto tagged = [](const tword* t, int ph) {
+        Ref r;
+        r.t = t;
+        r.ph = ph;
+        return r;
+    };
+    auto gemv = [&](int map, int epi, int S, int K, int n_items, const Ref& in, const float* norm_w) {
         PhaseDesc p = blank();
         p.type = PH_GEMV;
         p.map = map;
@@ -305,23 +369,29 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         p.S = S;
         p.K = K;
         p.n_items = n_items;
-        p.x = x;
-        p.x_ph = x_ph;
+        p.x = in.t;
+        p.x_ph = in.ph;
+        p.xa = in.a;
+        p.xa_cnt = in.c;
+        p.xa_n = in.n;
         p.norm_w = norm_w;
         p.eps = d.rms_eps;
         p.G = qq3::decode_stage_items(S, K, n_items, n_items);
         return p;
     };
     auto resid = [&](PhaseDesc& p) {  // y = hid + acc: a new version of the residual stream
-        p.res = hid;
-        p.res_ph = hid_ph;
+        p.res = hid.t;
+        p.res_ph = hid.ph;
+        p.ra = hid.a;
+        p.ra_cnt = hid.c;
+        p.ra_n = hid.n;
         p.y = take(E);
     };
     auto push_hid = [&](PhaseDesc& p) {
         prog.push_back(p);
-        hid = p.y;
-        hid_ph = (int)prog.size() - 1;
+        hid = tagged(p.y, (int)prog.size() - 1);
     };
+    int n_acc = 0;  // accumulated vectors handed out
     auto set_src = [](PhaseDesc& p, int i, const DTensor* t) {
         p.qs[i] = t->qs;
         p.d[i] = t->d;
@@ -331,7 +401,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         const float* an = L.t[QQ_ATTN_NORM]->f32;
         const float* fn = L.t[QQ_FFN_NORM]->f32;
         if (L.attn) {
-            PhaseDesc q = gemv(MK_CONCAT3, EK_STORE, 1, E, nq + 2 * nkv, hid, hid_ph, an);
+            PhaseDesc q = gemv(MK_CONCAT3, EK_STORE, 1, E, nq + 2 * nkv, hid, an);
             set_src(q, 0, L.t[QQ_WQ]);
             set_src(q, 1, L.t[QQ_WK]);
             set_src(q, 2, L.t[QQ_WV]);
@@ -360,12 +430,12 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             a.attn.n_split = m->n_split;
             a.attn.eps = d.rms_eps;
             prog.push_back(a);
-            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, nq, E, a.a_out, (int)prog.size() - 1, nullptr);
+            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, nq, E, tagged(a.a_out, (int)prog.size() - 1), nullptr);
             set_src(o, 0, L.t[QQ_WO]);
             resid(o);
             push_hid(o);
         } else {
-            PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, hid, hid_ph, an);
+            PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, hid, an);
             set_src(c, 0, L.t[QQ_IN_PROJ]);
             c.stride = E;
             c.conv_w = L.t[QQ_CONV]->f32;
@@ -373,15 +443,47 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             c.E = E;
             c.y = take(E);
             prog.push_back(c);
-            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, E, E, c.y, (int)prog.size() - 1, nullptr);
+            PhaseDesc o = gemv(MK_ROWS, EK_RESID, 1, E, E, tagged(c.y, (int)prog.size() - 1), nullptr);
             set_src(o, 0, L.t[QQ_OUT_PROJ]);
             resid(o);
             push_hid(o);
         }
-        if (L.moe) {
+        if (L.moe && fuse && hid.t) {
             const int k = d.n_expert_used;
             const int F = (int)L.t[QQ_GATE_EXPS]->ne[1];
-            PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_SWIGLU, 2, E, k * F, hid, hid_ph, fn);
+            PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_STORE, 2, E, k * F, hid, fn);
+            g.type = PH_MOE;
+            g.G = kMoeG;
+            set_src(g, 0, L.t[QQ_GATE_EXPS]);
+            set_src(g, 1, L.t[QQ_UP_EXPS]);
+            g.r_qs = L.t[QQ_ROUTER]->qs;
+            g.r_d = L.t[QQ_ROUTER]->d;
+            g.bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+            g.rec = m->rec + (size_t)L.moe_slot * m->rec_len;
+            g.ridx = m->ridx + (size_t)L.moe_slot * k;
+            g.rw = m->rw + (size_t)L.moe_slot * k;
+            g.n_expert = d.n_expert;
+            g.top_k = k;
+            g.mask = m->mask;
+            g.N = F;
+            g.dt_qs = L.dt_qs;
+            g.dt_d = L.dt_d;
+            g.n_out = E;
+            QQ_CHECK((size_t)(n_acc + 1) * aslot <= m->aarena_half, QQ_ERR_INVALID, "persistent program: accumulator arena too small");
+            g.acc = m->aarena + (size_t)n_acc * aslot;
+            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + E);
+            ++n_acc;
+            prog.push_back(g);
+            hid = Ref();
+            hid.a = g.acc;
+            hid.c = g.acc_cnt;
+            hid.n = qq3::num_sms();  // every CTA of the grid counts once
+        } else if (L.moe) {
+            // the down + combine phase reads its residual as tagged words
+            QQ_CHECK(hid.t != nullptr, QQ_ERR_UNSUPPORTED, "persistent program: MoE after an accumulated vector");
+            const int k = d.n_expert_used;
+            const int F = (int)L.t[QQ_GATE_EXPS]->ne[1];
+            PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_SWIGLU, 2, E, k * F, hid, fn);
             g.G = qq3::decode_stage_items(2, E, F, k * F);  // groups must not straddle experts
             set_src(g, 0, L.t[QQ_GATE_EXPS]);
             set_src(g, 1, L.t[QQ_UP_EXPS]);
@@ -414,12 +516,12 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             push_hid(dn);
         } else {
             const int F = (int)L.t[QQ_FFN_GATE]->ne[1];
-            PhaseDesc g = gemv(MK_PAIR, EK_SWIGLU, 2, E, F, hid, hid_ph, fn);
+            PhaseDesc g = gemv(MK_PAIR, EK_SWIGLU, 2, E, F, hid, fn);
             set_src(g, 0, L.t[QQ_FFN_GATE]);
             set_src(g, 1, L.t[QQ_FFN_UP]);
             g.y = take(F);
             prog.push_back(g);
-            PhaseDesc dn = gemv(MK_ROWS, EK_RESID, 1, F, E, g.y, (int)prog.size() - 1, nullptr);
+            PhaseDesc dn = gemv(MK_ROWS, EK_RESID, 1, F, E, tagged(g.y, (int)prog.size() - 1), nullptr);
             set_src(dn, 0, L.t[QQ_FFN_DOWN]);
             resid(dn);
             push_hid(dn);
@@ -427,7 +529,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     }
     if (want_logits) {
         const DTensor* out = m->output ? m->output : m->tok_embd;
-        PhaseDesc h = gemv(MK_ROWS, EK_ARGMAX, 1, E, d.n_vocab, hid, hid_ph, m->out_norm->f32);
+        PhaseDesc h = gemv(MK_ROWS, EK_ARGMAX, 1, E, d.n_vocab, hid, m->out_norm->f32);
         set_src(h, 0, out);
         h.logits = m->logits;
         h.best = &m->dctl->best;
@@ -1202,6 +1304,19 @@ int qq_model_stat(qq_model* m, int what, int64_t* value) {
             *value = m->step_kernels;
         } else if (what == QQ_STAT_N_MOE) {
             *value = m->n_moe;
+        } else if (what == QQ_STAT_STEP_PHASES || what == QQ_STAT_MOE_FUSED) {
+            int64_t n = 0;
+            if (mega_enabled(m)) {
+                const qq_model::Prog& pr = get_prog(m, 0, true);
+                if (what == QQ_STAT_STEP_PHASES) {
+                    n = pr.n;
+                } else {
+                    std::vector<qq3::PhaseDesc> h(pr.n);
+                    QQ_CUDA_TRY(cudaMemcpy(h.data(), pr.d_prog, sizeof(qq3::PhaseDesc) * pr.n, cudaMemcpyDeviceToHost));
+                    for (const auto& p : h) n += p.type == qq3::PH_MOE ? 1 : 0;
+                }
+            }
+            *value = n;
         } else {
             need(false, "qq_model_stat: unknown statistic");
         }

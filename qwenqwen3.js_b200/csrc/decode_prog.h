@@ -6,6 +6,12 @@
 // words it needs carry the tag of their producer phase, so data arrival is the only
 // synchronisation between CTAs; every phase writes its own output buffer, so no word is
 // written twice in one step.
+//
+// A fused MoE phase (PH_MOE) instead sums partial outputs of every CTA into an accumulated
+// vector (float atomics) and counts the CTAs that are done in a counter next to it; a reader
+// waits for the counter before it reads the vector.  Accumulated vectors and counters live in
+// an arena of two halves: step `epoch` uses half (epoch & 1) and zeroes the other half, which
+// the previous step used and the next step will use.
 #pragma once
 #include "kernels.h"
 
@@ -21,6 +27,7 @@ enum PhaseType : int {
     PH_DOWN4 = 2,   // MoE down + combine + residual over the 4 routed experts (consumer mode B)
     PH_ATTN = 3,    // GQA decode attention with QK-norm, RoPE and KV append
     PH_FINISH = 4,  // token = argmax, pos += 1, trace
+    PH_MOE = 5,     // router + expert gate/up + SwiGLU + down + combine + residual, one phase
 };
 
 enum MapKind : int { MK_ROWS = 0, MK_CONCAT3 = 1, MK_PAIR = 2, MK_STRIDE3 = 3, MK_EXPERT_PAIR = 4, MK_DOWN4 = 5 };
@@ -73,6 +80,20 @@ struct PhaseDesc {
     int emb_K, n_vocab;
     int* ctl;    // [token, pos]
     int* trace;  // per-sequence greedy ids by position
+    // accumulated vectors (addresses in arena half 0; the kernel adds the half of the step)
+    const float* xa;         // input read instead of x (nullable)
+    const unsigned* xa_cnt;  // its counter and the count that completes it
+    int xa_n;
+    int ra_n;
+    const float* ra;         // residual read instead of res by EK_RESID (nullable)
+    const unsigned* ra_cnt;
+    // PH_MOE: the expert down tensor transposed, and the accumulated output
+    const int8_t* dt_qs;     // [n_expert][N][n_out] int8: row j of expert e = column j of its down
+    const __half* dt_d;      // [n_expert][N/32][n_out] block scales
+    float* acc;              // [n_out] sum over CTAs (+ the residual), zero at the start of the step
+    unsigned* acc_cnt;       // CTAs done (gridDim.x completes it)
+    int n_out;
+    int pad3;
 };
 
 // Control block of the persistent kernel, one per model (shared by all its programs).
@@ -80,7 +101,9 @@ struct DecodeCtl {
     unsigned int epoch;       // steps run; tags of the current step derive from it
     unsigned int end_ticket;  // CTAs done with the current step (the last one closes the step)
     unsigned long long best;  // argmax key of the logits (reset by the CTA that closes the step)
-    unsigned int pad[28];
+    float* arena;             // accumulated vectors and counters: two halves of arena_half words
+    long long arena_half;
+    unsigned int pad[24];
 };
 
 // Shared-memory plan of the persistent kernel: a byte ring of kDecRingBytes holding up to
@@ -92,10 +115,20 @@ constexpr int kDecMaxStageBytes = 72 * 1024;
 constexpr int kDecDigitBytes = 24 * 1024;
 constexpr int kDecAttnBytes = 20 * 1024;
 
+// Fused MoE phase: hidden units per gate/up stage and per down stage, rows of the output per
+// consumer thread (the 128 threads of a consumer set cover n_out = 2048).
+constexpr int kMoeG = 16;
+constexpr int kMoeDU = 16;
+constexpr int kMoeRows = 16;
+constexpr int kMoeOut = 128 * kMoeRows;
+constexpr int kMoeMaxUnits = 512;  // hidden units one CTA may own
+
 // Launch one decode step (grid = one CTA per SM).
 void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, int* err, cudaStream_t s);
 // Items per stage for a streamed phase (a power of two >= 4 dividing n_div when possible).
 int decode_stage_items(int S, int K, int n_div, int n_total);
+// Whether a fused MoE phase of these shapes fits (input K, N hidden units per expert, n_out).
+bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k);
 // Whether a phase fits the persistent kernel's shared-memory plan.
 bool decode_phase_fits(const PhaseDesc& p);
 

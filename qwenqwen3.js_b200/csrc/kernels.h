@@ -96,6 +96,10 @@ void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16,
                         const GemmGroups* groups, cudaStream_t s);
 void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 
+// Per expert e of a packed Q8_0 tensor (rows = n_expert x R, K): t_qs[e][k][r] = qs[e R + r][k]
+// and t_d[e][k/32][r] = d[e R + r][k/32] (the fused decode MoE reads down columns as rows).
+void launch_transpose_experts(const DTensor& W, int n_expert, int8_t* t_qs, __half* t_d, cudaStream_t s);
+
 // ---- MoE block for T rows regrouped by expert on the tensor cores (kernels_moe_grouped.cu) ----
 size_t moe_grouped_scratch_bytes(int T, int top_k, int n_expert, int64_t K, int64_t F);
 // idx/w: routed ids and weights [T][top_k]; out[T][K] = sum_s w[t][s] * down_e(silu(gate_e x) * up_e x)

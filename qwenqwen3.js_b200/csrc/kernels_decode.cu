@@ -33,6 +33,18 @@ constexpr int kMaxRowsPerWarp = 8;      // rows a consumer warp dots per stage
 constexpr uint32_t kProducerBackoffNs = 200;
 constexpr int kRouteWarp = 1;           // consumer warp that computes the top-k
 constexpr int kStageTarget = 64 * 1024; // stage size the item count per stage aims for
+// L2 prefetch, per CTA, of the rows of the phases after an MoE layer (which do not depend on
+// the routing), issued while the CTA routes: DRAM is otherwise idle then
+constexpr uint32_t kRoutePrefetchBytes = 0;
+// Weight rows are read once per step (1.66 GB through a 126 MB L2): copy them evict-first so
+// that activations, norms, K/V rows and the shared router rows stay in L2
+constexpr bool kWeightsEvictFirst = true;
+
+// bulk copy of weight rows into a ring stage
+__device__ __forceinline__ void weight_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    if (kWeightsEvictFirst) bulk_g2s_hint(dst, src, bytes, bar, pol);
+    else bulk_g2s(dst, src, bytes, bar);
+}
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
@@ -108,7 +120,32 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
-__device__ __forceinline__ bool streamed(int type) { return type == PH_GEMV || type == PH_DOWN4; }
+__device__ __forceinline__ bool streamed(int type) { return type == PH_GEMV || type == PH_DOWN4 || type == PH_MOE; }
+
+// Bounded wait until the counter of an accumulated vector reaches n (acquire: the vector's
+// atomics, published by the writers' fences before they counted, are visible afterwards).
+__device__ __forceinline__ void wait_cnt(const unsigned* c, unsigned n, int* err) {
+    for (uint32_t it = 0; it < kSpinLimit; ++it) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+        if (v >= n) return;
+        if ((it & 255u) == 255u && ld_volatile(err)) return;
+    }
+    set_err(err, 4);
+}
+
+// The hidden units [u0, u1) of the fused MoE phase this CTA owns: the U = top_k * N units of
+// the routed experts (slot-major) split into nearly equal runs of whole quads.
+__device__ __forceinline__ void moe_range(int U, int& u0, int& u1) {
+    const long long nq = U >> 2;
+    u0 = 4 * (int)(nq * blockIdx.x / gridDim.x);
+    u1 = 4 * (int)(nq * (blockIdx.x + 1) / gridDim.x);
+}
+
+// Units of the next stage at u: at most cap, within the run, and within one expert.
+__device__ __forceinline__ int moe_stage_len(int u, int u1, int N, int cap) {
+    return min(min(cap, u1 - u), (u / N + 1) * N - u);
+}
 
 __device__ __forceinline__ bool dec_masked(const uint32_t* mask, int e) {
     return mask && ((mask[e >> 5] >> (e & 31)) & 1u);
@@ -157,6 +194,13 @@ __device__ __forceinline__ void load_phase(const PhaseDesc* pp, PhaseRegs& R, co
 
 __device__ __forceinline__ bool expert_map(int map) { return map == MK_EXPERT_PAIR || map == MK_DOWN4; }
 
+// Element k (runtime, < 4) of a 4-array held in registers (a dynamic index would move the
+// whole struct to local memory).
+template <typename T>
+__device__ __forceinline__ T pick4(const T (&a)[4], int k) {
+    return k == 0 ? a[0] : (k == 1 ? a[1] : (k == 2 ? a[2] : a[3]));
+}
+
 // Row pointers of the group starting at item0 (registers only).
 __device__ __forceinline__ void group_ptrs(const PhaseRegs& R, int item0, const int8_t* (&q)[4],
                                            const __half* (&d)[4], bool (&on)[4]) {
@@ -184,10 +228,10 @@ __device__ __forceinline__ void group_ptrs(const PhaseRegs& R, int item0, const 
             break;
         case MK_EXPERT_PAIR: {
             const int k = item0 / R.N, j0 = item0 - k * R.N;
-            const int64_t row = (int64_t)R.e[k] * R.N + j0;
+            const int64_t row = (int64_t)pick4(R.e, k) * R.N + j0;
             q[0] = R.q[0] + row * K; d[0] = R.d[0] + row * KS;
             q[1] = R.q[1] + row * K; d[1] = R.d[1] + row * KS;
-            on[0] = on[1] = R.on[k];
+            on[0] = on[1] = pick4(R.on, k);
             break;
         }
         case MK_DOWN4:
@@ -251,14 +295,91 @@ struct ProdRing {
     }
 };
 
+// L2 prefetch of this CTA's groups of a streamed phase, up to `budget` bytes; returns the rest.
+__device__ uint32_t prefetch_phase_l2(const PhaseDesc* pp, uint32_t budget) {
+    PhaseRegs R;
+    load_phase(pp, R, nullptr);
+    const int K = R.K, S = R.S, G = R.G;
+    const int n_groups = (R.n_items + G - 1) / G;
+    for (int g = blockIdx.x; g < n_groups && budget > 0; g += gridDim.x) {
+        const int item0 = g * G;
+        const int rows = min(G, R.n_items - item0);
+        const int8_t* q[4];
+        const __half* d[4];
+        bool on[4] = {false, false, false, false};
+        group_ptrs(R, item0, q, d, on);
+        const uint32_t qb = (uint32_t)rows * K, db = round16((uint32_t)rows * (K >> 4));
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            if (s >= S || !on[s]) continue;
+            bulk_prefetch_l2(q[s], qb);
+            bulk_prefetch_l2(d[s], db);
+            budget = qb + db >= budget ? 0u : budget - (qb + db);
+        }
+    }
+    return budget;
+}
+
+// The stages of this CTA's run of a fused MoE phase, in consumption order: first the gate and
+// up rows of its hidden units (kMoeG units a stage, never straddling two experts), then the
+// same units' rows of the transposed down tensor with the block scales they need (kMoeDU units
+// a stage).  A masked expert's stages carry no bytes.
+__device__ __forceinline__ bool moe_produce(const PhaseDesc* pp, const DecRing& r, const DecRoute* route,
+                                            ProdRing& pr, uint64_t pol, int* err) {
+    const int K = pp->K, N = pp->N, EO = pp->n_out;
+    int u0, u1;
+    moe_range(pp->top_k * N, u0, u1);
+    const uint32_t qsz = qs_stride(kMoeG, K), dsz = d_stride(kMoeG, K), need = stage_bytes(2, kMoeG, K);
+    const int64_t KS = K >> 5;
+    for (int u = u0; u < u1; ++pr.i) {
+        const int n = moe_stage_len(u, u1, N, kMoeG);
+        const int s = u / N, j = u - s * N;
+        const int e = route->id[s];
+        const bool on = !dec_masked(pp->mask, e);
+        int slot;
+        uint8_t* sb;
+        if (!pr.alloc(r, need, err, slot, sb)) return false;
+        const uint32_t qb = (uint32_t)n * K, db = round16((uint32_t)n * (K >> 4));
+        mbar_arrive_expect_tx(&r.full[slot], on ? 2u * (qb + db) : 0u);
+        if (on) {
+            const int64_t row = (int64_t)e * N + j;
+            weight_g2s(sb, pp->qs[0] + row * K, qb, &r.full[slot], pol);
+            weight_g2s(sb + qsz, pp->qs[1] + row * K, qb, &r.full[slot], pol);
+            weight_g2s(sb + 2 * qsz, pp->d[0] + row * KS, db, &r.full[slot], pol);
+            weight_g2s(sb + 2 * qsz + dsz, pp->d[1] + row * KS, db, &r.full[slot], pol);
+        }
+        u += n;
+    }
+    const uint32_t dq = (uint32_t)kMoeDU * EO, need2 = (dq + 4u * EO + 127u) & ~127u;
+    for (int u = u0; u < u1; ++pr.i) {
+        const int n = moe_stage_len(u, u1, N, kMoeDU);
+        const int s = u / N, j = u - s * N;
+        const int e = route->id[s];
+        const bool on = !dec_masked(pp->mask, e);
+        int slot;
+        uint8_t* sb;
+        if (!pr.alloc(r, need2, err, slot, sb)) return false;
+        const int b0 = j >> 5, nb = ((j + n - 1) >> 5) - b0 + 1;  // <= 2 scale rows
+        const uint32_t qb = (uint32_t)n * EO, sbytes = (uint32_t)nb * EO * 2u;
+        mbar_arrive_expect_tx(&r.full[slot], on ? qb + sbytes : 0u);
+        if (on) {
+            weight_g2s(sb, pp->dt_qs + ((int64_t)e * N + j) * EO, qb, &r.full[slot], pol);
+            weight_g2s(sb + dq, pp->dt_d + ((int64_t)e * (N >> 5) + b0) * EO, sbytes, &r.full[slot], pol);
+        }
+        u += n;
+    }
+    return true;
+}
+
 __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, DecRoute* route, int* err) {
     ProdRing pr;
+    const uint64_t pol = l2_policy_evict_first();
     uint32_t routed = 0;  // MoE layers whose routing this CTA has seen
     for (int ph = 0; ph < n_phases; ph++) {
         const PhaseDesc* pp = prog + ph;
         if (!streamed(pp->type)) continue;
         const bool ex = expert_map(pp->map);
-        if (pp->map == MK_EXPERT_PAIR) {
+        if (pp->map == MK_EXPERT_PAIR || pp->type == PH_MOE) {
             // The router rows go first, as two stages of up to 16 rows (one per consumer set).
             const int K = pp->K, ne = pp->n_expert;
             for (int h = 0; h < 2; ++h, ++pr.i) {
@@ -273,10 +394,22 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                     bulk_g2s(sb + qs_stride(16, K), pp->r_d + (int64_t)16 * h * (K >> 5), db, &r.full[slot]);
                 }
             }
+            if (kRoutePrefetchBytes > 0) {
+                uint32_t budget = kRoutePrefetchBytes;
+                for (int ph2 = ph + 1; ph2 < n_phases && budget > 0; ph2++) {
+                    const PhaseDesc* p2 = prog + ph2;
+                    if (p2->type == PH_MOE || p2->type == PH_DOWN4 || p2->map == MK_EXPERT_PAIR) break;
+                    if (p2->type == PH_GEMV) budget = prefetch_phase_l2(p2, budget);
+                }
+            }
             // Wait for this CTA's routing.  (Pulling the next layer's rows into L2 meanwhile was
             // measured slower: it competes with the expert rows for DRAM right after routing.)
             if (!slot_wait(&route->bar, routed & 1u, err, kProducerBackoffNs)) goto drain;
             ++routed;
+        }
+        if (pp->type == PH_MOE) {
+            if (!moe_produce(pp, r, route, pr, pol, err)) goto drain;
+            continue;
         }
         {
             PhaseRegs R;
@@ -296,13 +429,15 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                 group_ptrs(R, item0, q, d, on);
                 const uint32_t qb = (uint32_t)rows * K, db = round16((uint32_t)rows * (K >> 4));
                 uint32_t tx = 0;
-                for (int s = 0; s < S; s++)
-                    if (on[s]) tx += qb + db;
+#pragma unroll
+                for (int s = 0; s < 4; s++)
+                    if (s < S && on[s]) tx += qb + db;
                 mbar_arrive_expect_tx(&r.full[slot], tx);  // release: publishes r.off[slot] too
-                for (int s = 0; s < S; s++) {
-                    if (!on[s]) continue;
-                    bulk_g2s(sb + s * qsz, q[s], qb, &r.full[slot]);
-                    bulk_g2s(sb + S * qsz + s * dsz, d[s], db, &r.full[slot]);
+#pragma unroll
+                for (int s = 0; s < 4; s++) {
+                    if (s >= S || !on[s]) continue;
+                    weight_g2s(sb + s * qsz, q[s], qb, &r.full[slot], pol);
+                    weight_g2s(sb + S * qsz + s * dsz, d[s], db, &r.full[slot], pol);
                 }
             }
         }
@@ -315,11 +450,38 @@ drain:
 
 // ---- consumer helpers --------------------------------------------------------------------
 
+// Where a phase reads its input: tagged words, or an accumulated vector once its counter is
+// complete; optionally also the counter of an accumulated residual the phase's epilogue reads,
+// and a shared-memory copy of the raw (un-normalised) input.
+struct StageIn {
+    const tword* x;
+    uint32_t tag;
+    const float* xa;
+    const unsigned* cnt;
+    unsigned n;
+    const unsigned* rcnt;
+    unsigned rn;
+    float* raw;
+};
+
+__device__ __forceinline__ StageIn stage_in(const PhaseDesc& p, uint32_t epoch, long long aoff) {
+    StageIn in;
+    in.x = p.x;
+    in.tag = step_tag(epoch, p.x_ph);
+    in.xa = p.xa ? p.xa + aoff : nullptr;
+    in.cnt = p.xa ? p.xa_cnt + aoff : nullptr;
+    in.n = (unsigned)p.xa_n;
+    in.rcnt = p.ra ? p.ra_cnt + aoff : nullptr;
+    in.rn = (unsigned)p.ra_n;
+    in.raw = nullptr;
+    return in;
+}
+
 // Digitise an input of runtime length K <= kMaxStageK (8 elements per consumer thread per
 // pass, at most 4 passes held in registers), with an optional RMSNorm (tensor.js:103-114;
 // sum of squares in double as the JS does).
-__device__ void dec_stage_digits(const tword* __restrict__ x, uint32_t tag, const float* __restrict__ norm_w,
-                                 float eps, int K, uint4* dig, float* xsc, double* red, int* err) {
+__device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ norm_w, float eps, int K, uint4* dig,
+                                 float* xsc, double* red, int* err) {
     const int t = threadIdx.x;
     float xv[4][8];
     double ss = 0.0;
@@ -335,14 +497,41 @@ __device__ void dec_stage_digits(const tword* __restrict__ x, uint32_t tag, cons
             nw[ps][1] = ld_early_f4(norm_w + e0 + 4);
         }
     }
+    if (in.rcnt && t == 0) wait_cnt(in.rcnt, in.rn, err);  // the barrier after staging publishes it
+    if (in.xa) {
+        if (t == 0) wait_cnt(in.cnt, in.n, err);
+        named_bar(1, kConsumerThreads);
 #pragma unroll
-    for (int ps = 0; ps < 4; ps++) {
-        const int e0 = 8 * t + ps * 8 * kConsumerThreads;
-        if (e0 < K) {
-            wait_tw8(x + e0, tag, err, xv[ps]);
-        } else {
+        for (int ps = 0; ps < 4; ps++) {
+            const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+            if (e0 < K) {
+                a = __ldcg(reinterpret_cast<const float4*>(in.xa + e0));
+                b = __ldcg(reinterpret_cast<const float4*>(in.xa + e0 + 4));
+            }
+            xv[ps][0] = a.x; xv[ps][1] = a.y; xv[ps][2] = a.z; xv[ps][3] = a.w;
+            xv[ps][4] = b.x; xv[ps][5] = b.y; xv[ps][6] = b.z; xv[ps][7] = b.w;
+        }
+    } else {
 #pragma unroll
-            for (int e = 0; e < 8; e++) xv[ps][e] = 0.f;
+        for (int ps = 0; ps < 4; ps++) {
+            const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+            if (e0 < K) {
+                wait_tw8(in.x + e0, in.tag, err, xv[ps]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) xv[ps][e] = 0.f;
+            }
+        }
+    }
+    if (in.raw) {
+#pragma unroll
+        for (int ps = 0; ps < 4; ps++) {
+            const int e0 = 8 * t + ps * 8 * kConsumerThreads;
+            if (e0 < K) {
+                reinterpret_cast<float4*>(in.raw + e0)[0] = make_float4(xv[ps][0], xv[ps][1], xv[ps][2], xv[ps][3]);
+                reinterpret_cast<float4*>(in.raw + e0)[1] = make_float4(xv[ps][4], xv[ps][5], xv[ps][6], xv[ps][7]);
+            }
         }
     }
     if (norm_w) {
@@ -594,7 +783,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
 template <int S, int IPW>
 __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R, const DecRing& r, uint32_t& i,
                                           const uint4* dig, const float* xsc, uint32_t tag_out, uint32_t tag_res,
-                                          unsigned long long& best_k, int* err) {
+                                          const float* ra, unsigned long long& best_k, int* err) {
     constexpr int NR = S * IPW;
     constexpr int NRP = NR == 3 ? 4 : (NR > 4 ? 8 : NR);  // rows padded for the halving reduction
     constexpr int SH = NRP == 8 ? 2 : (NRP == 4 ? 3 : (NRP == 2 ? 4 : 5));  // lane >> SH = row of the sum
@@ -619,7 +808,7 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
         // phase wait sees the error word and all consumer warps return together)
         if (!slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err)) break;
         const uint8_t* sb = r.base + r.off[slot];
-        const bool gon = R.map != MK_EXPERT_PAIR || R.on[(g * G) / R.N];
+        const bool gon = R.map != MK_EXPERT_PAIR || pick4(R.on, (g * G) / R.N);
         const int li0 = w * IPW;
         const int n_left = R.n_items - g * G - li0;  // items of this warp that exist
         const int n_have = n_left >= IPW ? IPW : (n_left > 0 ? n_left : 0);
@@ -628,7 +817,8 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
         float pre[5] = {0.f, 0.f, 0.f, 0.f, 0.f};  // epilogue operands, fetched before the dots
         if (mine) {
             if (epi == EK_RESID) {
-                pre[0] = wait_tw(p.res + item, tag_res, err);
+                // an accumulated residual is complete: its counter was awaited while staging
+                pre[0] = ra ? __ldcg(ra + item) : wait_tw(p.res + item, tag_res, err);
             } else if (epi == EK_CONV) {
                 pre[0] = p.state[item];
                 pre[1] = p.state[p.E + item];
@@ -730,6 +920,151 @@ __device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R
             st_tw(y + g * kG + lane, yold + moe, tag_out);
         }
         named_bar(2 + set, 128);
+    }
+}
+
+// ---- fused MoE: router, expert gate/up + SwiGLU, down and combine in one phase -------------
+// lfm2-engine.js:413-487 restated as a split over the hidden units of the routed experts: the
+// CTA owning units [u0, u1) computes h_u = w_slot * silu(gate_u . x) * (up_u . x) for its units,
+// then its partial out[r] = sum_u h_u * down[r][u] for all n_out rows from the transposed down
+// rows, and adds it to the accumulated output with float atomics.  One CTA also adds the
+// residual rows it owns.  The sum is the JS combine (w_k-weighted expert outputs in slot order
+// plus the residual), reassociated; its rounding differs by ~1e-7 relative.
+
+// out-row partials of the units [k0, k1) of a down stage whose scale row is dsc (one 32-unit
+// block): part[r] = sum_k h_k q_k[r], then acc[r] += part[r] * d[r]
+__device__ __forceinline__ void moe_down_seg(const uint8_t* q, int EO, const float* h, int k0, int k1,
+                                             const __half* dsc, float (&acc)[kMoeRows]) {
+    float part[kMoeRows];
+#pragma unroll
+    for (int j = 0; j < kMoeRows; j++) part[j] = 0.f;
+    for (int k = k0; k < k1; k++) {
+        const float hv = h[k];
+        const uint4 w = *reinterpret_cast<const uint4*>(q + (size_t)k * EO);
+        const uint32_t ww[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                // byte b + 128 in the low mantissa bits of 2^23: exact int8 -> float in two ops
+                const float f = __uint_as_float(__byte_perm(ww[c], 0x4B000000u, 0x7650u + b)) - 8388736.0f;
+                part[4 * c + b] = fmaf(hv, f, part[4 * c + b]);
+            }
+    }
+    const uint4 s0 = reinterpret_cast<const uint4*>(dsc)[0], s1 = reinterpret_cast<const uint4*>(dsc)[1];
+    const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&sw[j]));
+        acc[2 * j] = fmaf(part[2 * j], dd.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(part[2 * j + 1], dd.y, acc[2 * j + 1]);
+    }
+}
+
+// scratch: raw input [kMoeOut] (written by the staging), set-1 partials [kMoeOut], h [kMoeMaxUnits]
+__device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
+                          const DecRoute* route, float* scratch, float* acc_out, unsigned* cnt, int* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int set = warp / 4, w = warp % 4;
+    const int K = p.K, nch = K >> 4, N = p.N, EO = p.n_out;
+    const float* raw = scratch;
+    float* comb = scratch + kMoeOut;
+    float* hbuf = comb + kMoeOut;
+    int u0, u1;
+    moe_range(p.top_k * N, u0, u1);
+    bool ok = true;
+    // gate/up: warp w of the stage's set dots items IPW w .. IPW w + IPW - 1 (gate and up rows
+    // interleaved)
+    {
+        constexpr int IPW = kMoeG / 4, NR = 2 * IPW;
+        constexpr int SH = NR == 8 ? 2 : (NR == 4 ? 3 : 4);  // lane >> SH = row of the sum
+        static_assert(NR == 2 || NR == 4 || NR == 8, "kMoeG");
+        const uint32_t qsz = qs_stride(kMoeG, K), dsz = d_stride(kMoeG, K);
+        const int row = lane >> SH;
+        const bool lead = (lane & ((1 << SH) - 1)) == 0 && (row & 1) == 0;
+        const int my_j = w * IPW + (row >> 1);
+        for (int u = u0; u < u1; ++i) {
+            const int n = moe_stage_len(u, u1, N, kMoeG);
+            const int s = u / N;
+            if ((int)(i % kSets) == set && ok) {
+                const int slot = i % kDecSlots;
+                ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
+                if (ok) {
+                    const uint8_t* sb = r.base + r.off[slot];
+                    const int8_t* q[NR];
+                    const __half* d[NR];
+#pragma unroll
+                    for (int j = 0; j < NR; j++) {
+                        const int li = w * IPW + (j >> 1), src = j & 1;
+                        q[j] = reinterpret_cast<const int8_t*>(sb + src * qsz) + (size_t)li * K;
+                        d[j] = reinterpret_cast<const __half*>(sb + 2 * qsz + src * dsz) + li * (K >> 5);
+                    }
+                    float a[NR];
+                    rows_dot<NR>(q, d, dig, xsc, nch, nch, a);
+                    const float a0 = warp_reduce_rows<NR>(a);
+                    const float a1 = __shfl_down_sync(0xffffffffu, a0, 1 << SH);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&r.empty[slot]);
+                    if (lead && my_j < n)
+                        hbuf[u - u0 + my_j] = dec_masked(p.mask, route->id[s]) ? 0.f : silu_mul(a0, a1) * route->w[s];
+                }
+            }
+            u += n;
+        }
+    }
+    named_bar(1, kConsumerThreads);  // h complete
+    // down: thread tp of the stage's set accumulates out rows 16 tp .. 16 tp + 15
+    const int tp = threadIdx.x & 127;
+    float acc[kMoeRows];
+#pragma unroll
+    for (int j = 0; j < kMoeRows; j++) acc[j] = 0.f;
+    {
+        const uint32_t dq = (uint32_t)kMoeDU * EO;
+        for (int u = u0; u < u1; ++i) {
+            const int n = moe_stage_len(u, u1, N, kMoeDU);
+            const int s = u / N, j0 = u - s * N;
+            if ((int)(i % kSets) == set && ok) {
+                const int slot = i % kDecSlots;
+                ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
+                if (ok) {
+                    if (!dec_masked(p.mask, route->id[s])) {  // a masked expert's stage holds no bytes
+                        const uint8_t* sb = r.base + r.off[slot];
+                        const __half* dsc = reinterpret_cast<const __half*>(sb + dq) + tp * kMoeRows;
+                        const int kb = min(n, 32 - (j0 & 31));  // units in the first scale block
+                        moe_down_seg(sb + tp * 16, EO, hbuf + (u - u0), 0, kb, dsc, acc);
+                        if (kb < n) moe_down_seg(sb + tp * 16, EO, hbuf + (u - u0), kb, n, dsc + EO, acc);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&r.empty[slot]);
+                }
+            }
+            u += n;
+        }
+    }
+    // combine the two sets, add the owned residual rows, accumulate, count this CTA
+    if (set == 1) {
+#pragma unroll
+        for (int j = 0; j < kMoeRows; j += 4)
+            *reinterpret_cast<float4*>(comb + tp * kMoeRows + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    }
+    named_bar(1, kConsumerThreads);
+    if (set == 0) {
+        const bool owner = tp % (int)gridDim.x == (int)blockIdx.x;
+#pragma unroll
+        for (int j = 0; j < kMoeRows; j += 4) {
+            const float4 c = *reinterpret_cast<const float4*>(comb + tp * kMoeRows + j);
+            float4 v = make_float4(acc[j] + c.x, acc[j + 1] + c.y, acc[j + 2] + c.z, acc[j + 3] + c.w);
+            if (owner) {
+                const float4 x = *reinterpret_cast<const float4*>(raw + tp * kMoeRows + j);
+                v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+            }
+            atomicAdd(reinterpret_cast<float4*>(acc_out + tp * kMoeRows + j), v);
+        }
+    }
+    named_bar(1, kConsumerThreads);
+    if (threadIdx.x == 0) {
+        __threadfence();  // cumulative over the CTA's atomics (ordered before by the barrier)
+        atomicAdd(cnt, 1u);
     }
 }
 
@@ -967,6 +1302,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (lane == 0) dec_producer(prog, n_phases, r, &route, err);
         return;
     }
+    // this step's half of the accumulated-vector arena; zero the other half (the previous step
+    // used it, the next one will: kernel boundaries order the zeroing against both)
+    long long aoff = 0;
+    {
+        float* arena = ctl->arena;
+        const long long half = ctl->arena_half;
+        const int par = (int)(epoch & 1u);
+        aoff = par * half;
+        if (arena && half > 0) {
+            float* z = arena + (1 - par) * half;
+            for (long long k = (long long)blockIdx.x * kConsumerThreads + threadIdx.x; k < half;
+                 k += (long long)gridDim.x * kConsumerThreads)
+                z[k] = 0.f;
+        }
+    }
     uint32_t i = 0;  // ring position, advanced exactly as the producer advances it
     for (int ph = 0; ph < n_phases; ph++) {
         const PhaseDesc& p = prog[ph];
@@ -1012,23 +1362,24 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (p.r_qs && warp == kRouteWarp && lane < p.n_expert && p.bias) bias_v = ld_early_f32(p.bias + lane);
             uint4* dig = reinterpret_cast<uint4*>(dig_base);
             float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
-            dec_stage_digits(p.x, step_tag(epoch, p.x_ph), p.norm_w, p.eps, K, dig, xsc, red, err);
+            dec_stage_digits(stage_in(p, epoch, aoff), p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
             if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
+            const float* ra = p.ra ? p.ra + aoff : nullptr;
             PhaseRegs R;
             load_phase(&p, R, expert_map(p.map) ? &route : nullptr);
             unsigned long long best_k = 0ull;
             const int ipw = R.G / 4;
             const uint32_t tres = step_tag(epoch, p.res_ph);
-            if (R.S == 1 && ipw == 8) consume_a<1, 8>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 2 && ipw == 4) consume_a<2, 4>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else if (R.S == 3 && ipw == 2) consume_a<3, 2>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
-            else consume_a<3, 1>(p, R, r, i, dig, xsc, tag, tres, best_k, err);
+            if (R.S == 1 && ipw == 8) consume_a<1, 8>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 2 && ipw == 4) consume_a<2, 4>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else if (R.S == 3 && ipw == 2) consume_a<3, 2>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            else consume_a<3, 1>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
             if (p.epi == EK_ARGMAX) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -1043,6 +1394,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     if (m) atomicMax(p.best, m);
                 }
             }
+        } else if (p.type == PH_MOE) {
+            // every CTA routes and owns a run of hidden units (all count into the output)
+            const int K = p.K, nch = K >> 4;
+            float bias_v = 0.f;
+            if (warp == kRouteWarp && lane < p.n_expert && p.bias) bias_v = ld_early_f32(p.bias + lane);
+            uint4* dig = reinterpret_cast<uint4*>(dig_base);
+            float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
+            float* scratch = reinterpret_cast<float*>(dig_base + kDecDigitBytes);
+            StageIn in = stage_in(p, epoch, aoff);
+            in.raw = scratch;
+            dec_stage_digits(in, p.norm_w, p.eps, K, dig, xsc, red, err);
+            named_bar(1, kConsumerThreads);
+            dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
+            moe_fused(p, r, i, dig, xsc, &route, scratch, p.acc + aoff, p.acc_cnt + aoff, err);
         } else if (p.type == PH_DOWN4) {
             if ((int)blockIdx.x >= (p.n_items + kG - 1) / kG) continue;
             PhaseRegs R;
@@ -1051,7 +1416,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             // the four expert inputs are one vector of 4K (blocks never straddle two of them)
             uint4* dig = reinterpret_cast<uint4*>(dig_base);
             float* xsc_all = reinterpret_cast<float*>(dig + 3 * 4 * nch);
-            dec_stage_digits(p.x, step_tag(epoch, p.x_ph), nullptr, 0.f, 4 * K, dig, xsc_all, red, err);
+            dec_stage_digits(stage_in(p, epoch, aoff), nullptr, 0.f, 4 * K, dig, xsc_all, red, err);
             named_bar(1, kConsumerThreads);
             const int src = warp % 4;
             const uint4* dg = dig + src * nch;
@@ -1097,7 +1462,21 @@ int decode_stage_items(int S, int K, int n_div, int n_total) {
     return G;
 }
 
+bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k) {
+    static_assert((size_t)(2 * kMoeOut + kMoeMaxUnits) * 4 <= (size_t)kDecAttnBytes, "fused MoE scratch");
+    if (K < 64 || K % 64 || n_out != kMoeOut || K != n_out) return false;  // the residual is the input
+    if (N < 32 || N % 32 || top_k != 4 || n_expert < 4 || n_expert > kMaxRoutes) return false;
+    const int64_t quads = (int64_t)top_k * N / 4;
+    if ((quads + num_sms() - 1) / num_sms() * 4 > kMoeMaxUnits) return false;
+    const size_t gu = 2 * ((size_t)kMoeG * K + (((size_t)kMoeG * (K >> 4) + 15) & ~(size_t)15));
+    const size_t dn = (size_t)kMoeDU * n_out + 4 * (size_t)n_out;
+    if (gu > (size_t)kDecMaxStageBytes || dn > (size_t)kDecMaxStageBytes) return false;
+    if ((size_t)16 * K + K > (size_t)kDecMaxStageBytes) return false;  // router stages
+    return (size_t)3 * (K >> 4) * 16 + (size_t)(K >> 5) * 4 <= (size_t)kDecDigitBytes;
+}
+
 bool decode_phase_fits(const PhaseDesc& p) {
+    if (p.type == PH_MOE) return p.r_qs && p.dt_qs && decode_moe_fits(p.K, p.N, p.n_out, p.n_expert, p.top_k);
     if (p.type != PH_GEMV && p.type != PH_DOWN4) {
         if (p.type == PH_ATTN) {
             const int G = p.attn.n_head / p.attn.n_kv, hd = p.attn.hd;

@@ -21,6 +21,39 @@ __global__ void k_repack_q8(const uint16_t* __restrict__ raw, int64_t n_blocks, 
     d[b] = __ushort_as_half(p[0]);
 }
 
+// Transpose of n_mat row-major matrices [rows][cols] -> [cols][rows], 32 x 32 tiles through
+// shared memory (both sides coalesced).
+template <typename T>
+__global__ void k_transpose(const T* __restrict__ in, int rows, int cols, T* __restrict__ out) {
+    __shared__ T tile[32][33];
+    const int64_t m = blockIdx.z;
+    const T* src = in + m * rows * (int64_t)cols;
+    T* dst = out + m * rows * (int64_t)cols;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+        const int r = r0 + y, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[y][threadIdx.x] = src[(int64_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+        const int c = c0 + y, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) dst[(int64_t)c * rows + r] = tile[threadIdx.x][y];
+    }
+}
+
+void launch_transpose_experts(const DTensor& W, int n_expert, int8_t* t_qs, __half* t_d, cudaStream_t s) {
+    const int64_t rows = W.rows / n_expert, K = W.K;
+    QQ_CHECK(W.type == 8 && W.rows % n_expert == 0 && K % 32 == 0 && rows <= (1 << 20) && K <= (1 << 20), -4,
+             "expert transpose: unsupported tensor");
+    const dim3 blk(32, 8);
+    k_transpose<int8_t><<<dim3((unsigned)((K + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)n_expert), blk, 0, s>>>(
+        W.qs, (int)rows, (int)K, t_qs);
+    QQ_CUDA_TRY(cudaGetLastError());
+    k_transpose<__half><<<dim3((unsigned)((K / 32 + 31) / 32), (unsigned)((rows + 31) / 32), (unsigned)n_expert), blk, 0, s>>>(
+        W.d, (int)rows, (int)(K / 32), t_d);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
 void launch_repack_q8(const uint8_t* raw, int64_t n_blocks, int8_t* qs, __half* d, cudaStream_t s) {
     if (n_blocks <= 0) return;
     const int t = 256;

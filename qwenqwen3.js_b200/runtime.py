@@ -103,6 +103,8 @@ QQ_NOALLOC_MAX_FF = 4096
 
 QQ_STAT_STEP_KERNELS = 0
 QQ_STAT_N_MOE = 1
+QQ_STAT_STEP_PHASES = 2
+QQ_STAT_MOE_FUSED = 3
 QQ_KERN_MOE_LAYER = 0
 QQ_KERN_MOE_GATEUP = 1
 QQ_KERN_MOE_DOWN = 2

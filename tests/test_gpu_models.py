@@ -170,6 +170,45 @@ def test_lfm2_8b_a1b_truncated_full_width(qq3, orc):
     eng.close()
 
 
+def test_lfm2_full_width_fused_moe(qq3, orc):
+    """Full LFM2 widths with 8 experts: every MoE layer of the persistent step is one fused phase
+    (router, expert gate/up, down and combine summed into an accumulated vector).  Routed
+    tokens with an expert mask, then a device decode loop (the accumulator halves alternate
+    every step), match the oracle."""
+    spec = qq3.synth.lfm2_8b_a1b(seed=55)
+    spec.n_layers = 4
+    spec.attn_layers = (2,)
+    spec.n_expert = 8
+    g, eng, ref = _pair(qq3, orc, spec, max_ctx=64)
+    assert eng.model.stat(qq3.runtime.QQ_STAT_MOE_FUSED) == 2
+    toks = qq3.synth.uniform_tokens(6, 9, spec.n_vocab)
+    masked = {1, 6}
+    eng.expertMask = masked
+    ref.set_expert_mask(masked)
+    for p, t in enumerate(toks):
+        want, hid, rec = ref.forward(int(t), p, False, dump=True, routing=True)
+        got = eng.forward(int(t), p, False)
+        assert rel_err(got, want) < TOL
+        assert int(np.argmax(got)) == int(np.argmax(want))
+        _check_routing(eng, rec)
+    eng.resetKVCache()
+    ref.reset()
+    eng.expertMask = None
+    ref.set_expert_mask([])
+    prompt = qq3.synth.uniform_tokens(5, 12, spec.n_vocab).tolist()
+    eng.prefill(prompt[:-1])
+    dev = eng.model.decode_loop(prompt[-1], len(prompt) - 1, 9)
+    for p, t in enumerate(prompt[:-1]):
+        ref.forward(t, p, True)
+    cur, pos, ref_ids = prompt[-1], len(prompt) - 1, []
+    for _ in range(9):
+        cur = int(np.argmax(ref.forward(cur, pos, False)))
+        ref_ids.append(cur)
+        pos += 1
+    assert dev.tolist() == ref_ids
+    eng.close()
+
+
 def test_qwen3_0p6b_config_greedy(qq3, orc):
     """BASELINE config 1 (Qwen3-0.6B shapes, 28 layers): 32-token prompt + 64 greedy steps."""
     spec = qq3.synth.qwen3_0p6b(seed=1234)
