@@ -599,27 +599,30 @@ __device__ __forceinline__ float block_dot(const uint4 w0, const uint4 w1, const
 // 32-weight blocks l, l+32, ... of every row (one float combination per block); the digits of a
 // block are read once for all rows.  Every row is computed (rows past the valid ones point at
 // valid shared memory and their sums are discarded), so the compiler can interleave the NR x 3
-// dp4a chains.
+// dp4a chains.  A block is two 16-byte halves 32 bytes apart from the next lane's: lanes with
+// bit 2 set read their second half first, so each quarter-warp's 16-byte loads cover all 32
+// banks once (no conflict); the digits are read in the same order, so the sums are unchanged.
 template <int NR>
 __device__ __forceinline__ void rows_dot(const int8_t* const (&q)[NR], const __half* const (&d)[NR],
                                          const uint4* dig, const float* xsc, int nch, int pstride, float (&acc)[NR]) {
     const int lane = threadIdx.x & 31;
     const int nb = nch >> 1;
+    const int h0 = (lane >> 2) & 1, h1 = h0 ^ 1;  // the half read first, then the other
 #pragma unroll
     for (int r = 0; r < NR; r++) acc[r] = 0.f;
-#pragma unroll (NR > 4 ? 1 : 2)
+#pragma unroll 1
     for (int b = lane; b < nb; b += 32) {
         uint4 g[3][2];
 #pragma unroll
         for (int pl = 0; pl < 3; pl++) {
-            g[pl][0] = dig[pl * pstride + 2 * b];
-            g[pl][1] = dig[pl * pstride + 2 * b + 1];
+            g[pl][0] = dig[pl * pstride + 2 * b + h0];
+            g[pl][1] = dig[pl * pstride + 2 * b + h1];
         }
         const float sx = xsc[b];
 #pragma unroll
         for (int r = 0; r < NR; r++) {
             const uint4* wp = reinterpret_cast<const uint4*>(q[r] + 32 * b);
-            const uint4 w0 = wp[0], w1 = wp[1];
+            const uint4 w0 = wp[h0], w1 = wp[h1];
             const float dw = __half2float(d[r][b]);
             acc[r] = fmaf(block_dot(w0, w1, g), dw * sx, acc[r]);
         }
