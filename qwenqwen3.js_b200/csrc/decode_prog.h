@@ -8,8 +8,8 @@
 // written twice in one step.
 //
 // A fused MoE phase (PH_MOE) instead sums partial outputs of every CTA into an accumulated
-// vector (float atomics) and counts the CTAs that are done in a counter next to it; a reader
-// waits for the counter before it reads the vector.  Accumulated vectors and counters live in
+// vector (a bulk f32 add-reduction at L2 per CTA) and counts the CTAs that are done in a
+// counter next to it; a reader waits for the counter before it reads the vector.  Accumulated vectors and counters live in
 // an arena of two halves: step `epoch` uses half (epoch & 1) and zeroes the other half, which
 // the previous step used and the next step will use.
 #pragma once

@@ -30,7 +30,7 @@ constexpr int kDecThreads = kThreads2;  // 8 consumer warps + 1 producer warp
 constexpr int kMaxRoutes = 32;          // experts the fused router handles
 constexpr int kMaxStageK = 8192;        // largest K of a streamed phase (4 staging passes)
 constexpr int kMaxRowsPerWarp = 8;      // rows a consumer warp dots per stage
-constexpr uint32_t kProducerBackoffNs = 200;
+constexpr uint32_t kProducerBackoffNs = 0;  // producer ring waits poll tightly (see slot_wait)
 constexpr int kRouteWarp = 1;           // consumer warp that computes the top-k
 constexpr int kStageTarget = 64 * 1024; // stage size the item count per stage aims for
 // L2 prefetch, per CTA, of the rows of the phases after an MoE layer (which do not depend on
@@ -106,9 +106,9 @@ __device__ __forceinline__ void wait_tw8(const tword* p, uint32_t tag, int* err,
     for (int j = 0; j < 8; j++) v[j] = tw_val(w[j]);
 }
 
-// Bounded wait on a ring / routing mbarrier.  The producer backs off with __nanosleep after a
-// few polls (it shares an SM sub-partition with consumer warps 0 and 4); consumers poll tightly
-// (measured: a consumer backoff cost ~1.3% of the step, the producer's none).
+// Bounded wait on a ring / routing mbarrier, polling tightly unless backoff_ns is given (then
+// __nanosleep between polls after the first few).  Measured on the decode step: a backoff in
+// the consumers cost ~1.3% of the step, a 200 ns backoff in the producer ~1.6%.
 __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* err, uint32_t backoff_ns = 0) {
     const uint32_t a = smem_u32(bar);
     for (uint32_t it = 0; it < kWaitPolls; ++it) {
@@ -123,7 +123,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* e
 __device__ __forceinline__ bool streamed(int type) { return type == PH_GEMV || type == PH_DOWN4 || type == PH_MOE; }
 
 // Bounded wait until the counter of an accumulated vector reaches n (acquire: the vector's
-// atomics, published by the writers' fences before they counted, are visible afterwards).
+// reductions, published by the writers' fences before they counted, are visible afterwards).
 __device__ __forceinline__ void wait_cnt(const unsigned* c, unsigned n, int* err) {
     for (uint32_t it = 0; it < kSpinLimit; ++it) {
         unsigned v;
@@ -930,7 +930,7 @@ __device__ __forceinline__ void consume_b(const PhaseDesc& p, const PhaseRegs& R
 // lfm2-engine.js:413-487 restated as a split over the hidden units of the routed experts: the
 // CTA owning units [u0, u1) computes h_u = w_slot * silu(gate_u . x) * (up_u . x) for its units,
 // then its partial out[r] = sum_u h_u * down[r][u] for all n_out rows from the transposed down
-// rows, and adds it to the accumulated output with float atomics.  One CTA also adds the
+// rows, and adds it to the accumulated output with a bulk reduction.  One CTA also adds the
 // residual rows it owns.  The sum is the JS combine (w_k-weighted expert outputs in slot order
 // plus the residual), reassociated; its rounding differs by ~1e-7 relative.
 
@@ -1044,7 +1044,9 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
             u += n;
         }
     }
-    // combine the two sets, add the owned residual rows, accumulate, count this CTA
+    // combine the two sets, add the owned residual rows, add the CTA's vector to the output with
+    // one bulk reduction (at L2; 8x fewer requests than per-thread float4 atomics, which contend
+    // on the same lines from every CTA), count this CTA
     if (set == 1) {
 #pragma unroll
         for (int j = 0; j < kMoeRows; j += 4)
@@ -1061,12 +1063,14 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
                 const float4 x = *reinterpret_cast<const float4*>(raw + tp * kMoeRows + j);
                 v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
             }
-            atomicAdd(reinterpret_cast<float4*>(acc_out + tp * kMoeRows + j), v);
+            *reinterpret_cast<float4*>(comb + tp * kMoeRows + j) = v;
         }
+        fence_proxy_async_smem();  // the bulk reduction reads comb through the async proxy
     }
     named_bar(1, kConsumerThreads);
     if (threadIdx.x == 0) {
-        __threadfence();  // cumulative over the CTA's atomics (ordered before by the barrier)
+        bulk_add_f32_s2g(acc_out, comb, (uint32_t)EO * 4u);  // returns once the sums are performed
+        __threadfence();
         atomicAdd(cnt, 1u);
     }
 }

@@ -84,6 +84,22 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     return p;
 }
 
+// Bulk reduction of a shared-memory f32 vector into global memory (dst[i] += src[i], performed
+// at L2), 16-byte aligned, size a multiple of 16; then wait for it to complete and order its
+// writes (async proxy) before this thread's later generic accesses.
+__device__ __forceinline__ void bulk_add_f32_s2g(float* dst, const float* src, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Make this thread's generic shared-memory writes visible to later async-proxy (bulk copy)
+// reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Bulk prefetch of global memory into L2 (16-byte aligned address, size a multiple of 16).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
