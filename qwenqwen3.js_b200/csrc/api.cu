@@ -263,21 +263,19 @@ size_t tarena_bound(const qq_model* m) {
     return (size_t)(3 * d.n_layers + 2) * v;
 }
 
-// Whether the MoE layers run as fused phases (router + experts + down in one phase, outputs
-// accumulated); QQ3_MOE_FUSED=0 selects the two-phase form (gate/up, then down + combine).
-bool moe_fused(const qq_model* m) {
+// Whether the FFN of layer L runs as one fused phase of the persistent step (router, gate/up,
+// SwiGLU, down and combine; outputs accumulated): an MoE layer, or a dense FFN as a single
+// expert.  QQ3_MOE_FUSED=0 selects the two-phase forms (gate/up, then down).
+bool ffn_fused(const qq_model* m, const Layer& L) {
     const char* env = getenv("QQ3_MOE_FUSED");
     if (env && atoi(env) == 0) return false;
     const qq_model_desc& d = m->d;
-    bool any = false;
-    for (const Layer& L : m->layers) {
-        if (!L.moe) continue;
-        any = true;
-        if (!qq3::decode_moe_fits(d.n_embd, (int)L.t[QQ_GATE_EXPS]->ne[1], d.n_embd, d.n_expert, d.n_expert_used) ||
-            (int)L.t[QQ_DOWN_EXPS]->K != (int)L.t[QQ_GATE_EXPS]->ne[1])
-            return false;
-    }
-    return any;
+    const DTensor* gate = L.t[L.moe ? QQ_GATE_EXPS : QQ_FFN_GATE];
+    const DTensor* down = L.t[L.moe ? QQ_DOWN_EXPS : QQ_FFN_DOWN];
+    if (!gate || !down) return false;
+    const int F = (int)gate->ne[1];
+    return (int)down->K == F && (L.moe ? qq3::decode_moe_fits(d.n_embd, F, d.n_embd, d.n_expert, d.n_expert_used)
+                                       : qq3::decode_moe_fits(d.n_embd, F, d.n_embd, 1, 1));
 }
 
 // The decode step as a phase program for the persistent kernel (kernels_decode.cu); the same
@@ -287,7 +285,8 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     using namespace qq3;
     const qq_model_desc& d = m->d;
     const int E = d.n_embd, hd = d.head_dim, nq = d.n_head * hd, nkv = d.n_head_kv * hd;
-    const bool fuse = moe_fused(m);
+    bool fuse = false;  // any fused FFN phase (they need the accumulator arena)
+    for (const Layer& L : m->layers) fuse = fuse || ffn_fused(m, L);
     if (!m->tarena) {
         m->tarena_len = tarena_bound(m);
         m->tarena = dalloc<tword>(m->tarena_len);
@@ -301,7 +300,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     // fused MoE: one accumulated vector (E floats) + counter (padded to 32 words) per MoE layer
     const size_t aslot = ((size_t)E + 32 + 31) & ~(size_t)31;
     if (fuse && !m->aarena) {
-        m->aarena_half = aslot * (size_t)std::max(m->n_moe, 1);
+        m->aarena_half = aslot * (size_t)d.n_layers;
         m->aarena = dalloc<float>(2 * m->aarena_half);
         cudaStream_t s = m->ctx->stream;
         QQ_CUDA_TRY(cudaMemsetAsync(m->aarena, 0, sizeof(float) * 2 * m->aarena_half, s));
@@ -310,11 +309,11 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->arena, &a, sizeof(a), cudaMemcpyHostToDevice, s));
         QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->arena_half, &h, sizeof(h), cudaMemcpyHostToDevice, s));
         for (Layer& L : m->layers) {
-            if (!L.moe || L.dt_qs) continue;
-            const DTensor& W = *L.t[QQ_DOWN_EXPS];
+            if (!ffn_fused(m, L) || L.dt_qs) continue;
+            const DTensor& W = *L.t[L.moe ? QQ_DOWN_EXPS : QQ_FFN_DOWN];
             L.dt_qs = dalloc<int8_t>((size_t)W.rows * W.K);
             L.dt_d = dalloc<__half>((size_t)W.rows * (W.K / 32));
-            qq3::launch_transpose_experts(W, d.n_expert, L.dt_qs, L.dt_d, s);
+            qq3::launch_transpose_experts(W, L.moe ? d.n_expert : 1, L.dt_qs, L.dt_d, s);
         }
         QQ_CUDA_TRY(cudaStreamSynchronize(s));  // the pointers above are host locals
     }
@@ -448,7 +447,36 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             resid(o);
             push_hid(o);
         }
-        if (L.moe && fuse && hid.t) {
+        auto take_acc = [&](PhaseDesc& g) {
+            QQ_CHECK((size_t)(n_acc + 1) * aslot <= m->aarena_half, QQ_ERR_INVALID,
+                     "persistent program: accumulator arena too small");
+            g.acc = m->aarena + (size_t)n_acc * aslot;
+            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + E);
+            ++n_acc;
+        };
+        auto set_hid_acc = [&](const PhaseDesc& g) {
+            hid = Ref();
+            hid.a = g.acc;
+            hid.c = g.acc_cnt;
+            hid.n = qq3::num_sms();  // every CTA of the grid counts once
+        };
+        if (!L.moe && ffn_fused(m, L) && hid.t && L.dt_qs) {
+            const int F = (int)L.t[QQ_FFN_GATE]->ne[1];
+            PhaseDesc g = gemv(MK_PAIR, EK_STORE, 2, E, F, hid, fn);
+            g.type = PH_MOE;  // without a router (r_qs null): one expert of weight 1
+            g.G = kMoeG;
+            set_src(g, 0, L.t[QQ_FFN_GATE]);
+            set_src(g, 1, L.t[QQ_FFN_UP]);
+            g.n_expert = 1;
+            g.top_k = 1;
+            g.N = F;
+            g.dt_qs = L.dt_qs;
+            g.dt_d = L.dt_d;
+            g.n_out = E;
+            take_acc(g);
+            prog.push_back(g);
+            set_hid_acc(g);
+        } else if (L.moe && ffn_fused(m, L) && hid.t && L.dt_qs) {
             const int k = d.n_expert_used;
             const int F = (int)L.t[QQ_GATE_EXPS]->ne[1];
             PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_STORE, 2, E, k * F, hid, fn);
@@ -469,15 +497,9 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             g.dt_qs = L.dt_qs;
             g.dt_d = L.dt_d;
             g.n_out = E;
-            QQ_CHECK((size_t)(n_acc + 1) * aslot <= m->aarena_half, QQ_ERR_INVALID, "persistent program: accumulator arena too small");
-            g.acc = m->aarena + (size_t)n_acc * aslot;
-            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + E);
-            ++n_acc;
+            take_acc(g);
             prog.push_back(g);
-            hid = Ref();
-            hid.a = g.acc;
-            hid.c = g.acc_cnt;
-            hid.n = qq3::num_sms();  // every CTA of the grid counts once
+            set_hid_acc(g);
         } else if (L.moe) {
             // the down + combine phase reads its residual as tagged words
             QQ_CHECK(hid.t != nullptr, QQ_ERR_UNSUPPORTED, "persistent program: MoE after an accumulated vector");
@@ -1313,7 +1335,7 @@ int qq_model_stat(qq_model* m, int what, int64_t* value) {
                 } else {
                     std::vector<qq3::PhaseDesc> h(pr.n);
                     QQ_CUDA_TRY(cudaMemcpy(h.data(), pr.d_prog, sizeof(qq3::PhaseDesc) * pr.n, cudaMemcpyDeviceToHost));
-                    for (const auto& p : h) n += p.type == qq3::PH_MOE ? 1 : 0;
+                    for (const auto& p : h) n += p.type == qq3::PH_MOE && p.r_qs ? 1 : 0;
                 }
             }
             *value = n;

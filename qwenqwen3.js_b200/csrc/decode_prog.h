@@ -28,6 +28,7 @@ enum PhaseType : int {
     PH_ATTN = 3,    // GQA decode attention with QK-norm, RoPE and KV append
     PH_FINISH = 4,  // token = argmax, pos += 1, trace
     PH_MOE = 5,     // router + expert gate/up + SwiGLU + down + combine + residual, one phase
+                    // (a dense FFN: the same without the router, as one expert of weight 1)
 };
 
 enum MapKind : int { MK_ROWS = 0, MK_CONCAT3 = 1, MK_PAIR = 2, MK_STRIDE3 = 3, MK_EXPERT_PAIR = 4, MK_DOWN4 = 5 };

@@ -320,6 +320,15 @@ __device__ uint32_t prefetch_phase_l2(const PhaseDesc* pp, uint32_t budget) {
     return budget;
 }
 
+// Expert of slot s of a fused FFN phase, and whether its rows are skipped: the routed expert
+// (masked ones skipped), or the single dense FFN "expert" 0 of a phase without a router.
+__device__ __forceinline__ int ffn_expert(const PhaseDesc* pp, const DecRoute* route, int s) {
+    return pp->r_qs ? route->id[s] : 0;
+}
+__device__ __forceinline__ bool ffn_skip(const PhaseDesc* pp, const DecRoute* route, int s) {
+    return pp->r_qs && dec_masked(pp->mask, route->id[s]);
+}
+
 // The stages of this CTA's run of a fused MoE phase, in consumption order: first the gate and
 // up rows of its hidden units (kMoeG units a stage, never straddling two experts), then the
 // same units' rows of the transposed down tensor with the block scales they need (kMoeDU units
@@ -334,8 +343,8 @@ __device__ __forceinline__ bool moe_produce(const PhaseDesc* pp, const DecRing& 
     for (int u = u0; u < u1; ++pr.i) {
         const int n = moe_stage_len(u, u1, N, kMoeG);
         const int s = u / N, j = u - s * N;
-        const int e = route->id[s];
-        const bool on = !dec_masked(pp->mask, e);
+        const int e = ffn_expert(pp, route, s);
+        const bool on = !ffn_skip(pp, route, s);
         int slot;
         uint8_t* sb;
         if (!pr.alloc(r, need, err, slot, sb)) return false;
@@ -354,8 +363,8 @@ __device__ __forceinline__ bool moe_produce(const PhaseDesc* pp, const DecRing& 
     for (int u = u0; u < u1; ++pr.i) {
         const int n = moe_stage_len(u, u1, N, kMoeDU);
         const int s = u / N, j = u - s * N;
-        const int e = route->id[s];
-        const bool on = !dec_masked(pp->mask, e);
+        const int e = ffn_expert(pp, route, s);
+        const bool on = !ffn_skip(pp, route, s);
         int slot;
         uint8_t* sb;
         if (!pr.alloc(r, need2, err, slot, sb)) return false;
@@ -379,7 +388,7 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
         const PhaseDesc* pp = prog + ph;
         if (!streamed(pp->type)) continue;
         const bool ex = expert_map(pp->map);
-        if (pp->map == MK_EXPERT_PAIR || pp->type == PH_MOE) {
+        if (pp->r_qs && (pp->map == MK_EXPERT_PAIR || pp->type == PH_MOE)) {  // a phase with a router
             // The router rows go first, as two stages of up to 16 rows (one per consumer set).
             const int K = pp->K, ne = pp->n_expert;
             for (int h = 0; h < 2; ++h, ++pr.i) {
@@ -1009,7 +1018,8 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&r.empty[slot]);
                     if (lead && my_j < n)
-                        hbuf[u - u0 + my_j] = dec_masked(p.mask, route->id[s]) ? 0.f : silu_mul(a0, a1) * route->w[s];
+                        hbuf[u - u0 + my_j] =
+                            ffn_skip(&p, route, s) ? 0.f : silu_mul(a0, a1) * (p.r_qs ? route->w[s] : 1.0f);
                 }
             }
             u += n;
@@ -1030,7 +1040,7 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
                 const int slot = i % kDecSlots;
                 ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
                 if (ok) {
-                    if (!dec_masked(p.mask, route->id[s])) {  // a masked expert's stage holds no bytes
+                    if (!ffn_skip(&p, route, s)) {  // a masked expert's stage holds no bytes
                         const uint8_t* sb = r.base + r.off[slot];
                         const __half* dsc = reinterpret_cast<const __half*>(sb + dq) + tp * kMoeRows;
                         const int kb = min(n, 32 - (j0 & 31));  // units in the first scale block
@@ -1413,7 +1423,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             in.raw = scratch;
             dec_stage_digits(in, p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
-            dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
+            if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
             moe_fused(p, r, i, dig, xsc, &route, scratch, p.acc + aoff, p.acc_cnt + aoff, err);
         } else if (p.type == PH_DOWN4) {
             if ((int)blockIdx.x >= (p.n_items + kG - 1) / kG) continue;
@@ -1472,7 +1482,9 @@ int decode_stage_items(int S, int K, int n_div, int n_total) {
 bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k) {
     static_assert((size_t)(2 * kMoeOut + kMoeMaxUnits) * 4 <= (size_t)kDecAttnBytes, "fused MoE scratch");
     if (K < 64 || K % 64 || n_out != kMoeOut || K != n_out) return false;  // the residual is the input
-    if (N < 32 || N % 32 || top_k != 4 || n_expert < 4 || n_expert > kMaxRoutes) return false;
+    // routed (top-4 of 4..32 experts), or a dense FFN as one expert without a router
+    const bool dense = n_expert == 1 && top_k == 1;
+    if (N < 32 || N % 32 || (!dense && (top_k != 4 || n_expert < 4 || n_expert > kMaxRoutes))) return false;
     const int64_t quads = (int64_t)top_k * N / 4;
     if ((quads + num_sms() - 1) / num_sms() * 4 > kMoeMaxUnits) return false;
     const size_t gu = 2 * ((size_t)kMoeG * K + (((size_t)kMoeG * (K >> 4) + 15) & ~(size_t)15));
@@ -1483,7 +1495,8 @@ bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k) {
 }
 
 bool decode_phase_fits(const PhaseDesc& p) {
-    if (p.type == PH_MOE) return p.r_qs && p.dt_qs && decode_moe_fits(p.K, p.N, p.n_out, p.n_expert, p.top_k);
+    if (p.type == PH_MOE)
+        return p.dt_qs && (p.r_qs || p.n_expert == 1) && decode_moe_fits(p.K, p.N, p.n_out, p.n_expert, p.top_k);
     if (p.type != PH_GEMV && p.type != PH_DOWN4) {
         if (p.type == PH_ATTN) {
             const int G = p.attn.n_head / p.attn.n_kv, hd = p.attn.hd;
