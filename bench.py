@@ -331,11 +331,69 @@ def run_reference(args, ws, rank):
     print(json.dumps(res), flush=True)
 
 
+def run_moe_block_ep(args, ws, rank, local):
+    """BASELINE config 3 on N GPUs: the LFM2-MoE block expert-parallel (experts sharded evenly,
+    NCCL all-to-all dispatch and combine; qwenqwen3.js_b200/ep.py).  Each rank owns T token
+    rows (weak scaling); one step = one EP forward of every rank's rows."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    qq3 = load_package()
+    qq3.build.build_all()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
+    prefix = "blk.2."
+    names = {prefix + n for n in ("ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                  "ffn_down_exps.weight", "exp_probs_b.bias")}
+    tensors = qq3.synth.build_tensors(spec, only=names)
+    ctx = qq3.runtime.Context(local)
+    block = qq3.ep.EPMoEBlock(ctx, tensors, prefix, spec.n_expert, 4, rank, ws)
+    T = args.tokens
+    stream = torch.cuda.Stream(device=local)
+    with torch.cuda.stream(stream):
+        x = torch.from_numpy(qq3.synth.normal_f32(T * 2048, seed=T + 977 * rank).reshape(T, 2048)).cuda()
+        for _ in range(args.warmup):
+            block.forward(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = block.forward(x)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    q8 = 34 / 32
+    flops = ws * T * (2 * 2048 * 32 + 4 * 3 * 2 * 2048 * 1792)
+    res = {"metric": "tokens/s through the LFM2-MoE block (expert-parallel)", "value": round(ws * T / (ms * 1e-3), 1),
+           "unit": "tokens/s", "n_gpus": ws, "tokens_per_gpu": T, "ms_per_step": round(ms, 4),
+           "tflops": round(flops / (ms * 1e-3) / 1e12, 2), "scaling": "weak", "steps": args.steps,
+           "warmup": args.warmup, "parallelism": f"ep{ws}",
+           "expert_bytes_per_gpu": int(spec.n_expert // ws * 3 * 2048 * 1792 * q8),
+           "path": "route -> NCCL all-to-all (counts, rows, ids) -> grouped tcgen05 expert GEMMs -> "
+                   "NCCL all-to-all back -> slot-order combine",
+           "out_checksum": round(float(out.double().abs().sum()), 3)}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    block.close()
+    dist.destroy_process_group()
+    ctx.close()
+
+
 def run_moe_block(args, ws, rank, local):
     """the isolated LFM2-MoE block on T tokens (also the small case the
     ncu captures use).  One step = one qq_moe_block call over T token rows."""
     import torch
 
+    if ws > 1:
+        run_moe_block_ep(args, ws, rank, local)
+        return
     qq3 = load_package()
     qq3.build.build_all()
     torch.cuda.set_device(local)

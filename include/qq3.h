@@ -217,6 +217,28 @@ int qq_bench_kernel(qq_model* m, int what, int iters, float* ms);
 int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
                  float* out_dev, float* routing_dev);
 
+/* ---------------------------------------------------------------- expert-parallel MoE pieces */
+
+/* No reference counterpart (the JS runs every expert in one process): the three parts of
+ * qq_moe_block a rank of an expert-parallel group calls around its own row exchange (NCCL
+ * all-to-all in the caller), with experts sharded evenly over the ranks.
+ *  qq_moe_route    router logits, sigmoid, top-k and weights of T token rows
+ *                  (lfm2-engine.js:417-447): idx_dev [T][top_k] global expert ids, w_dev
+ *                  [T][top_k], routing_dev (nullable) [T][2*top_k + n_expert] the records.  Uses
+ *                  layer->t[QQ_ROUTER] and [QQ_EXP_BIAS].
+ *  qq_moe_experts  y_dev[r] = down_e(silu(gate_e . x_r) * (up_e . x_r)) for R rows x_dev [R][K],
+ *                  e = eid_dev[r] in 0..n_local-1, the rank's own experts: layer->t[QQ_GATE_EXPS],
+ *                  [QQ_UP_EXPS], [QQ_DOWN_EXPS] hold n_local experts (GGUF [K, F, n_local],
+ *                  [F, K, n_local]).  Unweighted (the weights stay with the token's owner).
+ *  qq_moe_combine  out_dev[t] = sum over slots s (in order) of w_dev[t][s] * y_dev[pos_dev[t][s]]
+ *                  (lfm2-engine.js:459-486), rows of K floats. */
+int qq_moe_route(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
+                 int32_t* idx_dev, float* w_dev, float* routing_dev);
+int qq_moe_experts(qq_ctx* ctx, const qq_layer_desc* layer, int n_local, const float* x_dev, const int32_t* eid_dev,
+                   int R, float* y_dev);
+int qq_moe_combine(qq_ctx* ctx, const float* y_dev, const int32_t* pos_dev, const float* w_dev, int T, int top_k,
+                   int K, float* out_dev);
+
 /* ---------------------------------------------------------------- allocation-free MoE block */
 
 /* No counterpart in the reference.  qq_moe_block without any device allocation, for callers

@@ -11,5 +11,5 @@ Layout:
 
 The directory name is not a Python identifier, so loaders register it as ``qq3``.
 """
-from . import build, gguf, runtime, synth  # noqa: F401
+from . import build, ep, gguf, runtime, synth  # noqa: F401
 from .engine import Lfm2CudaEngine, Qwen3CudaEngine, engine_for  # noqa: F401

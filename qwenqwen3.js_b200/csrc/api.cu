@@ -1449,4 +1449,58 @@ int qq_moe_block(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_
     });
 }
 
+int qq_moe_route(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev, int T,
+                 int32_t* idx_dev, float* w_dev, float* routing_dev) {
+    return guard([&] {
+        need(ctx && layer && x_dev && idx_dev && w_dev && T >= 0, "qq_moe_route: bad argument");
+        const DTensor* router = dt(layer->t[QQ_ROUTER]);
+        const DTensor* bias = dt(layer->t[QQ_EXP_BIAS]);
+        need(router != nullptr, "qq_moe_route: the router tensor is required");
+        check_shape(router, QQ_TYPE_Q8_0, router->ne[0], n_expert, 1, "ffn_gate_inp.weight");
+        if (bias) check_shape(bias, QQ_TYPE_F32, n_expert, 1, 1, "exp_probs_b.bias");
+        if (T == 0) return;
+        DeviceGuard dg(ctx->device);
+        cudaStream_t s = ctx->stream;
+        float* rec = routing_dev;
+        if (!rec) rec = static_cast<float*>(ctx_scratch(ctx, (size_t)T * (2 * top_k + n_expert) * 4));
+        qq3::launch_lfm2_router(*router, bias ? bias->f32 : nullptr, x_dev, T, nullptr, 0.f, n_expert, top_k, rec,
+                                idx_dev, w_dev, s);
+    });
+}
+
+int qq_moe_experts(qq_ctx* ctx, const qq_layer_desc* layer, int n_local, const float* x_dev, const int32_t* eid_dev,
+                   int R, float* y_dev) {
+    return guard([&] {
+        need(ctx && layer && R >= 0 && n_local >= 1 && (R == 0 || (x_dev && eid_dev && y_dev)),
+             "qq_moe_experts: bad argument");
+        const DTensor* gate = dt(layer->t[QQ_GATE_EXPS]);
+        const DTensor* up = dt(layer->t[QQ_UP_EXPS]);
+        const DTensor* down = dt(layer->t[QQ_DOWN_EXPS]);
+        need(gate && up && down, "qq_moe_experts: expert tensors are required");
+        const int64_t K = gate->ne[0], F = gate->ne[1];
+        check_shape(gate, QQ_TYPE_Q8_0, K, F, n_local, "ffn_gate_exps.weight");
+        check_shape(up, QQ_TYPE_Q8_0, K, F, n_local, "ffn_up_exps.weight");
+        check_shape(down, QQ_TYPE_Q8_0, F, K, n_local, "ffn_down_exps.weight");
+        QQ_CHECK(n_local <= 256 && qq3::gemm_q8_supported(*gate) && qq3::gemm_q8_supported(*down) &&
+                     !getenv_flag("QQ3_NO_TCGEN05"),
+                 QQ_ERR_UNSUPPORTED, "qq_moe_experts: needs the tensor-core grouped GEMM");
+        if (R == 0) return;
+        DeviceGuard dg(ctx->device);
+        // each row is its own (token, slot) pair: top_k 1, weight 1
+        void* scratch = ctx_scratch(ctx, qq3::moe_grouped_scratch_bytes(R, 1, n_local, K, F));
+        qq3::launch_moe_grouped(*gate, *up, *down, eid_dev, nullptr, nullptr, x_dev, R, 1, n_local, scratch, y_dev,
+                                ctx->stream);
+    });
+}
+
+int qq_moe_combine(qq_ctx* ctx, const float* y_dev, const int32_t* pos_dev, const float* w_dev, int T, int top_k,
+                   int K, float* out_dev) {
+    return guard([&] {
+        need(ctx && T >= 0 && top_k >= 1 && K >= 1 && (T == 0 || (y_dev && pos_dev && w_dev && out_dev)),
+             "qq_moe_combine: bad argument");
+        DeviceGuard dg(ctx->device);
+        qq3::launch_moe_combine_rows(y_dev, pos_dev, w_dev, T, top_k, K, out_dev, ctx->stream);
+    });
+}
+
 }  // extern "C"

@@ -101,6 +101,9 @@ void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 void launch_transpose_experts(const DTensor& W, int n_expert, int8_t* t_qs, __half* t_d, cudaStream_t s);
 
 // ---- MoE block for T rows regrouped by expert on the tensor cores (kernels_moe_grouped.cu) ----
+// out[t] = sum_s w[t][s] * y[pos[t][s]] (w nullable: weight 1), rows of K floats
+void launch_moe_combine_rows(const float* y, const int* pos, const float* w, int T, int top_k, int K, float* out,
+                             cudaStream_t s);
 size_t moe_grouped_scratch_bytes(int T, int top_k, int n_expert, int64_t K, int64_t F);
 // idx/w: routed ids and weights [T][top_k]; out[T][K] = sum_s w[t][s] * down_e(silu(gate_e x) * up_e x)
 // over the slots whose expert is not set in mask (nullable bitset)

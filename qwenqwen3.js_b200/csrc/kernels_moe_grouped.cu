@@ -83,9 +83,12 @@ __global__ void k_moe_combine(const float* __restrict__ down, const int* __restr
         const int t = (int)(i / K), c = (int)(i % K);
         float acc = 0.f;
         for (int s = 0; s < top_k; s++) {  // slot order; a masked expert is skipped (lfm2-engine.js:459-486)
-            const int e = idx[t * top_k + s];
-            if (mask && ((mask[e >> 5] >> (e & 31)) & 1u)) continue;
-            acc += w[t * top_k + s] * down[(size_t)pos[t * top_k + s] * K + c];
+            if (mask) {
+                const int e = idx[t * top_k + s];
+                if ((mask[e >> 5] >> (e & 31)) & 1u) continue;
+            }
+            const float ws = w ? w[t * top_k + s] : 1.0f;  // no weights: each row of its own
+            acc += ws * down[(size_t)pos[t * top_k + s] * K + c];
         }
         out[i] = acc;
     }
@@ -94,6 +97,13 @@ __global__ void k_moe_combine(const float* __restrict__ down, const int* __restr
 unsigned grid_for(size_t n) { return (unsigned)std::min<size_t>((n + 255) / 256, (size_t)148 * 32); }
 
 }  // namespace
+
+void launch_moe_combine_rows(const float* y, const int* pos, const float* w, int T, int top_k, int K, float* out,
+                             cudaStream_t s) {
+    if (T <= 0) return;
+    k_moe_combine<<<grid_for((size_t)T * K), 256, 0, s>>>(y, pos, w, nullptr, nullptr, T, top_k, K, out);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
 
 size_t moe_grouped_scratch_bytes(int T, int top_k, int n_expert, int64_t K, int64_t F) {
     const size_t P = (size_t)T * top_k;

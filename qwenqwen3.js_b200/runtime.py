@@ -96,6 +96,9 @@ _SIGS = {
     "qq_model_stat": (_I, [_P, _I, C.POINTER(_I64)]),
     "qq_bench_kernel": (_I, [_P, _I, _I, C.POINTER(C.c_float)]),
     "qq_moe_block_noalloc": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
+    "qq_moe_route": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P, _P]),
+    "qq_moe_experts": (_I, [_P, C.POINTER(LayerDesc), _I, _P, _P, _I, _P]),
+    "qq_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
 }
 
 QQ_NOALLOC_MAX_TOKENS = 1024
@@ -180,7 +183,15 @@ class Context:
         except Exception:
             pass
 
+    # cudaStreamLegacy: the legacy default stream, which torch reports as handle 0
+    CUDA_STREAM_LEGACY = 0x1
+
     def set_stream(self, cuda_stream: int | None) -> None:
+        """Run later work on a caller's stream: a cudaStream_t handle (torch's `cuda_stream`),
+        where 0 means the legacy default stream (torch's default stream reports 0) and None the
+        context's own stream.  (The C ABI reads NULL as the context's own stream.)"""
+        if cuda_stream == 0:
+            cuda_stream = self.CUDA_STREAM_LEGACY
         check(self.lib.qq_set_stream(self.h, cuda_stream))
 
     def synchronize(self) -> None:
@@ -210,6 +221,19 @@ class Context:
         """qq_moe_block without device allocation (scratch in the library's fixed device array)."""
         check(self.lib.qq_moe_block_noalloc(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(out_dev),
                                             _ptr(routing_dev)))
+
+
+    # expert-parallel pieces of the MoE block (device pointers; see include/qq3.h)
+    def moe_route(self, layer: LayerDesc, n_expert: int, top_k: int, x_dev, T: int, idx_dev, w_dev,
+                  routing_dev=None) -> None:
+        check(self.lib.qq_moe_route(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(idx_dev),
+                                    _ptr(w_dev), _ptr(routing_dev)))
+
+    def moe_experts(self, layer: LayerDesc, n_local: int, x_dev, eid_dev, R: int, y_dev) -> None:
+        check(self.lib.qq_moe_experts(self.h, C.byref(layer), n_local, _ptr(x_dev), _ptr(eid_dev), R, _ptr(y_dev)))
+
+    def moe_combine(self, y_dev, pos_dev, w_dev, T: int, top_k: int, K: int, out_dev) -> None:
+        check(self.lib.qq_moe_combine(self.h, _ptr(y_dev), _ptr(pos_dev), _ptr(w_dev), T, top_k, K, _ptr(out_dev)))
 
 
 class Tensor:
