@@ -298,7 +298,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         QQ_CUDA_TRY(cudaMemsetAsync(m->dctl, 0, sizeof(DecodeCtl), m->ctx->stream));
     }
     // fused MoE: one accumulated vector (E floats) + counter (padded to 32 words) per MoE layer
-    const size_t aslot = ((size_t)E + 32 + 31) & ~(size_t)31;
+    const size_t aslot = ((size_t)qq3::kAccCopies * E + 32 + 31) & ~(size_t)31;
     if (fuse && !m->aarena) {
         m->aarena_half = aslot * (size_t)d.n_layers;
         m->aarena = dalloc<float>(2 * m->aarena_half);
@@ -451,7 +451,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             QQ_CHECK((size_t)(n_acc + 1) * aslot <= m->aarena_half, QQ_ERR_INVALID,
                      "persistent program: accumulator arena too small");
             g.acc = m->aarena + (size_t)n_acc * aslot;
-            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + E);
+            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + (size_t)qq3::kAccCopies * E);
             ++n_acc;
         };
         auto set_hid_acc = [&](const PhaseDesc& g) {

@@ -123,6 +123,10 @@ constexpr int kMoeDU = 16;
 constexpr int kMoeRows = 16;
 constexpr int kMoeOut = 128 * kMoeRows;
 constexpr int kMoeMaxUnits = 512;  // hidden units one CTA may own
+// Copies of each accumulated vector: CTA c adds into copy c % kAccCopies (fewer same-line
+// reductions contend at L2); a reader sums the copies.  A slot is [kAccCopies][n] floats, then
+// the counter.
+constexpr int kAccCopies = 1;
 
 // Launch one decode step (grid = one CTA per SM).
 void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, int* err, cudaStream_t s);

@@ -515,8 +515,13 @@ __device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ no
             const int e0 = 8 * t + ps * 8 * kConsumerThreads;
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
             if (e0 < K) {
-                a = __ldcg(reinterpret_cast<const float4*>(in.xa + e0));
-                b = __ldcg(reinterpret_cast<const float4*>(in.xa + e0 + 4));
+#pragma unroll
+                for (int c = 0; c < kAccCopies; c++) {  // the copies of the accumulated vector
+                    const float4 ca = __ldcg(reinterpret_cast<const float4*>(in.xa + (size_t)c * K + e0));
+                    const float4 cb = __ldcg(reinterpret_cast<const float4*>(in.xa + (size_t)c * K + e0 + 4));
+                    a.x += ca.x; a.y += ca.y; a.z += ca.z; a.w += ca.w;
+                    b.x += cb.x; b.y += cb.y; b.z += cb.z; b.w += cb.w;
+                }
             }
             xv[ps][0] = a.x; xv[ps][1] = a.y; xv[ps][2] = a.z; xv[ps][3] = a.w;
             xv[ps][4] = b.x; xv[ps][5] = b.y; xv[ps][6] = b.z; xv[ps][7] = b.w;
@@ -550,12 +555,9 @@ __device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ no
             for (int e = 0; e < 8; e++) ss += (double)xv[ps][e] * xv[ps][e];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if ((t & 31) == 0) red[t >> 5] = ss;
-        named_bar(1, kConsumerThreads);
-        double tot = 0.0;
-#pragma unroll
-        for (int w = 0; w < kCW; w++) tot += red[w];
-        const float inv = (float)(1.0 / sqrt(tot / (double)K + (double)eps));
+        if ((t & 31) == 0) red[t >> 5] = ss;  // stage_scale() sums the warps' parts after the barrier
+        // the digits are of w.x: the common factor 1/rms scales the dot products instead, so
+        // the digits need not wait for the CTA-wide sum
 #pragma unroll
         for (int ps = 0; ps < 4; ps++) {
             const int e0 = 8 * t + ps * 8 * kConsumerThreads;
@@ -563,7 +565,7 @@ __device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ no
                 const float4 wa = nw[ps][0], wb = nw[ps][1];
                 const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-                for (int e = 0; e < 8; e++) xv[ps][e] = (wv[e] * xv[ps][e]) * inv;
+                for (int e = 0; e < 8; e++) xv[ps][e] = wv[e] * xv[ps][e];
             }
         }
     }
@@ -572,6 +574,17 @@ __device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ no
         const int e0 = 8 * t + ps * 8 * kConsumerThreads;
         if (ps * 8 * kConsumerThreads < K) digitise8(xv[ps], e0, K, dig, xsc);
     }
+}
+
+// The RMSNorm factor 1/sqrt(mean(x^2) + eps) of the staged input (tensor.js:103-114, the sum in
+// double), from the warps' partial sums; valid after the barrier that follows the staging.
+// Without a fused norm the scale is 1.
+__device__ __forceinline__ float stage_scale(const double* red, const float* norm_w, int K, float eps) {
+    if (!norm_w) return 1.0f;
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < kCW; w++) tot += red[w];
+    return (float)(1.0 / sqrt(tot / (double)K + (double)eps));
 }
 
 // 24 dp4a of one 32-weight Q8_0 block (w0 | w1) against its three digit planes, combined in
@@ -710,7 +723,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g * (1.0f /
 // lfm2-engine.js:417-447: logits = W_router . norm(h); p = sigmoid(logits); top-k on p + bias
 // (stable: the lower expert id wins a tie); weights = p / (sum + 1e-6).
 __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
-                          int nch, float bias_v, DecRoute* route, int* err) {
+                          float sc, int nch, float bias_v, DecRoute* route, int* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.K, ne = p.n_expert;
     const int set = warp / 4, w = warp % 4;
@@ -732,7 +745,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
         }
         float acc[4];
         rows_dot<4>(q, d, dig, xsc, nch, nch, acc);
-        const float sum = warp_reduce_rows<4>(acc);
+        const float sum = warp_reduce_rows<4>(acc) * sc;
         __syncwarp();
         if (lane == 0) mbar_arrive(&r.empty[slot]);
         const int j = lane >> 3;
@@ -794,8 +807,8 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
 // NR = S IPW <= 4 rows (item-major, source-minor), so its row dots and reductions overlap.
 template <int S, int IPW>
 __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R, const DecRing& r, uint32_t& i,
-                                          const uint4* dig, const float* xsc, uint32_t tag_out, uint32_t tag_res,
-                                          const float* ra, unsigned long long& best_k, int* err) {
+                                          const uint4* dig, const float* xsc, float sc, uint32_t tag_out,
+                                          uint32_t tag_res, const float* ra, unsigned long long& best_k, int* err) {
     constexpr int NR = S * IPW;
     constexpr int NRP = NR == 3 ? 4 : (NR > 4 ? 8 : NR);  // rows padded for the halving reduction
     constexpr int SH = NRP == 8 ? 2 : (NRP == 4 ? 3 : (NRP == 2 ? 4 : 5));  // lane >> SH = row of the sum
@@ -830,7 +843,12 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
         if (mine) {
             if (epi == EK_RESID) {
                 // an accumulated residual is complete: its counter was awaited while staging
-                pre[0] = ra ? __ldcg(ra + item) : wait_tw(p.res + item, tag_res, err);
+                if (ra) {
+#pragma unroll
+                    for (int c = 0; c < kAccCopies; c++) pre[0] += __ldcg(ra + (size_t)c * R.n_items + item);
+                } else {
+                    pre[0] = wait_tw(p.res + item, tag_res, err);
+                }
             } else if (epi == EK_CONV) {
                 pre[0] = p.state[item];
                 pre[1] = p.state[p.E + item];
@@ -850,7 +868,7 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
         }
         float acc[NRP];
         rows_dot<NRP>(q, d, dig, xsc, nch, nch, acc);
-        const float a0 = warp_reduce_rows<NRP>(acc);
+        const float a0 = warp_reduce_rows<NRP>(acc) * sc;
         const float a1 = S > 1 ? __shfl_down_sync(0xffffffffu, a0, 1 << SH) : 0.f;
         const float a2 = S > 2 ? __shfl_down_sync(0xffffffffu, a0, 2 << SH) : 0.f;
         __syncwarp();
@@ -975,7 +993,7 @@ __device__ __forceinline__ void moe_down_seg(const uint8_t* q, int EO, const flo
 
 // scratch: raw input [kMoeOut] (written by the staging), set-1 partials [kMoeOut], h [kMoeMaxUnits]
 __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
-                          const DecRoute* route, float* scratch, float* acc_out, unsigned* cnt, int* err) {
+                          float sc, const DecRoute* route, float* scratch, float* acc_out, unsigned* cnt, int* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int set = warp / 4, w = warp % 4;
     const int K = p.K, nch = K >> 4, N = p.N, EO = p.n_out;
@@ -1013,7 +1031,7 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
                     }
                     float a[NR];
                     rows_dot<NR>(q, d, dig, xsc, nch, nch, a);
-                    const float a0 = warp_reduce_rows<NR>(a);
+                    const float a0 = warp_reduce_rows<NR>(a) * sc;
                     const float a1 = __shfl_down_sync(0xffffffffu, a0, 1 << SH);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&r.empty[slot]);
@@ -1079,7 +1097,7 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     }
     named_bar(1, kConsumerThreads);
     if (threadIdx.x == 0) {
-        bulk_add_f32_s2g(acc_out, comb, (uint32_t)EO * 4u);  // returns once the sums are performed
+        bulk_add_f32_s2g(acc_out + (size_t)(blockIdx.x % kAccCopies) * EO, comb, (uint32_t)EO * 4u);  // returns once performed
         __threadfence();
         atomicAdd(cnt, 1u);
     }
@@ -1381,22 +1399,23 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
             dec_stage_digits(stage_in(p, epoch, aoff), p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
-            if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
+            const float sc = stage_scale(red, p.norm_w, K, p.eps);
+            if (p.r_qs) dec_route(p, r, i, dig, xsc, sc, nch, bias_v, &route, err);
             const float* ra = p.ra ? p.ra + aoff : nullptr;
             PhaseRegs R;
             load_phase(&p, R, expert_map(p.map) ? &route : nullptr);
             unsigned long long best_k = 0ull;
             const int ipw = R.G / 4;
             const uint32_t tres = step_tag(epoch, p.res_ph);
-            if (R.S == 1 && ipw == 8) consume_a<1, 8>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 2 && ipw == 4) consume_a<2, 4>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else if (R.S == 3 && ipw == 2) consume_a<3, 2>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
-            else consume_a<3, 1>(p, R, r, i, dig, xsc, tag, tres, ra, best_k, err);
+            if (R.S == 1 && ipw == 8) consume_a<1, 8>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 1 && ipw == 4) consume_a<1, 4>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 1 && ipw == 2) consume_a<1, 2>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 1) consume_a<1, 1>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 2 && ipw == 4) consume_a<2, 4>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 2 && ipw == 2) consume_a<2, 2>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else if (R.S == 3 && ipw == 2) consume_a<3, 2>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            else consume_a<3, 1>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
             if (p.epi == EK_ARGMAX) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -1423,8 +1442,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             in.raw = scratch;
             dec_stage_digits(in, p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
-            if (p.r_qs) dec_route(p, r, i, dig, xsc, nch, bias_v, &route, err);
-            moe_fused(p, r, i, dig, xsc, &route, scratch, p.acc + aoff, p.acc_cnt + aoff, err);
+            const float sc = stage_scale(red, p.norm_w, K, p.eps);
+            if (p.r_qs) dec_route(p, r, i, dig, xsc, sc, nch, bias_v, &route, err);
+            moe_fused(p, r, i, dig, xsc, sc, &route, scratch, p.acc + aoff, p.acc_cnt + aoff, err);
         } else if (p.type == PH_DOWN4) {
             if ((int)blockIdx.x >= (p.n_items + kG - 1) / kG) continue;
             PhaseRegs R;
