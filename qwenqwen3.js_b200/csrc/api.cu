@@ -75,9 +75,12 @@ struct Layer {
     bool attn = false, moe = false;
     const DTensor* t[QQ_SLOT_COUNT] = {nullptr};
     int attn_slot = -1, moe_slot = -1;
-    // the expert down tensor transposed for the fused decode MoE (owned; built on first use)
+    // the FFN down tensor (experts) and the short-conv out_proj transposed for the fused phases
+    // of the persistent decode step (owned; built on first use)
     int8_t* dt_qs = nullptr;
     __half* dt_d = nullptr;
+    int8_t* ot_qs = nullptr;
+    __half* ot_d = nullptr;
 };
 
 struct qq_model {
@@ -147,10 +150,12 @@ void free_model(qq_model* m) {
     if (m->tarena) cudaFree(m->tarena);
     if (m->aarena) cudaFree(m->aarena);
     for (Layer& L : m->layers) {
-        if (L.dt_qs) cudaFree(L.dt_qs);
-        if (L.dt_d) cudaFree(L.dt_d);
+        for (void* q : {(void*)L.dt_qs, (void*)L.dt_d, (void*)L.ot_qs, (void*)L.ot_d})
+            if (q) cudaFree(q);
         L.dt_qs = nullptr;
         L.dt_d = nullptr;
+        L.ot_qs = nullptr;
+        L.ot_d = nullptr;
     }
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
                     m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
@@ -278,6 +283,16 @@ bool ffn_fused(const qq_model* m, const Layer& L) {
                                        : qq3::decode_moe_fits(d.n_embd, F, d.n_embd, 1, 1));
 }
 
+// Whether the short-conv block of layer L (in_proj, conv, out_proj) runs as one fused phase;
+// QQ3_CONV_FUSED=0 keeps two phases (in_proj + conv, then out_proj).
+bool conv_fused(const qq_model* m, const Layer& L) {
+    const char* env = getenv("QQ3_CONV_FUSED");
+    if ((env && atoi(env) == 0) || L.attn || !L.t[QQ_IN_PROJ] || !L.t[QQ_OUT_PROJ] || !L.t[QQ_CONV]) return false;
+    const int E = m->d.n_embd;
+    return L.t[QQ_IN_PROJ]->ne[1] == 3 * E && L.t[QQ_OUT_PROJ]->K == E && L.t[QQ_OUT_PROJ]->rows == E &&
+           qq3::decode_moe_fits(E, E, E, 1, 1, 3);
+}
+
 // The decode step as a phase program for the persistent kernel (kernels_decode.cu); the same
 // sequence of operations as enqueue_step.  Each phase writes its own tagged output buffer and
 // names the phase that wrote each vector it reads.
@@ -286,7 +301,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     const qq_model_desc& d = m->d;
     const int E = d.n_embd, hd = d.head_dim, nq = d.n_head * hd, nkv = d.n_head_kv * hd;
     bool fuse = false;  // any fused FFN phase (they need the accumulator arena)
-    for (const Layer& L : m->layers) fuse = fuse || ffn_fused(m, L);
+    for (const Layer& L : m->layers) fuse = fuse || ffn_fused(m, L) || conv_fused(m, L);
     if (!m->tarena) {
         m->tarena_len = tarena_bound(m);
         m->tarena = dalloc<tword>(m->tarena_len);
@@ -300,7 +315,7 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
     // fused MoE: one accumulated vector (E floats) + counter (padded to 32 words) per MoE layer
     const size_t aslot = ((size_t)qq3::kAccCopies * E + 32 + 31) & ~(size_t)31;
     if (fuse && !m->aarena) {
-        m->aarena_half = aslot * (size_t)d.n_layers;
+        m->aarena_half = aslot * (size_t)d.n_layers * 2;  // up to two fused phases per layer
         m->aarena = dalloc<float>(2 * m->aarena_half);
         cudaStream_t s = m->ctx->stream;
         QQ_CUDA_TRY(cudaMemsetAsync(m->aarena, 0, sizeof(float) * 2 * m->aarena_half, s));
@@ -309,11 +324,18 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->arena, &a, sizeof(a), cudaMemcpyHostToDevice, s));
         QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->arena_half, &h, sizeof(h), cudaMemcpyHostToDevice, s));
         for (Layer& L : m->layers) {
-            if (!ffn_fused(m, L) || L.dt_qs) continue;
-            const DTensor& W = *L.t[L.moe ? QQ_DOWN_EXPS : QQ_FFN_DOWN];
-            L.dt_qs = dalloc<int8_t>((size_t)W.rows * W.K);
-            L.dt_d = dalloc<__half>((size_t)W.rows * (W.K / 32));
-            qq3::launch_transpose_experts(W, L.moe ? d.n_expert : 1, L.dt_qs, L.dt_d, s);
+            if (ffn_fused(m, L) && !L.dt_qs) {
+                const DTensor& W = *L.t[L.moe ? QQ_DOWN_EXPS : QQ_FFN_DOWN];
+                L.dt_qs = dalloc<int8_t>((size_t)W.rows * W.K);
+                L.dt_d = dalloc<__half>((size_t)W.rows * (W.K / 32));
+                qq3::launch_transpose_experts(W, L.moe ? d.n_expert : 1, L.dt_qs, L.dt_d, s);
+            }
+            if (conv_fused(m, L) && !L.ot_qs) {
+                const DTensor& W = *L.t[QQ_OUT_PROJ];
+                L.ot_qs = dalloc<int8_t>((size_t)W.rows * W.K);
+                L.ot_d = dalloc<__half>((size_t)W.rows * (W.K / 32));
+                qq3::launch_transpose_experts(W, 1, L.ot_qs, L.ot_d, s);
+            }
         }
         QQ_CUDA_TRY(cudaStreamSynchronize(s));  // the pointers above are host locals
     }
@@ -399,6 +421,19 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
         const Layer& L = m->layers[l];
         const float* an = L.t[QQ_ATTN_NORM]->f32;
         const float* fn = L.t[QQ_FFN_NORM]->f32;
+        auto take_acc = [&](PhaseDesc& g) {
+            QQ_CHECK((size_t)(n_acc + 1) * aslot <= m->aarena_half, QQ_ERR_INVALID,
+                     "persistent program: accumulator arena too small");
+            g.acc = m->aarena + (size_t)n_acc * aslot;
+            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + (size_t)qq3::kAccCopies * E);
+            ++n_acc;
+        };
+        auto set_hid_acc = [&](const PhaseDesc& g) {
+            hid = Ref();
+            hid.a = g.acc;
+            hid.c = g.acc_cnt;
+            hid.n = qq3::num_sms();  // every CTA of the grid counts once
+        };
         if (L.attn) {
             PhaseDesc q = gemv(MK_CONCAT3, EK_STORE, 1, E, nq + 2 * nkv, hid, an);
             set_src(q, 0, L.t[QQ_WQ]);
@@ -433,6 +468,24 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             set_src(o, 0, L.t[QQ_WO]);
             resid(o);
             push_hid(o);
+        } else if (conv_fused(m, L) && L.ot_qs) {
+            // in_proj + conv + out_proj as one phase over channels, accumulated (+ residual)
+            PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, hid, an);
+            c.type = PH_FUSED;
+            set_src(c, 0, L.t[QQ_IN_PROJ]);
+            c.stride = E;
+            c.conv_w = L.t[QQ_CONV]->f32;
+            c.state = m->conv(seq, l);
+            c.E = E;
+            c.N = E;
+            c.n_expert = 1;
+            c.top_k = 1;
+            c.dt_qs = L.ot_qs;
+            c.dt_d = L.ot_d;
+            c.n_out = E;
+            take_acc(c);
+            prog.push_back(c);
+            set_hid_acc(c);
         } else {
             PhaseDesc c = gemv(MK_STRIDE3, EK_CONV, 3, E, E, hid, an);
             set_src(c, 0, L.t[QQ_IN_PROJ]);
@@ -447,23 +500,10 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             resid(o);
             push_hid(o);
         }
-        auto take_acc = [&](PhaseDesc& g) {
-            QQ_CHECK((size_t)(n_acc + 1) * aslot <= m->aarena_half, QQ_ERR_INVALID,
-                     "persistent program: accumulator arena too small");
-            g.acc = m->aarena + (size_t)n_acc * aslot;
-            g.acc_cnt = reinterpret_cast<unsigned*>(g.acc + (size_t)qq3::kAccCopies * E);
-            ++n_acc;
-        };
-        auto set_hid_acc = [&](const PhaseDesc& g) {
-            hid = Ref();
-            hid.a = g.acc;
-            hid.c = g.acc_cnt;
-            hid.n = qq3::num_sms();  // every CTA of the grid counts once
-        };
-        if (!L.moe && ffn_fused(m, L) && hid.t && L.dt_qs) {
+        if (!L.moe && ffn_fused(m, L) && L.dt_qs) {
             const int F = (int)L.t[QQ_FFN_GATE]->ne[1];
             PhaseDesc g = gemv(MK_PAIR, EK_STORE, 2, E, F, hid, fn);
-            g.type = PH_MOE;  // without a router (r_qs null): one expert of weight 1
+            g.type = PH_FUSED;  // without a router (r_qs null): one expert of weight 1
             g.G = kMoeG;
             set_src(g, 0, L.t[QQ_FFN_GATE]);
             set_src(g, 1, L.t[QQ_FFN_UP]);
@@ -476,11 +516,11 @@ std::vector<qq3::PhaseDesc> build_program(qq_model* m, int seq, bool want_logits
             take_acc(g);
             prog.push_back(g);
             set_hid_acc(g);
-        } else if (L.moe && ffn_fused(m, L) && hid.t && L.dt_qs) {
+        } else if (L.moe && ffn_fused(m, L) && L.dt_qs) {
             const int k = d.n_expert_used;
             const int F = (int)L.t[QQ_GATE_EXPS]->ne[1];
             PhaseDesc g = gemv(MK_EXPERT_PAIR, EK_STORE, 2, E, k * F, hid, fn);
-            g.type = PH_MOE;
+            g.type = PH_FUSED;
             g.G = kMoeG;
             set_src(g, 0, L.t[QQ_GATE_EXPS]);
             set_src(g, 1, L.t[QQ_UP_EXPS]);
@@ -1335,7 +1375,7 @@ int qq_model_stat(qq_model* m, int what, int64_t* value) {
                 } else {
                     std::vector<qq3::PhaseDesc> h(pr.n);
                     QQ_CUDA_TRY(cudaMemcpy(h.data(), pr.d_prog, sizeof(qq3::PhaseDesc) * pr.n, cudaMemcpyDeviceToHost));
-                    for (const auto& p : h) n += p.type == qq3::PH_MOE && p.r_qs ? 1 : 0;
+                    for (const auto& p : h) n += p.type == qq3::PH_FUSED && p.r_qs ? 1 : 0;
                 }
             }
             *value = n;

@@ -7,7 +7,7 @@
 // synchronisation between CTAs; every phase writes its own output buffer, so no word is
 // written twice in one step.
 //
-// A fused MoE phase (PH_MOE) instead sums partial outputs of every CTA into an accumulated
+// A fused phase (PH_FUSED) instead sums partial outputs of every CTA into an accumulated
 // vector (a bulk f32 add-reduction at L2 per CTA) and counts the CTAs that are done in a
 // counter next to it; a reader waits for the counter before it reads the vector.  Accumulated vectors and counters live in
 // an arena of two halves: step `epoch` uses half (epoch & 1) and zeroes the other half, which
@@ -27,8 +27,9 @@ enum PhaseType : int {
     PH_DOWN4 = 2,   // MoE down + combine + residual over the 4 routed experts (consumer mode B)
     PH_ATTN = 3,    // GQA decode attention with QK-norm, RoPE and KV append
     PH_FINISH = 4,  // token = argmax, pos += 1, trace
-    PH_MOE = 5,     // router + expert gate/up + SwiGLU + down + combine + residual, one phase
-                    // (a dense FFN: the same without the router, as one expert of weight 1)
+    PH_FUSED = 5,   // a layer half split over units, outputs accumulated: an FFN (router + expert
+                    // gate/up + SwiGLU + down + combine + residual; a dense FFN as one expert of
+                    // weight 1), or a short-conv block (in_proj + conv + out_proj + residual)
 };
 
 enum MapKind : int { MK_ROWS = 0, MK_CONCAT3 = 1, MK_PAIR = 2, MK_STRIDE3 = 3, MK_EXPERT_PAIR = 4, MK_DOWN4 = 5 };
@@ -88,7 +89,7 @@ struct PhaseDesc {
     int ra_n;
     const float* ra;         // residual read instead of res by EK_RESID (nullable)
     const unsigned* ra_cnt;
-    // PH_MOE: the expert down tensor transposed, and the accumulated output
+    // PH_FUSED: the expert down tensor transposed, and the accumulated output
     const int8_t* dt_qs;     // [n_expert][N][n_out] int8: row j of expert e = column j of its down
     const __half* dt_d;      // [n_expert][N/32][n_out] block scales
     float* acc;              // [n_out] sum over CTAs (+ the residual), zero at the start of the step
@@ -119,6 +120,7 @@ constexpr int kDecAttnBytes = 20 * 1024;
 // Fused MoE phase: hidden units per gate/up stage and per down stage, rows of the output per
 // consumer thread (the 128 threads of a consumer set cover n_out = 2048).
 constexpr int kMoeG = 16;
+constexpr int kConvG = 8;  // units per first-part stage of a fused short-conv phase (3 rows each)
 constexpr int kMoeDU = 16;
 constexpr int kMoeRows = 16;
 constexpr int kMoeOut = 128 * kMoeRows;
@@ -132,8 +134,9 @@ constexpr int kAccCopies = 1;
 void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, int* err, cudaStream_t s);
 // Items per stage for a streamed phase (a power of two >= 4 dividing n_div when possible).
 int decode_stage_items(int S, int K, int n_div, int n_total);
-// Whether a fused MoE phase of these shapes fits (input K, N hidden units per expert, n_out).
-bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k);
+// Whether a fused phase of these shapes fits (input K, N units per expert, n_out outputs; S = 2
+// sources per unit for an FFN, 3 for a short-conv layer).
+bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k, int S = 2);
 // Whether a phase fits the persistent kernel's shared-memory plan.
 bool decode_phase_fits(const PhaseDesc& p);
 

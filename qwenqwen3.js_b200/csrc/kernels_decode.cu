@@ -120,7 +120,7 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
-__device__ __forceinline__ bool streamed(int type) { return type == PH_GEMV || type == PH_DOWN4 || type == PH_MOE; }
+__device__ __forceinline__ bool streamed(int type) { return type == PH_GEMV || type == PH_DOWN4 || type == PH_FUSED; }
 
 // Bounded wait until the counter of an accumulated vector reaches n (acquire: the vector's
 // reductions, published by the writers' fences before they counted, are visible afterwards).
@@ -329,19 +329,29 @@ __device__ __forceinline__ bool ffn_skip(const PhaseDesc* pp, const DecRoute* ro
     return pp->r_qs && dec_masked(pp->mask, route->id[s]);
 }
 
-// The stages of this CTA's run of a fused MoE phase, in consumption order: first the gate and
-// up rows of its hidden units (kMoeG units a stage, never straddling two experts), then the
-// same units' rows of the transposed down tensor with the block scales they need (kMoeDU units
-// a stage).  A masked expert's stages carry no bytes.
-__device__ __forceinline__ bool moe_produce(const PhaseDesc* pp, const DecRing& r, const DecRoute* route,
-                                            ProdRing& pr, uint64_t pol, int* err) {
+// First-part sources of a fused phase: the SwiGLU form (an FFN) dots a unit's gate and up rows,
+// the short-conv form its B, C and x rows of in_proj (rows j, j + E, j + 2E).
+__device__ __forceinline__ int fused_sources(const PhaseDesc* pp) { return pp->epi == EK_CONV ? 3 : 2; }
+__device__ __forceinline__ int fused_stage_units(int S) { return S == 3 ? kConvG : kMoeG; }
+__device__ __forceinline__ int64_t fused_row(const PhaseDesc* pp, int src, int e, int j) {
+    return pp->epi == EK_CONV ? (int64_t)j + (int64_t)src * pp->stride : (int64_t)e * pp->N + j;
+}
+
+// The stages of this CTA's run of a fused phase, in consumption order: first the S source rows
+// of its units (G units a stage, never straddling two experts), then the same units' rows of
+// the transposed second matrix (down, or out_proj) with the block scales they need (kMoeDU
+// units a stage).  A masked expert's stages carry no bytes.
+__device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing& r, const DecRoute* route,
+                                              ProdRing& pr, uint64_t pol, int* err) {
     const int K = pp->K, N = pp->N, EO = pp->n_out;
+    const int S = fused_sources(pp), G = fused_stage_units(S);
+    const bool conv = pp->epi == EK_CONV;
     int u0, u1;
     moe_range(pp->top_k * N, u0, u1);
-    const uint32_t qsz = qs_stride(kMoeG, K), dsz = d_stride(kMoeG, K), need = stage_bytes(2, kMoeG, K);
+    const uint32_t qsz = qs_stride(G, K), dsz = d_stride(G, K), need = stage_bytes(S, G, K);
     const int64_t KS = K >> 5;
     for (int u = u0; u < u1; ++pr.i) {
-        const int n = moe_stage_len(u, u1, N, kMoeG);
+        const int n = moe_stage_len(u, u1, N, G);
         const int s = u / N, j = u - s * N;
         const int e = ffn_expert(pp, route, s);
         const bool on = !ffn_skip(pp, route, s);
@@ -349,13 +359,17 @@ __device__ __forceinline__ bool moe_produce(const PhaseDesc* pp, const DecRing& 
         uint8_t* sb;
         if (!pr.alloc(r, need, err, slot, sb)) return false;
         const uint32_t qb = (uint32_t)n * K, db = round16((uint32_t)n * (K >> 4));
-        mbar_arrive_expect_tx(&r.full[slot], on ? 2u * (qb + db) : 0u);
+        mbar_arrive_expect_tx(&r.full[slot], on ? (uint32_t)S * (qb + db) : 0u);
         if (on) {
-            const int64_t row = (int64_t)e * N + j;
-            weight_g2s(sb, pp->qs[0] + row * K, qb, &r.full[slot], pol);
-            weight_g2s(sb + qsz, pp->qs[1] + row * K, qb, &r.full[slot], pol);
-            weight_g2s(sb + 2 * qsz, pp->d[0] + row * KS, db, &r.full[slot], pol);
-            weight_g2s(sb + 2 * qsz + dsz, pp->d[1] + row * KS, db, &r.full[slot], pol);
+#pragma unroll
+            for (int src = 0; src < 3; src++) {
+                if (src >= S) break;
+                const int64_t row = fused_row(pp, src, e, j);
+                const int8_t* q = conv ? pp->qs[0] : pp->qs[src];
+                const __half* d = conv ? pp->d[0] : pp->d[src];
+                weight_g2s(sb + src * qsz, q + row * K, qb, &r.full[slot], pol);
+                weight_g2s(sb + S * qsz + src * dsz, d + row * KS, db, &r.full[slot], pol);
+            }
         }
         u += n;
     }
@@ -388,7 +402,7 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
         const PhaseDesc* pp = prog + ph;
         if (!streamed(pp->type)) continue;
         const bool ex = expert_map(pp->map);
-        if (pp->r_qs && (pp->map == MK_EXPERT_PAIR || pp->type == PH_MOE)) {  // a phase with a router
+        if (pp->r_qs && (pp->map == MK_EXPERT_PAIR || pp->type == PH_FUSED)) {  // a phase with a router
             // The router rows go first, as two stages of up to 16 rows (one per consumer set).
             const int K = pp->K, ne = pp->n_expert;
             for (int h = 0; h < 2; ++h, ++pr.i) {
@@ -407,7 +421,7 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                 uint32_t budget = kRoutePrefetchBytes;
                 for (int ph2 = ph + 1; ph2 < n_phases && budget > 0; ph2++) {
                     const PhaseDesc* p2 = prog + ph2;
-                    if (p2->type == PH_MOE || p2->type == PH_DOWN4 || p2->map == MK_EXPERT_PAIR) break;
+                    if (p2->type == PH_FUSED || p2->type == PH_DOWN4 || p2->map == MK_EXPERT_PAIR) break;
                     if (p2->type == PH_GEMV) budget = prefetch_phase_l2(p2, budget);
                 }
             }
@@ -416,8 +430,8 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
             if (!slot_wait(&route->bar, routed & 1u, err, kProducerBackoffNs)) goto drain;
             ++routed;
         }
-        if (pp->type == PH_MOE) {
-            if (!moe_produce(pp, r, route, pr, pol, err)) goto drain;
+        if (pp->type == PH_FUSED) {
+            if (!fused_produce(pp, r, route, pr, pol, err)) goto drain;
             continue;
         }
         {
@@ -991,6 +1005,80 @@ __device__ __forceinline__ void moe_down_seg(const uint8_t* q, int EO, const flo
     }
 }
 
+// First part of a fused phase: the stages of the CTA's units [u0, u1); warp w of a stage's set
+// dots units IPW w .. IPW w + IPW - 1 (their S rows interleaved) and the lane holding a unit's
+// first sum writes the unit's value to hbuf: w_slot * silu(gate . x) * (up . x) for an FFN
+// (tensor.js:168-180), or for a short-conv channel C * (k0 s0 + k1 s1 + k2 (B . x)) with the
+// conv state shifted (lfm2-engine.js:294-321).  False after a failed wait.
+template <int S, int IPW>
+__device__ __forceinline__ bool fused_part1(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig,
+                                            const float* xsc, float sc, const DecRoute* route, int u0, int u1,
+                                            float* hbuf, int* err) {
+    constexpr int G = 4 * IPW, NR = S * IPW;
+    constexpr int NRP = NR == 3 ? 4 : (NR > 4 ? 8 : NR);  // rows padded for the halving reduction
+    constexpr int SH = NRP == 8 ? 2 : (NRP == 4 ? 3 : (NRP == 2 ? 4 : 5));  // lane >> SH = row of the sum
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int set = warp / 4, w = warp % 4;
+    const int K = p.K, nch = K >> 4, N = p.N;
+    const uint32_t qsz = qs_stride(G, K), dsz = d_stride(G, K);
+    const int row = lane >> SH;
+    const bool lead = (lane & ((1 << SH) - 1)) == 0 && row < NR && row % S == 0;
+    const int my_j = w * IPW + row / S;
+    bool ok = true;
+    for (int u = u0; u < u1; ++i) {
+        const int n = moe_stage_len(u, u1, N, G);
+        const int s = u / N;
+        if ((int)(i % kSets) == set && ok) {
+            const int slot = i % kDecSlots;
+            const bool mine = lead && my_j < n;
+            const int ch = u - s * N + my_j;  // the unit within its expert (a conv channel)
+            float pre[5] = {0.f, 0.f, 0.f, 0.f, 0.f};  // conv state and taps, requested before the wait
+            if (S == 3 && mine) {
+                pre[0] = p.state[ch];
+                pre[1] = p.state[p.E + ch];
+                pre[2] = p.conv_w[ch * 3];
+                pre[3] = p.conv_w[ch * 3 + 1];
+                pre[4] = p.conv_w[ch * 3 + 2];
+            }
+            ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
+            if (ok) {
+                const uint8_t* sb = r.base + r.off[slot];
+                const int8_t* q[NRP];
+                const __half* d[NRP];
+#pragma unroll
+                for (int j = 0; j < NRP; j++) {
+                    const int jj = j < NR ? j : 0;
+                    const int li = w * IPW + jj / S, src = jj % S;
+                    q[j] = reinterpret_cast<const int8_t*>(sb + src * qsz) + (size_t)li * K;
+                    d[j] = reinterpret_cast<const __half*>(sb + S * qsz + src * dsz) + li * (K >> 5);
+                }
+                float a[NRP];
+                rows_dot<NRP>(q, d, dig, xsc, nch, nch, a);
+                const float a0 = warp_reduce_rows<NRP>(a) * sc;
+                const float a1 = __shfl_down_sync(0xffffffffu, a0, 1 << SH);
+                const float a2 = S > 2 ? __shfl_down_sync(0xffffffffu, a0, 2 << SH) : 0.f;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&r.empty[slot]);
+                if (mine) {
+                    float h;
+                    if (S == 3) {
+                        const float bx = a0 * a2;
+                        const float co = pre[2] * pre[0] + pre[3] * pre[1] + pre[4] * bx;
+                        p.state[ch] = pre[1];
+                        p.state[p.E + ch] = bx;
+                        h = a1 * co;
+                    } else {
+                        h = ffn_skip(&p, route, s) ? 0.f : silu_mul(a0, a1) * (p.r_qs ? route->w[s] : 1.0f);
+                    }
+                    hbuf[u - u0 + my_j] = h;
+                }
+            }
+        }
+        u += n;
+    }
+    return ok;
+}
+
 // scratch: raw input [kMoeOut] (written by the staging), set-1 partials [kMoeOut], h [kMoeMaxUnits]
 __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
                           float sc, const DecRoute* route, float* scratch, float* acc_out, unsigned* cnt, int* err) {
@@ -1002,47 +1090,9 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     float* hbuf = comb + kMoeOut;
     int u0, u1;
     moe_range(p.top_k * N, u0, u1);
-    bool ok = true;
-    // gate/up: warp w of the stage's set dots items IPW w .. IPW w + IPW - 1 (gate and up rows
-    // interleaved)
-    {
-        constexpr int IPW = kMoeG / 4, NR = 2 * IPW;
-        constexpr int SH = NR == 8 ? 2 : (NR == 4 ? 3 : 4);  // lane >> SH = row of the sum
-        static_assert(NR == 2 || NR == 4 || NR == 8, "kMoeG");
-        const uint32_t qsz = qs_stride(kMoeG, K), dsz = d_stride(kMoeG, K);
-        const int row = lane >> SH;
-        const bool lead = (lane & ((1 << SH) - 1)) == 0 && (row & 1) == 0;
-        const int my_j = w * IPW + (row >> 1);
-        for (int u = u0; u < u1; ++i) {
-            const int n = moe_stage_len(u, u1, N, kMoeG);
-            const int s = u / N;
-            if ((int)(i % kSets) == set && ok) {
-                const int slot = i % kDecSlots;
-                ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
-                if (ok) {
-                    const uint8_t* sb = r.base + r.off[slot];
-                    const int8_t* q[NR];
-                    const __half* d[NR];
-#pragma unroll
-                    for (int j = 0; j < NR; j++) {
-                        const int li = w * IPW + (j >> 1), src = j & 1;
-                        q[j] = reinterpret_cast<const int8_t*>(sb + src * qsz) + (size_t)li * K;
-                        d[j] = reinterpret_cast<const __half*>(sb + 2 * qsz + src * dsz) + li * (K >> 5);
-                    }
-                    float a[NR];
-                    rows_dot<NR>(q, d, dig, xsc, nch, nch, a);
-                    const float a0 = warp_reduce_rows<NR>(a) * sc;
-                    const float a1 = __shfl_down_sync(0xffffffffu, a0, 1 << SH);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&r.empty[slot]);
-                    if (lead && my_j < n)
-                        hbuf[u - u0 + my_j] =
-                            ffn_skip(&p, route, s) ? 0.f : silu_mul(a0, a1) * (p.r_qs ? route->w[s] : 1.0f);
-                }
-            }
-            u += n;
-        }
-    }
+    const bool ok = fused_sources(&p) == 3
+                        ? fused_part1<3, kConvG / 4>(p, r, i, dig, xsc, sc, route, u0, u1, hbuf, err)
+                        : fused_part1<2, kMoeG / 4>(p, r, i, dig, xsc, sc, route, u0, u1, hbuf, err);
     named_bar(1, kConsumerThreads);  // h complete
     // down: thread tp of the stage's set accumulates out rows 16 tp .. 16 tp + 15
     const int tp = threadIdx.x & 127;
@@ -1050,14 +1100,15 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
 #pragma unroll
     for (int j = 0; j < kMoeRows; j++) acc[j] = 0.f;
     {
+        bool live = ok;
         const uint32_t dq = (uint32_t)kMoeDU * EO;
         for (int u = u0; u < u1; ++i) {
             const int n = moe_stage_len(u, u1, N, kMoeDU);
             const int s = u / N, j0 = u - s * N;
-            if ((int)(i % kSets) == set && ok) {
+            if ((int)(i % kSets) == set && live) {
                 const int slot = i % kDecSlots;
-                ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
-                if (ok) {
+                live = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
+                if (live) {
                     if (!ffn_skip(&p, route, s)) {  // a masked expert's stage holds no bytes
                         const uint8_t* sb = r.base + r.off[slot];
                         const __half* dsc = reinterpret_cast<const __half*>(sb + dq) + tp * kMoeRows;
@@ -1430,7 +1481,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     if (m) atomicMax(p.best, m);
                 }
             }
-        } else if (p.type == PH_MOE) {
+        } else if (p.type == PH_FUSED) {
             // every CTA routes and owns a run of hidden units (all count into the output)
             const int K = p.K, nch = K >> 4;
             float bias_v = 0.f;
@@ -1499,7 +1550,7 @@ int decode_stage_items(int S, int K, int n_div, int n_total) {
     return G;
 }
 
-bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k) {
+bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k, int S) {
     static_assert((size_t)(2 * kMoeOut + kMoeMaxUnits) * 4 <= (size_t)kDecAttnBytes, "fused MoE scratch");
     if (K < 64 || K % 64 || n_out != kMoeOut || K != n_out) return false;  // the residual is the input
     // routed (top-4 of 4..32 experts), or a dense FFN as one expert without a router
@@ -1507,7 +1558,9 @@ bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k) {
     if (N < 32 || N % 32 || (!dense && (top_k != 4 || n_expert < 4 || n_expert > kMaxRoutes))) return false;
     const int64_t quads = (int64_t)top_k * N / 4;
     if ((quads + num_sms() - 1) / num_sms() * 4 > kMoeMaxUnits) return false;
-    const size_t gu = 2 * ((size_t)kMoeG * K + (((size_t)kMoeG * (K >> 4) + 15) & ~(size_t)15));
+    if (S != 2 && S != 3) return false;
+    const size_t G = S == 3 ? kConvG : kMoeG;
+    const size_t gu = (size_t)S * (G * K + ((G * (K >> 4) + 15) & ~(size_t)15));
     const size_t dn = (size_t)kMoeDU * n_out + 4 * (size_t)n_out;
     if (gu > (size_t)kDecMaxStageBytes || dn > (size_t)kDecMaxStageBytes) return false;
     if ((size_t)16 * K + K > (size_t)kDecMaxStageBytes) return false;  // router stages
@@ -1515,8 +1568,10 @@ bool decode_moe_fits(int K, int N, int n_out, int n_expert, int top_k) {
 }
 
 bool decode_phase_fits(const PhaseDesc& p) {
-    if (p.type == PH_MOE)
-        return p.dt_qs && (p.r_qs || p.n_expert == 1) && decode_moe_fits(p.K, p.N, p.n_out, p.n_expert, p.top_k);
+    if (p.type == PH_FUSED)
+        return p.dt_qs && (p.r_qs || p.n_expert == 1) &&
+               (p.epi != EK_CONV || (p.state && p.conv_w && p.stride == p.N && p.E == p.N)) &&
+               decode_moe_fits(p.K, p.N, p.n_out, p.n_expert, p.top_k, p.epi == EK_CONV ? 3 : 2);
     if (p.type != PH_GEMV && p.type != PH_DOWN4) {
         if (p.type == PH_ATTN) {
             const int G = p.attn.n_head / p.attn.n_kv, hd = p.attn.hd;
