@@ -119,7 +119,7 @@ constexpr int kDecAttnBytes = 20 * 1024;
 
 // Fused MoE phase: hidden units per gate/up stage and per down stage, rows of the output per
 // consumer thread (the 128 threads of a consumer set cover n_out = 2048).
-constexpr int kMoeG = 16;
+constexpr int kMoeG = 8;  // measured (us/step): 16 units (69.6 KB stages) 760, 8 units 724, 4 units 814
 constexpr int kConvG = 8;  // units per first-part stage of a fused short-conv phase (3 rows each)
 constexpr int kMoeDU = 16;
 constexpr int kMoeRows = 16;
