@@ -259,6 +259,13 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
             if (!ok) break;
             const __half2 dc = *reinterpret_cast<const __half2*>(&dcur);
             const int c0 = part * (WPT / 8);  // first 8-weight chunk of this thread in the row
+            // SPLIT = 3 in half2 arithmetic when |d| < 1/4: then |q d| < 32, so 2048 wh and 2048 d
+            // are finite fp16 values (each thread's weights share one block scale here)
+            const float dfs = __low2float(dc);
+            const bool split_fast = SPLIT == 3 && RT == 2 && fabsf(dfs) < 0.25f;
+            const __half2 d2s = __low2half2(dc);
+            const __half2 d2k = __float2half2_rn(dfs * 2048.0f);
+            const __half2 m2k = __float2half2_rn(-2048.0f);
 #pragma unroll
             for (int c = 0; c < WPT / 8; c++) {
                 const uint4 r4 = raw[c >> 1];
@@ -269,6 +276,26 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                     dq4(w0, d2, o.x, o.y);
                     dq4(w1, d2, o.z, o.w);
                     *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = o;
+                } else if (split_fast) {
+                    // wh = RN16(q d) (one HMUL2) and wl = RN16((q d - wh) 2048) (one HFMA2 on
+                    // d 2048 and -2048 wh, both exact scalings): the same bits as the f32 path
+                    // below, at full-rate half2 arithmetic instead of conversions
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const uint32_t u = (j ? w1 : w0) ^ 0x80808080u;  // b + 128 per byte
+                        uint32_t pa = __byte_perm(u, 0x64646464u, 0x5140), pb = __byte_perm(u, 0x64646464u, 0x5342);
+                        const __half2 bias = __float2half2_rn(1152.0f);
+                        const __half2 qa = __hsub2(*reinterpret_cast<__half2*>(&pa), bias);  // exact q pairs
+                        const __half2 qb = __hsub2(*reinterpret_cast<__half2*>(&pb), bias);
+                        const __half2 ha = __hmul2(qa, d2s), hb = __hmul2(qb, d2s);
+                        hw[2 * j] = h2bits(ha);
+                        hw[2 * j + 1] = h2bits(hb);
+                        lw[2 * j] = h2bits(__hfma2(qa, d2k, __hmul2(ha, m2k)));
+                        lw[2 * j + 1] = h2bits(__hfma2(qb, d2k, __hmul2(hb, m2k)));
+                    }
+                    *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(b_tile(st, 1) + sw128(brow, c0 + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                 } else {
                     const float df = __low2float(dc);
                     uint32_t hw[4], lw[4];
