@@ -112,7 +112,8 @@ struct qq_model {
     float* dump = nullptr;    // [n_layers][n_embd] for qq_forward_dump
     int* h_ctl = nullptr;     // pinned staging [2 * h_ctl_cap]
     size_t h_ctl_cap = 0;
-    int* h_small = nullptr;   // pinned [4]
+    int* h_small = nullptr;   // pinned [8]: suppress id, argmax, token, pos, kernel error word
+    int suppress_set = INT32_MIN;  // the suppress id last copied to the device
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
     cudaStream_t cap = nullptr;
     // persistent decode kernel programs, per (sequence, with logits)
@@ -707,8 +708,10 @@ void check_kernel_error(cudaStream_t s) {
 }
 
 void set_suppress(qq_model* m, int id) {
+    if (id == m->suppress_set) return;  // the device copy already holds it
     m->h_small[0] = id;
     QQ_CUDA_TRY(cudaMemcpyAsync(m->suppress, m->h_small, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+    m->suppress_set = id;
 }
 
 // ---- batched prefill -------------------------------------------------------------------
@@ -1198,7 +1201,7 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
             QQ_CUDA_TRY(cudaMemsetAsync(m->suppress, 0xff, 4, ctx->stream));
             m->best = dalloc<unsigned long long>(1);
             m->dump = dalloc<float>((size_t)d.n_layers * E);
-            QQ_CUDA_TRY(cudaMallocHost(&m->h_small, 4 * sizeof(int)));
+            QQ_CUDA_TRY(cudaMallocHost(&m->h_small, 8 * sizeof(int)));
             QQ_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking));
             QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
         } catch (...) {
@@ -1234,8 +1237,10 @@ int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, 
             QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, sizeof(float) * m->d.n_vocab, cudaMemcpyDeviceToHost, s));
         if (logits && argmax_out)
             QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->ctl, sizeof(int), cudaMemcpyDeviceToHost, s));
+        // the kernels' error word rides along: one synchronisation per call
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 4, qq3::kernel_err_ptr(), sizeof(int), cudaMemcpyDeviceToHost, s));
         QQ_CUDA_TRY(cudaStreamSynchronize(s));
-        check_kernel_error(s);
+        if (m->h_small[4]) check_kernel_error(s);  // reads it again, clears it and throws
         if (logits && argmax_out) *argmax_out = m->h_small[1];
     });
 }
