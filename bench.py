@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark: Q8_0 LFM2-8B-A1B-shaped greedy decode on B200.
+"""Benchmark: Q8_0 LFM2-8B-A1B-shaped greedy decode on B200 (benchmark config 4).
 
 One "step" = one greedy decode token (batch 1) through all 24 layers: 18 short-conv +
 6 GQA attention layers, 2 dense FFNs, 22 MoE FFNs (32 experts, top-4), lm_head + argmax.
@@ -251,7 +251,7 @@ def run_ours(args, ws, rank, local):
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32 (Q8_0 weights, f32 activations)",
         "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)",
-        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (BASELINE config 4)",
+        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (benchmark config 4)",
                    "layers": "24 (18 short-conv, 6 GQA attention; 2 dense FFN 7168, 22 MoE 32x top-4 x 1792)",
                    "hidden": 2048, "vocab": 65536, "prompt": args.prompt, "global_batch": ws,
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
@@ -323,7 +323,7 @@ def run_reference(args, ws, rank):
         "warmup": args.warmup, "ms_per_step": round(1000.0 / cb["value"], 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64 accumulate (JS numbers), f32 stores",
         "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)", "impl": "reference",
-        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (BASELINE config 4)",
+        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (benchmark config 4)",
                    "prompt": 16, "note": "bounded slice: 16-token prompt instead of 512 (CPU time)"},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -332,7 +332,7 @@ def run_reference(args, ws, rank):
 
 
 def run_moe_block_ep(args, ws, rank, local):
-    """BASELINE config 3 on N GPUs: the LFM2-MoE block expert-parallel (experts sharded evenly,
+    """benchmark config 3 on N GPUs: the LFM2-MoE block expert-parallel (experts sharded evenly,
     NCCL all-to-all dispatch and combine; qwenqwen3.js_b200/ep.py).  Each rank owns T token
     rows (weak scaling); one step = one EP forward of every rank's rows."""
     import torch
@@ -387,7 +387,7 @@ def run_moe_block_ep(args, ws, rank, local):
 
 
 def run_moe_block(args, ws, rank, local):
-    """the isolated LFM2-MoE block on T tokens (also the small case the
+    """benchmark config 3: the isolated LFM2-MoE block on T tokens (also the small case the
     ncu captures use).  One step = one qq_moe_block call over T token rows."""
     import torch
 
@@ -447,7 +447,7 @@ def run_moe_block(args, ws, rank, local):
 
 
 def run_matmul(args, ws, rank, local):
-    """one Q8_0 matmul Y[M][N] = X[M][K] . W^T (qq_q8_matmul). M = 1 runs the
+    """benchmark config 2: one Q8_0 matmul Y[M][N] = X[M][K] . W^T (qq_q8_matmul). M = 1 runs the
     streamed GEMV, M >= 2 the tcgen05 tensor-core kernel."""
     import torch
 

@@ -116,12 +116,12 @@ class ModelSpec:
 
 
 def qwen3_0p6b(seed: int = 1234) -> ModelSpec:
-    """Qwen3-0.6B architecture."""
+    """benchmark config 1: Qwen3-0.6B architecture."""
     return ModelSpec("qwen3", 28, 1024, 16, 8, 128, 151936, 3072, 1e6, 1e-6, seed=seed, name="Qwen3-0.6B")
 
 
 def qwen3_8b(seed: int = 1234) -> ModelSpec:
-    """Qwen3-8B-shaped, untied embeddings."""
+    """benchmark config 5: Qwen3-8B-shaped, untied embeddings."""
     return ModelSpec("qwen3", 36, 4096, 32, 8, 128, 151936, 12288, 1e6, 1e-6, tied=False, seed=seed, name="Qwen3-8B")
 
 
@@ -129,7 +129,7 @@ LFM2_8B_ATTN_LAYERS = (2, 6, 10, 14, 18, 21)
 
 
 def lfm2_8b_a1b(seed: int = 1234) -> ModelSpec:
-    """LFM2-8B-A1B-shaped hybrid MoE (18 short-conv + 6 attention layers)."""
+    """benchmark config 4: LFM2-8B-A1B-shaped hybrid MoE (18 short-conv + 6 attention layers)."""
     return ModelSpec("lfm2moe", 24, 2048, 32, 8, 64, 65536, 7168, 1e6, 1e-5, context_length=128000,
                      attn_layers=LFM2_8B_ATTN_LAYERS, n_expert=32, n_expert_used=4, n_ff_exp=1792, n_dense_lead=2,
                      seed=seed, name="LFM2-8B-A1B")

@@ -210,7 +210,7 @@ def test_lfm2_full_width_fused_moe(qq3, orc):
 
 
 def test_qwen3_0p6b_config_greedy(qq3, orc):
-    """BASELINE config 1 (Qwen3-0.6B shapes, 28 layers): 32-token prompt + 64 greedy steps."""
+    """benchmark config 1 (Qwen3-0.6B shapes, 28 layers): 32-token prompt + 64 greedy steps."""
     spec = qq3.synth.qwen3_0p6b(seed=1234)
     g, eng, ref = _pair(qq3, orc, spec, max_ctx=128)
     prompt = qq3.synth.uniform_tokens(32, 1234, spec.n_vocab)
@@ -221,7 +221,7 @@ def test_qwen3_0p6b_config_greedy(qq3, orc):
 
 
 def test_lfm2_8b_a1b_config_greedy_slice(qq3, orc):
-    """BASELINE config 4 (all 24 layers) on a bounded slice: 16-token prompt + 8 greedy steps."""
+    """benchmark config 4 (all 24 layers) on a bounded slice: 16-token prompt + 8 greedy steps."""
     spec = qq3.synth.lfm2_8b_a1b(seed=1234)
     g, eng, ref = _pair(qq3, orc, spec, max_ctx=64)
     prompt = qq3.synth.uniform_tokens(16, 4321, spec.n_vocab)

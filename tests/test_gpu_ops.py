@@ -166,7 +166,7 @@ def test_moe_block_vs_oracle(qq3, orc, gpu_ctx, torch, T):
 
 
 def test_moe_block_t2048_sampled_rows(qq3, orc, gpu_ctx, torch):
-    """BASELINE config 3 at T = 2048 (grouped tensor-core path): every row on the GPU, a seeded
+    """benchmark config 3 at T = 2048 (grouped tensor-core path): every row on the GPU, a seeded
     sample of rows on the oracle (the block is row-independent)."""
     orc.set_threads(8)
     T = 2048
