@@ -446,6 +446,80 @@ def run_moe_block(args, ws, rank, local):
     ctx.close()
 
 
+def run_batch_decode(args, ws, rank, local):
+    """benchmark config 5, decode part: the Qwen3-8B-shaped dense model (36 layers, hidden 4096,
+    32/8 heads of 128, FFN 12288, vocab 151936, untied output), 16 concurrent sequences, each
+    prefilled with a seeded uniform prompt (untimed), then K greedy steps of all 16 sequences
+    through the public engine API (Qwen3CudaEngine.forward_batch -> qq_forward_batch): each step
+    copies 16 tokens and positions host->device and reads the 16 greedy ids back.  One step
+    streams the 8.04 GB of layer and output weights once for all sequences plus every sequence's
+    K/V rows (f32 cache)."""
+    import torch
+
+    qq3 = load_package()
+    qq3.build.build_all()
+    torch.cuda.set_device(local)
+    spec = qq3.synth.qwen3_8b(seed=SEED + rank)
+    n = args.seqs
+    prompt = args.prompt if args.prompt is not None else 4096
+    g = qq3.synth.memory_model(spec)
+    ctx = qq3.runtime.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    max_ctx = prompt + args.warmup + args.steps + 1
+    eng = qq3.Qwen3CudaEngine(g, ctx=ctx, max_ctx=max_ctx, n_seq=n)
+    cur, pos = [], []
+    t0 = time.time()
+    for s in range(n):
+        toks = qq3.synth.uniform_tokens(prompt, SEED + 100 * rank + s, spec.n_vocab)
+        if prompt > 1:
+            eng.prefill(toks[:-1].tolist(), pos0=0, seq=s)
+        cur.append(int(toks[-1]))
+        pos.append(prompt - 1)
+    ctx.synchronize()
+    prefill_s = time.time() - t0
+    seqs = list(range(n))
+
+    def step():
+        _, am = eng.forward_batch(seqs, cur, pos, want_logits_array=False)
+        for s in range(n):
+            cur[s] = int(am[s])
+            pos[s] += 1
+
+    for _ in range(args.warmup):
+        step()
+    kv_pos = sum(pos) + n  # positions attended in the first timed step (grows by n per step)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    L, E, F, V = spec.n_layers, spec.n_embd, spec.n_ff, spec.n_vocab
+    nq, nkv = spec.n_head * spec.head_dim, spec.n_head_kv * spec.head_dim
+    w_bytes = 34 / 32 * (L * (E * (2 * nq + 2 * nkv) + 3 * E * F) + E * V)
+    kv_bytes = L * nkv * 4 * 2 * (kv_pos + n * (args.steps - 1) / 2)  # mean over the timed steps
+    peak, kind = _peaks()
+    gbs = (w_bytes + kv_bytes) / (ms * 1e-3) / 1e9
+    res = {"metric": "decode tok/s (Qwen3-8B-shaped, 16 concurrent sequences)", "impl": "ours",
+           "value": round(n / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "int8xf16",
+           "data": "synthetic (seeded random-init Q8_0 weights, uniform prompt ids)",
+           "config": {"workload": "qwen3-8b-batch-decode", "sequences": n, "prompt": prompt,
+                      "path": "qq_forward_batch: tcgen05 GEMMs over the 16 rows, f32 KV cache",
+                      "l2": "weights 8.04 GB + KV per step, far above the 126 MB L2"},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "peak_kind": kind,
+                        "bytes_per_step": {"weights": round(w_bytes), "kv": round(kv_bytes)}},
+           "prefill_s": round(prefill_s, 2), "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    eng.close()
+    ctx.close()
+
+
 def run_matmul(args, ws, rank, local):
     """benchmark config 2: one Q8_0 matmul Y[M][N] = X[M][K] . W^T (qq_q8_matmul). M = 1 runs the
     streamed GEMV, M >= 2 the tcgen05 tensor-core kernel."""
@@ -488,12 +562,14 @@ def run_matmul(args, ws, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--case", choices=["decode", "moe-block", "matmul"], default="decode")
+    ap.add_argument("--case", choices=["decode", "moe-block", "matmul", "batch-decode"], default="decode")
     ap.add_argument("--M", type=int, default=4096, help="rows for --case matmul")
     ap.add_argument("--N", type=int, default=151936, help="output columns for --case matmul")
     ap.add_argument("--K", type=int, default=1024, help="inner dimension for --case matmul")
     ap.add_argument("--tokens", type=int, default=1, help="token rows for --case moe-block")
-    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (decode)")
+    ap.add_argument("--prompt", type=int, default=None,
+                    help=f"prompt length (decode: {PROMPT}; batch-decode: 4096 per sequence)")
+    ap.add_argument("--seqs", type=int, default=16, help="concurrent sequences for --case batch-decode")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)
@@ -505,6 +581,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.prompt is None and args.case != "batch-decode":
+        args.prompt = PROMPT
     ws, rank, local = _dist()
     if args.impl == "reference":
         run_reference(args, ws, rank)
@@ -512,6 +590,8 @@ def main():
         run_moe_block(args, ws, rank, local)
     elif args.case == "matmul":
         run_matmul(args, ws, rank, local)
+    elif args.case == "batch-decode":
+        run_batch_decode(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
 

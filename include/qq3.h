@@ -158,6 +158,18 @@ int qq_model_destroy(qq_model* m);
  *   suppress_id (>= 0) excluded first (thinking suppression, tensor.js:247-248). */
 int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, int pos0, int want_logits,
                float* logits_out, int32_t* argmax_out, int suppress_id);
+/* One forward(tokenId, position, false) step for each of n independent sequences at once:
+ * token_ids[i] at position positions[i] of sequence seq_ids[i] (distinct ids, each < n_seq),
+ * the same as n separate qq_forward calls (qwen3-engine.js:115-245, lfm2-engine.js:228-269) up to
+ * the tensor-core GEMM's f32 accumulation order.  The reference serves one sequence per engine;
+ * this is the batched decode of the 16-sequence Qwen3-8B configuration: each weight streams from
+ * HBM once for all n rows.  With want_logits != 0:
+ *   logits_out (nullable) receives n x n_vocab floats (row i for sequence seq_ids[i]),
+ *   argmax_out (nullable) receives n greedy ids (sampleGreedy, tensor.js:231-237) with
+ *   suppress_id (>= 0) excluded (tensor.js:247-248).
+ * The routing record of each MoE layer (qq_read_routing) is that of row n-1. */
+int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_ids, const int32_t* positions, int n,
+                     int want_logits, float* logits_out, int32_t* argmax_out, int suppress_id);
 /* Greedy generate(): reset, prefill, then up to max_steps decode steps, stopping at
  * eos_id (qwen3-engine.js:397-457, lfm2-engine.js:523-583, webgpu.js:1032-1098,
  * 2047-2117 with temperature 0 and thinkingMode 'suppress').  out_tokens gets the

@@ -126,6 +126,12 @@ struct qq_model {
     // batched prefill buffers for up to pf_cap tokens (grow-only)
     int pf_cap = 0;
     void* pf_arena = nullptr;
+    // multi-sequence decode rows (qq_forward_batch) for up to bt_cap rows (grow-only):
+    // device [token | seq | pos | argmax] x bt_cap ints, logits [bt_cap][n_vocab], pinned staging
+    int bt_cap = 0;
+    int* bt_i = nullptr;
+    float* bt_logits = nullptr;
+    int* h_bt = nullptr;
     qq3::tword* tarena = nullptr;    // tagged activations: one buffer per phase output
     size_t tarena_len = 0;
     float* aarena = nullptr;         // accumulated vectors + counters, two halves of aarena_half words
@@ -148,6 +154,9 @@ void free_model(qq_model* m) {
     m->progs.clear();
     if (m->dctl) cudaFree(m->dctl);
     if (m->pf_arena) cudaFree(m->pf_arena);
+    if (m->bt_i) cudaFree(m->bt_i);
+    if (m->bt_logits) cudaFree(m->bt_logits);
+    if (m->h_bt) cudaFreeHost(m->h_bt);
     if (m->tarena) cudaFree(m->tarena);
     if (m->aarena) cudaFree(m->aarena);
     for (Layer& L : m->layers) {
@@ -851,6 +860,97 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
     }
 }
 
+// ---- multi-sequence decode step -----------------------------------------------------------
+// One forward() step of each of T independent sequences at once: row t is token tok[t] of
+// sequence seq[t] at position pos[t] (distinct sequences).  The layer pieces are those of the
+// batched prefill -- projections as tensor-core GEMMs over the T rows (each weight streams once
+// for all the sequences), the MoE regrouped by expert -- with a row map for RoPE, the K/V
+// append, attention and the short-conv state; then the output norm, the lm_head GEMM and a
+// first-max argmax per row.  The MoE routing record kept for onRouterUpdate is that of the last
+// row.  Same results as T separate forward() calls up to the GEMM's f32 accumulation order.
+void batch_step(qq_model* m, int T, bool want_logits) {
+    const qq_model_desc& d = m->d;
+    cudaStream_t s = m->ctx->stream;
+    const int E = d.n_embd, hd = d.head_dim;
+    PrefillBufs b = prefill_bufs(m, T);
+    const int* tok = m->bt_i;
+    const int* seq = m->bt_i + m->bt_cap;
+    const int* pos = m->bt_i + 2 * m->bt_cap;
+    QQ_CUDA_TRY(cudaMemcpyAsync(m->bt_i, m->h_bt, sizeof(int) * 3 * m->bt_cap, cudaMemcpyHostToDevice, s));
+    qq3::launch_embed_rows(*m->tok_embd, tok, T, d.n_vocab, b.hidden, s);
+    const size_t TE = (size_t)T * E;
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
+        if (L.attn) {
+            qq3::launch_gemm_q8(*L.t[QQ_WQ], b.xn, T, b.x16, b.q, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WV], b.xn, T, b.x16, b.v, s);
+            qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
+            qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
+            qq3::launch_rope_rows_at(b.q, T, d.n_head, hd, m->rope_cs, pos, s);
+            qq3::launch_rope_rows_at(b.k, T, d.n_head_kv, hd, m->rope_cs, pos, s);
+            float* kc = m->k_cache + L.attn_slot * m->kv_stride_layer();
+            float* vc = m->v_cache + L.attn_slot * m->kv_stride_layer();
+            qq3::launch_kv_append_at(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, seq, pos, m->kv_stride_seq(), kc, vc, s);
+            qq3::launch_attn_rows_at(b.q, kc, vc, T, seq, pos, m->kv_stride_seq(), d.n_head, d.n_head_kv, hd,
+                                     d.max_ctx, b.attn, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WO], b.attn, T, b.x16, b.tmp, s);
+        } else {
+            qq3::launch_gemm_q8(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.bcx, s);
+            qq3::launch_conv_rows_at(b.bcx, L.t[QQ_CONV]->f32, m->conv(0, l), (size_t)d.n_layers * 2 * E, seq, T, E,
+                                     b.y, s);
+            qq3::launch_gemm_q8(*L.t[QQ_OUT_PROJ], b.y, T, b.x16, b.tmp, s);
+        }
+        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
+        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, s);
+        if (L.moe) {
+            const int k = d.n_expert_used;
+            const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+            qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, b.xn, T, nullptr, 0.f, d.n_expert, k, b.rec, b.idx, b.w, s);
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->rec + (size_t)L.moe_slot * m->rec_len, b.rec + (size_t)(T - 1) * m->rec_len,
+                                        sizeof(float) * m->rec_len, cudaMemcpyDeviceToDevice, s));
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->ridx + (size_t)L.moe_slot * k, b.idx + (size_t)(T - 1) * k,
+                                        sizeof(int) * k, cudaMemcpyDeviceToDevice, s));
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->rw + (size_t)L.moe_slot * k, b.w + (size_t)(T - 1) * k, sizeof(float) * k,
+                                        cudaMemcpyDeviceToDevice, s));
+            qq3::launch_moe_grouped(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], *L.t[QQ_DOWN_EXPS], b.idx, b.w, m->mask,
+                                    b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
+        } else {
+            const size_t F = L.t[QQ_FFN_GATE]->ne[1];
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.g, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s);
+            qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s);
+        }
+        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
+    }
+    if (!want_logits) return;
+    qq3::launch_rmsnorm(b.hidden, T, E, m->out_norm->f32, d.rms_eps, b.xn, s);
+    const DTensor* out = m->output ? m->output : m->tok_embd;
+    qq3::launch_gemm_q8(*out, b.xn, T, b.x16, m->bt_logits, s);
+    qq3::launch_argmax_rows(m->bt_logits, T, d.n_vocab, m->suppress, m->bt_i + 3 * m->bt_cap, s);
+}
+
+// grow the multi-sequence row buffers to hold T rows (device and pinned staging)
+void ensure_batch_rows(qq_model* m, int T) {
+    if (T <= m->bt_cap) return;
+    QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    if (m->bt_i) cudaFree(m->bt_i);
+    if (m->bt_logits) cudaFree(m->bt_logits);
+    if (m->h_bt) cudaFreeHost(m->h_bt);
+    m->bt_i = nullptr;
+    m->bt_logits = nullptr;
+    m->h_bt = nullptr;
+    m->bt_cap = 0;
+    int cap = 16;
+    while (cap < T) cap *= 2;
+    m->bt_i = static_cast<int*>(dmalloc(sizeof(int) * 4 * cap));
+    m->bt_logits = static_cast<float*>(dmalloc(sizeof(float) * (size_t)cap * m->d.n_vocab));
+    QQ_CUDA_TRY(cudaMallocHost(&m->h_bt, sizeof(int) * 4 * cap));
+    m->bt_cap = cap;
+}
+
 bool batched_prefill_ok(qq_model* m) {
     if (getenv_flag("QQ3_NO_TCGEN05")) return false;
     if (const char* v = getenv("QQ3_PREFILL_BATCH"))
@@ -1242,6 +1342,58 @@ int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, 
         QQ_CUDA_TRY(cudaStreamSynchronize(s));
         if (m->h_small[4]) check_kernel_error(s);  // reads it again, clears it and throws
         if (logits && argmax_out) *argmax_out = m->h_small[1];
+    });
+}
+
+int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_ids, const int32_t* positions, int n,
+                     int want_logits, float* logits_out, int32_t* argmax_out, int suppress_id) {
+    return guard([&] {
+        need(m && seq_ids && token_ids && positions && n >= 1, "qq_forward_batch: NULL argument or n < 1");
+        std::vector<char> seen((size_t)m->d.n_seq, 0);
+        for (int i = 0; i < n; i++) {
+            check_seq_pos(m, seq_ids[i], positions[i], 1);
+            need(!seen[(size_t)seq_ids[i]], "qq_forward_batch: a sequence appears twice in one call");
+            seen[(size_t)seq_ids[i]] = 1;
+            need(token_ids[i] >= 0 && token_ids[i] < m->d.n_vocab, "token id out of range");
+        }
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        const bool logits = want_logits != 0;
+        const size_t V = (size_t)m->d.n_vocab;
+        if (logits) set_suppress(m, suppress_id);
+        if (n == 1 || !batched_prefill_ok(m)) {
+            // one sequence (or no tensor-core path): the per-token decode step, row by row
+            for (int i = 0; i < n; i++) {
+                run_tokens(m, token_ids + i, 1, seq_ids[i], positions[i], logits);
+                if (logits && logits_out)
+                    QQ_CUDA_TRY(cudaMemcpyAsync(logits_out + i * V, m->logits, sizeof(float) * V,
+                                                cudaMemcpyDeviceToHost, s));
+                if (logits && argmax_out) {
+                    QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->ctl, sizeof(int), cudaMemcpyDeviceToHost, s));
+                    QQ_CUDA_TRY(cudaStreamSynchronize(s));
+                    argmax_out[i] = m->h_small[1];
+                }
+            }
+            QQ_CUDA_TRY(cudaStreamSynchronize(s));
+            check_kernel_error(s);
+            return;
+        }
+        ensure_batch_rows(m, n);
+        for (int i = 0; i < n; i++) {
+            m->h_bt[i] = token_ids[i];
+            m->h_bt[m->bt_cap + i] = seq_ids[i];
+            m->h_bt[2 * m->bt_cap + i] = positions[i];
+        }
+        batch_step(m, n, logits);
+        if (logits && logits_out)
+            QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->bt_logits, sizeof(float) * V * n, cudaMemcpyDeviceToHost, s));
+        if (logits && argmax_out)
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->h_bt + 3 * m->bt_cap, m->bt_i + 3 * m->bt_cap, sizeof(int) * n,
+                                        cudaMemcpyDeviceToHost, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // also: the pinned staging is read asynchronously above
+        check_kernel_error(s);
+        if (logits && argmax_out)
+            for (int i = 0; i < n; i++) argmax_out[i] = m->h_bt[3 * m->bt_cap + i];
     });
 }
 

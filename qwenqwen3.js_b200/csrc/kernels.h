@@ -121,6 +121,18 @@ void launch_add_rows(float* x, const float* d, size_t n, cudaStream_t s);
 void launch_swiglu_rows(const float* g, const float* u, size_t n, float* h, cudaStream_t s);
 void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T, int pos0, int n_head, int n_kv,
                          int hd, int max_ctx, float* out, cudaStream_t s);
+// multi-sequence decode rows (kernels_prefill.cu): row t is sequence seq[t] (device) at position
+// pos[t] (device); the KV cache / conv state of sequence s start seq_stride / state_stride floats
+// after the given base pointer
+void launch_rope_rows_at(float* x, int T, int n_heads, int hd, const float* cs, const int* pos, cudaStream_t s);
+void launch_kv_append_at(const float* k, const float* v, int T, int n_kv, int hd, int max_ctx, const int* seq,
+                         const int* pos, size_t seq_stride, float* kc, float* vc, cudaStream_t s);
+void launch_attn_rows_at(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
+                         size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* out, cudaStream_t s);
+void launch_conv_rows_at(const float* bcx, const float* w, float* state, size_t state_stride, const int* seq, int T,
+                         int E, float* y, cudaStream_t s);
+// out[t] = first-max argmax of logits row t, *suppress (nullable; < 0: none) left out
+void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, int* out, cudaStream_t s);
 
 // ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
 // Each returns false when the shape is outside the streamed path (the caller then uses the

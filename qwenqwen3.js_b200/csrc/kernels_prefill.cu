@@ -11,6 +11,9 @@
 //   k_attn_prefill    causal GQA attention of each token over positions 0..pos0+t
 //                     (qwen3-engine.js:249-301, lfm2-engine.js:329-390)
 //   k_add_rows / k_swiglu_rows   residual add and SwiGLU (tensor.js:168-185)
+// The same pieces with a row map (`*_at`: row t is sequence seq[t] at position pos[t]) run one
+// forward() step of several independent sequences at once, plus k_argmax_rows (sampleGreedy per
+// row) for their greedy ids.
 #include "kernels.h"
 
 namespace qq3 {
@@ -90,21 +93,15 @@ __global__ void k_swiglu_rows(const float* __restrict__ g, const float* __restri
     }
 }
 
-// One CTA per (token t, kv head): warp g scores query head kvh*G + g against positions
-// 0..pos0+t in tiles of 32 (one position per lane), online softmax, V accumulation (lane owns
-// HD/32 dims).  q: [T][n_head][HD] (normalised, rotated); out: [T][n_head][HD].
+// Causal GQA attention of one query head over positions 0..len-1 of one kv head's cache rows,
+// by one warp: tiles of 32 positions (one per lane), online softmax, V accumulation (lane owns
+// HD/32 dims).  qh: the normalised, rotated query; o: HD outputs.
 template <int HD>
-__global__ void k_attn_prefill(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                               int pos0, int n_head, int n_kv, int max_ctx, float* __restrict__ out) {
+__device__ __forceinline__ void attn_row(const float* __restrict__ qh, const float* __restrict__ kb,
+                                         const float* __restrict__ vb, int len, float* __restrict__ o) {
     constexpr int PL = HD / 32;
-    const int t = blockIdx.x, kvh = blockIdx.y;
-    const int G = n_head / n_kv;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp >= G) return;
-    const int h = kvh * G + warp;
-    const int len = pos0 + t + 1;
+    const int lane = threadIdx.x & 31;
     const float scale = (float)(1.0 / sqrt((double)HD));
-    const float* qh = q + ((size_t)t * n_head + h) * HD;
     float qv[HD];
 #pragma unroll
     for (int j = 0; j < HD; j += 4) {
@@ -114,8 +111,6 @@ __global__ void k_attn_prefill(const float* __restrict__ q, const float* __restr
         qv[j + 2] = v4.z;
         qv[j + 3] = v4.w;
     }
-    const float* kb = kc + (size_t)kvh * max_ctx * HD;
-    const float* vb = vc + (size_t)kvh * max_ctx * HD;
     float m = -INFINITY, l = 0.f, acc[PL];
 #pragma unroll
     for (int j = 0; j < PL; j++) acc[j] = 0.f;
@@ -150,9 +145,119 @@ __global__ void k_attn_prefill(const float* __restrict__ q, const float* __restr
         }
         m = m_new;
     }
-    float* o = out + ((size_t)t * n_head + h) * HD + lane * PL;
+    o += lane * PL;
 #pragma unroll
     for (int j = 0; j < PL; j++) o[j] = acc[j] / l;
+}
+
+// One CTA per (token t, kv head): warp g scores query head kvh*G + g against positions
+// 0..pos0+t.  q: [T][n_head][HD] (normalised, rotated); out: [T][n_head][HD].
+template <int HD>
+__global__ void k_attn_prefill(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                               int pos0, int n_head, int n_kv, int max_ctx, float* __restrict__ out) {
+    const int t = blockIdx.x, kvh = blockIdx.y;
+    const int G = n_head / n_kv;
+    const int warp = threadIdx.x >> 5;
+    if (warp >= G) return;
+    const int h = kvh * G + warp;
+    attn_row<HD>(q + ((size_t)t * n_head + h) * HD, kc + (size_t)kvh * max_ctx * HD, vc + (size_t)kvh * max_ctx * HD,
+                 pos0 + t + 1, out + ((size_t)t * n_head + h) * HD);
+}
+
+// ---- multi-sequence decode rows: row t is sequence seq[t] at position pos[t] ----------------
+// (one forward() step of each of T independent sequences; the caches of sequence s start at
+// seq_stride * s floats from the layer's base pointer)
+
+__global__ void k_rope_rows_at(float* __restrict__ x, int T, int n_heads, int hd, const float* __restrict__ cs,
+                               const int* __restrict__ pos) {
+    const int half = hd / 2;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * n_heads * half;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i % half);
+        const size_t row = i / half;
+        const int t = (int)(row / n_heads);
+        float* v = x + row * hd;
+        const size_t p = (size_t)pos[t];
+        const float c = cs[p * hd + 2 * j], s = cs[p * hd + 2 * j + 1];
+        const float x0 = v[j], x1 = v[j + half];
+        v[j] = x0 * c - x1 * s;
+        v[j + half] = x0 * s + x1 * c;
+    }
+}
+
+__global__ void k_kv_append_at(const float* __restrict__ k, const float* __restrict__ v, int T, int n_kv, int hd,
+                               int max_ctx, const int* __restrict__ seq, const int* __restrict__ pos,
+                               size_t seq_stride, float* __restrict__ kc, float* __restrict__ vc) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * n_kv * hd;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int dd = (int)(i % hd);
+        const int h = (int)((i / hd) % n_kv);
+        const int t = (int)(i / ((size_t)hd * n_kv));
+        const size_t dst = (size_t)seq[t] * seq_stride + ((size_t)h * max_ctx + pos[t]) * hd + dd;
+        kc[dst] = k[i];
+        vc[dst] = v[i];
+    }
+}
+
+template <int HD>
+__global__ void k_attn_rows_at(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                               const int* __restrict__ seq, const int* __restrict__ pos, size_t seq_stride, int n_head,
+                               int n_kv, int max_ctx, float* __restrict__ out) {
+    const int t = blockIdx.x, kvh = blockIdx.y;
+    const int G = n_head / n_kv;
+    const int warp = threadIdx.x >> 5;
+    if (warp >= G) return;
+    const int h = kvh * G + warp;
+    const size_t base = (size_t)seq[t] * seq_stride + (size_t)kvh * max_ctx * HD;
+    attn_row<HD>(q + ((size_t)t * n_head + h) * HD, kc + base, vc + base, pos[t] + 1,
+                 out + ((size_t)t * n_head + h) * HD);
+}
+
+// one short-conv step per row with its sequence's 2-tap state (lfm2-engine.js:282-325);
+// state of sequence s at state + s * state_stride: [s0 | s1] of E floats
+__global__ void k_conv_rows_at(const float* __restrict__ bcx, const float* __restrict__ w, float* __restrict__ state,
+                               size_t state_stride, const int* __restrict__ seq, int T, int E, float* __restrict__ y) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < (size_t)T * E;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / E), c = (int)(i % E);
+        float* st = state + (size_t)seq[t] * state_stride;
+        const float s0 = st[c], s1 = st[E + c];
+        const float k0 = w[c * 3], k1 = w[c * 3 + 1], k2 = w[c * 3 + 2];
+        const float* r = bcx + (size_t)t * 3 * E;
+        const float bx = r[c] * r[2 * E + c];
+        const float co = k0 * s0 + k1 * s1 + k2 * bx;
+        y[i] = r[E + c] * co;
+        st[c] = s1;
+        st[E + c] = bx;
+    }
+}
+
+// first-max argmax of each row of logits [T][V] (sampleGreedy, tensor.js:231-237), the id
+// *suppress (>= 0) left out (thinking suppression, tensor.js:247-248); one CTA per row
+constexpr int kArgmaxThreads = 512;
+__global__ void __launch_bounds__(kArgmaxThreads)
+    k_argmax_rows(const float* __restrict__ logits, int V, const int* __restrict__ suppress, int* __restrict__ out) {
+    const int t = blockIdx.x;
+    const int skip = suppress ? *suppress : -1;
+    const float* r = logits + (size_t)t * V;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+        if (i != skip) {
+            const unsigned long long k = argmax_key(r[i], i);
+            best = k > best ? k : best;
+        }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    __shared__ unsigned long long keys[kArgmaxThreads / 32];
+    if ((threadIdx.x & 31) == 0) keys[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = 0ull;
+        for (int w = 0; w < kArgmaxThreads / 32; w++) m = keys[w] > m ? keys[w] : m;
+        out[t] = argmax_key_index(m);
+    }
 }
 
 }  // namespace
@@ -196,6 +301,44 @@ void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T
     if (hd == 64) k_attn_prefill<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, pos0, n_head, n_kv, max_ctx, out);
     else if (hd == 128) k_attn_prefill<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, pos0, n_head, n_kv, max_ctx, out);
     else QQ_CHECK(false, -4, "prefill attention: head_dim must be 64 or 128");
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_rope_rows_at(float* x, int T, int n_heads, int hd, const float* cs, const int* pos, cudaStream_t s) {
+    k_rope_rows_at<<<grid_n((size_t)T * n_heads * hd / 2), 256, 0, s>>>(x, T, n_heads, hd, cs, pos);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_kv_append_at(const float* k, const float* v, int T, int n_kv, int hd, int max_ctx, const int* seq,
+                         const int* pos, size_t seq_stride, float* kc, float* vc, cudaStream_t s) {
+    k_kv_append_at<<<grid_n((size_t)T * n_kv * hd), 256, 0, s>>>(k, v, T, n_kv, hd, max_ctx, seq, pos, seq_stride,
+                                                                   kc, vc);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_attn_rows_at(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
+                         size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* out, cudaStream_t s) {
+    const int G = n_head / n_kv;
+    QQ_CHECK(G >= 1 && G <= 32 && n_head % n_kv == 0, -4, "batched attention: unsupported head grouping");
+    if (T <= 0) return;
+    dim3 grid((unsigned)T, (unsigned)n_kv);
+    if (hd == 64)
+        k_attn_rows_at<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, out);
+    else if (hd == 128)
+        k_attn_rows_at<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, out);
+    else QQ_CHECK(false, -4, "batched attention: head_dim must be 64 or 128");
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_conv_rows_at(const float* bcx, const float* w, float* state, size_t state_stride, const int* seq, int T,
+                         int E, float* y, cudaStream_t s) {
+    k_conv_rows_at<<<grid_n((size_t)T * E), 256, 0, s>>>(bcx, w, state, state_stride, seq, T, E, y);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, int* out, cudaStream_t s) {
+    if (T <= 0) return;
+    k_argmax_rows<<<(unsigned)T, kArgmaxThreads, 0, s>>>(logits, V, suppress, out);
     QQ_CUDA_TRY(cudaGetLastError());
 }
 

@@ -160,6 +160,21 @@ class _CudaEngine:
         self._emit_routing()
         return am
 
+    def forward_batch(self, seqs, tokenIds, positions, skipLogits: bool = False, suppress_id: int = -1,
+                      want_logits_array: bool = True):
+        """forward(tokenIds[i], positions[i], skipLogits) of sequence seqs[i] for every i in one
+        step (the engine was created with n_seq > max(seqs)).  Returns the logits rows
+        [len(seqs)][nVocab] and the device greedy ids (suppress_id excluded), or (None, None) with
+        skipLogits.  onRouterUpdate sees the routing of the last row."""
+        if skipLogits:
+            self.model.forward_batch(seqs, tokenIds, positions, want_logits=False)
+            self._emit_routing()
+            return None, None
+        logits, am = self.model.forward_batch(seqs, tokenIds, positions, want_logits=True,
+                                              logits=want_logits_array, suppress_id=suppress_id)
+        self._emit_routing()
+        return logits, am
+
     def prefill(self, tokenIds, pos0: int = 0, seq: int = 0) -> None:
         """forward(t, pos, true) for each token, in one C-ABI call."""
         self.model.forward(tokenIds, seq=seq, pos0=pos0, want_logits=False)

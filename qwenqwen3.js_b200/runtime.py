@@ -86,6 +86,8 @@ _SIGS = {
     "qq_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
     "qq_model_destroy": (_I, [_P]),
     "qq_forward": (_I, [_P, C.POINTER(C.c_int32), _I, _I, _I, _I, _P, C.POINTER(C.c_int32), _I]),
+    "qq_forward_batch": (_I, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_int32), _I, _I, _P,
+                              C.POINTER(C.c_int32), _I]),
     "qq_generate": (_I, [_P, _I, C.POINTER(C.c_int32), _I, _I, _I, _I, C.POINTER(C.c_int32), C.POINTER(_I)]),
     "qq_reset": (_I, [_P, _I]),
     "qq_read_routing": (_I, [_P, _I, _P]),
@@ -308,6 +310,22 @@ class Model:
                                       1 if want_logits else 0, _ptr(out), C.byref(am) if want_logits else None,
                                       suppress_id))
         return out, am.value
+
+    def forward_batch(self, seqs, tokens, positions, want_logits: bool = True, logits: bool = True,
+                      suppress_id: int = -1):
+        """One step of each sequence seqs[i] (token tokens[i] at positions[i]); returns
+        (logits [n][n_vocab] or None, greedy ids [n] or None)."""
+        i32 = lambda a: np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))  # noqa: E731
+        sq, tk, ps = i32(seqs), i32(tokens), i32(positions)
+        n = len(sq)
+        if len(tk) != n or len(ps) != n:
+            raise ValueError("forward_batch: seqs, tokens and positions differ in length")
+        out = np.empty((n, self.n_vocab), dtype=np.float32) if (want_logits and logits) else None
+        am = np.full(n, -1, dtype=np.int32) if want_logits else None
+        p32 = lambda a: a.ctypes.data_as(C.POINTER(C.c_int32))  # noqa: E731
+        check(self.ctx.lib.qq_forward_batch(self.h, p32(sq), p32(tk), p32(ps), n, 1 if want_logits else 0,
+                                            _ptr(out), p32(am) if am is not None else None, suppress_id))
+        return out, am
 
     def forward_dump(self, token: int, seq: int, pos: int) -> np.ndarray:
         out = np.empty((self.n_layers, self.n_embd), dtype=np.float32)
