@@ -123,8 +123,8 @@ struct qq_model {
     };
     std::map<std::pair<int, int>, Prog> progs;
     qq3::DecodeCtl* dctl = nullptr;  // model-wide control block of the persistent kernel
-    // batched prefill buffers for up to pf_cap tokens (grow-only)
-    int pf_cap = 0;
+    // batched prefill / multi-sequence buffers (grow-only, pf_bytes allocated)
+    size_t pf_bytes = 0;
     void* pf_arena = nullptr;
     // multi-sequence decode rows (qq_forward_batch) for up to bt_cap rows (grow-only):
     // device [token | seq | pos | argmax] x bt_cap ints, logits [bt_cap][n_vocab], pinned staging
@@ -743,6 +743,7 @@ struct PrefillBufs {
     int* idx;
     __half* x16;
     void* moe;
+    void* rows;  // few-row GEMM scratch (T <= kGemmFewMax), else null
 };
 
 PrefillBufs prefill_bufs(qq_model* m, int T) {
@@ -763,18 +764,19 @@ PrefillBufs prefill_bufs(qq_model* m, int T) {
                             al(C * F * 4), al(C * F * 4), al(C * F * 4),           // g u h
                             al(C * (2 * k + d.n_expert) * 4), al(C * k * 4), al(C * k * 4),  // rec w idx
                             al(C * std::max({E, nq, F}) * 2 * (qq3::gemm_exact() ? 2 : 1)),  // x16 (hi, lo)
-                            Fe ? al(qq3::moe_grouped_scratch_bytes(T, k, d.n_expert, E, Fe)) : 0};
+                            Fe ? al(qq3::moe_grouped_scratch_bytes(T, k, d.n_expert, E, Fe)) : 0,
+                            T <= qq3::kGemmFewMax ? al(qq3::gemm_rows_scratch_bytes(T)) : 0};  // few-row GEMM
     size_t total = 0;
     for (size_t v : sizes) total += v;
-    if (T > m->pf_cap) {
+    if (total > m->pf_bytes) {
         if (m->pf_arena) {
             QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
             cudaFree(m->pf_arena);
             m->pf_arena = nullptr;
-            m->pf_cap = 0;
+            m->pf_bytes = 0;
         }
         m->pf_arena = dmalloc(total);
-        m->pf_cap = T;
+        m->pf_bytes = total;
     }
     char* b = static_cast<char*>(m->pf_arena);
     size_t i = 0;
@@ -802,6 +804,7 @@ PrefillBufs prefill_bufs(qq_model* m, int T) {
     p.idx = reinterpret_cast<int*>(take());
     p.x16 = reinterpret_cast<__half*>(take());
     p.moe = take();
+    p.rows = T <= qq3::kGemmFewMax ? take() : nullptr;
     return p;
 }
 
@@ -877,15 +880,16 @@ void batch_step(qq_model* m, int T, bool want_logits) {
     const int* seq = m->bt_i + m->bt_cap;
     const int* pos = m->bt_i + 2 * m->bt_cap;
     QQ_CUDA_TRY(cudaMemcpyAsync(m->bt_i, m->h_bt, sizeof(int) * 3 * m->bt_cap, cudaMemcpyHostToDevice, s));
+    if (b.rows) qq3::gemm_rows_reset(b.rows, s);
     qq3::launch_embed_rows(*m->tok_embd, tok, T, d.n_vocab, b.hidden, s);
     const size_t TE = (size_t)T * E;
     for (int l = 0; l < d.n_layers; l++) {
         const Layer& L = m->layers[l];
         qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
         if (L.attn) {
-            qq3::launch_gemm_q8(*L.t[QQ_WQ], b.xn, T, b.x16, b.q, s);
-            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s);
-            qq3::launch_gemm_q8(*L.t[QQ_WV], b.xn, T, b.x16, b.v, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WQ], b.xn, T, b.x16, b.rows, b.q, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WK], b.xn, T, b.x16, b.rows, b.k, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WV], b.xn, T, b.x16, b.rows, b.v, s);
             qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
             qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
             qq3::launch_rope_rows_at(b.q, T, d.n_head, hd, m->rope_cs, pos, s);
@@ -895,12 +899,12 @@ void batch_step(qq_model* m, int T, bool want_logits) {
             qq3::launch_kv_append_at(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, seq, pos, m->kv_stride_seq(), kc, vc, s);
             qq3::launch_attn_rows_at(b.q, kc, vc, T, seq, pos, m->kv_stride_seq(), d.n_head, d.n_head_kv, hd,
                                      d.max_ctx, b.attn, s);
-            qq3::launch_gemm_q8(*L.t[QQ_WO], b.attn, T, b.x16, b.tmp, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WO], b.attn, T, b.x16, b.rows, b.tmp, s);
         } else {
-            qq3::launch_gemm_q8(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.bcx, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.rows, b.bcx, s);
             qq3::launch_conv_rows_at(b.bcx, L.t[QQ_CONV]->f32, m->conv(0, l), (size_t)d.n_layers * 2 * E, seq, T, E,
                                      b.y, s);
-            qq3::launch_gemm_q8(*L.t[QQ_OUT_PROJ], b.y, T, b.x16, b.tmp, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_OUT_PROJ], b.y, T, b.x16, b.rows, b.tmp, s);
         }
         qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
         qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, s);
@@ -918,17 +922,17 @@ void batch_step(qq_model* m, int T, bool want_logits) {
                                     b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
         } else {
             const size_t F = L.t[QQ_FFN_GATE]->ne[1];
-            qq3::launch_gemm_q8(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.g, s);
-            qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.rows, b.g, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.rows, b.u, s);
             qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
-            qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.rows, b.tmp, s);
         }
         qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
     }
     if (!want_logits) return;
     qq3::launch_rmsnorm(b.hidden, T, E, m->out_norm->f32, d.rms_eps, b.xn, s);
     const DTensor* out = m->output ? m->output : m->tok_embd;
-    qq3::launch_gemm_q8(*out, b.xn, T, b.x16, m->bt_logits, s);
+    qq3::launch_gemm_q8_few(*out, b.xn, T, b.x16, b.rows, m->bt_logits, s);
     qq3::launch_argmax_rows(m->bt_logits, T, d.n_vocab, m->suppress, m->bt_i + 3 * m->bt_cap, s);
 }
 
@@ -1152,7 +1156,14 @@ int qq_q8_matmul(qq_ctx* ctx, const qq_tensor* W, const float* x_dev, int M, flo
         const int64_t K = W->t.ne[0], N = W->t.ne[1];
         if (M >= 2 && qq3::gemm_q8_supported(W->t) && !getenv_flag("QQ3_NO_TCGEN05")) {
             // tensor cores: fp16 operands, f32 accumulation in TMEM (kernels_gemm.cu)
-            __half* x16 = static_cast<__half*>(ctx_scratch(ctx, qq3::gemm_q8_scratch_bytes(M, K)));
+            const size_t xb = (qq3::gemm_q8_scratch_bytes(M, K) + 255) & ~(size_t)255;
+            if (M <= qq3::kGemmFewMax) {  // few rows: weights on the MMA's 128-row side, split-K
+                char* sc = static_cast<char*>(ctx_scratch(ctx, xb + qq3::gemm_rows_scratch_bytes(M)));
+                qq3::gemm_rows_reset(sc + xb, ctx->stream);
+                qq3::launch_gemm_q8_few(W->t, x_dev, M, reinterpret_cast<__half*>(sc), sc + xb, y_dev, ctx->stream);
+                return;
+            }
+            __half* x16 = static_cast<__half*>(ctx_scratch(ctx, xb));
             qq3::launch_gemm_q8(W->t, x_dev, M, x16, y_dev, ctx->stream);
             return;
         }

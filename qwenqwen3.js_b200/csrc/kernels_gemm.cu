@@ -97,7 +97,8 @@ struct Cfg {
     static constexpr int ATile = kBM * kBK * 2;       // 16 KB
     static constexpr int BTile = BN * kBK * 2;        // 32 KB / 16 KB
     static constexpr int RawTile = BN * kBK;          // int8
-    static constexpr int Stage = NT * ATile + NT * BTile + RawTile;
+    static constexpr int DTile = BN * 16;             // block scales: 8 fp16 per row (4 K steps)
+    static constexpr int Stage = NT * ATile + NT * BTile + RawTile + DTile;
     static constexpr int Smem = kStages * Stage + 1024;
     static constexpr uint32_t Idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
     static constexpr int RowThreads = 256 / BN;       // converter threads per B row
@@ -113,6 +114,59 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t a, uint64_t b, 
 
 __device__ __forceinline__ uint32_t h2bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
+// 32 weights of one row (raw[0..1], block scale dc) -> the hi and lo fp16 planes of the swizzled
+// K-major tiles bh / bl, 16-byte chunks c0 .. c0 + 3 of row brow (the SPLIT = 3 conversion above)
+__device__ __forceinline__ void split3_convert(const uint4 (&raw)[2], __half2 dc, uint8_t* bh, uint8_t* bl, int brow,
+                                               int c0) {
+    const float dfs = __low2float(dc);
+    uint32_t hw[4][4], lw[4][4];
+    if (fabsf(dfs) < 0.25f) {  // one branch for the four chunks, so their chains interleave
+        const __half2 d2s = __low2half2(dc);
+        const __half2 d2k = __float2half2_rn(dfs * 2048.0f);
+        const __half2 m2k = __float2half2_rn(-2048.0f);
+        const __half2 bias = __float2half2_rn(1152.0f);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 r4 = raw[c >> 1];
+            const uint32_t w0 = (c & 1) ? r4.z : r4.x, w1 = (c & 1) ? r4.w : r4.y;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const uint32_t u = (j ? w1 : w0) ^ 0x80808080u;
+                uint32_t pa = __byte_perm(u, 0x64646464u, 0x5140), pb = __byte_perm(u, 0x64646464u, 0x5342);
+                const __half2 qa = __hsub2(*reinterpret_cast<__half2*>(&pa), bias);
+                const __half2 qb = __hsub2(*reinterpret_cast<__half2*>(&pb), bias);
+                const __half2 ha = __hmul2(qa, d2s), hb = __hmul2(qb, d2s);
+                hw[c][2 * j] = h2bits(ha);
+                hw[c][2 * j + 1] = h2bits(hb);
+                lw[c][2 * j] = h2bits(__hfma2(qa, d2k, __hmul2(ha, m2k)));
+                lw[c][2 * j + 1] = h2bits(__hfma2(qb, d2k, __hmul2(hb, m2k)));
+            }
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 r4 = raw[c >> 1];
+            const uint32_t w0 = (c & 1) ? r4.z : r4.x, w1 = (c & 1) ? r4.w : r4.y;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t word = j < 2 ? w0 : w1;
+                const int sh = 16 * (j & 1);
+                const float wa = (float)(int8_t)((word >> sh) & 0xff) * dfs;
+                const float wb = (float)(int8_t)((word >> (sh + 8)) & 0xff) * dfs;
+                const __half2 h = __floats2half2_rn(wa, wb);
+                const float2 hf = __half22float2(h);
+                hw[c][j] = h2bits(h);
+                lw[c][j] = h2bits(__floats2half2_rn((wa - hf.x) * 2048.f, (wb - hf.y) * 2048.f));
+            }
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        *reinterpret_cast<uint4*>(bh + sw128(brow, c0 + c)) = make_uint4(hw[c][0], hw[c][1], hw[c][2], hw[c][3]);
+        *reinterpret_cast<uint4*>(bl + sw128(brow, c0 + c)) = make_uint4(lw[c][0], lw[c][1], lw[c][2], lw[c][3]);
+    }
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -123,9 +177,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 template <int SPLIT>
 __global__ void __launch_bounds__(kThreadsG2, 1)
-    k_gemm_q8_tma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int K,
-                  const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, const int4* __restrict__ tiles,
-                  const int* __restrict__ n_tiles, int* err) {
+    k_gemm_q8_tma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmD, int d_tma, int M, int K, const __half* __restrict__ d, int N,
+                  float* __restrict__ C, int ldc, const int4* __restrict__ tiles, const int* __restrict__ n_tiles,
+                  int* err) {
     using G = Cfg<SPLIT>;
     constexpr int BN = G::BN;
     // Dense: CTA (x, y) computes rows [128x, 128x + 128) x columns [BN y, BN y + BN).
@@ -155,6 +210,7 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
     auto a_tile = [&](uint8_t* st, int h) { return st + h * G::ATile; };
     auto b_tile = [&](uint8_t* st, int h) { return st + G::NT * G::ATile + h * G::BTile; };
     auto raw_tile = [&](uint8_t* st) { return st + G::NT * (G::ATile + G::BTile); };
+    auto d_tile = [&](uint8_t* st) { return reinterpret_cast<const __half*>(raw_tile(st) + G::RawTile); };
     if (warp == kConvWarps + 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
                      "r"(kTmemCols)
@@ -189,8 +245,11 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                 mbar_arrive_expect_tx(&full_a[s], (uint32_t)(G::NT * G::ATile));
                 tma_2d(a_tile(st, 0), &tmA, kt * kBK, m0, &full_a[s]);
                 if (SPLIT == 3) tma_2d(a_tile(st, 1), &tmA, kt * kBK, M + m0, &full_a[s]);
-                mbar_arrive_expect_tx(&full_raw[s], (uint32_t)G::RawTile);
+                mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(G::RawTile + (d_tma ? G::DTile : 0)));
                 tma_2d(raw_tile(st), &tmB, kt * kBK, nb0, &full_raw[s]);
+                // the block scales of this K step ride in the same stage (8 per row from an
+                // 8-aligned block index, which holds blocks 2kt and 2kt + 1)
+                if (d_tma) tma_2d(raw_tile(st) + G::RawTile, &tmD, (2 * kt) & ~7, nb0, &full_raw[s]);
             }
             // every issued copy lands before the CTA can exit (already true unless a wait failed)
             for (int kt = (issued > kStages ? issued - kStages : 0); kt < issued; kt++) {
@@ -238,12 +297,12 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
             }
             return h2bits(v);
         };
-        uint32_t dnext = load_d(0);
+        uint32_t dnext = d_tma ? 0u : load_d(0);
         for (int kt = 0; kt < nk && ok; kt++) {
             const int s = kt % kStages;
             const uint32_t pu = (uint32_t)((kt / kStages) & 1);
-            const uint32_t dcur = dnext;
-            if (kt + 1 < nk) dnext = load_d(kt + 1);
+            uint32_t dcur = dnext;
+            if (!d_tma && kt + 1 < nk) dnext = load_d(kt + 1);
             uint8_t* st = smem + s * G::Stage;
             ok = __all_sync(0xffffffffu, bar_wait(&full_raw[s], pu, err));  // warp-uniform outcome
             uint4 raw[WPT / 16];
@@ -251,6 +310,10 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
                 const uint4* rp = reinterpret_cast<const uint4*>(raw_tile(st) + brow * kBK + part * WPT);
 #pragma unroll
                 for (int j = 0; j < WPT / 16; j++) raw[j] = rp[j];
+                if (d_tma) {  // rows past N were zero-filled by the copy
+                    const __half* ds = d_tile(st) + brow * 8 + ((2 * kt + (RT == 2 ? part : 0)) & 7);
+                    dcur = h2bits(RT == 2 ? __halves2half2(ds[0], ds[0]) : __halves2half2(ds[0], ds[1]));
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&raw_free[s]);
@@ -259,59 +322,19 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
             if (!ok) break;
             const __half2 dc = *reinterpret_cast<const __half2*>(&dcur);
             const int c0 = part * (WPT / 8);  // first 8-weight chunk of this thread in the row
-            // SPLIT = 3 in half2 arithmetic when |d| < 1/4: then |q d| < 32, so 2048 wh and 2048 d
-            // are finite fp16 values (each thread's weights share one block scale here)
-            const float dfs = __low2float(dc);
-            const bool split_fast = SPLIT == 3 && RT == 2 && fabsf(dfs) < 0.25f;
-            const __half2 d2s = __low2half2(dc);
-            const __half2 d2k = __float2half2_rn(dfs * 2048.0f);
-            const __half2 m2k = __float2half2_rn(-2048.0f);
+            if constexpr (SPLIT == 3) {
+                // exact hi/lo pair (RT == 2: each thread's 32 weights share one block scale)
+                split3_convert(*reinterpret_cast<const uint4(*)[2]>(raw), dc, b_tile(st, 0), b_tile(st, 1), brow, c0);
+            } else {
 #pragma unroll
-            for (int c = 0; c < WPT / 8; c++) {
-                const uint4 r4 = raw[c >> 1];
-                const uint32_t w0 = (c & 1) ? r4.z : r4.x, w1 = (c & 1) ? r4.w : r4.y;
-                if (SPLIT == 1) {
+                for (int c = 0; c < WPT / 8; c++) {
+                    const uint4 r4 = raw[c >> 1];
+                    const uint32_t w0 = (c & 1) ? r4.z : r4.x, w1 = (c & 1) ? r4.w : r4.y;
                     const __half2 d2 = (c >> 2) ? __high2half2(dc) : __low2half2(dc);
                     uint4 o;
                     dq4(w0, d2, o.x, o.y);
                     dq4(w1, d2, o.z, o.w);
                     *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = o;
-                } else if (split_fast) {
-                    // wh = RN16(q d) (one HMUL2) and wl = RN16((q d - wh) 2048) (one HFMA2 on
-                    // d 2048 and -2048 wh, both exact scalings): the same bits as the f32 path
-                    // below, at full-rate half2 arithmetic instead of conversions
-                    uint32_t hw[4], lw[4];
-#pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        const uint32_t u = (j ? w1 : w0) ^ 0x80808080u;  // b + 128 per byte
-                        uint32_t pa = __byte_perm(u, 0x64646464u, 0x5140), pb = __byte_perm(u, 0x64646464u, 0x5342);
-                        const __half2 bias = __float2half2_rn(1152.0f);
-                        const __half2 qa = __hsub2(*reinterpret_cast<__half2*>(&pa), bias);  // exact q pairs
-                        const __half2 qb = __hsub2(*reinterpret_cast<__half2*>(&pb), bias);
-                        const __half2 ha = __hmul2(qa, d2s), hb = __hmul2(qb, d2s);
-                        hw[2 * j] = h2bits(ha);
-                        hw[2 * j + 1] = h2bits(hb);
-                        lw[2 * j] = h2bits(__hfma2(qa, d2k, __hmul2(ha, m2k)));
-                        lw[2 * j + 1] = h2bits(__hfma2(qb, d2k, __hmul2(hb, m2k)));
-                    }
-                    *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                    *reinterpret_cast<uint4*>(b_tile(st, 1) + sw128(brow, c0 + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-                } else {
-                    const float df = __low2float(dc);
-                    uint32_t hw[4], lw[4];
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const uint32_t word = j < 2 ? w0 : w1;
-                        const int sh = 16 * (j & 1);
-                        const float wa = (float)(int8_t)((word >> sh) & 0xff) * df;        // exact
-                        const float wb = (float)(int8_t)((word >> (sh + 8)) & 0xff) * df;
-                        const __half2 h = __floats2half2_rn(wa, wb);
-                        const float2 hf = __half22float2(h);
-                        hw[j] = h2bits(h);
-                        lw[j] = h2bits(__floats2half2_rn((wa - hf.x) * 2048.f, (wb - hf.y) * 2048.f));  // exact
-                    }
-                    *reinterpret_cast<uint4*>(b_tile(st, 0) + sw128(brow, c0 + c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                    *reinterpret_cast<uint4*>(b_tile(st, 1) + sw128(brow, c0 + c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                 }
             }
             fence_async_smem();
@@ -357,6 +380,284 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
     __syncthreads();
     if (warp == kConvWarps + 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---- few-row form (M <= 32 activation rows): weights on the MMA's M side, split-K ---------------
+// With a handful of activation rows (a multi-sequence decode step) the 128-row activation tile
+// above leaves 7/8 of every MMA empty and the grid holds only ceil(N / 128) CTAs, so the weights
+// stream through a few SMs.  Here a work item is 128 weight rows (the UMMA's M operand) against
+// all MN (16 or 32) activation rows (its N operand) over one of S splits of the K steps, and one
+// persistent CTA per SM walks its items:
+//   warp 8    streams the raw int8 weight tiles (8 KB per K step) into a ring that is released
+//             as soon as the converters hold a tile in registers, so 64-80 KB of HBM reads per
+//             SM stay in flight across item boundaries;
+//   warp 10   loads the fp16 activation tiles (hi, lo) of each K step into their own ring;
+//   warps 0-7 convert weights to the exact fp16 hi/lo pair in the operand ring, and after an
+//             item's last K step read its accumulators and store them;
+//   warp 9    issues D1 += wh.xh, D2 += wl.xh + wh.xl into one of two TMEM accumulator pairs
+//             (items alternate, so an item's MMAs overlap the previous item's epilogue).
+// With S > 1 each split writes its partial sums to scratch [S][M][N]; the last CTA to finish a row
+// tile (arrival ticket) adds them in split order, so the result does not depend on scheduling.
+// Exact three-product split only (as SPLIT = 3 above).
+constexpr int kRowsBM = 128;       // weight rows per item
+constexpr int kRowsMaxItems = 296; // S * row tiles <= this when S > 1
+constexpr int kRowsTickets = 256;  // >= row tiles whenever S > 1
+constexpr int kRowsWarps = 11;     // 8 converters, raw producer, MMA issuer, activation producer
+constexpr int kRowsThreads = kRowsWarps * 32;
+
+// Three rings: raw int8 weights (TMA from HBM, released once the converters hold a tile in
+// registers), fp16 activations (TMA from L2, released by the MMAs that read them) and converted
+// fp16 weights (released by the MMAs).  The activation ring is deep enough that its loads never
+// wait on the MMA chain.  208 KB of shared memory either way.
+template <int MN>
+struct RowsCfg {
+    static constexpr int RawStages = MN == 16 ? 8 : 7;
+    static constexpr int OpStages = 3;
+    static constexpr int XStages = MN == 16 ? 8 : 6;
+    static constexpr int WTile = kRowsBM * kBK * 2;  // 16 KB fp16 weights (hi or lo)
+    static constexpr int XTile = MN * kBK * 2;       // 2 / 4 KB fp16 activations (hi or lo)
+    static constexpr int RawTile = kRowsBM * kBK;    // 8 KB int8
+    static constexpr int DTile = kRowsBM * 16;       // block scales: 8 fp16 per row (4 K steps)
+    static constexpr int RawStage = RawTile + DTile;
+    static constexpr int OpStage = 2 * WTile;
+    static constexpr int XStage = 2 * XTile;
+    static constexpr int Smem = OpStages * OpStage + XStages * XStage + RawStages * RawStage + 1024;
+    static constexpr uint32_t Idesc = (1u << 4) | ((uint32_t)(MN >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
+    static constexpr uint32_t AccCols = 64;           // per accumulator pair: D1 at +0, D2 at +32
+    static constexpr uint32_t TmemCols = 2 * AccCols;
+};
+
+template <int MN>
+__global__ void __launch_bounds__(kRowsThreads, 1)
+    k_gemm_q8_rows(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmD, int d_tma, int M, int K,
+                   const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, float* __restrict__ part,
+                   unsigned int* __restrict__ tickets, int S, int n_items, int* err) {
+    using G = RowsCfg<MN>;
+    extern __shared__ uint8_t smem_raw[];
+    constexpr int R = G::RawStages, O = G::OpStages, X = G::XStages;
+    __shared__ __align__(8) uint64_t full_raw[R], raw_free[R], full_x[X], x_free[X], conv_done[O], op_free[O],
+        acc_full[2], acc_free[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int last_flag;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int nk = (K + kBK - 1) / kBK;
+    const int KB = K >> 5;
+    // shared memory: converted weight stages | activation stages | raw weight stages
+    auto w_tile = [&](int os, int h) { return smem + os * G::OpStage + h * G::WTile; };
+    auto x_tile = [&](int xs, int h) { return smem + O * G::OpStage + xs * G::XStage + h * G::XTile; };
+    auto raw_tile = [&](int rs) { return smem + O * G::OpStage + X * G::XStage + rs * G::RawStage; };
+    auto d_tile = [&](int rs) { return reinterpret_cast<const __half*>(raw_tile(rs) + G::RawTile); };
+    // item it: row tile it / S, split it % S (K steps [kt0, kt1))
+    auto item_range = [&](int it, int& n0, int& sp, int& kt0, int& kt1) {
+        n0 = (it / S) * kRowsBM;
+        sp = it % S;
+        kt0 = (int)(((long long)sp * nk) / S);
+        kt1 = (int)(((long long)(sp + 1) * nk) / S);
+    };
+    if (warp == 9) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "r"(G::TmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (t == 0) {
+        for (int r = 0; r < R; r++) {
+            mbar_init(&full_raw[r], 1);
+            mbar_init(&raw_free[r], kConvWarps);
+        }
+        for (int x = 0; x < X; x++) {
+            mbar_init(&full_x[x], 1);
+            mbar_init(&x_free[x], 1);
+        }
+        for (int o = 0; o < O; o++) {
+            mbar_init(&conv_done[o], kConvWarps);
+            mbar_init(&op_free[o], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_free[a], kConvWarps);
+        }
+        mbar_fence_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+    if (warp == 8) {
+        if (lane == 0) {  // raw weight producer
+            int r = 0;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                int n0, sp, kt0, kt1;
+                item_range(it, n0, sp, kt0, kt1);
+                for (int kt = kt0; kt < kt1 && ok; kt++, r++) {
+                    const int rs = r % R;
+                    if (r >= R) ok = bar_wait(&raw_free[rs], (uint32_t)((r / R - 1) & 1), err);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&full_raw[rs], (uint32_t)(G::RawTile + (d_tma ? G::DTile : 0)));
+                    tma_2d(raw_tile(rs), &tmW, kt * kBK, n0, &full_raw[rs]);
+                    if (d_tma) tma_2d(raw_tile(rs) + G::RawTile, &tmD, (2 * kt) & ~7, n0, &full_raw[rs]);
+                }
+            }
+            for (int i = (r > R ? r - R : 0); i < r; i++)  // copies land before exit
+                bar_wait(&full_raw[i % R], (uint32_t)((i / R) & 1), err);
+        }
+    } else if (warp == 10) {
+        if (lane == 0) {  // activation producer: hi rows at 0, lo rows at M
+            int o = 0;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                int n0, sp, kt0, kt1;
+                item_range(it, n0, sp, kt0, kt1);
+                for (int kt = kt0; kt < kt1 && ok; kt++, o++) {
+                    const int xs = o % X;
+                    if (o >= X) ok = bar_wait(&x_free[xs], (uint32_t)((o / X - 1) & 1), err);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(&full_x[xs], (uint32_t)G::XStage);
+                    tma_2d(x_tile(xs, 0), &tmX, kt * kBK, 0, &full_x[xs]);
+                    tma_2d(x_tile(xs, 1), &tmX, kt * kBK, M, &full_x[xs]);
+                }
+            }
+            for (int i = (o > X ? o - X : 0); i < o; i++)
+                bar_wait(&full_x[i % X], (uint32_t)((i / X) & 1), err);
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {  // MMA issuer
+            int o = 0, j = 0;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, j++) {
+                int n0, sp, kt0, kt1;
+                item_range(it, n0, sp, kt0, kt1);
+                const int ab = j & 1;
+                if (j >= 2) ok = bar_wait(&acc_free[ab], (uint32_t)((j / 2 - 1) & 1), err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t acc_d = tmem + (uint32_t)ab * G::AccCols;
+                for (int kt = kt0; kt < kt1 && ok; kt++, o++) {
+                    const int os = o % O, xs = o % X;
+                    ok = bar_wait(&full_x[xs], (uint32_t)((o / X) & 1), err) &&
+                         bar_wait(&conv_done[os], (uint32_t)((o / O) & 1), err);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t wh = smem_u32(w_tile(os, 0)), wl = smem_u32(w_tile(os, 1));
+                    const uint32_t xh = smem_u32(x_tile(xs, 0)), xl = smem_u32(x_tile(xs, 1));
+#pragma unroll
+                    for (int ks = 0; ks < kBK / 16; ks++) {
+                        const uint32_t acc = (kt != kt0 || ks != 0) ? 1u : 0u;
+                        umma_f16(acc_d, umma_desc(wh + 32u * ks), umma_desc(xh + 32u * ks), G::Idesc, acc);
+                        umma_f16(acc_d + 32u, umma_desc(wl + 32u * ks), umma_desc(xh + 32u * ks), G::Idesc, acc);
+                        umma_f16(acc_d + 32u, umma_desc(wh + 32u * ks), umma_desc(xl + 32u * ks), G::Idesc, 1u);
+                    }
+                    umma_commit(&op_free[os]);
+                    umma_commit(&x_free[xs]);
+                }
+                umma_commit(&acc_full[ab]);  // covers the item's MMAs (also after a failed wait)
+            }
+        }
+    } else {
+        // converters (two threads per weight row, one Q8_0 block each per K step) and epilogue
+        const int brow = t >> 1, part_k = t & 1;
+        const int q = warp & 3, hb = warp >> 2;  // epilogue: TMEM lanes 32q.., activation rows 16hb..
+        int o = 0, j = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, j++) {
+            int n0, sp, kt0, kt1;
+            item_range(it, n0, sp, kt0, kt1);
+            const int n = n0 + brow;
+            auto load_d = [&](int kt) -> uint32_t {
+                __half2 v = __float2half2_rn(0.f);
+                const int kb = 2 * kt + part_k;
+                if (n < N && kb < KB) {
+                    const __half h = d[(size_t)n * KB + kb];
+                    v = __halves2half2(h, h);
+                }
+                return h2bits(v);
+            };
+            uint32_t dnext = d_tma ? 0u : load_d(kt0);
+            for (int kt = kt0; kt < kt1 && ok; kt++, o++) {
+                const int rs = o % R, os = o % O;
+                uint32_t dcur = dnext;
+                if (!d_tma && kt + 1 < kt1) dnext = load_d(kt + 1);
+                ok = __all_sync(0xffffffffu, bar_wait(&full_raw[rs], (uint32_t)((o / R) & 1), err));
+                uint4 raw[2];
+                if (ok) {
+                    const uint4* rp = reinterpret_cast<const uint4*>(raw_tile(rs) + brow * kBK + part_k * 32);
+                    raw[0] = rp[0];
+                    raw[1] = rp[1];
+                    if (d_tma) {  // rows past N were zero-filled by the copy
+                        const __half h = d_tile(rs)[brow * 8 + ((2 * kt + part_k) & 7)];
+                        dcur = h2bits(__halves2half2(h, h));
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&raw_free[rs]);
+                if (ok && o >= O)
+                    ok = __all_sync(0xffffffffu, bar_wait(&op_free[os], (uint32_t)((o / O - 1) & 1), err));
+                if (!ok) break;
+                split3_convert(raw, *reinterpret_cast<const __half2*>(&dcur), w_tile(os, 0), w_tile(os, 1), brow,
+                               part_k * 4);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&conv_done[os]);
+            }
+            // epilogue of item j: accumulator pair j & 1
+            const int ab = j & 1;
+            if (ok) ok = bar_wait(&acc_full[ab], (uint32_t)((j / 2) & 1), err);
+            ok = __all_sync(0xffffffffu, ok);
+            tc_fence_after();
+            float f[16];
+            const bool has = hb * 16 < MN;
+            if (ok && has) {
+                uint32_t v[16], v2[16];
+                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)ab * G::AccCols + (uint32_t)(hb * 16);
+                tmem_ld16(taddr, v);
+                tmem_ld16(taddr + 32u, v2);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int i = 0; i < 16; i++) f[i] = fmaf(__uint_as_float(v2[i]), 1.0f / 2048.0f, __uint_as_float(v[i]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_free[ab]);
+            const int nn = n0 + q * 32 + lane;
+            if (ok && has && nn < N) {
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int m = hb * 16 + i;
+                    if (m < M) {
+                        if (S == 1) C[(size_t)m * ldc + nn] = f[i];
+                        else part[((size_t)sp * M + m) * N + nn] = f[i];
+                    }
+                }
+            }
+            if (S > 1) {  // every item takes a ticket (also after a failed wait, so the tickets reset)
+                __threadfence();
+                named_bar(1, kConvWarps * 32);
+                if (t == 0) {
+                    const int tile = it / S;
+                    const unsigned prev = atomicAdd(&tickets[tile], 1u);
+                    last_flag = prev == (unsigned)(S - 1);
+                    if (last_flag) tickets[tile] = 0u;
+                }
+                named_bar(1, kConvWarps * 32);
+                if (last_flag) {
+                    __threadfence();
+                    for (int i = t; i < M * kRowsBM; i += kConvWarps * 32) {
+                        const int m = i / kRowsBM, c = n0 + i % kRowsBM;
+                        if (c < N) {
+                            float acc = __ldcg(part + (size_t)m * N + c);
+                            for (int s2 = 1; s2 < S; s2++) acc += __ldcg(part + ((size_t)s2 * M + m) * N + c);
+                            C[(size_t)m * ldc + c] = acc;
+                        }
+                    }
+                }
+                named_bar(1, kConvWarps * 32);  // last_flag is rewritten by the next item
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(G::TmemCols));
 }
 
 // x -> (xh, xl) with xh = fp16(x), xl = fp16((x - xh) * 2048), rows of xl after those of xh
@@ -420,6 +721,15 @@ CUtensorMap tensor_map(void* base, CUtensorMapDataType type, int elem_bytes, uin
     return m;
 }
 
+// Block scales by TMA when the rows of the scale plane are 16-byte multiples (K % 256 == 0): a
+// box of 8 scales x `rows` rows per K step.  Otherwise the converters load them directly.
+bool scales_by_tma(const DTensor& W) { return (W.K / 32) % 8 == 0 && ((uintptr_t)W.d & 15u) == 0; }
+
+CUtensorMap scale_map(const DTensor& W, int rows) {
+    return tensor_map(W.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)(W.K / 32), (uint64_t)W.rows, 8,
+                      (uint32_t)rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 }  // namespace
 
 template <int SPLIT>
@@ -433,6 +743,8 @@ void launch_split(const DTensor& W, int64_t N, const __half* a16, int M, float* 
                                       (uint64_t)M * (SPLIT == 3 ? 2 : 1), kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
     const CUtensorMap tb = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, kBK,
                                       G::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const bool d_tma = scales_by_tma(W);
+    const CUtensorMap td = d_tma ? scale_map(W, G::BN) : tb;
     static bool init = false;
     if (!init) {
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_tma<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::Smem));
@@ -441,10 +753,79 @@ void launch_split(const DTensor& W, int64_t N, const __half* a16, int M, float* 
     QQ_CHECK(N <= (int64_t)65535 * G::BN, QQ_ERR_INVALID, "tensor-core Q8_0 matmul: too many columns");
     const unsigned gx = groups ? (unsigned)groups->max_tiles : (unsigned)((M + kBM - 1) / kBM);
     dim3 grid(gx, (unsigned)((N + G::BN - 1) / G::BN));
-    k_gemm_q8_tma<SPLIT><<<grid, kThreadsG2, G::Smem, s>>>(ta, tb, M, (int)K, W.d, (int)N, y, ldc,
+    k_gemm_q8_tma<SPLIT><<<grid, kThreadsG2, G::Smem, s>>>(ta, tb, td, d_tma ? 1 : 0, M, (int)K, W.d, (int)N, y, ldc,
                                                            groups ? groups->tiles : nullptr,
                                                            groups ? groups->n_tiles : nullptr, kernel_err_ptr());
     QQ_CUDA_TRY(cudaGetLastError());
+}
+
+namespace {
+
+// splits S of the K steps per 128-row tile: fewest rounds of one item per SM per unit of work
+int rows_splits(int64_t N, int64_t K) {
+    const int tiles = (int)((N + kRowsBM - 1) / kRowsBM);
+    const int nk = (int)((K + kBK - 1) / kBK);
+    const int sms = num_sms();
+    int best = 1;
+    double best_t = (double)((tiles + sms - 1) / sms);
+    for (int S = 2; S <= 16 && 2 * S <= nk && tiles * S <= kRowsMaxItems; S++) {
+        const double tt = (double)((tiles * S + sms - 1) / sms) / S;
+        if (tt < best_t - 1e-9) {
+            best = S;
+            best_t = tt;
+        }
+    }
+    return best;
+}
+
+template <int MN>
+void launch_rows(const DTensor& W, const __half* a16, int M, float* y, int ldc, void* rows_scratch, cudaStream_t s) {
+    using G = RowsCfg<MN>;
+    const int64_t K = W.K, N = W.rows;
+    const CUtensorMap tx = tensor_map(const_cast<__half*>(a16), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
+                                      (uint64_t)M * 2, kBK, MN, CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMap tw = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, kBK,
+                                      kRowsBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const bool d_tma = scales_by_tma(W);
+    const CUtensorMap td = d_tma ? scale_map(W, kRowsBM) : tw;
+    static bool init = false;
+    if (!init) {
+        QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_rows<MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::Smem));
+        init = true;
+    }
+    const int S = rows_splits(N, K);
+    const int64_t items = ((N + kRowsBM - 1) / kRowsBM) * S;
+    QQ_CHECK(items <= (int64_t)1 << 30, QQ_ERR_INVALID, "few-row Q8_0 matmul: too many rows");
+    const unsigned grid = (unsigned)std::min<int64_t>(items, num_sms());
+    unsigned int* tickets = static_cast<unsigned int*>(rows_scratch);
+    float* part = reinterpret_cast<float*>(static_cast<char*>(rows_scratch) + kRowsTickets * sizeof(unsigned int));
+    k_gemm_q8_rows<MN><<<grid, kRowsThreads, G::Smem, s>>>(tx, tw, td, d_tma ? 1 : 0, M, (int)K, W.d, (int)N, y, ldc,
+                                                           part, tickets, S,
+                                                           (int)items, kernel_err_ptr());
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+}  // namespace
+
+size_t gemm_rows_scratch_bytes(int M) {
+    return kRowsTickets * sizeof(unsigned int) + (size_t)kRowsMaxItems * kRowsBM * (size_t)std::max(M, 1) * 4;
+}
+
+void gemm_rows_reset(void* rows_scratch, cudaStream_t s) {
+    QQ_CUDA_TRY(cudaMemsetAsync(rows_scratch, 0, kRowsTickets * sizeof(unsigned int), s));
+}
+
+void launch_gemm_q8_few(const DTensor& W, const float* x, int M, __half* x16, void* rows_scratch, float* y,
+                        cudaStream_t s) {
+    if (M <= 0 || W.rows <= 0) return;
+    if (!rows_scratch || M > kGemmFewMax || !gemm_exact()) {
+        launch_gemm_q8(W, x, M, x16, y, s);
+        return;
+    }
+    QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
+    launch_f32_to_f16(x, x16, (size_t)M * W.K, s);
+    if (M <= 16) launch_rows<16>(W, x16, M, y, (int)W.rows, rows_scratch, s);
+    else launch_rows<32>(W, x16, M, y, (int)W.rows, rows_scratch, s);
 }
 
 void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16, int M, float* y, int ldc,

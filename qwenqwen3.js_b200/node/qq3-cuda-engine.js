@@ -75,6 +75,16 @@ class CudaEngineBase {
         return this.bufLogits;
     }
 
+    // One step of several sequences (qq_forward_batch; the engine was created with nSeq > max(seqs)):
+    // forward(tokenIds[i], positions[i], skipLogits) of sequence seqs[i].  Resolves to
+    // {logits: Float32Array(n * nVocab), argmax: Int32Array(n)}, or null with skipLogits.
+    async forwardBatch(seqs, tokenIds, positions, skipLogits = false) {
+        const r = await qq3.forwardBatch(this.model, Int32Array.from(seqs), Int32Array.from(tokenIds),
+                                         Int32Array.from(positions), skipLogits ? 0 : 1, -1, this.nVocab);
+        if (this.onRouterUpdate) this._readbackRoutingData();
+        return skipLogits ? null : r;
+    }
+
     // routing records [topK ids | topK weights | nExperts probs] (webgpu.js:1922-1945)
     _readbackRoutingData() {
         const k = this.nExpertsUsed, n = this.nExperts;

@@ -248,6 +248,85 @@ static napi_value Forward(napi_env env, napi_callback_info info) {
     return promise;
 }
 
+// ---- forwardBatch: one step of several sequences (qq_forward_batch) as async work ----
+struct BatchWork {
+    napi_async_work work;
+    napi_deferred deferred;
+    qq_model* m;
+    std::vector<int32_t> seqs, tokens, positions, argmax;
+    int want_logits, suppress, n_vocab;
+    std::vector<float> logits;
+    int rc = 0;
+    std::string err;
+};
+
+static void BatchExecute(napi_env, void* data) {
+    BatchWork* w = static_cast<BatchWork*>(data);
+    const int n = (int)w->seqs.size();
+    if (w->want_logits) {
+        w->logits.resize((size_t)n * w->n_vocab);
+        w->argmax.assign(n, -1);
+    }
+    w->rc = qq_forward_batch(w->m, w->seqs.data(), w->tokens.data(), w->positions.data(), n, w->want_logits,
+                             w->want_logits ? w->logits.data() : nullptr, w->want_logits ? w->argmax.data() : nullptr,
+                             w->suppress);
+    if (w->rc) w->err = qq_last_error();
+}
+
+static void BatchComplete(napi_env env, napi_status, void* data) {
+    BatchWork* w = static_cast<BatchWork*>(data);
+    if (w->rc) {
+        napi_value msg, err;
+        napi_create_string_utf8(env, ("libqq3cuda: " + w->err).c_str(), NAPI_AUTO_LENGTH, &msg);
+        napi_create_error(env, nullptr, msg, &err);
+        napi_reject_deferred(env, w->deferred, err);
+    } else {
+        napi_value result;
+        napi_create_object(env, &result);
+        if (w->want_logits) {
+            napi_value ab, f32, ab2, i32;
+            void* buf = nullptr;
+            napi_create_arraybuffer(env, w->logits.size() * 4, &buf, &ab);
+            std::memcpy(buf, w->logits.data(), w->logits.size() * 4);
+            napi_create_typedarray(env, napi_float32_array, w->logits.size(), ab, 0, &f32);
+            napi_set_named_property(env, result, "logits", f32);  // row i = sequence seqs[i]
+            napi_create_arraybuffer(env, w->argmax.size() * 4, &buf, &ab2);
+            std::memcpy(buf, w->argmax.data(), w->argmax.size() * 4);
+            napi_create_typedarray(env, napi_int32_array, w->argmax.size(), ab2, 0, &i32);
+            napi_set_named_property(env, result, "argmax", i32);
+        }
+        napi_resolve_deferred(env, w->deferred, result);
+    }
+    napi_delete_async_work(env, w->work);
+    delete w;
+}
+
+// forwardBatch(model, Int32Array seqs, Int32Array tokens, Int32Array positions, wantLogits, suppressId,
+//              nVocab) -> Promise<{logits, argmax}>
+static napi_value ForwardBatch(napi_env env, napi_callback_info info) {
+    size_t argc = 7;
+    napi_value argv[7];
+    NAPI_CALL(env, napi_get_cb_info(env, info, &argc, argv, nullptr, nullptr));
+    BatchWork* w = new BatchWork;
+    w->m = static_cast<qq_model*>(unwrap_ptr(env, argv[0]));
+    size_t n = 0;
+    int32_t* p = typed_data<int32_t>(env, argv[1], &n);
+    w->seqs.assign(p, p + n);
+    p = typed_data<int32_t>(env, argv[2], &n);
+    w->tokens.assign(p, p + n);
+    p = typed_data<int32_t>(env, argv[3], &n);
+    w->positions.assign(p, p + n);
+    w->want_logits = get_i32(env, argv[4]);
+    w->suppress = get_i32(env, argv[5]);
+    w->n_vocab = get_i32(env, argv[6]);
+    napi_value promise, name;
+    napi_create_promise(env, &w->deferred, &promise);
+    napi_create_string_utf8(env, "qq3.forwardBatch", NAPI_AUTO_LENGTH, &name);
+    napi_create_async_work(env, nullptr, name, BatchExecute, BatchComplete, w, &w->work);
+    napi_queue_async_work(env, w->work);
+    return promise;
+}
+
 // readRouting(model, moeLayer, recLen) -> Float32Array [idx | w | probs] (webgpu.js:1617-1618)
 static napi_value ReadRouting(napi_env env, napi_callback_info info) {
     size_t argc = 3;
@@ -309,6 +388,7 @@ static napi_value ModuleInit(napi_env env, napi_value exports) {
         {"freeTensor", nullptr, FreeTensor, nullptr, nullptr, nullptr, napi_default, nullptr},
         {"modelCreate", nullptr, ModelCreate, nullptr, nullptr, nullptr, napi_default, nullptr},
         {"forward", nullptr, Forward, nullptr, nullptr, nullptr, napi_default, nullptr},
+        {"forwardBatch", nullptr, ForwardBatch, nullptr, nullptr, nullptr, napi_default, nullptr},
         {"readRouting", nullptr, ReadRouting, nullptr, nullptr, nullptr, napi_default, nullptr},
         {"setExpertMask", nullptr, SetExpertMask, nullptr, nullptr, nullptr, napi_default, nullptr},
         {"reset", nullptr, Reset, nullptr, nullptr, nullptr, napi_default, nullptr},

@@ -84,9 +84,11 @@ def test_q8_matmul_large_m_sampled_rows(qq3, orc, gpu_ctx, torch, M):
     W.free()
 
 
-@pytest.mark.parametrize("M,N,K", [(2, 96, 32), (3, 1000, 96), (130, 257, 2048), (129, 4096, 1024)])
+@pytest.mark.parametrize("M,N,K", [(2, 96, 32), (3, 1000, 96), (17, 1000, 4096), (32, 3072, 12288),
+                                   (130, 257, 2048), (129, 4096, 1024)])
 def test_q8_matmul_tensor_core_ragged(qq3, orc, gpu_ctx, torch, M, N, K):
-    """Ragged tiles of the tensor-core path: M and N off the 128 x 256 tile, K % 64 == 32."""
+    """Ragged tiles of the tensor-core paths: M and N off the tiles, K % 64 == 32; M <= 32 takes
+    the few-row kernel (16- and 32-row operand tiles, K split over CTAs), larger M the 128-row one."""
     orc.set_threads(8)
     raw = qq3.synth.q8_0_blocks(N * K, seed=31 * N + K, mode=1)
     x = qq3.synth.normal_f32(M * K, seed=5 * M + 1).reshape(M, K)
