@@ -460,6 +460,8 @@ def run_batch_decode(args, ws, rank, local):
     qq3.build.build_all()
     torch.cuda.set_device(local)
     spec = qq3.synth.qwen3_8b(seed=SEED + rank)
+    if args.layers:
+        spec.n_layers = args.layers  # profiling knob: every layer streams the same bytes
     n = args.seqs
     prompt = args.prompt if args.prompt is not None else 4096
     g = qq3.synth.memory_model(spec)
@@ -507,7 +509,7 @@ def run_batch_decode(args, ws, rank, local):
            "value": round(n / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "int8xf16",
            "data": "synthetic (seeded random-init Q8_0 weights, uniform prompt ids)",
-           "config": {"workload": "qwen3-8b-batch-decode", "sequences": n, "prompt": prompt,
+           "config": {"workload": "qwen3-8b-batch-decode", "sequences": n, "prompt": prompt, "layers": L,
                       "path": "qq_forward_batch: tcgen05 GEMMs over the 16 rows, f32 KV cache",
                       "l2": "weights 8.04 GB + KV per step, far above the 126 MB L2"},
            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
@@ -570,6 +572,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=None,
                     help=f"prompt length (decode: {PROMPT}; batch-decode: 4096 per sequence)")
     ap.add_argument("--seqs", type=int, default=16, help="concurrent sequences for --case batch-decode")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="layers of the batch-decode model (profiling knob; default: all 36 of the configuration)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=8)

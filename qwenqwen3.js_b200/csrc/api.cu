@@ -131,6 +131,8 @@ struct qq_model {
     int bt_cap = 0;
     int* bt_i = nullptr;
     float* bt_logits = nullptr;
+    float* bt_attn = nullptr;  // split-attention partial states of the rows
+    void* bt_keys = nullptr;   // row-argmax partial keys
     int* h_bt = nullptr;
     qq3::tword* tarena = nullptr;    // tagged activations: one buffer per phase output
     size_t tarena_len = 0;
@@ -156,6 +158,8 @@ void free_model(qq_model* m) {
     if (m->pf_arena) cudaFree(m->pf_arena);
     if (m->bt_i) cudaFree(m->bt_i);
     if (m->bt_logits) cudaFree(m->bt_logits);
+    if (m->bt_attn) cudaFree(m->bt_attn);
+    if (m->bt_keys) cudaFree(m->bt_keys);
     if (m->h_bt) cudaFreeHost(m->h_bt);
     if (m->tarena) cudaFree(m->tarena);
     if (m->aarena) cudaFree(m->aarena);
@@ -871,7 +875,7 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
 // append, attention and the short-conv state; then the output norm, the lm_head GEMM and a
 // first-max argmax per row.  The MoE routing record kept for onRouterUpdate is that of the last
 // row.  Same results as T separate forward() calls up to the GEMM's f32 accumulation order.
-void batch_step(qq_model* m, int T, bool want_logits) {
+void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
     const qq_model_desc& d = m->d;
     cudaStream_t s = m->ctx->stream;
     const int E = d.n_embd, hd = d.head_dim;
@@ -897,8 +901,8 @@ void batch_step(qq_model* m, int T, bool want_logits) {
             float* kc = m->k_cache + L.attn_slot * m->kv_stride_layer();
             float* vc = m->v_cache + L.attn_slot * m->kv_stride_layer();
             qq3::launch_kv_append_at(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, seq, pos, m->kv_stride_seq(), kc, vc, s);
-            qq3::launch_attn_rows_at(b.q, kc, vc, T, seq, pos, m->kv_stride_seq(), d.n_head, d.n_head_kv, hd,
-                                     d.max_ctx, b.attn, s);
+            qq3::launch_attn_rows_split(b.q, kc, vc, T, seq, pos, max_len, m->kv_stride_seq(), d.n_head, d.n_head_kv,
+                                        hd, d.max_ctx, m->bt_attn, b.attn, s);
             qq3::launch_gemm_q8_few(*L.t[QQ_WO], b.attn, T, b.x16, b.rows, b.tmp, s);
         } else {
             qq3::launch_gemm_q8_few(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.rows, b.bcx, s);
@@ -933,7 +937,7 @@ void batch_step(qq_model* m, int T, bool want_logits) {
     qq3::launch_rmsnorm(b.hidden, T, E, m->out_norm->f32, d.rms_eps, b.xn, s);
     const DTensor* out = m->output ? m->output : m->tok_embd;
     qq3::launch_gemm_q8_few(*out, b.xn, T, b.x16, b.rows, m->bt_logits, s);
-    qq3::launch_argmax_rows(m->bt_logits, T, d.n_vocab, m->suppress, m->bt_i + 3 * m->bt_cap, s);
+    qq3::launch_argmax_rows(m->bt_logits, T, d.n_vocab, m->suppress, m->bt_keys, m->bt_i + 3 * m->bt_cap, s);
 }
 
 // grow the multi-sequence row buffers to hold T rows (device and pinned staging)
@@ -942,15 +946,23 @@ void ensure_batch_rows(qq_model* m, int T) {
     QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
     if (m->bt_i) cudaFree(m->bt_i);
     if (m->bt_logits) cudaFree(m->bt_logits);
+    if (m->bt_attn) cudaFree(m->bt_attn);
+    if (m->bt_keys) cudaFree(m->bt_keys);
     if (m->h_bt) cudaFreeHost(m->h_bt);
     m->bt_i = nullptr;
     m->bt_logits = nullptr;
+    m->bt_attn = nullptr;
+    m->bt_keys = nullptr;
     m->h_bt = nullptr;
     m->bt_cap = 0;
     int cap = 16;
     while (cap < T) cap *= 2;
     m->bt_i = static_cast<int*>(dmalloc(sizeof(int) * 4 * cap));
     m->bt_logits = static_cast<float*>(dmalloc(sizeof(float) * (size_t)cap * m->d.n_vocab));
+    m->bt_keys = dmalloc(qq3::argmax_rows_scratch_bytes(cap));
+    if (m->n_attn > 0)
+        m->bt_attn = static_cast<float*>(
+            dmalloc(sizeof(float) * qq3::attn_rows_part_floats(cap, m->d.n_head, m->d.head_dim, m->d.max_ctx)));
     QQ_CUDA_TRY(cudaMallocHost(&m->h_bt, sizeof(int) * 4 * cap));
     m->bt_cap = cap;
 }
@@ -1390,12 +1402,14 @@ int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_i
             return;
         }
         ensure_batch_rows(m, n);
+        int max_len = 1;
         for (int i = 0; i < n; i++) {
             m->h_bt[i] = token_ids[i];
             m->h_bt[m->bt_cap + i] = seq_ids[i];
             m->h_bt[2 * m->bt_cap + i] = positions[i];
+            max_len = std::max(max_len, positions[i] + 1);
         }
-        batch_step(m, n, logits);
+        batch_step(m, n, max_len, logits);
         if (logits && logits_out)
             QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->bt_logits, sizeof(float) * V * n, cudaMemcpyDeviceToHost, s));
         if (logits && argmax_out)

@@ -137,12 +137,21 @@ void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T
 void launch_rope_rows_at(float* x, int T, int n_heads, int hd, const float* cs, const int* pos, cudaStream_t s);
 void launch_kv_append_at(const float* k, const float* v, int T, int n_kv, int hd, int max_ctx, const int* seq,
                          const int* pos, size_t seq_stride, float* kc, float* vc, cudaStream_t s);
-void launch_attn_rows_at(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
-                         size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* out, cudaStream_t s);
 void launch_conv_rows_at(const float* bcx, const float* w, float* state, size_t state_stride, const int* seq, int T,
                          int E, float* y, cudaStream_t s);
-// out[t] = first-max argmax of logits row t, *suppress (nullable; < 0: none) left out
-void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, int* out, cudaStream_t s);
+// out[t] = first-max argmax of logits row t, *suppress (nullable; < 0: none) left out;
+// scratch: argmax_rows_scratch_bytes(T) bytes
+size_t argmax_rows_scratch_bytes(int T);
+void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, void* scratch, int* out,
+                        cudaStream_t s);
+// attention of the rows split over positions (chunks of attn_rows_chunk()), partial states in
+// part (attn_rows_part_floats(T, n_head, hd, max_ctx) floats), merged in split order into out;
+// max_len = the longest row's length (positions attended, pos + 1)
+int attn_rows_chunk();
+size_t attn_rows_part_floats(int T, int n_head, int hd, int max_ctx);
+void launch_attn_rows_split(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
+                            int max_len, size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* part,
+                            float* out, cudaStream_t s);
 
 // ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
 // Each returns false when the shape is outside the streamed path (the caller then uses the

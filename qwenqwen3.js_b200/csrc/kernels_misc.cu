@@ -120,7 +120,9 @@ __global__ void k_rmsnorm(const float* __restrict__ x, int n, const float* __res
 
 void launch_rmsnorm(float* x, int64_t n_rows, int n, const float* w, float eps, float* y, cudaStream_t s) {
     if (n_rows <= 0) return;
-    k_rmsnorm<<<(unsigned)n_rows, 256, 0, s>>>(x, n, w, eps, y);
+    // long rows (the hidden state) get more threads: shorter per-thread sums, less latency
+    const int threads = n >= 2048 ? 1024 : (n >= 512 ? 256 : 128);
+    k_rmsnorm<<<(unsigned)n_rows, threads, 0, s>>>(x, n, w, eps, y);
     QQ_CUDA_TRY(cudaGetLastError());
 }
 

@@ -150,6 +150,67 @@ __device__ __forceinline__ void attn_row(const float* __restrict__ qh, const flo
     for (int j = 0; j < PL; j++) o[j] = acc[j] / l;
 }
 
+// The same over positions [p_begin, p_end) without the final division: writes the partial
+// softmax state (HD accumulators, then max m and sum l) to part (HD + 2 floats); m = -inf and
+// l = 0 for an empty range.
+template <int HD>
+__device__ __forceinline__ void attn_row_part(const float* __restrict__ qh, const float* __restrict__ kb,
+                                              const float* __restrict__ vb, int p_begin, int p_end,
+                                              float* __restrict__ part) {
+    constexpr int PL = HD / 32;
+    const int lane = threadIdx.x & 31;
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    float qv[HD];
+#pragma unroll
+    for (int j = 0; j < HD; j += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(qh + j);
+        qv[j] = v4.x;
+        qv[j + 1] = v4.y;
+        qv[j + 2] = v4.z;
+        qv[j + 3] = v4.w;
+    }
+    float m = -INFINITY, l = 0.f, acc[PL];
+#pragma unroll
+    for (int j = 0; j < PL; j++) acc[j] = 0.f;
+    for (int p0 = p_begin; p0 < p_end; p0 += 32) {
+        const int p = p0 + lane;
+        float s = -INFINITY;
+        if (p < p_end) {
+            const float* kr = kb + (size_t)p * HD;
+            float dot = 0.f;
+#pragma unroll
+            for (int j = 0; j < HD; j += 4) {
+                const float4 k4 = __ldg(reinterpret_cast<const float4*>(kr + j));
+                dot = fmaf(qv[j], k4.x, dot);
+                dot = fmaf(qv[j + 1], k4.y, dot);
+                dot = fmaf(qv[j + 2], k4.z, dot);
+                dot = fmaf(qv[j + 3], k4.w, dot);
+            }
+            s = dot * scale;
+        }
+        const float m_new = fmaxf(m, warp_max(s));
+        const float pl = p < p_end ? expf(s - m_new) : 0.f;
+        const float cf = expf(m - m_new);
+        l = l * cf + warp_sum(pl);
+#pragma unroll
+        for (int j = 0; j < PL; j++) acc[j] *= cf;
+        const int n = min(32, p_end - p0);
+        for (int jj = 0; jj < n; jj++) {
+            const float pj = __shfl_sync(0xffffffffu, pl, jj);
+            const float* vr = vb + (size_t)(p0 + jj) * HD + lane * PL;
+#pragma unroll
+            for (int j = 0; j < PL; j++) acc[j] = fmaf(pj, __ldg(vr + j), acc[j]);
+        }
+        m = m_new;
+    }
+#pragma unroll
+    for (int j = 0; j < PL; j++) part[lane * PL + j] = acc[j];
+    if (lane == 0) {
+        part[HD] = m;
+        part[HD + 1] = l;
+    }
+}
+
 // One CTA per (token t, kv head): warp g scores query head kvh*G + g against positions
 // 0..pos0+t.  q: [T][n_head][HD] (normalised, rotated); out: [T][n_head][HD].
 template <int HD>
@@ -199,18 +260,52 @@ __global__ void k_kv_append_at(const float* __restrict__ k, const float* __restr
     }
 }
 
+// The rows' attention split over positions: CTA (row t, kv head, split p) takes positions
+// [p*chunk, min(len, (p+1)*chunk)) for the G query heads of its kv head (one warp each) and writes
+// partial states part[(t * n_head + h) * n_split + p]; k_attn_merge then combines the splits of
+// each (row, head) in split order: with M = max m_p, out = sum_p e^(m_p - M) acc_p / sum_p e^(m_p - M) l_p.
 template <int HD>
-__global__ void k_attn_rows_at(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                               const int* __restrict__ seq, const int* __restrict__ pos, size_t seq_stride, int n_head,
-                               int n_kv, int max_ctx, float* __restrict__ out) {
-    const int t = blockIdx.x, kvh = blockIdx.y;
+__global__ void k_attn_rows_split(const float* __restrict__ q, const float* __restrict__ kc,
+                                  const float* __restrict__ vc, const int* __restrict__ seq,
+                                  const int* __restrict__ pos, size_t seq_stride, int n_head, int n_kv, int max_ctx,
+                                  int chunk, int n_split, float* __restrict__ part) {
+    const int t = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
     const int G = n_head / n_kv;
     const int warp = threadIdx.x >> 5;
     if (warp >= G) return;
     const int h = kvh * G + warp;
+    const int len = pos[t] + 1;
+    const int b = sp * chunk, e = min(len, b + chunk);
     const size_t base = (size_t)seq[t] * seq_stride + (size_t)kvh * max_ctx * HD;
-    attn_row<HD>(q + ((size_t)t * n_head + h) * HD, kc + base, vc + base, pos[t] + 1,
-                 out + ((size_t)t * n_head + h) * HD);
+    attn_row_part<HD>(q + ((size_t)t * n_head + h) * HD, kc + base, vc + base, b, e,
+                      part + (((size_t)t * n_head + h) * n_split + sp) * (HD + 2));
+}
+
+// one warp per (row, head): lane owns HD/32 output dims
+template <int HD>
+__global__ void k_attn_merge(const float* __restrict__ part, const int* __restrict__ pos, int T, int n_head, int chunk,
+                             int n_split, float* __restrict__ out) {
+    constexpr int PL = HD / 32;
+    const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (w >= T * n_head) return;
+    const int t = w / n_head, h = w % n_head;
+    const int used = (pos[t] + 1 + chunk - 1) / chunk;  // splits holding positions
+    const float* pp = part + ((size_t)t * n_head + h) * n_split * (HD + 2);
+    float M = -INFINITY;
+    for (int sp = 0; sp < used; sp++) M = fmaxf(M, pp[sp * (HD + 2) + HD]);
+    float acc[PL], L = 0.f;
+#pragma unroll
+    for (int j = 0; j < PL; j++) acc[j] = 0.f;
+    for (int sp = 0; sp < used; sp++) {
+        const float* q = pp + sp * (HD + 2);
+        const float f = expf(q[HD] - M);
+        L += f * q[HD + 1];
+#pragma unroll
+        for (int j = 0; j < PL; j++) acc[j] = fmaf(f, q[lane * PL + j], acc[j]);
+    }
+    float* o = out + ((size_t)t * n_head + h) * HD + lane * PL;
+#pragma unroll
+    for (int j = 0; j < PL; j++) o[j] = acc[j] / L;
 }
 
 // one short-conv step per row with its sequence's 2-tap state (lfm2-engine.js:282-325);
@@ -233,15 +328,21 @@ __global__ void k_conv_rows_at(const float* __restrict__ bcx, const float* __res
 }
 
 // first-max argmax of each row of logits [T][V] (sampleGreedy, tensor.js:231-237), the id
-// *suppress (>= 0) left out (thinking suppression, tensor.js:247-248); one CTA per row
-constexpr int kArgmaxThreads = 512;
+// *suppress (>= 0) left out (thinking suppression, tensor.js:247-248), in two passes: CTA
+// (row t, part p) reduces a slice of the row to a packed key (argmax_key: the larger value, then the
+// lower index, wins), then one warp per row takes the largest of the kArgmaxParts keys
+constexpr int kArgmaxThreads = 256;
+constexpr int kArgmaxParts = 32;
 __global__ void __launch_bounds__(kArgmaxThreads)
-    k_argmax_rows(const float* __restrict__ logits, int V, const int* __restrict__ suppress, int* __restrict__ out) {
-    const int t = blockIdx.x;
+    k_argmax_rows_part(const float* __restrict__ logits, int V, const int* __restrict__ suppress,
+                       unsigned long long* __restrict__ keys) {
+    const int t = blockIdx.x, p = blockIdx.y;
     const int skip = suppress ? *suppress : -1;
+    const int per = (V + kArgmaxParts - 1) / kArgmaxParts;
+    const int b = p * per, e = min(V, b + per);
     const float* r = logits + (size_t)t * V;
     unsigned long long best = 0ull;
-    for (int i = threadIdx.x; i < V; i += blockDim.x)
+    for (int i = b + threadIdx.x; i < e; i += blockDim.x)
         if (i != skip) {
             const unsigned long long k = argmax_key(r[i], i);
             best = k > best ? k : best;
@@ -250,15 +351,27 @@ __global__ void __launch_bounds__(kArgmaxThreads)
         const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
         best = k > best ? k : best;
     }
-    __shared__ unsigned long long keys[kArgmaxThreads / 32];
-    if ((threadIdx.x & 31) == 0) keys[threadIdx.x >> 5] = best;
+    __shared__ unsigned long long ks[kArgmaxThreads / 32];
+    if ((threadIdx.x & 31) == 0) ks[threadIdx.x >> 5] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
         unsigned long long m = 0ull;
-        for (int w = 0; w < kArgmaxThreads / 32; w++) m = keys[w] > m ? keys[w] : m;
-        out[t] = argmax_key_index(m);
+        for (int w = 0; w < kArgmaxThreads / 32; w++) m = ks[w] > m ? ks[w] : m;
+        keys[(size_t)t * kArgmaxParts + p] = m;
     }
 }
+
+__global__ void k_argmax_rows_final(const unsigned long long* __restrict__ keys, int T, int* __restrict__ out) {
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    unsigned long long best = keys[(size_t)t * kArgmaxParts + lane];  // kArgmaxParts == 32 lanes
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if (lane == 0) out[t] = argmax_key_index(best);
+}
+static_assert(kArgmaxParts == 32, "one key per lane in k_argmax_rows_final");
 
 }  // namespace
 
@@ -316,17 +429,38 @@ void launch_kv_append_at(const float* k, const float* v, int T, int n_kv, int hd
     QQ_CUDA_TRY(cudaGetLastError());
 }
 
-void launch_attn_rows_at(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
-                         size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* out, cudaStream_t s) {
+int attn_rows_chunk() { return 64; }
+
+size_t attn_rows_part_floats(int T, int n_head, int hd, int max_ctx) {
+    const int n_split = (max_ctx + attn_rows_chunk() - 1) / attn_rows_chunk();
+    return (size_t)T * n_head * n_split * (hd + 2);
+}
+
+void launch_attn_rows_split(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
+                            int max_len, size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* part,
+                            float* out, cudaStream_t s) {
     const int G = n_head / n_kv;
     QQ_CHECK(G >= 1 && G <= 32 && n_head % n_kv == 0, -4, "batched attention: unsupported head grouping");
     if (T <= 0) return;
-    dim3 grid((unsigned)T, (unsigned)n_kv);
-    if (hd == 64)
-        k_attn_rows_at<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, out);
-    else if (hd == 128)
-        k_attn_rows_at<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, out);
-    else QQ_CHECK(false, -4, "batched attention: head_dim must be 64 or 128");
+    const int chunk = attn_rows_chunk(), n_split = (max_ctx + chunk - 1) / chunk;
+    QQ_CHECK(n_split <= 65535 && max_len >= 1 && max_len <= max_ctx, -4, "batched attention: bad context length");
+    // splits up to the longest row (max_len positions); a split past a row's own length writes an
+    // empty state, and the merge reads only the splits that hold positions of its row
+    dim3 grid((unsigned)T, (unsigned)n_kv, (unsigned)((max_len + chunk - 1) / chunk));
+    const unsigned mg = (unsigned)(((size_t)T * n_head * 32 + 255) / 256);
+    if (hd == 64) {
+        k_attn_rows_split<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, chunk,
+                                                      n_split, part);
+        QQ_CUDA_TRY(cudaGetLastError());
+        k_attn_merge<64><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out);
+    } else if (hd == 128) {
+        k_attn_rows_split<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, chunk,
+                                                       n_split, part);
+        QQ_CUDA_TRY(cudaGetLastError());
+        k_attn_merge<128><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out);
+    } else {
+        QQ_CHECK(false, -4, "batched attention: head_dim must be 64 or 128");
+    }
     QQ_CUDA_TRY(cudaGetLastError());
 }
 
@@ -336,9 +470,15 @@ void launch_conv_rows_at(const float* bcx, const float* w, float* state, size_t 
     QQ_CUDA_TRY(cudaGetLastError());
 }
 
-void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, int* out, cudaStream_t s) {
+size_t argmax_rows_scratch_bytes(int T) { return (size_t)T * kArgmaxParts * sizeof(unsigned long long); }
+
+void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, void* scratch, int* out,
+                        cudaStream_t s) {
     if (T <= 0) return;
-    k_argmax_rows<<<(unsigned)T, kArgmaxThreads, 0, s>>>(logits, V, suppress, out);
+    unsigned long long* keys = static_cast<unsigned long long*>(scratch);
+    k_argmax_rows_part<<<dim3((unsigned)T, kArgmaxParts), kArgmaxThreads, 0, s>>>(logits, V, suppress, keys);
+    QQ_CUDA_TRY(cudaGetLastError());
+    k_argmax_rows_final<<<(unsigned)((T * 32 + 255) / 256), 256, 0, s>>>(keys, T, out);
     QQ_CUDA_TRY(cudaGetLastError());
 }
 

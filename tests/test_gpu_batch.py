@@ -132,3 +132,35 @@ def test_forward_batch_qwen3_8b_width_16_sequences(qq3, orc):
             cur[s] = int(am[s])
             pos[s] += 1
     eng.close()
+
+
+@pytest.mark.parametrize("arch", ["qwen3", "lfm2"])
+def test_forward_batch_long_context(qq3, orc, arch):
+    """Rows at 40, 150 and 90 positions: the batched attention splits positions over CTAs (64 per
+    split) and merges the splits, for head_dim 128 (Qwen3) and 64 (LFM2)."""
+    spec = qq3.synth.tiny_lfm2(seed=37) if arch == "lfm2" else qq3.synth.tiny_qwen3(seed=37)
+    g = qq3.synth.memory_model(spec)
+    lens = [40, 150, 90]
+    eng = qq3.engine_for(g, device=0, max_ctx=160, n_seq=len(lens))
+    refs = [orc.OracleModel(g, max_ctx=160, threads=8) for _ in lens]
+    cur, pos = [], []
+    for s, n in enumerate(lens):
+        toks = qq3.synth.uniform_tokens(n, 90 + s, spec.n_vocab)
+        for p, t in enumerate(toks[:-1]):  # per-token steps: no batched prefill in this test
+            eng.forward(int(t), p, True, seq=s)
+            refs[s].forward(int(t), p, True)
+        cur.append(int(toks[-1]))
+        pos.append(n - 1)
+    exempt = set()
+    for step in range(3):
+        logits, am = eng.forward_batch([0, 1, 2], cur, pos)
+        for s in range(len(lens)):
+            want, _, rec = refs[s].forward(cur[s], pos[s], False, routing=True)
+            if arch == "lfm2" and _router_gap(g, spec, rec) < 1e-5:
+                exempt.add(s)
+            if s not in exempt:
+                assert rel_err(logits[s], want) < TOL, f"step {step}, sequence {s}: logits"
+                assert int(am[s]) == int(np.argmax(want)), f"step {step}, sequence {s}: greedy id"
+            cur[s] = int(np.argmax(want))
+            pos[s] += 1
+    eng.close()
