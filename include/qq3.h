@@ -84,6 +84,23 @@ int qq_q8_matmul(qq_ctx* ctx, const qq_tensor* W, const float* x_dev, int M, flo
  * head, perHeadRMSNorm, tensor.js:117-129).  w is an F32 tensor of length n. y may equal x. */
 int qq_rmsnorm(qq_ctx* ctx, const float* x_dev, int64_t n_rows, int n, const qq_tensor* w, float eps,
                float* y_dev);
+/* applyRoPE (tensor.js:132-147) in place on n_rows rows of n_heads x head_dim floats, row r at
+ * position pos0 + r: split-half rotation by theta = position / base^(i / (head_dim/2)), cos and
+ * sin computed in double and rounded to f32 (the table the model's RoPE kernels read). */
+int qq_rope(qq_ctx* ctx, float* x_dev, int n_rows, int n_heads, int head_dim, int pos0, double base);
+/* The attention core of one decode step, _selfAttentionCore (qwen3-engine.js:249-291,
+ * lfm2-engine.js:329-378): GQA attention of q_dev [n_head][head_dim] (already normalised and
+ * rotated) over positions 0..pos of a K/V cache laid out [n_kv][max_ctx][head_dim] (f32, the
+ * kv-cache.js:8-11 layout), query head h reading KV head floor(h n_kv / n_head); out_dev
+ * [n_head][head_dim].  Positions split over CTAs, merged in split order.  head_dim 64 or 128. */
+int qq_attention_decode(qq_ctx* ctx, const float* q_dev, const float* k_cache_dev, const float* v_cache_dev,
+                        int n_head, int n_kv, int head_dim, int max_ctx, int pos, float* out_dev);
+/* embeddingLookupQ80 (tensor.js:56-77) of n host token ids: out_dev [n][ne0], exact. */
+int qq_embed(qq_ctx* ctx, const qq_tensor* E, const int32_t* tokens, int n, float* out_dev);
+/* SwiGLU pieces siluInPlace + mulInPlace (tensor.js:168-180): h = silu(g) * u over n floats. */
+int qq_swiglu(qq_ctx* ctx, const float* g_dev, const float* u_dev, int64_t n, float* h_dev);
+/* addVec (tensor.js:181-185): x += d over n floats (the residual add). */
+int qq_add(qq_ctx* ctx, float* x_dev, const float* d_dev, int64_t n);
 
 /* ---------------------------------------------------------------- model */
 

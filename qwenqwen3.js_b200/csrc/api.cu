@@ -1197,6 +1197,82 @@ int qq_rmsnorm(qq_ctx* ctx, const float* x_dev, int64_t n_rows, int n, const qq_
     });
 }
 
+int qq_rope(qq_ctx* ctx, float* x_dev, int n_rows, int n_heads, int head_dim, int pos0, double base) {
+    return guard([&] {
+        need(ctx && x_dev && n_rows >= 0 && n_heads >= 1 && pos0 >= 0, "qq_rope: bad argument");
+        need(head_dim >= 2 && head_dim % 2 == 0, "qq_rope: head_dim must be even");
+        if (n_rows == 0) return;
+        DeviceGuard dg(ctx->device);
+        cudaStream_t s = ctx->stream;
+        // cos/sin of (pos0 + r) * base^(-i/half) in double, stored f32 (tensor.js:137-140), the
+        // table layout of the model's RoPE rows
+        const int half = head_dim / 2;
+        std::vector<float> tab((size_t)n_rows * head_dim);
+        for (int r = 0; r < n_rows; r++)
+            for (int i = 0; i < half; i++) {
+                const double th = (double)(pos0 + r) * (1.0 / std::pow(base, (double)i / (double)half));
+                tab[(size_t)r * head_dim + 2 * i] = (float)std::cos(th);
+                tab[(size_t)r * head_dim + 2 * i + 1] = (float)std::sin(th);
+            }
+        float* cs = static_cast<float*>(ctx_scratch(ctx, tab.size() * sizeof(float)));
+        QQ_CUDA_TRY(cudaMemcpyAsync(cs, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice, s));
+        qq3::launch_rope_rows(x_dev, n_rows, n_heads, head_dim, cs, 0, s);
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // tab is a local buffer
+    });
+}
+
+int qq_attention_decode(qq_ctx* ctx, const float* q_dev, const float* k_cache_dev, const float* v_cache_dev,
+                        int n_head, int n_kv, int head_dim, int max_ctx, int pos, float* out_dev) {
+    return guard([&] {
+        need(ctx && q_dev && k_cache_dev && v_cache_dev && out_dev, "qq_attention_decode: NULL argument");
+        need(n_kv >= 1 && n_head >= n_kv && n_head % n_kv == 0, "qq_attention_decode: n_head must be a multiple of n_kv");
+        need(pos >= 0 && pos < max_ctx, "qq_attention_decode: pos outside the cache");
+        QQ_CHECK(head_dim == 64 || head_dim == 128, QQ_ERR_UNSUPPORTED, "qq_attention_decode: head_dim must be 64 or 128");
+        DeviceGuard dg(ctx->device);
+        cudaStream_t s = ctx->stream;
+        // scratch: [sequence 0, position] | split partial states
+        const size_t part = qq3::attn_rows_part_floats(1, n_head, head_dim, max_ctx) * sizeof(float);
+        char* sc = static_cast<char*>(ctx_scratch(ctx, 256 + part));
+        const int rowmap[2] = {0, pos};
+        QQ_CUDA_TRY(cudaMemcpyAsync(sc, rowmap, sizeof(rowmap), cudaMemcpyHostToDevice, s));
+        const int* dev = reinterpret_cast<const int*>(sc);
+        qq3::launch_attn_rows_split(q_dev, k_cache_dev, v_cache_dev, 1, dev, dev + 1, pos + 1, 0, n_head, n_kv,
+                                    head_dim, max_ctx, reinterpret_cast<float*>(sc + 256), out_dev, s);
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // rowmap is a local buffer
+    });
+}
+
+int qq_embed(qq_ctx* ctx, const qq_tensor* E, const int32_t* tokens, int n, float* out_dev) {
+    return guard([&] {
+        need(ctx && E && tokens && out_dev && n >= 0, "qq_embed: bad argument");
+        QQ_CHECK(E->t.type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED, "qq_embed: the embedding must be Q8_0");
+        for (int i = 0; i < n; i++) need(tokens[i] >= 0 && tokens[i] < E->t.rows, "qq_embed: token id out of range");
+        if (n == 0) return;
+        DeviceGuard dg(ctx->device);
+        cudaStream_t s = ctx->stream;
+        int* tok = static_cast<int*>(ctx_scratch(ctx, sizeof(int) * (size_t)n));
+        QQ_CUDA_TRY(cudaMemcpyAsync(tok, tokens, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, s));
+        qq3::launch_embed_rows(E->t, tok, n, (int)E->t.rows, out_dev, s);
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // tokens is the caller's host buffer
+    });
+}
+
+int qq_swiglu(qq_ctx* ctx, const float* g_dev, const float* u_dev, int64_t n, float* h_dev) {
+    return guard([&] {
+        need(ctx && g_dev && u_dev && h_dev && n >= 0, "qq_swiglu: bad argument");
+        DeviceGuard dg(ctx->device);
+        qq3::launch_swiglu_rows(g_dev, u_dev, (size_t)n, h_dev, ctx->stream);
+    });
+}
+
+int qq_add(qq_ctx* ctx, float* x_dev, const float* d_dev, int64_t n) {
+    return guard([&] {
+        need(ctx && x_dev && d_dev && n >= 0, "qq_add: bad argument");
+        DeviceGuard dg(ctx->device);
+        qq3::launch_add_rows(x_dev, d_dev, (size_t)n, ctx->stream);
+    });
+}
+
 int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
     return guard([&] {
         need(ctx && desc && out && desc->layers, "qq_model_create: NULL argument");

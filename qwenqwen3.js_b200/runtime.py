@@ -83,6 +83,11 @@ _SIGS = {
     "qq_dequant": (_I, [_P, _P]),
     "qq_q8_matmul": (_I, [_P, _P, _P, _I, _P]),
     "qq_rmsnorm": (_I, [_P, _P, _I64, _I, _P, C.c_float, _P]),
+    "qq_rope": (_I, [_P, _P, _I, _I, _I, _I, C.c_double]),
+    "qq_attention_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "qq_embed": (_I, [_P, _P, C.POINTER(C.c_int32), _I, _P]),
+    "qq_swiglu": (_I, [_P, _P, _P, _I64, _P]),
+    "qq_add": (_I, [_P, _P, _P, _I64]),
     "qq_model_create": (_I, [_P, C.POINTER(ModelDesc), C.POINTER(_P)]),
     "qq_model_destroy": (_I, [_P]),
     "qq_forward": (_I, [_P, C.POINTER(C.c_int32), _I, _I, _I, _I, _P, C.POINTER(C.c_int32), _I]),
@@ -212,6 +217,24 @@ class Context:
 
     def rmsnorm(self, x_dev, n_rows: int, n: int, w: "Tensor", eps: float, y_dev) -> None:
         check(self.lib.qq_rmsnorm(self.h, _ptr(x_dev), n_rows, n, w.h, eps, _ptr(y_dev)))
+
+    def rope(self, x_dev, n_rows: int, n_heads: int, head_dim: int, pos0: int, base: float) -> None:
+        check(self.lib.qq_rope(self.h, _ptr(x_dev), n_rows, n_heads, head_dim, pos0, base))
+
+    def attention_decode(self, q_dev, k_cache_dev, v_cache_dev, n_head: int, n_kv: int, head_dim: int, max_ctx: int,
+                         pos: int, out_dev) -> None:
+        check(self.lib.qq_attention_decode(self.h, _ptr(q_dev), _ptr(k_cache_dev), _ptr(v_cache_dev), n_head, n_kv,
+                                           head_dim, max_ctx, pos, _ptr(out_dev)))
+
+    def embed(self, E: "Tensor", tokens, out_dev) -> None:
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        check(self.lib.qq_embed(self.h, E.h, t.ctypes.data_as(C.POINTER(C.c_int32)), len(t), _ptr(out_dev)))
+
+    def swiglu(self, g_dev, u_dev, n: int, h_dev) -> None:
+        check(self.lib.qq_swiglu(self.h, _ptr(g_dev), _ptr(u_dev), n, _ptr(h_dev)))
+
+    def add(self, x_dev, d_dev, n: int) -> None:
+        check(self.lib.qq_add(self.h, _ptr(x_dev), _ptr(d_dev), n))
 
     def moe_block(self, layer: LayerDesc, n_expert: int, top_k: int, x_dev, T: int, out_dev, routing_dev=None) -> None:
         check(self.lib.qq_moe_block(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(out_dev),

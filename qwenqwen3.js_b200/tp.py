@@ -183,11 +183,12 @@ def merge_greedy(pairs: list[tuple[float, int, bool]]) -> int:
 
 @dataclass
 class TPOps:
-    """The arithmetic a rank runs (rows are float32 vectors; weights are shard entries):
-    embed(token) -> [E]; rmsnorm(x, w_entry, eps) -> x; matmul(w_entry, x) -> [N];
-    head_rmsnorm(x, n_heads, w_entry, eps) -> x; rope(x, n_heads, pos) -> x;
+    """The arithmetic a rank runs.  Vectors are whatever the ops use (numpy on CPU, device tensors
+    on a GPU); weights are shard entries (ggml type, ne, raw) or what the ops made of them:
+    embed(token) -> [E]; rmsnorm(x, w, eps) -> x'; matmul(w, x) -> [N];
+    head_rmsnorm(x, n_heads, w, eps) -> x'; rope(x, n_heads, pos) -> x';
     kv_store(layer, pos, k, v); attention(layer, pos, q) -> [local heads * hd] over this rank's
-    query/KV heads; silu_mul(g, u) -> h."""
+    query/KV heads; silu_mul(g, u) -> h; add(x, d) -> x + d; to_host(x) -> numpy float32."""
 
     embed: object
     rmsnorm: object
@@ -197,16 +198,18 @@ class TPOps:
     kv_store: object
     attention: object
     silu_mul: object
+    add: object
+    to_host: object
 
 
 def tp_forward(token: int, pos: int, plan: TPPlan, shards: dict, ops: TPOps, eps: float, n_layers: int,
                all_reduce, gather_pairs, want_logits: bool = True):
     """Qwen3Engine.forward(token, pos, !want_logits) on this rank's shards.  all_reduce(x) returns
     the element-wise sum over the ranks; gather_pairs(pair) returns every rank's local_greedy
-    pair in rank order.  Returns (this rank's vocab-shard logits, global greedy id) or
+    pair in rank order.  Returns (this rank's vocab-shard logits as numpy, global greedy id) or
     (None, None) without logits."""
     nq, nkv = len(plan.q_heads), len(plan.kv_heads)
-    x = np.asarray(ops.embed(token), dtype=np.float32)
+    x = ops.embed(token)
     for i in range(n_layers):
         p = f"blk.{i}."
         xn = ops.rmsnorm(x, shards[p + "attn_norm.weight"], eps)
@@ -217,12 +220,110 @@ def tp_forward(token: int, pos: int, plan: TPPlan, shards: dict, ops: TPOps, eps
         k = ops.rope(ops.head_rmsnorm(k, nkv, shards[p + "attn_k_norm.weight"], eps), nkv, pos)
         ops.kv_store(i, pos, k, v)
         att = ops.attention(i, pos, q)
-        x = (x + all_reduce(ops.matmul(shards[p + "attn_output.weight"], att))).astype(np.float32)
+        x = ops.add(x, all_reduce(ops.matmul(shards[p + "attn_output.weight"], att)))
         xn = ops.rmsnorm(x, shards[p + "ffn_norm.weight"], eps)
         h = ops.silu_mul(ops.matmul(shards[p + "ffn_gate.weight"], xn), ops.matmul(shards[p + "ffn_up.weight"], xn))
-        x = (x + all_reduce(ops.matmul(shards[p + "ffn_down.weight"], h))).astype(np.float32)
+        x = ops.add(x, all_reduce(ops.matmul(shards[p + "ffn_down.weight"], h)))
     if not want_logits:
         return None, None
     xn = ops.rmsnorm(x, shards["output_norm.weight"], eps)
-    logits = ops.matmul(shards["output.weight"], xn)
+    logits = ops.to_host(ops.matmul(shards["output.weight"], xn))
     return logits, merge_greedy(gather_pairs(local_greedy(logits, plan.vocab_rows.start)))
+
+
+# ---- the GPU binding -------------------------------------------------------------------------
+
+class GPURank:
+    """One rank's shards on its GPU and the TPOps that run them through the library
+    (runtime.Context: Q8_0 GEMVs, RMSNorm, RoPE, split attention over a local f32 K/V cache
+    [layer][local KV head][max_ctx][head_dim], SwiGLU, residual add).  Device vectors are torch
+    tensors on `stream`, which the context also runs on, so no operation needs another stream's
+    results.  all_reduce for tp_forward: `GPURank.nccl_all_reduce` (torch.distributed, NCCL)."""
+
+    def __init__(self, ctx, plan: TPPlan, shards: dict, head_dim: int, rope_base: float, max_ctx: int,
+                 n_layers: int, stream):
+        import torch
+
+        self.torch = torch
+        self.ctx, self.plan, self.hd = ctx, plan, head_dim
+        self.stream = stream
+        ctx.set_stream(stream.cuda_stream)
+        self.dev = torch.device("cuda", ctx.device)
+        self.w = {name: ctx.upload(raw, t, ne) for name, (t, ne, raw) in shards.items()}
+        self.shards = {name: self.w[name] for name in shards}  # tp_forward looks weights up by name
+        nkv = len(plan.kv_heads)
+        self.kc = torch.zeros((n_layers, nkv, max_ctx, head_dim), dtype=torch.float32, device=self.dev)
+        self.vc = torch.zeros_like(self.kc)
+        self.max_ctx, self.base = max_ctx, rope_base
+
+    def _new(self, n):
+        with self.torch.cuda.stream(self.stream):  # allocations belong to the stream that uses them
+            return self.torch.empty(n, dtype=self.torch.float32, device=self.dev)
+
+    def ops(self) -> TPOps:
+        ctx, hd, plan = self.ctx, self.hd, self.plan
+        nq, nkv = len(plan.q_heads), len(plan.kv_heads)
+        E = plan.n_embd
+
+        def embed(token):
+            out = self._new(E)
+            ctx.embed(self.w["token_embd.weight"], [token], out)
+            return out
+
+        def rmsnorm(x, w, eps):
+            y = self._new(x.numel())
+            ctx.rmsnorm(x, 1, x.numel(), w, eps, y)
+            return y
+
+        def matmul(w, x):
+            y = self._new(int(w.ne[1]))
+            ctx.q8_matmul(w, x, 1, y)
+            return y
+
+        def head_rmsnorm(x, n, w, eps):
+            y = self._new(x.numel())
+            ctx.rmsnorm(x, n, hd, w, eps, y)
+            return y
+
+        def rope(x, n, pos):
+            ctx.rope(x, 1, n, hd, pos, self.base)
+            return x
+
+        def kv_store(layer, pos, k, v):
+            with self.torch.cuda.stream(self.stream):
+                self.kc[layer, :, pos].copy_(k.view(nkv, hd))
+                self.vc[layer, :, pos].copy_(v.view(nkv, hd))
+
+        def attention(layer, pos, q):
+            out = self._new(nq * hd)
+            ctx.attention_decode(q, self.kc[layer], self.vc[layer], nq, nkv, hd, self.max_ctx, pos, out)
+            return out
+
+        def silu_mul(g, u):
+            h = self._new(g.numel())
+            ctx.swiglu(g, u, g.numel(), h)
+            return h
+
+        def add(x, d):
+            ctx.add(x, d, x.numel())
+            return x
+
+        def to_host(x):
+            self.stream.synchronize()
+            return x.cpu().numpy()
+
+        return TPOps(embed, rmsnorm, matmul, head_rmsnorm, rope, kv_store, attention, silu_mul, add, to_host)
+
+    def nccl_all_reduce(self, x):
+        """Sum of x over the ranks of the default process group, in place (NCCL over NVLink)."""
+        import torch.distributed as dist
+
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            with self.torch.cuda.stream(self.stream):
+                dist.all_reduce(x)
+        return x
+
+    def close(self):
+        for t in self.w.values():
+            t.free()
+        self.w.clear()

@@ -104,6 +104,64 @@ def test_q8_matmul_tensor_core_ragged(qq3, orc, gpu_ctx, torch, M, N, K):
     W.free()
 
 
+def test_rope_vs_oracle(qq3, orc, gpu_ctx, torch):
+    """qq_rope against applyRoPE (tensor.js:132-147): rows at consecutive positions."""
+    rows, heads, hd, pos0, base = 3, 4, 128, 37, 1e6
+    x = qq3.synth.normal_f32(rows * heads * hd, seed=61).reshape(rows, heads * hd)
+    xd = _dev(torch, x)
+    gpu_ctx.rope(xd, rows, heads, hd, pos0, base)
+    gpu_ctx.synchronize()
+    got = xd.cpu().numpy()
+    for r in range(rows):
+        want = orc.rope(x[r], heads, hd, pos0 + r, base)
+        assert rel_err(got[r], want) < 1e-5, f"row {r}"
+
+
+@pytest.mark.parametrize("n_head,n_kv,hd,pos", [(4, 2, 128, 150), (8, 2, 64, 0), (32, 8, 64, 700)])
+def test_attention_decode_vs_f64(qq3, gpu_ctx, torch, n_head, n_kv, hd, pos):
+    """qq_attention_decode against _selfAttentionCore (qwen3-engine.js:249-291) evaluated in f64:
+    query head h reads KV head floor(h n_kv / n_head), softmax over positions 0..pos."""
+    max_ctx = 768
+    q = qq3.synth.normal_f32(n_head * hd, seed=62).reshape(n_head, hd)
+    kc = qq3.synth.normal_f32(n_kv * max_ctx * hd, seed=63).reshape(n_kv, max_ctx, hd)
+    vc = qq3.synth.normal_f32(n_kv * max_ctx * hd, seed=64).reshape(n_kv, max_ctx, hd)
+    out = torch.full((n_head, hd), float("nan"), dtype=torch.float32, device="cuda")
+    gpu_ctx.attention_decode(_dev(torch, q), _dev(torch, kc), _dev(torch, vc), n_head, n_kv, hd, max_ctx, pos, out)
+    gpu_ctx.synchronize()
+    got = out.cpu().numpy()
+    for h in range(n_head):
+        kv = h * n_kv // n_head
+        s = kc[kv, :pos + 1].astype(np.float64) @ q[h].astype(np.float64) / np.sqrt(hd)
+        w = np.exp(s - s.max())
+        want = (w / w.sum()) @ vc[kv, :pos + 1].astype(np.float64)
+        assert rel_err(got[h], want) < 1e-4, f"head {h}"
+
+
+def test_embed_and_swiglu(qq3, orc, gpu_ctx, torch):
+    """qq_embed is embeddingLookupQ80 bit for bit (tensor.js:56-77); qq_swiglu is silu(g) * u
+    (tensor.js:168-180)."""
+    K, V = 256, 1000
+    raw = qq3.synth.q8_0_blocks(K * V, seed=65, mode=1)
+    E = gpu_ctx.upload(raw, 8, [K, V])
+    toks = [0, 7, V - 1, 7]
+    out = torch.empty((len(toks), K), dtype=torch.float32, device="cuda")
+    gpu_ctx.embed(E, toks, out)
+    got = out.cpu().numpy()
+    for i, t in enumerate(toks):
+        assert np.array_equal(got[i], orc.embedding(raw, [K, V], t)), f"token {t}"
+    with pytest.raises(RuntimeError):
+        gpu_ctx.embed(E, [V], out)
+    E.free()
+    n = 3000
+    g = qq3.synth.normal_f32(n, seed=66) * 4
+    u = qq3.synth.normal_f32(n, seed=67)
+    h = torch.empty(n, dtype=torch.float32, device="cuda")
+    gpu_ctx.swiglu(_dev(torch, g), _dev(torch, u), n, h)
+    gpu_ctx.synchronize()
+    want = orc.silu(g) * u
+    assert rel_err(h.cpu().numpy(), want) < 1e-6
+
+
 def test_rmsnorm_vs_oracle(qq3, orc, gpu_ctx, torch):
     n, rows = 2048, 5
     x = qq3.synth.normal_f32(n * rows, seed=3).reshape(rows, n) * 3

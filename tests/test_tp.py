@@ -67,6 +67,8 @@ def _oracle_ops(orc, tp, plan, shards, hd, base, max_ctx, n_layers):
         kv_store=kv_store,
         attention=attention,
         silu_mul=lambda g, u: (orc.silu(g) * np.asarray(u, np.float32)).astype(np.float32),
+        add=lambda a, b: (a + b).astype(np.float32),
+        to_host=lambda a: np.asarray(a, np.float32),
     )
 
 
