@@ -285,7 +285,8 @@ def _oracle():
     return orc
 
 
-def cpu_baseline(g, spec, budget_s: float = 12.0, prompt_len: int = 8, steps=None, warmup: int = 0):
+def cpu_baseline(g, spec, budget_s: float = 12.0, prompt_len: int = 8, steps=None, warmup: int = 0,
+                 label: str = "LFM2-8B-A1B-shaped decode"):
     """The oracle (C restatement of the JS CPU path) on the host cores: prompt_len-token
     prompt, then greedy decode steps (time-bounded unless steps is given)."""
     orc = _oracle()
@@ -307,8 +308,9 @@ def cpu_baseline(g, spec, budget_s: float = 12.0, prompt_len: int = 8, steps=Non
         if (steps is not None and n >= steps) or (steps is None and (el >= budget_s and n >= 2)):
             break
     return {"value": round(n / el, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"LFM2-8B-A1B-shaped decode: {prompt_len}-token prompt then {n} greedy steps "
-                      f"(all 24 layers, f64-accumulating C restatement of the JS CPU path, {cores} threads)"}
+            "sample": f"{label}: {prompt_len}-token prompt then {n} greedy steps "
+                      f"(all {spec.n_layers} layers, f64-accumulating C restatement of the JS CPU path, "
+                      f"{cores} threads)"}
 
 
 def run_reference(args, ws, rank):
@@ -516,10 +518,14 @@ def run_batch_decode(args, ws, rank, local):
                         "frac": round(gbs / peak, 4), "peak_kind": kind,
                         "bytes_per_step": {"weights": round(w_bytes), "kv": round(kv_bytes)}},
            "prefill_s": round(prefill_s, 2), "clocks": clk.summary()}
-    if rank == 0:
-        print(json.dumps(res), flush=True)
     eng.close()
     ctx.close()
+    if rank == 0 and not args.no_cpu_baseline:
+        # the reference serves one sequence per engine: one sequence, a short prompt (CPU time)
+        res["cpu_baseline"] = cpu_baseline(g, spec, budget_s=args.cpu_seconds, prompt_len=8,
+                                           label="Qwen3-8B-shaped decode of one sequence")
+    if rank == 0:
+        print(json.dumps(res), flush=True)
 
 
 def run_matmul(args, ws, rank, local):
