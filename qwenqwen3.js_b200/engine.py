@@ -30,9 +30,9 @@ def sample_greedy(logits: np.ndarray) -> int:
 def sample_top_p_top_k(logits: np.ndarray, temperature: float, top_p: float, top_k: int, rng=random.random) -> int:
     """sampleTopPTopK (tensor.js:188-228)."""
     x = logits.astype(np.float64)
-    mx = x.max()
+    mx = float(np.max(np.where(np.isnan(x), -np.inf, x)))  # `logits[i] > maxVal` skips NaN
     e = np.exp((x - mx) / temperature).astype(np.float32)  # stored into the Float32Array
-    s = float(e.astype(np.float64).sum())
+    s = float(np.cumsum(e.astype(np.float64))[-1])  # sumExp: a sequential f64 sum, as the JS loop
     p = (e.astype(np.float64) * (1.0 / s)).astype(np.float32)
     order = np.argsort(-p, kind="stable")
     probs = p[order].astype(np.float64)

@@ -112,3 +112,58 @@ def test_host_sampling_mirrors_tensor_js(qq3):
     # renormalise after the cut, so a draw above it falls through to the last sorted id
     assert sample_top_p_top_k(logits, 0.7, 0.9, 1, rng=lambda: 0.1) == 1
     assert sample_top_p_top_k(logits, 0.7, 0.9, 1, rng=lambda: 0.999) == 3
+
+
+def _js_top_p_top_k(logits, temperature, top_p, top_k, r):
+    """sampleTopPTopK (tensor.js:188-228) transcribed loop for loop: f64 arithmetic (JS numbers),
+    f32 rounding where the JS stores into the Float32Array, a stable sort, Math.random() = r."""
+    x = [float(v) for v in np.asarray(logits, np.float32)]
+    n = len(x)
+    mx = -np.inf
+    for v in x:
+        if v > mx:
+            mx = v
+    s = 0.0
+    for i in range(n):
+        x[i] = float(np.float32(np.exp((x[i] - mx) / temperature)))
+        s += x[i]
+    inv = 1.0 / s
+    for i in range(n):
+        x[i] = float(np.float32(x[i] * inv))
+    idx = sorted(([x[i], i] for i in range(n)), key=lambda a: -a[0])  # Python's sort is stable
+    k_limit = min(top_k, n) if top_k > 0 else n
+    for i in range(k_limit, n):
+        idx[i][0] = 0.0
+    cum = 0.0
+    for i in range(n):
+        cum += idx[i][0]
+        if cum >= top_p:
+            for j in range(i + 1, n):
+                idx[j][0] = 0.0
+            break
+    cum = 0.0
+    for i in range(n):
+        cum += idx[i][0]
+        if r <= cum:
+            return idx[i][1]
+    return idx[n - 1][1]
+
+
+def test_top_p_top_k_matches_js_transcription(qq3):
+    """The host sampler picks the same id as the literal JS loops on random logits (with ties),
+    temperatures, top-p, top-k and random draws.  (A NaN logit makes every JS probability NaN and
+    the result then depends on the JS engine's sort, so it is not a case here.)"""
+    from qq3.engine import sample_top_p_top_k
+
+    rng = np.random.default_rng(11)
+    for case in range(300):
+        n = int(rng.integers(1, 60))
+        logits = (rng.standard_normal(n) * rng.choice([0.5, 3.0, 20.0])).astype(np.float32)
+        if case % 5 == 0:
+            logits = np.round(logits)  # ties
+        t = float(rng.choice([0.3, 0.7, 1.0, 1.5]))
+        top_p = float(rng.choice([0.5, 0.9, 0.95, 1.0]))
+        top_k = int(rng.choice([0, 1, 5, 40]))
+        r = float(rng.random())
+        want = _js_top_p_top_k(logits, t, top_p, top_k, r)
+        assert sample_top_p_top_k(logits.copy(), t, top_p, top_k, rng=lambda: r) == want, case
