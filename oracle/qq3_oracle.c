@@ -68,11 +68,127 @@ static void matmul_f32(const uint8_t* w, int64_t in_dim, int64_t out_dim, const 
     }
 }
 
-/* matmulGeneric (tensor.js:485-496), F32 and Q8_0 only; a 3-D tensor is treated as its
+/* ---- k-quants (tensor.js:267-664) ----------------------------------------------------------
+ * Column c of a [ne0, ne1] tensor is ceil(ne0 / 256) contiguous superblocks; element e of a
+ * superblock is the JS expression below evaluated in doubles (JS numbers, the same operation
+ * order), its f16 fields read exactly.  The JS layouts are restated as they are written there. */
+#define ORC_QK_K 256
+
+static int kq_block_bytes(int type) {
+    switch (type) {
+        case ORC_TYPE_Q2_K: return 84;   /* tensor.js:271 */
+        case ORC_TYPE_Q3_K: return 110;  /* tensor.js:272 */
+        case ORC_TYPE_Q4_K: return 144;  /* tensor.js:273 */
+        case ORC_TYPE_Q5_K: return 176;  /* tensor.js:274 */
+        case ORC_TYPE_Q6_K: return 210;  /* tensor.js:275 */
+        default: return 0;
+    }
+}
+
+static int is_kquant(int type) { return kq_block_bytes(type) != 0; }
+
+/* _q4kGetScaleMin (tensor.js:278-289): 6-bit scale and min of sub-block sub of the 12-byte array */
+static void q4k_scale_min(const uint8_t* s, int sub, int* sc, int* mn) {
+    if (sub < 4) {
+        *sc = s[sub] & 63;
+        *mn = s[sub + 4] & 63;
+    } else {
+        const int ss = sub - 4;
+        *sc = (s[sub + 4] & 0xF) | ((s[ss] >> 6) << 4);
+        *mn = (s[sub + 4] >> 4) | ((s[sub] >> 6) << 4);
+    }
+}
+
+/* _q3kGetScale (tensor.js:295-302): 6-bit scale minus 32 */
+static int q3k_scale(const uint8_t* s, int sub) {
+    const int lo4 = (s[sub & 7] >> ((sub >> 3) << 2)) & 0xF;
+    const int hi2 = (s[8 + (sub & 3)] >> ((sub >> 2) * 2)) & 0x3;
+    return (lo4 | (hi2 << 4)) - 32;
+}
+
+/* Element e (0..255) of the superblock at bb, as matmulQ{2..6}KxF32 and _q{2..6}kColumn compute
+ * it (tensor.js:304-466, 551-664). */
+static double kq_value(int type, const uint8_t* bb, int e) {
+    switch (type) {
+        case ORC_TYPE_Q2_K: { /* scales[16]@0 qs[64]@16 d@80 dmin@82 (tensor.js:304-334) */
+            const double d = rd_f16(bb + 80), dmin = rd_f16(bb + 82);
+            const int sb = bb[e >> 4];
+            const int q = (bb[16 + (e >> 7) * 32 + ((e >> 4) & 1) * 16 + (e & 15)] >> (((e >> 5) & 3) * 2)) & 0x3;
+            return d * (double)(sb & 0xF) * (double)q - dmin * (double)((sb >> 4) & 0xF);
+        }
+        case ORC_TYPE_Q3_K: { /* hmask[32]@0 qs[64]@32 scales[12]@96 d@108 (tensor.js:336-366) */
+            const double d = rd_f16(bb + 108);
+            const int scale = q3k_scale(bb + 96, e >> 4);
+            const int hbit = (bb[((e >> 4) & 1) * 16 + (e & 15)] >> (e >> 5)) & 1;
+            const int low2 = (bb[32 + (e >> 7) * 32 + ((e >> 4) & 1) * 16 + (e & 15)] >> (((e >> 5) & 3) * 2)) & 3;
+            return d * (double)scale * (double)((low2 | (hbit << 2)) - 4);
+        }
+        case ORC_TYPE_Q4_K: { /* d@0 dmin@2 scales[12]@4 qs[128]@16 (tensor.js:368-397) */
+            const double d = rd_f16(bb), dmin = rd_f16(bb + 2);
+            int sc, mn;
+            q4k_scale_min(bb + 4, (e >> 6) * 2 + ((e >> 5) & 1), &sc, &mn);
+            const int qb = bb[16 + (e >> 6) * 32 + (e & 31)];
+            const int q4 = ((e >> 5) & 1) ? (qb >> 4) & 0xF : qb & 0xF;
+            return d * (double)sc * (double)q4 - dmin * (double)mn;
+        }
+        case ORC_TYPE_Q5_K: { /* d@0 dmin@2 scales[12]@4 qh[32]@16 qs[128]@48 (tensor.js:399-430) */
+            const double d = rd_f16(bb), dmin = rd_f16(bb + 2);
+            const int sub = (e >> 6) * 2 + ((e >> 5) & 1);
+            int sc, mn;
+            q4k_scale_min(bb + 4, sub, &sc, &mn);
+            const int hbit = (bb[16 + (e & 31)] >> sub) & 1;
+            const int qb = bb[48 + (e >> 6) * 32 + (e & 31)];
+            const int low4 = ((e >> 5) & 1) ? (qb >> 4) & 0xF : qb & 0xF;
+            return d * (double)sc * (double)(low4 | (hbit << 4)) - dmin * (double)mn;
+        }
+        case ORC_TYPE_Q6_K: { /* ql[128]@0 qh[64]@128 scales[16]@192 d@208 (tensor.js:432-466) */
+            const double d = rd_f16(bb + 208);
+            const int ql = bb[(e >> 7) * 64 + ((e >> 5) & 1) * 32 + (e & 31)];
+            const int low4 = ((e >> 6) & 1) ? (ql >> 4) & 0xF : ql & 0xF;
+            const int high2 = (bb[128 + (e >> 7) * 32 + (e & 31)] >> (((e >> 5) & 3) * 2)) & 0x3;
+            const int sidx = (e >> 7) * 8 + ((e >> 5) & 3) * 2 + ((e & 31) >> 4);
+            const int scale = (int)(int8_t)bb[192 + sidx];
+            return d * (double)scale * (double)((low4 | (high2 << 4)) - 32);
+        }
+        default: abort();
+    }
+}
+
+/* matmulQ{2..6}KxF32 (tensor.js:304-466): dot += input * weight in doubles, f32 store. */
+static void matmul_kq(int type, const uint8_t* w, int64_t in_dim, int64_t out_dim, const float* x, float* y) {
+    const int64_t bpc = (in_dim + ORC_QK_K - 1) / ORC_QK_K;
+    const int bs = kq_block_bytes(type);
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1 && out_dim >= 64)
+    for (int64_t c = 0; c < out_dim; c++) {
+        double dot = 0;
+        for (int64_t b = 0; b < bpc; b++) {
+            const uint8_t* bb = w + ((size_t)c * bpc + b) * bs;
+            const int64_t eb = b * ORC_QK_K;
+            const int64_t n = in_dim - eb < ORC_QK_K ? in_dim - eb : ORC_QK_K;
+            for (int e = 0; e < n; e++) dot += (double)x[eb + e] * kq_value(type, bb, e);
+        }
+        y[c] = (float)dot;
+    }
+}
+
+/* _q{2..6}kColumn (tensor.js:525-664): column c as floats (each value stored into a Float32Array). */
+static void kq_column(int type, const uint8_t* w, int64_t out_dim, int64_t c, float* out) {
+    const int64_t bpc = (out_dim + ORC_QK_K - 1) / ORC_QK_K;
+    const int bs = kq_block_bytes(type);
+    for (int64_t b = 0; b < bpc; b++) {
+        const uint8_t* bb = w + ((size_t)c * bpc + b) * bs;
+        const int64_t eb = b * ORC_QK_K;
+        const int64_t n = out_dim - eb < ORC_QK_K ? out_dim - eb : ORC_QK_K;
+        for (int e = 0; e < n; e++) out[eb + e] = (float)kq_value(type, bb, e);
+    }
+}
+
+/* matmulGeneric (tensor.js:485-496): F32, Q8_0 and the k-quants; a 3-D tensor is treated as its
  * first [ne0, ne1] matrix, as a meta object with that shape would be. */
 void orc_matmul(const orc_tensor* w, const float* x, float* y) {
     if (w->type == ORC_TYPE_Q8_0) matmul_q8(w->data, w->ne[0], w->ne[1], x, y);
     else if (w->type == ORC_TYPE_F32) matmul_f32(w->data, w->ne[0], w->ne[1], x, y);
+    else if (is_kquant(w->type)) matmul_kq(w->type, w->data, w->ne[0], w->ne[1], x, y);
     else abort();
 }
 
@@ -87,6 +203,10 @@ void orc_embedding(const orc_tensor* w, int32_t token, float* out) {
     if (w->type == ORC_TYPE_F32) {
         const uint8_t* base = w->data + (size_t)token * out_dim * 4;
         for (int64_t i = 0; i < out_dim; i++) out[i] = rd_f32(base + i * 4);
+        return;
+    }
+    if (is_kquant(w->type)) {  /* embeddingLookupGeneric -> _lookupKQuantColumn (tensor.js:511-549) */
+        kq_column(w->type, w->data, out_dim, token, out);
         return;
     }
     if (w->type != ORC_TYPE_Q8_0) abort();
@@ -106,6 +226,10 @@ void orc_dequant(const orc_tensor* w, float* out) {
     int64_t n = 1;
     for (int i = 0; i < w->n_dims; i++) n *= w->ne[i];
     if (w->type == ORC_TYPE_F32) { memcpy(out, w->data, (size_t)n * 4); return; }
+    if (is_kquant(w->type)) {  /* every column through its column reader, in storage order */
+        for (int64_t c = 0; c < n / w->ne[0]; c++) kq_column(w->type, w->data, w->ne[0], c, out + c * w->ne[0]);
+        return;
+    }
     const int64_t nb = (n + 31) / 32;
     for (int64_t b = 0; b < nb; b++) {
         const uint8_t* blk = w->data + b * 34;

@@ -30,6 +30,12 @@ extern "C" {
 #define ORC_TYPE_F32 0
 #define ORC_TYPE_F16 1
 #define ORC_TYPE_Q8_0 8
+/* k-quants (tensor.js:267-664): 256-value superblocks */
+#define ORC_TYPE_Q2_K 10
+#define ORC_TYPE_Q3_K 11
+#define ORC_TYPE_Q4_K 12
+#define ORC_TYPE_Q5_K 13
+#define ORC_TYPE_Q6_K 14
 
 /* A raw GGUF tensor: host bytes exactly as stored in the file, plus its ggml shape
  * (ne[0] fastest-varying), i.e. the meta object of gguf.js:235-254. */

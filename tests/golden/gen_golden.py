@@ -9,7 +9,8 @@ on micro-sized seeded inputs.  tests/test_oracle.py requires the C oracle to rep
 these vectors, and the GPU tests compare against the C oracle.  Parity with the reference
 itself stays unpinned.
 
-Run:  python tests/golden/gen_golden.py   (rewrites the .npz files in this folder)
+Run:  python tests/golden/gen_golden.py   (rewrites the .npz files in this folder; with the
+      argument `kquants`, only kquants.npz)
 """
 from __future__ import annotations
 
@@ -337,6 +338,122 @@ def ops_vectors(qq3):
                 greedy=np.asarray([argmax_first(v)], np.int32))
 
 
+# ---- k-quants (tensor.js:267-664), transcribed type by type -------------------------------
+
+QK_K = 256
+KQ_BYTES = {10: 84, 11: 110, 12: 144, 13: 176, 14: 210}
+
+
+def q4k_get_scale_min(u8, base, sub):
+    """_q4kGetScaleMin (tensor.js:278-289)."""
+    if sub < 4:
+        return u8[base + sub] & 63, u8[base + sub + 4] & 63
+    ss = sub - 4
+    s = (u8[base + sub + 4] & 0xF) | ((u8[base + ss] >> 6) << 4)
+    m = (u8[base + sub + 4] >> 4) | ((u8[base + sub] >> 6) << 4)
+    return s, m
+
+
+def q3k_get_scale(u8, base, sub):
+    """_q3kGetScale (tensor.js:295-302)."""
+    lo4 = (u8[base + (sub & 7)] >> ((sub >> 3) << 2)) & 0xF
+    hi2 = (u8[base + 8 + (sub & 3)] >> ((sub >> 2) * 2)) & 0x3
+    return (lo4 | (hi2 << 4)) - 32
+
+
+def kq_weight(t, u8, bb, e):
+    """The per-element weight of matmulQ{2..6}KxF32 (tensor.js:304-466), a JS number."""
+    if t == 10:
+        d, dmin = read_f16(u8, bb + 80), read_f16(u8, bb + 82)
+        sb = u8[bb + (e >> 4)]
+        qb = bb + 16 + (e >> 7) * 32 + ((e >> 4) & 1) * 16 + (e & 15)
+        q = (u8[qb] >> (((e >> 5) & 3) * 2)) & 0x3
+        return d * (sb & 0xF) * q - dmin * ((sb >> 4) & 0xF)
+    if t == 11:
+        d = read_f16(u8, bb + 108)
+        scale = q3k_get_scale(u8, bb + 96, e >> 4)
+        hbit = (u8[bb + ((e >> 4) & 1) * 16 + (e & 15)] >> (e >> 5)) & 1
+        qb = bb + 32 + (e >> 7) * 32 + ((e >> 4) & 1) * 16 + (e & 15)
+        low2 = (u8[qb] >> (((e >> 5) & 3) * 2)) & 3
+        return d * scale * ((low2 | (hbit << 2)) - 4)
+    if t == 12:
+        d, dmin = read_f16(u8, bb), read_f16(u8, bb + 2)
+        sc, mn = q4k_get_scale_min(u8, bb + 4, (e >> 6) * 2 + ((e >> 5) & 1))
+        qs = u8[bb + 16 + (e >> 6) * 32 + (e & 31)]
+        q4 = (qs >> 4) & 0xF if (e >> 5) & 1 else qs & 0xF
+        return d * sc * q4 - dmin * mn
+    if t == 13:
+        d, dmin = read_f16(u8, bb), read_f16(u8, bb + 2)
+        sc, mn = q4k_get_scale_min(u8, bb + 4, (e >> 6) * 2 + ((e >> 5) & 1))
+        qh_bit = (e >> 6) * 2 + ((e >> 5) & 1)
+        high = (u8[bb + 16 + (e & 31)] >> qh_bit) & 1
+        qs = u8[bb + 48 + (e >> 6) * 32 + (e & 31)]
+        low4 = (qs >> 4) & 0xF if (e >> 5) & 1 else qs & 0xF
+        return d * sc * (low4 | (high << 4)) - dmin * mn
+    if t == 14:
+        d = read_f16(u8, bb + 208)
+        ql = u8[bb + (e >> 7) * 64 + ((e >> 5) & 1) * 32 + (e & 31)]
+        low4 = (ql >> 4) & 0xF if (e >> 6) & 1 else ql & 0xF
+        qh = u8[bb + 128 + (e >> 7) * 32 + (e & 31)]
+        high2 = (qh >> (((e >> 5) & 3) * 2)) & 0x3
+        sbyte = u8[bb + 192 + (e >> 7) * 8 + ((e >> 5) & 3) * 2 + ((e & 31) >> 4)]
+        scale = sbyte - 256 if sbyte >= 128 else sbyte
+        return d * scale * ((low4 | (high2 << 4)) - 32)
+    raise ValueError(t)
+
+
+def matmul_kq(t, w: bytes, in_dim, out_dim, x):
+    """matmulQ{2..6}KxF32 (tensor.js:304-466): dot += input * weight, f32 store."""
+    bpc = -(-in_dim // QK_K)
+    out = []
+    for c in range(out_dim):
+        dot = 0.0
+        for b in range(bpc):
+            bb = (c * bpc + b) * KQ_BYTES[t]
+            for e in range(min(QK_K, in_dim - b * QK_K)):
+                dot += x[b * QK_K + e] * kq_weight(t, w, bb, e)
+        out.append(f32(dot))
+    return out
+
+
+def column_kq(t, w: bytes, out_dim, c):
+    """_q{2..6}kColumn (tensor.js:551-664): one column stored into a Float32Array."""
+    bpc = -(-out_dim // QK_K)
+    out = []
+    for b in range(bpc):
+        bb = (c * bpc + b) * KQ_BYTES[t]
+        for e in range(min(QK_K, out_dim - b * QK_K)):
+            out.append(f32(kq_weight(t, w, bb, e)))
+    return out
+
+
+def kquant_vectors():
+    """Seeded random superblocks of every k-quant type (random bytes, finite f16 scale fields),
+    K = 512 and a ragged K = 300 (the last superblock partly used), 4 columns, 2 input rows."""
+    rng = np.random.default_rng(2024)
+    d_off = {10: (80, 82), 11: (108,), 12: (0, 2), 13: (0, 2), 14: (208,)}
+    out = {}
+    for t in (10, 11, 12, 13, 14):
+        for K in (512, 300):
+            N = 4
+            nblk = N * -(-K // QK_K)
+            raw = rng.integers(0, 256, size=nblk * KQ_BYTES[t], dtype=np.uint8)
+            for b in range(nblk):
+                for off in d_off[t]:
+                    v = np.float16(abs(rng.normal(0, 0.02)) + 1e-4)
+                    raw[b * KQ_BYTES[t] + off: b * KQ_BYTES[t] + off + 2] = np.frombuffer(v.tobytes(), np.uint8)
+            x = rng.standard_normal((2, K)).astype(np.float32)
+            w = raw.tobytes()
+            y = [matmul_kq(t, w, K, N, [float(v) for v in row]) for row in x]
+            cols = [column_kq(t, w, K, c) for c in range(N)]
+            key = f"t{t}_k{K}"
+            out[key + "_raw"] = raw
+            out[key + "_x"] = x
+            out[key + "_y"] = np.asarray(y, np.float32)
+            out[key + "_cols"] = np.asarray(cols, np.float32)
+    return out
+
+
 def main():
     qq3, lfm, qw = micro_specs()
     np.savez_compressed(HERE / "ops.npz", **ops_vectors(qq3))
@@ -344,8 +461,12 @@ def main():
     np.savez_compressed(HERE / "micro_lfm2.npz", **run_model(qq3, lfm, toks_l, 4))
     toks_q = qq3.synth.uniform_tokens(5, 78, qw.n_vocab)
     np.savez_compressed(HERE / "micro_qwen3.npz", **run_model(qq3, qw, toks_q, 4))
+    np.savez_compressed(HERE / "kquants.npz", **kquant_vectors())
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["kquants"]:  # only the k-quant vectors (leaves the other files as they are)
+        np.savez_compressed(HERE / "kquants.npz", **kquant_vectors())
+    else:
+        main()

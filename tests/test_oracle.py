@@ -97,3 +97,29 @@ def test_oracle_matches_numpy_float64(qq3, orc):
     got = orc.matmul(raw, 8, [K, N], x)
     assert np.allclose(got, want, rtol=0, atol=1e-6 * np.abs(want).max())
     assert np.array_equal(orc.dequant(raw, 8, [K, N]), qq3.synth.dequant_q8_0(raw, K * N))
+
+
+@pytest.mark.parametrize("t", [10, 11, 12, 13, 14])
+def test_kquants_golden(orc, t):
+    """k-quant matmuls, column lookups and dequantisation (Q2_K..Q6_K, tensor.js:267-664) of the
+    C oracle against the independent transcription's vectors, bit for bit (K = 512 and a ragged
+    K = 300 whose last superblock is partly used)."""
+    g = _load("kquants.npz")
+    for K in (512, 300):
+        key = f"t{t}_k{K}"
+        raw, x, y, cols = g[key + "_raw"], g[key + "_x"], g[key + "_y"], g[key + "_cols"]
+        N = cols.shape[0]
+        assert np.array_equal(orc.matmul(raw, t, [K, N], x), y), key
+        for c in range(N):
+            assert np.array_equal(_column(orc, raw, t, K, N, c), cols[c]), (key, c)
+        assert np.array_equal(orc.dequant(raw, t, [K, N]), cols.reshape(-1)), key
+
+
+def _column(orc, raw, t, K, N, c):
+    """embeddingLookupGeneric of a k-quant tensor (tensor.js:511-549): column c."""
+    import ctypes as C
+
+    tens = orc.make_tensor(raw, t, [K, N])
+    out = np.empty(K, dtype=np.float32)
+    orc.lib().orc_embedding(C.byref(tens), c, out.ctypes.data)
+    return out
