@@ -392,6 +392,60 @@ static void lfm2_moe_token(const orc_layer* L, int n_embd, int n_expert, int top
     }
 }
 
+/* Qwen3Engine._moEFFN (qwen3-engine.js:304-362): softmax router, stable top-k of the
+ * probabilities, weights renormalised by their sum (no seed, no bias), slot-order accumulation
+ * into a Float32Array, masked experts skipped without renormalising. */
+static void qwen3_moe_token(const orc_layer* L, int n_embd, int n_expert, int top_k, const float* normed,
+                            float* moe_out, float* routing, const uint8_t* mask, float* probs, float* g, float* u,
+                            float* dn) {
+    /* 1. router logits and softmaxInPlace over them (:306-307) */
+    orc_matmul(&L->t[ORC_ROUTER], normed, probs);
+    orc_softmax(probs, 0, n_expert);
+    /* 2. stable descending sort of (prob, id), first top_k (:310-316) */
+    int top[256];
+    double topw[256];
+    uint8_t taken[256];
+    memset(taken, 0, sizeof(taken));
+    for (int k = 0; k < top_k; k++) {
+        int best = -1;
+        for (int e = 0; e < n_expert; e++) {
+            if (taken[e]) continue;
+            if (best < 0 || probs[e] > probs[best]) best = e;
+        }
+        taken[best] = 1;
+        top[k] = best;
+        topw[k] = probs[best];
+    }
+    /* 3. renormalisation (:318-320) */
+    double sum_w = 0;
+    for (int k = 0; k < top_k; k++) sum_w += topw[k];
+    const double inv = sum_w > 0 ? 1.0 / sum_w : 0.0;
+    if (routing) { /* onRouterUpdate record (:323-330): [ids | weights | probs] */
+        for (int k = 0; k < top_k; k++) {
+            routing[k] = (float)top[k];
+            routing[top_k + k] = (float)(topw[k] * inv);
+        }
+        for (int e = 0; e < n_expert; e++) routing[2 * top_k + e] = probs[e];
+    }
+    /* 4. experts in slot order (:333-359) */
+    const int64_t n_ff = L->t[ORC_GATE_EXPS].ne[1];
+    for (int64_t i = 0; i < n_embd; i++) moe_out[i] = 0.0f;
+    for (int k = 0; k < top_k; k++) {
+        const int e = top[k];
+        if (mask && mask[e]) continue;
+        const double weight = topw[k] * inv;
+        orc_tensor gs = expert_slice(&L->t[ORC_GATE_EXPS], e);
+        orc_tensor us = expert_slice(&L->t[ORC_UP_EXPS], e);
+        orc_tensor ds = expert_slice(&L->t[ORC_DOWN_EXPS], e);
+        orc_matmul(&gs, normed, g);
+        orc_silu(g, n_ff);
+        orc_matmul(&us, normed, u);
+        orc_mul(g, u, n_ff);
+        orc_matmul(&ds, g, dn);
+        for (int64_t i = 0; i < n_embd; i++) moe_out[i] = (float)((double)moe_out[i] + weight * (double)dn[i]);
+    }
+}
+
 void orc_lfm2_moe(const orc_layer* layer, int n_embd, int n_expert, int top_k, const float* normed, int64_t T,
                   float* out, float* routing, const uint8_t* mask) {
     const int64_t n_ff = layer->t[ORC_GATE_EXPS].ne[1];
@@ -427,6 +481,8 @@ struct orc_model {
 int orc_n_moe_layers(const orc_model* m) { return m->n_moe; }
 
 int orc_model_create(const orc_model_desc* desc, orc_model** out) {
+    /* the routers keep their top-k in fixed arrays */
+    if (desc->n_expert > 256 || desc->n_expert_used > 64 || desc->n_expert_used > desc->n_expert) return -3;
     orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
     if (!m) return -1;
     m->d = *desc;
@@ -613,8 +669,12 @@ int orc_forward(orc_model* m, int32_t token, int32_t position, int skip_logits, 
         if (L->is_moe) {
             const int K = m->d.n_expert_used, NE = m->d.n_expert;
             float* rec = routing ? routing + (size_t)m->moe_slot[l] * (2 * K + NE) : NULL;
-            lfm2_moe_token(L, E, NE, K, m->normed, m->moe_out, rec, m->mask, m->r_logits, m->r_w, m->r_sel,
-                           m->ffn, m->ffn_tmp, m->e_dn);
+            if (m->d.arch == 0) /* Qwen3 family: softmax router (qwen3-engine.js:198-199, 304-362) */
+                qwen3_moe_token(L, E, NE, K, m->normed, m->moe_out, rec, m->mask, m->r_w, m->ffn, m->ffn_tmp,
+                                m->e_dn);
+            else
+                lfm2_moe_token(L, E, NE, K, m->normed, m->moe_out, rec, m->mask, m->r_logits, m->r_w, m->r_sel,
+                               m->ffn, m->ffn_tmp, m->e_dn);
             orc_add(m->hidden, m->moe_out, E);
         } else {
             dense_ffn(m, L);

@@ -286,6 +286,10 @@ class Qwen3CudaEngine(_CudaEngine):
         self.headDim = self.nQ // self.nHeads
         self.nExperts = 0
         self.nExpertsUsed = 0
+        if any(gguf.getTensorMetaByName(f"blk.{i}.ffn_gate_inp.weight") is not None for i in range(self.nLayers)):
+            # Qwen3-MoE routes by softmax (qwen3-engine.js:304-362); the device MoE path is the LFM2
+            # sigmoid router, so such a model is refused rather than routed wrongly
+            raise NotImplementedError("Qwen3-MoE (softmax-routed experts) is not supported on the GPU yet")
 
     def _is_attn(self, i):
         return True

@@ -109,10 +109,10 @@ class ModelSpec:
     extra: dict = field(default_factory=dict)
 
     def is_attn(self, i: int) -> bool:
-        return self.arch == "qwen3" or i in self.attn_layers
+        return self.arch in ("qwen3", "qwen3moe") or i in self.attn_layers
 
     def is_moe(self, i: int) -> bool:
-        return self.arch == "lfm2moe" and self.n_expert > 0 and i >= self.n_dense_lead
+        return self.arch in ("lfm2moe", "qwen3moe") and self.n_expert > 0 and i >= self.n_dense_lead
 
 
 def qwen3_0p6b(seed: int = 1234) -> ModelSpec:
@@ -150,7 +150,7 @@ def tensor_specs(spec: ModelSpec) -> list[tuple[str, int, list]]:
     E, V, hd = spec.n_embd, spec.n_vocab, spec.head_dim
     nq, nkv = spec.n_head * hd, spec.n_head_kv * hd
     out = [("token_embd.weight", TYPE_Q8_0, [E, V])]
-    if spec.arch == "qwen3":
+    if spec.arch in ("qwen3", "qwen3moe"):
         out.append(("output_norm.weight", TYPE_F32, [E]))
     else:
         out.append(("token_embd_norm.weight", TYPE_F32, [E]))
@@ -172,8 +172,9 @@ def tensor_specs(spec: ModelSpec) -> list[tuple[str, int, list]]:
             out += [(b + "ffn_gate_inp.weight", TYPE_Q8_0, [E, NE]),
                     (b + "ffn_gate_exps.weight", TYPE_Q8_0, [E, F, NE]),
                     (b + "ffn_up_exps.weight", TYPE_Q8_0, [E, F, NE]),
-                    (b + "ffn_down_exps.weight", TYPE_Q8_0, [F, E, NE]),
-                    (b + "exp_probs_b.bias", TYPE_F32, [NE])]
+                    (b + "ffn_down_exps.weight", TYPE_Q8_0, [F, E, NE])]
+            if spec.arch == "lfm2moe":  # the Qwen3-MoE router has no selection bias
+                out.append((b + "exp_probs_b.bias", TYPE_F32, [NE]))
         else:
             F = spec.n_ff
             out += [(b + "ffn_gate.weight", TYPE_Q8_0, [E, F]), (b + "ffn_up.weight", TYPE_Q8_0, [E, F]),
@@ -237,6 +238,10 @@ def kv_metadata(spec: ModelSpec) -> list[tuple[str, int, object, int | None]]:
           (a + "attention.value_length", U32, spec.head_dim, None)]
     if spec.arch == "qwen3":
         kv.append((a + "attention.head_count_kv", U32, spec.n_head_kv, None))
+    elif spec.arch == "qwen3moe":  # the keys Qwen3Engine reads for MoE layers (qwen3-engine.js:40-41, 89-94)
+        kv += [(a + "attention.head_count_kv", U32, spec.n_head_kv, None),
+               (a + "expert_count", U32, spec.n_expert, None), (a + "expert_used_count", U32, spec.n_expert_used, None),
+               (a + "expert_feed_forward_length", U32, spec.n_ff_exp, None)]
     else:
         per_layer = [spec.n_head_kv if spec.is_attn(i) else 0 for i in range(spec.n_layers)]
         kv += [(a + "attention.head_count_kv", ARR, per_layer, U32), (a + "expert_count", U32, spec.n_expert, None),

@@ -10,7 +10,7 @@ these vectors, and the GPU tests compare against the C oracle.  Parity with the 
 itself stays unpinned.
 
 Run:  python tests/golden/gen_golden.py   (rewrites the .npz files in this folder; with the
-      argument `kquants`, only kquants.npz)
+      argument `kquants` or `qwen3moe`, only kquants.npz or micro_qwen3moe.npz)
 """
 from __future__ import annotations
 
@@ -216,9 +216,36 @@ class Engine:
         y = [f32(bcx[E + d] * co[d]) for d in range(E)]
         return W.mm(b + "shortconv.out_proj.weight", y)
 
+    def moe_qwen3(self, l, normed):
+        """Qwen3Engine._moEFFN (qwen3-engine.js:304-362): softmax router, stable top-k, weights
+        renormalised by their plain sum. Returns (out, record)."""
+        W, c = self.W, self.c
+        b = f"blk.{l}."
+        ne, k = c["n_expert"], c["n_used"]
+        probs = softmax(W.mm(b + "ffn_gate_inp.weight", normed))
+        top = sorted(range(ne), key=lambda e: -probs[e])[:k]  # stable sort, descending
+        tw = [probs[e] for e in top]
+        s = 0.0
+        for w in tw:
+            s += w
+        inv = 1.0 / s if s > 0 else 0.0
+        rec = [float(e) for e in top] + [f32(w * inv) for w in tw] + probs
+        out = [0.0] * c["n_embd"]
+        for j, e in enumerate(top):
+            if e in self.mask:
+                continue
+            weight = tw[j] * inv
+            g = silu(W.mm(b + "ffn_gate_exps.weight", normed, e))
+            g = mul(g, W.mm(b + "ffn_up_exps.weight", normed, e))
+            dn = W.mm(b + "ffn_down_exps.weight", g, e)
+            out = [f32(out[i] + weight * dn[i]) for i in range(len(out))]
+        return out, rec
+
     def moe(self, l, normed):
         """Lfm2Engine._moEFFN (lfm2-engine.js:413-487). Returns (out, record)."""
         W, c = self.W, self.c
+        if c["arch"] == "qwen3moe":
+            return self.moe_qwen3(l, normed)
         b = f"blk.{l}."
         ne, k = c["n_expert"], c["n_used"]
         logits = W.mm(b + "ffn_gate_inp.weight", normed)
@@ -290,12 +317,18 @@ def micro_specs():
     return qq3, lfm, qw
 
 
+def micro_qwen3moe_spec(qq3):
+    """A micro Qwen3-MoE: every layer attention + an 8-expert, top-2 softmax-routed FFN."""
+    return qq3.synth.ModelSpec("qwen3moe", 2, 64, 2, 1, 64, 96, 64, 1e6, 1e-6, n_expert=8, n_expert_used=2,
+                               n_ff_exp=32, seed=2026, name="micro-qwen3moe")
+
+
 def run_model(qq3, spec, tokens, n_gen):
     tensors = qq3.synth.build_tensors(spec)
     W = Weights(tensors)
     cfg = dict(n_embd=spec.n_embd, n_head=spec.n_head, n_head_kv=spec.n_head_kv, head_dim=spec.head_dim,
                eps=float(np.float32(spec.eps)), rope=spec.rope_base, n_layers=spec.n_layers,
-               n_expert=spec.n_expert, n_used=spec.n_expert_used,
+               n_expert=spec.n_expert, n_used=spec.n_expert_used, arch=spec.arch,
                out_norm="token_embd_norm.weight" if spec.arch == "lfm2moe" else "output_norm.weight")
     eng = Engine(W, cfg)
     logits, hidden, recs = [], [], []
@@ -462,11 +495,21 @@ def main():
     toks_q = qq3.synth.uniform_tokens(5, 78, qw.n_vocab)
     np.savez_compressed(HERE / "micro_qwen3.npz", **run_model(qq3, qw, toks_q, 4))
     np.savez_compressed(HERE / "kquants.npz", **kquant_vectors())
+    write_qwen3moe(qq3)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 
+def write_qwen3moe(qq3):
+    spec = micro_qwen3moe_spec(qq3)
+    toks = qq3.synth.uniform_tokens(5, 79, spec.n_vocab)
+    np.savez_compressed(HERE / "micro_qwen3moe.npz", **run_model(qq3, spec, toks, 4))
+
+
 if __name__ == "__main__":
-    if sys.argv[1:] == ["kquants"]:  # only the k-quant vectors (leaves the other files as they are)
+    # with an argument, only that file (leaves the others as they are)
+    if sys.argv[1:] == ["kquants"]:
         np.savez_compressed(HERE / "kquants.npz", **kquant_vectors())
+    elif sys.argv[1:] == ["qwen3moe"]:
+        write_qwen3moe(micro_specs()[0])
     else:
         main()

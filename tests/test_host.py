@@ -97,6 +97,12 @@ def test_engine_hparams_mirror_js(qq3):
     q = object.__new__(qq3.Qwen3CudaEngine)
     q._read_hparams(g)
     assert (q.nLayers, q.nEmb, q.nHeads, q.nHeadKV, q.headDim, q.nVocab, q.maxCtx) == (28, 1024, 16, 8, 128, 151936, 4096)
+    # a Qwen3-MoE file is refused by the device engine, not routed with the LFM2 router
+    spec = qq3.synth.ModelSpec("qwen3moe", 2, 64, 2, 1, 64, 96, 64, 1e6, 1e-6, n_expert=8, n_expert_used=2,
+                               n_ff_exp=32)
+    g = qq3.synth.MemoryGGUF(spec, {n: (t, ne, np.zeros(1, np.uint8)) for n, t, ne in qq3.synth.tensor_specs(spec)})
+    with pytest.raises(NotImplementedError):
+        object.__new__(qq3.Qwen3CudaEngine)._read_hparams(g)
 
 
 def test_host_sampling_mirrors_tensor_js(qq3):
