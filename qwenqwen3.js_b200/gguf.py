@@ -22,22 +22,29 @@ KV_TYPES = dict(UINT8=0, INT8=1, UINT16=2, INT16=3, UINT32=4, INT32=5, FLOAT32=6
                 UINT64=10, INT64=11, FLOAT64=12)
 _SCALAR = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
 
-# tensor types used here (gguf.js:25-34)
+# tensor types (gguf.js:25-34)
 TYPE_F32 = 0
 TYPE_F16 = 1
 TYPE_Q8_0 = 8
+TYPE_Q2_K, TYPE_Q3_K, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 10, 11, 12, 13, 14
+
+# (values per block, bytes per block), as _tensorNbytes (gguf.js:302-341) sizes them over all
+# elements.  The 32-value legacy types take the ggml block sizes: gguf.js gives Q4_0/Q4_1/Q5_0/
+# Q5_1 32 quant bytes per block (34/36/42/44) where a block holds 16 (18/20/22/24); no matmul of
+# the reference reads those types.
+_BLOCKS = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24),
+           TYPE_Q8_0: (32, 34), 9: (32, 36), TYPE_Q2_K: (256, 84), TYPE_Q3_K: (256, 110), TYPE_Q4_K: (256, 144),
+           TYPE_Q5_K: (256, 176), TYPE_Q6_K: (256, 210)}
 
 
 def tensor_nbytes(shape, ggml_type: int) -> int:
-    """Exact byte size (gguf.js:302-341 for the types this path uses)."""
+    """Exact byte size of a tensor of this shape and ggml type.  An unknown type is an error (the
+    JS assumes F32 with a warning, which misplaces every later tensor's bytes)."""
     n = int(np.prod([int(s) for s in shape], dtype=np.int64))
-    if ggml_type == TYPE_F32:
-        return n * 4
-    if ggml_type == TYPE_F16:
-        return n * 2
-    if ggml_type == TYPE_Q8_0:
-        return -(-n // 32) * 34
-    raise ValueError(f"unsupported tensor type {ggml_type}")
+    if ggml_type not in _BLOCKS:
+        raise ValueError(f"unsupported tensor type {ggml_type}")
+    per, size = _BLOCKS[ggml_type]
+    return -(-n // per) * size
 
 
 @dataclass

@@ -10,7 +10,7 @@ these vectors, and the GPU tests compare against the C oracle.  Parity with the 
 itself stays unpinned.
 
 Run:  python tests/golden/gen_golden.py   (rewrites the .npz files in this folder; with the
-      argument `kquants` or `qwen3moe`, only kquants.npz or micro_qwen3moe.npz)
+      argument `kquants`, `qwen3moe` or `qwen3kq`, only that file)
 """
 from __future__ import annotations
 
@@ -157,6 +157,8 @@ class Weights:
     def mm(self, n, x, expert=None):
         ne = self.ne(n)
         raw = self.raw(n)
+        if self.t[n][0] in KQ_BYTES:  # matmulGeneric's k-quant cases (tensor.js:485-496)
+            return matmul_kq(self.t[n][0], raw, ne[0], ne[1], x)
         if expert is not None:
             bpc = -(-ne[0] // 32) * 34
             raw = raw[expert * ne[1] * bpc:(expert + 1) * ne[1] * bpc]  # _expertSlice (lfm2-engine.js:490-505)
@@ -276,7 +278,10 @@ class Engine:
     def forward(self, token, pos, skip=False):
         W, c = self.W, self.c
         E, eps = c["n_embd"], c["eps"]
-        hidden = embedding_q80(W.raw("token_embd.weight"), E, token)
+        if W.t["token_embd.weight"][0] in KQ_BYTES:  # embeddingLookupGeneric (tensor.js:499-523)
+            hidden = column_kq(W.t["token_embd.weight"][0], W.raw("token_embd.weight"), E, token)
+        else:
+            hidden = embedding_q80(W.raw("token_embd.weight"), E, token)
         recs, hid = [], []
         slot = 0
         for l in range(c["n_layers"]):
@@ -323,8 +328,36 @@ def micro_qwen3moe_spec(qq3):
                                n_ff_exp=32, seed=2026, name="micro-qwen3moe")
 
 
-def run_model(qq3, spec, tokens, n_gen):
-    tensors = qq3.synth.build_tensors(spec)
+def micro_qwen3kq_spec(qq3):
+    """A micro Qwen3 (hidden 256) whose embedding / tied lm_head and several projections are k-quants."""
+    return qq3.synth.ModelSpec("qwen3", 2, 256, 2, 1, 128, 96, 256, 1e6, 1e-6, seed=2027, name="micro-qwen3-kq")
+
+
+# tensor -> k-quant type in the micro k-quant model (the rest stay Q8_0 / F32)
+KQ_ASSIGN = {"token_embd.weight": 14, "blk.0.attn_q.weight": 12, "blk.0.ffn_down.weight": 14,
+             "blk.1.attn_output.weight": 13, "blk.1.ffn_gate.weight": 10, "blk.1.ffn_up.weight": 11}
+
+
+def kquantize(tensors, seed):
+    """Replace the KQ_ASSIGN tensors by seeded random superblocks of their k-quant type (finite,
+    small f16 scale fields)."""
+    rng = np.random.default_rng(seed)
+    d_off = {10: (80, 82), 11: (108,), 12: (0, 2), 13: (0, 2), 14: (208,)}
+    out = dict(tensors)
+    for name, t in KQ_ASSIGN.items():
+        _, ne, _ = tensors[name]
+        nblk = ne[1] * -(-ne[0] // QK_K)
+        raw = rng.integers(0, 256, size=nblk * KQ_BYTES[t], dtype=np.uint8)
+        for b in range(nblk):
+            for off in d_off[t]:
+                v = np.float16(abs(rng.normal(0, 4e-4)) + 1e-5)
+                raw[b * KQ_BYTES[t] + off: b * KQ_BYTES[t] + off + 2] = np.frombuffer(v.tobytes(), np.uint8)
+        out[name] = (t, ne, raw)
+    return out
+
+
+def run_model(qq3, spec, tokens, n_gen, tensors=None):
+    tensors = tensors if tensors is not None else qq3.synth.build_tensors(spec)
     W = Weights(tensors)
     cfg = dict(n_embd=spec.n_embd, n_head=spec.n_head, n_head_kv=spec.n_head_kv, head_dim=spec.head_dim,
                eps=float(np.float32(spec.eps)), rope=spec.rope_base, n_layers=spec.n_layers,
@@ -496,7 +529,15 @@ def main():
     np.savez_compressed(HERE / "micro_qwen3.npz", **run_model(qq3, qw, toks_q, 4))
     np.savez_compressed(HERE / "kquants.npz", **kquant_vectors())
     write_qwen3moe(qq3)
+    write_qwen3kq(qq3)
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+def write_qwen3kq(qq3):
+    spec = micro_qwen3kq_spec(qq3)
+    toks = qq3.synth.uniform_tokens(4, 80, spec.n_vocab)
+    tensors = kquantize(qq3.synth.build_tensors(spec), 2028)
+    np.savez_compressed(HERE / "micro_qwen3kq.npz", **run_model(qq3, spec, toks, 3, tensors))
 
 
 def write_qwen3moe(qq3):
@@ -511,5 +552,7 @@ if __name__ == "__main__":
         np.savez_compressed(HERE / "kquants.npz", **kquant_vectors())
     elif sys.argv[1:] == ["qwen3moe"]:
         write_qwen3moe(micro_specs()[0])
+    elif sys.argv[1:] == ["qwen3kq"]:
+        write_qwen3kq(micro_specs()[0])
     else:
         main()

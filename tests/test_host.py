@@ -173,3 +173,28 @@ def test_top_p_top_k_matches_js_transcription(qq3):
         r = float(rng.random())
         want = _js_top_p_top_k(logits, t, top_p, top_k, r)
         assert sample_top_p_top_k(logits.copy(), t, top_p, top_k, rng=lambda: r) == want, case
+
+
+def test_gguf_reads_k_quant_and_legacy_tensors(qq3, tmp_path):
+    """A GGUF holding k-quant and legacy quantised tensors parses, and every tensor reads back its
+    own bytes (block sizes: 84/110/144/176/210 per 256 values, 18/20/22/24/36 per 32)."""
+    G = qq3.gguf
+    w = G.GGUFWriter()
+    w.add_kv("general.architecture", G.KV_TYPES["STRING"], "qwen3")
+    rng = np.random.default_rng(3)
+    want = {}
+    for t in (2, 3, 6, 7, 9, 10, 11, 12, 13, 14):
+        shape = [512, 3]
+        raw = rng.integers(0, 256, size=G.tensor_nbytes(shape, t), dtype=np.uint8)
+        w.add_tensor(f"t{t}", shape, t, raw)
+        want[f"t{t}"] = (t, raw)
+    path = tmp_path / "k.gguf"
+    w.write(path)
+    r = G.GGUFReader.fromFile(path)
+    for name, (t, raw) in want.items():
+        m = r.getTensorMetaByName(name)
+        assert m.type == t and m.shape == [512, 3]
+        assert np.array_equal(m.raw(), raw), name
+    assert G.tensor_nbytes([512, 3], 12) == 6 * 144 and G.tensor_nbytes([64], 2) == 2 * 18
+    with pytest.raises(ValueError):
+        G.tensor_nbytes([32], 15)

@@ -49,15 +49,15 @@ class _Npz:
 def _micro(qq3, which):
     from tests.golden.gen_golden import micro_specs  # noqa: F401  (same specs as the generator)
 
-    from tests.golden.gen_golden import micro_qwen3moe_spec
+    from tests.golden.gen_golden import micro_qwen3kq_spec, micro_qwen3moe_spec
 
     _, lfm, qw = micro_specs()
-    spec = {"lfm2": lfm, "qwen3": qw, "qwen3moe": micro_qwen3moe_spec(qq3)}[which]
+    spec = {"lfm2": lfm, "qwen3": qw, "qwen3moe": micro_qwen3moe_spec(qq3), "qwen3kq": micro_qwen3kq_spec(qq3)}[which]
     kv = qq3.synth.kv_values(spec)
     return spec, _Npz(_load(f"micro_{which}.npz"), kv)
 
 
-@pytest.mark.parametrize("which", ["lfm2", "qwen3", "qwen3moe"])
+@pytest.mark.parametrize("which", ["lfm2", "qwen3", "qwen3moe", "qwen3kq"])
 def test_micro_model_golden(qq3, orc, which):
     spec, g = _micro(qq3, which)
     m = orc.OracleModel(g, max_ctx=32, threads=1)
