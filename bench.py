@@ -270,7 +270,8 @@ def run_ours(args, ws, rank, local):
         "setup_s": {"weight_generation": round(gen_s, 1)},
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline(g, spec, budget_s=args.cpu_seconds)
+        res["cpu_baseline"] = cpu_decode(g, spec, qq3.synth.uniform_tokens(args.prompt, SEED, spec.n_vocab),
+                                         budget_s=args.cpu_seconds)
     if dist:
         dist.destroy_process_group()
     if rank == 0:
@@ -285,17 +286,32 @@ def _oracle():
     return orc
 
 
-def cpu_baseline(g, spec, budget_s: float = 12.0, prompt_len: int = 8, steps=None, warmup: int = 0,
-                 label: str = "LFM2-8B-A1B-shaped decode"):
-    """The oracle (C restatement of the JS CPU path) on the host cores: prompt_len-token
-    prompt, then greedy decode steps (time-bounded unless steps is given)."""
+def _cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_decode(g, spec, prompt, steps=None, warmup: int = 0, budget_s: float = 12.0, single_s: float = 0.0,
+               label: str = "LFM2-8B-A1B-shaped decode"):
+    """The oracle (C restatement of the JS CPU path) on the host cores, on the same workload as
+    the GPU arm: the whole prompt (all but its last token without logits, as generate() does),
+    then greedy decode steps -- `steps` of them, or as many as fit in budget_s seconds -- timed on
+    all host threads.  With single_s > 0 the decode then continues on one thread (the JS engine is
+    single-threaded) for about that many seconds."""
     orc = _oracle()
     cores = os.cpu_count() or 1
-    m = orc.OracleModel(g, max_ctx=prompt_len + (steps or 256) + warmup + 8, threads=cores)
-    prompt = load_package().synth.uniform_tokens(prompt_len, SEED, spec.n_vocab)
+    n_steps = steps if steps is not None else 4096
+    m = orc.OracleModel(g, max_ctx=len(prompt) + warmup + n_steps + 64, threads=cores)
+    t0 = time.perf_counter()
     for p, t in enumerate(prompt[:-1]):
         m.forward(int(t), p, True)
-    cur, pos = int(prompt[-1]), prompt_len - 1
+    prefill_s = time.perf_counter() - t0
+    cur, pos = int(prompt[-1]), len(prompt) - 1
     for _ in range(warmup):
         cur = int(np.argmax(m.forward(cur, pos, False)))
         pos += 1
@@ -305,28 +321,91 @@ def cpu_baseline(g, spec, budget_s: float = 12.0, prompt_len: int = 8, steps=Non
         pos += 1
         n += 1
         el = time.perf_counter() - t0
-        if (steps is not None and n >= steps) or (steps is None and (el >= budget_s and n >= 2)):
+        if (steps is not None and n >= steps) or (steps is None and (el >= budget_s and n >= 2)) or n >= n_steps:
             break
-    return {"value": round(n / el, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{label}: {prompt_len}-token prompt then {n} greedy steps "
-                      f"(all {spec.n_layers} layers, f64-accumulating C restatement of the JS CPU path, "
-                      f"{cores} threads)"}
+    res = {"value": round(n / el, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+           "cpu_model": _cpu_model(), "nproc": cores,
+           "sample": f"{label}: {len(prompt)}-token prompt ({len(prompt) - 1} prefill tokens in "
+                     f"{prefill_s:.1f} s), {warmup} warm-up + {n} timed greedy steps at positions "
+                     f"{len(prompt) - 1 + warmup}.., all {spec.n_layers} layers, f64-accumulating C restatement of "
+                     f"the JS CPU path, {cores} threads"}
+    if single_s > 0:
+        orc.set_threads(1)
+        k, t0 = 0, time.perf_counter()
+        while True:
+            cur = int(np.argmax(m.forward(cur, pos, False)))
+            pos += 1
+            k += 1
+            el1 = time.perf_counter() - t0
+            if el1 >= single_s and k >= 1:
+                break
+        orc.set_threads(cores)
+        res["single_thread"] = {"value": round(k / el1, 4), "unit": "tok/s", "cores": 1,
+                                "sample": f"{k} greedy steps on one thread, continuing the same decode"}
+    return res
+
+
+def _model_file(spec_seed: int) -> tuple[Path, Path] | None:
+    """The config-4 model written to a GGUF file by a separate process (so that the timed CPU arm's
+    process loads nothing but the oracle), plus its prompt ids, in the repository's scratch folder
+    (git- and snapshot-ignored).  None when there is no room for the 8.9 GB file."""
+    d = ROOT / "_scratch"
+    d.mkdir(exist_ok=True)
+    path = d / f"qq3_lfm2_8b_a1b_seed{spec_seed}.gguf"
+    ids = path.with_suffix(".prompt.npy")
+    if path.exists() and ids.exists():
+        return path, ids
+    st = os.statvfs(d)
+    if st.f_bavail * st.f_frsize < 10 * 1024 ** 3:
+        return None
+    r = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--write-model", str(path)],
+                       capture_output=True, text=True)
+    if r.returncode == 0 and path.exists() and ids.exists():
+        return path, ids
+    for f in (path, ids):
+        try:
+            f.unlink()
+        except OSError:
+            pass
+    return None
+
+
+def write_model(path: str) -> None:
+    qq3 = load_package()
+    spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
+    tmp = Path(path + ".part")
+    qq3.synth.write_gguf(spec, tmp)
+    np.save(Path(path).with_suffix(".prompt.npy"), qq3.synth.uniform_tokens(PROMPT, SEED, spec.n_vocab))
+    tmp.rename(path)
 
 
 def run_reference(args, ws, rank):
+    """The reference algorithm's CPU implementation on the host cores, on the GPU arm's workload:
+    the same seeded model, the same 512-token prompt, then K timed greedy steps (after W warm-up
+    steps) on all host threads, and a single-thread sample of the same decode."""
     if rank != 0:
         return
     qq3 = load_package()
     spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
-    g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
-    cb = cpu_baseline(g, spec, prompt_len=16, steps=args.steps, warmup=args.warmup)
+    files = _model_file(SEED)
+    if files is not None:
+        g = qq3.gguf.GGUFReader.fromFile(files[0])
+        prompt = np.load(files[1])
+        weights = "written by a separate process to a GGUF file, memory-mapped here"
+    else:
+        g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
+        prompt = qq3.synth.uniform_tokens(PROMPT, SEED, spec.n_vocab)
+        weights = "generated in this process (no scratch directory had room for the GGUF file)"
+    cb = cpu_decode(g, spec, prompt, steps=args.steps, warmup=args.warmup, single_s=args.cpu_seconds)
     res = {
         "metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1000.0 / cb["value"], 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64 accumulate (JS numbers), f32 stores",
         "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)", "impl": "reference",
         "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 (benchmark config 4)",
-                   "prompt": 16, "note": "bounded slice: 16-token prompt instead of 512 (CPU time)"},
+                   "layers": "24 (18 short-conv, 6 GQA attention; 2 dense FFN 7168, 22 MoE 32x top-4 x 1792)",
+                   "hidden": 2048, "vocab": 65536, "prompt": len(prompt), "global_batch": 1,
+                   "same_config": True, "weights": weights},
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -522,8 +601,8 @@ def run_batch_decode(args, ws, rank, local):
     ctx.close()
     if rank == 0 and not args.no_cpu_baseline:
         # the reference serves one sequence per engine: one sequence, a short prompt (CPU time)
-        res["cpu_baseline"] = cpu_baseline(g, spec, budget_s=args.cpu_seconds, prompt_len=8,
-                                           label="Qwen3-8B-shaped decode of one sequence")
+        res["cpu_baseline"] = cpu_decode(g, spec, qq3.synth.uniform_tokens(8, SEED, spec.n_vocab),
+                                         budget_s=args.cpu_seconds, label="Qwen3-8B-shaped decode of one sequence")
     if rank == 0:
         print(json.dumps(res), flush=True)
 
@@ -588,7 +667,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n-expert", type=int, default=32,
                     help="experts per MoE layer (profiling knob: a token streams the same bytes for any count >= 4)")
+    ap.add_argument("--write-model", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.write_model:
+        write_model(args.write_model)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.prompt is None and args.case != "batch-decode":

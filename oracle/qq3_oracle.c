@@ -35,25 +35,60 @@ double orc_f16_to_double(uint16_t h) {
     return sign ? -v : v;
 }
 
-static double rd_f16(const uint8_t* p) { return orc_f16_to_double((uint16_t)(p[0] | (p[1] << 8))); }
+/* every binary16 value as a double (the values orc_f16_to_double gives), filled when the
+ * library is loaded */
+static double g_f16_tab[65536];
+__attribute__((constructor)) static void f16_tab_fill(void) {
+    for (int h = 0; h < 65536; h++) g_f16_tab[h] = orc_f16_to_double((uint16_t)h);
+}
+static inline double rd_f16(const uint8_t* p) { return g_f16_tab[p[0] | (p[1] << 8)]; }
 static float rd_f32(const uint8_t* p) { float f; memcpy(&f, p, 4); return f; }
 
-/* matmulQ80xF32 (tensor.js:26-53): output[c] = sum_b sum_i (x*q)*d, f64 sum, f32 store. */
+/* matmulQ80xF32 (tensor.js:26-53): output[c] = sum_b sum_i (x*q)*d, f64 sum, f32 store.
+ * Four columns are walked together so that their four f64 sums form independent dependency
+ * chains; each column's own sequence of operations (and so its result) is the JS loop's. */
 static void matmul_q8(const uint8_t* w, int64_t in_dim, int64_t out_dim, const float* x, float* y) {
     const int64_t bpc = (in_dim + 31) / 32;
+    const int64_t n4 = (out_dim + 3) / 4;
 #pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1 && out_dim >= 64)
-    for (int64_t c = 0; c < out_dim; c++) {
-        double dot = 0;
-        const uint8_t* col = w + (size_t)c * bpc * 34;
-        for (int64_t b = 0; b < bpc; b++) {
-            const uint8_t* blk = col + b * 34;
-            const double d = rd_f16(blk);
-            const int8_t* qs = (const int8_t*)(blk + 2);
-            const int64_t eb = b * 32;
-            for (int i = 0; i < 32 && eb + i < in_dim; i++)
-                dot += ((double)x[eb + i] * (double)qs[i]) * d;
+    for (int64_t c4 = 0; c4 < n4; c4++) {
+        const int64_t c0 = c4 * 4;
+        if (c0 + 4 > out_dim) {
+            for (int64_t c = c0; c < out_dim; c++) {
+                double dot = 0;
+                const uint8_t* col = w + (size_t)c * bpc * 34;
+                for (int64_t b = 0; b < bpc; b++) {
+                    const uint8_t* blk = col + b * 34;
+                    const double d = rd_f16(blk);
+                    const int8_t* qs = (const int8_t*)(blk + 2);
+                    const int64_t eb = b * 32;
+                    for (int i = 0; i < 32 && eb + i < in_dim; i++) dot += ((double)x[eb + i] * (double)qs[i]) * d;
+                }
+                y[c] = (float)dot;
+            }
+            continue;
         }
-        y[c] = (float)dot;
+        double dot0 = 0, dot1 = 0, dot2 = 0, dot3 = 0;
+        const uint8_t* col0 = w + (size_t)c0 * bpc * 34;
+        const size_t cs = (size_t)bpc * 34;
+        for (int64_t b = 0; b < bpc; b++) {
+            const uint8_t* b0 = col0 + b * 34;
+            const double d0 = rd_f16(b0), d1 = rd_f16(b0 + cs), d2 = rd_f16(b0 + 2 * cs), d3 = rd_f16(b0 + 3 * cs);
+            const int8_t *q0 = (const int8_t*)(b0 + 2), *q1 = (const int8_t*)(b0 + cs + 2),
+                         *q2 = (const int8_t*)(b0 + 2 * cs + 2), *q3 = (const int8_t*)(b0 + 3 * cs + 2);
+            const int64_t eb = b * 32;
+            for (int i = 0; i < 32 && eb + i < in_dim; i++) {
+                const double xi = (double)x[eb + i];
+                dot0 += (xi * (double)q0[i]) * d0;
+                dot1 += (xi * (double)q1[i]) * d1;
+                dot2 += (xi * (double)q2[i]) * d2;
+                dot3 += (xi * (double)q3[i]) * d3;
+            }
+        }
+        y[c0] = (float)dot0;
+        y[c0 + 1] = (float)dot1;
+        y[c0 + 2] = (float)dot2;
+        y[c0 + 3] = (float)dot3;
     }
 }
 

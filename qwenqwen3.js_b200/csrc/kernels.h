@@ -176,8 +176,12 @@ void set_pdl(int on);
 // 0 forces the register-streamed kernels of kernels_gemv.cu everywhere (A/B measurements)
 void set_stream_path(int on);
 int stream_path();
-// error word written by bounded waits that gave up (0 = none); read-and-clear
+// error word written by bounded waits that gave up (0 = none); read-and-clear.  The address is
+// that of the current device's copy of the word (resolved once per device).
 int* kernel_err_ptr();
+// true the first time it is called for (key, current device): per-device one-time set-up such as
+// cudaFuncSetAttribute, which applies to the current device only
+bool first_use_on_device(const void* key);
 int take_kernel_error(cudaStream_t s);
 
 }  // namespace qq3

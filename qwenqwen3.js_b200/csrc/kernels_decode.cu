@@ -1603,11 +1603,8 @@ bool decode_phase_fits(const PhaseDesc& p) {
 
 void launch_decode_step(const PhaseDesc* prog, int n_phases, DecodeCtl* ctl, int* err, cudaStream_t s) {
     const size_t smem = (size_t)kDecRingBytes + kDecDigitBytes + kDecAttnBytes + 2 * kDecSlots * 8 + 2 * kDecSlots * 4;
-    static bool init = false;
-    if (!init) {
+    if (first_use_on_device(reinterpret_cast<const void*>(k_decode)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        init = true;
-    }
     static int per_sm = -1;
     if (per_sm < 0) QQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode, kDecThreads, smem));
     QQ_CHECK(per_sm >= 1, -4, "persistent decode kernel does not fit on an SM");

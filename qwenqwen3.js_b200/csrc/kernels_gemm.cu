@@ -745,11 +745,8 @@ void launch_split(const DTensor& W, int64_t N, const __half* a16, int M, float* 
                                       G::BN, CU_TENSOR_MAP_SWIZZLE_NONE);
     const bool d_tma = scales_by_tma(W);
     const CUtensorMap td = d_tma ? scale_map(W, G::BN) : tb;
-    static bool init = false;
-    if (!init) {
+    if (first_use_on_device(reinterpret_cast<const void*>(k_gemm_q8_tma<SPLIT>)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_tma<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::Smem));
-        init = true;
-    }
     QQ_CHECK(N <= (int64_t)65535 * G::BN, QQ_ERR_INVALID, "tensor-core Q8_0 matmul: too many columns");
     const unsigned gx = groups ? (unsigned)groups->max_tiles : (unsigned)((M + kBM - 1) / kBM);
     dim3 grid(gx, (unsigned)((N + G::BN - 1) / G::BN));
@@ -788,11 +785,8 @@ void launch_rows(const DTensor& W, const __half* a16, int M, float* y, int ldc, 
                                       kRowsBM, CU_TENSOR_MAP_SWIZZLE_NONE);
     const bool d_tma = scales_by_tma(W);
     const CUtensorMap td = d_tma ? scale_map(W, kRowsBM) : tw;
-    static bool init = false;
-    if (!init) {
+    if (first_use_on_device(reinterpret_cast<const void*>(k_gemm_q8_rows<MN>)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_rows<MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::Smem));
-        init = true;
-    }
     const int S = rows_splits(N, K);
     const int64_t items = ((N + kRowsBM - 1) / kRowsBM) * S;
     QQ_CHECK(items <= (int64_t)1 << 30, QQ_ERR_INVALID, "few-row Q8_0 matmul: too many rows");

@@ -260,10 +260,11 @@ static void launch(const XStage& st, const Map& map, const Epi& epi, int n_items
     for (int v = 0; v < st.nvec; v++)
         QQ_CHECK(st.x[v] && ((uintptr_t)st.x[v] & 15u) == 0, -1, "GEMV input must be a 16-byte aligned device pointer");
     QQ_CHECK(((uintptr_t)st.norm_w & 15u) == 0, -1, "norm weight must be 16-byte aligned");
-    static int per_sm = 0;
+    static int per_sm = 0;  // the same on every B200
     auto kern = k_gemv<S, Map, Epi>;
-    if (!per_sm) {
+    if (first_use_on_device(reinterpret_cast<const void*>(kern)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxStageBytes));
+    if (!per_sm) {
         QQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, 48 * 1024));
         if (per_sm < 1) per_sm = 1;
     }

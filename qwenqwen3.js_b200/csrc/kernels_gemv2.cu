@@ -18,6 +18,10 @@
 // Consumer mode B: source s has its own input h[s] (MoE down over the top-k experts); each
 //   warp computes one source for all kG items of a stage, partials meet in shared memory and
 //   are combined in slot order with the routing weights.
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "gemv2_core.cuh"
 
 namespace qq3 {
@@ -410,10 +414,35 @@ void set_pdl(int on) { g_pdl = on; }
 
 __device__ int g_kernel_err;
 
+namespace {
+std::mutex g_dev_mu;
+constexpr int kMaxDevices = 64;
+int* g_err_addr[kMaxDevices] = {nullptr};
+std::set<std::pair<const void*, int>> g_dev_once;
+
+int current_device() {
+    int dev = 0;
+    QQ_CUDA_TRY(cudaGetDevice(&dev));
+    QQ_CHECK(dev >= 0 && dev < kMaxDevices, -1, "device index too large");
+    return dev;
+}
+}  // namespace
+
 int* kernel_err_ptr() {
-    static int* p = nullptr;
-    if (!p) QQ_CUDA_TRY(cudaGetSymbolAddress((void**)&p, g_kernel_err));
-    return p;
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    if (!g_err_addr[dev]) {
+        void* p = nullptr;
+        QQ_CUDA_TRY(cudaGetSymbolAddress(&p, g_kernel_err));
+        g_err_addr[dev] = static_cast<int*>(p);
+    }
+    return g_err_addr[dev];
+}
+
+bool first_use_on_device(const void* key) {
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    return g_dev_once.insert({key, dev}).second;
 }
 
 int take_kernel_error(cudaStream_t s) {
@@ -458,11 +487,8 @@ static void launch_a(const XStage& st, const Map& map, const Epi& epi, int n_ite
     const int stages = pick_stages(per, fixed);
     const size_t smem = ring_bytes(S, K, stages) + fixed + 2 * (size_t)stages * sizeof(uint64_t);
     auto kern = k_gemv2<S, CPL, Map, Epi>;
-    static bool init = false;
-    if (!init) {
+    if (first_use_on_device(reinterpret_cast<const void*>(kern)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        init = true;
-    }
     const int groups = (n_items + kG - 1) / kG;
     const int grid = groups < num_sms() ? groups : num_sms();
     launch_ex(kern, grid, smem, s, st, map, epi, n_items, stages, kernel_err_ptr());
@@ -535,16 +561,16 @@ bool launch2_moe_down_combine(const DTensor& down_exps, const int* idx, const fl
     const int groups = (N + kG - 1) / kG;
     const int grid = groups < num_sms() ? groups : num_sms();
     if (K <= 512) {
-        static bool init = false;
-        if (!init) { QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); init = true; }
+        if (first_use_on_device(reinterpret_cast<const void*>(k_moe_down2<4, 1>)))
+            QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         launch_ex(k_moe_down2<4, 1>, grid, smem, s, down_exps.qs, down_exps.d, idx, w, mask, h, hidden, K, N, stages, kernel_err_ptr());
     } else if (K <= 1024) {
-        static bool init = false;
-        if (!init) { QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); init = true; }
+        if (first_use_on_device(reinterpret_cast<const void*>(k_moe_down2<4, 2>)))
+            QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         launch_ex(k_moe_down2<4, 2>, grid, smem, s, down_exps.qs, down_exps.d, idx, w, mask, h, hidden, K, N, stages, kernel_err_ptr());
     } else {
-        static bool init = false;
-        if (!init) { QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024)); init = true; }
+        if (first_use_on_device(reinterpret_cast<const void*>(k_moe_down2<4, 4>)))
+            QQ_CUDA_TRY(cudaFuncSetAttribute(k_moe_down2<4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         launch_ex(k_moe_down2<4, 4>, grid, smem, s, down_exps.qs, down_exps.d, idx, w, mask, h, hidden, K, N, stages, kernel_err_ptr());
     }
     return true;

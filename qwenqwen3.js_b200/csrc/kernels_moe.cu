@@ -98,11 +98,8 @@ void launch_lfm2_router(const DTensor& router, const float* bias, const float* x
     QQ_CHECK(((uintptr_t)x & 15u) == 0 && ((uintptr_t)norm_w & 15u) == 0 && K % 32 == 0, -1,
              "router input must be 16-byte aligned with K % 32 == 0");
     const size_t smem = (size_t)K * sizeof(float);
-    static bool init = false;
-    if (!init) {
+    if (first_use_on_device(reinterpret_cast<const void*>(k_lfm2_router)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_lfm2_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-        init = true;
-    }
     k_lfm2_router<<<T, kGemvThreads, smem, s>>>(router.qs, router.d, bias, x, K, norm_w, eps, n_expert, top_k, record,
                                                 idx, w);
     QQ_CUDA_TRY(cudaGetLastError());

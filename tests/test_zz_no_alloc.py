@@ -34,13 +34,28 @@ def _layer(qq3, ctx):
     return L, keep
 
 
-def test_moe_block_noalloc_matches_allocating_entry_point(qq3, gpu_ctx):
+def _layer_tensors(qq3):
+    spec = qq3.synth.lfm2_8b_a1b(seed=99)
+    names = {f"blk.2.{n}" for n in ("ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                    "ffn_down_exps.weight", "exp_probs_b.bias")}
+    return {k.split(".", 2)[2]: v for k, v in qq3.synth.build_tensors(spec, only=names).items()}
+
+
+def test_moe_block_noalloc_matches_allocating_entry_point(qq3, orc, gpu_ctx):
+    """Three calls in a row -- 6 rows with routing records, 3 rows without (the records then live
+    in the library's array), and 1024 rows, the stated maximum (where qq_moe_block regroups the
+    rows by expert on the tensor cores while this entry point serves them token by token) --
+    against qq_moe_block on every row and record, and against the CPU oracle on a sample of rows."""
     import torch
 
     L, keep = _layer(qq3, gpu_ctx)
-    # two calls in a row; the second is smaller and takes the records from the scratch array
-    for call, (T, with_records) in enumerate([(6, True), (3, False)]):
-        x = torch.from_numpy(qq3.synth.normal_f32(T * 2048, seed=100 + call).reshape(T, 2048)).cuda()
+    tensors = _layer_tensors(qq3)
+    bias = tensors["exp_probs_b.bias"][2].view(np.float32)
+    orc.set_threads(8)
+    limit = qq3.runtime.QQ_NOALLOC_MAX_TOKENS
+    for call, (T, with_records) in enumerate([(6, True), (3, False), (limit, True)]):
+        x_host = qq3.synth.normal_f32(T * 2048, seed=100 + call).reshape(T, 2048)
+        x = torch.from_numpy(x_host).cuda()
         want = torch.empty((T, 2048), dtype=torch.float32, device="cuda")
         want_rec = torch.empty((T, 40), dtype=torch.float32, device="cuda")
         torch.cuda.synchronize()
@@ -56,11 +71,21 @@ def test_moe_block_noalloc_matches_allocating_entry_point(qq3, gpu_ctx):
         for t in range(T):
             assert rel_err(g[t], w[t]) < TOL, f"call {call}, token {t}"
         if with_records:
-            assert np.array_equal(got_rec.cpu().numpy()[:, :4], want_rec.cpu().numpy()[:, :4])
+            # the same router kernel on both paths: ids, weights and probabilities agree exactly
+            assert np.array_equal(got_rec.cpu().numpy(), want_rec.cpu().numpy()), f"call {call}: routing records"
+        # the CPU oracle (the restated _moEFFN) on every row of the small calls, 12 rows of the large
+        rows = np.arange(T) if T <= 8 else np.unique(np.concatenate([[0, T - 1], qq3.synth.uniform_tokens(10, 7, T)]))
+        ref, ref_rec = orc.lfm2_moe(tensors, 2048, 32, 4, x_host[rows])
+        ids = want_rec.cpu().numpy()[:, :4]  # equal to the no-alloc call's (checked above when it returns them)
+        for i, t in enumerate(rows):
+            if not np.array_equal(ids[t], ref_rec[i, :4]):
+                s = np.sort(ref_rec[i, 8:] + bias)[::-1]
+                assert abs(s[3] - s[4]) < 1e-5, f"call {call}, token {t}: top-k differs without a near-tie"
+                continue
+            assert rel_err(g[t], ref[i]) < TOL, f"call {call}, token {t}: vs oracle"
     # beyond the stated limit the call is refused before any GPU work
-    big = qq3.runtime.QQ_NOALLOC_MAX_TOKENS + 1
     with pytest.raises(qq3.runtime.QQError) as e:
-        gpu_ctx.moe_block_noalloc(L, 32, 4, 16, big, 16, None)
+        gpu_ctx.moe_block_noalloc(L, 32, 4, 16, limit + 1, 16, None)
     assert "exceeds the limit" in str(e.value)
     for k in keep:
         k.free()
