@@ -193,6 +193,47 @@ int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_i
  * generated ids; *n_out their count. */
 int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps, int think_id,
                 int eos_id, int32_t* out_tokens, int* n_out);
+/* ---------------------------------------------------------------- sampling on the device */
+
+/* thinkingMode (tensor.js:240-243) */
+#define QQ_THINK_SUPPRESS 0 /* logits[think_id] = -Infinity before sampling */
+#define QQ_THINK_SHORTEN 1  /* until end_think_id was produced, force it while it ranks in the top_k */
+#define QQ_THINK_FULL 2     /* no control */
+#define QQ_SAMPLE_MAX_TOP_K 1024
+
+/* The generate() sampling options (qwen3-engine.js:397-405, lfm2-engine.js:523-542).  temperature
+ * <= 0 is greedy; otherwise sampleTopPTopK (tensor.js:188-228) with 1 <= top_k <= 1024 (the JS
+ * default is 40; top_k = 0, "no limit", is not served on the device).  Think ids outside the
+ * vocabulary disable think control.  seed picks the stream of uniform draws that replaces
+ * Math.random(): the draw after the logits of position p of sequence s is
+ * qq_sample_uniform(seed, s, p). */
+typedef struct qq_sample_params {
+    double temperature;
+    double top_p;
+    int32_t top_k;
+    int32_t think_mode; /* QQ_THINK_* */
+    int32_t think_id, end_think_id;
+    uint64_t seed;
+} qq_sample_params;
+
+/* forward(token_id, pos, false) then sampleWithThinkControl on the device: *token_out is the
+ * next token (4-byte readback instead of the logits).  think_done is the caller's
+ * thinkOpts.thinkingDone.  Replaces the logits readback + host sampling of generate()
+ * (webgpu.js:2030, 2092). */
+int qq_forward_sample(qq_model* m, int32_t token_id, int seq_id, int pos, const qq_sample_params* params,
+                      int think_done, int32_t* token_out);
+/* generate() with sampling (qwen3-engine.js:397-457, lfm2-engine.js:523-583): prefill, then up
+ * to max_steps sampled tokens; without a stop token (eos_id < 0) every step and its sampling run
+ * on the device with no host round trip. */
+int qq_generate_sample(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps,
+                       const qq_sample_params* params, int eos_id, int32_t* out_tokens, int* n_out);
+/* Op level: sampleWithThinkControl over logits_dev[n] with the given uniform draw r in [0, 1)
+ * (tensor.js:244-265 with Math.random() = r). */
+int qq_sample_logits(qq_ctx* ctx, const float* logits_dev, int n, const qq_sample_params* params, double r,
+                     int think_done, int32_t* token_out);
+/* The uniform draw the device sampler uses after the logits of position pos of sequence seq_id. */
+int qq_sample_uniform(uint64_t seed, int seq_id, int pos, double* r_out);
+
 /* resetState()/resetKVCache() (lfm2-engine.js:216-224, kv-cache.js:50-52): zero the
  * conv states of seq_id; the KV cache is overwritten before it is read. */
 int qq_reset(qq_model* m, int seq_id);

@@ -112,7 +112,7 @@ struct qq_model {
     float* dump = nullptr;    // [n_layers][n_embd] for qq_forward_dump
     int* h_ctl = nullptr;     // pinned staging [2 * h_ctl_cap]
     size_t h_ctl_cap = 0;
-    int* h_small = nullptr;   // pinned [8]: suppress id, argmax, token, pos, kernel error word
+    int* h_small = nullptr;   // pinned [8]: suppress id, argmax, token, pos, kernel error word, think flag
     int suppress_set = INT32_MIN;  // the suppress id last copied to the device
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
     cudaStream_t cap = nullptr;
@@ -138,6 +138,13 @@ struct qq_model {
     size_t tarena_len = 0;
     float* aarena = nullptr;         // accumulated vectors + counters, two halves of aarena_half words
     size_t aarena_half = 0;
+    // device sampling (allocated on first use): arguments, per-sequence 'thinking done' flags,
+    // probability keys [n_vocab], the sampled id; pinned staging for the arguments
+    qq3::SampleArgs* sargs = nullptr;
+    int* think_done = nullptr;
+    uint32_t* spk = nullptr;
+    int* sout = nullptr;
+    qq3::SampleArgs* h_sargs = nullptr;
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
@@ -174,11 +181,12 @@ void free_model(qq_model* m) {
     void* bufs[] = {m->hidden, m->qkv, m->attn_out, m->y, m->h, m->logits, m->k_cache, m->v_cache, m->conv_state,
                     m->trace, m->rope_cs, m->attn_part, m->attn_counter, m->rec, m->rlogits, m->rcounter, m->ridx, m->rw,
                     m->mask, m->ctl,
-                    m->suppress, m->best, m->dump};
+                    m->suppress, m->best, m->dump, m->sargs, m->think_done, m->spk, m->sout};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_ctl) cudaFreeHost(m->h_ctl);
     if (m->h_small) cudaFreeHost(m->h_small);
+    if (m->h_sargs) cudaFreeHost(m->h_sargs);
     if (m->cap) cudaStreamDestroy(m->cap);
 }
 
@@ -725,6 +733,93 @@ void set_suppress(qq_model* m, int id) {
     m->h_small[0] = id;
     QQ_CUDA_TRY(cudaMemcpyAsync(m->suppress, m->h_small, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
     m->suppress_set = id;
+}
+
+// ---- device sampling ------------------------------------------------------------------
+// sampleWithThinkControl (tensor.js:244-265) after a decode step, on the step's logits.
+
+qq3::SampleArgs sample_args(const qq_sample_params* p) {
+    need(p != nullptr, "sampling parameters are required");
+    need(p->think_mode >= QQ_THINK_SUPPRESS && p->think_mode <= QQ_THINK_FULL, "unknown thinking mode");
+    // top_k ranks the end-of-thinking id in 'shorten' mode and limits top-k sampling; sampling
+    // (temperature > 0) needs at least one candidate
+    need(p->top_k >= (p->temperature > 0.0 ? 1 : 0) && p->top_k <= QQ_SAMPLE_MAX_TOP_K,
+         "top_k must be in [1, " + std::to_string(QQ_SAMPLE_MAX_TOP_K) + "] for device sampling");
+    need(!(p->temperature > 0.0) || p->top_p == p->top_p, "top_p is NaN");
+    qq3::SampleArgs a;
+    a.temperature = p->temperature;
+    a.top_p = p->top_p;
+    a.top_k = p->top_k;
+    a.think_mode = p->think_mode;
+    a.think_id = p->think_id;
+    a.end_think_id = p->end_think_id;
+    a.seed = p->seed;
+    return a;
+}
+
+void ensure_sampling(qq_model* m) {
+    if (m->sargs) return;
+    m->sargs = dalloc<qq3::SampleArgs>(1);
+    m->think_done = dalloc<int>((size_t)m->d.n_seq);
+    m->spk = dalloc<uint32_t>((size_t)m->d.n_vocab);
+    m->sout = dalloc<int>(1);
+    QQ_CUDA_TRY(cudaMallocHost(&m->h_sargs, sizeof(qq3::SampleArgs)));
+}
+
+// the arguments and the sequence's 'thinking done' flag, in stream order
+void put_sample_state(qq_model* m, const qq3::SampleArgs& a, int seq, int think_done) {
+    cudaStream_t s = m->ctx->stream;
+    QQ_CUDA_TRY(cudaStreamSynchronize(s));  // the pinned staging may still feed an earlier copy
+    *m->h_sargs = a;
+    m->h_small[5] = think_done ? 1 : 0;
+    QQ_CUDA_TRY(cudaMemcpyAsync(m->sargs, m->h_sargs, sizeof(qq3::SampleArgs), cudaMemcpyHostToDevice, s));
+    QQ_CUDA_TRY(cudaMemcpyAsync(m->think_done + seq, m->h_small + 5, sizeof(int), cudaMemcpyHostToDevice, s));
+}
+
+int* trace_of(qq_model* m, int seq) { return m->trace + (size_t)seq * (m->d.max_ctx + 1); }
+
+// the decode step followed by the sampler, as one graph per sequence (key (seq, 2))
+cudaGraphExec_t get_sample_graph(qq_model* m, int seq) {
+    auto key = std::make_pair(seq, 2);
+    auto it = m->graphs.find(key);
+    if (it != m->graphs.end()) return it->second;
+    const bool mega = mega_enabled(m);
+    qq_model::Prog* pr = mega ? &get_prog(m, seq, true) : nullptr;
+    cudaGraph_t g = nullptr;
+    QQ_CUDA_TRY(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeRelaxed));
+    try {
+        if (mega) qq3::launch_decode_step(pr->d_prog, pr->n, m->dctl, qq3::kernel_err_ptr(), m->cap);
+        else enqueue_step(m, seq, true, m->cap, false);
+        qq3::launch_sample(m->logits, m->d.n_vocab, m->sargs, m->think_done + seq, -1.0, seq, -1, m->ctl,
+                           trace_of(m, seq), m->sout, m->spk, m->cap);
+    } catch (...) {
+        cudaStreamEndCapture(m->cap, &g);
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        throw;
+    }
+    QQ_CUDA_TRY(cudaStreamEndCapture(m->cap, &g));
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    QQ_CUDA_TRY(e);
+    m->graphs[key] = ge;
+    return ge;
+}
+
+// sample after the logits of position pos (already computed), into ctl[0] and *m->sout
+void sample_after(qq_model* m, int seq, int pos) {
+    qq3::launch_sample(m->logits, m->d.n_vocab, m->sargs, m->think_done + seq, -1.0, seq, pos, m->ctl,
+                       trace_of(m, seq), m->sout, m->spk, m->ctx->stream);
+}
+
+int read_sampled(qq_model* m) {
+    cudaStream_t s = m->ctx->stream;
+    QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->sout, sizeof(int), cudaMemcpyDeviceToHost, s));
+    QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 4, qq3::kernel_err_ptr(), sizeof(int), cudaMemcpyDeviceToHost, s));
+    QQ_CUDA_TRY(cudaStreamSynchronize(s));
+    if (m->h_small[4]) check_kernel_error(s);
+    return m->h_small[1];
 }
 
 // ---- batched prefill -------------------------------------------------------------------
@@ -1577,6 +1672,100 @@ int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, in
             }
         }
         *n_out = n;
+    });
+}
+
+int qq_forward_sample(qq_model* m, int32_t token_id, int seq_id, int pos, const qq_sample_params* params,
+                      int think_done, int32_t* token_out) {
+    return guard([&] {
+        need(m && token_out, "qq_forward_sample: NULL argument");
+        check_seq_pos(m, seq_id, pos, 1);
+        const qq3::SampleArgs a = sample_args(params);
+        DeviceGuard dg(m->ctx->device);
+        ensure_sampling(m);
+        put_sample_state(m, a, seq_id, think_done);
+        run_tokens(m, &token_id, 1, seq_id, pos, true);
+        sample_after(m, seq_id, pos);
+        *token_out = read_sampled(m);
+    });
+}
+
+int qq_generate_sample(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps,
+                       const qq_sample_params* params, int eos_id, int32_t* out_tokens, int* n_out) {
+    return guard([&] {
+        need(m && prompt && n_prompt >= 1 && max_steps >= 0 && n_out && (out_tokens || max_steps == 0),
+             "qq_generate_sample: bad argument");
+        check_seq_pos(m, seq_id, 0, n_prompt + max_steps);
+        const qq3::SampleArgs a = sample_args(params);
+        DeviceGuard dg(m->ctx->device);
+        cudaStream_t s = m->ctx->stream;
+        ensure_sampling(m);
+        // resetState(): conv states to zero; KV positions are rewritten before use
+        QQ_CUDA_TRY(cudaMemsetAsync(m->conv(seq_id, 0), 0, sizeof(float) * m->d.n_layers * 2 * m->d.n_embd, s));
+        // thinkingDone starts true only in 'suppress' mode (lfm2-engine.js:537-542)
+        put_sample_state(m, a, seq_id, a.think_mode == QQ_THINK_SUPPRESS);
+        run_tokens(m, prompt, n_prompt, seq_id, 0, true);
+        sample_after(m, seq_id, n_prompt - 1);
+        int cur = read_sampled(m);
+        int n = 0;
+        if (eos_id < 0) {
+            // no stop token: the whole continuation runs on the device (step + sampler graph)
+            if (max_steps > 0) {
+                std::vector<int32_t> tail(max_steps);
+                cudaGraphExec_t g = get_sample_graph(m, seq_id);
+                for (int i = 0; i < max_steps; i++) QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+                QQ_CUDA_TRY(cudaMemcpyAsync(tail.data(), trace_of(m, seq_id) + n_prompt + 1,
+                                            sizeof(int) * max_steps, cudaMemcpyDeviceToHost, s));
+                QQ_CUDA_TRY(cudaStreamSynchronize(s));
+                check_kernel_error(s);
+                for (int i = 0; i < max_steps; i++) out_tokens[n++] = i == 0 ? cur : tail[i - 1];
+            }
+        } else {
+            for (int step = 0; step < max_steps; step++) {
+                if (cur == eos_id) break;
+                int32_t t = cur;
+                run_tokens(m, &t, 1, seq_id, n_prompt + step, true);
+                sample_after(m, seq_id, n_prompt + step);
+                out_tokens[n++] = cur;
+                cur = read_sampled(m);
+            }
+        }
+        *n_out = n;
+    });
+}
+
+int qq_sample_logits(qq_ctx* ctx, const float* logits_dev, int n, const qq_sample_params* params, double r,
+                     int think_done, int32_t* token_out) {
+    return guard([&] {
+        need(ctx && logits_dev && token_out && n >= 1, "qq_sample_logits: bad argument");
+        need(r >= 0.0 && r < 1.0, "qq_sample_logits: r must be a uniform draw in [0, 1)");
+        const qq3::SampleArgs a = sample_args(params);
+        DeviceGuard dg(ctx->device);
+        cudaStream_t s = ctx->stream;
+        // scratch: [args | out, flag | keys]
+        char* sc = static_cast<char*>(ctx_scratch(ctx, 256 + sizeof(uint32_t) * (size_t)n));
+        auto* dargs = reinterpret_cast<qq3::SampleArgs*>(sc);
+        int* dout = reinterpret_cast<int*>(sc + 128);
+        int* dflag = dout + 1;
+        struct {
+            qq3::SampleArgs a;
+            int flag;
+        } h{a, think_done ? 1 : 0};
+        QQ_CUDA_TRY(cudaMemcpyAsync(dargs, &h.a, sizeof(h.a), cudaMemcpyHostToDevice, s));
+        QQ_CUDA_TRY(cudaMemcpyAsync(dflag, &h.flag, sizeof(int), cudaMemcpyHostToDevice, s));
+        qq3::launch_sample(logits_dev, n, dargs, dflag, r, 0, 0, nullptr, nullptr, dout,
+                           reinterpret_cast<uint32_t*>(sc + 256), s);
+        int v = -1;
+        QQ_CUDA_TRY(cudaMemcpyAsync(&v, dout, sizeof(int), cudaMemcpyDeviceToHost, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        *token_out = v;
+    });
+}
+
+int qq_sample_uniform(uint64_t seed, int seq_id, int pos, double* r_out) {
+    return guard([&] {
+        need(r_out != nullptr, "qq_sample_uniform: NULL argument");
+        *r_out = qq3::sample_uniform(seed, seq_id, pos);
     });
 }
 

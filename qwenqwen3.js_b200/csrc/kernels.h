@@ -176,6 +176,35 @@ void set_pdl(int on);
 // 0 forces the register-streamed kernels of kernels_gemv.cu everywhere (A/B measurements)
 void set_stream_path(int on);
 int stream_path();
+// ---- next-token sampling (kernels_sample.cu) ----
+constexpr int kSampleMaxTopK = 1024;
+constexpr int kThinkSuppress = 0, kThinkShorten = 1, kThinkFull = 2;
+struct SampleArgs {
+    double temperature, top_p;  // JS numbers
+    int top_k;                  // 1..kSampleMaxTopK
+    int think_mode;             // kThink*
+    int think_id, end_think_id;
+    unsigned long long seed;
+};
+// The uniform draw in [0, 1) for (seed, sequence, position): a splitmix64 finaliser over the
+// three, top 53 bits.  Host code reproduces it bit for bit.
+__host__ __device__ inline double sample_uniform(unsigned long long seed, int seq, int pos) {
+    unsigned long long z = seed ^ (0x9E3779B97F4A7C15ull * (unsigned long long)(unsigned)(pos + 1)) ^
+                           (0xD1B54A32D192ED03ull * (unsigned long long)(unsigned)(seq + 1));
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return (double)(z >> 11) * (1.0 / 9007199254740992.0);
+}
+// sampleWithThinkControl over logits[n] into out[0].  r >= 0 is the uniform draw; r < 0 draws
+// sample_uniform(seed, seq, pos), pos < 0 meaning ctl[1] - 1.  With ctl set the token also
+// becomes ctl[0] and trace[ctl[1]] (the step's greedy id is replaced).  think_done (nullable) is
+// the per-sequence "thinking done" flag of the 'shorten' mode; set when endThinkId is produced.
+// scratch: n words.
+void launch_sample(const float* logits, int n, const SampleArgs* args_dev, int* think_done, double r, int seq,
+                   int pos, int* ctl, int* trace, int* out, uint32_t* scratch, cudaStream_t s);
+
 // error word written by bounded waits that gave up (0 = none); read-and-clear.  The address is
 // that of the current device's copy of the word (resolved once per device).
 int* kernel_err_ptr();

@@ -207,8 +207,14 @@ class _CudaEngine:
             m += 1
 
     def generate(self, tokenIds, maxSteps=512, temperature=0.7, topP=0.9, topK=40, thinkingMode="suppress",
-                 onToken=None, onPrefill=None, onFinish=None, abortSignal=None):
-        """generate(tokenIds, options) (qwen3-engine.js:397-457, lfm2-engine.js:523-583)."""
+                 onToken=None, onPrefill=None, onFinish=None, abortSignal=None, seed=None):
+        """generate(tokenIds, options) (qwen3-engine.js:397-457, lfm2-engine.js:523-583).
+
+        Sampling runs on the device (qq_forward_sample: one 4-byte readback a token) for every
+        option set the device sampler serves -- greedy, and top-k/top-p with 1 <= topK <= 1024
+        (the JS default is 40).  Math.random() is replaced by the device's seeded draws (seed:
+        default a random 64-bit value).  topK = 0 ("no limit") with temperature > 0 samples the
+        logits on the host, exactly as tensor.js:188-228."""
         think = dict(mode=thinkingMode, thinkId=self.THINK_ID, endThinkId=self.END_THINK_ID,
                      thinkingDone=thinkingMode == "suppress")
         aborted = (lambda: bool(abortSignal and getattr(abortSignal, "aborted", False)))
@@ -216,6 +222,11 @@ class _CudaEngine:
         n = len(tokenIds)
         device_greedy = temperature <= 0 and thinkingMode in ("suppress", "full")
         suppress = self.THINK_ID if thinkingMode == "suppress" and self.THINK_ID < self.nVocab else -1
+        dev_params = None
+        if not device_greedy and (temperature <= 0 or 1 <= topK <= rt.QQ_SAMPLE_MAX_TOP_K):
+            dev_params = rt.sample_params(temperature, topP, max(0, min(int(topK), rt.QQ_SAMPLE_MAX_TOP_K)),
+                                          thinkingMode, self.THINK_ID, self.END_THINK_ID,
+                                          random.getrandbits(64) if seed is None else seed)
         if aborted():
             return None
         if n > 1:
@@ -233,6 +244,10 @@ class _CudaEngine:
         def step(tok, pos):
             if device_greedy:
                 return self.forward_argmax(tok, pos, suppress)
+            if dev_params is not None:
+                nxt = self.model.forward_sample(tok, pos, dev_params, think["thinkingDone"])
+                self._emit_routing()
+                return nxt
             logits = self.forward(tok, pos, False).copy()
             if think["thinkId"] >= self.nVocab:
                 think_local = dict(think, mode="full")

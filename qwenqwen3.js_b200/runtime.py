@@ -54,6 +54,37 @@ class QQError(RuntimeError):
         self.code = code
 
 
+class SampleParams(C.Structure):
+    """qq_sample_params: generate()'s sampling options (tensor.js:188-265)."""
+    _fields_ = [("temperature", C.c_double), ("top_p", C.c_double), ("top_k", C.c_int32), ("think_mode", C.c_int32),
+                ("think_id", C.c_int32), ("end_think_id", C.c_int32), ("seed", C.c_uint64)]
+
+
+QQ_THINK_SUPPRESS = 0
+QQ_THINK_SHORTEN = 1
+QQ_THINK_FULL = 2
+QQ_SAMPLE_MAX_TOP_K = 1024
+THINK_MODES = {"suppress": QQ_THINK_SUPPRESS, "shorten": QQ_THINK_SHORTEN, "full": QQ_THINK_FULL}
+
+
+def sample_params(temperature: float, top_p: float, top_k: int, think_mode: str = "suppress", think_id: int = -1,
+                  end_think_id: int = -1, seed: int = 0) -> SampleParams:
+    return SampleParams(float(temperature), float(top_p), int(top_k), THINK_MODES[think_mode], int(think_id),
+                        int(end_think_id), int(seed) & 0xFFFFFFFFFFFFFFFF)
+
+
+def sample_uniform(seed: int, seq: int, pos: int) -> float:
+    """The device sampler's uniform draw after the logits of position pos of sequence seq (the
+    same splitmix64 finaliser and 53-bit scaling as sample_uniform in csrc/kernels.h)."""
+    M = 0xFFFFFFFFFFFFFFFF
+    z = (seed & M) ^ ((0x9E3779B97F4A7C15 * ((pos + 1) & 0xFFFFFFFF)) & M) ^ ((0xD1B54A32D192ED03 * ((seq + 1) & 0xFFFFFFFF)) & M)
+    z = (z + 0x9E3779B97F4A7C15) & M
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+    z ^= z >> 31
+    return (z >> 11) * (1.0 / 9007199254740992.0)
+
+
 class LayerDesc(C.Structure):
     _fields_ = [("is_attn", C.c_int32), ("is_moe", C.c_int32), ("t", C.c_void_p * SLOT_COUNT)]
 
@@ -103,6 +134,11 @@ _SIGS = {
     "qq_model_stat": (_I, [_P, _I, C.POINTER(_I64)]),
     "qq_bench_kernel": (_I, [_P, _I, _I, C.POINTER(C.c_float)]),
     "qq_moe_block_noalloc": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
+    "qq_forward_sample": (_I, [_P, C.c_int32, _I, _I, C.POINTER(SampleParams), _I, C.POINTER(C.c_int32)]),
+    "qq_generate_sample": (_I, [_P, _I, C.POINTER(C.c_int32), _I, _I, C.POINTER(SampleParams), _I,
+                                C.POINTER(C.c_int32), C.POINTER(_I)]),
+    "qq_sample_logits": (_I, [_P, _P, _I, C.POINTER(SampleParams), C.c_double, _I, C.POINTER(C.c_int32)]),
+    "qq_sample_uniform": (_I, [C.c_uint64, _I, _I, C.POINTER(C.c_double)]),
     "qq_moe_route": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P, _P]),
     "qq_moe_experts": (_I, [_P, C.POINTER(LayerDesc), _I, _P, _P, _I, _P]),
     "qq_moe_combine": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
@@ -247,6 +283,12 @@ class Context:
         check(self.lib.qq_moe_block_noalloc(self.h, C.byref(layer), n_expert, top_k, _ptr(x_dev), T, _ptr(out_dev),
                                             _ptr(routing_dev)))
 
+    def sample_logits(self, logits_dev, n: int, params: SampleParams, r: float, think_done: bool = False) -> int:
+        """sampleWithThinkControl on device logits with the uniform draw r (qq_sample_logits)."""
+        tok = C.c_int32(-1)
+        check(self.lib.qq_sample_logits(self.h, _ptr(logits_dev), n, C.byref(params), float(r),
+                                        1 if think_done else 0, C.byref(tok)))
+        return tok.value
 
     # expert-parallel pieces of the MoE block (device pointers; see include/qq3.h)
     def moe_route(self, layer: LayerDesc, n_expert: int, top_k: int, x_dev, T: int, idx_dev, w_dev,
@@ -369,6 +411,23 @@ class Model:
         check(self.ctx.lib.qq_generate(self.h, seq, p.ctypes.data_as(C.POINTER(C.c_int32)), len(p), max_steps,
                                        think_id, eos_id, out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(n)))
         return out[: n.value]
+
+    def generate_sample(self, prompt, max_steps: int, params: SampleParams, eos_id: int = -1,
+                        seq: int = 0) -> np.ndarray:
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))
+        out = np.empty(max(max_steps, 1), dtype=np.int32)
+        n = C.c_int(0)
+        check(self.ctx.lib.qq_generate_sample(self.h, seq, p.ctypes.data_as(C.POINTER(C.c_int32)), len(p), max_steps,
+                                              C.byref(params), eos_id, out.ctypes.data_as(C.POINTER(C.c_int32)),
+                                              C.byref(n)))
+        return out[: n.value]
+
+    def forward_sample(self, token: int, pos: int, params: SampleParams, think_done: bool = False,
+                       seq: int = 0) -> int:
+        tok = C.c_int32(-1)
+        check(self.ctx.lib.qq_forward_sample(self.h, int(token), seq, pos, C.byref(params), 1 if think_done else 0,
+                                             C.byref(tok)))
+        return tok.value
 
     def reset(self, seq: int = 0) -> None:
         check(self.ctx.lib.qq_reset(self.h, seq))

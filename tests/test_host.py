@@ -198,3 +198,19 @@ def test_gguf_reads_k_quant_and_legacy_tensors(qq3, tmp_path):
     assert G.tensor_nbytes([512, 3], 12) == 6 * 144 and G.tensor_nbytes([64], 2) == 2 * 18
     with pytest.raises(ValueError):
         G.tensor_nbytes([32], 15)
+
+
+def test_sample_uniform_twin_matches_library(qq3):
+    """The device sampler's draws (qq_sample_uniform, a host function of the library) and their
+    Python twin agree bit for bit, so a host can reproduce every Math.random() replacement."""
+    import ctypes as C
+
+    lib = qq3.runtime.load()
+    rng = np.random.default_rng(3)
+    for _ in range(200):
+        seed = int(rng.integers(0, 2 ** 63)) * 2 + int(rng.integers(0, 2))
+        seq, pos = int(rng.integers(0, 64)), int(rng.integers(0, 1 << 20))
+        r = C.c_double(-1.0)
+        qq3.runtime.check(lib.qq_sample_uniform(C.c_uint64(seed), seq, pos, C.byref(r)))
+        assert r.value == qq3.runtime.sample_uniform(seed, seq, pos)
+        assert 0.0 <= r.value < 1.0
