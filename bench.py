@@ -165,7 +165,10 @@ def run_ours(args, ws, rank, local):
     g = qq3.synth.MemoryGGUF(spec, tensors)
     max_ctx = args.prompt + args.warmup + 2 * args.steps + 16
     # sequence 1 only serves the clock-sampling soak, so sequence 0's state stays the true continuation
+    t_up = time.time()
     eng = qq3.Lfm2CudaEngine(g, device=local, max_ctx=max_ctx, n_seq=2)
+    torch.cuda.synchronize()
+    upload_s = time.time() - t_up
     stream = torch.cuda.Stream(device=local)
     eng.ctx.set_stream(stream.cuda_stream)
     prompt = qq3.synth.uniform_tokens(args.prompt, SEED + rank, spec.n_vocab)
@@ -267,7 +270,9 @@ def run_ours(args, ws, rank, local):
         "clocks": clk.summary(),
         "prefill": {"tokens": args.prompt - 1, "ms": round(prefill_s * 1e3, 2),
                     "tok_s": round((args.prompt - 1) / prefill_s, 1), "note": "untimed setup, host wall clock"},
-        "setup_s": {"weight_generation": round(gen_s, 1)},
+        "setup_s": {"weight_generation": round(gen_s, 1), "engine_create": round(upload_s, 2),
+                    "weight_upload_gbs": round(eng.uploadBytes / upload_s / 1e9, 2),
+                    "note": "engine_create = streamed upload of the raw GGUF bytes (pinned ring) + model binding"},
     }
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_decode(g, spec, qq3.synth.uniform_tokens(args.prompt, SEED, spec.n_vocab),

@@ -68,6 +68,19 @@ int qq_synchronize(qq_ctx* ctx);
 int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type, const int64_t* ne, int n_dims,
                      qq_tensor** out);
 int qq_free_tensor(qq_tensor* t);
+/* Streaming upload of a whole model (GGUFReader.fromFile's per-tensor slices, gguf.js:350-374,
+ * each uploaded raw as GPUDevice.uploadBuffer does, webgpu.js:370-383, 569-624): the bytes go
+ * through a ring of pinned staging slots (staging_bytes in all; 0 = 128 MiB) so that the host
+ * copy of one chunk, the DMA of the previous one and the device-side Q8_0 split of the one
+ * before overlap.  qq_upload_tensor_async returns once the caller's bytes are copied (the caller
+ * keeps ownership, as with qq_upload_tensor); the tensors it creates may be used after
+ * qq_upload_finish, which waits for the device work, frees the ring and the uploader (also on
+ * failure) and reports the bytes uploaded. */
+typedef struct qq_uploader qq_uploader;
+int qq_upload_begin(qq_ctx* ctx, size_t staging_bytes, qq_uploader** out);
+int qq_upload_tensor_async(qq_uploader* u, const void* host, size_t nbytes, int ggml_type, const int64_t* ne,
+                           int n_dims, qq_tensor** out);
+int qq_upload_finish(qq_uploader* u, size_t* bytes_out);
 /* Shape/type of an uploaded tensor (the meta.shape / meta.type fields, gguf.js:235-254). */
 int qq_tensor_info(const qq_tensor* t, int* ggml_type, int64_t* ne4, int* n_dims);
 /* out_dev[i] = element i in storage order, dequantised as q*d (bit-exact; the column

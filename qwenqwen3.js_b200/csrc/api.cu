@@ -246,8 +246,11 @@ void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool d
             int* idx = m->ridx + (size_t)L.moe_slot * k;
             float* w = m->rw + (size_t)L.moe_slot * k;
             const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
-            if (!(qq3::stream_path() && qq3::launch2_router(*L.t[QQ_ROUTER], bias, sf, d.n_expert, k, m->rlogits,
-                                                            m->rcounter, rec, idx, w, s)))
+            if (d.arch == QQ_ARCH_QWEN3)
+                qq3::launch_router(*L.t[QQ_ROUTER], nullptr, m->hidden, 1, sf.norm_w, sf.eps, d.n_expert, k, true, rec,
+                                   idx, w, s);
+            else if (!(qq3::stream_path() && qq3::launch2_router(*L.t[QQ_ROUTER], bias, sf, d.n_expert, k, m->rlogits,
+                                                                 m->rcounter, rec, idx, w, s)))
                 qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, m->hidden, 1, sf.norm_w, sf.eps, d.n_expert, k, rec,
                                         idx, w, s);
             qq3::launch_moe_gateup(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], idx, m->mask, k, sf, m->h, s);
@@ -634,7 +637,9 @@ bool mega_enabled(qq_model* m) {
     if (m->mega < 0) {
         // the persistent step is the default; QQ3_PERSISTENT=0 selects the per-phase kernels
         const char* env = getenv("QQ3_PERSISTENT");
-        bool ok = !(env && atoi(env) == 0) && qq3::stream_path();
+        // the persistent step's fused FFN phase routes with the LFM2 rule only: a softmax-routed
+        // (Qwen3-MoE) model takes the per-phase kernels
+        bool ok = !(env && atoi(env) == 0) && qq3::stream_path() && !(m->d.arch == QQ_ARCH_QWEN3 && m->n_moe > 0);
         if (ok) {
             std::vector<qq3::PhaseDesc> prog;
             try {
@@ -941,7 +946,8 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
         if (L.moe) {
             const int k = d.n_expert_used;
             const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
-            qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, b.xn, T, nullptr, 0.f, d.n_expert, k, b.rec, b.idx, b.w, s);
+            qq3::launch_router(*L.t[QQ_ROUTER], bias, b.xn, T, nullptr, 0.f, d.n_expert, k, d.arch == QQ_ARCH_QWEN3,
+                               b.rec, b.idx, b.w, s);
             // the layer's routing record / ids / weights: those of the last token
             QQ_CUDA_TRY(cudaMemcpyAsync(m->rec + (size_t)L.moe_slot * m->rec_len, b.rec + (size_t)(T - 1) * m->rec_len,
                                         sizeof(float) * m->rec_len, cudaMemcpyDeviceToDevice, s));
@@ -1010,7 +1016,8 @@ void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
         if (L.moe) {
             const int k = d.n_expert_used;
             const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
-            qq3::launch_lfm2_router(*L.t[QQ_ROUTER], bias, b.xn, T, nullptr, 0.f, d.n_expert, k, b.rec, b.idx, b.w, s);
+            qq3::launch_router(*L.t[QQ_ROUTER], bias, b.xn, T, nullptr, 0.f, d.n_expert, k, d.arch == QQ_ARCH_QWEN3,
+                               b.rec, b.idx, b.w, s);
             QQ_CUDA_TRY(cudaMemcpyAsync(m->rec + (size_t)L.moe_slot * m->rec_len, b.rec + (size_t)(T - 1) * m->rec_len,
                                         sizeof(float) * m->rec_len, cudaMemcpyDeviceToDevice, s));
             QQ_CUDA_TRY(cudaMemcpyAsync(m->ridx + (size_t)L.moe_slot * k, b.idx + (size_t)(T - 1) * k,
@@ -1420,13 +1427,19 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                     check_shape(L.t[QQ_OUT_PROJ], QQ_TYPE_Q8_0, E, E, 1, (b + "shortconv.out_proj.weight").c_str());
                 }
                 if (L.moe) {
-                    QQ_CHECK(d.arch == QQ_ARCH_LFM2, QQ_ERR_UNSUPPORTED,
-                             "qq_model_create: Qwen3-MoE softmax routing is not in this build");
-                    QQ_CHECK(d.n_expert_used == 4 && d.n_expert <= 32, QQ_ERR_UNSUPPORTED,
-                             "qq_model_create: MoE layers need top-4 of <= 32 experts in this build");
+                    if (d.arch == QQ_ARCH_LFM2)
+                        QQ_CHECK(d.n_expert_used == 4 && d.n_expert <= 32, QQ_ERR_UNSUPPORTED,
+                                 "qq_model_create: LFM2 MoE layers need top-4 of <= 32 experts in this build");
+                    else  // Qwen3-MoE: softmax router (qwen3-engine.js:304-363)
+                        QQ_CHECK(d.n_expert_used >= 1 && d.n_expert_used <= 8 && d.n_expert <= 128 &&
+                                     d.n_expert_used <= d.n_expert,
+                                 QQ_ERR_UNSUPPORTED,
+                                 "qq_model_create: Qwen3-MoE layers need top-k <= 8 of <= 128 experts in this build");
                     L.moe_slot = m->n_moe++;
                     const int64_t F = L.t[QQ_GATE_EXPS] ? L.t[QQ_GATE_EXPS]->ne[1] : 0;
-                    check_shape(L.t[QQ_ROUTER], QQ_TYPE_Q8_0, E, d.n_expert, 1, (b + "ffn_gate_inp.weight").c_str());
+                    const int rtype = (d.arch == QQ_ARCH_QWEN3 && L.t[QQ_ROUTER] && L.t[QQ_ROUTER]->type == QQ_TYPE_F32)
+                                          ? QQ_TYPE_F32 : QQ_TYPE_Q8_0;
+                    check_shape(L.t[QQ_ROUTER], rtype, E, d.n_expert, 1, (b + "ffn_gate_inp.weight").c_str());
                     check_shape(L.t[QQ_GATE_EXPS], QQ_TYPE_Q8_0, E, F, d.n_expert, (b + "ffn_gate_exps.weight").c_str());
                     check_shape(L.t[QQ_UP_EXPS], QQ_TYPE_Q8_0, E, F, d.n_expert, (b + "ffn_up_exps.weight").c_str());
                     check_shape(L.t[QQ_DOWN_EXPS], QQ_TYPE_Q8_0, F, E, d.n_expert, (b + "ffn_down_exps.weight").c_str());

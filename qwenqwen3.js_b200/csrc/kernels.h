@@ -73,6 +73,10 @@ int attention_splits(int max_ctx);
 // record[t] = [ids | normalised weights | sigmoid probs] (2k+E floats), idx[t][k], w[t][k].
 void launch_lfm2_router(const DTensor& router, const float* bias, const float* x, int T, const float* norm_w,
                         float eps, int n_expert, int top_k, float* record, int* idx, float* w, cudaStream_t s);
+// The router of either family for T rows: softmax = true is the Qwen3-MoE rule
+// (qwen3-engine.js:304-321), false the LFM2 rule above.  <= 128 experts, top_k <= 8, Q8_0 or F32 rows.
+void launch_router(const DTensor& router, const float* bias, const float* x, int T, const float* norm_w, float eps,
+                   int n_expert, int top_k, bool softmax, float* record, int* idx, float* w, cudaStream_t s);
 
 int num_sms();
 

@@ -123,19 +123,21 @@ struct MapExpertPair {  // item = k*N + j: gate/up row j of expert idx[k]
 };
 
 template <int S>
-struct MapExpertDown {  // item j: row j of expert idx[s] for every slot s, input h[s]
+struct MapExpertDown {  // item j: row j of expert idx[s] for every slot s < top_k, input h[s]
     const int8_t* qs; const __half* d;
     const int* idx; const uint32_t* mask;
     int64_t K; int N;
+    int top_k = S;  // slots past top_k (a top_k below S) are off
     __device__ void get(int item, Rows<S>& r) const {
 #pragma unroll
         for (int s = 0; s < S; s++) {
-            const int e = idx[s];
+            const bool live = s < top_k;
+            const int e = live ? idx[s] : 0;
             const int64_t row = (int64_t)e * N + item;
             r.q[s] = qs + row * K;
             r.d[s] = d + row * (K >> 5);
-            r.xsel[s] = s;
-            r.on[s] = !masked(mask, e);
+            r.xsel[s] = live ? s : 0;
+            r.on[s] = live && !masked(mask, e);
         }
     }
 };
@@ -346,15 +348,20 @@ void launch_moe_gateup(const DTensor& gate_exps, const DTensor& up_exps, const i
 void launch_moe_down_combine(const DTensor& down_exps, const int* idx, const float* w, const uint32_t* mask,
                              int top_k, const float* h, float* hidden, cudaStream_t s) {
     check_q8(down_exps);
-    QQ_CHECK(top_k == 4, -4, "MoE down-combine is built for top_k = 4");
-    if (g_stream_path && launch2_moe_down_combine(down_exps, idx, w, mask, top_k, h, hidden, s)) return;
+    QQ_CHECK(top_k >= 1 && top_k <= 8, -4, "MoE down-combine: top_k must be 1..8");
+    if (top_k == 4 && g_stream_path && launch2_moe_down_combine(down_exps, idx, w, mask, top_k, h, hidden, s)) return;
     const int K = (int)down_exps.K, N = (int)down_exps.ne[1];
     XStage st;
     st.nvec = top_k;
     st.K = K;
     for (int k = 0; k < top_k; k++) st.x[k] = h + (size_t)k * K;
-    MapExpertDown<4> m{down_exps.qs, down_exps.d, idx, mask, K, N};
-    launch<4>(st, m, EpiMoECombine<4>{w, hidden}, N, s);
+    if (top_k == 4) {
+        MapExpertDown<4> m{down_exps.qs, down_exps.d, idx, mask, K, N};
+        launch<4>(st, m, EpiMoECombine<4>{w, hidden}, N, s);
+    } else {  // any other top_k (Qwen3-MoE routes 8): up to 8 slots, the unused ones off
+        MapExpertDown<8> m{down_exps.qs, down_exps.d, idx, mask, K, N, top_k};
+        launch<8>(st, m, EpiMoECombine<8>{w, hidden}, N, s);
+    }
 }
 
 }  // namespace qq3

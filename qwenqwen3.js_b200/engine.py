@@ -94,6 +94,8 @@ class _CudaEngine:
         self.eosTokenId = int(gguf.getKeyValue("tokenizer.ggml.eos_token_id", -1))
         self.stopTokenIds: set = set()
         self._tensors: dict = {}
+        self._uploader = None
+        self.uploadBytes = 0
         self._build()
         self.bufLogits = np.zeros(self.nVocab, dtype=np.float32)
 
@@ -108,10 +110,22 @@ class _CudaEngine:
         if meta is None:
             return None
         if name not in self._tensors:
-            self._tensors[name] = self.ctx.upload(meta.raw(), meta.type, meta.shape)
+            up = self._uploader
+            self._tensors[name] = (up.upload if up is not None else self.ctx.upload)(meta.raw(), meta.type, meta.shape)
         return self._tensors[name]
 
     def _build(self):
+        """Upload every tensor the engine reads (streamed through a pinned ring: the host copy, the
+        DMA and the device-side Q8_0 split of consecutive chunks overlap), then bind the model."""
+        self._uploader = self.ctx.streaming_upload()
+        try:
+            self._bind()
+        finally:
+            if self._uploader is not None:  # an upload failed part-way
+                up, self._uploader = self._uploader, None
+                up.finish()
+
+    def _bind(self):
         layers = (rt.LayerDesc * self.nLayers)()
         for i in range(self.nLayers):
             L = layers[i]
@@ -139,6 +153,8 @@ class _CudaEngine:
         out = self._upload("output.weight")
         d.output = out.h.value if out is not None else None
         d.layers = C.cast(layers, C.POINTER(rt.LayerDesc))
+        up, self._uploader = self._uploader, None
+        self.uploadBytes = up.finish() if up is not None else 0  # tensors are ready from here on
         self.model = rt.Model(self.ctx, d, layers, list(self._tensors.values()))
 
     # --- reference API
@@ -299,18 +315,22 @@ class Qwen3CudaEngine(_CudaEngine):
         self.nVocab = int(gguf.getTensorMetaByName("token_embd.weight").shape[1])
         self.nQ = int(gguf.getTensorMetaByName("blk.0.attn_q.weight").shape[1])
         self.headDim = self.nQ // self.nHeads
-        self.nExperts = 0
-        self.nExpertsUsed = 0
-        if any(gguf.getTensorMetaByName(f"blk.{i}.ffn_gate_inp.weight") is not None for i in range(self.nLayers)):
-            # Qwen3-MoE routes by softmax (qwen3-engine.js:304-362); the device MoE path is the LFM2
-            # sigmoid router, so such a model is refused rather than routed wrongly
-            raise NotImplementedError("Qwen3-MoE (softmax-routed experts) is not supported on the GPU yet")
+        self._moe = [gguf.getTensorMetaByName(f"blk.{i}.ffn_gate_inp.weight") is not None
+                     for i in range(self.nLayers)]
+        if any(self._moe):
+            # Qwen3-MoE (qwen3-engine.js:37-41): softmax-routed experts, counts from the metadata
+            arch = gguf.getKeyValue("general.architecture", "qwen3")
+            self.nExperts = int(_num(gguf.getKeyValue(f"{arch}.expert_count"), 128))
+            self.nExpertsUsed = int(_num(gguf.getKeyValue(f"{arch}.expert_used_count"), 8))
+        else:
+            self.nExperts = 0
+            self.nExpertsUsed = 0
 
     def _is_attn(self, i):
         return True
 
     def _is_moe(self, i):
-        return False
+        return self._moe[i]
 
 
 class Lfm2CudaEngine(_CudaEngine):

@@ -134,6 +134,9 @@ _SIGS = {
     "qq_model_stat": (_I, [_P, _I, C.POINTER(_I64)]),
     "qq_bench_kernel": (_I, [_P, _I, _I, C.POINTER(C.c_float)]),
     "qq_moe_block_noalloc": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
+    "qq_upload_begin": (_I, [_P, C.c_size_t, C.POINTER(_P)]),
+    "qq_upload_tensor_async": (_I, [_P, _P, C.c_size_t, _I, C.POINTER(_I64), _I, C.POINTER(_P)]),
+    "qq_upload_finish": (_I, [_P, C.POINTER(C.c_size_t)]),
     "qq_forward_sample": (_I, [_P, C.c_int32, _I, _I, C.POINTER(SampleParams), _I, C.POINTER(C.c_int32)]),
     "qq_generate_sample": (_I, [_P, _I, C.POINTER(C.c_int32), _I, _I, C.POINTER(SampleParams), _I,
                                 C.POINTER(C.c_int32), C.POINTER(_I)]),
@@ -248,6 +251,11 @@ class Context:
         check(self.lib.qq_upload_tensor(self.h, raw.ctypes.data, raw.nbytes, ggml_type, arr, len(ne), C.byref(h)))
         return Tensor(self, h, ggml_type, ne)
 
+    def streaming_upload(self, staging_bytes: int = 0) -> "Uploader":
+        """Upload many tensors through a pinned staging ring (qq_upload_begin .. qq_upload_finish);
+        use as a context manager, the tensors are ready when it exits."""
+        return Uploader(self, staging_bytes)
+
     def q8_matmul(self, W: "Tensor", x_dev, M: int, y_dev) -> None:
         check(self.lib.qq_q8_matmul(self.h, W.h, _ptr(x_dev), M, _ptr(y_dev)))
 
@@ -337,6 +345,39 @@ class Tensor:
                 self.free()
         except Exception:
             pass
+
+
+class Uploader:
+    """qq_uploader: streaming upload of many tensors (see Context.streaming_upload)."""
+
+    def __init__(self, ctx: "Context", staging_bytes: int = 0):
+        self.ctx = ctx
+        self.h = C.c_void_p()
+        self.bytes = 0
+        check(ctx.lib.qq_upload_begin(ctx.h, staging_bytes, C.byref(self.h)))
+
+    def upload(self, raw: np.ndarray, ggml_type: int, ne) -> "Tensor":
+        raw = np.ascontiguousarray(raw)
+        ne = list(int(v) for v in ne)
+        arr = (C.c_int64 * len(ne))(*ne)
+        h = C.c_void_p()
+        check(self.ctx.lib.qq_upload_tensor_async(self.h, raw.ctypes.data, raw.nbytes, ggml_type, arr, len(ne),
+                                                  C.byref(h)))
+        return Tensor(self.ctx, h, ggml_type, ne)
+
+    def finish(self) -> int:
+        if self.h:
+            n = C.c_size_t(0)
+            h, self.h = self.h, C.c_void_p()
+            check(self.ctx.lib.qq_upload_finish(h, C.byref(n)))
+            self.bytes = n.value
+        return self.bytes
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.finish()
 
 
 class Model:

@@ -105,6 +105,7 @@ class ModelSpec:
     n_dense_lead: int = 0
     seed: int = 1234
     zipf_s: float = 1.1
+    router_f32: bool = False  # Qwen3-MoE GGUFs store the router as F32
     name: str = ""
     extra: dict = field(default_factory=dict)
 
@@ -139,6 +140,12 @@ def tiny_qwen3(seed: int = 7) -> ModelSpec:
     return ModelSpec("qwen3", 3, 256, 4, 2, 128, 1024, 512, 1e6, 1e-6, seed=seed, name="tiny-qwen3")
 
 
+def tiny_qwen3moe(seed: int = 7, router_f32: bool = False) -> ModelSpec:
+    """A small Qwen3-MoE (softmax-routed): 128 experts, top-8, as Qwen3-30B-A3B routes."""
+    return ModelSpec("qwen3moe", 3, 256, 4, 2, 64, 1024, 512, 1e6, 1e-6, n_expert=128, n_expert_used=8, n_ff_exp=64,
+                     router_f32=router_f32, seed=seed, name="tiny-qwen3moe")
+
+
 def tiny_lfm2(seed: int = 7, n_layers: int = 6) -> ModelSpec:
     return ModelSpec("lfm2moe", n_layers, 256, 4, 2, 64, 768, 512, 1e6, 1e-5, context_length=128000,
                      attn_layers=(2, 5), n_expert=8, n_expert_used=4, n_ff_exp=128, n_dense_lead=2, seed=seed,
@@ -169,7 +176,7 @@ def tensor_specs(spec: ModelSpec) -> list[tuple[str, int, list]]:
                     (b + "shortconv.out_proj.weight", TYPE_Q8_0, [E, E])]
         if spec.is_moe(i):
             F, NE = spec.n_ff_exp, spec.n_expert
-            out += [(b + "ffn_gate_inp.weight", TYPE_Q8_0, [E, NE]),
+            out += [(b + "ffn_gate_inp.weight", TYPE_F32 if spec.router_f32 else TYPE_Q8_0, [E, NE]),
                     (b + "ffn_gate_exps.weight", TYPE_Q8_0, [E, F, NE]),
                     (b + "ffn_up_exps.weight", TYPE_Q8_0, [E, F, NE]),
                     (b + "ffn_down_exps.weight", TYPE_Q8_0, [F, E, NE])]
@@ -220,6 +227,8 @@ def generate_tensor(spec: ModelSpec, name: str, ggml_type: int, ne, cache: dict 
         return bias.view(np.uint8)
     if ggml_type == TYPE_Q8_0:
         return q8_0_blocks(n, seed, 0)
+    if name.endswith("ffn_gate_inp.weight"):  # an F32 router
+        return normal_f32(n, seed, 0.0, 0.05).view(np.uint8)
     if "shortconv.conv" in name:
         return normal_f32(n, seed, 0.0, 0.1).view(np.uint8)
     return np.ones(n, dtype=np.float32).view(np.uint8)  # RMSNorm weights

@@ -277,3 +277,34 @@ def test_batched_prefill_vs_oracle(qq3, orc, arch):
     assert rel_err(got, want) < TOL
     assert int(np.argmax(got)) == int(np.argmax(want))
     eng.close()
+
+
+@pytest.mark.parametrize("router_f32", [False, True])
+def test_qwen3_moe_softmax_router_vs_oracle(qq3, orc, router_f32):
+    """Qwen3-MoE (qwen3-engine.js:304-363): softmax over 128 router logits, top-8, weights
+    renormalised over the selected probabilities.  Per-token logits and routing records (ids
+    identical except near-ties, weights and probabilities), then a 70-token prompt through the
+    batched prefill (grouped tensor-core experts) and greedy generate, against the oracle."""
+    spec = qq3.synth.tiny_qwen3moe(seed=71, router_f32=router_f32)
+    g, eng, ref = _pair(qq3, orc, spec, max_ctx=128)
+    k, E = spec.n_expert_used, spec.n_expert
+    toks = qq3.synth.uniform_tokens(8, 3, spec.n_vocab)
+    for p, t in enumerate(toks):
+        want, _, rec = ref.forward(int(t), p, False, routing=True)
+        got = eng.forward(int(t), p, False)
+        assert rel_err(got, want) < TOL, f"pos {p}"
+        assert int(np.argmax(got)) == int(np.argmax(want))
+        for m in range(spec.n_layers):
+            gr = eng.model.read_routing(m, 2 * k + E)
+            assert rel_err(gr[2 * k:], rec[m][2 * k:]) < 1e-5, f"pos {p} layer {m}: softmax probs"
+            if np.array_equal(gr[:k], rec[m][:k]):
+                assert rel_err(gr[k:2 * k], rec[m][k:2 * k]) < 1e-5
+            else:
+                srt = np.sort(rec[m][2 * k:])[::-1]
+                assert srt[k - 1] - srt[k] < 1e-5, f"pos {p} layer {m}: top-k {gr[:k]} vs {rec[m][:k]}"
+    eng.resetKVCache()
+    prompt = qq3.synth.uniform_tokens(70, 4, spec.n_vocab)
+    want = ref.generate(prompt, 12)
+    got = eng.model.generate(prompt, 12)
+    assert got.tolist() == want.tolist()
+    eng.close()

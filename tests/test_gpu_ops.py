@@ -31,6 +31,29 @@ def _dev(torch, a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+def test_streaming_upload_bit_exact(qq3, orc, gpu_ctx, torch):
+    """Tensors uploaded through the pinned staging ring (qq_upload_begin/_async/_finish) equal the
+    oracle's dequantisation bit for bit: a small staging ring (4 slots of 68 KB) splits the larger
+    tensors into many chunks whose boundaries fall mid-row, and F32 tensors ride along."""
+    shapes = [(8, [1024, 1792]), (8, [32, 96]), (0, [2048]), (8, [2048, 1792, 3]), (0, [3, 2048]), (8, [64, 5])]
+    raws = []
+    for i, (t, ne) in enumerate(shapes):
+        n = int(np.prod(ne))
+        raws.append(qq3.synth.q8_0_blocks(n, seed=300 + i, mode=1) if t == 8 else
+                    qq3.synth.normal_f32(n, seed=300 + i).view(np.uint8))
+    with gpu_ctx.streaming_upload(staging_bytes=4 * 68 * 1024) as up:
+        tensors = [up.upload(raw, t, ne) for (t, ne), raw in zip(shapes, raws)]
+    assert up.bytes == sum(r.nbytes for r in raws)
+    for (t, ne), raw, W in zip(shapes, raws, tensors):
+        n = int(np.prod(ne))
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        W.dequant(out)
+        gpu_ctx.synchronize()
+        want = orc.dequant(raw, 8, ne) if t == 8 else raw.view(np.float32)
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32)), ne
+        W.free()
+
+
 @pytest.mark.parametrize("N,K", SWEEP + [(1792, 2048 * 32), (96, 32)])
 def test_dequant_bit_exact(qq3, orc, gpu_ctx, torch, N, K):
     raw = qq3.synth.q8_0_blocks(N * K, seed=100 + N + K, mode=1)

@@ -97,12 +97,13 @@ def test_engine_hparams_mirror_js(qq3):
     q = object.__new__(qq3.Qwen3CudaEngine)
     q._read_hparams(g)
     assert (q.nLayers, q.nEmb, q.nHeads, q.nHeadKV, q.headDim, q.nVocab, q.maxCtx) == (28, 1024, 16, 8, 128, 151936, 4096)
-    # a Qwen3-MoE file is refused by the device engine, not routed with the LFM2 router
+    # a Qwen3-MoE file: expert counts from its metadata, MoE layers where a router exists
     spec = qq3.synth.ModelSpec("qwen3moe", 2, 64, 2, 1, 64, 96, 64, 1e6, 1e-6, n_expert=8, n_expert_used=2,
                                n_ff_exp=32)
     g = qq3.synth.MemoryGGUF(spec, {n: (t, ne, np.zeros(1, np.uint8)) for n, t, ne in qq3.synth.tensor_specs(spec)})
-    with pytest.raises(NotImplementedError):
-        object.__new__(qq3.Qwen3CudaEngine)._read_hparams(g)
+    m = object.__new__(qq3.Qwen3CudaEngine)
+    m._read_hparams(g)
+    assert (m.nExperts, m.nExpertsUsed) == (8, 2) and [m._is_moe(i) for i in range(2)] == [True, True]
 
 
 def test_host_sampling_mirrors_tensor_js(qq3):
