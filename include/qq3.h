@@ -53,6 +53,16 @@ const char* qq_last_error(void);
  * process and one context per GPU. */
 int qq_init(const int* devices, int n_devices, qq_ctx** out);
 int qq_destroy(qq_ctx* ctx);
+/* ---- multi-GPU: one NCCL communicator per context (one process per GPU) ----
+ * The expert-parallel and tensor-parallel paths enqueue their exchanges on the context stream
+ * through this communicator.  Rank 0 makes the id (qq_comm_unique_id), the host distributes it,
+ * every rank calls qq_comm_init; a rank that does not join within timeout_ms (0 = 120 s) turns
+ * into QQ_ERR_CUDA on the others and an aborted communicator, not a hang.  No reference
+ * counterpart: the reference runs on one device. */
+#define QQ_COMM_ID_BYTES 128
+int qq_comm_unique_id(void* id_out);
+int qq_comm_init(qq_ctx* ctx, const void* id, int rank, int world, int timeout_ms);
+int qq_comm_destroy(qq_ctx* ctx);
 /* Make subsequent work of this context run on a caller-owned cudaStream_t (NULL = the
  * context's own stream). */
 int qq_set_stream(qq_ctx* ctx, void* cuda_stream);
@@ -171,6 +181,13 @@ typedef struct qq_model_desc {
     qq_tensor* output_norm; /* output_norm.weight (Qwen3) / token_embd_norm.weight (LFM2) */
     qq_tensor* output;      /* output.weight, or NULL for tied embeddings */
     const qq_layer_desc* layers;
+    /* Expert parallelism (no reference counterpart): > 1 splits the experts of every MoE layer
+     * evenly over ep_world ranks -- this rank (its context's communicator rank, qq_comm_init with
+     * world ep_world) holds experts [rank E/ep_world, (rank+1) E/ep_world), so the expert tensors
+     * have ne[2] = E/ep_world -- and every MoE layer exchanges token rows with the other ranks.
+     * Every rank then makes the same forward calls with the same token counts (the calls are
+     * collective).  0 or 1: one rank holds every expert. */
+    int32_t ep_world;
 } qq_model_desc;
 
 /* Bind uploaded tensors into an engine.  Replaces Qwen3GPUEngine.create /

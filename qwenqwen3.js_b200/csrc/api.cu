@@ -19,6 +19,7 @@
 #include <numeric>
 
 #include "api_internal.h"
+#include "comm.h"
 #include "decode_prog.h"
 
 namespace qq3 {
@@ -145,6 +146,12 @@ struct qq_model {
     uint32_t* spk = nullptr;
     int* sout = nullptr;
     qq3::SampleArgs* h_sargs = nullptr;
+    // expert parallelism: this rank's share of the experts, and the exchange buffers (grow-only,
+    // for ep_cap rows per destination rank)
+    int ep_world = 1, ep_rank = 0, n_expert_local = 0;
+    int ep_cap = 0;
+    void* ep_arena = nullptr;
+    float* ep_xn = nullptr;  // the normalised FFN input of a decode step [n_embd]
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
@@ -169,6 +176,8 @@ void free_model(qq_model* m) {
     if (m->bt_keys) cudaFree(m->bt_keys);
     if (m->h_bt) cudaFreeHost(m->h_bt);
     if (m->tarena) cudaFree(m->tarena);
+    if (m->ep_arena) cudaFree(m->ep_arena);
+    if (m->ep_xn) cudaFree(m->ep_xn);
     if (m->aarena) cudaFree(m->aarena);
     for (Layer& L : m->layers) {
         for (void* q : {(void*)L.dt_qs, (void*)L.dt_d, (void*)L.ot_qs, (void*)L.ot_d})
@@ -188,6 +197,97 @@ void free_model(qq_model* m) {
     if (m->h_small) cudaFreeHost(m->h_small);
     if (m->h_sargs) cudaFreeHost(m->h_sargs);
     if (m->cap) cudaStreamDestroy(m->cap);
+}
+
+// ---- expert-parallel MoE -------------------------------------------------------------------
+// The MoE of layer L for T rows xn (normalised FFN inputs) routed to idx / w (global expert ids,
+// T x top_k), with this rank holding n_expert_local experts: plan + gather the rows per owner
+// rank (kernels_ep.cu), NCCL exchange, the grouped expert GEMMs over the rows received (each
+// owner's weighted partial sum of the slots it serves), NCCL exchange back, and
+// hidden[t] += the partial sums in rank order.  Collective: every rank calls it with the same T.
+struct EpBufs {
+    int *pos, *tok_of, *sids, *rids;
+    float *swts, *rwts, *sx, *rx, *y, *back;
+    void* moe;
+};
+
+EpBufs ep_bufs(qq_model* m, int C) {
+    const qq_model_desc& d = m->d;
+    const size_t W = m->ep_world, E = d.n_embd, k = d.n_expert_used;
+    size_t F = 0;
+    for (const Layer& L : m->layers)
+        if (L.moe) F = std::max<size_t>(F, L.t[QQ_GATE_EXPS]->ne[1]);
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    auto sizes = [&](size_t c) {
+        return std::vector<size_t>{al(W * c * 4),     al(W * c * 4),      al(W * c * k * 4), al(W * c * k * 4),
+                                   al(W * c * k * 4), al(W * c * k * 4), al(W * c * E * 4), al(W * c * E * 4),
+                                   al(W * c * E * 4), al(W * c * E * 4),
+                                   al(qq3::moe_grouped_scratch_bytes((int)(W * c), (int)k, m->n_expert_local, E, F))};
+    };
+    if (C > m->ep_cap) {
+        if (m->ep_arena) {
+            QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+            cudaFree(m->ep_arena);
+            m->ep_arena = nullptr;
+            m->ep_cap = 0;
+        }
+        size_t total = 0;
+        for (size_t v : sizes(C)) total += v;
+        m->ep_arena = dmalloc(total);
+        m->ep_cap = C;
+    }
+    const std::vector<size_t> sz = sizes(m->ep_cap);
+    char* b = static_cast<char*>(m->ep_arena);
+    size_t i = 0;
+    auto take = [&]() {
+        char* r = b;
+        b += sz[i++];
+        return r;
+    };
+    EpBufs e;
+    e.pos = reinterpret_cast<int*>(take());
+    e.tok_of = reinterpret_cast<int*>(take());
+    e.sids = reinterpret_cast<int*>(take());
+    e.rids = reinterpret_cast<int*>(take());
+    e.swts = reinterpret_cast<float*>(take());
+    e.rwts = reinterpret_cast<float*>(take());
+    e.sx = reinterpret_cast<float*>(take());
+    e.rx = reinterpret_cast<float*>(take());
+    e.y = reinterpret_cast<float*>(take());
+    e.back = reinterpret_cast<float*>(take());
+    e.moe = take();
+    return e;
+}
+
+void ep_moe(qq_model* m, const Layer& L, const float* xn, int T, const int* idx, const float* w, float* hidden,
+            cudaStream_t s) {
+    const qq_model_desc& d = m->d;
+    const int W = m->ep_world, E = d.n_embd, k = d.n_expert_used, C = T;
+    qq_ctx* c = m->ctx;
+    EpBufs b = ep_bufs(m, C);
+    qq3::launch_ep_plan(idx, w, m->mask, T, k, d.n_expert, W, C, b.pos, b.tok_of, b.sids, b.swts, s);
+    qq3::launch_ep_gather(xn, b.tok_of, W, C, E, b.sx, s);
+    const size_t rowb = (size_t)C * E * 4, slotb = (size_t)C * k * 4;
+    qq3::comm_group_start();
+    for (int r = 0; r < W; r++) {
+        qq3::comm_send(c, b.sx + (size_t)r * C * E, rowb, r, s);
+        qq3::comm_send(c, b.sids + (size_t)r * C * k, slotb, r, s);
+        qq3::comm_send(c, b.swts + (size_t)r * C * k, slotb, r, s);
+        qq3::comm_recv(c, b.rx + (size_t)r * C * E, rowb, r, s);
+        qq3::comm_recv(c, b.rids + (size_t)r * C * k, slotb, r, s);
+        qq3::comm_recv(c, b.rwts + (size_t)r * C * k, slotb, r, s);
+    }
+    qq3::comm_group_end(c);
+    // the owner side: weighted partial sums of the slots this rank serves, row by received row
+    qq3::launch_moe_grouped(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], *L.t[QQ_DOWN_EXPS], b.rids, b.rwts, nullptr, b.rx,
+                            W * C, k, m->n_expert_local, b.moe, b.y, s);
+    qq3::comm_group_start();
+    for (int r = 0; r < W; r++) {
+        qq3::comm_send(c, b.y + (size_t)r * C * E, rowb, r, s);
+        qq3::comm_recv(c, b.back + (size_t)r * C * E, rowb, r, s);
+    }
+    qq3::comm_group_end(c);
+    qq3::launch_ep_combine(b.back, b.pos, W, T, C, E, hidden, s);
 }
 
 // One decode step for sequence `seq` (token/position in m->ctl), as the fixed kernel
@@ -240,7 +340,17 @@ void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool d
         sf.K = E;
         sf.norm_w = L.t[QQ_FFN_NORM]->f32;
         sf.eps = d.rms_eps;
-        if (L.moe) {
+        if (L.moe && m->ep_world > 1) {
+            const int k = d.n_expert_used;
+            float* rec = m->rec + (size_t)L.moe_slot * m->rec_len;
+            int* idx = m->ridx + (size_t)L.moe_slot * k;
+            float* w = m->rw + (size_t)L.moe_slot * k;
+            const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
+            qq3::launch_rmsnorm(m->hidden, 1, E, sf.norm_w, sf.eps, m->ep_xn, s);
+            qq3::launch_router(*L.t[QQ_ROUTER], bias, m->ep_xn, 1, nullptr, 0.f, d.n_expert, k, d.arch == QQ_ARCH_QWEN3,
+                               rec, idx, w, s);
+            ep_moe(m, L, m->ep_xn, 1, idx, w, m->hidden, s);
+        } else if (L.moe) {
             const int k = d.n_expert_used;
             float* rec = m->rec + (size_t)L.moe_slot * m->rec_len;
             int* idx = m->ridx + (size_t)L.moe_slot * k;
@@ -639,7 +749,8 @@ bool mega_enabled(qq_model* m) {
         const char* env = getenv("QQ3_PERSISTENT");
         // the persistent step's fused FFN phase routes with the LFM2 rule only: a softmax-routed
         // (Qwen3-MoE) model takes the per-phase kernels
-        bool ok = !(env && atoi(env) == 0) && qq3::stream_path() && !(m->d.arch == QQ_ARCH_QWEN3 && m->n_moe > 0);
+        bool ok = !(env && atoi(env) == 0) && qq3::stream_path() && !(m->d.arch == QQ_ARCH_QWEN3 && m->n_moe > 0) &&
+                  m->ep_world <= 1;  // expert-parallel steps exchange rows between ranks: per-phase kernels
         if (ok) {
             std::vector<qq3::PhaseDesc> prog;
             try {
@@ -706,6 +817,13 @@ cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
     if (mega) m->step_kernels = 1;
     m->graphs[key] = ge;
     return ge;
+}
+
+// One decode step of sequence seq on stream s: its captured graph, or, for an expert-parallel
+// model (whose NCCL exchanges the host enqueues between the kernels), the kernel sequence itself.
+void launch_step(qq_model* m, int seq, bool want_logits, cudaStream_t s) {
+    if (m->ep_world > 1) enqueue_step(m, seq, want_logits, s, false);
+    else QQ_CUDA_TRY(cudaGraphLaunch(get_graph(m, seq, want_logits), s));
 }
 
 void ensure_h_ctl(qq_model* m, size_t n) {
@@ -955,6 +1073,10 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
                                         sizeof(int) * k, cudaMemcpyDeviceToDevice, s));
             QQ_CUDA_TRY(cudaMemcpyAsync(m->rw + (size_t)L.moe_slot * k, b.w + (size_t)(T - 1) * k, sizeof(float) * k,
                                         cudaMemcpyDeviceToDevice, s));
+            if (m->ep_world > 1) {
+                ep_moe(m, L, b.xn, T, b.idx, b.w, b.hidden, s);  // adds the MoE output to the rows
+                continue;
+            }
             qq3::launch_moe_grouped(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], *L.t[QQ_DOWN_EXPS], b.idx, b.w, m->mask,
                                     b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
         } else {
@@ -1024,6 +1146,10 @@ void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
                                         sizeof(int) * k, cudaMemcpyDeviceToDevice, s));
             QQ_CUDA_TRY(cudaMemcpyAsync(m->rw + (size_t)L.moe_slot * k, b.w + (size_t)(T - 1) * k, sizeof(float) * k,
                                         cudaMemcpyDeviceToDevice, s));
+            if (m->ep_world > 1) {
+                ep_moe(m, L, b.xn, T, b.idx, b.w, b.hidden, s);  // adds the MoE output to the rows
+                continue;
+            }
             qq3::launch_moe_grouped(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], *L.t[QQ_DOWN_EXPS], b.idx, b.w, m->mask,
                                     b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
         } else {
@@ -1104,9 +1230,8 @@ void run_tokens(qq_model* m, const int32_t* token_ids, int n, int seq, int pos0,
     }
     for (int i = 0; i < n; i++) {
         const bool logits = want_logits && i == n - 1;
-        cudaGraphExec_t g = get_graph(m, seq, logits);
         QQ_CUDA_TRY(cudaMemcpyAsync(m->ctl, m->h_ctl + 2 * i, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-        QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+        launch_step(m, seq, logits, s);
     }
 }
 
@@ -1152,6 +1277,7 @@ int qq_destroy(qq_ctx* ctx) {
         DeviceGuard dg(ctx->device);
         cudaStreamSynchronize(ctx->stream);
         if (ctx->scratch) cudaFree(ctx->scratch);
+        qq3::comm_destroy(ctx);
         if (ctx->own) cudaStreamDestroy(ctx->own);
         delete ctx;
     });
@@ -1385,6 +1511,12 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
         QQ_CHECK(d.head_dim == 64 || d.head_dim == 128, QQ_ERR_UNSUPPORTED, "qq_model_create: head_dim must be 64/128");
         QQ_CHECK(d.n_head / d.n_head_kv <= 8, QQ_ERR_UNSUPPORTED, "qq_model_create: GQA group larger than 8");
         need(d.max_ctx >= 1 && d.n_seq >= 1 && d.n_vocab >= 1, "qq_model_create: bad max_ctx/n_seq/n_vocab");
+        if (d.ep_world > 1) {
+            need(ctx->comm != nullptr && ctx->comm_world == d.ep_world,
+                 "qq_model_create: expert parallelism over ep_world ranks needs a communicator of that size (qq_comm_init)");
+            need(d.n_expert > 0 && d.n_expert % d.ep_world == 0,
+                 "qq_model_create: the experts must split evenly over ep_world ranks");
+        }
         const int E = d.n_embd, hd = d.head_dim;
         const int nq = d.n_head * hd, nkv = d.n_head_kv * hd;
         DeviceGuard dg(ctx->device);
@@ -1440,9 +1572,10 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                     const int rtype = (d.arch == QQ_ARCH_QWEN3 && L.t[QQ_ROUTER] && L.t[QQ_ROUTER]->type == QQ_TYPE_F32)
                                           ? QQ_TYPE_F32 : QQ_TYPE_Q8_0;
                     check_shape(L.t[QQ_ROUTER], rtype, E, d.n_expert, 1, (b + "ffn_gate_inp.weight").c_str());
-                    check_shape(L.t[QQ_GATE_EXPS], QQ_TYPE_Q8_0, E, F, d.n_expert, (b + "ffn_gate_exps.weight").c_str());
-                    check_shape(L.t[QQ_UP_EXPS], QQ_TYPE_Q8_0, E, F, d.n_expert, (b + "ffn_up_exps.weight").c_str());
-                    check_shape(L.t[QQ_DOWN_EXPS], QQ_TYPE_Q8_0, F, E, d.n_expert, (b + "ffn_down_exps.weight").c_str());
+                    const int nl = d.n_expert / std::max(d.ep_world, 1);  // experts this rank holds
+                    check_shape(L.t[QQ_GATE_EXPS], QQ_TYPE_Q8_0, E, F, nl, (b + "ffn_gate_exps.weight").c_str());
+                    check_shape(L.t[QQ_UP_EXPS], QQ_TYPE_Q8_0, E, F, nl, (b + "ffn_up_exps.weight").c_str());
+                    check_shape(L.t[QQ_DOWN_EXPS], QQ_TYPE_Q8_0, F, E, nl, (b + "ffn_down_exps.weight").c_str());
                     if (L.t[QQ_EXP_BIAS])
                         check_shape(L.t[QQ_EXP_BIAS], QQ_TYPE_F32, d.n_expert, 1, 1, (b + "exp_probs_b.bias").c_str());
                     need(F % 32 == 0, "expert FFN width must be a multiple of 32");
@@ -1456,6 +1589,12 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                     if (F > m->n_ff_max) m->n_ff_max = (int)F;
                 }
             }
+            if (d.ep_world > 1) {
+                m->ep_world = d.ep_world;
+                m->ep_rank = ctx->comm_rank;
+                m->ep_xn = dalloc<float>(E);
+            }
+            m->n_expert_local = d.n_expert / std::max(m->ep_world, 1);
             m->n_split = qq3::attention_splits(d.max_ctx);
             m->rec_len = 2 * d.n_expert_used + d.n_expert;
             m->hidden = dalloc<float>(E);
@@ -1633,11 +1772,10 @@ int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_ste
         DeviceGuard dg(m->ctx->device);
         cudaStream_t s = m->ctx->stream;
         set_suppress(m, suppress_id);
-        cudaGraphExec_t g = get_graph(m, seq_id, true);
         m->h_small[2] = first_token;
         m->h_small[3] = pos0;
         QQ_CUDA_TRY(cudaMemcpyAsync(m->ctl, m->h_small + 2, 2 * sizeof(int), cudaMemcpyHostToDevice, s));
-        for (int i = 0; i < n_steps; i++) QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+        for (int i = 0; i < n_steps; i++) launch_step(m, seq_id, true, s);
         if (tokens_out && n_steps > 0)
             QQ_CUDA_TRY(cudaMemcpyAsync(tokens_out, m->trace + (size_t)seq_id * (m->d.max_ctx + 1) + pos0 + 1,
                                         sizeof(int) * n_steps, cudaMemcpyDeviceToHost, s));
@@ -1665,8 +1803,7 @@ int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, in
             // no stop token: the whole continuation runs on the device
             if (max_steps > 0) {
                 std::vector<int32_t> tail(max_steps);
-                cudaGraphExec_t g = get_graph(m, seq_id, true);
-                for (int i = 0; i < max_steps; i++) QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+                for (int i = 0; i < max_steps; i++) launch_step(m, seq_id, true, s);
                 QQ_CUDA_TRY(cudaMemcpyAsync(tail.data(), m->trace + (size_t)seq_id * (m->d.max_ctx + 1) + n_prompt + 1,
                                             sizeof(int) * max_steps, cudaMemcpyDeviceToHost, s));
                 QQ_CUDA_TRY(cudaStreamSynchronize(s));
@@ -1725,8 +1862,15 @@ int qq_generate_sample(qq_model* m, int seq_id, const int32_t* prompt, int n_pro
             // no stop token: the whole continuation runs on the device (step + sampler graph)
             if (max_steps > 0) {
                 std::vector<int32_t> tail(max_steps);
-                cudaGraphExec_t g = get_sample_graph(m, seq_id);
-                for (int i = 0; i < max_steps; i++) QQ_CUDA_TRY(cudaGraphLaunch(g, s));
+                for (int i = 0; i < max_steps; i++) {
+                    if (m->ep_world > 1) {  // host-enqueued steps (see launch_step), then the sampler
+                        enqueue_step(m, seq_id, true, s, false);
+                        qq3::launch_sample(m->logits, m->d.n_vocab, m->sargs, m->think_done + seq_id, -1.0, seq_id, -1,
+                                           m->ctl, trace_of(m, seq_id), m->sout, m->spk, s);
+                    } else {
+                        QQ_CUDA_TRY(cudaGraphLaunch(get_sample_graph(m, seq_id), s));
+                    }
+                }
                 QQ_CUDA_TRY(cudaMemcpyAsync(tail.data(), trace_of(m, seq_id) + n_prompt + 1,
                                             sizeof(int) * max_steps, cudaMemcpyDeviceToHost, s));
                 QQ_CUDA_TRY(cudaStreamSynchronize(s));

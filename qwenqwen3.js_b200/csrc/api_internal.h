@@ -18,6 +18,10 @@ struct qq_ctx {
     // scratch arena for op-level calls (grow-only)
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    // NCCL communicator of the multi-GPU paths (comm.cu; an ncclComm_t), or null
+    void* comm = nullptr;
+    int comm_rank = 0, comm_world = 1;
+    int comm_timeout_ms = 120000;
 };
 
 struct qq_tensor {

@@ -180,6 +180,16 @@ void set_pdl(int on);
 // 0 forces the register-streamed kernels of kernels_gemv.cu everywhere (A/B measurements)
 void set_stream_path(int on);
 int stream_path();
+// ---- expert-parallel exchange, token side (kernels_ep.cu) ----
+// per destination rank r of W: pos[r][t] (token t's row in r's block, or -1), tok_of[r][q] (the
+// token of row q, or -1), ids[r][q][s] (owner-local expert of slot s, or -1) and wts[r][q][s]
+void launch_ep_plan(const int* idx, const float* w, const uint32_t* mask, int T, int top_k, int n_expert, int W, int C,
+                    int* pos, int* tok_of, int* ids, float* wts, cudaStream_t s);
+// send rows: out[r][q] = x[tok_of[r][q]] (zero where there is no token)
+void launch_ep_gather(const float* x, const int* tok_of, int W, int C, int E, float* out, cudaStream_t s);
+// hidden[t] += sum over r (rank order) of back[r][pos[r][t]]
+void launch_ep_combine(const float* back, const int* pos, int W, int T, int C, int E, float* hidden, cudaStream_t s);
+
 // ---- next-token sampling (kernels_sample.cu) ----
 constexpr int kSampleMaxTopK = 1024;
 constexpr int kThinkSuppress = 0, kThinkShorten = 1, kThinkFull = 2;

@@ -23,12 +23,15 @@ constexpr int kMaxExperts = 256;
 __global__ void __launch_bounds__(kPlanThreads)
     k_moe_plan(const int* __restrict__ idx, int P, int top_k, int n_expert, int* __restrict__ pos,
                int* __restrict__ row_token, int4* __restrict__ tiles, int* __restrict__ n_tiles) {
+    // a pair whose expert id is outside [0, n_expert) (-1: a slot another rank serves, in the
+    // expert-parallel exchange) is not computed: pos = -1, and the combine skips it
     __shared__ int cnt[kMaxExperts], cursor[kMaxExperts];
+    __shared__ int n_valid;
     for (int e = threadIdx.x; e < n_expert; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int e = min(max(idx[i], 0), n_expert - 1);
-        atomicAdd(&cnt[e], 1);
+        const int e = idx[i];
+        if (e >= 0 && e < n_expert) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -39,15 +42,21 @@ __global__ void __launch_bounds__(kPlanThreads)
             off += cnt[e];
         }
         *n_tiles = nt;
+        n_valid = off;
     }
     __syncthreads();
     // any order of the rows inside an expert gives the same per-row results
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int e = min(max(idx[i], 0), n_expert - 1);
+        const int e = idx[i];
+        if (e < 0 || e >= n_expert) {
+            pos[i] = -1;
+            continue;
+        }
         const int p = atomicAdd(&cursor[e], 1);
         pos[i] = p;
         row_token[p] = i / top_k;
     }
+    for (int p = n_valid + threadIdx.x; p < P; p += blockDim.x) row_token[p] = 0;  // rows no GEMM reads
 }
 
 // GEMM operand of value v at index i: fp16(v), and when split (the exact GEMM) the scaled
@@ -83,12 +92,14 @@ __global__ void k_moe_combine(const float* __restrict__ down, const int* __restr
         const int t = (int)(i / K), c = (int)(i % K);
         float acc = 0.f;
         for (int s = 0; s < top_k; s++) {  // slot order; a masked expert is skipped (lfm2-engine.js:459-486)
+            const int p = pos[t * top_k + s];
+            if (p < 0) continue;  // a slot served elsewhere
             if (mask) {
                 const int e = idx[t * top_k + s];
                 if ((mask[e >> 5] >> (e & 31)) & 1u) continue;
             }
             const float ws = w ? w[t * top_k + s] : 1.0f;  // no weights: each row of its own
-            acc += ws * down[(size_t)pos[t * top_k + s] * K + c];
+            acc += ws * down[(size_t)p * K + c];
         }
         out[i] = acc;
     }

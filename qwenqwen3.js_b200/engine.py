@@ -81,10 +81,17 @@ class _CudaEngine:
     THINK_ID = 151667
     END_THINK_ID = 151668
 
+    EXPERT_TENSORS = ("ffn_gate_exps.weight", "ffn_up_exps.weight", "ffn_down_exps.weight")
+
     def __init__(self, gguf, *, ctx: rt.Context | None = None, device: int = 0, max_ctx: int | None = None,
-                 n_seq: int = 1):
+                 n_seq: int = 1, ep_world: int = 1):
+        """ep_world > 1: expert parallelism -- ctx carries a communicator of ep_world ranks
+        (Context.comm_init) and this engine uploads only its rank's share of every expert tensor;
+        every rank then makes the same forward calls with the same token counts."""
         self.gguf = gguf
         self.ctx = ctx or rt.Context(device)
+        self.epWorld = int(ep_world)
+        self.epRank = 0
         self._read_hparams(gguf)
         if max_ctx is not None:
             self.maxCtx = int(max_ctx)
@@ -111,7 +118,15 @@ class _CudaEngine:
             return None
         if name not in self._tensors:
             up = self._uploader
-            self._tensors[name] = (up.upload if up is not None else self.ctx.upload)(meta.raw(), meta.type, meta.shape)
+            raw, shape = meta.raw(), list(meta.shape)
+            if self.epWorld > 1 and name.endswith(self.EXPERT_TENSORS):
+                # this rank's experts: a contiguous run of the packed [ne0, ne1, E] tensor
+                # (_expertSlice, lfm2-engine.js:490-505)
+                per = shape[2] // self.epWorld
+                stride = raw.nbytes // shape[2]
+                raw = raw[self.epRank * per * stride:(self.epRank + 1) * per * stride]
+                shape = shape[:2] + [per]
+            self._tensors[name] = (up.upload if up is not None else self.ctx.upload)(raw, meta.type, shape)
         return self._tensors[name]
 
     def _build(self):
@@ -126,6 +141,8 @@ class _CudaEngine:
                 up.finish()
 
     def _bind(self):
+        if self.epWorld > 1:
+            self.epRank = self.ctx.comm_rank()
         layers = (rt.LayerDesc * self.nLayers)()
         for i in range(self.nLayers):
             L = layers[i]
@@ -153,6 +170,7 @@ class _CudaEngine:
         out = self._upload("output.weight")
         d.output = out.h.value if out is not None else None
         d.layers = C.cast(layers, C.POINTER(rt.LayerDesc))
+        d.ep_world = self.epWorld
         up, self._uploader = self._uploader, None
         self.uploadBytes = up.finish() if up is not None else 0  # tensors are ready from here on
         self.model = rt.Model(self.ctx, d, layers, list(self._tensors.values()))

@@ -54,6 +54,16 @@ class QQError(RuntimeError):
         self.code = code
 
 
+QQ_COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """A new NCCL unique id for qq_comm_init (made on one rank, shared with the others)."""
+    buf = C.create_string_buffer(QQ_COMM_ID_BYTES)
+    check(load().qq_comm_unique_id(buf))
+    return buf.raw
+
+
 class SampleParams(C.Structure):
     """qq_sample_params: generate()'s sampling options (tensor.js:188-265)."""
     _fields_ = [("temperature", C.c_double), ("top_p", C.c_double), ("top_k", C.c_int32), ("think_mode", C.c_int32),
@@ -95,7 +105,7 @@ class ModelDesc(C.Structure):
         ("n_head_kv", C.c_int32), ("head_dim", C.c_int32), ("n_vocab", C.c_int32), ("n_expert", C.c_int32),
         ("n_expert_used", C.c_int32), ("max_ctx", C.c_int32), ("n_seq", C.c_int32), ("rms_eps", C.c_float),
         ("rope_base", C.c_double), ("tok_embd", C.c_void_p), ("output_norm", C.c_void_p), ("output", C.c_void_p),
-        ("layers", C.POINTER(LayerDesc)),
+        ("layers", C.POINTER(LayerDesc)), ("ep_world", C.c_int32),
     ]
 
 
@@ -134,6 +144,9 @@ _SIGS = {
     "qq_model_stat": (_I, [_P, _I, C.POINTER(_I64)]),
     "qq_bench_kernel": (_I, [_P, _I, _I, C.POINTER(C.c_float)]),
     "qq_moe_block_noalloc": (_I, [_P, C.POINTER(LayerDesc), _I, _I, _P, _I, _P, _P]),
+    "qq_comm_unique_id": (_I, [_P]),
+    "qq_comm_init": (_I, [_P, _P, _I, _I, _I]),
+    "qq_comm_destroy": (_I, [_P]),
     "qq_upload_begin": (_I, [_P, C.c_size_t, C.POINTER(_P)]),
     "qq_upload_tensor_async": (_I, [_P, _P, C.c_size_t, _I, C.POINTER(_I64), _I, C.POINTER(_P)]),
     "qq_upload_finish": (_I, [_P, C.POINTER(C.c_size_t)]),
@@ -250,6 +263,30 @@ class Context:
         h = C.c_void_p()
         check(self.lib.qq_upload_tensor(self.h, raw.ctypes.data, raw.nbytes, ggml_type, arr, len(ne), C.byref(h)))
         return Tensor(self, h, ggml_type, ne)
+
+    # --- multi-GPU: the context's NCCL communicator (qq_comm_*)
+    def comm_init(self, comm_id: bytes, rank: int, world: int, timeout_ms: int = 0) -> None:
+        buf = C.create_string_buffer(bytes(comm_id), QQ_COMM_ID_BYTES)
+        check(self.lib.qq_comm_init(self.h, buf, rank, world, timeout_ms))
+        self._comm = (rank, world)
+
+    def comm_rank(self) -> int:
+        if not getattr(self, "_comm", None):
+            raise QQError(QQ_ERR_INVALID, "this context has no communicator (comm_init)")
+        return self._comm[0]
+
+    def comm_init_from_torch(self, timeout_ms: int = 0) -> None:
+        """Communicator over the ranks of the default torch.distributed group: rank 0 makes the
+        id, torch.distributed broadcasts it."""
+        import torch.distributed as dist
+
+        obj = [comm_unique_id() if dist.get_rank() == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        self.comm_init(obj[0], dist.get_rank(), dist.get_world_size(), timeout_ms)
+
+    def comm_destroy(self) -> None:
+        check(self.lib.qq_comm_destroy(self.h))
+        self._comm = None
 
     def streaming_upload(self, staging_bytes: int = 0) -> "Uploader":
         """Upload many tensors through a pinned staging ring (qq_upload_begin .. qq_upload_finish);

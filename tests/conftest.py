@@ -26,6 +26,14 @@ def orc():
 
 
 @pytest.fixture(scope="session")
+def torch():
+    import torch as t
+
+    assert t.cuda.is_available()
+    return t
+
+
+@pytest.fixture(scope="session")
 def gpu_ctx(qq3):
     qq3.build.build_all()
     ctx = qq3.runtime.Context(int(os.environ.get("QQ3_TEST_DEVICE", "0")))
