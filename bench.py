@@ -10,8 +10,9 @@ uniform token ids, prefilled untimed; then W warm-up and K timed decode steps.
             inputs in HBM; each step streams 1.66 GB of weights, far above the 126 MB L2)
   e2e    -- tok/s through the public engine API (Lfm2CudaEngine.forward_argmax): each step
             copies its token/position host->device and reads the argmax back
-  N > 1  -- independent replicas, one per GPU (one process per GPU; the batch-1 decode has
-            no exchange step), value = total tokens / max-over-ranks time
+  N > 1  -- expert-parallel: each rank holds 32/N experts of every MoE layer and serves one
+            sequence; every MoE layer exchanges token rows over NCCL (run_ep);
+            value = total tokens / max-over-ranks time
 
 `--impl reference` times the reference algorithm's CPU implementation (the C restatement
 of the JS CPU path in oracle/, all host threads) on a bounded slice of the same workload.
@@ -217,6 +218,14 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     ms_e2e = e2.elapsed_time(e3)
 
+    # ---- optional per-phase trace of the persistent step (--trace): critical-path time per phase kind
+    phase_trace = None
+    if args.trace and eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS) == 1:
+        eng.model.decode_trace(True)
+        eng.model.decode_loop(cur, pos, 4, seq=1, suppress_id=suppress, want_tokens=False)
+        stamps, kinds = eng.model.decode_trace(False, read=True)
+        phase_trace = trace_summary(stamps, kinds)
+
     # ---- dominant kernel (expert gate/up GEMV) and whole MoE layer, timed alone over all layers
     nbytes = _lfm2_model_bytes(spec)
     ms_gateup = eng.model.bench_kernel(qq3.runtime.QQ_KERN_MOE_GATEUP, 3)
@@ -270,6 +279,7 @@ def run_ours(args, ws, rank, local):
         "clocks": clk.summary(),
         "prefill": {"tokens": args.prompt - 1, "ms": round(prefill_s * 1e3, 2),
                     "tok_s": round((args.prompt - 1) / prefill_s, 1), "note": "untimed setup, host wall clock"},
+        "phase_trace": phase_trace,
         "setup_s": {"weight_generation": round(gen_s, 1), "engine_create": round(upload_s, 2),
                     "weight_upload_gbs": round(eng.uploadBytes / upload_s / 1e9, 2),
                     "note": "engine_create = streamed upload of the raw GGUF bytes (pinned ring) + model binding"},
@@ -282,6 +292,172 @@ def run_ours(args, ws, rank, local):
     if rank == 0:
         print(json.dumps(res), flush=True)
     eng.close()
+
+
+PHASE_TYPES = {0: "embed", 1: "gemv", 2: "down4", 3: "attention", 4: "finish", 5: "fused"}
+EPI_KINDS = {0: "store", 1: "resid", 2: "swiglu", 3: "conv", 4: "argmax"}
+
+
+def trace_summary(stamps, kinds) -> dict:
+    """Critical path of a traced persistent step: per phase, the end of its last CTA minus the end
+    of the previous phase's last CTA, summed per phase kind (type/epilogue[/routed])."""
+    stamps = stamps.astype(np.int64)
+    t0 = int(stamps[:, 0].min())
+    ends = stamps[:, 1:].max(axis=0) - t0
+    out: dict = {}
+    prev = 0
+    for ph, k in enumerate(kinds):
+        label = f"{PHASE_TYPES.get(int(k) & 255, '?')}/{EPI_KINDS.get((int(k) >> 8) & 255, '?')}" + \
+                ("/routed" if (int(k) >> 16) & 1 else "")
+        crit = int(ends[ph]) - prev
+        prev = int(ends[ph])
+        e = out.setdefault(label, {"count": 0, "crit_us": 0.0})
+        e["count"] += 1
+        e["crit_us"] += crit / 1e3
+    for e in out.values():
+        e["crit_us_per_phase"] = round(e["crit_us"] / e["count"], 2)
+        e["crit_us"] = round(e["crit_us"], 1)
+    return {"step_us": round(int(ends[-1]) / 1e3, 1), "by_kind": out,
+            "note": "one traced step (%globaltimer per CTA and phase, qq_decode_trace)"}
+
+
+def run_ep(args, ws, rank, local):
+    """benchmark config 4 on N GPUs, expert-parallel: every rank holds 32/N experts of each MoE
+    layer (plus the replicated non-expert weights) and serves its own sequence, a seeded
+    512-token prompt; every MoE layer exchanges token rows over the library's NCCL communicator
+    (rows dispatched once per owner rank, the owners' grouped tensor-core expert GEMMs, partial
+    sums back).  Prefill: each rank's 511 prompt tokens through the batched path.  value = decode
+    tok/s over all ranks (N sequences x K steps / max-over-ranks time), weak scaling."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    qq3 = load_package()
+    qq3.build.build_all()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
+    t0 = time.time()
+    g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
+    gen_s = time.time() - t0
+    ctx = qq3.runtime.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    ctx.comm_init_from_torch(timeout_ms=120000)
+    n_prof = 4
+    max_ctx = args.prompt + args.warmup + 2 * args.steps + n_prof + 16
+    t_up = time.time()
+    eng = qq3.Lfm2CudaEngine(g, ctx=ctx, max_ctx=max_ctx, ep_world=ws)
+    upload_s = time.time() - t_up
+    prompt = qq3.synth.uniform_tokens(args.prompt, SEED + rank, spec.n_vocab)
+    suppress = THINK_ID if THINK_ID < spec.n_vocab else -1
+
+    def max_ms(v):
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    # prefill: one untimed pass (buffers, first-use set-up), then the timed one, then its split
+    eng.prefill(prompt[:-1].tolist())
+    eng.resetKVCache()
+    dist.barrier()
+    torch.cuda.synchronize()
+    p0, p1 = ev(), ev()
+    p0.record(stream)
+    eng.prefill(prompt[:-1].tolist())
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = max_ms(p0.elapsed_time(p1))
+    eng.resetKVCache()
+    eng.model.ep_profile(True)
+    eng.prefill(prompt[:-1].tolist())
+    split_pf = eng.model.ep_profile(False)
+    # decode
+    pos = args.prompt - 1
+    toks = eng.model.decode_loop(int(prompt[-1]), pos, args.warmup, suppress_id=suppress)
+    pos += args.warmup
+    cur = int(toks[-1])
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        out = eng.model.decode_loop(cur, pos, args.steps, suppress_id=suppress)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_ms(e0.elapsed_time(e1))
+    pos += args.steps
+    cur = int(out[-1])
+    # e2e: the public engine API, host token in / argmax out per step
+    dist.barrier()
+    torch.cuda.synchronize()
+    e2, e3 = ev(), ev()
+    e2.record(stream)
+    for _ in range(args.steps):
+        cur = eng.forward_argmax(cur, pos, suppress)
+        pos += 1
+    e3.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = max_ms(e2.elapsed_time(e3))
+    # the split of the decode exchanges
+    eng.model.ep_profile(True)
+    eng.model.decode_loop(cur, pos, n_prof, suppress_id=suppress)
+    split_dec = eng.model.ep_profile(False)
+    nbytes = _lfm2_model_bytes(spec)
+    peak, peak_kind = _peaks()
+    step_ms = ms / args.steps
+    # kernels of one expert-parallel decode step (per-phase path): embed; per short-conv layer 2,
+    # per attention layer 3; per dense FFN 2; per MoE layer rmsnorm + router + plan + gather +
+    # 7 of the grouped expert block + combine = 12; lm_head + argmax finish 2
+    n_attn = sum(1 for i in range(spec.n_layers) if spec.is_attn(i))
+    n_moe = sum(1 for i in range(spec.n_layers) if spec.is_moe(i))
+    step_kernels = 1 + 2 * (spec.n_layers - n_attn) + 3 * n_attn + 2 * (spec.n_layers - n_moe) + 12 * n_moe + 2
+
+    def per_exchange(sp):
+        n = max(sp["exchanges"], 1)
+        return {k: round(sp[k] / n * 1e3, 2) for k in ("dispatch", "experts", "ret", "combine")} | {"exchanges": sp["exchanges"]}
+
+    dec_split, pf_split = per_exchange(split_dec), per_exchange(split_pf)
+    coll = {"dispatch": dec_split["dispatch"], "combine (return)": dec_split["ret"]}
+    res = {
+        "metric": METRIC, "value": round(ws * args.steps / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32 (Q8_0 weights, f32 activations)",
+        "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)",
+        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 per rank, expert-parallel "
+                               "(benchmark config 4)",
+                   "layers": "24 (18 short-conv, 6 GQA attention; 2 dense FFN 7168, 22 MoE 32x top-4 x 1792)",
+                   "hidden": 2048, "vocab": 65536, "prompt": args.prompt, "global_batch": ws,
+                   "parallelism": f"ep{ws} (experts sharded {spec.n_expert // ws} per rank; non-expert weights "
+                                  "replicated; one sequence per rank)",
+                   "l2": "inputs larger than L2: each step streams >1 GB of weights per rank"},
+        "roofline": {"bound": "hbm", "kernel": "whole expert-parallel decode step (per-phase kernels + NCCL exchanges)",
+                     "achieved": round(nbytes["weights_per_token"] / (step_ms * 1e-3) / 1e9, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(nbytes["weights_per_token"] / (step_ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                     "note": "achieved = one token's algorithmic weight bytes (all its 4 experts) per rank and step; "
+                             "the experts a rank streams are shared by the ranks' tokens"},
+        "e2e": {"value": round(ws * args.steps / (ms_e2e * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 4, "api": "Lfm2CudaEngine.forward_argmax -> qq_forward (expert-parallel)"},
+        "gpu_launches": int(step_kernels * args.steps),
+        "clocks": clk.summary(),
+        "ep_prefill": {"tokens_per_rank": args.prompt - 1, "ms": round(prefill_ms, 3),
+                       "tok_s": round(ws * (args.prompt - 1) / (prefill_ms * 1e-3), 1),
+                       "us_per_exchange": pf_split, "note": "max over ranks, CUDA events"},
+        "ep_decode_us_per_exchange": dec_split,
+        "limiting_collective": max(coll, key=coll.get),
+        "setup_s": {"weight_generation": round(gen_s, 1), "engine_create": round(upload_s, 2)},
+    }
+    eng.close()
+    dist.barrier()
+    ctx.comm_destroy()
+    ctx.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
 
 
 def _oracle():
@@ -545,7 +721,13 @@ def run_batch_decode(args, ws, rank, local):
     qq3 = load_package()
     qq3.build.build_all()
     torch.cuda.set_device(local)
-    spec = qq3.synth.qwen3_8b(seed=SEED + rank)
+    dist = None
+    if ws > 1:  # tensor-parallel: every rank holds its shards of the same model and sequences
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    spec = qq3.synth.qwen3_8b(seed=SEED)
     if args.layers:
         spec.n_layers = args.layers  # profiling knob: every layer streams the same bytes
     n = args.seqs
@@ -554,18 +736,24 @@ def run_batch_decode(args, ws, rank, local):
     ctx = qq3.runtime.Context(local)
     stream = torch.cuda.Stream(device=local)
     ctx.set_stream(stream.cuda_stream)
+    if dist:
+        ctx.comm_init_from_torch(timeout_ms=120000)
     max_ctx = prompt + args.warmup + args.steps + 1
-    eng = qq3.Qwen3CudaEngine(g, ctx=ctx, max_ctx=max_ctx, n_seq=n)
+    eng = qq3.Qwen3CudaEngine(g, ctx=ctx, max_ctx=max_ctx, n_seq=n, tp_world=ws)
     cur, pos = [], []
     t0 = time.time()
     for s in range(n):
-        toks = qq3.synth.uniform_tokens(prompt, SEED + 100 * rank + s, spec.n_vocab)
+        toks = qq3.synth.uniform_tokens(prompt, SEED + s, spec.n_vocab)
         if prompt > 1:
             eng.prefill(toks[:-1].tolist(), pos0=0, seq=s)
         cur.append(int(toks[-1]))
         pos.append(prompt - 1)
     ctx.synchronize()
     prefill_s = time.time() - t0
+    if dist:
+        t = torch.tensor([prefill_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_s = float(t[0])
     seqs = list(range(n))
 
     def step():
@@ -578,6 +766,9 @@ def run_batch_decode(args, ws, rank, local):
         step()
     kv_pos = sum(pos) + n  # positions attended in the first timed step (grows by n per step)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
     with Clocks(local) as clk:
         e0.record(stream)
         for _ in range(args.steps):
@@ -585,6 +776,10 @@ def run_batch_decode(args, ws, rank, local):
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    if dist:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
     L, E, F, V = spec.n_layers, spec.n_embd, spec.n_ff, spec.n_vocab
     nq, nkv = spec.n_head * spec.head_dim, spec.n_head_kv * spec.head_dim
     w_bytes = 34 / 32 * (L * (E * (2 * nq + 2 * nkv) + 3 * E * F) + E * V)
@@ -592,19 +787,24 @@ def run_batch_decode(args, ws, rank, local):
     peak, kind = _peaks()
     gbs = (w_bytes + kv_bytes) / (ms * 1e-3) / 1e9
     res = {"metric": "decode tok/s (Qwen3-8B-shaped, 16 concurrent sequences)", "impl": "ours",
-           "value": round(n / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+           "value": round(n / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+           "scaling": "strong" if ws > 1 else "weak", "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "int8xf16",
            "data": "synthetic (seeded random-init Q8_0 weights, uniform prompt ids)",
            "config": {"workload": "qwen3-8b-batch-decode", "sequences": n, "prompt": prompt, "layers": L,
                       "path": "qq_forward_batch: tcgen05 GEMMs over the 16 rows, f32 KV cache",
                       "l2": "weights 8.04 GB + KV per step, far above the 126 MB L2"},
-           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(gbs / peak, 4), "peak_kind": kind,
+           "roofline": {"bound": "hbm", "achieved": round(gbs / ws, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / ws / peak, 4), "peak_kind": kind, "per": "GPU (each rank streams 1/N)",
                         "bytes_per_step": {"weights": round(w_bytes), "kv": round(kv_bytes)}},
            "prefill_s": round(prefill_s, 2), "clocks": clk.summary()}
     eng.close()
+    if dist:
+        dist.barrier()
+        ctx.comm_destroy()
+        dist.destroy_process_group()
     ctx.close()
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         # the reference serves one sequence per engine: one sequence, a short prompt (CPU time)
         res["cpu_baseline"] = cpu_decode(g, spec, qq3.synth.uniform_tokens(8, SEED, spec.n_vocab),
                                          budget_s=args.cpu_seconds, label="Qwen3-8B-shaped decode of one sequence")
@@ -672,6 +872,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n-expert", type=int, default=32,
                     help="experts per MoE layer (profiling knob: a token streams the same bytes for any count >= 4)")
+    ap.add_argument("--trace", action="store_true",
+                    help="add the per-phase critical-path breakdown of the persistent decode step")
     ap.add_argument("--write-model", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.write_model:
@@ -690,6 +892,8 @@ def main():
         run_matmul(args, ws, rank, local)
     elif args.case == "batch-decode":
         run_batch_decode(args, ws, rank, local)
+    elif ws > 1:
+        run_ep(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
 

@@ -188,6 +188,16 @@ typedef struct qq_model_desc {
      * Every rank then makes the same forward calls with the same token counts (the calls are
      * collective).  0 or 1: one rank holds every expert. */
     int32_t ep_world;
+    /* Tensor parallelism for dense Qwen3 (no reference counterpart): > 1 splits every layer over
+     * tp_world ranks (the context's communicator, world tp_world).  The hyper-parameters above stay
+     * the whole model's; the tensors are this rank's shards: wq/wk/wv the rows of its query heads
+     * [r nH/G, (r+1) nH/G) and KV heads, wo the matching input columns, ffn_gate/up the rows of
+     * its FFN units [r F/G, (r+1) F/G) and ffn_down those input columns, output (required) the
+     * vocab rows [r V/G, (r+1) V/G); token_embd and the norms whole.  wo and ffn_down partial
+     * sums are all-reduced; the greedy id is the first maximum over the ranks' shards.  Steps run
+     * through qq_forward / qq_forward_batch (collective: every rank makes the same calls).
+     * 0 or 1: no split. */
+    int32_t tp_world;
 } qq_model_desc;
 
 /* Bind uploaded tensors into an engine.  Replaces Qwen3GPUEngine.create /
@@ -285,6 +295,18 @@ int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_ste
 
 /* ---------------------------------------------------------------- diagnostics */
 
+/* Per-phase trace of the persistent decode step (no reference counterpart; the breakdown behind
+ * the decode-step profile): enable = 1 makes every later step's CTAs stamp %globaltimer at their
+ * start and at the end of each phase (the last step's stamps are kept); enable = 0 stops it.
+ * stamps_out (nullable) receives the stamps of the last traced step, [n_ctas][n_phases + 1] ns;
+ * kinds_out (nullable, n_phases ints) each phase's type | epilogue << 8 | routed << 16. */
+int qq_decode_trace(qq_model* m, int enable, uint64_t* stamps_out, int32_t* kinds_out, int* n_phases, int* n_ctas);
+/* Expert-parallel models: switch the CUDA-event split of every MoE exchange on (enable = 1) or
+ * off, and read (ms_out, nullable, 5 floats) the time summed since the last call over the
+ * exchanges recorded: [dispatch (plan + gather + NCCL send/recv), experts (owner GEMMs),
+ * return (NCCL send/recv back), combine, number of exchanges]. */
+int qq_ep_profile(qq_model* m, int enable, float* ms_out);
+
 /* Statistics of a model (no reference counterpart; used by the benchmark):
  *   QQ_STAT_STEP_KERNELS  kernels launched by one decode step with logits
  *   QQ_STAT_N_MOE         number of MoE layers
@@ -352,7 +374,10 @@ int qq_moe_combine(qq_ctx* ctx, const float* y_dev, const int32_t* pos_dev, cons
  * n_expert <= 32; beyond them the call fails with QQ_ERR_INVALID and does no GPU work.
  * The first call on a device resolves the array's device address (cudaGetSymbolAddress); make
  * that first call before any stream capture.  All calls on a device share the array and it
- * keeps the last call's contents: calls whose GPU work overlaps race. */
+ * keeps the last call's contents: calls whose GPU work overlaps race.
+ * Cost: the rows are served token by token (two expert GEMV launches per row, 2T launches for T
+ * rows), where qq_moe_block regroups T >= 16 rows by expert on the tensor cores, so large T is
+ * much slower here than there. */
 #define QQ_NOALLOC_MAX_TOKENS 1024
 #define QQ_NOALLOC_MAX_FF 4096
 int qq_moe_block_noalloc(qq_ctx* ctx, const qq_layer_desc* layer, int n_expert, int top_k, const float* x_dev,

@@ -8,6 +8,7 @@
 //   * greedy decode can run entirely on the device: the step's last kernel writes the
 //     argmax back as the next step's token (qq_decode_loop).
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -124,6 +125,7 @@ struct qq_model {
     };
     std::map<std::pair<int, int>, Prog> progs;
     qq3::DecodeCtl* dctl = nullptr;  // model-wide control block of the persistent kernel
+    unsigned long long* trace_buf = nullptr;  // per-CTA phase stamps (qq_decode_trace)
     // batched prefill / multi-sequence buffers (grow-only, pf_bytes allocated)
     size_t pf_bytes = 0;
     void* pf_arena = nullptr;
@@ -152,6 +154,17 @@ struct qq_model {
     int ep_cap = 0;
     void* ep_arena = nullptr;
     float* ep_xn = nullptr;  // the normalised FFN input of a decode step [n_embd]
+    // optional CUDA-event split of every exchange (qq_ep_profile): dispatch, experts, return, combine
+    bool ep_prof = false;
+    std::vector<std::array<cudaEvent_t, 5>> ep_evs;
+    // tensor parallelism (dense Qwen3): this rank's vocab rows [v0, v0 + v_local) of the lm_head;
+    // d.n_head / d.n_head_kv hold this rank's head counts; greedy keys of all ranks [G][cap][32],
+    // gathered logits [G][cap][v_local], the shard-local suppressed id
+    int tp_world = 1, tp_rank = 0, v_local = 0, v0 = 0;
+    void* tp_keys = nullptr;
+    float* tp_logits = nullptr;
+    int* tp_suppress = nullptr;
+    int tp_cap = 0;
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
@@ -169,6 +182,7 @@ void free_model(qq_model* m) {
         if (kv.second.d_prog) cudaFree(kv.second.d_prog);
     m->progs.clear();
     if (m->dctl) cudaFree(m->dctl);
+    if (m->trace_buf) cudaFree(m->trace_buf);
     if (m->pf_arena) cudaFree(m->pf_arena);
     if (m->bt_i) cudaFree(m->bt_i);
     if (m->bt_logits) cudaFree(m->bt_logits);
@@ -177,6 +191,12 @@ void free_model(qq_model* m) {
     if (m->h_bt) cudaFreeHost(m->h_bt);
     if (m->tarena) cudaFree(m->tarena);
     if (m->ep_arena) cudaFree(m->ep_arena);
+    if (m->tp_keys) cudaFree(m->tp_keys);
+    if (m->tp_logits) cudaFree(m->tp_logits);
+    if (m->tp_suppress) cudaFree(m->tp_suppress);
+    for (auto& ev : m->ep_evs)
+        for (auto e : ev) cudaEventDestroy(e);
+    m->ep_evs.clear();
     if (m->ep_xn) cudaFree(m->ep_xn);
     if (m->aarena) cudaFree(m->aarena);
     for (Layer& L : m->layers) {
@@ -265,6 +285,11 @@ void ep_moe(qq_model* m, const Layer& L, const float* xn, int T, const int* idx,
     const int W = m->ep_world, E = d.n_embd, k = d.n_expert_used, C = T;
     qq_ctx* c = m->ctx;
     EpBufs b = ep_bufs(m, C);
+    std::array<cudaEvent_t, 5> ev{};
+    if (m->ep_prof) {
+        for (auto& e : ev) QQ_CUDA_TRY(cudaEventCreate(&e));
+        QQ_CUDA_TRY(cudaEventRecord(ev[0], s));
+    }
     qq3::launch_ep_plan(idx, w, m->mask, T, k, d.n_expert, W, C, b.pos, b.tok_of, b.sids, b.swts, s);
     qq3::launch_ep_gather(xn, b.tok_of, W, C, E, b.sx, s);
     const size_t rowb = (size_t)C * E * 4, slotb = (size_t)C * k * 4;
@@ -278,16 +303,23 @@ void ep_moe(qq_model* m, const Layer& L, const float* xn, int T, const int* idx,
         qq3::comm_recv(c, b.rwts + (size_t)r * C * k, slotb, r, s);
     }
     qq3::comm_group_end(c);
+    if (m->ep_prof) QQ_CUDA_TRY(cudaEventRecord(ev[1], s));
     // the owner side: weighted partial sums of the slots this rank serves, row by received row
     qq3::launch_moe_grouped(*L.t[QQ_GATE_EXPS], *L.t[QQ_UP_EXPS], *L.t[QQ_DOWN_EXPS], b.rids, b.rwts, nullptr, b.rx,
                             W * C, k, m->n_expert_local, b.moe, b.y, s);
+    if (m->ep_prof) QQ_CUDA_TRY(cudaEventRecord(ev[2], s));
     qq3::comm_group_start();
     for (int r = 0; r < W; r++) {
         qq3::comm_send(c, b.y + (size_t)r * C * E, rowb, r, s);
         qq3::comm_recv(c, b.back + (size_t)r * C * E, rowb, r, s);
     }
     qq3::comm_group_end(c);
+    if (m->ep_prof) QQ_CUDA_TRY(cudaEventRecord(ev[3], s));
     qq3::launch_ep_combine(b.back, b.pos, W, T, C, E, hidden, s);
+    if (m->ep_prof) {
+        QQ_CUDA_TRY(cudaEventRecord(ev[4], s));
+        m->ep_evs.push_back(ev);
+    }
 }
 
 // One decode step for sequence `seq` (token/position in m->ctl), as the fixed kernel
@@ -855,6 +887,11 @@ void set_suppress(qq_model* m, int id) {
     if (id == m->suppress_set) return;  // the device copy already holds it
     m->h_small[0] = id;
     QQ_CUDA_TRY(cudaMemcpyAsync(m->suppress, m->h_small, sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+    if (m->tp_world > 1) {
+        m->h_small[6] = (id >= m->v0 && id < m->v0 + m->v_local) ? id - m->v0 : -1;
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->tp_suppress, m->h_small + 6, sizeof(int), cudaMemcpyHostToDevice,
+                                    m->ctx->stream));
+    }
     m->suppress_set = id;
 }
 
@@ -1054,6 +1091,7 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
             qq3::launch_kv_append(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, pos0, kc, vc, s);
             qq3::launch_attn_prefill(b.q, kc, vc, T, pos0, d.n_head, d.n_head_kv, hd, d.max_ctx, b.attn, s);
             qq3::launch_gemm_q8(*L.t[QQ_WO], b.attn, T, b.x16, b.tmp, s);
+            if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);
         } else {
             qq3::launch_gemm_q8(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.bcx, s);
             qq3::launch_conv_prefill(b.bcx, L.t[QQ_CONV]->f32, m->conv(seq, l), T, E, b.y, s);
@@ -1085,6 +1123,7 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
             qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s);
             qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
             qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s);
+            if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);
         }
         qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
     }
@@ -1098,6 +1137,22 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
 // append, attention and the short-conv state; then the output norm, the lm_head GEMM and a
 // first-max argmax per row.  The MoE routing record kept for onRouterUpdate is that of the last
 // row.  Same results as T separate forward() calls up to the GEMM's f32 accumulation order.
+// the tensor-parallel gather buffers for T rows (grow-only): keys of all ranks + this rank's, and
+// all ranks' logits shards
+void ensure_tp_bufs(qq_model* m, int T) {
+    if (T <= m->tp_cap) return;
+    QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    if (m->tp_keys) cudaFree(m->tp_keys);
+    if (m->tp_logits) cudaFree(m->tp_logits);
+    m->tp_keys = nullptr;
+    m->tp_logits = nullptr;
+    int cap = 16;
+    while (cap < T) cap *= 2;
+    m->tp_keys = dmalloc((size_t)(m->tp_world + 1) * cap * 32 * sizeof(unsigned long long));
+    m->tp_logits = static_cast<float*>(dmalloc((size_t)m->tp_world * cap * m->v_local * sizeof(float)));
+    m->tp_cap = cap;
+}
+
 void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
     const qq_model_desc& d = m->d;
     cudaStream_t s = m->ctx->stream;
@@ -1127,6 +1182,7 @@ void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
             qq3::launch_attn_rows_split(b.q, kc, vc, T, seq, pos, max_len, m->kv_stride_seq(), d.n_head, d.n_head_kv,
                                         hd, d.max_ctx, m->bt_attn, b.attn, s);
             qq3::launch_gemm_q8_few(*L.t[QQ_WO], b.attn, T, b.x16, b.rows, b.tmp, s);
+            if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);  // heads' partial sums
         } else {
             qq3::launch_gemm_q8_few(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.rows, b.bcx, s);
             qq3::launch_conv_rows_at(b.bcx, L.t[QQ_CONV]->f32, m->conv(0, l), (size_t)d.n_layers * 2 * E, seq, T, E,
@@ -1158,6 +1214,7 @@ void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
             qq3::launch_gemm_q8_few(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.rows, b.u, s);
             qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
             qq3::launch_gemm_q8_few(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.rows, b.tmp, s);
+            if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);  // units' partial sums
         }
         qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
     }
@@ -1165,7 +1222,30 @@ void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
     qq3::launch_rmsnorm(b.hidden, T, E, m->out_norm->f32, d.rms_eps, b.xn, s);
     const DTensor* out = m->output ? m->output : m->tok_embd;
     qq3::launch_gemm_q8_few(*out, b.xn, T, b.x16, b.rows, m->bt_logits, s);
+    if (m->tp_world > 1) {
+        // this shard's greedy keys (global ids), all ranks' keys, then the first global maximum
+        ensure_tp_bufs(m, T);
+        const size_t kb = (size_t)T * 32 * sizeof(unsigned long long);
+        char* keys_all = static_cast<char*>(m->tp_keys);
+        char* mine = keys_all + (size_t)m->tp_world * m->tp_cap * 32 * sizeof(unsigned long long);
+        qq3::launch_argmax_rows_keys(m->bt_logits, T, m->v_local, m->tp_suppress, m->v0, mine, s);
+        qq3::comm_allgather(m->ctx, mine, keys_all, kb, s);
+        qq3::launch_argmax_merge(keys_all, m->tp_world, T, m->bt_i + 3 * m->bt_cap, s);
+        return;
+    }
     qq3::launch_argmax_rows(m->bt_logits, T, d.n_vocab, m->suppress, m->bt_keys, m->bt_i + 3 * m->bt_cap, s);
+}
+
+// the vocab shards' logits of T rows from every rank into host logits [T][n_vocab]
+void tp_logits_to_host(qq_model* m, int T, float* host) {
+    cudaStream_t s = m->ctx->stream;
+    ensure_tp_bufs(m, T);
+    const size_t per = (size_t)T * m->v_local;
+    qq3::comm_allgather(m->ctx, m->bt_logits, m->tp_logits, per * sizeof(float), s);
+    for (int g = 0; g < m->tp_world; g++)
+        QQ_CUDA_TRY(cudaMemcpy2DAsync(host + (size_t)g * m->v_local, sizeof(float) * m->d.n_vocab,
+                                      m->tp_logits + (size_t)g * per, sizeof(float) * m->v_local,
+                                      sizeof(float) * m->v_local, T, cudaMemcpyDeviceToHost, s));
 }
 
 // grow the multi-sequence row buffers to hold T rows (device and pinned staging)
@@ -1211,6 +1291,21 @@ bool batched_prefill_ok(qq_model* m) {
 void run_tokens(qq_model* m, const int32_t* token_ids, int n, int seq, int pos0, bool want_logits) {
     cudaStream_t s = m->ctx->stream;
     for (int i = 0; i < n; i++) need(token_ids[i] >= 0 && token_ids[i] < m->d.n_vocab, "token id out of range");
+    if (m->tp_world > 1) {
+        // tensor-parallel: the prompt through the batched layers, the token with logits as a
+        // one-row multi-sequence step (its greedy id and vocab shard in bt_i / bt_logits)
+        const int n_batch = want_logits ? n - 1 : n;
+        for (int c = 0; c < n_batch; c += kPrefillChunk)
+            prefill_chunk(m, token_ids + c, std::min(kPrefillChunk, n_batch - c), seq, pos0 + c);
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));  // the host token array is read asynchronously above
+        if (!want_logits) return;
+        ensure_batch_rows(m, 1);
+        m->h_bt[0] = token_ids[n - 1];
+        m->h_bt[m->bt_cap] = seq;
+        m->h_bt[2 * m->bt_cap] = pos0 + n - 1;
+        batch_step(m, 1, pos0 + n, true);
+        return;
+    }
     // a long prefix runs batched; the token that needs logits takes the decode step below
     const int n_batch = want_logits ? n - 1 : n;
     if (n_batch >= kBatchedPrefillMin && batched_prefill_ok(m)) {
@@ -1504,7 +1599,21 @@ int qq_add(qq_ctx* ctx, float* x_dev, const float* d_dev, int64_t n) {
 int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
     return guard([&] {
         need(ctx && desc && out && desc->layers, "qq_model_create: NULL argument");
-        const qq_model_desc& d = *desc;
+        // with tensor parallelism the model below is this rank's share: its heads, its vocab rows
+        qq_model_desc dl = *desc;
+        const int G = std::max(desc->tp_world, 1);
+        if (G > 1) {
+            need(desc->arch == QQ_ARCH_QWEN3, "qq_model_create: tensor parallelism is for dense Qwen3 models");
+            need(ctx->comm != nullptr && ctx->comm_world == G,
+                 "qq_model_create: tensor parallelism over tp_world ranks needs a communicator of that size");
+            need(desc->ep_world <= 1, "qq_model_create: expert and tensor parallelism do not combine");
+            need(desc->n_head % G == 0 && desc->n_head_kv % G == 0 && desc->n_vocab % G == 0,
+                 "qq_model_create: heads and vocab must split evenly over tp_world ranks");
+            need(desc->output != nullptr, "qq_model_create: tensor parallelism needs the rank's output rows");
+            dl.n_head /= G;
+            dl.n_head_kv /= G;
+        }
+        const qq_model_desc& d = dl;
         need(d.arch == QQ_ARCH_QWEN3 || d.arch == QQ_ARCH_LFM2, "qq_model_create: unknown arch");
         need(d.n_layers >= 1 && d.n_embd >= 32 && d.n_embd % 32 == 0, "qq_model_create: bad n_layers/n_embd");
         need(d.n_head >= 1 && d.n_head_kv >= 1 && d.n_head % d.n_head_kv == 0, "qq_model_create: bad head counts");
@@ -1530,7 +1639,7 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
             m->out_norm = dt(d.output_norm);
             check_shape(m->out_norm, QQ_TYPE_F32, E, 1, 1, "output norm");
             m->output = dt(d.output);
-            if (m->output) check_shape(m->output, QQ_TYPE_Q8_0, E, d.n_vocab, 1, "output.weight");
+            if (m->output) check_shape(m->output, QQ_TYPE_Q8_0, E, d.n_vocab / G, 1, "output.weight");
             m->layers.resize(d.n_layers);
             for (int l = 0; l < d.n_layers; l++) {
                 const qq_layer_desc& ld = d.layers[l];
@@ -1588,6 +1697,15 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                     need(F % 32 == 0, "FFN width must be a multiple of 32");
                     if (F > m->n_ff_max) m->n_ff_max = (int)F;
                 }
+            }
+            if (G > 1) {
+                m->tp_world = G;
+                m->tp_rank = ctx->comm_rank;
+                m->v_local = d.n_vocab / G;
+                m->v0 = m->tp_rank * m->v_local;
+                m->tp_suppress = dalloc<int>(1);
+                QQ_CUDA_TRY(cudaMemsetAsync(m->tp_suppress, 0xff, 4, ctx->stream));
+                m->mega = 0;  // steps run through the multi-row path (batch_step)
             }
             if (d.ep_world > 1) {
                 m->ep_world = d.ep_world;
@@ -1679,6 +1797,15 @@ int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, 
         const bool logits = want_logits != 0;
         if (logits) set_suppress(m, suppress_id);
         run_tokens(m, token_ids, n_tokens, seq_id, pos0, logits);
+        if (m->tp_world > 1) {
+            if (logits && logits_out) tp_logits_to_host(m, 1, logits_out);
+            if (logits) QQ_CUDA_TRY(cudaMemcpyAsync(m->h_small + 1, m->bt_i + 3 * m->bt_cap, sizeof(int),
+                                                    cudaMemcpyDeviceToHost, s));
+            QQ_CUDA_TRY(cudaStreamSynchronize(s));
+            check_kernel_error(s);
+            if (logits && argmax_out) *argmax_out = m->h_small[1];
+            return;
+        }
         if (logits && logits_out)
             QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, sizeof(float) * m->d.n_vocab, cudaMemcpyDeviceToHost, s));
         if (logits && argmax_out)
@@ -1707,7 +1834,7 @@ int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_i
         const bool logits = want_logits != 0;
         const size_t V = (size_t)m->d.n_vocab;
         if (logits) set_suppress(m, suppress_id);
-        if (n == 1 || !batched_prefill_ok(m)) {
+        if (m->tp_world <= 1 && (n == 1 || !batched_prefill_ok(m))) {
             // one sequence (or no tensor-core path): the per-token decode step, row by row
             for (int i = 0; i < n; i++) {
                 run_tokens(m, token_ids + i, 1, seq_ids[i], positions[i], logits);
@@ -1733,8 +1860,10 @@ int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_i
             max_len = std::max(max_len, positions[i] + 1);
         }
         batch_step(m, n, max_len, logits);
-        if (logits && logits_out)
-            QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->bt_logits, sizeof(float) * V * n, cudaMemcpyDeviceToHost, s));
+        if (logits && logits_out) {
+            if (m->tp_world > 1) tp_logits_to_host(m, n, logits_out);
+            else QQ_CUDA_TRY(cudaMemcpyAsync(logits_out, m->bt_logits, sizeof(float) * V * n, cudaMemcpyDeviceToHost, s));
+        }
         if (logits && argmax_out)
             QQ_CUDA_TRY(cudaMemcpyAsync(m->h_bt + 3 * m->bt_cap, m->bt_i + 3 * m->bt_cap, sizeof(int) * n,
                                         cudaMemcpyDeviceToHost, s));
@@ -1747,6 +1876,7 @@ int qq_forward_batch(qq_model* m, const int32_t* seq_ids, const int32_t* token_i
 
 int qq_forward_dump(qq_model* m, int32_t token_id, int seq_id, int pos, float* hidden_out) {
     return guard([&] {
+        need(m && m->tp_world <= 1, "qq_forward_dump: not available for a tensor-parallel model (use qq_forward / qq_forward_batch)");
         need(m && hidden_out, "qq_forward_dump: NULL argument");
         check_seq_pos(m, seq_id, pos, 1);
         need(token_id >= 0 && token_id < m->d.n_vocab, "token id out of range");
@@ -1766,6 +1896,7 @@ int qq_forward_dump(qq_model* m, int32_t token_id, int seq_id, int pos, float* h
 int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_steps, int suppress_id,
                    int32_t* tokens_out) {
     return guard([&] {
+        need(m && m->tp_world <= 1, "qq_decode_loop: not available for a tensor-parallel model (use qq_forward / qq_forward_batch)");
         need(m != nullptr && n_steps >= 0, "qq_decode_loop: bad argument");
         check_seq_pos(m, seq_id, pos0, n_steps);
         need(first_token >= 0 && first_token < m->d.n_vocab, "token id out of range");
@@ -1787,6 +1918,7 @@ int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_ste
 int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps, int think_id,
                 int eos_id, int32_t* out_tokens, int* n_out) {
     return guard([&] {
+        need(m && m->tp_world <= 1, "qq_generate: not available for a tensor-parallel model (use qq_forward / qq_forward_batch)");
         need(m && prompt && n_prompt >= 1 && max_steps >= 0 && n_out, "qq_generate: bad argument");
         check_seq_pos(m, seq_id, 0, n_prompt + max_steps);
         DeviceGuard dg(m->ctx->device);
@@ -1828,6 +1960,7 @@ int qq_generate(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, in
 int qq_forward_sample(qq_model* m, int32_t token_id, int seq_id, int pos, const qq_sample_params* params,
                       int think_done, int32_t* token_out) {
     return guard([&] {
+        need(m && m->tp_world <= 1, "qq_forward_sample: not available for a tensor-parallel model (use qq_forward / qq_forward_batch)");
         need(m && token_out, "qq_forward_sample: NULL argument");
         check_seq_pos(m, seq_id, pos, 1);
         const qq3::SampleArgs a = sample_args(params);
@@ -1843,6 +1976,7 @@ int qq_forward_sample(qq_model* m, int32_t token_id, int seq_id, int pos, const 
 int qq_generate_sample(qq_model* m, int seq_id, const int32_t* prompt, int n_prompt, int max_steps,
                        const qq_sample_params* params, int eos_id, int32_t* out_tokens, int* n_out) {
     return guard([&] {
+        need(m && m->tp_world <= 1, "qq_generate_sample: not available for a tensor-parallel model (use qq_forward / qq_forward_batch)");
         need(m && prompt && n_prompt >= 1 && max_steps >= 0 && n_out && (out_tokens || max_steps == 0),
              "qq_generate_sample: bad argument");
         check_seq_pos(m, seq_id, 0, n_prompt + max_steps);
@@ -1986,6 +2120,58 @@ int qq_model_stat(qq_model* m, int what, int64_t* value) {
         } else {
             need(false, "qq_model_stat: unknown statistic");
         }
+    });
+}
+
+int qq_decode_trace(qq_model* m, int enable, uint64_t* stamps_out, int32_t* kinds_out, int* n_phases,
+                    int* n_ctas) {
+    return guard([&] {
+        need(m && n_phases && n_ctas, "qq_decode_trace: NULL argument");
+        DeviceGuard dg(m->ctx->device);
+        need(mega_enabled(m), "qq_decode_trace: the model does not run the persistent decode step");
+        cudaStream_t s = m->ctx->stream;
+        qq_model::Prog& pr = get_prog(m, 0, true);
+        const int np = pr.n, nc = qq3::num_sms();
+        *n_phases = np;
+        *n_ctas = nc;
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        if (stamps_out && m->trace_buf)
+            QQ_CUDA_TRY(cudaMemcpy(stamps_out, m->trace_buf, sizeof(uint64_t) * (size_t)nc * (np + 1),
+                                   cudaMemcpyDeviceToHost));
+        if (kinds_out) {
+            // per phase: type | epi << 8 | (routed ? 1 << 16 : 0)
+            std::vector<qq3::PhaseDesc> host((size_t)np);
+            QQ_CUDA_TRY(cudaMemcpy(host.data(), pr.d_prog, sizeof(qq3::PhaseDesc) * np, cudaMemcpyDeviceToHost));
+            for (int i = 0; i < np; i++)
+                kinds_out[i] = host[i].type | (host[i].epi << 8) | (host[i].r_qs ? 1 << 16 : 0);
+        }
+        if (enable && !m->trace_buf) m->trace_buf = dalloc<unsigned long long>((size_t)nc * (np + 1));
+        unsigned long long* ptr = enable ? m->trace_buf : nullptr;
+        QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->trace, &ptr, sizeof(ptr), cudaMemcpyHostToDevice, s));
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+    });
+}
+
+int qq_ep_profile(qq_model* m, int enable, float* ms_out) {
+    return guard([&] {
+        need(m != nullptr, "qq_ep_profile: NULL model");
+        need(m->ep_world > 1, "qq_ep_profile: not an expert-parallel model");
+        DeviceGuard dg(m->ctx->device);
+        QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+        float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+        for (auto& ev : m->ep_evs) {
+            for (int i = 0; i < 4; i++) {
+                float v = 0.f;
+                QQ_CUDA_TRY(cudaEventElapsedTime(&v, ev[i], ev[i + 1]));
+                acc[i] += v;
+            }
+            for (auto e : ev) cudaEventDestroy(e);
+        }
+        acc[4] = (float)m->ep_evs.size();
+        m->ep_evs.clear();
+        if (ms_out)
+            for (int i = 0; i < 5; i++) ms_out[i] = acc[i];
+        m->ep_prof = enable != 0;
     });
 }
 

@@ -105,7 +105,10 @@ struct DecodeCtl {
     unsigned long long best;  // argmax key of the logits (reset by the CTA that closes the step)
     float* arena;             // accumulated vectors and counters: two halves of arena_half words
     long long arena_half;
-    unsigned int pad[24];
+    // per-phase trace (nullable): CTA c writes the %globaltimer at its start to
+    // trace[c * (n_phases + 1)] and at the end of phase ph to trace[c * (n_phases + 1) + ph + 1]
+    unsigned long long* trace;
+    unsigned int pad[22];
 };
 
 // Shared-memory plan of the persistent kernel: a byte ring of kDecRingBytes holding up to

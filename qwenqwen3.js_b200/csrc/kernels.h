@@ -180,6 +180,13 @@ void set_pdl(int on);
 // 0 forces the register-streamed kernels of kernels_gemv.cu everywhere (A/B measurements)
 void set_stream_path(int on);
 int stream_path();
+// ---- tensor-parallel greedy id over vocab shards (kernels_prefill.cu) ----
+// keys [T][32] of a vocab shard whose row 0 is global row idx0 (suppress: a shard-local id or -1)
+void launch_argmax_rows_keys(const float* logits, int T, int V, const int* suppress, int idx0, void* keys,
+                             cudaStream_t s);
+// out[t] = first global maximum over the G shards' keys [G][T][32]
+void launch_argmax_merge(const void* keys, int G, int T, int* out, cudaStream_t s);
+
 // ---- expert-parallel exchange, token side (kernels_ep.cu) ----
 // per destination rank r of W: pos[r][t] (token t's row in r's block, or -1), tok_of[r][q] (the
 // token of row q, or -1), ids[r][q][s] (owner-local expert of slot s, or -1) and wts[r][q][s]

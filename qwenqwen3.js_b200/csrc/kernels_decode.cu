@@ -61,6 +61,12 @@ __device__ __forceinline__ float ld_early_f32(const float* p) {
     return v;
 }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ uint32_t step_tag(uint32_t epoch, int ph) { return epoch * 256u + (uint32_t)ph + 1u; }
 
 __device__ __forceinline__ void st_tw(tword* p, float v, uint32_t tag) {
@@ -1375,6 +1381,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // every CTA reads the epoch before any CTA can close the step (the closing CTA is the last
     // one to finish all phases)
     const uint32_t epoch = *reinterpret_cast<const volatile unsigned int*>(&ctl->epoch);
+    unsigned long long* trace = ctl->trace ? ctl->trace + (size_t)blockIdx.x * (n_phases + 1) : nullptr;
+    if (trace && threadIdx.x == 0) trace[0] = globaltimer_ns();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDecSlots; s++) {
             mbar_init(&r.full[s], 1);
@@ -1513,6 +1521,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         // the CTA's warps leave the phase together (shared digits and scratch are reused)
         named_bar(1, kConsumerThreads);
+        if (trace && threadIdx.x == 0) trace[ph + 1] = globaltimer_ns();
     }
     // close the step: the last CTA to get here finishes the token and advances the epoch
     if (threadIdx.x == 0) {

@@ -334,7 +334,7 @@ __global__ void k_conv_rows_at(const float* __restrict__ bcx, const float* __res
 constexpr int kArgmaxThreads = 256;
 constexpr int kArgmaxParts = 32;
 __global__ void __launch_bounds__(kArgmaxThreads)
-    k_argmax_rows_part(const float* __restrict__ logits, int V, const int* __restrict__ suppress,
+    k_argmax_rows_part(const float* __restrict__ logits, int V, const int* __restrict__ suppress, int idx0,
                        unsigned long long* __restrict__ keys) {
     const int t = blockIdx.x, p = blockIdx.y;
     const int skip = suppress ? *suppress : -1;
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kArgmaxThreads)
     unsigned long long best = 0ull;
     for (int i = b + threadIdx.x; i < e; i += blockDim.x)
         if (i != skip) {
-            const unsigned long long k = argmax_key(r[i], i);
+            const unsigned long long k = argmax_key(r[i], idx0 + i);  // idx0: a vocab shard's first row
             best = k > best ? k : best;
         }
     for (int o = 16; o > 0; o >>= 1) {
@@ -476,9 +476,43 @@ void launch_argmax_rows(const float* logits, int T, int V, const int* suppress, 
                         cudaStream_t s) {
     if (T <= 0) return;
     unsigned long long* keys = static_cast<unsigned long long*>(scratch);
-    k_argmax_rows_part<<<dim3((unsigned)T, kArgmaxParts), kArgmaxThreads, 0, s>>>(logits, V, suppress, keys);
+    k_argmax_rows_part<<<dim3((unsigned)T, kArgmaxParts), kArgmaxThreads, 0, s>>>(logits, V, suppress, 0, keys);
     QQ_CUDA_TRY(cudaGetLastError());
     k_argmax_rows_final<<<(unsigned)((T * 32 + 255) / 256), 256, 0, s>>>(keys, T, out);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+namespace {
+// out[t] = the index of the largest key of row t over the G ranks' kArgmaxParts keys each
+// (keys [G][T][kArgmaxParts], rank-major as an all-gather leaves them)
+__global__ void k_argmax_merge(const unsigned long long* __restrict__ keys, int G, int T, int* __restrict__ out) {
+    const int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    unsigned long long best = 0ull;
+    for (int g = 0; g < G; g++) {
+        const unsigned long long k = keys[((size_t)g * T + t) * kArgmaxParts + lane];
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+        best = k > best ? k : best;
+    }
+    if (lane == 0) out[t] = argmax_key_index(best);
+}
+}  // namespace
+
+void launch_argmax_rows_keys(const float* logits, int T, int V, const int* suppress, int idx0, void* keys,
+                             cudaStream_t s) {
+    if (T <= 0) return;
+    k_argmax_rows_part<<<dim3((unsigned)T, kArgmaxParts), kArgmaxThreads, 0, s>>>(
+        logits, V, suppress, idx0, static_cast<unsigned long long*>(keys));
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_argmax_merge(const void* keys, int G, int T, int* out, cudaStream_t s) {
+    if (T <= 0) return;
+    k_argmax_merge<<<(unsigned)((T * 32 + 255) / 256), 256, 0, s>>>(static_cast<const unsigned long long*>(keys), G,
+                                                                     T, out);
     QQ_CUDA_TRY(cudaGetLastError());
 }
 

@@ -84,14 +84,19 @@ class _CudaEngine:
     EXPERT_TENSORS = ("ffn_gate_exps.weight", "ffn_up_exps.weight", "ffn_down_exps.weight")
 
     def __init__(self, gguf, *, ctx: rt.Context | None = None, device: int = 0, max_ctx: int | None = None,
-                 n_seq: int = 1, ep_world: int = 1):
+                 n_seq: int = 1, ep_world: int = 1, tp_world: int = 1):
         """ep_world > 1: expert parallelism -- ctx carries a communicator of ep_world ranks
         (Context.comm_init) and this engine uploads only its rank's share of every expert tensor;
-        every rank then makes the same forward calls with the same token counts."""
+        every rank then makes the same forward calls with the same token counts.
+        tp_world > 1 (dense Qwen3): tensor parallelism over the communicator's ranks -- this engine
+        uploads its rank's shards (tp.shard_model: its heads, FFN units and vocab rows); steps go
+        through forward / forward_batch, made by every rank alike."""
         self.gguf = gguf
         self.ctx = ctx or rt.Context(device)
         self.epWorld = int(ep_world)
         self.epRank = 0
+        self.tpWorld = int(tp_world)
+        self._shards = None
         self._read_hparams(gguf)
         if max_ctx is not None:
             self.maxCtx = int(max_ctx)
@@ -113,6 +118,14 @@ class _CudaEngine:
 
     # --- upload + model binding
     def _upload(self, name):
+        if self._shards is not None:  # tensor-parallel: this rank's shard of the tensor
+            if name not in self._shards:
+                return None
+            if name not in self._tensors:
+                t, ne, raw = self._shards[name]
+                up = self._uploader
+                self._tensors[name] = (up.upload if up is not None else self.ctx.upload)(raw, t, ne)
+            return self._tensors[name]
         meta = self.gguf.getTensorMetaByName(name)
         if meta is None:
             return None
@@ -143,6 +156,13 @@ class _CudaEngine:
     def _bind(self):
         if self.epWorld > 1:
             self.epRank = self.ctx.comm_rank()
+        if self.tpWorld > 1:
+            from .tp import TPPlan, shard_model
+
+            n_ff = int(self.gguf.getTensorMetaByName("blk.0.ffn_gate.weight").shape[1])
+            plan = TPPlan(self.nHeads, self.nHeadKV, self.headDim, self.nEmb, n_ff, self.nVocab, self.tpWorld,
+                          self.ctx.comm_rank())
+            self._shards = shard_model(self.gguf, plan)
         layers = (rt.LayerDesc * self.nLayers)()
         for i in range(self.nLayers):
             L = layers[i]
@@ -171,6 +191,7 @@ class _CudaEngine:
         d.output = out.h.value if out is not None else None
         d.layers = C.cast(layers, C.POINTER(rt.LayerDesc))
         d.ep_world = self.epWorld
+        d.tp_world = self.tpWorld
         up, self._uploader = self._uploader, None
         self.uploadBytes = up.finish() if up is not None else 0  # tensors are ready from here on
         self.model = rt.Model(self.ctx, d, layers, list(self._tensors.values()))

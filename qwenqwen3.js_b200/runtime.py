@@ -105,7 +105,7 @@ class ModelDesc(C.Structure):
         ("n_head_kv", C.c_int32), ("head_dim", C.c_int32), ("n_vocab", C.c_int32), ("n_expert", C.c_int32),
         ("n_expert_used", C.c_int32), ("max_ctx", C.c_int32), ("n_seq", C.c_int32), ("rms_eps", C.c_float),
         ("rope_base", C.c_double), ("tok_embd", C.c_void_p), ("output_norm", C.c_void_p), ("output", C.c_void_p),
-        ("layers", C.POINTER(LayerDesc)), ("ep_world", C.c_int32),
+        ("layers", C.POINTER(LayerDesc)), ("ep_world", C.c_int32), ("tp_world", C.c_int32),
     ]
 
 
@@ -147,6 +147,8 @@ _SIGS = {
     "qq_comm_unique_id": (_I, [_P]),
     "qq_comm_init": (_I, [_P, _P, _I, _I, _I]),
     "qq_comm_destroy": (_I, [_P]),
+    "qq_ep_profile": (_I, [_P, _I, _P]),
+    "qq_decode_trace": (_I, [_P, _I, _P, _P, C.POINTER(_I), C.POINTER(_I)]),
     "qq_upload_begin": (_I, [_P, C.c_size_t, C.POINTER(_P)]),
     "qq_upload_tensor_async": (_I, [_P, _P, C.c_size_t, _I, C.POINTER(_I64), _I, C.POINTER(_P)]),
     "qq_upload_finish": (_I, [_P, C.POINTER(C.c_size_t)]),
@@ -524,6 +526,26 @@ class Model:
         ms = C.c_float(0)
         check(self.ctx.lib.qq_bench_kernel(self.h, what, iters, C.byref(ms)))
         return ms.value
+
+    def decode_trace(self, enable: bool, read: bool = False):
+        """Switch the per-phase %globaltimer trace of the persistent step; with read, return
+        (stamps [n_ctas][n_phases + 1] ns of the last traced step, phase kinds [n_phases])."""
+        np_, nc = C.c_int(0), C.c_int(0)
+        check(self.ctx.lib.qq_decode_trace(self.h, 1 if enable else 0, None, None, C.byref(np_), C.byref(nc)))
+        if not read:
+            return None
+        st = np.zeros((nc.value, np_.value + 1), dtype=np.uint64)
+        kinds = np.zeros(np_.value, dtype=np.int32)
+        check(self.ctx.lib.qq_decode_trace(self.h, 1 if enable else 0, st.ctypes.data, kinds.ctypes.data,
+                                           C.byref(np_), C.byref(nc)))
+        return st, kinds
+
+    def ep_profile(self, enable: bool):
+        """Switch the per-exchange CUDA-event split on/off; returns the split summed since the
+        last call: dict(dispatch, experts, ret, combine) in ms and the exchange count."""
+        out = (C.c_float * 5)()
+        check(self.ctx.lib.qq_ep_profile(self.h, 1 if enable else 0, out))
+        return dict(dispatch=out[0], experts=out[1], ret=out[2], combine=out[3], exchanges=int(out[4]))
 
     def set_expert_mask(self, ids) -> None:
         ids = np.ascontiguousarray(np.asarray(sorted(ids), dtype=np.int32))
