@@ -38,6 +38,14 @@ extern "C" {
 /* ggml tensor types accepted by qq_upload_tensor (gguf.js:25-34) */
 #define QQ_TYPE_F32 0
 #define QQ_TYPE_Q8_0 8
+/* k-quants (tensor.js:267-664): 256-value superblocks of 84 / 110 / 144 / 176 / 210 bytes; kept
+ * raw on the device.  qq_dequant, qq_q8_matmul and qq_embed accept them, and a dense Qwen3 model
+ * may use them for any projection, the embedding and the lm_head (ne0 % 256 == 0). */
+#define QQ_TYPE_Q2_K 10
+#define QQ_TYPE_Q3_K 11
+#define QQ_TYPE_Q4_K 12
+#define QQ_TYPE_Q5_K 13
+#define QQ_TYPE_Q6_K 14
 
 typedef struct qq_ctx qq_ctx;
 typedef struct qq_tensor qq_tensor;

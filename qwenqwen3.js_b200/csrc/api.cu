@@ -165,6 +165,12 @@ struct qq_model {
     float* tp_logits = nullptr;
     int* tp_suppress = nullptr;
     int tp_cap = 0;
+    // a model with k-quant weights: decode steps op by op (enqueue_step_generic); its buffers:
+    // gate, up [n_ff_max] and a hidden-sized partial; greedy scratch and the step's id
+    bool generic = false;
+    float* gen_buf = nullptr;
+    void* gen_keys = nullptr;
+    int* gen_tok = nullptr;
     int mega = -1;  // -1 unknown, 0 no (a phase does not fit or disabled), 1 yes
     int64_t step_kernels = 0;  // kernel nodes in the decode-step graph (with logits)
 
@@ -191,6 +197,9 @@ void free_model(qq_model* m) {
     if (m->h_bt) cudaFreeHost(m->h_bt);
     if (m->tarena) cudaFree(m->tarena);
     if (m->ep_arena) cudaFree(m->ep_arena);
+    if (m->gen_buf) cudaFree(m->gen_buf);
+    if (m->gen_keys) cudaFree(m->gen_keys);
+    if (m->gen_tok) cudaFree(m->gen_tok);
     if (m->tp_keys) cudaFree(m->tp_keys);
     if (m->tp_logits) cudaFree(m->tp_logits);
     if (m->tp_suppress) cudaFree(m->tp_suppress);
@@ -322,9 +331,82 @@ void ep_moe(qq_model* m, const Layer& L, const float* xn, int T, const int* idx,
     }
 }
 
+// y = W . x for one row, whatever W's type (Q8_0: the streamed GEMV; k-quant: raw superblocks)
+void gemv_any(const DTensor& W, const float* x, float* y, cudaStream_t s) {
+    if (qq3::kq_block_bytes(W.type)) {
+        qq3::launch_kq_matmul(W, x, 1, y, (int)W.rows, s);
+        return;
+    }
+    qq3::XStage st;
+    st.x[0] = x;
+    st.K = (int)W.K;
+    qq3::launch_gemv_rows(W, 0, W.rows, st, y, false, s);
+}
+
+// Qwen3Engine.forward (qwen3-engine.js:115-245) op by op, for models with k-quant weights (real
+// GGUF mixes such as Q4_K_M): RMSNorm, each projection as its own matmul of whatever type the
+// tensor has, the decode attention (QK-norm, RoPE, KV append fused), SwiGLU, residual adds;
+// then the output norm, lm_head and the first-max greedy id into the control words.
+void enqueue_step_generic(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool dump) {
+    const qq_model_desc& d = m->d;
+    const int E = d.n_embd, hd = d.head_dim;
+    const int nq = d.n_head * hd, nkv = d.n_head_kv * hd;
+    float* g = m->gen_buf;
+    float* u = g + m->n_ff_max;
+    float* part = u + m->n_ff_max;
+    if (qq3::kq_block_bytes(m->tok_embd->type)) qq3::launch_kq_embed(*m->tok_embd, m->ctl, d.n_vocab, m->hidden, s);
+    else qq3::launch_embed(*m->tok_embd, m->ctl, m->hidden, nullptr, s);
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[l];
+        qq3::launch_rmsnorm(m->hidden, 1, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, m->y, s);
+        gemv_any(*L.t[QQ_WQ], m->y, m->qkv, s);
+        gemv_any(*L.t[QQ_WK], m->y, m->qkv + nq, s);
+        gemv_any(*L.t[QQ_WV], m->y, m->qkv + nq + nkv, s);
+        qq3::AttnArgs a;
+        a.qkv = m->qkv;
+        a.q_norm = L.t[QQ_Q_NORM]->f32;
+        a.k_norm = L.t[QQ_K_NORM]->f32;
+        a.rope_cs = m->rope_cs;
+        a.k_cache = m->k_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+        a.v_cache = m->v_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
+        a.out = m->attn_out;
+        a.part = m->attn_part;
+        a.counter = m->attn_counter;
+        a.pos = m->ctl + 1;
+        a.n_head = d.n_head;
+        a.n_kv = d.n_head_kv;
+        a.hd = hd;
+        a.max_ctx = d.max_ctx;
+        a.n_split = m->n_split;
+        a.eps = d.rms_eps;
+        qq3::launch_attention_decode(a, s);
+        gemv_any(*L.t[QQ_WO], m->attn_out, part, s);
+        qq3::launch_add_rows(m->hidden, part, E, s);
+        qq3::launch_rmsnorm(m->hidden, 1, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, m->y, s);
+        const size_t F = L.t[QQ_FFN_GATE]->ne[1];
+        gemv_any(*L.t[QQ_FFN_GATE], m->y, g, s);
+        gemv_any(*L.t[QQ_FFN_UP], m->y, u, s);
+        qq3::launch_swiglu_rows(g, u, F, m->h, s);
+        gemv_any(*L.t[QQ_FFN_DOWN], m->h, part, s);
+        qq3::launch_add_rows(m->hidden, part, E, s);
+        if (dump)
+            QQ_CUDA_TRY(cudaMemcpyAsync(m->dump + (size_t)l * E, m->hidden, sizeof(float) * E,
+                                        cudaMemcpyDeviceToDevice, s));
+    }
+    if (!want_logits) return;
+    qq3::launch_rmsnorm(m->hidden, 1, E, m->out_norm->f32, d.rms_eps, m->y, s);
+    gemv_any(m->output ? *m->output : *m->tok_embd, m->y, m->logits, s);
+    qq3::launch_argmax_rows(m->logits, 1, d.n_vocab, m->suppress, m->gen_keys, m->gen_tok, s);
+    qq3::launch_finish_token(m->gen_tok, m->ctl, m->trace + (size_t)seq * (d.max_ctx + 1), s);
+}
+
 // One decode step for sequence `seq` (token/position in m->ctl), as the fixed kernel
 // sequence of Qwen3Engine.forward / Lfm2Engine.forward.
 void enqueue_step(qq_model* m, int seq, bool want_logits, cudaStream_t s, bool dump) {
+    if (m->generic) {
+        enqueue_step_generic(m, seq, want_logits, s, dump);
+        return;
+    }
     const qq_model_desc& d = m->d;
     const int E = d.n_embd, hd = d.head_dim;
     const int nq = d.n_head * hd;
@@ -1276,7 +1358,7 @@ void ensure_batch_rows(qq_model* m, int T) {
 }
 
 bool batched_prefill_ok(qq_model* m) {
-    if (getenv_flag("QQ3_NO_TCGEN05")) return false;
+    if (getenv_flag("QQ3_NO_TCGEN05") || m->generic) return false;
     if (const char* v = getenv("QQ3_PREFILL_BATCH"))
         if (atoi(v) == 0) return false;
     const qq_model_desc& d = m->d;
@@ -1399,8 +1481,8 @@ int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type
     return guard([&] {
         need(ctx && host && ne && out, "qq_upload_tensor: NULL argument");
         need(n_dims >= 1 && n_dims <= 4, "qq_upload_tensor: n_dims must be 1..4");
-        QQ_CHECK(ggml_type == QQ_TYPE_F32 || ggml_type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED,
-                 "qq_upload_tensor: only F32 (0) and Q8_0 (8) tensors are supported");
+        QQ_CHECK(ggml_type == QQ_TYPE_F32 || ggml_type == QQ_TYPE_Q8_0 || qq3::kq_block_bytes(ggml_type) > 0,
+                 QQ_ERR_UNSUPPORTED, "qq_upload_tensor: F32 (0), Q8_0 (8) and Q2_K..Q6_K (10..14) tensors only");
         DTensor t;
         t.type = ggml_type;
         t.n_dims = n_dims;
@@ -1414,7 +1496,15 @@ int qq_upload_tensor(qq_ctx* ctx, const void* host, size_t nbytes, int ggml_type
         t.rows = n / t.ne[0];
         t.device = ctx->device;
         DeviceGuard dg(ctx->device);
-        if (ggml_type == QQ_TYPE_F32) {
+        if (const int bs = qq3::kq_block_bytes(ggml_type)) {
+            // k-quant superblocks stay raw (kernels_kquant.cu reads them in place)
+            need(t.ne[0] % 256 == 0, "qq_upload_tensor: k-quant tensors need ne[0] % 256 == 0");
+            const size_t bytes = (size_t)(n / 256) * bs;
+            need(nbytes >= bytes, "qq_upload_tensor: buffer shorter than the k-quant superblocks");
+            t.qs = dalloc<int8_t>(bytes + 256);
+            QQ_CUDA_TRY(cudaMemcpyAsync(t.qs, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+            QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        } else if (ggml_type == QQ_TYPE_F32) {
             need(nbytes >= (size_t)n * 4, "qq_upload_tensor: buffer shorter than ne0*ne1*... floats");
             t.f32 = dalloc<float>((size_t)n);
             // ordered on the context stream: a pageable cudaMemcpy may return before its DMA
@@ -1477,6 +1567,8 @@ int qq_dequant(const qq_tensor* t, float* out_dev) {
         if (t->t.type == QQ_TYPE_F32)
             QQ_CUDA_TRY(cudaMemcpyAsync(out_dev, t->t.f32, sizeof(float) * t->t.K * t->t.rows,
                                         cudaMemcpyDeviceToDevice, s));
+        else if (qq3::kq_block_bytes(t->t.type))
+            qq3::launch_kq_dequant(t->t, 0, t->t.rows, out_dev, s);
         else
             qq3::launch_dequant_q8(t->t, out_dev, s);
     });
@@ -1486,9 +1578,14 @@ int qq_q8_matmul(qq_ctx* ctx, const qq_tensor* W, const float* x_dev, int M, flo
     return guard([&] {
         need(ctx && W && x_dev && y_dev, "qq_q8_matmul: NULL argument");
         need(M >= 0, "qq_q8_matmul: M < 0");
-        QQ_CHECK(W->t.type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED, "qq_q8_matmul: W must be Q8_0");
+        QQ_CHECK(W->t.type == QQ_TYPE_Q8_0 || qq3::kq_block_bytes(W->t.type), QQ_ERR_UNSUPPORTED,
+                 "qq_q8_matmul: W must be Q8_0 or a k-quant");
         DeviceGuard dg(ctx->device);
         const int64_t K = W->t.ne[0], N = W->t.ne[1];
+        if (qq3::kq_block_bytes(W->t.type)) {  // k-quant: raw superblocks, CUDA-core matmul
+            qq3::launch_kq_matmul(W->t, x_dev, M, y_dev, (int)N, ctx->stream);
+            return;
+        }
         if (M >= 2 && qq3::gemm_q8_supported(W->t) && !getenv_flag("QQ3_NO_TCGEN05")) {
             // tensor cores: fp16 operands, f32 accumulation in TMEM (kernels_gemm.cu)
             const size_t xb = (qq3::gemm_q8_scratch_bytes(M, K) + 255) & ~(size_t)255;
@@ -1568,11 +1665,17 @@ int qq_attention_decode(qq_ctx* ctx, const float* q_dev, const float* k_cache_de
 int qq_embed(qq_ctx* ctx, const qq_tensor* E, const int32_t* tokens, int n, float* out_dev) {
     return guard([&] {
         need(ctx && E && tokens && out_dev && n >= 0, "qq_embed: bad argument");
-        QQ_CHECK(E->t.type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED, "qq_embed: the embedding must be Q8_0");
+        QQ_CHECK(E->t.type == QQ_TYPE_Q8_0 || qq3::kq_block_bytes(E->t.type), QQ_ERR_UNSUPPORTED,
+                 "qq_embed: the embedding must be Q8_0 or a k-quant");
         for (int i = 0; i < n; i++) need(tokens[i] >= 0 && tokens[i] < E->t.rows, "qq_embed: token id out of range");
         if (n == 0) return;
         DeviceGuard dg(ctx->device);
         cudaStream_t s = ctx->stream;
+        if (qq3::kq_block_bytes(E->t.type)) {  // embeddingLookupGeneric -> the k-quant column reader
+            for (int i = 0; i < n; i++) qq3::launch_kq_dequant(E->t, tokens[i], 1, out_dev + (size_t)i * E->t.K, s);
+            QQ_CUDA_TRY(cudaStreamSynchronize(s));
+            return;
+        }
         int* tok = static_cast<int*>(ctx_scratch(ctx, sizeof(int) * (size_t)n));
         QQ_CUDA_TRY(cudaMemcpyAsync(tok, tokens, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, s));
         qq3::launch_embed_rows(E->t, tok, n, (int)E->t.rows, out_dev, s);
@@ -1634,12 +1737,23 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
         m->d = d;
         m->d.layers = nullptr;
         try {
+            // k-quant weights (a dense Qwen3 on one GPU) run the op-by-op step: the type a check accepts
+            bool any_moe = false;
+            for (int l = 0; l < d.n_layers; l++) any_moe = any_moe || d.layers[l].is_moe;
+            const bool kq_ok = d.arch == QQ_ARCH_QWEN3 && !any_moe && G <= 1 && d.ep_world <= 1;
+            auto wt = [&](const DTensor* t) {
+                if (t && qq3::kq_block_bytes(t->type) && kq_ok) {
+                    m->generic = true;
+                    return t->type;
+                }
+                return (int)QQ_TYPE_Q8_0;
+            };
             m->tok_embd = dt(d.tok_embd);
-            check_shape(m->tok_embd, QQ_TYPE_Q8_0, E, d.n_vocab, 1, "token_embd.weight");
+            check_shape(m->tok_embd, wt(m->tok_embd), E, d.n_vocab, 1, "token_embd.weight");
             m->out_norm = dt(d.output_norm);
             check_shape(m->out_norm, QQ_TYPE_F32, E, 1, 1, "output norm");
             m->output = dt(d.output);
-            if (m->output) check_shape(m->output, QQ_TYPE_Q8_0, E, d.n_vocab / G, 1, "output.weight");
+            if (m->output) check_shape(m->output, wt(m->output), E, d.n_vocab / G, 1, "output.weight");
             m->layers.resize(d.n_layers);
             for (int l = 0; l < d.n_layers; l++) {
                 const qq_layer_desc& ld = d.layers[l];
@@ -1655,10 +1769,10 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                 check_shape(L.t[QQ_FFN_NORM], QQ_TYPE_F32, E, 1, 1, (b + "ffn_norm.weight").c_str());
                 if (L.attn) {
                     L.attn_slot = m->n_attn++;
-                    check_shape(L.t[QQ_WQ], QQ_TYPE_Q8_0, E, nq, 1, (b + "attn_q.weight").c_str());
-                    check_shape(L.t[QQ_WK], QQ_TYPE_Q8_0, E, nkv, 1, (b + "attn_k.weight").c_str());
-                    check_shape(L.t[QQ_WV], QQ_TYPE_Q8_0, E, nkv, 1, (b + "attn_v.weight").c_str());
-                    check_shape(L.t[QQ_WO], QQ_TYPE_Q8_0, nq, E, 1, (b + "attn_output.weight").c_str());
+                    check_shape(L.t[QQ_WQ], wt(L.t[QQ_WQ]), E, nq, 1, (b + "attn_q.weight").c_str());
+                    check_shape(L.t[QQ_WK], wt(L.t[QQ_WK]), E, nkv, 1, (b + "attn_k.weight").c_str());
+                    check_shape(L.t[QQ_WV], wt(L.t[QQ_WV]), E, nkv, 1, (b + "attn_v.weight").c_str());
+                    check_shape(L.t[QQ_WO], wt(L.t[QQ_WO]), nq, E, 1, (b + "attn_output.weight").c_str());
                     check_shape(L.t[QQ_Q_NORM], QQ_TYPE_F32, hd, 1, 1, (b + "attn_q_norm.weight").c_str());
                     check_shape(L.t[QQ_K_NORM], QQ_TYPE_F32, hd, 1, 1, (b + "attn_k_norm.weight").c_str());
                 } else {
@@ -1691,9 +1805,9 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                     if (d.n_expert_used * F > m->n_ff_max) m->n_ff_max = (int)(d.n_expert_used * F);
                 } else {
                     const int64_t F = L.t[QQ_FFN_GATE] ? L.t[QQ_FFN_GATE]->ne[1] : 0;
-                    check_shape(L.t[QQ_FFN_GATE], QQ_TYPE_Q8_0, E, F, 1, (b + "ffn_gate.weight").c_str());
-                    check_shape(L.t[QQ_FFN_UP], QQ_TYPE_Q8_0, E, F, 1, (b + "ffn_up.weight").c_str());
-                    check_shape(L.t[QQ_FFN_DOWN], QQ_TYPE_Q8_0, F, E, 1, (b + "ffn_down.weight").c_str());
+                    check_shape(L.t[QQ_FFN_GATE], wt(L.t[QQ_FFN_GATE]), E, F, 1, (b + "ffn_gate.weight").c_str());
+                    check_shape(L.t[QQ_FFN_UP], wt(L.t[QQ_FFN_UP]), E, F, 1, (b + "ffn_up.weight").c_str());
+                    check_shape(L.t[QQ_FFN_DOWN], wt(L.t[QQ_FFN_DOWN]), F, E, 1, (b + "ffn_down.weight").c_str());
                     need(F % 32 == 0, "FFN width must be a multiple of 32");
                     if (F > m->n_ff_max) m->n_ff_max = (int)F;
                 }
@@ -1713,6 +1827,12 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
                 m->ep_xn = dalloc<float>(E);
             }
             m->n_expert_local = d.n_expert / std::max(m->ep_world, 1);
+            if (m->generic) {
+                m->mega = 0;
+                m->gen_buf = dalloc<float>(2 * (size_t)std::max(m->n_ff_max, 32) + E);
+                m->gen_keys = dmalloc(qq3::argmax_rows_scratch_bytes(1));
+                m->gen_tok = dalloc<int>(1);
+            }
             m->n_split = qq3::attention_splits(d.max_ctx);
             m->rec_len = 2 * d.n_expert_used + d.n_expert;
             m->hidden = dalloc<float>(E);

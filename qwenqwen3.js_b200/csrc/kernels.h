@@ -180,6 +180,17 @@ void set_pdl(int on);
 // 0 forces the register-streamed kernels of kernels_gemv.cu everywhere (A/B measurements)
 void set_stream_path(int on);
 int stream_path();
+// ---- k-quant weights, raw superblocks in DTensor::qs (kernels_kquant.cu) ----
+int kq_block_bytes(int type);  // 0 for a type that is not a k-quant
+// rows [row0, row0 + n_rows) dequantised bit-exactly (the reference's f64 value rounded to f32)
+void launch_kq_dequant(const DTensor& W, int64_t row0, int64_t n_rows, float* out, cudaStream_t s);
+// y[m][n] = W[n] . x[m] for m < M (x [M][K], 16-byte aligned), y row stride ldy
+void launch_kq_matmul(const DTensor& W, const float* x, int M, float* y, int ldy, cudaStream_t s);
+// out[0..K) = the embedding row of the token *tok_dev (k-quant column reader)
+void launch_kq_embed(const DTensor& W, const int* tok_dev, int n_vocab, float* out, cudaStream_t s);
+// ctl = [*tok, ctl[1] + 1], trace[ctl[1]] = *tok (a decode step's last word)
+void launch_finish_token(const int* tok, int* ctl, int* trace, cudaStream_t s);
+
 // ---- tensor-parallel greedy id over vocab shards (kernels_prefill.cu) ----
 // keys [T][32] of a vocab shard whose row 0 is global row idx0 (suppress: a shard-local id or -1)
 void launch_argmax_rows_keys(const float* logits, int T, int V, const int* suppress, int idx0, void* keys,

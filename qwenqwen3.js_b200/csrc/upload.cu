@@ -105,8 +105,8 @@ extern "C" int qq_upload_tensor_async(qq_uploader* u, const void* host, size_t n
     return guard([&] {
         need(u && u->stream && host && ne && out, "qq_upload_tensor_async: NULL argument or finished uploader");
         need(n_dims >= 1 && n_dims <= 4, "qq_upload_tensor_async: n_dims must be 1..4");
-        QQ_CHECK(ggml_type == QQ_TYPE_F32 || ggml_type == QQ_TYPE_Q8_0, QQ_ERR_UNSUPPORTED,
-                 "qq_upload_tensor_async: only F32 (0) and Q8_0 (8) tensors are supported");
+        QQ_CHECK(ggml_type == QQ_TYPE_F32 || ggml_type == QQ_TYPE_Q8_0 || qq3::kq_block_bytes(ggml_type) > 0,
+                 QQ_ERR_UNSUPPORTED, "qq_upload_tensor_async: F32 (0), Q8_0 (8) and Q2_K..Q6_K (10..14) only");
         DTensor t;
         t.type = ggml_type;
         t.n_dims = n_dims;
@@ -121,7 +121,13 @@ extern "C" int qq_upload_tensor_async(qq_uploader* u, const void* host, size_t n
         t.device = u->ctx->device;
         DeviceGuard dg(u->ctx->device);
         size_t total;
-        if (ggml_type == QQ_TYPE_F32) {
+        const int kbs = qq3::kq_block_bytes(ggml_type);
+        if (kbs) {  // k-quant superblocks stay raw: DMA'd straight to their destination
+            need(t.ne[0] % 256 == 0, "qq_upload_tensor_async: k-quant tensors need ne[0] % 256 == 0");
+            total = (size_t)(n / 256) * kbs;
+            need(nbytes >= total, "qq_upload_tensor_async: buffer shorter than the k-quant superblocks");
+            QQ_CUDA_TRY(cudaMalloc(&t.qs, total + 256));
+        } else if (ggml_type == QQ_TYPE_F32) {
             total = (size_t)n * 4;
             need(nbytes >= total, "qq_upload_tensor_async: buffer shorter than ne0*ne1*... floats");
             QQ_CUDA_TRY(cudaMalloc(&t.f32, total));
@@ -143,9 +149,9 @@ extern "C" int qq_upload_tensor_async(qq_uploader* u, const void* host, size_t n
                 const size_t slot = u->next++ % kUploadSlots;
                 QQ_CUDA_TRY(cudaEventSynchronize(u->done[slot]));  // the slot's previous chunk is consumed
                 par_copy(u->pinned[slot], src + off, len);
-                if (ggml_type == QQ_TYPE_F32) {
-                    QQ_CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(t.f32) + off, u->pinned[slot], len,
-                                                cudaMemcpyHostToDevice, u->stream));
+                if (ggml_type == QQ_TYPE_F32 || kbs) {
+                    uint8_t* dst = kbs ? reinterpret_cast<uint8_t*>(t.qs) : reinterpret_cast<uint8_t*>(t.f32);
+                    QQ_CUDA_TRY(cudaMemcpyAsync(dst + off, u->pinned[slot], len, cudaMemcpyHostToDevice, u->stream));
                 } else {
                     QQ_CUDA_TRY(cudaMemcpyAsync(u->draw[slot], u->pinned[slot], len, cudaMemcpyHostToDevice, u->stream));
                     const int64_t b0 = (int64_t)(off / 34);
