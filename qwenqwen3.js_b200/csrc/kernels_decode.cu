@@ -1413,6 +1413,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
     uint32_t i = 0;  // ring position, advanced exactly as the producer advances it
     for (int ph = 0; ph < n_phases; ph++) {
+        // the previous phase is over for this CTA (also when it skipped that phase)
+        if (trace && threadIdx.x == 0 && ph > 0) trace[ph] = globaltimer_ns();
         const PhaseDesc& p = prog[ph];
         const uint32_t tag = step_tag(epoch, ph);
         if (p.type == PH_EMBED) {
@@ -1521,8 +1523,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         // the CTA's warps leave the phase together (shared digits and scratch are reused)
         named_bar(1, kConsumerThreads);
-        if (trace && threadIdx.x == 0) trace[ph + 1] = globaltimer_ns();
     }
+    if (trace && threadIdx.x == 0) trace[n_phases] = globaltimer_ns();
     // close the step: the last CTA to get here finishes the token and advances the epoch
     if (threadIdx.x == 0) {
         __threadfence();

@@ -40,10 +40,10 @@ __global__ void __launch_bounds__(kGemvThreads)
     const int nch = K >> 4;
     for (int e = warp; e < n_expert; e += kGemvWarps) {
         float acc = 0.f;
-        if (rf) {  // F32 router row: lane-strided float4 dot
+        if (rf) {  // F32 router row: lane-strided float4 dot (stage_x keeps float4 c at (c & 3) * nch + c / 4)
             const float4* row = reinterpret_cast<const float4*>(rf + (size_t)e * K);
             for (int c = lane; c < (K >> 2); c += 32) {
-                const float4 a = __ldg(row + c), b = xs[c];
+                const float4 a = __ldg(row + c), b = xs[(c & 3) * nch + (c >> 2)];
                 acc = fmaf(a.x, b.x, fmaf(a.y, b.y, fmaf(a.z, b.z, fmaf(a.w, b.w, acc))));
             }
         } else {
