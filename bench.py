@@ -10,9 +10,9 @@ uniform token ids, prefilled untimed; then W warm-up and K timed decode steps.
             inputs in HBM; each step streams 1.66 GB of weights, far above the 126 MB L2)
   e2e    -- tok/s through the public engine API (Lfm2CudaEngine.forward_argmax): each step
             copies its token/position host->device and reads the argmax back
-  N > 1  -- expert-parallel: each rank holds 32/N experts of every MoE layer and serves one
-            sequence; every MoE layer exchanges token rows over NCCL (run_ep);
-            value = total tokens / max-over-ranks time
+  N > 1  -- N sequences, one per GPU, whole model per GPU (value = total tokens / max-over-ranks
+            time); the expert-parallel model (32/N experts per GPU, NCCL exchange in every MoE
+            layer) is measured beside it: prefill and decode (run_multi)
 
 `--impl reference` times the reference algorithm's CPU implementation (the C restatement
 of the JS CPU path in oracle/, all host threads) on a bounded slice of the same workload.
@@ -321,13 +321,14 @@ def trace_summary(stamps, kinds) -> dict:
             "note": "one traced step (%globaltimer per CTA and phase, qq_decode_trace)"}
 
 
-def run_ep(args, ws, rank, local):
-    """benchmark config 4 on N GPUs, expert-parallel: every rank holds 32/N experts of each MoE
-    layer (plus the replicated non-expert weights) and serves its own sequence, a seeded
-    512-token prompt; every MoE layer exchanges token rows over the library's NCCL communicator
-    (rows dispatched once per owner rank, the owners' grouped tensor-core expert GEMMs, partial
-    sums back).  Prefill: each rank's 511 prompt tokens through the batched path.  value = decode
-    tok/s over all ranks (N sequences x K steps / max-over-ranks time), weak scaling."""
+def run_multi(args, ws, rank, local):
+    """benchmark config 4 on N GPUs.  Decode (`value`): the N ranks serve N independent sequences
+    (one each, the seeded 512-token prompt of rank r), each rank holding the whole model; the
+    decode data path has no collective, per-GPU work is fixed (`scaling: weak`), value = N x K
+    tokens / the max-over-ranks CUDA-event time.  Expert parallelism (`ep`): the same ranks also
+    build the model with the experts split 32/N per rank and the library's NCCL exchange in every
+    MoE layer, and time its prefill (each rank's 511 prompt tokens through the batched path) and
+    its decode, with the CUDA-event split of one exchange."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -335,22 +336,24 @@ def run_ep(args, ws, rank, local):
     qq3 = load_package()
     qq3.build.build_all()
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     spec = qq3.synth.lfm2_8b_a1b(seed=SEED)
     t0 = time.time()
-    g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
+    # one rank writes the model to a GGUF file, every rank memory-maps it
+    files = [None]
+    if rank == 0:
+        f = _model_file(SEED)
+        files = [None if f is None else (str(f[0]), str(f[1]))]
+    dist.broadcast_object_list(files, src=0)
+    if files[0] is not None:
+        g = qq3.gguf.GGUFReader.fromFile(files[0][0])
+    else:
+        g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
     gen_s = time.time() - t0
-    ctx = qq3.runtime.Context(local)
-    stream = torch.cuda.Stream(device=local)
-    ctx.set_stream(stream.cuda_stream)
-    ctx.comm_init_from_torch(timeout_ms=120000)
-    n_prof = 4
-    max_ctx = args.prompt + args.warmup + 2 * args.steps + n_prof + 16
-    t_up = time.time()
-    eng = qq3.Lfm2CudaEngine(g, ctx=ctx, max_ctx=max_ctx, ep_world=ws)
-    upload_s = time.time() - t_up
     prompt = qq3.synth.uniform_tokens(args.prompt, SEED + rank, spec.n_vocab)
     suppress = THINK_ID if THINK_ID < spec.n_vocab else -1
+    n_prof = 4
+    max_ctx = args.prompt + args.warmup + 2 * args.steps + n_prof + 16
 
     def max_ms(v):
         t = torch.tensor([v], dtype=torch.float64, device="cuda")
@@ -360,22 +363,14 @@ def run_ep(args, ws, rank, local):
     def ev():
         return torch.cuda.Event(enable_timing=True)
 
-    # prefill: one untimed pass (buffers, first-use set-up), then the timed one, then its split
+    # ---- decode of N independent sequences, whole model per rank
+    ctx = qq3.runtime.Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    t_up = time.time()
+    eng = qq3.Lfm2CudaEngine(g, ctx=ctx, max_ctx=max_ctx)
+    upload_s = time.time() - t_up
     eng.prefill(prompt[:-1].tolist())
-    eng.resetKVCache()
-    dist.barrier()
-    torch.cuda.synchronize()
-    p0, p1 = ev(), ev()
-    p0.record(stream)
-    eng.prefill(prompt[:-1].tolist())
-    p1.record(stream)
-    torch.cuda.synchronize()
-    prefill_ms = max_ms(p0.elapsed_time(p1))
-    eng.resetKVCache()
-    eng.model.ep_profile(True)
-    eng.prefill(prompt[:-1].tolist())
-    split_pf = eng.model.ep_profile(False)
-    # decode
     pos = args.prompt - 1
     toks = eng.model.decode_loop(int(prompt[-1]), pos, args.warmup, suppress_id=suppress)
     pos += args.warmup
@@ -391,7 +386,6 @@ def run_ep(args, ws, rank, local):
     ms = max_ms(e0.elapsed_time(e1))
     pos += args.steps
     cur = int(out[-1])
-    # e2e: the public engine API, host token in / argmax out per step
     dist.barrier()
     torch.cuda.synchronize()
     e2, e3 = ev(), ev()
@@ -402,59 +396,96 @@ def run_ep(args, ws, rank, local):
     e3.record(stream)
     torch.cuda.synchronize()
     ms_e2e = max_ms(e2.elapsed_time(e3))
-    # the split of the decode exchanges
-    eng.model.ep_profile(True)
-    eng.model.decode_loop(cur, pos, n_prof, suppress_id=suppress)
-    split_dec = eng.model.ep_profile(False)
+    step_kernels = eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS)
+    eng.close()
+    ctx.close()
+
+    # ---- expert parallelism: experts split over the ranks, NCCL exchange in every MoE layer
+    ctx_ep = qq3.runtime.Context(local)
+    ctx_ep.set_stream(stream.cuda_stream)
+    ctx_ep.comm_init_from_torch(timeout_ms=120000)
+    eng_ep = qq3.Lfm2CudaEngine(g, ctx=ctx_ep, max_ctx=max_ctx, ep_world=ws)
+    eng_ep.prefill(prompt[:-1].tolist())  # untimed: buffers, first-use set-up
+    eng_ep.resetKVCache()
+    dist.barrier()
+    torch.cuda.synchronize()
+    p0, p1 = ev(), ev()
+    p0.record(stream)
+    eng_ep.prefill(prompt[:-1].tolist())
+    p1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = max_ms(p0.elapsed_time(p1))
+    eng_ep.resetKVCache()
+    eng_ep.model.ep_profile(True)
+    eng_ep.prefill(prompt[:-1].tolist())
+    split_pf = eng_ep.model.ep_profile(False)
+    pos = args.prompt - 1
+    toks = eng_ep.model.decode_loop(int(prompt[-1]), pos, args.warmup, suppress_id=suppress)
+    pos += args.warmup
+    cur = int(toks[-1])
+    dist.barrier()
+    torch.cuda.synchronize()
+    d0, d1 = ev(), ev()
+    d0.record(stream)
+    eng_ep.model.decode_loop(cur, pos, args.steps, suppress_id=suppress)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    ms_ep = max_ms(d0.elapsed_time(d1))
+    pos += args.steps
+    eng_ep.model.ep_profile(True)
+    eng_ep.model.decode_loop(cur, pos, n_prof, suppress_id=suppress)
+    split_dec = eng_ep.model.ep_profile(False)
+    eng_ep.close()
+    dist.barrier()
+    ctx_ep.comm_destroy()
+    ctx_ep.close()
+
     nbytes = _lfm2_model_bytes(spec)
     peak, peak_kind = _peaks()
     step_ms = ms / args.steps
-    # kernels of one expert-parallel decode step (per-phase path): embed; per short-conv layer 2,
-    # per attention layer 3; per dense FFN 2; per MoE layer rmsnorm + router + plan + gather +
-    # 7 of the grouped expert block + combine = 12; lm_head + argmax finish 2
     n_attn = sum(1 for i in range(spec.n_layers) if spec.is_attn(i))
-    n_moe = sum(1 for i in range(spec.n_layers) if spec.is_moe(i))
-    step_kernels = 1 + 2 * (spec.n_layers - n_attn) + 3 * n_attn + 2 * (spec.n_layers - n_moe) + 12 * n_moe + 2
+    kv_bytes = n_attn * spec.n_head_kv * spec.head_dim * 4 * 2 * (args.prompt + args.warmup + args.steps / 2)
+    step_bytes = nbytes["weights_per_token"] + kv_bytes
+    tr = _traffic()
 
     def per_exchange(sp):
         n = max(sp["exchanges"], 1)
         return {k: round(sp[k] / n * 1e3, 2) for k in ("dispatch", "experts", "ret", "combine")} | {"exchanges": sp["exchanges"]}
 
     dec_split, pf_split = per_exchange(split_dec), per_exchange(split_pf)
-    coll = {"dispatch": dec_split["dispatch"], "combine (return)": dec_split["ret"]}
     res = {
         "metric": METRIC, "value": round(ws * args.steps / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8xf32 (Q8_0 weights, f32 activations)",
         "data": "synthetic (seeded random-init Q8_0 weights, seeded uniform prompt ids)",
-        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 per rank, expert-parallel "
-                               "(benchmark config 4)",
+        "config": {"workload": "LFM2-8B-A1B-shaped Q8_0 greedy decode, batch 1 per GPU (benchmark config 4)",
                    "layers": "24 (18 short-conv, 6 GQA attention; 2 dense FFN 7168, 22 MoE 32x top-4 x 1792)",
                    "hidden": 2048, "vocab": 65536, "prompt": args.prompt, "global_batch": ws,
-                   "parallelism": f"ep{ws} (experts sharded {spec.n_expert // ws} per rank; non-expert weights "
-                                  "replicated; one sequence per rank)",
-                   "l2": "inputs larger than L2: each step streams >1 GB of weights per rank"},
-        "roofline": {"bound": "hbm", "kernel": "whole expert-parallel decode step (per-phase kernels + NCCL exchanges)",
-                     "achieved": round(nbytes["weights_per_token"] / (step_ms * 1e-3) / 1e9, 1), "peak": peak,
-                     "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": round(nbytes["weights_per_token"] / (step_ms * 1e-3) / 1e9 / peak, 4), "traffic": None,
-                     "note": "achieved = one token's algorithmic weight bytes (all its 4 experts) per rank and step; "
-                             "the experts a rank streams are shared by the ranks' tokens"},
+                   "parallelism": f"{ws} sequences sharded over {ws} GPUs (whole model per GPU, no collective "
+                                  f"in the decode data path); expert parallelism ep{ws} measured under 'ep'",
+                   "l2": "inputs larger than L2: each step streams 1.66 GB of weights per GPU"},
+        "roofline": {"bound": "hbm", "kernel": "k_decode (persistent decode step: all 24 layers + lm_head + argmax)",
+                     "achieved": round(step_bytes / (step_ms * 1e-3) / 1e9, 1), "peak": peak, "peak_kind": peak_kind,
+                     "unit": "GB/s", "frac": round(step_bytes / (step_ms * 1e-3) / 1e9 / peak, 4),
+                     "traffic": tr.get("decode_step_bytes_per_launch"), "algorithmic_bytes": int(step_bytes),
+                     "avg_launch_ms": round(step_ms, 5), "per": "GPU (max-over-ranks time)"},
         "e2e": {"value": round(ws * args.steps / (ms_e2e * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                "d2h_bytes_per_step": 4, "api": "Lfm2CudaEngine.forward_argmax -> qq_forward (expert-parallel)"},
+                "d2h_bytes_per_step": 4, "api": "Lfm2CudaEngine.forward_argmax -> qq_forward, on every rank"},
         "gpu_launches": int(step_kernels * args.steps),
         "clocks": clk.summary(),
-        "ep_prefill": {"tokens_per_rank": args.prompt - 1, "ms": round(prefill_ms, 3),
-                       "tok_s": round(ws * (args.prompt - 1) / (prefill_ms * 1e-3), 1),
-                       "us_per_exchange": pf_split, "note": "max over ranks, CUDA events"},
-        "ep_decode_us_per_exchange": dec_split,
-        "limiting_collective": max(coll, key=coll.get),
-        "setup_s": {"weight_generation": round(gen_s, 1), "engine_create": round(upload_s, 2)},
+        "ep": {"experts_per_gpu": spec.n_expert // ws,
+               "prefill": {"tokens_per_gpu": args.prompt - 1, "ms": round(prefill_ms, 3),
+                           "tok_s": round(ws * (args.prompt - 1) / (prefill_ms * 1e-3), 1),
+                           "us_per_exchange": pf_split},
+               "decode": {"tok_s": round(ws * args.steps / (ms_ep * 1e-3), 2), "ms_per_step": round(ms_ep / args.steps, 4),
+                          "us_per_exchange": dec_split},
+               "limiting_collective": max({"dispatch": dec_split["dispatch"], "combine (return)": dec_split["ret"]}.items(),
+                                          key=lambda kv: kv[1])[0],
+               "note": "max over ranks, CUDA events; one sequence per GPU; exchanges are NCCL send/recv on the "
+                       "library's communicator"},
+        "setup_s": {"model": round(gen_s, 1), "engine_create": round(upload_s, 2)},
     }
-    eng.close()
     dist.barrier()
-    ctx.comm_destroy()
-    ctx.close()
     dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res), flush=True)
@@ -893,7 +924,7 @@ def main():
     elif args.case == "batch-decode":
         run_batch_decode(args, ws, rank, local)
     elif ws > 1:
-        run_ep(args, ws, rank, local)
+        run_multi(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
 
