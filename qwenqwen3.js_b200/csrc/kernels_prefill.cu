@@ -15,8 +15,20 @@
 // forward() step of several independent sequences at once, plus k_argmax_rows (sampleGreedy per
 // row) for their greedy ids.
 #include "kernels.h"
+#include "pipe.cuh"
 
 namespace qq3 {
+
+// QQ3_ATTN_TILE=0 keeps the per-warp global-memory attention kernels (A/B measurements)
+static bool tiled_attention_off() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QQ3_ATTN_TILE");
+        v = (e && atoi(e) == 0) ? 1 : 0;
+    }
+    return v == 1;
+}
+
 
 namespace {
 
@@ -225,6 +237,133 @@ __global__ void k_attn_prefill(const float* __restrict__ q, const float* __restr
                  pos0 + t + 1, out + ((size_t)t * n_head + h) * HD);
 }
 
+// Causal attention of a prompt chunk by query tiles (flash-attention form on the CUDA cores, f32):
+// CTA (query tile, kv head) takes 64 query rows -- kPfTok = 64 / G consecutive tokens x the G query
+// heads of the kv head, 16 rows per warp -- and walks the keys 0 .. (its last token's position) in
+// tiles of 32: K is staged transposed (Kt[d][j], rows padded to 33), V as rows, each warp's queries
+// transposed (Qs[d][r]); a lane scores its key against the warp's 16 rows (one K word and four
+// broadcast float4 of queries per 16 FMAs), an online softmax per row, then a lane accumulates its
+// HD/32 output dims of the 16 rows over the tile's 32 keys (the probabilities broadcast from
+// shared memory).  Each K/V tile is read once per 64 query rows instead of once per query.
+constexpr int kPfWarps = 4, kPfRows = 16, kPfKeys = 32;
+
+template <int HD>
+__global__ void __launch_bounds__(kPfWarps * 32)
+    k_attn_prefill_tile(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int T,
+                        int pos0, int n_head, int n_kv, int max_ctx, float* __restrict__ out) {
+    constexpr int PL = HD / 32, H4 = HD / 4, KP = kPfKeys + 1;
+    extern __shared__ __align__(16) float smf[];
+    float* Kt = smf;                                    // [HD][KP]
+    float* Vs = Kt + HD * KP;                           // [kPfKeys][HD]
+    float* Qs = Vs + kPfKeys * HD;                      // [warp][HD][kPfRows]
+    float* Ps = Qs + kPfWarps * HD * kPfRows;           // [warp][kPfKeys][kPfRows]
+    const int G = n_head / n_kv;
+    const int QT = (kPfWarps * kPfRows) / G;            // tokens per tile
+    const int t0 = blockIdx.x * QT, kvh = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* qw = Qs + warp * HD * kPfRows;
+    float* pw = Ps + warp * kPfKeys * kPfRows;
+    // this warp's rows r = 16 warp + i: token t0 + r / G, head kvh G + r % G
+    for (int i = 0; i < kPfRows; i++) {
+        const int r = warp * kPfRows + i, t = t0 + r / G;
+        const float* qr = q + ((size_t)t * n_head + kvh * G + r % G) * HD;
+        for (int d = lane; d < HD; d += 32) qw[d * kPfRows + i] = t < T ? qr[d] : 0.f;
+    }
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    float m[kPfRows], l[kPfRows], acc[kPfRows][PL];
+#pragma unroll
+    for (int i = 0; i < kPfRows; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < PL; j++) acc[i][j] = 0.f;
+    }
+    const int t_last = min(T, t0 + QT) - 1;
+    const int n_keys = pos0 + t_last + 1;  // keys 0 .. the tile's last position
+    const float* kb = kc + (size_t)kvh * max_ctx * HD;
+    const float* vb = vc + (size_t)kvh * max_ctx * HD;
+    for (int k0 = 0; k0 < n_keys; k0 += kPfKeys) {
+        __syncthreads();  // the previous tile's K / V are no longer read
+        for (int f = threadIdx.x; f < kPfKeys * H4; f += kPfWarps * 32) {
+            const int j = f / H4, d = (f % H4) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (k0 + j < n_keys) {
+                kv = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(k0 + j) * HD + d));
+                vv = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(k0 + j) * HD + d));
+            }
+            Kt[(d + 0) * KP + j] = kv.x;
+            Kt[(d + 1) * KP + j] = kv.y;
+            Kt[(d + 2) * KP + j] = kv.z;
+            Kt[(d + 3) * KP + j] = kv.w;
+            *reinterpret_cast<float4*>(Vs + j * HD + d) = vv;
+        }
+        __syncthreads();
+        // scores of key k0 + lane against the warp's rows
+        float sc[kPfRows];
+#pragma unroll
+        for (int i = 0; i < kPfRows; i++) sc[i] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < HD; d++) {
+            const float kv = Kt[d * KP + lane];
+            const float4* q4 = reinterpret_cast<const float4*>(qw + d * kPfRows);
+#pragma unroll
+            for (int c = 0; c < kPfRows / 4; c++) {
+                const float4 qv = q4[c];
+                sc[4 * c] = fmaf(qv.x, kv, sc[4 * c]);
+                sc[4 * c + 1] = fmaf(qv.y, kv, sc[4 * c + 1]);
+                sc[4 * c + 2] = fmaf(qv.z, kv, sc[4 * c + 2]);
+                sc[4 * c + 3] = fmaf(qv.w, kv, sc[4 * c + 3]);
+            }
+        }
+        const int key = k0 + lane;
+#pragma unroll
+        for (int i = 0; i < kPfRows; i++) {
+            const int r = warp * kPfRows + i, t = t0 + r / G;
+            const bool live = t < T && key <= pos0 + t;  // causal: keys up to the row's own position
+            const float s = live ? sc[i] * scale : -INFINITY;
+            const float mx = warp_max(s);
+            const float m_new = fmaxf(m[i], mx);
+            const float p = (live && m_new > -INFINITY) ? expf(s - m_new) : 0.f;
+            const float cf = m_new > -INFINITY ? expf(m[i] - m_new) : 1.f;
+            l[i] = l[i] * cf + warp_sum(p);
+            m[i] = m_new;
+#pragma unroll
+            for (int j = 0; j < PL; j++) acc[i][j] *= cf;
+            pw[lane * kPfRows + i] = p;
+        }
+        __syncwarp();
+        // values: lane's HD/32 dims of the warp's rows over the tile's keys
+        const int nk = min(kPfKeys, n_keys - k0);
+        for (int jj = 0; jj < nk; jj++) {
+            const float4* p4 = reinterpret_cast<const float4*>(pw + jj * kPfRows);
+            float vv[PL];
+#pragma unroll
+            for (int j = 0; j < PL; j++) vv[j] = Vs[jj * HD + lane * PL + j];
+#pragma unroll
+            for (int c = 0; c < kPfRows / 4; c++) {
+                const float4 pv = p4[c];
+#pragma unroll
+                for (int j = 0; j < PL; j++) {
+                    acc[4 * c][j] = fmaf(pv.x, vv[j], acc[4 * c][j]);
+                    acc[4 * c + 1][j] = fmaf(pv.y, vv[j], acc[4 * c + 1][j]);
+                    acc[4 * c + 2][j] = fmaf(pv.z, vv[j], acc[4 * c + 2][j]);
+                    acc[4 * c + 3][j] = fmaf(pv.w, vv[j], acc[4 * c + 3][j]);
+                }
+            }
+        }
+        __syncwarp();  // pw is rewritten by the next tile
+    }
+#pragma unroll
+    for (int i = 0; i < kPfRows; i++) {
+        const int r = warp * kPfRows + i, t = t0 + r / G;
+        if (t >= T) continue;
+        float* o = out + ((size_t)t * n_head + kvh * G + r % G) * HD + lane * PL;
+        const float inv = 1.f / l[i];
+#pragma unroll
+        for (int j = 0; j < PL; j++) o[j] = acc[i][j] * inv;
+    }
+}
+
 // ---- multi-sequence decode rows: row t is sequence seq[t] at position pos[t] ----------------
 // (one forward() step of each of T independent sequences; the caches of sequence s start at
 // seq_stride * s floats from the layer's base pointer)
@@ -279,6 +418,104 @@ __global__ void k_attn_rows_split(const float* __restrict__ q, const float* __re
     const size_t base = (size_t)seq[t] * seq_stride + (size_t)kvh * max_ctx * HD;
     attn_row_part<HD>(q + ((size_t)t * n_head + h) * HD, kc + base, vc + base, b, e,
                       part + (((size_t)t * n_head + h) * n_split + sp) * (HD + 2));
+}
+
+// The same split over positions with the split's K and V rows staged once per CTA: one 1-D bulk
+// copy each (a kv head's positions are contiguous, [pos][HD] f32) into shared memory, completing on
+// an mbarrier; the G warps (query heads of the kv head) then score and accumulate from shared
+// memory.  Lane l scores position p0 + l reading the K row's float4s in a lane-rotated order
+// ((i + l) mod HD/4), so a quarter-warp's loads fall in distinct bank groups; the query sits in
+// shared memory read in the same order.  The V pass reads one row per step, lane l its HD/32 dims.
+// Chunk = attn_rows_chunk() positions; numerics as attn_row_part (f32 dots in another order).
+template <int HD>
+__global__ void __launch_bounds__(256)
+    k_attn_rows_tile(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                     const int* __restrict__ seq, const int* __restrict__ pos, size_t seq_stride, int n_head, int n_kv,
+                     int max_ctx, int chunk, int n_split, float* __restrict__ part, int* err) {
+    constexpr int PL = HD / 32, H4 = HD / 4;
+    extern __shared__ __align__(128) uint8_t sm_raw[];
+    float* ks = reinterpret_cast<float*>(sm_raw);
+    float* vs = ks + (size_t)chunk * HD;
+    float* qs = vs + (size_t)chunk * HD;
+    __shared__ __align__(8) uint64_t bar;
+    const int t = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
+    const int G = n_head / n_kv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int len = pos[t] + 1;
+    const int b = sp * chunk, e = min(len, b + chunk), n_pos = e - b;
+    const size_t base = (size_t)seq[t] * seq_stride + (size_t)kvh * max_ctx * HD;
+    if (n_pos > 0 && threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (n_pos > 0 && threadIdx.x == 0) {
+        const uint32_t bytes = (uint32_t)n_pos * HD * 4u;
+        mbar_arrive_expect_tx(&bar, 2u * bytes);
+        bulk_g2s(ks, kc + base + (size_t)b * HD, bytes, &bar);
+        bulk_g2s(vs, vc + base + (size_t)b * HD, bytes, &bar);
+    }
+    if (warp >= G) return;  // (the copies are waited for by the warps that read them)
+    const int h = kvh * G + warp;
+    float* out = part + (((size_t)t * n_head + h) * n_split + sp) * (HD + 2);
+    if (n_pos <= 0) {  // a split past this row's length: an empty state
+        for (int j = lane; j < HD; j += 32) out[j] = 0.f;
+        if (lane == 0) {
+            out[HD] = -INFINITY;
+            out[HD + 1] = 0.f;
+        }
+        return;
+    }
+    float* qw = qs + warp * HD;
+    const float* qg = q + ((size_t)t * n_head + h) * HD;
+    for (int j = lane; j < HD; j += 32) qw[j] = qg[j];
+    __syncwarp();
+    bool ok = mbar_wait(&bar, 0u);
+    if (!ok) set_err(err, kErrFullWait);
+    ok = __all_sync(0xffffffffu, ok);
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    float m = -INFINITY, l = 0.f, acc[PL];
+#pragma unroll
+    for (int j = 0; j < PL; j++) acc[j] = 0.f;
+    const float4* q4 = reinterpret_cast<const float4*>(qw);
+    for (int p0 = 0; ok && p0 < n_pos; p0 += 32) {
+        const int pl_i = p0 + lane;
+        float s = -INFINITY;
+        if (pl_i < n_pos) {
+            const float4* k4 = reinterpret_cast<const float4*>(ks + (size_t)pl_i * HD);
+            float dot = 0.f;
+#pragma unroll 8
+            for (int i = 0; i < H4; i++) {
+                const int ii = (i + lane) & (H4 - 1);
+                const float4 kv = k4[ii], qv = q4[ii];
+                dot = fmaf(qv.x, kv.x, dot);
+                dot = fmaf(qv.y, kv.y, dot);
+                dot = fmaf(qv.z, kv.z, dot);
+                dot = fmaf(qv.w, kv.w, dot);
+            }
+            s = dot * scale;
+        }
+        const float m_new = fmaxf(m, warp_max(s));
+        const float pl = pl_i < n_pos ? expf(s - m_new) : 0.f;
+        const float cf = expf(m - m_new);
+        l = l * cf + warp_sum(pl);
+#pragma unroll
+        for (int j = 0; j < PL; j++) acc[j] *= cf;
+        const int n = min(32, n_pos - p0);
+        for (int jj = 0; jj < n; jj++) {
+            const float pj = __shfl_sync(0xffffffffu, pl, jj);
+            const float* vr = vs + (size_t)(p0 + jj) * HD + lane * PL;
+#pragma unroll
+            for (int j = 0; j < PL; j++) acc[j] = fmaf(pj, vr[j], acc[j]);
+        }
+        m = m_new;
+    }
+#pragma unroll
+    for (int j = 0; j < PL; j++) out[lane * PL + j] = acc[j];
+    if (lane == 0) {
+        out[HD] = m;
+        out[HD + 1] = l;
+    }
 }
 
 // one warp per (row, head): lane owns HD/32 output dims
@@ -410,6 +647,29 @@ void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T
                          int hd, int max_ctx, float* out, cudaStream_t s) {
     const int G = n_head / n_kv;
     QQ_CHECK(G >= 1 && G <= 32 && n_head % n_kv == 0, -4, "prefill attention: unsupported head grouping");
+    if (T <= 0) return;
+    if (G <= kPfWarps * kPfRows && (kPfWarps * kPfRows) % G == 0 && !tiled_attention_off()) {
+        // query tiles: K / V read once per 64 query rows (k_attn_prefill_tile)
+        const int QT = kPfWarps * kPfRows / G;
+        dim3 grid((unsigned)((T + QT - 1) / QT), (unsigned)n_kv);
+        const size_t smem = ((size_t)hd * (kPfKeys + 1) + (size_t)kPfKeys * hd + (size_t)kPfWarps * hd * kPfRows +
+                             (size_t)kPfWarps * kPfKeys * kPfRows) * sizeof(float);
+        if (hd == 64) {
+            if (first_use_on_device(reinterpret_cast<const void*>(k_attn_prefill_tile<64>)))
+                QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_prefill_tile<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem));
+            k_attn_prefill_tile<64><<<grid, kPfWarps * 32, smem, s>>>(q, kc, vc, T, pos0, n_head, n_kv, max_ctx, out);
+        } else if (hd == 128) {
+            if (first_use_on_device(reinterpret_cast<const void*>(k_attn_prefill_tile<128>)))
+                QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_prefill_tile<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem));
+            k_attn_prefill_tile<128><<<grid, kPfWarps * 32, smem, s>>>(q, kc, vc, T, pos0, n_head, n_kv, max_ctx, out);
+        } else {
+            QQ_CHECK(false, -4, "prefill attention: head_dim must be 64 or 128");
+        }
+        QQ_CUDA_TRY(cudaGetLastError());
+        return;
+    }
     dim3 grid((unsigned)T, (unsigned)n_kv);
     if (hd == 64) k_attn_prefill<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, pos0, n_head, n_kv, max_ctx, out);
     else if (hd == 128) k_attn_prefill<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, pos0, n_head, n_kv, max_ctx, out);
@@ -431,6 +691,8 @@ void launch_kv_append_at(const float* k, const float* v, int T, int n_kv, int hd
 
 int attn_rows_chunk() { return 64; }
 
+
+
 size_t attn_rows_part_floats(int T, int n_head, int hd, int max_ctx) {
     const int n_split = (max_ctx + attn_rows_chunk() - 1) / attn_rows_chunk();
     return (size_t)T * n_head * n_split * (hd + 2);
@@ -448,14 +710,34 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
     // empty state, and the merge reads only the splits that hold positions of its row
     dim3 grid((unsigned)T, (unsigned)n_kv, (unsigned)((max_len + chunk - 1) / chunk));
     const unsigned mg = (unsigned)(((size_t)T * n_head * 32 + 255) / 256);
+    // K and V of a split staged in shared memory once for the G query heads (k_attn_rows_tile),
+    // up to 8 heads per kv head; the per-warp global-memory form otherwise
+    const bool tile = G <= 8 && !tiled_attention_off();
+    const size_t smem = ((size_t)2 * chunk + G) * hd * sizeof(float);
     if (hd == 64) {
-        k_attn_rows_split<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, chunk,
-                                                      n_split, part);
+        if (tile) {
+            if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<64>)))
+                QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_rows_tile<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem));
+            k_attn_rows_tile<64><<<grid, 32 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
+                                                            chunk, n_split, part, kernel_err_ptr());
+        } else {
+            k_attn_rows_split<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, chunk,
+                                                          n_split, part);
+        }
         QQ_CUDA_TRY(cudaGetLastError());
         k_attn_merge<64><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out);
     } else if (hd == 128) {
-        k_attn_rows_split<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, chunk,
-                                                       n_split, part);
+        if (tile) {
+            if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<128>)))
+                QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_rows_tile<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem));
+            k_attn_rows_tile<128><<<grid, 32 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
+                                                             chunk, n_split, part, kernel_err_ptr());
+        } else {
+            k_attn_rows_split<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
+                                                           chunk, n_split, part);
+        }
         QQ_CUDA_TRY(cudaGetLastError());
         k_attn_merge<128><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out);
     } else {
