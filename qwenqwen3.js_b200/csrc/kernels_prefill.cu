@@ -714,11 +714,14 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
     // up to 8 heads per kv head; the per-warp global-memory form otherwise
     const bool tile = G <= 8 && !tiled_attention_off();
     const size_t smem = ((size_t)2 * chunk + G) * hd * sizeof(float);
+    // the attribute is set once per device, to the largest size any head grouping needs (G = 8):
+    // a launch may not ask for more dynamic shared memory than the attribute allows
+    const size_t smem_max = ((size_t)2 * chunk + 8) * hd * sizeof(float);
     if (hd == 64) {
         if (tile) {
             if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<64>)))
                 QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_rows_tile<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem));
+                                                 (int)smem_max));
             k_attn_rows_tile<64><<<grid, 32 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
                                                             chunk, n_split, part, kernel_err_ptr());
         } else {
@@ -731,7 +734,7 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
         if (tile) {
             if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<128>)))
                 QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_rows_tile<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)smem));
+                                                 (int)smem_max));
             k_attn_rows_tile<128><<<grid, 32 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
                                                              chunk, n_split, part, kernel_err_ptr());
         } else {
