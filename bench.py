@@ -218,18 +218,25 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     ms_e2e = e2.elapsed_time(e3)
 
-    # ---- optional per-phase trace of the persistent step (--trace): critical-path time per phase kind
+    # ---- per-phase trace of one step of the persistent kernel (after the timed regions): the
+    # MoE-layer HBM rate of the shipped path (bytes of one routed FFN phase / its critical-path
+    # time); with --trace the whole breakdown goes into the line
     phase_trace = None
-    if args.trace and eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS) == 1:
+    if eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS) == 1:
         eng.model.decode_trace(True)
         eng.model.decode_loop(cur, pos, 4, seq=1, suppress_id=suppress, want_tokens=False)
         stamps, kinds = eng.model.decode_trace(False, read=True)
-        phase_trace = trace_summary(stamps, kinds)
+        phase_trace = trace_summary(stamps, kinds, eng.model.decode_trace_sub())
 
     # ---- dominant kernel (expert gate/up GEMV) and whole MoE layer, timed alone over all layers
     nbytes = _lfm2_model_bytes(spec)
     ms_gateup = eng.model.bench_kernel(qq3.runtime.QQ_KERN_MOE_GATEUP, 3)
     ms_layer = eng.model.bench_kernel(qq3.runtime.QQ_KERN_MOE_LAYER, 3)
+    moe_persist_gbs = moe_persist_us = None
+    routed = (phase_trace or {}).get("by_kind", {}).get("fused/store/routed")
+    if routed:
+        moe_persist_us = routed["crit_us_per_phase"]
+        moe_persist_gbs = round(nbytes["moe_layer"] / (moe_persist_us * 1e-6) / 1e9, 1)
     step_kernels = eng.model.stat(qq3.runtime.QQ_STAT_STEP_KERNELS)
 
     if dist:
@@ -268,18 +275,22 @@ def run_ours(args, ws, rank, local):
                    "hidden": 2048, "vocab": 65536, "prompt": args.prompt, "global_batch": ws,
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
                    "l2": "inputs larger than L2: each step streams 1.66 GB of weights"},
-        # one MoE layer (router, gate/up, down) as separate kernels, timed alone over all 22 layers
-        "moe_layer_hbm_gbs": round(nbytes["moe_layer"] / (ms_layer * 1e-3) / 1e9, 1),
+        # one MoE layer (router, gate/up, down, combine) as one phase of the persistent step: its
+        # algorithmic bytes / its critical-path time in a traced step
+        "moe_layer_hbm_gbs": moe_persist_gbs,
+        "moe_layer_us": moe_persist_us,
+        # the same layer as separate kernels, timed alone over all 22 layers
+        "moe_layer_kernels_hbm_gbs": round(nbytes["moe_layer"] / (ms_layer * 1e-3) / 1e9, 1),
         "moe_gateup_kernel_gbs": round(nbytes["gateup"] / (ms_gateup * 1e-3) / 1e9, 1),
         "step_weight_gbs_per_gpu": round(nbytes["weights_per_token"] * args.steps / (ms * 1e-3) / 1e9, 1),
         "roofline": roof,
-        "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+        "e2e": {"value": round(e2e_tok_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 12,
                 "api": "Lfm2CudaEngine.forward_argmax -> qq_forward"},
         "gpu_launches": int(step_kernels * args.steps),
         "clocks": clk.summary(),
         "prefill": {"tokens": args.prompt - 1, "ms": round(prefill_s * 1e3, 2),
                     "tok_s": round((args.prompt - 1) / prefill_s, 1), "note": "untimed setup, host wall clock"},
-        "phase_trace": phase_trace,
+        "phase_trace": phase_trace if args.trace else None,
         "setup_s": {"weight_generation": round(gen_s, 1), "engine_create": round(upload_s, 2),
                     "weight_upload_gbs": round(eng.uploadBytes / upload_s / 1e9, 2),
                     "note": "engine_create = streamed upload of the raw GGUF bytes (pinned ring) + model binding"},
@@ -298,27 +309,51 @@ PHASE_TYPES = {0: "embed", 1: "gemv", 2: "down4", 3: "attention", 4: "finish", 5
 EPI_KINDS = {0: "store", 1: "resid", 2: "swiglu", 3: "conv", 4: "argmax"}
 
 
-def trace_summary(stamps, kinds) -> dict:
+SUB_POINTS = ("input", "staged", "routed", "first_stage", "part1", "part2", "reduced", "published",
+              "route_stage", "route_dots", "prod_routed", "prod_issue")
+
+
+def trace_summary(stamps, kinds, sub=None) -> dict:
     """Critical path of a traced persistent step: per phase, the end of its last CTA minus the end
-    of the previous phase's last CTA, summed per phase kind (type/epilogue[/routed])."""
+    of the previous phase's last CTA, summed per phase kind (type/epilogue[/routed]).  With the
+    sub-stamps, `timeline_us` gives per kind the time of each point of a phase (input wait over,
+    staged, routed, first weight stage, first / second part done, reduction performed, output
+    published) and of the phase end, measured from the end of the previous phase's last CTA:
+    the median and the maximum over the CTAs that reach it, averaged over the phases of the kind."""
     stamps = stamps.astype(np.int64)
     t0 = int(stamps[:, 0].min())
     ends = stamps[:, 1:].max(axis=0) - t0
     out: dict = {}
+    acc: dict = {}
     prev = 0
     for ph, k in enumerate(kinds):
         label = f"{PHASE_TYPES.get(int(k) & 255, '?')}/{EPI_KINDS.get((int(k) >> 8) & 255, '?')}" + \
                 ("/routed" if (int(k) >> 16) & 1 else "")
         crit = int(ends[ph]) - prev
-        prev = int(ends[ph])
         e = out.setdefault(label, {"count": 0, "crit_us": 0.0})
         e["count"] += 1
         e["crit_us"] += crit / 1e3
-    for e in out.values():
+        if sub is not None:
+            a = acc.setdefault(label, {})
+            pts = [(name, sub[:, ph, j].astype(np.int64)) for j, name in enumerate(SUB_POINTS)]
+            pts.append(("end", stamps[:, ph + 1]))
+            for name, col in pts:
+                v = col[col > t0] - t0 - prev  # stamps of earlier steps are older than t0
+                if v.size:
+                    r = a.setdefault(name, [0.0, 0.0, 0])
+                    r[0] += float(np.median(v)) / 1e3
+                    r[1] += float(v.max()) / 1e3
+                    r[2] += 1
+        prev = int(ends[ph])
+    for label, e in out.items():
         e["crit_us_per_phase"] = round(e["crit_us"] / e["count"], 2)
         e["crit_us"] = round(e["crit_us"], 1)
+        if label in acc:
+            e["timeline_us"] = {name: [round(r[0] / r[2], 2), round(r[1] / r[2], 2)]
+                                for name, r in acc[label].items()}
     return {"step_us": round(int(ends[-1]) / 1e3, 1), "by_kind": out,
-            "note": "one traced step (%globaltimer per CTA and phase, qq_decode_trace)"}
+            "note": "one traced step (%globaltimer per CTA and phase, qq_decode_trace; timeline_us: "
+                    "[median, max] over CTAs of each point, from the end of the previous phase)"}
 
 
 def run_multi(args, ws, rank, local):
@@ -474,7 +509,7 @@ def run_multi(args, ws, rank, local):
                      "traffic": tr.get("decode_step_bytes_per_launch"), "algorithmic_bytes": int(step_bytes),
                      "avg_launch_ms": round(step_ms, 5), "per": "GPU (max-over-ranks time)"},
         "e2e": {"value": round(ws * args.steps / (ms_e2e * 1e-3), 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
-                "d2h_bytes_per_step": 4, "api": "Lfm2CudaEngine.forward_argmax -> qq_forward, on every rank"},
+                "d2h_bytes_per_step": 12, "api": "Lfm2CudaEngine.forward_argmax -> qq_forward, on every rank"},
         "gpu_launches": int(step_kernels * args.steps),
         "clocks": clk.summary(),
         "ep": {"experts_per_gpu": spec.n_expert // ws,

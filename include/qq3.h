@@ -309,6 +309,14 @@ int qq_decode_loop(qq_model* m, int seq_id, int first_token, int pos0, int n_ste
  * stamps_out (nullable) receives the stamps of the last traced step, [n_ctas][n_phases + 1] ns;
  * kinds_out (nullable, n_phases ints) each phase's type | epilogue << 8 | routed << 16. */
 int qq_decode_trace(qq_model* m, int enable, uint64_t* stamps_out, int32_t* kinds_out, int* n_phases, int* n_ctas);
+/* Sub-phase stamps of the last traced step: out (nullable) receives [n_ctas][n_phases][*n_sub] ns
+ * stamps of thread 0 of each CTA at fixed points of a phase (0 where a phase does not reach one):
+ * 0 input wait over, 1 input staged, 2 token routed, 3 first weight stage landed, 4 first part
+ * done (gate/up + SwiGLU; all GEMV rows; attention keys), 5 second part done (down / out_proj),
+ * 6 bulk reduction performed (attention: split counter taken), 7 output published, 8 router stage
+ * landed, 9 router logits complete, 10 the producer thread saw the routing, 11 the producer thread
+ * issued the phase's first weight stage. */
+int qq_decode_trace_sub(qq_model* m, uint64_t* out, int* n_sub);
 /* Expert-parallel models: switch the CUDA-event split of every MoE exchange on (enable = 1) or
  * off, and read (ms_out, nullable, 5 floats) the time summed since the last call over the
  * exchanges recorded: [dispatch (plan + gather + NCCL send/recv), experts (owner GEMMs),

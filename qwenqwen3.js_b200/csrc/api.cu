@@ -108,13 +108,14 @@ struct qq_model {
     int* ridx = nullptr;
     float* rw = nullptr;
     uint32_t* mask = nullptr;
-    int* ctl = nullptr;       // [token, pos]
+    int* ctl = nullptr;       // [token, pos, error word copy, pad]: the persistent step's token
     int* suppress = nullptr;  // [1]
     unsigned long long* best = nullptr;
     float* dump = nullptr;    // [n_layers][n_embd] for qq_forward_dump
     int* h_ctl = nullptr;     // pinned staging [2 * h_ctl_cap]
     size_t h_ctl_cap = 0;
     int* h_small = nullptr;   // pinned [8]: suppress id, argmax, token, pos, kernel error word, think flag
+    int* h_io = nullptr;      // pinned [8]: one host step's token, pos in; argmax, pos, error word out
     int suppress_set = INT32_MIN;  // the suppress id last copied to the device
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
     cudaStream_t cap = nullptr;
@@ -224,6 +225,7 @@ void free_model(qq_model* m) {
         if (p) cudaFree(p);
     if (m->h_ctl) cudaFreeHost(m->h_ctl);
     if (m->h_small) cudaFreeHost(m->h_small);
+    if (m->h_io) cudaFreeHost(m->h_io);
     if (m->h_sargs) cudaFreeHost(m->h_sargs);
     if (m->cap) cudaStreamDestroy(m->cap);
 }
@@ -929,6 +931,36 @@ cudaGraphExec_t get_graph(qq_model* m, int seq, bool want_logits) {
     cudaGraphDestroy(g);
     QQ_CUDA_TRY(e);
     if (mega) m->step_kernels = 1;
+    m->graphs[key] = ge;
+    return ge;
+}
+
+// One host-driven greedy step of the persistent kernel as one graph (key (seq, 3)): the token
+// and position copied in from h_io[0..1], the step, and the argmax token, the next position and the
+// kernel error word (which the step's closing CTA copies into ctl[2]) copied out to h_io[2..4], so
+// that a step is one launch and one synchronisation.
+cudaGraphExec_t get_io_graph(qq_model* m, int seq) {
+    auto key = std::make_pair(seq, 3);
+    auto it = m->graphs.find(key);
+    if (it != m->graphs.end()) return it->second;
+    qq_model::Prog& pr = get_prog(m, seq, true);
+    cudaGraph_t g = nullptr;
+    QQ_CUDA_TRY(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeRelaxed));
+    try {
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->ctl, m->h_io, 2 * sizeof(int), cudaMemcpyHostToDevice, m->cap));
+        qq3::launch_decode_step(pr.d_prog, pr.n, m->dctl, qq3::kernel_err_ptr(), m->cap);
+        QQ_CUDA_TRY(cudaMemcpyAsync(m->h_io + 2, m->ctl, 3 * sizeof(int), cudaMemcpyDeviceToHost, m->cap));
+    } catch (...) {
+        cudaStreamEndCapture(m->cap, &g);
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        throw;
+    }
+    QQ_CUDA_TRY(cudaStreamEndCapture(m->cap, &g));
+    cudaGraphExec_t ge = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    QQ_CUDA_TRY(e);
     m->graphs[key] = ge;
     return ge;
 }
@@ -1879,13 +1911,14 @@ int qq_model_create(qq_ctx* ctx, const qq_model_desc* desc, qq_model** out) {
             QQ_CUDA_TRY(cudaMemsetAsync(m->ridx, 0, sizeof(int) * nm * std::max(d.n_expert_used, 1), ctx->stream));
             m->mask = dalloc<uint32_t>(8);
             QQ_CUDA_TRY(cudaMemsetAsync(m->mask, 0, 32, ctx->stream));
-            m->ctl = dalloc<int>(2);
-            QQ_CUDA_TRY(cudaMemsetAsync(m->ctl, 0, 8, ctx->stream));
+            m->ctl = dalloc<int>(4);
+            QQ_CUDA_TRY(cudaMemsetAsync(m->ctl, 0, 16, ctx->stream));
             m->suppress = dalloc<int>(1);
             QQ_CUDA_TRY(cudaMemsetAsync(m->suppress, 0xff, 4, ctx->stream));
             m->best = dalloc<unsigned long long>(1);
             m->dump = dalloc<float>((size_t)d.n_layers * E);
             QQ_CUDA_TRY(cudaMallocHost(&m->h_small, 8 * sizeof(int)));
+            QQ_CUDA_TRY(cudaMallocHost(&m->h_io, 8 * sizeof(int)));
             QQ_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking));
             QQ_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
         } catch (...) {
@@ -1916,6 +1949,19 @@ int qq_forward(qq_model* m, const int32_t* token_ids, int n_tokens, int seq_id, 
         cudaStream_t s = m->ctx->stream;
         const bool logits = want_logits != 0;
         if (logits) set_suppress(m, suppress_id);
+        if (n_tokens == 1 && logits && !logits_out && argmax_out && m->tp_world <= 1 && m->ep_world <= 1 &&
+            mega_enabled(m)) {
+            // one greedy token of the persistent step: one graph launch and one synchronisation
+            need(token_ids[0] >= 0 && token_ids[0] < m->d.n_vocab, "token id out of range");
+            cudaGraphExec_t ge = get_io_graph(m, seq_id);
+            m->h_io[0] = token_ids[0];
+            m->h_io[1] = pos0;
+            QQ_CUDA_TRY(cudaGraphLaunch(ge, s));
+            QQ_CUDA_TRY(cudaStreamSynchronize(s));
+            if (m->h_io[4]) check_kernel_error(s);  // reads the word again, clears it and throws
+            *argmax_out = m->h_io[2];
+            return;
+        }
         run_tokens(m, token_ids, n_tokens, seq_id, pos0, logits);
         if (m->tp_world > 1) {
             if (logits && logits_out) tp_logits_to_host(m, 1, logits_out);
@@ -2265,10 +2311,32 @@ int qq_decode_trace(qq_model* m, int enable, uint64_t* stamps_out, int32_t* kind
             for (int i = 0; i < np; i++)
                 kinds_out[i] = host[i].type | (host[i].epi << 8) | (host[i].r_qs ? 1 << 16 : 0);
         }
-        if (enable && !m->trace_buf) m->trace_buf = dalloc<unsigned long long>((size_t)nc * (np + 1));
-        unsigned long long* ptr = enable ? m->trace_buf : nullptr;
-        QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->trace, &ptr, sizeof(ptr), cudaMemcpyHostToDevice, s));
+        // phase stamps [nc][np + 1], then the sub-stamps [nc][np][kSubStamps] (zeroed: a point a
+        // phase does not reach reads 0)
+        const size_t n_main = (size_t)nc * (np + 1), n_sub = (size_t)nc * np * qq3::kSubStamps;
+        if (enable && !m->trace_buf) m->trace_buf = dalloc<unsigned long long>(n_main + n_sub);
+        if (enable) QQ_CUDA_TRY(cudaMemsetAsync(m->trace_buf + n_main, 0, sizeof(uint64_t) * n_sub, s));
+        unsigned long long* ptrs[2] = {enable ? m->trace_buf : nullptr, enable ? m->trace_buf + n_main : nullptr};
+        static_assert(offsetof(qq3::DecodeCtl, sub) == offsetof(qq3::DecodeCtl, trace) + sizeof(void*),
+                      "trace and sub pointers are adjacent");
+        QQ_CUDA_TRY(cudaMemcpyAsync(&m->dctl->trace, ptrs, sizeof(ptrs), cudaMemcpyHostToDevice, s));
         QQ_CUDA_TRY(cudaStreamSynchronize(s));
+    });
+}
+
+int qq_decode_trace_sub(qq_model* m, uint64_t* out, int* n_sub) {
+    return guard([&] {
+        need(m && n_sub, "qq_decode_trace_sub: NULL argument");
+        DeviceGuard dg(m->ctx->device);
+        need(mega_enabled(m), "qq_decode_trace_sub: the model does not run the persistent decode step");
+        qq_model::Prog& pr = get_prog(m, 0, true);
+        const int np = pr.n, nc = qq3::num_sms();
+        *n_sub = qq3::kSubStamps;
+        if (!out) return;
+        need(m->trace_buf != nullptr, "qq_decode_trace_sub: no traced step (qq_decode_trace)");
+        QQ_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+        QQ_CUDA_TRY(cudaMemcpy(out, m->trace_buf + (size_t)nc * (np + 1),
+                               sizeof(uint64_t) * (size_t)nc * np * qq3::kSubStamps, cudaMemcpyDeviceToHost));
     });
 }
 

@@ -36,7 +36,8 @@ enum MapKind : int { MK_ROWS = 0, MK_CONCAT3 = 1, MK_PAIR = 2, MK_STRIDE3 = 3, M
 
 enum EpiKind : int { EK_STORE = 0, EK_RESID = 1, EK_SWIGLU = 2, EK_CONV = 3, EK_ARGMAX = 4 };
 
-struct PhaseDesc {
+// 16-byte aligned and sized: the persistent kernel copies descriptors into shared memory
+struct alignas(16) PhaseDesc {
     int type, map, epi, S;
     int K;        // inner dimension (input length)
     int n_items;  // outputs of the phase
@@ -98,6 +99,8 @@ struct PhaseDesc {
     int pad3;
 };
 
+static_assert(sizeof(PhaseDesc) % 16 == 0, "phase descriptors are copied in 16-byte units");
+
 // Control block of the persistent kernel, one per model (shared by all its programs).
 struct DecodeCtl {
     unsigned int epoch;       // steps run; tags of the current step derive from it
@@ -108,8 +111,28 @@ struct DecodeCtl {
     // per-phase trace (nullable): CTA c writes the %globaltimer at its start to
     // trace[c * (n_phases + 1)] and at the end of phase ph to trace[c * (n_phases + 1) + ph + 1]
     unsigned long long* trace;
-    unsigned int pad[22];
+    // per-phase sub-stamps (nullable): thread 0 of CTA c writes %globaltimer at the points of
+    // DecSub to sub[(c * n_phases + ph) * kSubStamps + k]; a point a phase does not reach is left
+    unsigned long long* sub;
+    unsigned int pad[20];
 };
+
+// Points of a phase that the sub-stamps record (for thread 0 of each CTA).
+enum DecSub : int {
+    SUB_INPUT = 0,      // its input wait is over (the counter complete, or its tagged words carry the tag)
+    SUB_STAGED = 1,     // the input is staged (RMSNorm, digits) and the CTA's warps met
+    SUB_ROUTED = 2,     // the CTA has routed the token (routed FFN phases)
+    SUB_FIRST = 3,      // the first weight stage of the phase has landed (thread 0's set)
+    SUB_PART1 = 4,      // the first part is done: gate/up + SwiGLU (fused), all rows (GEMV), the keys (attention)
+    SUB_PART2 = 5,      // the down / out_proj stages are done (fused)
+    SUB_REDUCED = 6,    // the bulk reduction is performed (fused); the split counter is taken (attention)
+    SUB_PUBLISHED = 7,  // the counter is raised (fused); the merged head outputs are written (attention)
+    SUB_ROUTE_STAGE = 8,  // the first router stage of thread 0's set has landed (routed phases)
+    SUB_ROUTE_DOTS = 9,   // the router logits are complete (routed phases)
+    SUB_PROD_ROUTED = 10, // the producer thread has seen the routing (routed phases)
+    SUB_PROD_ISSUE = 11,  // the producer thread has issued the phase's first weight stage
+};
+constexpr int kSubStamps = 12;
 
 // Shared-memory plan of the persistent kernel: a byte ring of kDecRingBytes holding up to
 // kDecSlots in-flight stages of any size (so bytes in flight fill the ring whatever the phase),

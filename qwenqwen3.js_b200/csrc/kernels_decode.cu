@@ -55,6 +55,11 @@ __device__ __forceinline__ float4 ld_early_f4(const float* p) {
     asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
     return v;
 }
+__device__ __forceinline__ uint32_t ld_early_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ float ld_early_f32(const float* p) {
     float v;
     asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
@@ -65,6 +70,14 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
+}
+
+// The sub-stamps of the current phase of this CTA (thread 0 only sets and reads it; null when
+// the step is not traced).
+__shared__ unsigned long long* s_sub;
+
+__device__ __forceinline__ void sub_stamp(int k) {
+    if (threadIdx.x == 0 && s_sub) s_sub[k] = globaltimer_ns();
 }
 
 __device__ __forceinline__ uint32_t step_tag(uint32_t epoch, int ph) { return epoch * 256u + (uint32_t)ph + 1u; }
@@ -140,6 +153,18 @@ __device__ __forceinline__ void wait_cnt(const unsigned* c, unsigned n, int* err
     set_err(err, 4);
 }
 
+// Count one arrival with release semantics (this thread's earlier writes, and those ordered
+// before it by a CTA barrier, are visible to a reader that acquires the count).
+__device__ __forceinline__ void red_release_add(unsigned* c, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(c), "r"(v) : "memory");
+}
+// The same as an acquire-release read-modify-write that returns the previous count.
+__device__ __forceinline__ unsigned atom_acq_rel_add(unsigned* c, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(c), "r"(v) : "memory");
+    return old;
+}
+
 // The hidden units [u0, u1) of the fused MoE phase this CTA owns: the U = top_k * N units of
 // the routed experts (slot-major) split into nearly equal runs of whole quads.
 __device__ __forceinline__ void moe_range(int U, int& u0, int& u1) {
@@ -168,6 +193,7 @@ struct DecRing {
 // Routing of the current MoE layer, computed by the CTA itself (shared memory).
 struct DecRoute {
     int id[4];
+    int skip[4];  // the expert of slot s is masked (its rows are skipped)
     float w[4];
     float logit[kMaxRoutes];
     uint64_t bar;  // completes once per MoE layer: the producer may read id[]
@@ -332,7 +358,7 @@ __device__ __forceinline__ int ffn_expert(const PhaseDesc* pp, const DecRoute* r
     return pp->r_qs ? route->id[s] : 0;
 }
 __device__ __forceinline__ bool ffn_skip(const PhaseDesc* pp, const DecRoute* route, int s) {
-    return pp->r_qs && dec_masked(pp->mask, route->id[s]);
+    return pp->r_qs && route->skip[s];
 }
 
 // First-part sources of a fused phase: the SwiGLU form (an FFN) dots a unit's gate and up rows,
@@ -348,7 +374,7 @@ __device__ __forceinline__ int64_t fused_row(const PhaseDesc* pp, int src, int e
 // the transposed second matrix (down, or out_proj) with the block scales they need (kMoeDU
 // units a stage).  A masked expert's stages carry no bytes.
 __device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing& r, const DecRoute* route,
-                                              ProdRing& pr, uint64_t pol, int* err) {
+                                              ProdRing& pr, uint64_t pol, int* err, unsigned long long* sub) {
     const int K = pp->K, N = pp->N, EO = pp->n_out;
     const int S = fused_sources(pp), G = fused_stage_units(S);
     const bool conv = pp->epi == EK_CONV;
@@ -377,6 +403,7 @@ __device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing
                 weight_g2s(sb + S * qsz + src * dsz, d + row * KS, db, &r.full[slot], pol);
             }
         }
+        if (sub && u == u0) sub[SUB_PROD_ISSUE] = globaltimer_ns();
         u += n;
     }
     const uint32_t dq = (uint32_t)kMoeDU * EO, need2 = (dq + 4u * EO + 127u) & ~127u;
@@ -400,12 +427,28 @@ __device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing
     return true;
 }
 
-__device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, DecRoute* route, int* err) {
+// The producer's descriptors: phase ph in pdesc[ph & 1], copied by one bulk copy completing on
+// pbar[ph & 1], the copy of phase ph + 1 issued once phase ph's has landed.
+__device__ __forceinline__ void pdesc_fetch(const PhaseDesc* prog, int ph, PhaseDesc* pdesc, uint64_t* pbar) {
+    // the buffer was last read by this thread's generic loads (phase ph - 2): order them before
+    // the async-proxy write
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&pbar[ph & 1], (uint32_t)sizeof(PhaseDesc));
+    bulk_g2s(&pdesc[ph & 1], prog + ph, (uint32_t)sizeof(PhaseDesc), &pbar[ph & 1]);
+}
+
+__device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, DecRoute* route, PhaseDesc* pdesc,
+                             uint64_t* pbar, unsigned long long* sub, int* err) {
     ProdRing pr;
     const uint64_t pol = l2_policy_evict_first();
     uint32_t routed = 0;  // MoE layers whose routing this CTA has seen
+    int desc_landed = 0;  // descriptor copies waited for (one more may be in flight)
+    pdesc_fetch(prog, 0, pdesc, pbar);
     for (int ph = 0; ph < n_phases; ph++) {
-        const PhaseDesc* pp = prog + ph;
+        if (!slot_wait(&pbar[ph & 1], (uint32_t)(ph >> 1) & 1u, err)) goto drain;
+        desc_landed = ph + 1;
+        if (ph + 1 < n_phases) pdesc_fetch(prog, ph + 1, pdesc, pbar);
+        const PhaseDesc* pp = &pdesc[ph & 1];
         if (!streamed(pp->type)) continue;
         const bool ex = expert_map(pp->map);
         if (pp->r_qs && (pp->map == MK_EXPERT_PAIR || pp->type == PH_FUSED)) {  // a phase with a router
@@ -431,13 +474,16 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                     if (p2->type == PH_GEMV) budget = prefetch_phase_l2(p2, budget);
                 }
             }
-            // Wait for this CTA's routing.  (Pulling the next layer's rows into L2 meanwhile was
-            // measured slower: it competes with the expert rows for DRAM right after routing.)
+            // Wait for this CTA's routing.  (Pulling the rows of the next phase into L2 meanwhile,
+            // from the moment the phase's input is there, was measured slower: 706 -> 732 us per
+            // step; the copies compete with the expert rows and the next phase's own stream.)
             if (!slot_wait(&route->bar, routed & 1u, err, kProducerBackoffNs)) goto drain;
             ++routed;
+            if (sub) sub[(size_t)ph * kSubStamps + SUB_PROD_ROUTED] = globaltimer_ns();
         }
+        const uint32_t i_first = pr.i;  // the phase's first weight stage (stamped once issued)
         if (pp->type == PH_FUSED) {
-            if (!fused_produce(pp, r, route, pr, pol, err)) goto drain;
+            if (!fused_produce(pp, r, route, pr, pol, err, sub ? sub + (size_t)ph * kSubStamps : nullptr)) goto drain;
             continue;
         }
         {
@@ -468,13 +514,17 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                     weight_g2s(sb + s * qsz, q[s], qb, &r.full[slot], pol);
                     weight_g2s(sb + S * qsz + s * dsz, d[s], db, &r.full[slot], pol);
                 }
+                if (sub && pr.i == i_first) sub[(size_t)ph * kSubStamps + SUB_PROD_ISSUE] = globaltimer_ns();
             }
         }
     }
     return;
 drain:
-    // abort: let every copy already issued land before the CTA exits (bounded)
-    for (uint32_t j = pr.tail; j < pr.i; ++j) slot_wait(&r.full[j % kDecSlots], (j / kDecSlots) & 1u, err);
+    // abort: let every copy already issued land before the CTA exits (bounded by the poll limit,
+    // not cut short by the error word, which is set by now)
+    for (uint32_t j = pr.tail; j < pr.i; ++j) mbar_wait(&r.full[j % kDecSlots], (j / kDecSlots) & 1u);
+    if (desc_landed < n_phases)  // the descriptor copy in flight
+        mbar_wait(&pbar[desc_landed & 1], (uint32_t)(desc_landed >> 1) & 1u);
 }
 
 // ---- consumer helpers --------------------------------------------------------------------
@@ -528,7 +578,10 @@ __device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ no
     }
     if (in.rcnt && t == 0) wait_cnt(in.rcnt, in.rn, err);  // the barrier after staging publishes it
     if (in.xa) {
-        if (t == 0) wait_cnt(in.cnt, in.n, err);
+        if (t == 0) {
+            wait_cnt(in.cnt, in.n, err);
+            sub_stamp(SUB_INPUT);
+        }
         named_bar(1, kConsumerThreads);
 #pragma unroll
         for (int ps = 0; ps < 4; ps++) {
@@ -557,6 +610,7 @@ __device__ void dec_stage_digits(const StageIn& in, const float* __restrict__ no
                 for (int e = 0; e < 8; e++) xv[ps][e] = 0.f;
             }
         }
+        sub_stamp(SUB_INPUT);
     }
     if (in.raw) {
 #pragma unroll
@@ -747,12 +801,15 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.K, ne = p.n_expert;
     const int set = warp / 4, w = warp % 4;
+    // the expert mask word (n_expert <= 32) does not depend on the token: request it first
+    const uint32_t mword = (warp == kRouteWarp && p.mask) ? ld_early_u32(p.mask) : 0u;
     // the router rows arrive as two ring stages of 16 rows; warp w of the set dots rows 4w..4w+3
     for (int h = 0; h < 2; h++) {
         const uint32_t ih = i + h;
         if ((int)(ih % kSets) != set) continue;
         const int slot = ih % kDecSlots;
         const bool ok = slot_wait(&r.full[slot], (ih / kDecSlots) & 1u, err);
+        sub_stamp(SUB_ROUTE_STAGE);
         const uint8_t* sb = r.base + r.off[slot];
         const int row0 = 16 * h + 4 * w;
         const int n_rows = ok ? max(0, min(4, ne - row0)) : 0;
@@ -773,6 +830,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     }
     i += 2;
     named_bar(1, kConsumerThreads);
+    sub_stamp(SUB_ROUTE_DOTS);
     if (warp == kRouteWarp) {  // not warp 0: it shares a sub-partition with the producer warp
         const bool live = lane < ne;
         const float prob = live ? 1.0f / (1.0f + expf(-route->logit[lane])) : 0.f;
@@ -807,6 +865,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
             for (int k = 0; k < 4; k++)
                 if (lane == k) { wk = (float)((double)top_p[k] * inv); ik = top_i[k]; }
             route->id[lane] = ik;
+            route->skip[lane] = (int)((mword >> (ik & 31)) & 1u);
             route->w[lane] = wk;
             if (blockIdx.x == 0) {
                 p.ridx[lane] = ik;
@@ -846,12 +905,17 @@ __device__ __forceinline__ void consume_a(const PhaseDesc& p, const PhaseRegs& R
     const int row = lane >> SH;
     const bool lead = (lane & ((1 << SH) - 1)) == 0 && row < NR && row % S == 0;
     const int my_j = row / S;
+    bool first = true;
     for (int g = blockIdx.x; g < n_groups; g += gridDim.x, ++i) {
         if ((int)(i % kSets) != set) continue;
         const int slot = i % kDecSlots;
         // on a timeout leave the loop but keep every later barrier of the CTA (the next
         // phase wait sees the error word and all consumer warps return together)
         if (!slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err)) break;
+        if (first) {
+            sub_stamp(SUB_FIRST);
+            first = false;
+        }
         const uint8_t* sb = r.base + r.off[slot];
         const bool gon = R.map != MK_EXPERT_PAIR || pick4(R.on, (g * G) / R.N);
         const int li0 = w * IPW;
@@ -1030,7 +1094,7 @@ __device__ __forceinline__ bool fused_part1(const PhaseDesc& p, const DecRing& r
     const int row = lane >> SH;
     const bool lead = (lane & ((1 << SH) - 1)) == 0 && row < NR && row % S == 0;
     const int my_j = w * IPW + row / S;
-    bool ok = true;
+    bool ok = true, first = true;
     for (int u = u0; u < u1; ++i) {
         const int n = moe_stage_len(u, u1, N, G);
         const int s = u / N;
@@ -1047,6 +1111,10 @@ __device__ __forceinline__ bool fused_part1(const PhaseDesc& p, const DecRing& r
                 pre[4] = p.conv_w[ch * 3 + 2];
             }
             ok = slot_wait(&r.full[slot], (i / kDecSlots) & 1u, err);
+            if (ok && first) {
+                sub_stamp(SUB_FIRST);
+                first = false;
+            }
             if (ok) {
                 const uint8_t* sb = r.base + r.off[slot];
                 const int8_t* q[NRP];
@@ -1089,8 +1157,8 @@ __device__ __forceinline__ bool fused_part1(const PhaseDesc& p, const DecRing& r
 __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
                           float sc, const DecRoute* route, float* scratch, float* acc_out, unsigned* cnt, int* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int set = warp / 4, w = warp % 4;
-    const int K = p.K, nch = K >> 4, N = p.N, EO = p.n_out;
+    const int set = warp / 4;
+    const int N = p.N, EO = p.n_out;
     const float* raw = scratch;
     float* comb = scratch + kMoeOut;
     float* hbuf = comb + kMoeOut;
@@ -1100,6 +1168,7 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
                         ? fused_part1<3, kConvG / 4>(p, r, i, dig, xsc, sc, route, u0, u1, hbuf, err)
                         : fused_part1<2, kMoeG / 4>(p, r, i, dig, xsc, sc, route, u0, u1, hbuf, err);
     named_bar(1, kConsumerThreads);  // h complete
+    sub_stamp(SUB_PART1);
     // down: thread tp of the stage's set accumulates out rows 16 tp .. 16 tp + 15
     const int tp = threadIdx.x & 127;
     float acc[kMoeRows];
@@ -1129,6 +1198,7 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
             u += n;
         }
     }
+    sub_stamp(SUB_PART2);
     // combine the two sets, add the owned residual rows, add the CTA's vector to the output with
     // one bulk reduction (at L2; 8x fewer requests than per-thread float4 atomics, which contend
     // on the same lines from every CTA), count this CTA
@@ -1155,8 +1225,9 @@ __device__ void moe_fused(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     named_bar(1, kConsumerThreads);
     if (threadIdx.x == 0) {
         bulk_add_f32_s2g(acc_out + (size_t)(blockIdx.x % kAccCopies) * EO, comb, (uint32_t)EO * 4u);  // returns once performed
-        __threadfence();
-        atomicAdd(cnt, 1u);
+        sub_stamp(SUB_REDUCED);
+        red_release_add(cnt, 1u);
+        sub_stamp(SUB_PUBLISHED);
     }
 }
 
@@ -1227,6 +1298,7 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
             }
             for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads)
                 q_s[i] = wait_tw(qkv + (size_t)kvh * G * HD + i, tag_in, err);
+            sub_stamp(SUB_INPUT);
             const bool owns = p0 <= pos && pos < p1;
             if (owns)
                 for (int d = threadIdx.x; d < HD; d += kConsumerThreads) {
@@ -1301,6 +1373,7 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
                 }
                 named_bar(1, kConsumerThreads);  // the next tile reuses the buffers
             }
+            sub_stamp(SUB_PART1);
             if (warp < G) {
                 float* pp = part_base + ((size_t)warp * a.n_split + split) * (HD + 2);
 #pragma unroll
@@ -1317,12 +1390,13 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
         }
         named_bar(1, kConsumerThreads);
         if (threadIdx.x == 0) {
-            __threadfence();
-            is_last = atomicAdd(a.counter + kvh, 1u) == (unsigned)n_split - 1;
+            // release: the CTA's partials (ordered before by the barrier); acquire: the other
+            // splits' partials, which the barrier below orders before this CTA's merge loads
+            is_last = atom_acq_rel_add(a.counter + kvh, 1u) == (unsigned)n_split - 1;
+            sub_stamp(SUB_REDUCED);
         }
         named_bar(1, kConsumerThreads);
         if (is_last) {
-            __threadfence();
             // merge the splits; all loads of a thread are issued before the first use
             for (int i = threadIdx.x; i < G * HD; i += kConsumerThreads) {
                 const int g = i / HD, d = i - g * HD;
@@ -1355,6 +1429,7 @@ __device__ void dec_attention(const AttnArgs& a, const tword* qkv, uint32_t tag_
                 st_tw(out + (size_t)(kvh * G + g) * HD + d, A / L, tag_out);
             }
             if (threadIdx.x == 0) a.counter[kvh] = 0u;
+            sub_stamp(SUB_PUBLISHED);
         }
         named_bar(1, kConsumerThreads);
     }
@@ -1370,6 +1445,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     __shared__ float part[2][kG][4];
     __shared__ int set_ok[2];
     __shared__ DecRoute route;
+    // phase descriptors in shared memory: the consumers' current one (double-buffered, the next
+    // one loaded into registers during a phase) and the producer's (double-buffered bulk copies)
+    __shared__ PhaseDesc s_desc[2];
+    __shared__ PhaseDesc s_pdesc[2];
+    __shared__ __align__(8) uint64_t pdesc_bar[2];
     DecRing r;
     r.base = smem;
     uint8_t* dig_base = smem + kDecRingBytes;
@@ -1383,19 +1463,27 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const uint32_t epoch = *reinterpret_cast<const volatile unsigned int*>(&ctl->epoch);
     unsigned long long* trace = ctl->trace ? ctl->trace + (size_t)blockIdx.x * (n_phases + 1) : nullptr;
     if (trace && threadIdx.x == 0) trace[0] = globaltimer_ns();
+    unsigned long long* sub = ctl->sub ? ctl->sub + (size_t)blockIdx.x * n_phases * kSubStamps : nullptr;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDecSlots; s++) {
             mbar_init(&r.full[s], 1);
             mbar_init(&r.empty[s], kG);
         }
         mbar_init(&route.bar, 1);
+        mbar_init(&pdesc_bar[0], 1);
+        mbar_init(&pdesc_bar[1], 1);
         mbar_fence_init();
     }
     __syncthreads();
     if (warp == kCW) {
-        if (lane == 0) dec_producer(prog, n_phases, r, &route, err);
+        if (lane == 0) dec_producer(prog, n_phases, r, &route, s_pdesc, pdesc_bar, sub, err);
         return;
     }
+    // descriptor words: consumer thread t < kDescWords copies word t of the next phase's descriptor
+    constexpr int kDescWords = (int)(sizeof(PhaseDesc) / 4);
+    static_assert(kDescWords <= kConsumerThreads, "one descriptor word per consumer thread");
+    const uint32_t* progw = reinterpret_cast<const uint32_t*>(prog);
+    uint32_t desc_word = threadIdx.x < kDescWords ? __ldg(progw + threadIdx.x) : 0u;
     // this step's half of the accumulated-vector arena; zero the other half (the previous step
     // used it, the next one will: kernel boundaries order the zeroing against both)
     long long aoff = 0;
@@ -1415,7 +1503,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     for (int ph = 0; ph < n_phases; ph++) {
         // the previous phase is over for this CTA (also when it skipped that phase)
         if (trace && threadIdx.x == 0 && ph > 0) trace[ph] = globaltimer_ns();
-        const PhaseDesc& p = prog[ph];
+        if (threadIdx.x == 0) s_sub = sub ? sub + (size_t)ph * kSubStamps : nullptr;
+        // publish this phase's descriptor (loaded during the previous phase) and request the next
+        // one; every warp has left phase ph - 2, the last reader of this buffer
+        if (threadIdx.x < kDescWords) reinterpret_cast<uint32_t*>(&s_desc[ph & 1])[threadIdx.x] = desc_word;
+        named_bar(1, kConsumerThreads);
+        if (threadIdx.x < kDescWords && ph + 1 < n_phases)
+            desc_word = __ldg(progw + (size_t)(ph + 1) * kDescWords + threadIdx.x);
+        const PhaseDesc& p = s_desc[ph & 1];
         const uint32_t tag = step_tag(epoch, ph);
         if (p.type == PH_EMBED) {
             if (blockIdx.x != 0) continue;
@@ -1460,8 +1555,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             float* xsc = reinterpret_cast<float*>(dig + 3 * nch);
             dec_stage_digits(stage_in(p, epoch, aoff), p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
+            sub_stamp(SUB_STAGED);
             const float sc = stage_scale(red, p.norm_w, K, p.eps);
-            if (p.r_qs) dec_route(p, r, i, dig, xsc, sc, nch, bias_v, &route, err);
+            if (p.r_qs) {
+                dec_route(p, r, i, dig, xsc, sc, nch, bias_v, &route, err);
+                sub_stamp(SUB_ROUTED);
+            }
             const float* ra = p.ra ? p.ra + aoff : nullptr;
             PhaseRegs R;
             load_phase(&p, R, expert_map(p.map) ? &route : nullptr);
@@ -1477,6 +1576,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             else if (R.S == 2) consume_a<2, 1>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
             else if (R.S == 3 && ipw == 2) consume_a<3, 2>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
             else consume_a<3, 1>(p, R, r, i, dig, xsc, sc, tag, tres, ra, best_k, err);
+            sub_stamp(SUB_PART1);
             if (p.epi == EK_ARGMAX) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -1503,8 +1603,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             in.raw = scratch;
             dec_stage_digits(in, p.norm_w, p.eps, K, dig, xsc, red, err);
             named_bar(1, kConsumerThreads);
+            sub_stamp(SUB_STAGED);
             const float sc = stage_scale(red, p.norm_w, K, p.eps);
-            if (p.r_qs) dec_route(p, r, i, dig, xsc, sc, nch, bias_v, &route, err);
+            if (p.r_qs) {
+                dec_route(p, r, i, dig, xsc, sc, nch, bias_v, &route, err);
+                sub_stamp(SUB_ROUTED);
+            }
             moe_fused(p, r, i, dig, xsc, sc, &route, scratch, p.acc + aoff, p.acc_cnt + aoff, err);
         } else if (p.type == PH_DOWN4) {
             if ((int)blockIdx.x >= (p.n_items + kG - 1) / kG) continue;
@@ -1537,6 +1641,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 const int pos = f.ctl[1] + 1;
                 f.ctl[0] = tok;
                 f.ctl[1] = pos;
+                f.ctl[2] = ld_volatile(err);  // read back with the token by a host-driven step
                 f.trace[pos] = tok;
             }
             ctl->best = 0ull;

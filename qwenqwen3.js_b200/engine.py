@@ -210,8 +210,7 @@ class _CudaEngine:
 
     def forward_argmax(self, tokenId: int, position: int, suppress_id: int = -1, seq: int = 0) -> int:
         """forward() + device greedy argmax (4-byte readback instead of the logits)."""
-        _, am = self.model.forward([tokenId], seq=seq, pos0=position, want_logits=True, logits=False,
-                                   suppress_id=suppress_id)
+        am = self.model.forward_argmax(tokenId, seq=seq, pos=position, suppress_id=suppress_id)
         self._emit_routing()
         return am
 

@@ -149,6 +149,7 @@ _SIGS = {
     "qq_comm_destroy": (_I, [_P]),
     "qq_ep_profile": (_I, [_P, _I, _P]),
     "qq_decode_trace": (_I, [_P, _I, _P, _P, C.POINTER(_I), C.POINTER(_I)]),
+    "qq_decode_trace_sub": (_I, [_P, _P, C.POINTER(_I)]),
     "qq_upload_begin": (_I, [_P, C.c_size_t, C.POINTER(_P)]),
     "qq_upload_tensor_async": (_I, [_P, _P, C.c_size_t, _I, C.POINTER(_I64), _I, C.POINTER(_P)]),
     "qq_upload_finish": (_I, [_P, C.POINTER(C.c_size_t)]),
@@ -433,6 +434,10 @@ class Model:
         self.n_vocab = desc.n_vocab
         self.n_layers = desc.n_layers
         self.n_embd = desc.n_embd
+        # reusable ctypes arguments of forward_argmax (one greedy token per call)
+        self._tok1 = (C.c_int32 * 1)()
+        self._am1 = C.c_int32(-1)
+        self._am1_ref = C.byref(self._am1)
 
     def close(self) -> None:
         if self.h:
@@ -455,6 +460,13 @@ class Model:
                                       1 if want_logits else 0, _ptr(out), C.byref(am) if want_logits else None,
                                       suppress_id))
         return out, am.value
+
+    def forward_argmax(self, token: int, seq: int = 0, pos: int = 0, suppress_id: int = -1) -> int:
+        """One token with the device greedy id (qq_forward with want_logits and no logits copy),
+        without per-call array allocations."""
+        self._tok1[0] = token
+        check(self.ctx.lib.qq_forward(self.h, self._tok1, 1, seq, pos, 1, None, self._am1_ref, suppress_id))
+        return self._am1.value
 
     def forward_batch(self, seqs, tokens, positions, want_logits: bool = True, logits: bool = True,
                       suppress_id: int = -1):
@@ -539,6 +551,16 @@ class Model:
         check(self.ctx.lib.qq_decode_trace(self.h, 1 if enable else 0, st.ctypes.data, kinds.ctypes.data,
                                            C.byref(np_), C.byref(nc)))
         return st, kinds
+
+    def decode_trace_sub(self):
+        """Sub-phase stamps of the last traced step: [n_ctas][n_phases][n_sub] ns (0 where a phase
+        does not reach a point; the points are listed at qq_decode_trace_sub in qq3.h)."""
+        np_, nc, ns = C.c_int(0), C.c_int(0), C.c_int(0)
+        check(self.ctx.lib.qq_decode_trace(self.h, 0, None, None, C.byref(np_), C.byref(nc)))
+        check(self.ctx.lib.qq_decode_trace_sub(self.h, None, C.byref(ns)))
+        out = np.zeros((nc.value, np_.value, ns.value), dtype=np.uint64)
+        check(self.ctx.lib.qq_decode_trace_sub(self.h, out.ctypes.data, C.byref(ns)))
+        return out
 
     def ep_profile(self, enable: bool):
         """Switch the per-exchange CUDA-event split on/off; returns the split summed since the

@@ -135,6 +135,15 @@ def test_device_decode_loop_matches_host_loop(qq3, orc):
         ref_ids.append(cur)
         pos += 1
     assert dev.tolist() == ref_ids
+    # the same tokens one host call per step (the persistent step's graph with the token copies)
+    eng.resetKVCache()
+    eng.prefill(prompt[:-1])
+    cur, pos, host_ids = prompt[-1], len(prompt) - 1, []
+    for _ in range(12):
+        cur = eng.forward_argmax(cur, pos)
+        host_ids.append(cur)
+        pos += 1
+    assert host_ids == ref_ids
     eng.close()
 
 
