@@ -114,12 +114,11 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t a, uint64_t b, 
 
 __device__ __forceinline__ uint32_t h2bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// 32 weights of one row (raw[0..1], block scale dc) -> the hi and lo fp16 planes of the swizzled
-// K-major tiles bh / bl, 16-byte chunks c0 .. c0 + 3 of row brow (the SPLIT = 3 conversion above)
-__device__ __forceinline__ void split3_convert(const uint4 (&raw)[2], __half2 dc, uint8_t* bh, uint8_t* bl, int brow,
-                                               int c0) {
+// 32 weights of one row (raw[0..1] in K order, block scale dc) -> the exact hi and lo fp16 pairs
+// (the SPLIT = 3 conversion above): hw[c][w], lw[c][w] hold weights 8c + 2w and 8c + 2w + 1
+__device__ __forceinline__ void split3_words(const uint4 (&raw)[2], __half2 dc, uint32_t (&hw)[4][4],
+                                             uint32_t (&lw)[4][4]) {
     const float dfs = __low2float(dc);
-    uint32_t hw[4][4], lw[4][4];
     if (fabsf(dfs) < 0.25f) {  // one branch for the four chunks, so their chains interleave
         const __half2 d2s = __low2half2(dc);
         const __half2 d2k = __float2half2_rn(dfs * 2048.0f);
@@ -160,6 +159,14 @@ __device__ __forceinline__ void split3_convert(const uint4 (&raw)[2], __half2 dc
             }
         }
     }
+}
+
+// The same conversion stored into the hi and lo planes of the swizzled K-major tiles bh / bl,
+// 16-byte chunks c0 .. c0 + 3 of row brow
+__device__ __forceinline__ void split3_convert(const uint4 (&raw)[2], __half2 dc, uint8_t* bh, uint8_t* bl, int brow,
+                                               int c0) {
+    uint32_t hw[4][4], lw[4][4];
+    split3_words(raw, dc, hw, lw);
 #pragma unroll
     for (int c = 0; c < 4; c++) {
         *reinterpret_cast<uint4*>(bh + sw128(brow, c0 + c)) = make_uint4(hw[c][0], hw[c][1], hw[c][2], hw[c][3]);
@@ -386,46 +393,69 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
 // With a handful of activation rows (a multi-sequence decode step) the 128-row activation tile
 // above leaves 7/8 of every MMA empty and the grid holds only ceil(N / 128) CTAs, so the weights
 // stream through a few SMs.  Here a work item is 128 weight rows (the UMMA's M operand) against
-// all MN (16 or 32) activation rows (its N operand) over one of S splits of the K steps, and one
+// all MN (16 or 32) activation rows (its N operand) over one of S splits of the K range, and one
 // persistent CTA per SM walks its items:
-//   warp 8    streams the raw int8 weight tiles (8 KB per K step) into a ring that is released
-//             as soon as the converters hold a tile in registers, so 64-80 KB of HBM reads per
-//             SM stay in flight across item boundaries;
-//   warp 10   loads the fp16 activation tiles (hi, lo) of each K step into their own ring;
-//   warps 0-7 convert weights to the exact fp16 hi/lo pair in the operand ring, and after an
-//             item's last K step read its accumulators and store them;
-//   warp 9    issues D1 += wh.xh, D2 += wl.xh + wh.xl into one of two TMEM accumulator pairs
-//             (items alternate, so an item's MMAs overlap the previous item's epilogue).
+//   warp 8    streams raw int8 weight stages of 128 rows x 256 K (two 128-byte-wide swizzled TMA
+//             boxes, plus the 8 block scales per row of that K range) into a 5-deep ring;
+//   warp 10   loads the fp16 activation tiles (hi rows, then lo rows) of each 64-wide K step;
+//   warps 0-7 convert: thread (row r, K half h) turns its 32 weights of a K step into the exact
+//             fp16 hi/lo pairs and writes them to tensor memory (tcgen05.st, lane r), the MMA's
+//             A operand; after an item's last K step they read its accumulators and store them;
+//   warp 9    issues [hh | hl] += wh.[xh | xl] (N = 2 MN) and lh += wl.xh (N = MN) per 16 of K,
+//             with A read from tensor memory, into one of two accumulator pairs (items
+//             alternate, so an item's MMAs overlap the previous item's epilogue).
+// A in tensor memory keeps the converted weights out of shared memory: an N = 16 MMA with A in
+// shared memory re-reads its 4 KB A tile for 16 output columns, and those reads, the converted
+// stores and the raw stages share one pipe (measured: conversion, MMAs and loads added up).
 // With S > 1 each split writes its partial sums to scratch [S][M][N]; the last CTA to finish a row
 // tile (arrival ticket) adds them in split order, so the result does not depend on scheduling.
-// Exact three-product split only (as SPLIT = 3 above).
+// Exact three-product split only (as SPLIT = 3 above): y = hh + (hl + lh) / 2048.
 constexpr int kRowsBM = 128;       // weight rows per item
+constexpr int kRowsKR = 256;       // K of one raw weight stage (four 64-wide MMA K steps)
 constexpr int kRowsMaxItems = 296; // S * row tiles <= this when S > 1
 constexpr int kRowsTickets = 256;  // >= row tiles whenever S > 1
 constexpr int kRowsWarps = 11;     // 8 converters, raw producer, MMA issuer, activation producer
 constexpr int kRowsThreads = kRowsWarps * 32;
 
-// Three rings: raw int8 weights (TMA from HBM, released once the converters hold a tile in
-// registers), fp16 activations (TMA from L2, released by the MMAs that read them) and converted
-// fp16 weights (released by the MMAs).  The activation ring is deep enough that its loads never
-// wait on the MMA chain.  208 KB of shared memory either way.
 template <int MN>
 struct RowsCfg {
-    static constexpr int RawStages = MN == 16 ? 8 : 7;
-    static constexpr int OpStages = 3;
-    static constexpr int XStages = MN == 16 ? 8 : 6;
-    static constexpr int WTile = kRowsBM * kBK * 2;  // 16 KB fp16 weights (hi or lo)
-    static constexpr int XTile = MN * kBK * 2;       // 2 / 4 KB fp16 activations (hi or lo)
-    static constexpr int RawTile = kRowsBM * kBK;    // 8 KB int8
-    static constexpr int DTile = kRowsBM * 16;       // block scales: 8 fp16 per row (4 K steps)
-    static constexpr int RawStage = RawTile + DTile;
-    static constexpr int OpStage = 2 * WTile;
+    static constexpr int RawStages = 5;                 // 170 KB of weight reads in flight per SM
+    static constexpr int OpStages = 4;                  // converted K steps in tensor memory
+    static constexpr int XStages = OpStages;            // released by the same MMA commit
+    static constexpr int XTile = MN * kBK * 2;          // 2 / 4 KB fp16 activations (hi or lo)
+    static constexpr int RawBox = kRowsBM * 128;        // one swizzled 128-byte-wide box: 16 KB
+    static constexpr int DTile = kRowsBM * 16;          // block scales: 8 fp16 per row (256 K)
+    static constexpr int RawStage = (2 * RawBox + DTile + 1023) & ~1023;
     static constexpr int XStage = 2 * XTile;
-    static constexpr int Smem = OpStages * OpStage + XStages * XStage + RawStages * RawStage + 1024;
-    static constexpr uint32_t Idesc = (1u << 4) | ((uint32_t)(MN >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
-    static constexpr uint32_t AccCols = 64;           // per accumulator pair: D1 at +0, D2 at +32
-    static constexpr uint32_t TmemCols = 2 * AccCols;
+    static constexpr int Smem = RawStages * RawStage + XStages * XStage + 1024;
+    static constexpr uint32_t IdescHL = (1u << 4) | ((uint32_t)((2 * MN) >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
+    static constexpr uint32_t IdescL = (1u << 4) | ((uint32_t)(MN >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
+    static constexpr uint32_t AccCols = MN == 16 ? 64 : 128;  // per pair: [hh | hl] at +0, lh at +2 MN
+    static constexpr uint32_t OpCols = 64;              // per K step: hi (4 x 8 columns) | lo
+    static constexpr uint32_t OpBase = 2 * AccCols;
+    static constexpr uint32_t TmemCols = 512;
+    static_assert(OpBase + OpStages * OpCols <= TmemCols, "tensor memory columns");
+    static_assert(3 * MN <= (int)AccCols, "accumulator pair columns");
 };
+
+// tcgen05.mma with the A operand in tensor memory (kind::f16: fp16 x fp16 -> f32)
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+// 16 consecutive 32-bit tensor-memory columns of this thread's lane
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[4][4]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0][0]), "r"(v[0][1]), "r"(v[0][2]), "r"(v[0][3]), "r"(v[1][0]), "r"(v[1][1]), "r"(v[1][2]), "r"(v[1][3]),
+        "r"(v[2][0]), "r"(v[2][1]), "r"(v[2][2]), "r"(v[2][3]), "r"(v[3][0]), "r"(v[3][1]), "r"(v[3][2]), "r"(v[3][3])
+        : "memory");
+}
 
 template <int MN>
 __global__ void __launch_bounds__(kRowsThreads, 1)
@@ -436,25 +466,24 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     using G = RowsCfg<MN>;
     extern __shared__ uint8_t smem_raw[];
     constexpr int R = G::RawStages, O = G::OpStages, X = G::XStages;
-    __shared__ __align__(8) uint64_t full_raw[R], raw_free[R], full_x[X], x_free[X], conv_done[O], op_free[O],
-        acc_full[2], acc_free[2];
+    __shared__ __align__(8) uint64_t full_raw[R], raw_free[R], full_x[X], conv_done[O], op_free[O], acc_full[2],
+        acc_free[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int last_flag;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int nk = (K + kBK - 1) / kBK;
+    const int nk = (K + kBK - 1) / kBK;          // 64-wide MMA K steps
+    const int nr = (K + kRowsKR - 1) / kRowsKR;  // 256-wide raw stages
     const int KB = K >> 5;
-    // shared memory: converted weight stages | activation stages | raw weight stages
-    auto w_tile = [&](int os, int h) { return smem + os * G::OpStage + h * G::WTile; };
-    auto x_tile = [&](int xs, int h) { return smem + O * G::OpStage + xs * G::XStage + h * G::XTile; };
-    auto raw_tile = [&](int rs) { return smem + O * G::OpStage + X * G::XStage + rs * G::RawStage; };
-    auto d_tile = [&](int rs) { return reinterpret_cast<const __half*>(raw_tile(rs) + G::RawTile); };
-    // item it: row tile it / S, split it % S (K steps [kt0, kt1))
-    auto item_range = [&](int it, int& n0, int& sp, int& kt0, int& kt1) {
+    // shared memory: raw weight stages | activation stages
+    auto raw_stage = [&](int rs) { return smem + rs * G::RawStage; };
+    auto x_tile = [&](int xs, int h) { return smem + R * G::RawStage + xs * G::XStage + h * G::XTile; };
+    // item it: row tile it / S, split it % S (raw stages [r0, r1))
+    auto item_range = [&](int it, int& n0, int& sp, int& r0, int& r1) {
         n0 = (it / S) * kRowsBM;
         sp = it % S;
-        kt0 = (int)(((long long)sp * nk) / S);
-        kt1 = (int)(((long long)(sp + 1) * nk) / S);
+        r0 = (int)(((long long)sp * nr) / S);
+        r1 = (int)(((long long)(sp + 1) * nr) / S);
     };
     if (warp == 9) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -467,10 +496,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
             mbar_init(&full_raw[r], 1);
             mbar_init(&raw_free[r], kConvWarps);
         }
-        for (int x = 0; x < X; x++) {
-            mbar_init(&full_x[x], 1);
-            mbar_init(&x_free[x], 1);
-        }
+        for (int x = 0; x < X; x++) mbar_init(&full_x[x], 1);
         for (int o = 0; o < O; o++) {
             mbar_init(&conv_done[o], kConvWarps);
             mbar_init(&op_free[o], 1);
@@ -490,15 +516,17 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (lane == 0) {  // raw weight producer
             int r = 0;
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                int n0, sp, kt0, kt1;
-                item_range(it, n0, sp, kt0, kt1);
-                for (int kt = kt0; kt < kt1 && ok; kt++, r++) {
+                int n0, sp, r0, r1;
+                item_range(it, n0, sp, r0, r1);
+                for (int rt = r0; rt < r1 && ok; rt++, r++) {
                     const int rs = r % R;
                     if (r >= R) ok = bar_wait(&raw_free[rs], (uint32_t)((r / R - 1) & 1), err);
                     if (!ok) break;
-                    mbar_arrive_expect_tx(&full_raw[rs], (uint32_t)(G::RawTile + (d_tma ? G::DTile : 0)));
-                    tma_2d(raw_tile(rs), &tmW, kt * kBK, n0, &full_raw[rs]);
-                    if (d_tma) tma_2d(raw_tile(rs) + G::RawTile, &tmD, (2 * kt) & ~7, n0, &full_raw[rs]);
+                    mbar_arrive_expect_tx(&full_raw[rs], (uint32_t)(2 * G::RawBox + (d_tma ? G::DTile : 0)));
+                    // a box past K reads zeros (its K coordinate stays a multiple of 128 bytes)
+                    tma_2d(raw_stage(rs), &tmW, rt * kRowsKR, n0, &full_raw[rs]);
+                    tma_2d(raw_stage(rs) + G::RawBox, &tmW, rt * kRowsKR + 128, n0, &full_raw[rs]);
+                    if (d_tma) tma_2d(raw_stage(rs) + 2 * G::RawBox, &tmD, rt * 8, n0, &full_raw[rs]);
                 }
             }
             for (int i = (r > R ? r - R : 0); i < r; i++)  // copies land before exit
@@ -508,11 +536,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (lane == 0) {  // activation producer: hi rows at 0, lo rows at M
             int o = 0;
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                int n0, sp, kt0, kt1;
-                item_range(it, n0, sp, kt0, kt1);
-                for (int kt = kt0; kt < kt1 && ok; kt++, o++) {
+                int n0, sp, r0, r1;
+                item_range(it, n0, sp, r0, r1);
+                for (int kt = 4 * r0; kt < min(4 * r1, nk) && ok; kt++, o++) {
                     const int xs = o % X;
-                    if (o >= X) ok = bar_wait(&x_free[xs], (uint32_t)((o / X - 1) & 1), err);
+                    if (o >= X) ok = bar_wait(&op_free[xs], (uint32_t)((o / X - 1) & 1), err);
                     if (!ok) break;
                     mbar_arrive_expect_tx(&full_x[xs], (uint32_t)G::XStage);
                     tma_2d(x_tile(xs, 0), &tmX, kt * kBK, 0, &full_x[xs]);
@@ -526,78 +554,93 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (lane == 0) {  // MMA issuer
             int o = 0, j = 0;
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, j++) {
-                int n0, sp, kt0, kt1;
-                item_range(it, n0, sp, kt0, kt1);
+                int n0, sp, r0, r1;
+                item_range(it, n0, sp, r0, r1);
                 const int ab = j & 1;
                 if (j >= 2) ok = bar_wait(&acc_free[ab], (uint32_t)((j / 2 - 1) & 1), err);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t acc_d = tmem + (uint32_t)ab * G::AccCols;
-                for (int kt = kt0; kt < kt1 && ok; kt++, o++) {
+                for (int kt = 4 * r0; kt < min(4 * r1, nk) && ok; kt++, o++) {
                     const int os = o % O, xs = o % X;
                     ok = bar_wait(&full_x[xs], (uint32_t)((o / X) & 1), err) &&
                          bar_wait(&conv_done[os], (uint32_t)((o / O) & 1), err);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t wh = smem_u32(w_tile(os, 0)), wl = smem_u32(w_tile(os, 1));
-                    const uint32_t xh = smem_u32(x_tile(xs, 0)), xl = smem_u32(x_tile(xs, 1));
+                    const uint32_t a_hi = tmem + G::OpBase + (uint32_t)os * G::OpCols, a_lo = a_hi + 32u;
+                    const uint32_t xh = smem_u32(x_tile(xs, 0));
 #pragma unroll
                     for (int ks = 0; ks < kBK / 16; ks++) {
-                        const uint32_t acc = (kt != kt0 || ks != 0) ? 1u : 0u;
-                        umma_f16(acc_d, umma_desc(wh + 32u * ks), umma_desc(xh + 32u * ks), G::Idesc, acc);
-                        umma_f16(acc_d + 32u, umma_desc(wl + 32u * ks), umma_desc(xh + 32u * ks), G::Idesc, acc);
-                        umma_f16(acc_d + 32u, umma_desc(wh + 32u * ks), umma_desc(xl + 32u * ks), G::Idesc, 1u);
+                        const uint32_t acc = (kt != 4 * r0 || ks != 0) ? 1u : 0u;
+                        const uint64_t bx = umma_desc(xh + 32u * ks);
+                        umma_f16_tmem_a(acc_d, a_hi + 8u * ks, bx, G::IdescHL, acc);
+                        umma_f16_tmem_a(acc_d + 2u * MN, a_lo + 8u * ks, bx, G::IdescL, acc);
                     }
-                    umma_commit(&op_free[os]);
-                    umma_commit(&x_free[xs]);
+                    umma_commit(&op_free[os]);  // frees the operand columns and the activation stage
                 }
                 umma_commit(&acc_full[ab]);  // covers the item's MMAs (also after a failed wait)
             }
         }
     } else {
-        // converters (two threads per weight row, one Q8_0 block each per K step) and epilogue
-        const int brow = t >> 1, part_k = t & 1;
-        const int q = warp & 3, hb = warp >> 2;  // epilogue: TMEM lanes 32q.., activation rows 16hb..
-        int o = 0, j = 0;
+        // converters: thread t holds weight row t & 127 (its TMEM lane) and K half t >> 7 of each
+        // K step; epilogue: warp w reads TMEM lanes 32 (w % 4) .., activation rows 16 (w / 4) ..
+        const int row = t & 127, kh = t >> 7;
+        const int q = warp & 3, hb = warp >> 2;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        int o = 0, r = 0, j = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, j++) {
-            int n0, sp, kt0, kt1;
-            item_range(it, n0, sp, kt0, kt1);
-            const int n = n0 + brow;
-            auto load_d = [&](int kt) -> uint32_t {
-                __half2 v = __float2half2_rn(0.f);
-                const int kb = 2 * kt + part_k;
-                if (n < N && kb < KB) {
-                    const __half h = d[(size_t)n * KB + kb];
-                    v = __halves2half2(h, h);
-                }
-                return h2bits(v);
-            };
-            uint32_t dnext = d_tma ? 0u : load_d(kt0);
-            for (int kt = kt0; kt < kt1 && ok; kt++, o++) {
-                const int rs = o % R, os = o % O;
-                uint32_t dcur = dnext;
-                if (!d_tma && kt + 1 < kt1) dnext = load_d(kt + 1);
-                ok = __all_sync(0xffffffffu, bar_wait(&full_raw[rs], (uint32_t)((o / R) & 1), err));
-                uint4 raw[2];
-                if (ok) {
-                    const uint4* rp = reinterpret_cast<const uint4*>(raw_tile(rs) + brow * kBK + part_k * 32);
-                    raw[0] = rp[0];
-                    raw[1] = rp[1];
-                    if (d_tma) {  // rows past N were zero-filled by the copy
-                        const __half h = d_tile(rs)[brow * 8 + ((2 * kt + part_k) & 7)];
-                        dcur = h2bits(__halves2half2(h, h));
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&raw_free[rs]);
-                if (ok && o >= O)
-                    ok = __all_sync(0xffffffffu, bar_wait(&op_free[os], (uint32_t)((o / O - 1) & 1), err));
+            int n0, sp, r0, r1;
+            item_range(it, n0, sp, r0, r1);
+            const int n = n0 + row;
+            for (int rt = r0; rt < r1 && ok; rt++, r++) {
+                const int rs = r % R;
+                ok = __all_sync(0xffffffffu, bar_wait(&full_raw[rs], (uint32_t)((r / R) & 1), err));
                 if (!ok) break;
-                split3_convert(raw, *reinterpret_cast<const __half2*>(&dcur), w_tile(os, 0), w_tile(os, 1), brow,
-                               part_k * 4);
-                fence_async_smem();
+                // the row's 8 block scales of this raw stage (rows past N and blocks past K: 0)
+                uint4 s8 = make_uint4(0u, 0u, 0u, 0u);
+                if (d_tma) {
+                    s8 = *reinterpret_cast<const uint4*>(raw_stage(rs) + 2 * G::RawBox + row * 16);
+                } else if (n < N) {
+                    uint32_t sw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+                    for (int b = 0; b < 8; b++) {
+                        const int kb = 8 * rt + b;
+                        const uint32_t h = kb < KB ? (uint32_t)__half_as_ushort(d[(size_t)n * KB + kb]) : 0u;
+                        sw[b >> 1] |= h << (16 * (b & 1));
+                    }
+                    s8 = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+                }
+                const uint8_t* rowp = raw_stage(rs) + row * 128;
+                for (int js = 0; js < 4 && ok; js++) {
+                    const int kt = 4 * rt + js;
+                    if (kt >= nk) break;
+                    const int os = o % O;
+                    // 32 weights at K 64 js + 32 kh of the stage: box js / 2, 16-byte chunks c0 and
+                    // c0 + 1 of the row, stored at chunk c ^ (row & 7) (128-byte swizzle)
+                    const int c0 = 4 * (js & 1) + 2 * kh;
+                    const uint8_t* bp = rowp + (js >> 1) * G::RawBox;
+                    uint4 raw[2];
+                    raw[0] = *reinterpret_cast<const uint4*>(bp + ((c0 ^ (row & 7)) << 4));
+                    raw[1] = *reinterpret_cast<const uint4*>(bp + (((c0 + 1) ^ (row & 7)) << 4));
+                    const int b = 2 * js + kh;  // block within the stage
+                    const uint32_t sword = (b >> 1) == 0 ? s8.x : ((b >> 1) == 1 ? s8.y : ((b >> 1) == 2 ? s8.z : s8.w));
+                    const __half hs = __ushort_as_half((unsigned short)((b & 1) ? (sword >> 16) : (sword & 0xffffu)));
+                    if (o >= O) ok = __all_sync(0xffffffffu, bar_wait(&op_free[os], (uint32_t)((o / O - 1) & 1), err));
+                    if (!ok) break;
+                    tc_fence_after();
+                    uint32_t hw[4][4], lw[4][4];
+                    split3_words(raw, __halves2half2(hs, hs), hw, lw);
+                    const uint32_t col = tmem + lane_base + G::OpBase + (uint32_t)os * G::OpCols + 16u * kh;
+                    tmem_st16(col, hw);
+                    tmem_st16(col + 32u, lw);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&conv_done[os]);
+                    o++;
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&conv_done[os]);
+                if (lane == 0) mbar_arrive(&raw_free[rs]);  // the stage's bytes are in registers / TMEM
             }
             // epilogue of item j: accumulator pair j & 1
             const int ab = j & 1;
@@ -607,13 +650,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
             float f[16];
             const bool has = hb * 16 < MN;
             if (ok && has) {
-                uint32_t v[16], v2[16];
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)ab * G::AccCols + (uint32_t)(hb * 16);
-                tmem_ld16(taddr, v);
-                tmem_ld16(taddr + 32u, v2);
+                uint32_t v[16], v2[16], v3[16];
+                const uint32_t taddr = tmem + lane_base + (uint32_t)ab * G::AccCols + (uint32_t)(hb * 16);
+                tmem_ld16(taddr, v);                  // hh
+                tmem_ld16(taddr + (uint32_t)MN, v2);  // hl
+                tmem_ld16(taddr + 2u * MN, v3);       // lh
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int i = 0; i < 16; i++) f[i] = fmaf(__uint_as_float(v2[i]), 1.0f / 2048.0f, __uint_as_float(v[i]));
+                for (int i = 0; i < 16; i++)
+                    f[i] = fmaf(__uint_as_float(v2[i]) + __uint_as_float(v3[i]), 1.0f / 2048.0f, __uint_as_float(v[i]));
             }
             tc_fence_before();
             __syncwarp();
@@ -758,10 +803,10 @@ void launch_split(const DTensor& W, int64_t N, const __half* a16, int M, float* 
 
 namespace {
 
-// splits S of the K steps per 128-row tile: fewest rounds of one item per SM per unit of work
+// splits S of the raw K stages per 128-row tile: fewest rounds of one item per SM per unit of work
 int rows_splits(int64_t N, int64_t K) {
     const int tiles = (int)((N + kRowsBM - 1) / kRowsBM);
-    const int nk = (int)((K + kBK - 1) / kBK);
+    const int nk = (int)((K + kRowsKR - 1) / kRowsKR);
     const int sms = num_sms();
     int best = 1;
     double best_t = (double)((tiles + sms - 1) / sms);
@@ -781,8 +826,8 @@ void launch_rows(const DTensor& W, const __half* a16, int M, float* y, int ldc, 
     const int64_t K = W.K, N = W.rows;
     const CUtensorMap tx = tensor_map(const_cast<__half*>(a16), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)K,
                                       (uint64_t)M * 2, kBK, MN, CU_TENSOR_MAP_SWIZZLE_128B);
-    const CUtensorMap tw = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, kBK,
-                                      kRowsBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const CUtensorMap tw = tensor_map(W.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)K, (uint64_t)W.rows, 128,
+                                      kRowsBM, CU_TENSOR_MAP_SWIZZLE_128B);
     const bool d_tma = scales_by_tma(W);
     const CUtensorMap td = d_tma ? scale_map(W, kRowsBM) : tw;
     if (first_use_on_device(reinterpret_cast<const void*>(k_gemm_q8_rows<MN>)))
