@@ -168,7 +168,7 @@ __device__ __forceinline__ unsigned atom_acq_rel_add(unsigned* c, unsigned v) {
 // The hidden units [u0, u1) of the fused MoE phase this CTA owns: the U = top_k * N units of
 // the routed experts (slot-major) split into nearly equal runs of whole quads.
 __device__ __forceinline__ void moe_range(int U, int& u0, int& u1) {
-    const long long nq = U >> 2;
+    const uint32_t nq = (uint32_t)U >> 2;  // nq * gridDim.x < 2^32 for every phase that fits
     u0 = 4 * (int)(nq * blockIdx.x / gridDim.x);
     u1 = 4 * (int)(nq * (blockIdx.x + 1) / gridDim.x);
 }
@@ -196,6 +196,9 @@ struct DecRoute {
     int skip[4];  // the expert of slot s is masked (its rows are skipped)
     float w[4];
     float logit[kMaxRoutes];
+    float prob[kMaxRoutes];  // sigmoid of the logits
+    int top_i[4];            // the selected experts in selection order, and their probabilities
+    float top_p[4];
     uint64_t bar;  // completes once per MoE layer: the producer may read id[]
 };
 
@@ -373,8 +376,11 @@ __device__ __forceinline__ int64_t fused_row(const PhaseDesc* pp, int src, int e
 // of its units (G units a stage, never straddling two experts), then the same units' rows of
 // the transposed second matrix (down, or out_proj) with the block scales they need (kMoeDU
 // units a stage).  A masked expert's stages carry no bytes.
+// A routed phase passes its routing barrier: the first stage is reserved in the ring (and all the
+// bookkeeping done) before the wait for the routing, so the first expert copy leaves right after it.
 __device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing& r, const DecRoute* route,
-                                              ProdRing& pr, uint64_t pol, int* err, unsigned long long* sub) {
+                                              ProdRing& pr, uint64_t pol, int* err, unsigned long long* sub,
+                                              uint64_t* route_bar, uint32_t route_parity) {
     const int K = pp->K, N = pp->N, EO = pp->n_out;
     const int S = fused_sources(pp), G = fused_stage_units(S);
     const bool conv = pp->epi == EK_CONV;
@@ -385,11 +391,16 @@ __device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing
     for (int u = u0; u < u1; ++pr.i) {
         const int n = moe_stage_len(u, u1, N, G);
         const int s = u / N, j = u - s * N;
-        const int e = ffn_expert(pp, route, s);
-        const bool on = !ffn_skip(pp, route, s);
         int slot;
         uint8_t* sb;
         if (!pr.alloc(r, need, err, slot, sb)) return false;
+        if (route_bar) {
+            if (!slot_wait(route_bar, route_parity, err, kProducerBackoffNs)) return false;
+            route_bar = nullptr;
+            if (sub) sub[SUB_PROD_ROUTED] = globaltimer_ns();
+        }
+        const int e = ffn_expert(pp, route, s);
+        const bool on = !ffn_skip(pp, route, s);
         const uint32_t qb = (uint32_t)n * K, db = round16((uint32_t)n * (K >> 4));
         mbar_arrive_expect_tx(&r.full[slot], on ? (uint32_t)S * (qb + db) : 0u);
         if (on) {
@@ -406,6 +417,8 @@ __device__ __forceinline__ bool fused_produce(const PhaseDesc* pp, const DecRing
         if (sub && u == u0) sub[SUB_PROD_ISSUE] = globaltimer_ns();
         u += n;
     }
+    // a CTA without units still takes this phase of the routing barrier (phases are awaited in order)
+    if (route_bar && !slot_wait(route_bar, route_parity, err, kProducerBackoffNs)) return false;
     const uint32_t dq = (uint32_t)kMoeDU * EO, need2 = (dq + 4u * EO + 127u) & ~127u;
     for (int u = u0; u < u1; ++pr.i) {
         const int n = moe_stage_len(u, u1, N, kMoeDU);
@@ -474,16 +487,22 @@ __device__ void dec_producer(const PhaseDesc* prog, int n_phases, DecRing r, Dec
                     if (p2->type == PH_GEMV) budget = prefetch_phase_l2(p2, budget);
                 }
             }
-            // Wait for this CTA's routing.  (Pulling the rows of the next phase into L2 meanwhile,
-            // from the moment the phase's input is there, was measured slower: 706 -> 732 us per
-            // step; the copies compete with the expert rows and the next phase's own stream.)
-            if (!slot_wait(&route->bar, routed & 1u, err, kProducerBackoffNs)) goto drain;
+            // Wait for this CTA's routing (a fused phase waits inside fused_produce, after reserving
+            // its first stage).  (Pulling the rows of the next phase into L2 meanwhile, from the
+            // moment the phase's input is there, was measured slower: 706 -> 732 us per step; the
+            // copies compete with the expert rows and the next phase's own stream.)
+            if (pp->type != PH_FUSED) {
+                if (!slot_wait(&route->bar, routed & 1u, err, kProducerBackoffNs)) goto drain;
+                if (sub) sub[(size_t)ph * kSubStamps + SUB_PROD_ROUTED] = globaltimer_ns();
+            }
             ++routed;
-            if (sub) sub[(size_t)ph * kSubStamps + SUB_PROD_ROUTED] = globaltimer_ns();
         }
         const uint32_t i_first = pr.i;  // the phase's first weight stage (stamped once issued)
         if (pp->type == PH_FUSED) {
-            if (!fused_produce(pp, r, route, pr, pol, err, sub ? sub + (size_t)ph * kSubStamps : nullptr)) goto drain;
+            const bool rt = pp->r_qs != nullptr;
+            if (!fused_produce(pp, r, route, pr, pol, err, sub ? sub + (size_t)ph * kSubStamps : nullptr,
+                               rt ? &route->bar : nullptr, (routed - 1u) & 1u))
+                goto drain;
             continue;
         }
         {
@@ -826,44 +845,40 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
         __syncwarp();
         if (lane == 0) mbar_arrive(&r.empty[slot]);
         const int j = lane >> 3;
-        if ((lane & 7) == 0 && j < n_rows) route->logit[row0 + j] = sum;
+        if ((lane & 7) == 0 && j < n_rows) {
+            route->logit[row0 + j] = sum;
+            route->prob[row0 + j] = 1.0f / (1.0f + expf(-sum));
+        }
     }
     i += 2;
     named_bar(1, kConsumerThreads);
     sub_stamp(SUB_ROUTE_DOTS);
     if (warp == kRouteWarp) {  // not warp 0: it shares a sub-partition with the producer warp
         const bool live = lane < ne;
-        const float prob = live ? 1.0f / (1.0f + expf(-route->logit[lane])) : 0.f;
+        const float prob = live ? route->prob[lane] : 0.f;
         const float sel = live ? prob + bias_v : -INFINITY;
         // rank of this expert in the stable descending order of the selection scores (a higher
         // score first; the lower id first on a tie): 32 independent comparisons, no dependent
-        // reduction chain.  The top-k are the experts of rank 0..k-1 (lfm2-engine.js:434-442).
+        // reduction chain.  The top-k are the experts of rank 0..k-1 (lfm2-engine.js:434-442);
+        // the expert of rank k < 4 writes itself into slot k (ne >= 4 for a routed phase).
         int rank = 0;
 #pragma unroll
         for (int j = 0; j < 32; j++) {
             const float o = __shfl_sync(0xffffffffu, sel, j);
             rank += (o > sel || (o == sel && j < lane)) ? 1 : 0;
         }
-        double sum_w = 1e-6;
-        int top_i[4];
-        float top_p[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const unsigned m = __ballot_sync(0xffffffffu, live && rank == k);
-            int bi = m ? __ffs(m) - 1 : 0;
-            if (bi >= ne) bi = 0;
-            top_i[k] = bi;
-            top_p[k] = __shfl_sync(0xffffffffu, prob, bi & 31);
+        if (live && rank < 4) {
+            route->top_i[rank] = lane;
+            route->top_p[rank] = prob;
         }
-#pragma unroll
-        for (int k = 0; k < 4; k++) sum_w += (double)top_p[k];  // selection order, as the JS sums
-        const double inv = 1.0 / sum_w;
+        __syncwarp();
         if (lane < 4) {
-            float wk = 0.f;
-            int ik = 0;
+            double sum_w = 1e-6;
 #pragma unroll
-            for (int k = 0; k < 4; k++)
-                if (lane == k) { wk = (float)((double)top_p[k] * inv); ik = top_i[k]; }
+            for (int k = 0; k < 4; k++) sum_w += (double)route->top_p[k];  // selection order, as the JS sums
+            const double inv = 1.0 / sum_w;
+            const int ik = route->top_i[lane];
+            const float wk = (float)((double)route->top_p[lane] * inv);
             route->id[lane] = ik;
             route->skip[lane] = (int)((mword >> (ik & 31)) & 1u);
             route->w[lane] = wk;
