@@ -131,8 +131,12 @@ enum DecSub : int {
     SUB_ROUTE_DOTS = 9,   // the router logits are complete (routed phases)
     SUB_PROD_ROUTED = 10, // the producer thread has seen the routing (routed phases)
     SUB_PROD_ISSUE = 11,  // the producer thread has issued the phase's first weight stage
+    SUB_TOPK_START = 12,  // the top-k warp starts (routed phases)
+    SUB_TOPK_RANKS = 13,  // the top-k warp has the ranks
+    SUB_TOPK_DONE = 14,   // the top-k warp has the ids and weights (before it releases the producer)
+    SUB_SPARE = 15,
 };
-constexpr int kSubStamps = 12;
+constexpr int kSubStamps = 16;
 
 // Shared-memory plan of the persistent kernel: a byte ring of kDecRingBytes holding up to
 // kDecSlots in-flight stages of any size (so bytes in flight fill the ring whatever the phase),

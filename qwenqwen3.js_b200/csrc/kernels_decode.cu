@@ -79,6 +79,10 @@ __shared__ unsigned long long* s_sub;
 __device__ __forceinline__ void sub_stamp(int k) {
     if (threadIdx.x == 0 && s_sub) s_sub[k] = globaltimer_ns();
 }
+// The same from lane 0 of any consumer warp (s_sub is published by the barrier at the phase top).
+__device__ __forceinline__ void sub_stamp_lane0(int k) {
+    if ((threadIdx.x & 31) == 0 && s_sub) s_sub[k] = globaltimer_ns();
+}
 
 __device__ __forceinline__ uint32_t step_tag(uint32_t epoch, int ph) { return epoch * 256u + (uint32_t)ph + 1u; }
 
@@ -197,6 +201,7 @@ struct DecRoute {
     float w[4];
     float logit[kMaxRoutes];
     float prob[kMaxRoutes];  // sigmoid of the logits
+    __align__(16) float sel[kMaxRoutes];  // selection scores (prob + bias; -inf past n_expert)
     int top_i[4];            // the selected experts in selection order, and their probabilities
     float top_p[4];
     uint64_t bar;  // completes once per MoE layer: the producer may read id[]
@@ -854,6 +859,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
     named_bar(1, kConsumerThreads);
     sub_stamp(SUB_ROUTE_DOTS);
     if (warp == kRouteWarp) {  // not warp 0: it shares a sub-partition with the producer warp
+        sub_stamp_lane0(SUB_TOPK_START);
         const bool live = lane < ne;
         const float prob = live ? route->prob[lane] : 0.f;
         const float sel = live ? prob + bias_v : -INFINITY;
@@ -861,17 +867,28 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
         // score first; the lower id first on a tie): 32 independent comparisons, no dependent
         // reduction chain.  The top-k are the experts of rank 0..k-1 (lfm2-engine.js:434-442);
         // the expert of rank k < 4 writes itself into slot k (ne >= 4 for a routed phase).
-        int rank = 0;
+        // every lane reads all 32 scores back as 8 broadcast 16-byte loads (a chain of 32 shuffles
+        // measured ~0.6 us)
+        route->sel[lane] = sel;
+        __syncwarp();
+        int before[8];
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const float o = __shfl_sync(0xffffffffu, sel, j);
-            rank += (o > sel || (o == sel && j < lane)) ? 1 : 0;
+        for (int c = 0; c < 8; c++) {
+            const float4 o = reinterpret_cast<const float4*>(route->sel)[c];
+            const int j = 4 * c;
+            before[c] = ((o.x > sel || (o.x == sel && j < lane)) ? 1 : 0) +
+                        ((o.y > sel || (o.y == sel && j + 1 < lane)) ? 1 : 0) +
+                        ((o.z > sel || (o.z == sel && j + 2 < lane)) ? 1 : 0) +
+                        ((o.w > sel || (o.w == sel && j + 3 < lane)) ? 1 : 0);
         }
+        const int rank = ((before[0] + before[1]) + (before[2] + before[3])) +
+                         ((before[4] + before[5]) + (before[6] + before[7]));
         if (live && rank < 4) {
             route->top_i[rank] = lane;
             route->top_p[rank] = prob;
         }
         __syncwarp();
+        sub_stamp_lane0(SUB_TOPK_RANKS);
         if (lane < 4) {
             double sum_w = 1e-6;
 #pragma unroll
@@ -891,6 +908,7 @@ __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, con
         }
         if (blockIdx.x == 0 && live) p.rec[8 + lane] = prob;
         __syncwarp();
+        sub_stamp_lane0(SUB_TOPK_DONE);
         if (lane == 0) mbar_arrive(&route->bar);  // release: the producer may read id[]
     }
     named_bar(1, kConsumerThreads);
