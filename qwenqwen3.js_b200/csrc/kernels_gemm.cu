@@ -412,6 +412,7 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
 // Exact three-product split only (as SPLIT = 3 above): y = hh + (hl + lh) / 2048.
 constexpr int kRowsBM = 128;       // weight rows per item
 constexpr int kRowsKR = 256;       // K of one raw weight stage (four 64-wide MMA K steps)
+constexpr int kRowsKPS = 2;        // 64-wide K steps per operand stage (one handshake each)
 constexpr int kRowsMaxItems = 296; // S * row tiles <= this when S > 1
 constexpr int kRowsTickets = 256;  // >= row tiles whenever S > 1
 constexpr int kRowsWarps = 11;     // 8 converters, raw producer, MMA issuer, activation producer
@@ -420,21 +421,22 @@ constexpr int kRowsThreads = kRowsWarps * 32;
 template <int MN>
 struct RowsCfg {
     static constexpr int RawStages = 5;                 // 170 KB of weight reads in flight per SM
-    static constexpr int OpStages = 4;                  // converted K steps in tensor memory
+    static constexpr int OpStages = MN == 16 ? 3 : 2;   // operand stages (kRowsKPS K steps) in TMEM
     static constexpr int XStages = OpStages;            // released by the same MMA commit
     static constexpr int XTile = MN * kBK * 2;          // 2 / 4 KB fp16 activations (hi or lo)
     static constexpr int RawBox = kRowsBM * 128;        // one swizzled 128-byte-wide box: 16 KB
     static constexpr int DTile = kRowsBM * 16;          // block scales: 8 fp16 per row (256 K)
     static constexpr int RawStage = (2 * RawBox + DTile + 1023) & ~1023;
-    static constexpr int XStage = 2 * XTile;
+    static constexpr int XStage = kRowsKPS * 2 * XTile;  // per K step: hi rows, then lo rows
     static constexpr int Smem = RawStages * RawStage + XStages * XStage + 1024;
     static constexpr uint32_t IdescHL = (1u << 4) | ((uint32_t)((2 * MN) >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
     static constexpr uint32_t IdescL = (1u << 4) | ((uint32_t)(MN >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
     static constexpr uint32_t AccCols = MN == 16 ? 64 : 128;  // per pair: [hh | hl] at +0, lh at +2 MN
-    static constexpr uint32_t OpCols = 64;              // per K step: hi (4 x 8 columns) | lo
+    static constexpr uint32_t OpCols = 64 * kRowsKPS;   // per K step: hi (4 x 8 columns) | lo
     static constexpr uint32_t OpBase = 2 * AccCols;
     static constexpr uint32_t TmemCols = 512;
     static_assert(OpBase + OpStages * OpCols <= TmemCols, "tensor memory columns");
+    static_assert(kRowsKR / kBK % kRowsKPS == 0, "operand stages tile a raw stage");
     static_assert(3 * MN <= (int)AccCols, "accumulator pair columns");
 };
 
@@ -474,10 +476,14 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int nk = (K + kBK - 1) / kBK;          // 64-wide MMA K steps
     const int nr = (K + kRowsKR - 1) / kRowsKR;  // 256-wide raw stages
+    constexpr int SPR = kRowsKR / kBK / kRowsKPS;  // operand stages per raw stage
+    const int nks = (nk + kRowsKPS - 1) / kRowsKPS;  // operand stages of the whole K range
     const int KB = K >> 5;
     // shared memory: raw weight stages | activation stages
     auto raw_stage = [&](int rs) { return smem + rs * G::RawStage; };
-    auto x_tile = [&](int xs, int h) { return smem + R * G::RawStage + xs * G::XStage + h * G::XTile; };
+    auto x_tile = [&](int xs, int sub, int h) {
+        return smem + R * G::RawStage + xs * G::XStage + (2 * sub + h) * G::XTile;
+    };
     // item it: row tile it / S, split it % S (raw stages [r0, r1))
     auto item_range = [&](int it, int& n0, int& sp, int& r0, int& r1) {
         n0 = (it / S) * kRowsBM;
@@ -538,13 +544,18 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
                 int n0, sp, r0, r1;
                 item_range(it, n0, sp, r0, r1);
-                for (int kt = 4 * r0; kt < min(4 * r1, nk) && ok; kt++, o++) {
+                for (int ks2 = SPR * r0; ks2 < min(SPR * r1, nks) && ok; ks2++, o++) {
                     const int xs = o % X;
                     if (o >= X) ok = bar_wait(&op_free[xs], (uint32_t)((o / X - 1) & 1), err);
                     if (!ok) break;
+                    // a K step past K reads zeros (its coordinate stays a multiple of 128 bytes)
                     mbar_arrive_expect_tx(&full_x[xs], (uint32_t)G::XStage);
-                    tma_2d(x_tile(xs, 0), &tmX, kt * kBK, 0, &full_x[xs]);
-                    tma_2d(x_tile(xs, 1), &tmX, kt * kBK, M, &full_x[xs]);
+#pragma unroll
+                    for (int sub = 0; sub < kRowsKPS; sub++) {
+                        const int kt = kRowsKPS * ks2 + sub;
+                        tma_2d(x_tile(xs, sub, 0), &tmX, kt * kBK, 0, &full_x[xs]);
+                        tma_2d(x_tile(xs, sub, 1), &tmX, kt * kBK, M, &full_x[xs]);
+                    }
                 }
             }
             for (int i = (o > X ? o - X : 0); i < o; i++)
@@ -561,20 +572,25 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t acc_d = tmem + (uint32_t)ab * G::AccCols;
-                for (int kt = 4 * r0; kt < min(4 * r1, nk) && ok; kt++, o++) {
+                for (int ks2 = SPR * r0; ks2 < min(SPR * r1, nks) && ok; ks2++, o++) {
                     const int os = o % O, xs = o % X;
                     ok = bar_wait(&full_x[xs], (uint32_t)((o / X) & 1), err) &&
                          bar_wait(&conv_done[os], (uint32_t)((o / O) & 1), err);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t a_hi = tmem + G::OpBase + (uint32_t)os * G::OpCols, a_lo = a_hi + 32u;
-                    const uint32_t xh = smem_u32(x_tile(xs, 0));
 #pragma unroll
-                    for (int ks = 0; ks < kBK / 16; ks++) {
-                        const uint32_t acc = (kt != 4 * r0 || ks != 0) ? 1u : 0u;
-                        const uint64_t bx = umma_desc(xh + 32u * ks);
-                        umma_f16_tmem_a(acc_d, a_hi + 8u * ks, bx, G::IdescHL, acc);
-                        umma_f16_tmem_a(acc_d + 2u * MN, a_lo + 8u * ks, bx, G::IdescL, acc);
+                    for (int sub = 0; sub < kRowsKPS; sub++) {
+                        const int kt = kRowsKPS * ks2 + sub;
+                        if (kt >= nk) break;  // its operand columns were not written
+                        const uint32_t a_hi = tmem + G::OpBase + (uint32_t)os * G::OpCols + 64u * sub, a_lo = a_hi + 32u;
+                        const uint32_t xh = smem_u32(x_tile(xs, sub, 0));
+#pragma unroll
+                        for (int ks = 0; ks < kBK / 16; ks++) {
+                            const uint32_t acc = (kt != 4 * r0 || ks != 0) ? 1u : 0u;
+                            const uint64_t bx = umma_desc(xh + 32u * ks);
+                            umma_f16_tmem_a(acc_d, a_hi + 8u * ks, bx, G::IdescHL, acc);
+                            umma_f16_tmem_a(acc_d + 2u * MN, a_lo + 8u * ks, bx, G::IdescL, acc);
+                        }
                     }
                     umma_commit(&op_free[os]);  // frees the operand columns and the activation stage
                 }
@@ -614,7 +630,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 for (int js = 0; js < 4 && ok; js++) {
                     const int kt = 4 * rt + js;
                     if (kt >= nk) break;
-                    const int os = o % O;
+                    const int os = o % O, sub = js % kRowsKPS;
                     // 32 weights at K 64 js + 32 kh of the stage: box js / 2, 16-byte chunks c0 and
                     // c0 + 1 of the row, stored at chunk c ^ (row & 7) (128-byte swizzle)
                     const int c0 = 4 * (js & 1) + 2 * kh;
@@ -625,19 +641,24 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                     const int b = 2 * js + kh;  // block within the stage
                     const uint32_t sword = (b >> 1) == 0 ? s8.x : ((b >> 1) == 1 ? s8.y : ((b >> 1) == 2 ? s8.z : s8.w));
                     const __half hs = __ushort_as_half((unsigned short)((b & 1) ? (sword >> 16) : (sword & 0xffffu)));
-                    if (o >= O) ok = __all_sync(0xffffffffu, bar_wait(&op_free[os], (uint32_t)((o / O - 1) & 1), err));
+                    if (sub == 0 && o >= O)
+                        ok = __all_sync(0xffffffffu, bar_wait(&op_free[os], (uint32_t)((o / O - 1) & 1), err));
                     if (!ok) break;
-                    tc_fence_after();
+                    if (sub == 0) tc_fence_after();
                     uint32_t hw[4][4], lw[4][4];
                     split3_words(raw, __halves2half2(hs, hs), hw, lw);
-                    const uint32_t col = tmem + lane_base + G::OpBase + (uint32_t)os * G::OpCols + 16u * kh;
+                    const uint32_t col =
+                        tmem + lane_base + G::OpBase + (uint32_t)os * G::OpCols + 64u * sub + 16u * kh;
                     tmem_st16(col, hw);
                     tmem_st16(col + 32u, lw);
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&conv_done[os]);
-                    o++;
+                    // the operand stage is complete after its last K step (or the last one of K)
+                    if (sub == kRowsKPS - 1 || kt == nk - 1) {
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&conv_done[os]);
+                        o++;
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_free[rs]);  // the stage's bytes are in registers / TMEM
