@@ -311,7 +311,7 @@ EPI_KINDS = {0: "store", 1: "resid", 2: "swiglu", 3: "conv", 4: "argmax"}
 
 SUB_POINTS = ("input", "staged", "routed", "first_stage", "part1", "part2", "reduced", "published",
               "route_stage", "route_dots", "prod_routed", "prod_issue", "topk_start", "topk_ranks", "topk_done",
-              "spare")
+              "route_start")
 
 
 def trace_summary(stamps, kinds, sub=None) -> dict:

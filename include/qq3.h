@@ -316,7 +316,7 @@ int qq_decode_trace(qq_model* m, int enable, uint64_t* stamps_out, int32_t* kind
  * 6 bulk reduction performed (attention: split counter taken), 7 output published, 8 router stage
  * landed, 9 router logits complete, 10 the producer thread saw the routing, 11 the producer thread
  * issued the phase's first weight stage, 12-14 the top-k warp starts / has the ranks / has the ids
- * and weights, 15 unused. */
+ * and weights, 15 the CTA starts routing. */
 int qq_decode_trace_sub(qq_model* m, uint64_t* out, int* n_sub);
 /* Expert-parallel models: switch the CUDA-event split of every MoE exchange on (enable = 1) or
  * off, and read (ms_out, nullable, 5 floats) the time summed since the last call over the

@@ -134,7 +134,7 @@ enum DecSub : int {
     SUB_TOPK_START = 12,  // the top-k warp starts (routed phases)
     SUB_TOPK_RANKS = 13,  // the top-k warp has the ranks
     SUB_TOPK_DONE = 14,   // the top-k warp has the ids and weights (before it releases the producer)
-    SUB_SPARE = 15,
+    SUB_ROUTE_START = 15,  // the CTA starts routing (after the RMSNorm factor of the staged input)
 };
 constexpr int kSubStamps = 16;
 

@@ -822,6 +822,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g * (1.0f /
 // (stable: the lower expert id wins a tie); weights = p / (sum + 1e-6).
 __device__ void dec_route(const PhaseDesc& p, const DecRing& r, uint32_t& i, const uint4* dig, const float* xsc,
                           float sc, int nch, float bias_v, DecRoute* route, int* err) {
+    sub_stamp(SUB_ROUTE_START);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = p.K, ne = p.n_expert;
     const int set = warp / 4, w = warp % 4;
