@@ -135,6 +135,10 @@ void launch_add_rows(float* x, const float* d, size_t n, cudaStream_t s);
 void launch_swiglu_rows(const float* g, const float* u, size_t n, float* h, cudaStream_t s);
 void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T, int pos0, int n_head, int n_kv,
                          int hd, int max_ctx, float* out, cudaStream_t s);
+// the same on the tensor cores (kernels_attn_tc.cu): hd 64 or 128, 128 % (n_head / n_kv) == 0
+bool attn_prefill_tc_supported(int n_head, int n_kv, int hd);
+void launch_attn_prefill_tc(const float* q, const float* kc, const float* vc, int T, int pos0, int n_head, int n_kv,
+                            int hd, int max_ctx, float* out, cudaStream_t s);
 // multi-sequence decode rows (kernels_prefill.cu): row t is sequence seq[t] (device) at position
 // pos[t] (device); the KV cache / conv state of sequence s start seq_stride / state_stride floats
 // after the given base pointer

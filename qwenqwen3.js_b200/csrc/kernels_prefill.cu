@@ -648,6 +648,15 @@ void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T
     const int G = n_head / n_kv;
     QQ_CHECK(G >= 1 && G <= 32 && n_head % n_kv == 0, -4, "prefill attention: unsupported head grouping");
     if (T <= 0) return;
+    // tensor cores (kernels_attn_tc.cu) unless QQ3_ATTN_TC=0
+    static const bool tc_off = [] {
+        const char* e = getenv("QQ3_ATTN_TC");
+        return e && atoi(e) == 0;
+    }();
+    if (!tc_off && attn_prefill_tc_supported(n_head, n_kv, hd)) {
+        launch_attn_prefill_tc(q, kc, vc, T, pos0, n_head, n_kv, hd, max_ctx, out, s);
+        return;
+    }
     if (G <= kPfWarps * kPfRows && (kPfWarps * kPfRows) % G == 0 && !tiled_attention_off()) {
         // query tiles: K / V read once per 64 query rows (k_attn_prefill_tile)
         const int QT = kPfWarps * kPfRows / G;
