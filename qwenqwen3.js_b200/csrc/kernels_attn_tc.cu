@@ -140,40 +140,64 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int pass = 0; pass < 2; pass++) {
         for (int kt = 0; kt < n_tiles; kt++) {
             const int k0 = kt * kTcKeys;
-            // the K tile (keys past n_keys are zero), and in pass 2 V transposed
-            for (int f = t; f < kTcKeys * (HD / 8); f += kTcThreads) {
-                const int j = f / (HD / 8), c = f % (HD / 8);
-                float v[8];
-                if (k0 + j < n_keys) {
-                    const float* kr = kb + (size_t)(k0 + j) * HD + 8 * c;
-                    const float4 a = __ldg(reinterpret_cast<const float4*>(kr));
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(kr + 4));
-                    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-                } else {
+            // the K tile (keys past n_keys are zero), and in pass 2 V transposed; every load of a
+            // group of four tasks is issued before the first conversion (one round trip each)
+            constexpr int kTasks = kTcKeys * (HD / 8) / kTcThreads;  // per thread, K and V alike
+            static_assert(kTasks % 4 == 0, "task groups of four");
 #pragma unroll
-                    for (int i = 0; i < 8; i++) v[i] = 0.f;
+            for (int g0 = 0; g0 < kTasks; g0 += 4) {
+                float v[4][8];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int f = t + (g0 + u) * kTcThreads;
+                    const int j = f / (HD / 8), c = f % (HD / 8);
+                    if (k0 + j < n_keys) {
+                        const float* kr = kb + (size_t)(k0 + j) * HD + 8 * c;
+                        const float4 a = __ldg(reinterpret_cast<const float4*>(kr));
+                        const float4 b = __ldg(reinterpret_cast<const float4*>(kr + 4));
+                        v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+                        v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; i++) v[u][i] = 0.f;
+                    }
                 }
-                uint4 hi, lo;
-                split8(v, hi, lo);
-                const uint32_t off = tile_chunk(kTcKeys, j, c);
-                *reinterpret_cast<uint4*>(Kh + off) = hi;
-                *reinterpret_cast<uint4*>(Kl + off) = lo;
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int f = t + (g0 + u) * kTcThreads;
+                    const int j = f / (HD / 8), c = f % (HD / 8);
+                    uint4 hi, lo;
+                    split8(v[u], hi, lo);
+                    const uint32_t off = tile_chunk(kTcKeys, j, c);
+                    *reinterpret_cast<uint4*>(Kh + off) = hi;
+                    *reinterpret_cast<uint4*>(Kl + off) = lo;
+                }
             }
             if (pass == 1) {
-                // thread (dim d, 8 keys jc): consecutive threads read consecutive dims of a key row
-                for (int f = t; f < HD * (kTcKeys / 8); f += kTcThreads) {
-                    const int d = f % HD, jc = f / HD;
-                    float v[8];
+                // task (dim d, 8 keys jc): consecutive threads read consecutive dims of a key row
 #pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        const int j = k0 + 8 * jc + i;
-                        v[i] = j < n_keys ? __ldg(vb + (size_t)j * HD + d) : 0.f;
+                for (int g0 = 0; g0 < kTasks; g0 += 4) {
+                    float v[4][8];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int f = t + (g0 + u) * kTcThreads;
+                        const int d = f % HD, jc = f / HD;
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const int j = k0 + 8 * jc + i;
+                            v[u][i] = j < n_keys ? __ldg(vb + (size_t)j * HD + d) : 0.f;
+                        }
                     }
-                    uint4 hi, lo;
-                    split8(v, hi, lo);
-                    const uint32_t off = sw128(d, jc);
-                    *reinterpret_cast<uint4*>(Vh + off) = hi;
-                    *reinterpret_cast<uint4*>(Vl + off) = lo;
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int f = t + (g0 + u) * kTcThreads;
+                        const int d = f % HD, jc = f / HD;
+                        uint4 hi, lo;
+                        split8(v[u], hi, lo);
+                        const uint32_t off = sw128(d, jc);
+                        *reinterpret_cast<uint4*>(Vh + off) = hi;
+                        *reinterpret_cast<uint4*>(Vl + off) = lo;
+                    }
                 }
             }
             fence_async_smem();  // the tiles are read by the tensor cores (async proxy)
