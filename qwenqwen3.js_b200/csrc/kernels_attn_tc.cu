@@ -6,8 +6,9 @@
 // loops; here a CTA takes 128 query rows of one kv head (128 / G consecutive tokens x its G query
 // heads: the UMMA's M) and walks the keys in tiles of 64 (the N of the scores, the K of P.V):
 //
-//   pass 1   S = Q.K^T per tile on the tensor cores (TMEM accumulators); each of the 128 threads
-//            owns one query row (its TMEM lane) and keeps the row maximum m;
+//   pass 1   S = Q.K^T per tile on the tensor cores (TMEM accumulators); two of the 256 threads
+//            own a query row (its TMEM lane: warps w and w + 4), one half of its columns each,
+//            and keep the row maximum m;
 //   pass 2   S again; p = exp(s - m) (0 past the row's position), l += p, the tile's P written to
 //            shared memory as the A operand of O += P.V (O in TMEM); at the end o = O / l.
 //
@@ -31,7 +32,7 @@ namespace {
 
 constexpr int kTcRows = 128;   // query rows per CTA (UMMA M)
 constexpr int kTcKeys = 64;    // keys per tile
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 256;  // two threads per query row: column halves
 
 template <int HD>
 struct AttnTcCfg {
@@ -86,6 +87,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t* Pl = Ph + C::PPlane;
     __shared__ __align__(8) uint64_t mma_bar;
     __shared__ uint32_t tmem_slot;
+    __shared__ float row_red[kTcThreads];  // the two halves' row maxima, then sums
     const int t = threadIdx.x, warp = t >> 5;
     const int G = n_head / n_kv, QT = kTcRows / G;
     const int t0 = blockIdx.x * QT, kvh = blockIdx.y;
@@ -99,13 +101,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_init(&mma_bar, 1);
         mbar_fence_init();
     }
-    // thread t owns query row t: token t0 + t / G, head kvh G + t % G
-    const int row = t, tok = t0 + row / G, head = kvh * G + row % G;
+    // thread t holds query row t % 128 (token t0 + row / G, head kvh G + row % G), column half t / 128
+    const int row = t & (kTcRows - 1), half = t / kTcRows, tok = t0 + row / G, head = kvh * G + row % G;
     const bool live = tok < T;
     {
         const float* qr = q + ((size_t)tok * n_head + head) * HD;
 #pragma unroll 2
-        for (int c = 0; c < HD / 8; c++) {
+        for (int c = half * (HD / 16); c < (half + 1) * (HD / 16); c++) {
             float v[8];
             if (live) {
                 const float4 a = __ldg(reinterpret_cast<const float4*>(qr + 8 * c));
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const int t_last = min(T, t0 + QT) - 1;
     const int n_keys = pos0 + t_last + 1;  // keys 0 .. the tile's last position
     const int my_pos = pos0 + tok;         // this row sees keys 0 .. my_pos
@@ -138,17 +140,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int pass = 0; pass < 2; pass++) {
+        if (pass == 1) {  // the row maximum over both column halves
+            row_red[t] = m;
+            __syncthreads();
+            m = fmaxf(row_red[row], row_red[row + kTcRows]);
+            __syncthreads();
+        }
         for (int kt = 0; kt < n_tiles; kt++) {
             const int k0 = kt * kTcKeys;
             // the K tile (keys past n_keys are zero), and in pass 2 V transposed; every load of a
             // group of four tasks is issued before the first conversion (one round trip each)
             constexpr int kTasks = kTcKeys * (HD / 8) / kTcThreads;  // per thread, K and V alike
-            static_assert(kTasks % 4 == 0, "task groups of four");
+            constexpr int kGrp = kTasks < 4 ? kTasks : 4;
+            static_assert(kTasks % kGrp == 0, "task groups");
 #pragma unroll
-            for (int g0 = 0; g0 < kTasks; g0 += 4) {
-                float v[4][8];
+            for (int g0 = 0; g0 < kTasks; g0 += kGrp) {
+                float v[kGrp][8];
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
+                for (int u = 0; u < kGrp; u++) {
                     const int f = t + (g0 + u) * kTcThreads;
                     const int j = f / (HD / 8), c = f % (HD / 8);
                     if (k0 + j < n_keys) {
@@ -163,7 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
+                for (int u = 0; u < kGrp; u++) {
                     const int f = t + (g0 + u) * kTcThreads;
                     const int j = f / (HD / 8), c = f % (HD / 8);
                     uint4 hi, lo;
@@ -176,10 +185,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (pass == 1) {
                 // task (dim d, 8 keys jc): consecutive threads read consecutive dims of a key row
 #pragma unroll
-                for (int g0 = 0; g0 < kTasks; g0 += 4) {
-                    float v[4][8];
+                for (int g0 = 0; g0 < kTasks; g0 += kGrp) {
+                    float v[kGrp][8];
 #pragma unroll
-                    for (int u = 0; u < 4; u++) {
+                    for (int u = 0; u < kGrp; u++) {
                         const int f = t + (g0 + u) * kTcThreads;
                         const int d = f % HD, jc = f / HD;
 #pragma unroll
@@ -189,7 +198,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                     }
 #pragma unroll
-                    for (int u = 0; u < 4; u++) {
+                    for (int u = 0; u < kGrp; u++) {
                         const int f = t + (g0 + u) * kTcThreads;
                         const int d = f % HD, jc = f / HD;
                         uint4 hi, lo;
@@ -226,7 +235,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             // this row's scores: pass 1 the maximum, pass 2 p into the P tile
 #pragma unroll 1
-            for (int c0 = 0; c0 < kTcKeys; c0 += 16) {
+            for (int c0 = half * (kTcKeys / 2); c0 < (half + 1) * (kTcKeys / 2); c0 += 16) {
                 uint32_t s1[16], s2[16];
                 tmem_ld16(tmem + lane_base + C::ColS1 + (uint32_t)c0, s1);
                 tmem_ld16(tmem + lane_base + C::ColS2 + (uint32_t)c0, s2);
@@ -285,12 +294,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     }
-    // o = (O1 + O2 / 2048) / l for this row
+    // o = (O1 + O2 / 2048) / l for this row (l summed over both column halves)
+    row_red[t] = l;
+    __syncthreads();
+    l = row_red[row] + row_red[row + kTcRows];
     if (n_tiles > 0) {
         const float inv = l > 0.f ? 1.0f / l : 0.f;
         float* o = out + ((size_t)tok * n_head + head) * HD;
 #pragma unroll 1
-        for (int c0 = 0; c0 < HD; c0 += 16) {
+        for (int c0 = half * (HD / 2); c0 < (half + 1) * (HD / 2); c0 += 16) {
             uint32_t o1[16], o2[16];
             tmem_ld16(tmem + lane_base + C::ColO1 + (uint32_t)c0, o1);
             tmem_ld16(tmem + lane_base + C::ColO2 + (uint32_t)c0, o2);
