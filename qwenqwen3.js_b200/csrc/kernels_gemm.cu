@@ -378,32 +378,39 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
 // Exact three-product split only (as SPLIT = 3 above): y = hh + (hl + lh) / 2048.
 constexpr int kRowsBM = 128;       // weight rows per item
 constexpr int kRowsKR = 256;       // K of one raw weight stage (four 64-wide MMA K steps)
-constexpr int kRowsKPS = 2;        // 64-wide K steps per operand stage (one handshake each)
 constexpr int kRowsMaxItems = 296; // S * row tiles <= this when S > 1
 constexpr int kRowsTickets = 256;  // >= row tiles whenever S > 1
 constexpr int kRowsWarps = 11;     // 8 converters, raw producer, MMA issuer, activation producer
 constexpr int kRowsThreads = kRowsWarps * 32;
 
+// MN = 16 / 32: all activation rows of a few-row product in one item; MN = 128: the wide form for
+// many rows (prefill), items over (weight tile, 128-row activation tile) with one accumulator set
+// of 384 columns ([hh | hl] N = 256, lh N = 128), so the MMAs run at N = 256 / 128.
 template <int MN>
 struct RowsCfg {
-    static constexpr int RawStages = 5;                 // 170 KB of weight reads in flight per SM
-    static constexpr int OpStages = MN == 16 ? 3 : 2;   // operand stages (kRowsKPS K steps) in TMEM
+    static constexpr bool Wide = MN > 32;
+    static constexpr int KPS = Wide ? 1 : 2;            // 64-wide K steps per operand stage (one handshake)
+    static constexpr int RawStages = Wide ? 4 : 5;      // 136 / 170 KB of weight reads in flight per SM
+    static constexpr int OpStages = MN == 16 ? 3 : 2;   // operand stages in TMEM
     static constexpr int XStages = OpStages;            // released by the same MMA commit
-    static constexpr int XTile = MN * kBK * 2;          // 2 / 4 KB fp16 activations (hi or lo)
+    static constexpr int NumAcc = Wide ? 1 : 2;         // accumulator sets (items alternate)
+    static constexpr int RowsPerWarp = Wide ? MN / 2 : 16;  // activation rows a converter warp stores
+    static constexpr int XTile = MN * kBK * 2;          // fp16 activations (hi or lo) of one K step
     static constexpr int RawBox = kRowsBM * 128;        // one swizzled 128-byte-wide box: 16 KB
     static constexpr int DTile = kRowsBM * 16;          // block scales: 8 fp16 per row (256 K)
     static constexpr int RawStage = (2 * RawBox + DTile + 1023) & ~1023;
-    static constexpr int XStage = kRowsKPS * 2 * XTile;  // per K step: hi rows, then lo rows
+    static constexpr int XStage = KPS * 2 * XTile;      // per K step: hi rows, then lo rows
     static constexpr int Smem = RawStages * RawStage + XStages * XStage + 1024;
     static constexpr uint32_t IdescHL = (1u << 4) | ((uint32_t)((2 * MN) >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
     static constexpr uint32_t IdescL = (1u << 4) | ((uint32_t)(MN >> 3) << 17) | ((uint32_t)(kRowsBM >> 4) << 24);
-    static constexpr uint32_t AccCols = MN == 16 ? 64 : 128;  // per pair: [hh | hl] at +0, lh at +2 MN
-    static constexpr uint32_t OpCols = 64 * kRowsKPS;   // per K step: hi (4 x 8 columns) | lo
-    static constexpr uint32_t OpBase = 2 * AccCols;
+    static constexpr uint32_t AccCols = MN == 16 ? 64 : 3 * MN;  // per set: [hh | hl] at +0, lh at +2 MN
+    static constexpr uint32_t OpCols = 64 * KPS;        // per K step: hi (4 x 8 columns) | lo
+    static constexpr uint32_t OpBase = NumAcc * AccCols;
     static constexpr uint32_t TmemCols = 512;
     static_assert(OpBase + OpStages * OpCols <= TmemCols, "tensor memory columns");
-    static_assert(kRowsKR / kBK % kRowsKPS == 0, "operand stages tile a raw stage");
-    static_assert(3 * MN <= (int)AccCols, "accumulator pair columns");
+    static_assert(kRowsKR / kBK % KPS == 0, "operand stages tile a raw stage");
+    static_assert(3 * MN <= (int)AccCols && 2 * MN <= 256, "accumulator columns, MMA width");
+    static_assert(Smem <= 227 * 1024, "shared memory");
 };
 
 // tcgen05.mma with the A operand in tensor memory (kind::f16: fp16 x fp16 -> f32)
@@ -432,6 +439,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                    const __half* __restrict__ d, int N, float* __restrict__ C, int ldc, float* __restrict__ part,
                    unsigned int* __restrict__ tickets, int S, int n_items, int* err) {
     using G = RowsCfg<MN>;
+    constexpr int KPS = G::KPS, NA = G::NumAcc;
     extern __shared__ uint8_t smem_raw[];
     constexpr int R = G::RawStages, O = G::OpStages, X = G::XStages;
     __shared__ __align__(8) uint64_t full_raw[R], raw_free[R], full_x[X], conv_done[O], op_free[O], acc_full[2],
@@ -442,17 +450,20 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int nk = (K + kBK - 1) / kBK;          // 64-wide MMA K steps
     const int nr = (K + kRowsKR - 1) / kRowsKR;  // 256-wide raw stages
-    constexpr int SPR = kRowsKR / kBK / kRowsKPS;  // operand stages per raw stage
-    const int nks = (nk + kRowsKPS - 1) / kRowsKPS;  // operand stages of the whole K range
+    constexpr int SPR = kRowsKR / kBK / KPS;  // operand stages per raw stage
+    const int nks = (nk + KPS - 1) / KPS;     // operand stages of the whole K range
+    const int n_at = (M + MN - 1) / MN;       // activation tiles (1 unless wide)
     const int KB = K >> 5;
     // shared memory: raw weight stages | activation stages
     auto raw_stage = [&](int rs) { return smem + rs * G::RawStage; };
     auto x_tile = [&](int xs, int sub, int h) {
         return smem + R * G::RawStage + xs * G::XStage + (2 * sub + h) * G::XTile;
     };
-    // item it: row tile it / S, split it % S (raw stages [r0, r1))
-    auto item_range = [&](int it, int& n0, int& sp, int& r0, int& r1) {
-        n0 = (it / S) * kRowsBM;
+    // item it: tile it / S = (weight row tile, activation tile) = (rows n0.., activation rows
+    // a0..), split it % S (raw stages [r0, r1))
+    auto item_range = [&](int it, int& n0, int& a0, int& sp, int& r0, int& r1) {
+        n0 = (it / S / n_at) * kRowsBM;
+        a0 = (it / S % n_at) * MN;
         sp = it % S;
         r0 = (int)(((long long)sp * nr) / S);
         r1 = (int)(((long long)(sp + 1) * nr) / S);
@@ -488,8 +499,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (lane == 0) {  // raw weight producer
             int r = 0;
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                int n0, sp, r0, r1;
-                item_range(it, n0, sp, r0, r1);
+                int n0, a0, sp, r0, r1;
+                item_range(it, n0, a0, sp, r0, r1);
                 for (int rt = r0; rt < r1 && ok; rt++, r++) {
                     const int rs = r % R;
                     if (r >= R) ok = bar_wait(&raw_free[rs], (uint32_t)((r / R - 1) & 1), err);
@@ -508,8 +519,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (lane == 0) {  // activation producer: hi rows at 0, lo rows at M
             int o = 0;
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                int n0, sp, r0, r1;
-                item_range(it, n0, sp, r0, r1);
+                int n0, a0, sp, r0, r1;
+                item_range(it, n0, a0, sp, r0, r1);
                 for (int ks2 = SPR * r0; ks2 < min(SPR * r1, nks) && ok; ks2++, o++) {
                     const int xs = o % X;
                     if (o >= X) ok = bar_wait(&op_free[xs], (uint32_t)((o / X - 1) & 1), err);
@@ -517,10 +528,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                     // a K step past K reads zeros (its coordinate stays a multiple of 128 bytes)
                     mbar_arrive_expect_tx(&full_x[xs], (uint32_t)G::XStage);
 #pragma unroll
-                    for (int sub = 0; sub < kRowsKPS; sub++) {
-                        const int kt = kRowsKPS * ks2 + sub;
-                        tma_2d(x_tile(xs, sub, 0), &tmX, kt * kBK, 0, &full_x[xs]);
-                        tma_2d(x_tile(xs, sub, 1), &tmX, kt * kBK, M, &full_x[xs]);
+                    for (int sub = 0; sub < KPS; sub++) {
+                        const int kt = KPS * ks2 + sub;
+                        tma_2d(x_tile(xs, sub, 0), &tmX, kt * kBK, a0, &full_x[xs]);
+                        tma_2d(x_tile(xs, sub, 1), &tmX, kt * kBK, M + a0, &full_x[xs]);
                     }
                 }
             }
@@ -531,10 +542,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         if (lane == 0) {  // MMA issuer
             int o = 0, j = 0;
             for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, j++) {
-                int n0, sp, r0, r1;
-                item_range(it, n0, sp, r0, r1);
-                const int ab = j & 1;
-                if (j >= 2) ok = bar_wait(&acc_free[ab], (uint32_t)((j / 2 - 1) & 1), err);
+                int n0, a0, sp, r0, r1;
+                item_range(it, n0, a0, sp, r0, r1);
+                const int ab = j % NA;
+                if (j >= NA) ok = bar_wait(&acc_free[ab], (uint32_t)((j / NA - 1) & 1), err);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t acc_d = tmem + (uint32_t)ab * G::AccCols;
@@ -545,8 +556,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                     if (!ok) break;
                     tc_fence_after();
 #pragma unroll
-                    for (int sub = 0; sub < kRowsKPS; sub++) {
-                        const int kt = kRowsKPS * ks2 + sub;
+                    for (int sub = 0; sub < KPS; sub++) {
+                        const int kt = KPS * ks2 + sub;
                         if (kt >= nk) break;  // its operand columns were not written
                         const uint32_t a_hi = tmem + G::OpBase + (uint32_t)os * G::OpCols + 64u * sub, a_lo = a_hi + 32u;
                         const uint32_t xh = smem_u32(x_tile(xs, sub, 0));
@@ -571,8 +582,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         int o = 0, r = 0, j = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, j++) {
-            int n0, sp, r0, r1;
-            item_range(it, n0, sp, r0, r1);
+            int n0, a0, sp, r0, r1;
+            item_range(it, n0, a0, sp, r0, r1);
             const int n = n0 + row;
             for (int rt = r0; rt < r1 && ok; rt++, r++) {
                 const int rs = r % R;
@@ -596,7 +607,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 for (int js = 0; js < 4 && ok; js++) {
                     const int kt = 4 * rt + js;
                     if (kt >= nk) break;
-                    const int os = o % O, sub = js % kRowsKPS;
+                    const int os = o % O, sub = js % KPS;
                     // 32 weights at K 64 js + 32 kh of the stage: box js / 2, 16-byte chunks c0 and
                     // c0 + 1 of the row, stored at chunk c ^ (row & 7) (128-byte swizzle)
                     const int c0 = 4 * (js & 1) + 2 * kh;
@@ -618,7 +629,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                     tmem_st16(col, hw);
                     tmem_st16(col + 32u, lw);
                     // the operand stage is complete after its last K step (or the last one of K)
-                    if (sub == kRowsKPS - 1 || kt == nk - 1) {
+                    if (sub == KPS - 1 || kt == nk - 1) {
                         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                         tc_fence_before();
                         __syncwarp();
@@ -629,38 +640,41 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_free[rs]);  // the stage's bytes are in registers / TMEM
             }
-            // epilogue of item j: accumulator pair j & 1
-            const int ab = j & 1;
-            if (ok) ok = bar_wait(&acc_full[ab], (uint32_t)((j / 2) & 1), err);
+            // epilogue of item j: accumulator set j % NA; warp (q, hb) stores activation rows
+            // a0 + RowsPerWarp hb .. in chunks of 16
+            const int ab = j % NA;
+            if (ok) ok = bar_wait(&acc_full[ab], (uint32_t)((j / NA) & 1), err);
             ok = __all_sync(0xffffffffu, ok);
             tc_fence_after();
-            float f[16];
-            const bool has = hb * 16 < MN;
-            if (ok && has) {
-                uint32_t v[16], v2[16], v3[16];
-                const uint32_t taddr = tmem + lane_base + (uint32_t)ab * G::AccCols + (uint32_t)(hb * 16);
-                tmem_ld16(taddr, v);                  // hh
-                tmem_ld16(taddr + (uint32_t)MN, v2);  // hl
-                tmem_ld16(taddr + 2u * MN, v3);       // lh
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            const int nn = n0 + q * 32 + lane;
+#pragma unroll 1
+            for (int c16 = hb * G::RowsPerWarp; c16 < (hb + 1) * G::RowsPerWarp && c16 < MN; c16 += 16) {
+                float f[16];
+                if (ok) {
+                    uint32_t v[16], v2[16], v3[16];
+                    const uint32_t taddr = tmem + lane_base + (uint32_t)ab * G::AccCols + (uint32_t)c16;
+                    tmem_ld16(taddr, v);                  // hh
+                    tmem_ld16(taddr + (uint32_t)MN, v2);  // hl
+                    tmem_ld16(taddr + 2u * MN, v3);       // lh
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int i = 0; i < 16; i++)
-                    f[i] = fmaf(__uint_as_float(v2[i]) + __uint_as_float(v3[i]), 1.0f / 2048.0f, __uint_as_float(v[i]));
+                    for (int i = 0; i < 16; i++)
+                        f[i] = fmaf(__uint_as_float(v2[i]) + __uint_as_float(v3[i]), 1.0f / 2048.0f, __uint_as_float(v[i]));
+                }
+                if (ok && nn < N) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int m = a0 + c16 + i;
+                        if (m < M) {
+                            if (S == 1) C[(size_t)m * ldc + nn] = f[i];
+                            else part[((size_t)sp * M + m) * N + nn] = f[i];
+                        }
+                    }
+                }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_free[ab]);
-            const int nn = n0 + q * 32 + lane;
-            if (ok && has && nn < N) {
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const int m = hb * 16 + i;
-                    if (m < M) {
-                        if (S == 1) C[(size_t)m * ldc + nn] = f[i];
-                        else part[((size_t)sp * M + m) * N + nn] = f[i];
-                    }
-                }
-            }
             if (S > 1) {  // every item takes a ticket (also after a failed wait, so the tickets reset)
                 __threadfence();
                 named_bar(1, kConvWarps * 32);
@@ -819,12 +833,18 @@ void launch_rows(const DTensor& W, const __half* a16, int M, float* y, int ldc, 
     const CUtensorMap td = d_tma ? scale_map(W, kRowsBM) : tw;
     if (first_use_on_device(reinterpret_cast<const void*>(k_gemm_q8_rows<MN>)))
         QQ_CUDA_TRY(cudaFuncSetAttribute(k_gemm_q8_rows<MN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::Smem));
-    const int S = rows_splits(N, K);
-    const int64_t items = ((N + kRowsBM - 1) / kRowsBM) * S;
+    // the wide form takes its work from the activation tiles and never splits K
+    const int S = G::Wide ? 1 : rows_splits(N, K);
+    const int64_t n_at = (M + MN - 1) / MN;
+    QQ_CHECK(G::Wide || n_at == 1, QQ_ERR_INVALID, "few-row Q8_0 matmul: more rows than the form takes");
+    const int64_t items = ((N + kRowsBM - 1) / kRowsBM) * n_at * S;
     QQ_CHECK(items <= (int64_t)1 << 30, QQ_ERR_INVALID, "few-row Q8_0 matmul: too many rows");
     const unsigned grid = (unsigned)std::min<int64_t>(items, num_sms());
+    QQ_CHECK(S == 1 || rows_scratch, QQ_ERR_INVALID, "few-row Q8_0 matmul: split K needs the scratch");
     unsigned int* tickets = static_cast<unsigned int*>(rows_scratch);
-    float* part = reinterpret_cast<float*>(static_cast<char*>(rows_scratch) + kRowsTickets * sizeof(unsigned int));
+    float* part = rows_scratch ? reinterpret_cast<float*>(static_cast<char*>(rows_scratch) +
+                                                          kRowsTickets * sizeof(unsigned int))
+                               : nullptr;
     k_gemm_q8_rows<MN><<<grid, kRowsThreads, G::Smem, s>>>(tx, tw, td, d_tma ? 1 : 0, M, (int)K, W.d, (int)N, y, ldc,
                                                            part, tickets, S,
                                                            (int)items, kernel_err_ptr());
@@ -860,6 +880,17 @@ void launch_gemm_q8_f16(const DTensor& W, int64_t group_rows, const __half* a16,
     QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
     QQ_CHECK(N >= 1 && W.rows % N == 0 && M <= 65535 * kBM, QQ_ERR_INVALID, "tensor-core Q8_0 matmul: bad shape");
     if (M <= 0) return;
+    // a dense product of more rows with enough (weight tile, 128-row activation tile) items for
+    // every SM: the wide tensor-memory form (QQ3_GEMM_WIDE=0 keeps the 128-row activation tile)
+    static const bool wide_off = [] {
+        const char* e = getenv("QQ3_GEMM_WIDE");
+        return e && atoi(e) == 0;
+    }();
+    if (!groups && gemm_exact() && !wide_off && M > kGemmFewMax && N == W.rows &&
+        ((N + kRowsBM - 1) / kRowsBM) * ((M + 127) / 128) >= num_sms()) {
+        launch_rows<128>(W, a16, M, y, ldc, nullptr, s);
+        return;
+    }
     if (gemm_exact()) launch_split<3>(W, N, a16, M, y, ldc, groups, s);
     else launch_split<1>(W, N, a16, M, y, ldc, groups, s);
 }
