@@ -528,17 +528,33 @@ __global__ void k_attn_merge(const float* __restrict__ part, const int* __restri
     const int t = w / n_head, h = w % n_head;
     const int used = (pos[t] + 1 + chunk - 1) / chunk;  // splits holding positions
     const float* pp = part + ((size_t)t * n_head + h) * n_split * (HD + 2);
+    // the maximum over the splits: lane s reads splits s, s + 32, ... (all loads in flight)
     float M = -INFINITY;
-    for (int sp = 0; sp < used; sp++) M = fmaxf(M, pp[sp * (HD + 2) + HD]);
+    for (int sp = lane; sp < used; sp += 32) M = fmaxf(M, pp[sp * (HD + 2) + HD]);
+    M = warp_max(M);
+    // the weighted sums in split order, eight splits' loads issued before their first use
     float acc[PL], L = 0.f;
 #pragma unroll
     for (int j = 0; j < PL; j++) acc[j] = 0.f;
-    for (int sp = 0; sp < used; sp++) {
-        const float* q = pp + sp * (HD + 2);
-        const float f = expf(q[HD] - M);
-        L += f * q[HD + 1];
+    for (int s0 = 0; s0 < used; s0 += 8) {
+        float mv[8], lv[8], av[8][PL];
 #pragma unroll
-        for (int j = 0; j < PL; j++) acc[j] = fmaf(f, q[lane * PL + j], acc[j]);
+        for (int u = 0; u < 8; u++) {
+            const bool live = s0 + u < used;
+            const float* q = pp + (size_t)(s0 + u) * (HD + 2);
+            mv[u] = live ? q[HD] : -INFINITY;
+            lv[u] = live ? q[HD + 1] : 0.f;
+#pragma unroll
+            for (int j = 0; j < PL; j++) av[u][j] = live ? q[lane * PL + j] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            if (s0 + u >= used) break;
+            const float f = expf(mv[u] - M);
+            L += f * lv[u];
+#pragma unroll
+            for (int j = 0; j < PL; j++) acc[j] = fmaf(f, av[u][j], acc[j]);
+        }
     }
     float* o = out + ((size_t)t * n_head + h) * HD + lane * PL;
 #pragma unroll
