@@ -54,6 +54,12 @@ bool getenv_flag(const char* name) {
     return v && atoi(v) != 0;
 }
 
+// a switch that is on unless set to 0
+bool getenv_flag_zero(const char* name) {
+    const char* v = getenv(name);
+    return v && atoi(v) == 0;
+}
+
 void* ctx_scratch(qq_ctx* c, size_t bytes) {
     if (bytes > c->scratch_bytes) {
         if (c->scratch) {
@@ -118,6 +124,15 @@ struct qq_model {
     int* h_io = nullptr;      // pinned [8]: one host step's token, pos in; argmax, pos, error word out
     int suppress_set = INT32_MIN;  // the suppress id last copied to the device
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+    // captured multi-sequence steps, per (rows, want_logits): valid for the attention split count
+    // nz and the buffers it was captured with
+    struct BatchGraph {
+        cudaGraphExec_t exec = nullptr;
+        int nz = 0;
+        bool seen = false;  // the key ran once eagerly (kernel attributes are set)
+        const void* ptrs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    };
+    std::map<std::pair<int, int>, BatchGraph> bgraphs;
     cudaStream_t cap = nullptr;
     // persistent decode kernel programs, per (sequence, with logits)
     struct Prog {
@@ -184,6 +199,9 @@ namespace {
 
 void free_model(qq_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : m->bgraphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    m->bgraphs.clear();
     m->graphs.clear();
     for (auto& kv : m->progs)
         if (kv.second.d_prog) cudaFree(kv.second.d_prog);
@@ -1267,9 +1285,8 @@ void ensure_tp_bufs(qq_model* m, int T) {
     m->tp_cap = cap;
 }
 
-void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
+void batch_step_on(qq_model* m, int T, int max_len, bool want_logits, cudaStream_t s) {
     const qq_model_desc& d = m->d;
-    cudaStream_t s = m->ctx->stream;
     const int E = d.n_embd, hd = d.head_dim;
     PrefillBufs b = prefill_bufs(m, T);
     const int* tok = m->bt_i;
@@ -1348,6 +1365,60 @@ void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
         return;
     }
     qq3::launch_argmax_rows(m->bt_logits, T, d.n_vocab, m->suppress, m->bt_keys, m->bt_i + 3 * m->bt_cap, s);
+}
+
+// One multi-sequence step (rows in m->h_bt).  A dense single-GPU model replays it as a CUDA graph
+// (per rows and want_logits; re-captured when the attention split count ceil(max_len / 64) or a
+// buffer changes), which removes the launch gaps of its ~15 kernels per layer; the first step of
+// a key runs eagerly (it sets the kernels' attributes).  QQ3_BATCH_GRAPH=0 always runs eagerly.
+void batch_step(qq_model* m, int T, int max_len, bool want_logits) {
+    cudaStream_t s = m->ctx->stream;
+    static const bool graph_off = getenv_flag_zero("QQ3_BATCH_GRAPH");
+    bool dense = true;
+    for (const Layer& L : m->layers) dense = dense && !L.moe;
+    if (graph_off || !dense || m->tp_world > 1 || m->ep_world > 1) {
+        batch_step_on(m, T, max_len, want_logits, s);
+        return;
+    }
+    prefill_bufs(m, T);  // any growth of the row buffers happens before a capture
+    const int chunk = qq3::attn_rows_chunk();
+    const int nz = (max_len + chunk - 1) / chunk;
+    qq_model::BatchGraph& g = m->bgraphs[std::make_pair(T, want_logits ? 1 : 0)];
+    const void* ptrs[5] = {m->pf_arena, m->bt_i, m->h_bt, m->bt_attn, m->bt_logits};
+    const bool same_bufs = std::equal(ptrs, ptrs + 5, g.ptrs);
+    if (g.exec && (g.nz != nz || !same_bufs)) {
+        QQ_CUDA_TRY(cudaStreamSynchronize(s));
+        cudaGraphExecDestroy(g.exec);
+        g.exec = nullptr;
+    }
+    if (!g.seen) {
+        g.seen = true;
+        batch_step_on(m, T, max_len, want_logits, s);
+        return;
+    }
+    if (!g.exec) {
+        // captured with the longest length of this split count: the grid is the same
+        const int cap_len = std::min(nz * chunk, m->d.max_ctx);
+        cudaGraph_t gr = nullptr;
+        QQ_CUDA_TRY(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeRelaxed));
+        try {
+            batch_step_on(m, T, cap_len, want_logits, m->cap);
+        } catch (...) {
+            cudaStreamEndCapture(m->cap, &gr);
+            if (gr) cudaGraphDestroy(gr);
+            cudaGetLastError();
+            throw;
+        }
+        QQ_CUDA_TRY(cudaStreamEndCapture(m->cap, &gr));
+        cudaGraphExec_t ge = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&ge, gr, 0);
+        cudaGraphDestroy(gr);
+        QQ_CUDA_TRY(e);
+        g.exec = ge;
+        g.nz = nz;
+        std::copy(ptrs, ptrs + 5, g.ptrs);
+    }
+    QQ_CUDA_TRY(cudaGraphLaunch(g.exec, s));
 }
 
 // the vocab shards' logits of T rows from every rank into host logits [T][n_vocab]
