@@ -139,6 +139,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     float m = -INFINITY, l = 0.f;
     uint32_t phase = 0;
     bool ok = true;
+    // staging of a key tile: K rows (keys past n_keys are zero) and V transposed; a thread's
+    // kTasks tasks of each are 8 elements (K: key j, dims 8c..; V: dim d, keys 8jc..; consecutive
+    // threads read consecutive dims of a key row)
+    constexpr int kTasks = kTcKeys * (HD / 8) / kTcThreads;
+    auto load_k = [&](int k0, float (&v)[kTasks][8]) {
+#pragma unroll
+        for (int u = 0; u < kTasks; u++) {
+            const int f = t + u * kTcThreads;
+            const int j = f / (HD / 8), c = f % (HD / 8);
+            if (k0 + j < n_keys) {
+                const float* kr = kb + (size_t)(k0 + j) * HD + 8 * c;
+                const float4 a = __ldg(reinterpret_cast<const float4*>(kr));
+                const float4 b = __ldg(reinterpret_cast<const float4*>(kr + 4));
+                v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
+                v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[u][i] = 0.f;
+            }
+        }
+    };
+    auto store_k = [&](const float (&v)[kTasks][8]) {
+#pragma unroll
+        for (int u = 0; u < kTasks; u++) {
+            const int f = t + u * kTcThreads;
+            const int j = f / (HD / 8), c = f % (HD / 8);
+            uint4 hi, lo;
+            split8(v[u], hi, lo);
+            const uint32_t off = tile_chunk(kTcKeys, j, c);
+            *reinterpret_cast<uint4*>(Kh + off) = hi;
+            *reinterpret_cast<uint4*>(Kl + off) = lo;
+        }
+    };
+    auto load_v = [&](int k0, float (&v)[kTasks][8]) {
+#pragma unroll
+        for (int u = 0; u < kTasks; u++) {
+            const int f = t + u * kTcThreads;
+            const int d = f % HD, jc = f / HD;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int j = k0 + 8 * jc + i;
+                v[u][i] = j < n_keys ? __ldg(vb + (size_t)j * HD + d) : 0.f;
+            }
+        }
+    };
+    auto store_v = [&](const float (&v)[kTasks][8]) {
+#pragma unroll
+        for (int u = 0; u < kTasks; u++) {
+            const int f = t + u * kTcThreads;
+            const int d = f % HD, jc = f / HD;
+            uint4 hi, lo;
+            split8(v[u], hi, lo);
+            const uint32_t off = sw128(d, jc);
+            *reinterpret_cast<uint4*>(Vh + off) = hi;
+            *reinterpret_cast<uint4*>(Vl + off) = lo;
+        }
+    };
     for (int pass = 0; pass < 2; pass++) {
         if (pass == 1) {  // the row maximum over both column halves
             row_red[t] = m;
@@ -146,69 +203,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             m = fmaxf(row_red[row], row_red[row + kTcRows]);
             __syncthreads();
         }
+        // tile kt + 1's K (and V) are loaded into registers while tile kt's MMAs and softmax run
+        float kr[kTasks][8], vr[kTasks][8];
+        load_k(0, kr);
+        if (pass == 1) load_v(0, vr);
         for (int kt = 0; kt < n_tiles; kt++) {
             const int k0 = kt * kTcKeys;
-            // the K tile (keys past n_keys are zero), and in pass 2 V transposed; every load of a
-            // group of four tasks is issued before the first conversion (one round trip each)
-            constexpr int kTasks = kTcKeys * (HD / 8) / kTcThreads;  // per thread, K and V alike
-            constexpr int kGrp = kTasks < 4 ? kTasks : 4;
-            static_assert(kTasks % kGrp == 0, "task groups");
-#pragma unroll
-            for (int g0 = 0; g0 < kTasks; g0 += kGrp) {
-                float v[kGrp][8];
-#pragma unroll
-                for (int u = 0; u < kGrp; u++) {
-                    const int f = t + (g0 + u) * kTcThreads;
-                    const int j = f / (HD / 8), c = f % (HD / 8);
-                    if (k0 + j < n_keys) {
-                        const float* kr = kb + (size_t)(k0 + j) * HD + 8 * c;
-                        const float4 a = __ldg(reinterpret_cast<const float4*>(kr));
-                        const float4 b = __ldg(reinterpret_cast<const float4*>(kr + 4));
-                        v[u][0] = a.x; v[u][1] = a.y; v[u][2] = a.z; v[u][3] = a.w;
-                        v[u][4] = b.x; v[u][5] = b.y; v[u][6] = b.z; v[u][7] = b.w;
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 8; i++) v[u][i] = 0.f;
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < kGrp; u++) {
-                    const int f = t + (g0 + u) * kTcThreads;
-                    const int j = f / (HD / 8), c = f % (HD / 8);
-                    uint4 hi, lo;
-                    split8(v[u], hi, lo);
-                    const uint32_t off = tile_chunk(kTcKeys, j, c);
-                    *reinterpret_cast<uint4*>(Kh + off) = hi;
-                    *reinterpret_cast<uint4*>(Kl + off) = lo;
-                }
-            }
-            if (pass == 1) {
-                // task (dim d, 8 keys jc): consecutive threads read consecutive dims of a key row
-#pragma unroll
-                for (int g0 = 0; g0 < kTasks; g0 += kGrp) {
-                    float v[kGrp][8];
-#pragma unroll
-                    for (int u = 0; u < kGrp; u++) {
-                        const int f = t + (g0 + u) * kTcThreads;
-                        const int d = f % HD, jc = f / HD;
-#pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const int j = k0 + 8 * jc + i;
-                            v[u][i] = j < n_keys ? __ldg(vb + (size_t)j * HD + d) : 0.f;
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < kGrp; u++) {
-                        const int f = t + (g0 + u) * kTcThreads;
-                        const int d = f % HD, jc = f / HD;
-                        uint4 hi, lo;
-                        split8(v[u], hi, lo);
-                        const uint32_t off = sw128(d, jc);
-                        *reinterpret_cast<uint4*>(Vh + off) = hi;
-                        *reinterpret_cast<uint4*>(Vl + off) = lo;
-                    }
-                }
-            }
+            store_k(kr);
+            if (pass == 1) store_v(vr);
             fence_async_smem();  // the tiles are read by the tensor cores (async proxy)
             tc_fence_before();
             __syncthreads();
@@ -226,6 +228,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     umma_f16(tmem + C::ColS2, ql, kh, C::IdescS, 1u);
                 }
                 umma_commit(&mma_bar);
+            }
+            if (kt + 1 < n_tiles) {
+                load_k(k0 + kTcKeys, kr);
+                if (pass == 1) load_v(k0 + kTcKeys, vr);
             }
             if (!mbar_wait(&mma_bar, phase)) {
                 set_err(err, kErrFullWait);
