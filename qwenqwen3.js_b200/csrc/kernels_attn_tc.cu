@@ -6,17 +6,18 @@
 // loops; here a CTA takes 128 query rows of one kv head (128 / G consecutive tokens x its G query
 // heads: the UMMA's M) and walks the keys in tiles of 64 (the N of the scores, the K of P.V):
 //
-//   pass 1   S = Q.K^T per tile on the tensor cores (TMEM accumulators); two of the 256 threads
-//            own a query row (its TMEM lane: warps w and w + 4), one half of its columns each,
-//            and keep the row maximum m;
-//   pass 2   S again; p = exp(s - m) (0 past the row's position), l += p, the tile's P written to
-//            shared memory as the A operand of O += P.V (O in TMEM); at the end o = O / l.
+//   per tile S = Q.K^T on the tensor cores (TMEM accumulators); two of the 256 threads own a
+//            query row (its TMEM lane: warps w and w + 4), one half of its columns each;
+//            p = exp(s - mr) against the row's reference maximum mr (0 past the row's position),
+//            l += p, the tile's P written to shared memory as the A operand of O += P.V (O in
+//            TMEM); at the end o = O / l.
 //
 // Exact splits keep f32 accuracy on fp16 tensor cores: every operand x is the fp16 pair
 // xh = fp16(x), xl = fp16((x - xh) * 2048); S1 = qh.kh and S2 = qh.kl + ql.kh give
 // s = S1 + S2 / 2048 (the dropped ql.kl / 2^22 is below f32 rounding), and O1 = ph.vh,
-// O2 = ph.vl + pl.vh the same way.  Two passes (the row maximum first) instead of an online
-// softmax: the O accumulator in TMEM is never rescaled.
+// O2 = ph.vl + pl.vh the same way.  The reference maximum of a row moves only when a tile's
+// maximum exceeds it by more than e^8 (then O and l are rescaled in place), so p stays within
+// fp16 range and the TMEM accumulator is rescaled a few times per row at most.
 //
 // Operand tiles in shared memory are K-major with the 128-byte swizzle (`sw128`): Q [128][hd] and
 // K [64][hd] (hd / 64 column blocks of 64), V transposed to [hd][64 keys], P [128][64 keys].
@@ -63,6 +64,16 @@ __device__ __forceinline__ void split8(const float (&v)[8], uint4& hi, uint4& lo
                     pack_h2((v[2] - h[2]) * 2048.f, (v[3] - h[3]) * 2048.f),
                     pack_h2((v[4] - h[4]) * 2048.f, (v[5] - h[5]) * 2048.f),
                     pack_h2((v[6] - h[6]) * 2048.f, (v[7] - h[7]) * 2048.f));
+}
+
+// 16 consecutive 32-bit tensor-memory columns of this thread's lane
+__device__ __forceinline__ void tmem_st16_flat(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 
 // byte offset of 16-byte chunk c (8 fp16 of K) of row r in a K-major tile of `rows` rows
@@ -136,7 +147,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const float* vb = vc + (size_t)kvh * max_ctx * HD;
     const float scale = (float)(1.0 / sqrt((double)HD));
     const int n_tiles = (n_keys + kTcKeys - 1) / kTcKeys;
-    float m = -INFINITY, l = 0.f;
+    float l = 0.f;
     uint32_t phase = 0;
     bool ok = true;
     // staging of a key tile: K rows (keys past n_keys are zero) and V transposed; a thread's
@@ -196,109 +207,130 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             *reinterpret_cast<uint4*>(Vl + off) = lo;
         }
     };
-    for (int pass = 0; pass < 2; pass++) {
-        if (pass == 1) {  // the row maximum over both column halves
-            row_red[t] = m;
-            __syncthreads();
-            m = fmaxf(row_red[row], row_red[row + kTcRows]);
-            __syncthreads();
-        }
-        // tile kt + 1's K (and V) are loaded into registers while tile kt's MMAs and softmax run
-        float kr[kTasks][8], vr[kTasks][8];
-        load_k(0, kr);
-        if (pass == 1) load_v(0, vr);
-        for (int kt = 0; kt < n_tiles; kt++) {
-            const int k0 = kt * kTcKeys;
-            store_k(kr);
-            if (pass == 1) store_v(vr);
-            fence_async_smem();  // the tiles are read by the tensor cores (async proxy)
-            tc_fence_before();
-            __syncthreads();
-            if (t == 0) {
-                tc_fence_after();
-#pragma unroll
-                for (int ks = 0; ks < HD / 16; ks++) {
-                    const uint32_t qo = (uint32_t)(ks >> 2) * kTcRows * 128u + 32u * (ks & 3);
-                    const uint32_t ko = (uint32_t)(ks >> 2) * kTcKeys * 128u + 32u * (ks & 3);
-                    const uint32_t acc = ks ? 1u : 0u;
-                    const uint64_t qh = umma_desc(smem_u32(Qh + qo)), ql = umma_desc(smem_u32(Ql + qo));
-                    const uint64_t kh = umma_desc(smem_u32(Kh + ko)), kl = umma_desc(smem_u32(Kl + ko));
-                    umma_f16(tmem + C::ColS1, qh, kh, C::IdescS, acc);
-                    umma_f16(tmem + C::ColS2, qh, kl, C::IdescS, acc);
-                    umma_f16(tmem + C::ColS2, ql, kh, C::IdescS, 1u);
-                }
-                umma_commit(&mma_bar);
-            }
-            if (kt + 1 < n_tiles) {
-                load_k(k0 + kTcKeys, kr);
-                if (pass == 1) load_v(k0 + kTcKeys, vr);
-            }
-            if (!mbar_wait(&mma_bar, phase)) {
-                set_err(err, kErrFullWait);
-                ok = false;
-            }
-            phase ^= 1u;
+    // One pass over the key tiles, an online softmax against a reference maximum mr of the row
+    // (the same in both threads of the row): p = exp(s - mr); mr moves only when a tile's maximum
+    // exceeds it by more than kLazy, and then O (in TMEM) and l are rescaled by exp(mr_old -
+    // mr_new).  So p <= e^kLazy (an fp16 hi/lo pair holds it) and the accumulator is rarely touched.
+    constexpr float kLazy = 8.0f;
+    float mr = -INFINITY;
+    float kr[kTasks][8], vr[kTasks][8];
+    load_k(0, kr);
+    load_v(0, vr);
+    for (int kt = 0; kt < n_tiles; kt++) {
+        const int k0 = kt * kTcKeys;
+        store_k(kr);
+        store_v(vr);
+        fence_async_smem();  // the tiles are read by the tensor cores (async proxy)
+        tc_fence_before();
+        __syncthreads();
+        if (t == 0) {
             tc_fence_after();
-            // this row's scores: pass 1 the maximum, pass 2 p into the P tile
-#pragma unroll 1
-            for (int c0 = half * (kTcKeys / 2); c0 < (half + 1) * (kTcKeys / 2); c0 += 16) {
-                uint32_t s1[16], s2[16];
-                tmem_ld16(tmem + lane_base + C::ColS1 + (uint32_t)c0, s1);
-                tmem_ld16(tmem + lane_base + C::ColS2 + (uint32_t)c0, s2);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                float p[16];
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const int key = k0 + c0 + i;
-                    const bool valid = live && ok && key <= my_pos;
-                    const float s = fmaf(__uint_as_float(s2[i]), 1.0f / 2048.0f, __uint_as_float(s1[i])) * scale;
-                    if (pass == 0) {
-                        if (valid) m = fmaxf(m, s);
-                        p[i] = 0.f;
-                    } else {
-                        p[i] = valid ? expf(s - m) : 0.f;
-                        l += p[i];
-                    }
-                }
-                if (pass == 1) {
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        float v[8];
-#pragma unroll
-                        for (int i = 0; i < 8; i++) v[i] = p[8 * h + i];
-                        uint4 hi, lo;
-                        split8(v, hi, lo);
-                        const uint32_t off = sw128(row, (c0 >> 3) + h);
-                        *reinterpret_cast<uint4*>(Ph + off) = hi;
-                        *reinterpret_cast<uint4*>(Pl + off) = lo;
-                    }
-                }
+            for (int ks = 0; ks < HD / 16; ks++) {
+                const uint32_t qo = (uint32_t)(ks >> 2) * kTcRows * 128u + 32u * (ks & 3);
+                const uint32_t ko = (uint32_t)(ks >> 2) * kTcKeys * 128u + 32u * (ks & 3);
+                const uint32_t acc = ks ? 1u : 0u;
+                const uint64_t qh = umma_desc(smem_u32(Qh + qo)), ql = umma_desc(smem_u32(Ql + qo));
+                const uint64_t kh = umma_desc(smem_u32(Kh + ko)), kl = umma_desc(smem_u32(Kl + ko));
+                umma_f16(tmem + C::ColS1, qh, kh, C::IdescS, acc);
+                umma_f16(tmem + C::ColS2, qh, kl, C::IdescS, acc);
+                umma_f16(tmem + C::ColS2, ql, kh, C::IdescS, 1u);
             }
-            if (pass == 1) {
-                fence_async_smem();
-                tc_fence_before();
-                __syncthreads();
-                if (t == 0) {
-                    tc_fence_after();
+            umma_commit(&mma_bar);
+        }
+        // the next tile's K and V travel while this tile's MMAs and softmax run
+        if (kt + 1 < n_tiles) {
+            load_k(k0 + kTcKeys, kr);
+            load_v(k0 + kTcKeys, vr);
+        }
+        if (!mbar_wait(&mma_bar, phase)) {
+            set_err(err, kErrFullWait);
+            ok = false;
+        }
+        phase ^= 1u;
+        tc_fence_after();
+        // this thread's 32 scores of the tile (-inf past the row's position) and their maximum
+        float sv[kTcKeys / 2];
+        float tmax = -INFINITY;
 #pragma unroll
-                    for (int ks = 0; ks < kTcKeys / 16; ks++) {
-                        const uint32_t acc = (kt > 0 || ks > 0) ? 1u : 0u;
-                        const uint64_t ph = umma_desc(smem_u32(Ph + 32u * ks)), pl = umma_desc(smem_u32(Pl + 32u * ks));
-                        const uint64_t vh = umma_desc(smem_u32(Vh + 32u * ks)), vl = umma_desc(smem_u32(Vl + 32u * ks));
-                        umma_f16(tmem + C::ColO1, ph, vh, C::IdescO, acc);
-                        umma_f16(tmem + C::ColO2, ph, vl, C::IdescO, acc);
-                        umma_f16(tmem + C::ColO2, pl, vh, C::IdescO, 1u);
-                    }
-                    umma_commit(&mma_bar);
-                }
-                if (!mbar_wait(&mma_bar, phase)) {
-                    set_err(err, kErrFullWait);
-                    ok = false;
-                }
-                phase ^= 1u;
-                tc_fence_after();
+        for (int c = 0; c < kTcKeys / 2; c += 16) {
+            const int c0 = half * (kTcKeys / 2) + c;
+            uint32_t s1[16], s2[16];
+            tmem_ld16(tmem + lane_base + C::ColS1 + (uint32_t)c0, s1);
+            tmem_ld16(tmem + lane_base + C::ColS2 + (uint32_t)c0, s2);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const int key = k0 + c0 + i;
+                const bool valid = live && ok && key <= my_pos;
+                const float sc = fmaf(__uint_as_float(s2[i]), 1.0f / 2048.0f, __uint_as_float(s1[i])) * scale;
+                sv[c + i] = valid ? sc : -INFINITY;
+                tmax = fmaxf(tmax, sv[c + i]);
             }
         }
+        // the tile maximum of the row over both halves (row_red is next written after two barriers)
+        row_red[t] = tmax;
+        __syncthreads();
+        tmax = fmaxf(row_red[row], row_red[row + kTcRows]);
+        if (tmax > mr + kLazy) {
+            if (mr > -INFINITY) {  // rescale this thread's half of the O row and its l
+                const float f = expf(mr - tmax);
+                l *= f;
+#pragma unroll 1
+                for (int c0 = half * (HD / 2); c0 < (half + 1) * (HD / 2); c0 += 16) {
+                    uint32_t o1[16], o2[16];
+                    tmem_ld16(tmem + lane_base + C::ColO1 + (uint32_t)c0, o1);
+                    tmem_ld16(tmem + lane_base + C::ColO2 + (uint32_t)c0, o2);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        o1[i] = __float_as_uint(__uint_as_float(o1[i]) * f);
+                        o2[i] = __float_as_uint(__uint_as_float(o2[i]) * f);
+                    }
+                    tmem_st16_flat(tmem + lane_base + C::ColO1 + (uint32_t)c0, o1);
+                    tmem_st16_flat(tmem + lane_base + C::ColO2 + (uint32_t)c0, o2);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
+            mr = tmax;
+        }
+        // p = exp(s - mr) into this thread's half of the P row
+#pragma unroll
+        for (int c = 0; c < kTcKeys / 2; c += 8) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                v[i] = sv[c + i] == -INFINITY ? 0.f : expf(sv[c + i] - mr);
+                l += v[i];
+            }
+            uint4 hi, lo;
+            split8(v, hi, lo);
+            const uint32_t off = sw128(row, (half * (kTcKeys / 2) + c) >> 3);
+            *reinterpret_cast<uint4*>(Ph + off) = hi;
+            *reinterpret_cast<uint4*>(Pl + off) = lo;
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (t == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int ks = 0; ks < kTcKeys / 16; ks++) {
+                const uint32_t acc = (kt > 0 || ks > 0) ? 1u : 0u;
+                const uint64_t ph = umma_desc(smem_u32(Ph + 32u * ks)), pl = umma_desc(smem_u32(Pl + 32u * ks));
+                const uint64_t vh = umma_desc(smem_u32(Vh + 32u * ks)), vl = umma_desc(smem_u32(Vl + 32u * ks));
+                umma_f16(tmem + C::ColO1, ph, vh, C::IdescO, acc);
+                umma_f16(tmem + C::ColO2, ph, vl, C::IdescO, acc);
+                umma_f16(tmem + C::ColO2, pl, vh, C::IdescO, 1u);
+            }
+            umma_commit(&mma_bar);
+        }
+        if (!mbar_wait(&mma_bar, phase)) {
+            set_err(err, kErrFullWait);
+            ok = false;
+        }
+        phase ^= 1u;
+        tc_fence_after();
     }
     // o = (O1 + O2 / 2048) / l for this row (l summed over both column halves)
     row_red[t] = l;
