@@ -1212,8 +1212,8 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
         qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
         if (L.attn) {
             qq3::launch_gemm_q8(*L.t[QQ_WQ], b.xn, T, b.x16, b.q, s);
-            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s);
-            qq3::launch_gemm_q8(*L.t[QQ_WV], b.xn, T, b.x16, b.v, s);
+            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s, true);  // same input rows
+            qq3::launch_gemm_q8(*L.t[QQ_WV], b.xn, T, b.x16, b.v, s, true);
             qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
             qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
             qq3::launch_rope_rows(b.q, T, d.n_head, hd, m->rope_cs, pos0, s);
@@ -1252,7 +1252,7 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
         } else {
             const size_t F = L.t[QQ_FFN_GATE]->ne[1];
             qq3::launch_gemm_q8(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.g, s);
-            qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s, true);
             qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
             qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s);
             if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);
@@ -1301,8 +1301,8 @@ void batch_step_on(qq_model* m, int T, int max_len, bool want_logits, cudaStream
         qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
         if (L.attn) {
             qq3::launch_gemm_q8_few(*L.t[QQ_WQ], b.xn, T, b.x16, b.rows, b.q, s);
-            qq3::launch_gemm_q8_few(*L.t[QQ_WK], b.xn, T, b.x16, b.rows, b.k, s);
-            qq3::launch_gemm_q8_few(*L.t[QQ_WV], b.xn, T, b.x16, b.rows, b.v, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WK], b.xn, T, b.x16, b.rows, b.k, s, true);  // same input rows
+            qq3::launch_gemm_q8_few(*L.t[QQ_WV], b.xn, T, b.x16, b.rows, b.v, s, true);
             qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
             qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
             qq3::launch_rope_rows_at(b.q, T, d.n_head, hd, m->rope_cs, pos, s);
@@ -1342,7 +1342,7 @@ void batch_step_on(qq_model* m, int T, int max_len, bool want_logits, cudaStream
         } else {
             const size_t F = L.t[QQ_FFN_GATE]->ne[1];
             qq3::launch_gemm_q8_few(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.rows, b.g, s);
-            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.rows, b.u, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.rows, b.u, s, true);
             qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
             qq3::launch_gemm_q8_few(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.rows, b.tmp, s);
             if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);  // units' partial sums

@@ -87,7 +87,9 @@ bool gemm_q8_supported(const DTensor& W);
 // one fp16 product (~1e-3).  Operand buffers then hold hi rows followed by lo rows.
 bool gemm_exact();
 size_t gemm_q8_scratch_bytes(int64_t M, int64_t K);
-void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s);
+// x16_ready: x16 already holds x split into fp16 (the previous product had the same input)
+void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s,
+                    bool x16_ready = false);
 // Few-row form for 2 <= M <= kGemmFewMax rows (multi-sequence decode): weights on the MMA's
 // 128-row side, activation rows on its N side, K split over CTAs; rows_scratch holds
 // gemm_rows_scratch_bytes(M) bytes whose first 1 KB (arrival tickets) is zero before the first
@@ -97,7 +99,7 @@ constexpr int kGemmFewMax = 32;
 size_t gemm_rows_scratch_bytes(int M);
 void gemm_rows_reset(void* rows_scratch, cudaStream_t s);
 void launch_gemm_q8_few(const DTensor& W, const float* x, int M, __half* x16, void* rows_scratch, float* y,
-                        cudaStream_t s);
+                        cudaStream_t s, bool x16_ready = false);
 // Grouped form: W holds groups of group_rows rows (e.g. the experts of a packed tensor); work
 // item i = tiles[i] = (group, first row of a16, rows <= 128), *n_tiles items, max_tiles >= it.
 struct GemmGroups {

@@ -862,14 +862,14 @@ void gemm_rows_reset(void* rows_scratch, cudaStream_t s) {
 }
 
 void launch_gemm_q8_few(const DTensor& W, const float* x, int M, __half* x16, void* rows_scratch, float* y,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool x16_ready) {
     if (M <= 0 || W.rows <= 0) return;
     if (!rows_scratch || M > kGemmFewMax || !gemm_exact()) {
-        launch_gemm_q8(W, x, M, x16, y, s);
+        launch_gemm_q8(W, x, M, x16, y, s, x16_ready);
         return;
     }
     QQ_CHECK(gemm_q8_supported(W), QQ_ERR_INVALID, "tensor-core Q8_0 matmul: K must be a multiple of 32");
-    launch_f32_to_f16(x, x16, (size_t)M * W.K, s);
+    if (!x16_ready) launch_f32_to_f16(x, x16, (size_t)M * W.K, s);
     if (M <= 16) launch_rows<16>(W, x16, M, y, (int)W.rows, rows_scratch, s);
     else launch_rows<32>(W, x16, M, y, (int)W.rows, rows_scratch, s);
 }
@@ -903,9 +903,9 @@ void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
     QQ_CUDA_TRY(cudaGetLastError());
 }
 
-void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s) {
+void launch_gemm_q8(const DTensor& W, const float* x, int M, __half* x16, float* y, cudaStream_t s, bool x16_ready) {
     if (M <= 0 || W.rows <= 0) return;
-    launch_f32_to_f16(x, x16, (size_t)M * W.K, s);
+    if (!x16_ready) launch_f32_to_f16(x, x16, (size_t)M * W.K, s);
     launch_gemm_q8_f16(W, W.rows, x16, M, y, (int)W.rows, nullptr, s);
 }
 
