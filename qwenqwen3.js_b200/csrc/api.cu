@@ -1207,30 +1207,31 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
     QQ_CUDA_TRY(cudaMemcpyAsync(b.tok, tokens, sizeof(int) * T, cudaMemcpyHostToDevice, s));
     qq3::launch_embed_rows(*m->tok_embd, b.tok, T, d.n_vocab, b.hidden, s);
     const size_t TE = (size_t)T * E;
+    // the residual of the previous layer's FFN / MoE, added by the next norm; the last layer's is
+    // not added: nothing reads the rows' hidden state once the prompt's caches are written
+    const float* pend = nullptr;
     for (int l = 0; l < d.n_layers; l++) {
         const Layer& L = m->layers[l];
-        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
+        qq3::launch_add_rmsnorm_rows(b.hidden, pend, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, b.x16, s);
+        pend = nullptr;
         if (L.attn) {
-            qq3::launch_gemm_q8(*L.t[QQ_WQ], b.xn, T, b.x16, b.q, s);
-            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s, true);  // same input rows
+            qq3::launch_gemm_q8(*L.t[QQ_WQ], b.xn, T, b.x16, b.q, s, true);  // operand planes of the norm
+            qq3::launch_gemm_q8(*L.t[QQ_WK], b.xn, T, b.x16, b.k, s, true);
             qq3::launch_gemm_q8(*L.t[QQ_WV], b.xn, T, b.x16, b.v, s, true);
-            qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
-            qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
-            qq3::launch_rope_rows(b.q, T, d.n_head, hd, m->rope_cs, pos0, s);
-            qq3::launch_rope_rows(b.k, T, d.n_head_kv, hd, m->rope_cs, pos0, s);
             float* kc = m->k_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
             float* vc = m->v_cache + seq * m->kv_stride_seq() + L.attn_slot * m->kv_stride_layer();
-            qq3::launch_kv_append(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, pos0, kc, vc, s);
+            qq3::launch_qk_norm_rope_rows(b.q, b.k, b.v, T, d.n_head, d.n_head_kv, hd, L.t[QQ_Q_NORM]->f32,
+                                          L.t[QQ_K_NORM]->f32, d.rms_eps, m->rope_cs, nullptr, nullptr, pos0, 0,
+                                          d.max_ctx, kc, vc, s);
             qq3::launch_attn_prefill(b.q, kc, vc, T, pos0, d.n_head, d.n_head_kv, hd, d.max_ctx, b.attn, s);
             qq3::launch_gemm_q8(*L.t[QQ_WO], b.attn, T, b.x16, b.tmp, s);
             if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);
         } else {
-            qq3::launch_gemm_q8(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.bcx, s);
+            qq3::launch_gemm_q8(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.bcx, s, true);
             qq3::launch_conv_prefill(b.bcx, L.t[QQ_CONV]->f32, m->conv(seq, l), T, E, b.y, s);
             qq3::launch_gemm_q8(*L.t[QQ_OUT_PROJ], b.y, T, b.x16, b.tmp, s);
         }
-        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
-        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, s);
+        qq3::launch_add_rmsnorm_rows(b.hidden, b.tmp, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, b.x16, s);
         if (L.moe) {
             const int k = d.n_expert_used;
             const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
@@ -1251,13 +1252,13 @@ void prefill_chunk(qq_model* m, const int32_t* tokens, int T, int seq, int pos0)
                                     b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
         } else {
             const size_t F = L.t[QQ_FFN_GATE]->ne[1];
-            qq3::launch_gemm_q8(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.g, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.g, s, true);
             qq3::launch_gemm_q8(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.u, s, true);
-            qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
-            qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s);
+            qq3::launch_swiglu_rows_f16(b.g, b.u, (size_t)T * F, b.x16, s);
+            qq3::launch_gemm_q8(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.tmp, s, true);
             if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);
         }
-        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
+        pend = b.tmp;
     }
 }
 
@@ -1296,32 +1297,33 @@ void batch_step_on(qq_model* m, int T, int max_len, bool want_logits, cudaStream
     if (b.rows) qq3::gemm_rows_reset(b.rows, s);
     qq3::launch_embed_rows(*m->tok_embd, tok, T, d.n_vocab, b.hidden, s);
     const size_t TE = (size_t)T * E;
+    // the norms write the fp16 operand planes of the products that follow them (x16_ready), and
+    // the residual of the previous layer's FFN / MoE is added by the next norm
+    const float* pend = nullptr;
     for (int l = 0; l < d.n_layers; l++) {
         const Layer& L = m->layers[l];
-        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, s);
+        qq3::launch_add_rmsnorm_rows(b.hidden, pend, T, E, L.t[QQ_ATTN_NORM]->f32, d.rms_eps, b.xn, b.x16, s);
+        pend = nullptr;
         if (L.attn) {
-            qq3::launch_gemm_q8_few(*L.t[QQ_WQ], b.xn, T, b.x16, b.rows, b.q, s);
-            qq3::launch_gemm_q8_few(*L.t[QQ_WK], b.xn, T, b.x16, b.rows, b.k, s, true);  // same input rows
+            qq3::launch_gemm_q8_few(*L.t[QQ_WQ], b.xn, T, b.x16, b.rows, b.q, s, true);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WK], b.xn, T, b.x16, b.rows, b.k, s, true);
             qq3::launch_gemm_q8_few(*L.t[QQ_WV], b.xn, T, b.x16, b.rows, b.v, s, true);
-            qq3::launch_rmsnorm(b.q, (int64_t)T * d.n_head, hd, L.t[QQ_Q_NORM]->f32, d.rms_eps, b.q, s);
-            qq3::launch_rmsnorm(b.k, (int64_t)T * d.n_head_kv, hd, L.t[QQ_K_NORM]->f32, d.rms_eps, b.k, s);
-            qq3::launch_rope_rows_at(b.q, T, d.n_head, hd, m->rope_cs, pos, s);
-            qq3::launch_rope_rows_at(b.k, T, d.n_head_kv, hd, m->rope_cs, pos, s);
             float* kc = m->k_cache + L.attn_slot * m->kv_stride_layer();
             float* vc = m->v_cache + L.attn_slot * m->kv_stride_layer();
-            qq3::launch_kv_append_at(b.k, b.v, T, d.n_head_kv, hd, d.max_ctx, seq, pos, m->kv_stride_seq(), kc, vc, s);
+            qq3::launch_qk_norm_rope_rows(b.q, b.k, b.v, T, d.n_head, d.n_head_kv, hd, L.t[QQ_Q_NORM]->f32,
+                                          L.t[QQ_K_NORM]->f32, d.rms_eps, m->rope_cs, seq, pos, 0, m->kv_stride_seq(),
+                                          d.max_ctx, kc, vc, s);
             qq3::launch_attn_rows_split(b.q, kc, vc, T, seq, pos, max_len, m->kv_stride_seq(), d.n_head, d.n_head_kv,
-                                        hd, d.max_ctx, m->bt_attn, b.attn, s);
-            qq3::launch_gemm_q8_few(*L.t[QQ_WO], b.attn, T, b.x16, b.rows, b.tmp, s);
+                                        hd, d.max_ctx, m->bt_attn, b.attn, s, b.x16);
+            qq3::launch_gemm_q8_few(*L.t[QQ_WO], b.attn, T, b.x16, b.rows, b.tmp, s, true);
             if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);  // heads' partial sums
         } else {
-            qq3::launch_gemm_q8_few(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.rows, b.bcx, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_IN_PROJ], b.xn, T, b.x16, b.rows, b.bcx, s, true);
             qq3::launch_conv_rows_at(b.bcx, L.t[QQ_CONV]->f32, m->conv(0, l), (size_t)d.n_layers * 2 * E, seq, T, E,
                                      b.y, s);
             qq3::launch_gemm_q8_few(*L.t[QQ_OUT_PROJ], b.y, T, b.x16, b.rows, b.tmp, s);
         }
-        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
-        qq3::launch_rmsnorm(b.hidden, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, s);
+        qq3::launch_add_rmsnorm_rows(b.hidden, b.tmp, T, E, L.t[QQ_FFN_NORM]->f32, d.rms_eps, b.xn, b.x16, s);
         if (L.moe) {
             const int k = d.n_expert_used;
             const float* bias = L.t[QQ_EXP_BIAS] ? L.t[QQ_EXP_BIAS]->f32 : nullptr;
@@ -1341,18 +1343,18 @@ void batch_step_on(qq_model* m, int T, int max_len, bool want_logits, cudaStream
                                     b.xn, T, k, d.n_expert, b.moe, b.tmp, s);
         } else {
             const size_t F = L.t[QQ_FFN_GATE]->ne[1];
-            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.rows, b.g, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_GATE], b.xn, T, b.x16, b.rows, b.g, s, true);
             qq3::launch_gemm_q8_few(*L.t[QQ_FFN_UP], b.xn, T, b.x16, b.rows, b.u, s, true);
-            qq3::launch_swiglu_rows(b.g, b.u, (size_t)T * F, b.h, s);
-            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.rows, b.tmp, s);
+            qq3::launch_swiglu_rows_f16(b.g, b.u, (size_t)T * F, b.x16, s);
+            qq3::launch_gemm_q8_few(*L.t[QQ_FFN_DOWN], b.h, T, b.x16, b.rows, b.tmp, s, true);
             if (m->tp_world > 1) qq3::comm_allreduce_sum_f32(m->ctx, b.tmp, b.tmp, TE, s);  // units' partial sums
         }
-        qq3::launch_add_rows(b.hidden, b.tmp, TE, s);
+        pend = b.tmp;
     }
-    if (!want_logits) return;
-    qq3::launch_rmsnorm(b.hidden, T, E, m->out_norm->f32, d.rms_eps, b.xn, s);
+    if (!want_logits) return;  // the last residual add is left out with the logits: nothing reads it
+    qq3::launch_add_rmsnorm_rows(b.hidden, pend, T, E, m->out_norm->f32, d.rms_eps, b.xn, b.x16, s);
     const DTensor* out = m->output ? m->output : m->tok_embd;
-    qq3::launch_gemm_q8_few(*out, b.xn, T, b.x16, b.rows, m->bt_logits, s);
+    qq3::launch_gemm_q8_few(*out, b.xn, T, b.x16, b.rows, m->bt_logits, s, true);
     if (m->tp_world > 1) {
         // this shard's greedy keys (global ids), all ranks' keys, then the first global maximum
         ensure_tp_bufs(m, T);

@@ -161,7 +161,22 @@ int attn_rows_chunk();
 size_t attn_rows_part_floats(int T, int n_head, int hd, int max_ctx);
 void launch_attn_rows_split(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
                             int max_len, size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* part,
-                            float* out, cudaStream_t s);
+                            float* out, cudaStream_t s, __half* out16 = nullptr);
+// ---- fused row pieces (kernels_prefill.cu); y16 / out16: the fp16 operand planes of the next
+// tensor-core product (what launch_f32_to_f16 writes for it), so that product runs x16_ready ----
+// SwiGLU of n values into the operand planes only
+void launch_swiglu_rows_f16(const float* g, const float* u, size_t n, __half* y16, cudaStream_t s);
+// x += d (d nullable), then y = RMS norm of each row of n values (launch_rmsnorm's result) and,
+// when y16 is non-null, y's operand planes
+void launch_add_rmsnorm_rows(float* x, const float* d, int64_t n_rows, int n, const float* w, float eps, float* y,
+                             __half* y16, cudaStream_t s);
+// per-head norms and RoPE of the rows' query heads (in place) and key heads, and the keys and
+// values stored into the cache (cache layout and row map as launch_kv_append_at; seq nullable:
+// kc / vc are the sequence's own; pos nullable: positions pos0 + t)
+void launch_qk_norm_rope_rows(float* q, const float* k, const float* v, int T, int n_head, int n_kv, int hd,
+                              const float* qw, const float* kw, float eps, const float* cs, const int* seq,
+                              const int* pos, int pos0, size_t seq_stride, int max_ctx, float* kc, float* vc,
+                              cudaStream_t s);
 
 // ---- bulk-copy streamed GEMV path (kernels_gemv2.cu) ----
 // Each returns false when the shape is outside the streamed path (the caller then uses the

@@ -105,6 +105,111 @@ __global__ void k_swiglu_rows(const float* __restrict__ g, const float* __restri
     }
 }
 
+// The fp16 operand form of one activation for the tensor-core products (the planes
+// launch_f32_to_f16 writes): hi = fp16(v) at i and, when split, lo = fp16((v - hi) * 2048) at n + i
+__device__ __forceinline__ void store_f16_split(__half* __restrict__ y16, size_t n, size_t i, float v, int split) {
+    const __half h = __float2half_rn(v);
+    y16[i] = h;
+    if (split) y16[n + i] = __float2half_rn((v - __half2float(h)) * 2048.f);
+}
+
+// SwiGLU straight into the operand planes of the down projection (h itself is not stored)
+__global__ void k_swiglu_rows_f16(const float* __restrict__ g, const float* __restrict__ u, size_t n,
+                                  __half* __restrict__ y16, int split) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float a = g[i];
+        store_f16_split(y16, n, i, a * (1.0f / (1.0f + expf(-a))) * u[i], split);
+    }
+}
+
+// Residual add and the next RMS norm in one pass over a row (tensor.js:103-116, 181-186; block =
+// row): x += d (d nullable), y = (w * x) / rms(x) with the sum of squares taken exactly as
+// k_rmsnorm takes it (same thread striding and reduction order, so the same y), and y's operand
+// planes when y16 is non-null (n_all = rows x n values per plane)
+__global__ void k_add_rmsnorm_rows(float* __restrict__ x, const float* __restrict__ d, int n,
+                                   const float* __restrict__ w, float eps, float* __restrict__ y,
+                                   __half* __restrict__ y16, size_t n_all, int split) {
+    __shared__ double red[32];
+    const size_t r0 = (size_t)blockIdx.x * n;
+    float* xr = x + r0;
+    float* yr = y + r0;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = xr[i];
+        if (d) {
+            v += d[r0 + i];
+            xr[i] = v;
+        }
+        ss += (double)v * v;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += red[i];
+        red[0] = 1.0 / sqrt(t / (double)n + (double)eps);
+    }
+    __syncthreads();
+    const float inv = (float)red[0];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float o = (w[i] * xr[i]) * inv;
+        yr[i] = o;
+        if (y16) store_f16_split(y16, n_all, r0 + i, o, split);
+    }
+}
+
+// The query / key head norms, RoPE and the K/V append of the rows in one launch.  Block
+// (t, head), 128 threads: heads 0 .. n_head-1 are row t's query heads (normalised and rotated in
+// place), heads n_head .. n_head+n_kv-1 its key heads (normalised, rotated and stored with the
+// row's value head into the cache).  Row t is sequence seq[t] (nullable: the cache pointers are
+// the sequence's own) at position pos[t] (nullable: pos0 + t).  The norm is k_rmsnorm's with 128
+// threads and the rotation k_rope_rows' (tensor.js:117-147, kv-cache.js:16-32); hd <= 128, even.
+__global__ void __launch_bounds__(128)
+    k_qk_norm_rope_rows(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, int n_head,
+                        int n_kv, int hd, const float* __restrict__ qw, const float* __restrict__ kw, float eps,
+                        const float* __restrict__ cs, const int* __restrict__ seq, const int* __restrict__ pos,
+                        int pos0, size_t seq_stride, int max_ctx, float* __restrict__ kc, float* __restrict__ vc) {
+    __shared__ double red[4];
+    __shared__ float xs[128];
+    const int t = blockIdx.x, i = threadIdx.x;
+    const bool is_q = (int)blockIdx.y < n_head;
+    const int h = is_q ? (int)blockIdx.y : (int)blockIdx.y - n_head;
+    const size_t src = is_q ? ((size_t)t * n_head + h) * hd : ((size_t)t * n_kv + h) * hd;
+    const float xv = i < hd ? (is_q ? q[src + i] : k[src + i]) : 0.f;
+    double ss = (double)xv * xv;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((i & 31) == 0) red[i >> 5] = ss;
+    __syncthreads();
+    if (i == 0) {
+        double tt = 0.0;
+        for (int j = 0; j < 4; j++) tt += red[j];
+        red[0] = 1.0 / sqrt(tt / (double)hd + (double)eps);
+    }
+    __syncthreads();
+    const float inv = (float)red[0];
+    if (i < hd) xs[i] = ((is_q ? qw[i] : kw[i]) * xv) * inv;
+    __syncthreads();
+    const int half = hd >> 1;
+    const size_t p = (size_t)(pos ? pos[t] : pos0 + t);
+    float* dst;
+    if (is_q) {
+        dst = q + src;
+    } else {
+        const size_t at = (seq ? (size_t)seq[t] * seq_stride : 0) + ((size_t)h * max_ctx + p) * hd;
+        dst = kc + at;
+        if (i < hd) vc[at + i] = v[src + i];
+    }
+    if (i < half) {
+        const float c = cs[p * hd + 2 * i], s = cs[p * hd + 2 * i + 1];
+        const float x0 = xs[i], x1 = xs[i + half];
+        dst[i] = x0 * c - x1 * s;
+        dst[i + half] = x0 * s + x1 * c;
+    }
+}
+
 // Causal GQA attention of one query head over positions 0..len-1 of one kv head's cache rows,
 // by one warp: tiles of 32 positions (one per lane), online softmax, V accumulation (lane owns
 // HD/32 dims).  qh: the normalised, rotated query; o: HD outputs.
@@ -521,7 +626,7 @@ __global__ void __launch_bounds__(256)
 // one warp per (row, head): lane owns HD/32 output dims
 template <int HD>
 __global__ void k_attn_merge(const float* __restrict__ part, const int* __restrict__ pos, int T, int n_head, int chunk,
-                             int n_split, float* __restrict__ out) {
+                             int n_split, float* __restrict__ out, __half* __restrict__ out16, int split) {
     constexpr int PL = HD / 32;
     const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (w >= T * n_head) return;
@@ -556,9 +661,13 @@ __global__ void k_attn_merge(const float* __restrict__ part, const int* __restri
             for (int j = 0; j < PL; j++) acc[j] = fmaf(f, av[u][j], acc[j]);
         }
     }
-    float* o = out + ((size_t)t * n_head + h) * HD + lane * PL;
+    const size_t o0 = ((size_t)t * n_head + h) * HD + lane * PL;
 #pragma unroll
-    for (int j = 0; j < PL; j++) o[j] = acc[j] / L;
+    for (int j = 0; j < PL; j++) {
+        const float r = acc[j] / L;
+        out[o0 + j] = r;
+        if (out16) store_f16_split(out16, (size_t)T * n_head * HD, o0 + j, r, split);
+    }
 }
 
 // one short-conv step per row with its sequence's 2-tap state (lfm2-engine.js:282-325);
@@ -659,6 +768,33 @@ void launch_swiglu_rows(const float* g, const float* u, size_t n, float* h, cuda
     QQ_CUDA_TRY(cudaGetLastError());
 }
 
+void launch_swiglu_rows_f16(const float* g, const float* u, size_t n, __half* y16, cudaStream_t s) {
+    if (n == 0) return;
+    k_swiglu_rows_f16<<<grid_n(n), 256, 0, s>>>(g, u, n, y16, gemm_exact() ? 1 : 0);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_add_rmsnorm_rows(float* x, const float* d, int64_t n_rows, int n, const float* w, float eps, float* y,
+                             __half* y16, cudaStream_t s) {
+    if (n_rows <= 0) return;
+    // the thread count launch_rmsnorm uses for rows of n values (the same sums)
+    const int threads = n >= 2048 ? 1024 : (n >= 512 ? 256 : 128);
+    k_add_rmsnorm_rows<<<(unsigned)n_rows, threads, 0, s>>>(x, d, n, w, eps, y, y16, (size_t)n_rows * n,
+                                                            gemm_exact() ? 1 : 0);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
+void launch_qk_norm_rope_rows(float* q, const float* k, const float* v, int T, int n_head, int n_kv, int hd,
+                              const float* qw, const float* kw, float eps, const float* cs, const int* seq,
+                              const int* pos, int pos0, size_t seq_stride, int max_ctx, float* kc, float* vc,
+                              cudaStream_t s) {
+    QQ_CHECK(hd >= 2 && hd <= 128 && hd % 2 == 0, -4, "head norm + RoPE: head_dim must be even and at most 128");
+    if (T <= 0) return;
+    k_qk_norm_rope_rows<<<dim3((unsigned)T, (unsigned)(n_head + n_kv)), 128, 0, s>>>(
+        q, k, v, n_head, n_kv, hd, qw, kw, eps, cs, seq, pos, pos0, seq_stride, max_ctx, kc, vc);
+    QQ_CUDA_TRY(cudaGetLastError());
+}
+
 void launch_attn_prefill(const float* q, const float* kc, const float* vc, int T, int pos0, int n_head, int n_kv,
                          int hd, int max_ctx, float* out, cudaStream_t s) {
     const int G = n_head / n_kv;
@@ -725,7 +861,7 @@ size_t attn_rows_part_floats(int T, int n_head, int hd, int max_ctx) {
 
 void launch_attn_rows_split(const float* q, const float* kc, const float* vc, int T, const int* seq, const int* pos,
                             int max_len, size_t seq_stride, int n_head, int n_kv, int hd, int max_ctx, float* part,
-                            float* out, cudaStream_t s) {
+                            float* out, cudaStream_t s, __half* out16) {
     const int G = n_head / n_kv;
     QQ_CHECK(G >= 1 && G <= 32 && n_head % n_kv == 0, -4, "batched attention: unsupported head grouping");
     if (T <= 0) return;
@@ -738,6 +874,7 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
     // K and V of a split staged in shared memory once for the G query heads (k_attn_rows_tile),
     // up to 8 heads per kv head; the per-warp global-memory form otherwise
     const bool tile = G <= 8 && !tiled_attention_off();
+    const int split = gemm_exact() ? 1 : 0;
     const size_t smem = ((size_t)2 * chunk + G) * hd * sizeof(float);
     // the attribute is set once per device, to the largest size any head grouping needs (G = 8):
     // a launch may not ask for more dynamic shared memory than the attribute allows
@@ -754,7 +891,7 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
                                                           n_split, part);
         }
         QQ_CUDA_TRY(cudaGetLastError());
-        k_attn_merge<64><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out);
+        k_attn_merge<64><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out, out16, split);
     } else if (hd == 128) {
         if (tile) {
             if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<128>)))
@@ -767,7 +904,7 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
                                                            chunk, n_split, part);
         }
         QQ_CUDA_TRY(cudaGetLastError());
-        k_attn_merge<128><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out);
+        k_attn_merge<128><<<mg, 256, 0, s>>>(part, pos, T, n_head, chunk, n_split, out, out16, split);
     } else {
         QQ_CHECK(false, -4, "batched attention: head_dim must be 64 or 128");
     }
