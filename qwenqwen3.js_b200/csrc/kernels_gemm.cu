@@ -366,10 +366,13 @@ __global__ void __launch_bounds__(kThreadsG2, 1)
 //   warp 10   loads the fp16 activation tiles (hi rows, then lo rows) of each 64-wide K step;
 //   warps 0-7 convert: thread (row r, K half h) turns its 32 weights of a K step into the exact
 //             fp16 hi/lo pairs and writes them to tensor memory (tcgen05.st, lane r), the MMA's
-//             A operand; after an item's last K step they read its accumulators and store them;
+//             A operand, and go straight on to the next item's K steps;
 //   warp 9    issues [hh | hl] += wh.[xh | xl] (N = 2 MN) and lh += wl.xh (N = MN) per 16 of K,
 //             with A read from tensor memory, into one of two accumulator pairs (items
-//             alternate, so an item's MMAs overlap the previous item's epilogue).
+//             alternate, so an item's MMAs overlap the previous item's epilogue);
+//   warps 11-18 (two per 32 tensor-memory lanes, each half of the activation rows) read an
+//             item's accumulators once its MMAs are done and store them, so no converter waits
+//             for an item to drain.
 // A in tensor memory keeps the converted weights out of shared memory: an N = 16 MMA with A in
 // shared memory re-reads its 4 KB A tile for 16 output columns, and those reads, the converted
 // stores and the raw stages share one pipe (measured: conversion, MMAs and loads added up).
@@ -380,7 +383,9 @@ constexpr int kRowsBM = 128;       // weight rows per item
 constexpr int kRowsKR = 256;       // K of one raw weight stage (four 64-wide MMA K steps)
 constexpr int kRowsMaxItems = 296; // S * row tiles <= this when S > 1
 constexpr int kRowsTickets = 256;  // >= row tiles whenever S > 1
-constexpr int kRowsWarps = 11;     // 8 converters, raw producer, MMA issuer, activation producer
+constexpr int kRowsEpiWarp = 11;   // first epilogue warp
+constexpr int kRowsEpiWarps = 8;   // two per 32 tensor-memory lanes
+constexpr int kRowsWarps = kRowsEpiWarp + kRowsEpiWarps;  // 8 converters, 3 producer / issuer warps, epilogue
 constexpr int kRowsThreads = kRowsWarps * 32;
 
 // MN = 16 / 32: all activation rows of a few-row product in one item; MN = 128: the wide form for
@@ -394,7 +399,6 @@ struct RowsCfg {
     static constexpr int OpStages = MN == 16 ? 3 : 2;   // operand stages in TMEM
     static constexpr int XStages = OpStages;            // released by the same MMA commit
     static constexpr int NumAcc = Wide ? 1 : 2;         // accumulator sets (items alternate)
-    static constexpr int RowsPerWarp = Wide ? MN / 2 : 16;  // activation rows a converter warp stores
     static constexpr int XTile = MN * kBK * 2;          // fp16 activations (hi or lo) of one K step
     static constexpr int RawBox = kRowsBM * 128;        // one swizzled 128-byte-wide box: 16 KB
     static constexpr int DTile = kRowsBM * 16;          // block scales: 8 fp16 per row (256 K)
@@ -486,7 +490,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_free[a], kConvWarps);
+            mbar_init(&acc_free[a], kRowsEpiWarps);
         }
         mbar_fence_init();
     }
@@ -574,14 +578,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 umma_commit(&acc_full[ab]);  // covers the item's MMAs (also after a failed wait)
             }
         }
-    } else {
+    } else if (warp < kConvWarps) {
         // converters: thread t holds weight row t & 127 (its TMEM lane) and K half t >> 7 of each
-        // K step; epilogue: warp w reads TMEM lanes 32 (w % 4) .., activation rows 16 (w / 4) ..
+        // K step
         const int row = t & 127, kh = t >> 7;
-        const int q = warp & 3, hb = warp >> 2;
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        int o = 0, r = 0, j = 0;
-        for (int it = blockIdx.x; it < n_items; it += gridDim.x, j++) {
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        int o = 0, r = 0;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
             int n0, a0, sp, r0, r1;
             item_range(it, n0, a0, sp, r0, r1);
             const int n = n0 + row;
@@ -640,15 +643,26 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&raw_free[rs]);  // the stage's bytes are in registers / TMEM
             }
-            // epilogue of item j: accumulator set j % NA; warp (q, hb) stores activation rows
-            // a0 + RowsPerWarp hb .. in chunks of 16
+        }
+    } else {
+        // epilogue warps: warp w reads tensor-memory lanes 32 (w % 4) .. (weight rows) of item j's
+        // accumulator set j % NA and stores activation rows of its half hb, in chunks of 16 (the
+        // MN = 16 form: one chunk, stored by the first four warps)
+        constexpr int kEpiThreads = kRowsEpiWarps * 32;
+        constexpr int kHalf = MN > 16 ? MN / 2 : 16;
+        const int q = warp & 3, te = t - kRowsEpiWarp * 32, hb = te >> 7;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        int j = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, j++) {
+            int n0, a0, sp, r0, r1;
+            item_range(it, n0, a0, sp, r0, r1);
             const int ab = j % NA;
             if (ok) ok = bar_wait(&acc_full[ab], (uint32_t)((j / NA) & 1), err);
             ok = __all_sync(0xffffffffu, ok);
             tc_fence_after();
             const int nn = n0 + q * 32 + lane;
 #pragma unroll 1
-            for (int c16 = hb * G::RowsPerWarp; c16 < (hb + 1) * G::RowsPerWarp && c16 < MN; c16 += 16) {
+            for (int c16 = hb * kHalf; c16 < (hb + 1) * kHalf && c16 < MN; c16 += 16) {
                 float f[16];
                 if (ok) {
                     uint32_t v[16], v2[16], v3[16];
@@ -677,17 +691,17 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
             if (lane == 0) mbar_arrive(&acc_free[ab]);
             if (S > 1) {  // every item takes a ticket (also after a failed wait, so the tickets reset)
                 __threadfence();
-                named_bar(1, kConvWarps * 32);
-                if (t == 0) {
+                named_bar(1, kEpiThreads);
+                if (te == 0) {
                     const int tile = it / S;
                     const unsigned prev = atomicAdd(&tickets[tile], 1u);
                     last_flag = prev == (unsigned)(S - 1);
                     if (last_flag) tickets[tile] = 0u;
                 }
-                named_bar(1, kConvWarps * 32);
+                named_bar(1, kEpiThreads);
                 if (last_flag) {
                     __threadfence();
-                    for (int i = t; i < M * kRowsBM; i += kConvWarps * 32) {
+                    for (int i = te; i < M * kRowsBM; i += kEpiThreads) {
                         const int m = i / kRowsBM, c = n0 + i % kRowsBM;
                         if (c < N) {
                             float acc = __ldcg(part + (size_t)m * N + c);
@@ -696,7 +710,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
                         }
                     }
                 }
-                named_bar(1, kConvWarps * 32);  // last_flag is rewritten by the next item
+                named_bar(1, kEpiThreads);  // last_flag is rewritten by the next item
             }
         }
     }
