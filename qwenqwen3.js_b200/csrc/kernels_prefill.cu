@@ -29,7 +29,6 @@ static bool tiled_attention_off() {
     return v == 1;
 }
 
-
 namespace {
 
 unsigned grid_n(size_t n) { return (unsigned)std::min<size_t>((n + 255) / 256, (size_t)148 * 64); }
@@ -527,25 +526,30 @@ __global__ void k_attn_rows_split(const float* __restrict__ q, const float* __re
 
 // The same split over positions with the split's K and V rows staged once per CTA: one 1-D bulk
 // copy each (a kv head's positions are contiguous, [pos][HD] f32) into shared memory, completing on
-// an mbarrier; the G warps (query heads of the kv head) then score and accumulate from shared
-// memory.  Lane l scores position p0 + l reading the K row's float4s in a lane-rotated order
-// ((i + l) mod HD/4), so a quarter-warp's loads fall in distinct bank groups; the query sits in
-// shared memory read in the same order.  The V pass reads one row per step, lane l its HD/32 dims.
-// Chunk = attn_rows_chunk() positions; numerics as attn_row_part (f32 dots in another order).
+// an mbarrier; two warps per query head of the kv head then score and accumulate from shared
+// memory, warp half 0 the split's 32-position steps 0, 2, .., half 1 steps 1, 3, .. (each its own
+// online softmax), and half 0 combines the two states as the merge does (M = max, states scaled
+// by e^(m - M)).  Lane l scores position p0 + l reading the K row's float4s in a lane-rotated
+// order ((i + l) mod HD/4), so a quarter-warp's loads fall in distinct bank groups, in four
+// independent FMA chains (one per float4 component); the query sits in shared memory read in the
+// same order.  The V pass reads one row per step, lane l its HD/32 dims.  Chunk =
+// attn_rows_chunk() positions; numerics as attn_row_part up to the f32 summation order.
 template <int HD>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(512)
     k_attn_rows_tile(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                      const int* __restrict__ seq, const int* __restrict__ pos, size_t seq_stride, int n_head, int n_kv,
                      int max_ctx, int chunk, int n_split, float* __restrict__ part, int* err) {
     constexpr int PL = HD / 32, H4 = HD / 4;
     extern __shared__ __align__(128) uint8_t sm_raw[];
+    const int G = n_head / n_kv;
     float* ks = reinterpret_cast<float*>(sm_raw);
     float* vs = ks + (size_t)chunk * HD;
-    float* qs = vs + (size_t)chunk * HD;
+    float* qs = vs + (size_t)chunk * HD;  // [2 G][HD]: each warp's copy of its head's query
+    float* xs = qs + (size_t)2 * G * HD;  // [G][HD + 2]: half 1's state for half 0
     __shared__ __align__(8) uint64_t bar;
     const int t = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
-    const int G = n_head / n_kv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = warp >> 1, half = warp & 1;
     const int len = pos[t] + 1;
     const int b = sp * chunk, e = min(len, b + chunk), n_pos = e - b;
     const size_t base = (size_t)seq[t] * seq_stride + (size_t)kvh * max_ctx * HD;
@@ -560,14 +564,15 @@ __global__ void __launch_bounds__(256)
         bulk_g2s(ks, kc + base + (size_t)b * HD, bytes, &bar);
         bulk_g2s(vs, vc + base + (size_t)b * HD, bytes, &bar);
     }
-    if (warp >= G) return;  // (the copies are waited for by the warps that read them)
-    const int h = kvh * G + warp;
+    const int h = kvh * G + g;
     float* out = part + (((size_t)t * n_head + h) * n_split + sp) * (HD + 2);
-    if (n_pos <= 0) {  // a split past this row's length: an empty state
-        for (int j = lane; j < HD; j += 32) out[j] = 0.f;
-        if (lane == 0) {
-            out[HD] = -INFINITY;
-            out[HD + 1] = 0.f;
+    if (n_pos <= 0) {  // a split past this row's length (the whole CTA): an empty state
+        if (half == 0) {
+            for (int j = lane; j < HD; j += 32) out[j] = 0.f;
+            if (lane == 0) {
+                out[HD] = -INFINITY;
+                out[HD + 1] = 0.f;
+            }
         }
         return;
     }
@@ -583,22 +588,22 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < PL; j++) acc[j] = 0.f;
     const float4* q4 = reinterpret_cast<const float4*>(qw);
-    for (int p0 = 0; ok && p0 < n_pos; p0 += 32) {
+    for (int p0 = 32 * half; ok && p0 < n_pos; p0 += 64) {
         const int pl_i = p0 + lane;
         float s = -INFINITY;
         if (pl_i < n_pos) {
             const float4* k4 = reinterpret_cast<const float4*>(ks + (size_t)pl_i * HD);
-            float dot = 0.f;
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll 8
             for (int i = 0; i < H4; i++) {
                 const int ii = (i + lane) & (H4 - 1);
                 const float4 kv = k4[ii], qv = q4[ii];
-                dot = fmaf(qv.x, kv.x, dot);
-                dot = fmaf(qv.y, kv.y, dot);
-                dot = fmaf(qv.z, kv.z, dot);
-                dot = fmaf(qv.w, kv.w, dot);
+                d0 = fmaf(qv.x, kv.x, d0);
+                d1 = fmaf(qv.y, kv.y, d1);
+                d2 = fmaf(qv.z, kv.z, d2);
+                d3 = fmaf(qv.w, kv.w, d3);
             }
-            s = dot * scale;
+            s = ((d0 + d1) + (d2 + d3)) * scale;
         }
         const float m_new = fmaxf(m, warp_max(s));
         const float pl = pl_i < n_pos ? expf(s - m_new) : 0.f;
@@ -607,6 +612,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int j = 0; j < PL; j++) acc[j] *= cf;
         const int n = min(32, n_pos - p0);
+#pragma unroll 8
         for (int jj = 0; jj < n; jj++) {
             const float pj = __shfl_sync(0xffffffffu, pl, jj);
             const float* vr = vs + (size_t)(p0 + jj) * HD + lane * PL;
@@ -615,11 +621,26 @@ __global__ void __launch_bounds__(256)
         }
         m = m_new;
     }
+    // half 1 hands its state to half 0 (an empty state when the split has <= 32 positions)
+    float* xw = xs + (size_t)g * (HD + 2);
+    if (half == 1) {
 #pragma unroll
-    for (int j = 0; j < PL; j++) out[lane * PL + j] = acc[j];
+        for (int j = 0; j < PL; j++) xw[lane * PL + j] = acc[j];
+        if (lane == 0) {
+            xw[HD] = m;
+            xw[HD + 1] = l;
+        }
+    }
+    __syncthreads();
+    if (half == 1) return;
+    const float m1 = xw[HD], l1 = xw[HD + 1];
+    const float M = fmaxf(m, m1);
+    const float f0 = expf(m - M), f1 = expf(m1 - M);
+#pragma unroll
+    for (int j = 0; j < PL; j++) out[lane * PL + j] = acc[j] * f0 + xw[lane * PL + j] * f1;
     if (lane == 0) {
-        out[HD] = m;
-        out[HD + 1] = l;
+        out[HD] = M;
+        out[HD + 1] = l * f0 + l1 * f1;
     }
 }
 
@@ -875,16 +896,18 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
     // up to 8 heads per kv head; the per-warp global-memory form otherwise
     const bool tile = G <= 8 && !tiled_attention_off();
     const int split = gemm_exact() ? 1 : 0;
-    const size_t smem = ((size_t)2 * chunk + G) * hd * sizeof(float);
+    // K, V, two query copies per head, half 1's states (k_attn_rows_tile)
+    auto tile_smem = [&](int g) { return ((size_t)2 * chunk * hd + (size_t)2 * g * hd + (size_t)g * (hd + 2)) * sizeof(float); };
+    const size_t smem = tile_smem(G);
     // the attribute is set once per device, to the largest size any head grouping needs (G = 8):
     // a launch may not ask for more dynamic shared memory than the attribute allows
-    const size_t smem_max = ((size_t)2 * chunk + 8) * hd * sizeof(float);
+    const size_t smem_max = tile_smem(8);
     if (hd == 64) {
         if (tile) {
             if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<64>)))
                 QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_rows_tile<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)smem_max));
-            k_attn_rows_tile<64><<<grid, 32 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
+            k_attn_rows_tile<64><<<grid, 64 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
                                                             chunk, n_split, part, kernel_err_ptr());
         } else {
             k_attn_rows_split<64><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx, chunk,
@@ -897,7 +920,7 @@ void launch_attn_rows_split(const float* q, const float* kc, const float* vc, in
             if (first_use_on_device(reinterpret_cast<const void*>(k_attn_rows_tile<128>)))
                 QQ_CUDA_TRY(cudaFuncSetAttribute(k_attn_rows_tile<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)smem_max));
-            k_attn_rows_tile<128><<<grid, 32 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
+            k_attn_rows_tile<128><<<grid, 64 * G, smem, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
                                                              chunk, n_split, part, kernel_err_ptr());
         } else {
             k_attn_rows_split<128><<<grid, 32 * G, 0, s>>>(q, kc, vc, seq, pos, seq_stride, n_head, n_kv, max_ctx,
