@@ -215,3 +215,101 @@ def test_sample_uniform_twin_matches_library(qq3):
         qq3.runtime.check(lib.qq_sample_uniform(C.c_uint64(seed), seq, pos, C.byref(r)))
         assert r.value == qq3.runtime.sample_uniform(seed, seq, pos)
         assert 0.0 <= r.value < 1.0
+
+
+def _fake_engine(qq3, script, eos=2, stops=(7,)):
+    """A Qwen3 engine object without a device: the token that follows forward(t, pos) is
+    script[pos] (greedy on the device, or the only finite logit on the host path)."""
+    eng_mod = qq3.engine
+
+    class Fake(eng_mod.Qwen3CudaEngine):
+        def __init__(self):  # no GGUF, no context
+            self.nVocab = 64
+            self.eosTokenId = eos
+            self.stopTokenIds = set(stops)
+            self.calls = []
+            self.prefilled = []
+
+        def resetKVCache(self, seq=0):
+            self.calls.clear()
+
+        def prefill(self, tokenIds, pos0=0, seq=0):
+            self.prefilled = list(tokenIds)
+
+        def forward_argmax(self, tokenId, position, suppress_id=-1, seq=0):
+            self.calls.append((int(tokenId), int(position), int(suppress_id)))
+            return int(script[position])
+
+        def forward(self, tokenId, position, skipLogits=False, seq=0):
+            self.calls.append((int(tokenId), int(position), -2))
+            logits = np.full(self.nVocab, -1e30, dtype=np.float32)
+            logits[int(script[position])] = 0.0
+            return logits
+
+    return Fake()
+
+
+def _js_generate(token_ids, max_steps, eos, stops, next_after):
+    # qwen3-engine.js:397-457: sample after the last prompt token, then per step: stop on EOS or
+    # a stop id, forward the current token at position n + step, emit it, sample the next
+    cur = next_after(token_ids[-1], len(token_ids) - 1)
+    out = []
+    for step in range(max_steps):
+        if cur == eos or cur in stops:
+            break
+        nxt = next_after(cur, len(token_ids) + step)
+        out.append(cur)
+        cur = nxt
+    return out
+
+
+@pytest.mark.parametrize("case", ["eos", "stop_id", "max_steps", "host_sampler"])
+def test_generate_loop_mirrors_js(qq3, case):
+    rng = np.random.default_rng(11)
+    script = rng.integers(10, 60, size=256)
+    prompt = [3, 5, 8, 13]
+    n = len(prompt)
+    if case == "eos":
+        script[n + 4] = 2
+    elif case == "stop_id":
+        script[n + 2] = 7
+    eng = _fake_engine(qq3, script)
+    max_steps = 9 if case == "max_steps" else 40
+    want = _js_generate(prompt, max_steps, 2, {7}, lambda t, p: int(script[p]))
+    seen, finished = [], []
+    kw = dict(temperature=0.7, topP=0.9, topK=0) if case == "host_sampler" else dict(temperature=0)
+    got = eng.generate(prompt, maxSteps=max_steps, onToken=seen.append, onFinish=finished.append, **kw)
+    assert got == want
+    assert seen == want and finished == [want]
+    assert eng.prefilled == prompt[:-1]
+    # positions: the last prompt token at n - 1, then generated token s at n + s
+    assert [c[1] for c in eng.calls] == list(range(n - 1, n - 1 + len(eng.calls)))
+    assert [c[0] for c in eng.calls] == [prompt[-1]] + want[: len(eng.calls) - 1]
+    if case != "host_sampler":  # greedy on the device with the think id suppressed
+        assert all(c[2] == (eng.THINK_ID if eng.THINK_ID < eng.nVocab else -1) for c in eng.calls)
+    # script[n - 1] is the first generated token, script[n + s] the one after generated token s
+    if case == "eos":
+        assert len(want) == 5
+    elif case == "stop_id":
+        assert len(want) == 3
+    elif case == "max_steps":
+        assert len(want) == max_steps
+
+
+def test_generate_abort_returns_none(qq3):
+    script = np.full(64, 20)
+    eng = _fake_engine(qq3, script)
+
+    class Signal:
+        aborted = False
+
+    sig = Signal()
+
+    def on_token(t):
+        if len(eng.calls) >= 3:
+            sig.aborted = True
+
+    assert eng.generate([1, 4], maxSteps=20, temperature=0, onToken=on_token, abortSignal=sig) is None
+    assert len(eng.calls) == 3
+    sig.aborted = True
+    assert eng.generate([1, 4], maxSteps=20, temperature=0, abortSignal=sig) is None
