@@ -313,3 +313,21 @@ def test_generate_abort_returns_none(qq3):
     assert len(eng.calls) == 3
     sig.aborted = True
     assert eng.generate([1, 4], maxSteps=20, temperature=0, abortSignal=sig) is None
+
+
+def test_cpu_baseline_leg_on_a_tiny_model(qq3, orc):
+    """bench.py's CPU baseline leg (the oracle on the host cores) on a tiny model: its record
+    carries the fields the JSON line reports, the single-thread sample included."""
+    import sys
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    spec = qq3.synth.tiny_lfm2(seed=5)
+    g = qq3.synth.MemoryGGUF(spec, qq3.synth.build_tensors(spec))
+    prompt = qq3.synth.uniform_tokens(12, 5, spec.n_vocab)
+    cb = bench.cpu_decode(g, spec, prompt, steps=3, warmup=1, single_s=0.05, label="tiny LFM2")
+    assert cb["unit"] == "tok/s" and cb["kind"] == "port" and cb["value"] > 0
+    assert cb["cores"] >= 1 and cb["nproc"] == cb["cores"]
+    assert "12-token prompt" in cb["sample"] and "1 warm-up + 3 timed greedy steps" in cb["sample"]
+    assert cb["single_thread"]["cores"] == 1 and cb["single_thread"]["value"] > 0
